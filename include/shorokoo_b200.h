@@ -1,0 +1,142 @@
+/* shorokoo_b200 — C ABI of the B200 inference backend for Shorokoo.
+ *
+ * This is the native surface a Shorokoo backend plugin binds (through [LibraryImport] from C#, or
+ * ctypes from Python). It replaces the ONNX Runtime calls behind the reference's backend plugin
+ * interface:
+ *   IShorokooInferenceSessionFactory  src/Shorokoo/Core/Inference/Abstractions/IShorokooInferenceSessionFactory.cs:5-24
+ *   IShorokooInferenceSession         src/Shorokoo/Core/Inference/Abstractions/IShorokooInferenceSession.cs:3-13
+ *   IShorokooTensorValue              src/Shorokoo/Core/Inference/Abstractions/IShorokooTensorValue.cs:8-31
+ * whose ORT implementation is src/Backend/OnnxRuntime/Shorokoo.OnnxRuntime/{OrtSessionFactory,
+ * OrtInferenceSession,OrtTensorValue}.cs and whose GPU slot is
+ * src/Backend/OnnxRuntime/Shorokoo.LinuxGPU/LinuxGpuInferenceFactory.cs:5-8.
+ *
+ * Conventions: every function returning int32_t returns a status (SB_STATUS_*); on failure
+ * sb_last_error() gives a message for the calling thread. Element types use the ONNX
+ * TensorProto.DataType numbering (== ShorokooTensorElementType). All tensor data is HOST memory.
+ * Values are reference counted; every sb_value* handed out must be released exactly once.
+ */
+#ifndef SHOROKOO_B200_H_
+#define SHOROKOO_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SB_API __attribute__((visibility("default")))
+#else
+#define SB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SB_STATUS_OK 0
+#define SB_STATUS_INVALID_ARGUMENT 1 /* -> ArgumentException */
+#define SB_STATUS_UNSUPPORTED 2      /* -> NotSupportedException (unsupported op/dtype: hard error) */
+#define SB_STATUS_SHAPE_ERROR 3      /* -> ArgumentException */
+#define SB_STATUS_CUDA_ERROR 4       /* -> InvalidOperationException */
+#define SB_STATUS_OUT_OF_MEMORY 5    /* -> OutOfMemoryException */
+#define SB_STATUS_INTERNAL 6         /* -> InvalidOperationException */
+
+/* ShorokooOnnxValueType (src/Shorokoo/Core/Inference/Abstractions/ShorokooOnnxValueType.cs) */
+#define SB_VALUE_TENSOR 1
+#define SB_VALUE_SEQUENCE 2
+
+typedef struct sb_session sb_session;
+typedef struct sb_value sb_value;
+
+/* Library version (major*10000 + minor*100 + patch). */
+SB_API int32_t sb_version(void);
+/* Message of the last failing call on this thread ("" if none). Valid until the next call. */
+SB_API const char* sb_last_error(void);
+
+/* ---- IShorokooInferenceSessionFactory.CreateSession(modelBytes, graphOptimization, logSeverity)
+ * (IShorokooInferenceSessionFactory.cs:7-10; ORT: OrtSessionFactory.cs:23-42).
+ * Parses the ONNX ModelProto bytes (not retained) and rejects any operator without a B200
+ * implementation. graph_optimization (ShorokooGraphOptimization) and log_severity
+ * (ShorokooLogSeverity) are accepted for interface parity; plans are always fully optimised.
+ * Devices: SHOROKOO_B200_DEVICES (default: all visible CUDA devices); batches shard across them. */
+SB_API int32_t sb_session_create(const uint8_t* model, size_t model_len, int32_t graph_optimization,
+                          int32_t log_severity, sb_session** out);
+/* Same, with an explicit device range [first_device, first_device + num_devices). */
+SB_API int32_t sb_session_create_ex(const uint8_t* model, size_t model_len, int32_t graph_optimization,
+                             int32_t log_severity, int32_t num_devices, int32_t first_device,
+                             sb_session** out);
+/* IShorokooInferenceSession.Dispose (IDisposable). */
+SB_API void sb_session_destroy(sb_session* session);
+
+/* IShorokooInferenceSession.InputNames / OutputNames (IShorokooInferenceSession.cs:5-6).
+ * Inputs are reported in graph-input order (ComputeContext.cs:209-211 maps them positionally). */
+SB_API int32_t sb_session_input_count(const sb_session* session);
+SB_API const char* sb_session_input_name(const sb_session* session, int32_t index);
+SB_API int32_t sb_session_output_count(const sb_session* session);
+SB_API const char* sb_session_output_name(const sb_session* session, int32_t index);
+
+/* IShorokooInferenceSession.Run(inputs, outputNames) (IShorokooInferenceSession.cs:10-12;
+ * ORT: OrtInferenceSession.cs:15-36). Inputs by name; outputs in the order of out_names, written
+ * to out_values as new references owned by the caller (they outlive the session). */
+SB_API int32_t sb_session_run(sb_session* session, int32_t n_inputs, const char* const* in_names,
+                       sb_value* const* in_values, int32_t n_outputs, const char* const* out_names,
+                       sb_value** out_values);
+
+/* ---- IShorokooInferenceSessionFactory.CreateTensor<T> / CreateTensorFromRawBytes
+ * (IShorokooInferenceSessionFactory.cs:12-18; ORT: OrtSessionFactory.cs:44-91).
+ * Copies `nbytes` of element data (page-locked host memory when large). */
+SB_API int32_t sb_value_create_tensor(int32_t elem_type, const int64_t* shape, int32_t rank, const void* data,
+                               size_t nbytes, sb_value** out);
+/* Wraps caller memory without copying (ORT aliases managed arrays the same way,
+ * OrtSessionFactory.cs:56). The memory must stay valid and unchanged until the value is released. */
+SB_API int32_t sb_value_wrap_tensor(int32_t elem_type, const int64_t* shape, int32_t rank, void* data,
+                             size_t nbytes, sb_value** out);
+/* IShorokooInferenceSessionFactory.CreateStringTensor (IShorokooInferenceSessionFactory.cs:20-22). */
+SB_API int32_t sb_value_create_string_tensor(const char* const* strings, size_t count, const int64_t* shape,
+                                      int32_t rank, sb_value** out);
+/* IShorokooInferenceSessionFactory.CreateSequence (IShorokooInferenceSessionFactory.cs:23). */
+SB_API int32_t sb_value_create_sequence(sb_value* const* values, size_t count, sb_value** out);
+/* IShorokooTensorValue.Dispose. */
+SB_API void sb_value_release(sb_value* value);
+
+/* ---- IShorokooTensorValue accessors (IShorokooTensorValue.cs:10-30; ORT: OrtTensorValue.cs:11-56) */
+SB_API int32_t sb_value_type(const sb_value* value);      /* ValueType: SB_VALUE_TENSOR / SB_VALUE_SEQUENCE */
+SB_API int32_t sb_value_elem_type(const sb_value* value); /* ElementType */
+SB_API int32_t sb_value_rank(const sb_value* value);
+SB_API const int64_t* sb_value_shape(const sb_value* value); /* Shape */
+SB_API void* sb_value_data(sb_value* value);               /* GetTensor(Mutable)DataAsSpan: host memory */
+SB_API size_t sb_value_nbytes(const sb_value* value);
+SB_API size_t sb_value_string_count(const sb_value* value);           /* GetStringTensorData */
+SB_API const char* sb_value_string_at(const sb_value* value, size_t index);
+SB_API int32_t sb_value_count(const sb_value* value);                 /* GetValueCount */
+SB_API int32_t sb_value_at(const sb_value* value, int32_t index, sb_value** out); /* GetValue: new reference */
+SB_API int32_t sb_value_sequence_elem_type(const sb_value* value);    /* GetSequenceElementType */
+
+/* ---- Measurement (no counterpart in the reference interface) ------------------------------ */
+/* Uploads the inputs once, replays the captured kernel sequence `iters` times after `warmup`
+ * replays, and writes the device time per run (ms, CUDA events) for each device used into
+ * ms_per_device[0..*n_devices). */
+SB_API int32_t sb_session_time_device(sb_session* session, int32_t n_inputs, const char* const* in_names,
+                               sb_value* const* in_values, int32_t warmup, int32_t iters,
+                               double* ms_per_device, int32_t capacity, int32_t* n_devices);
+/* Times every launch of device 0's plan separately; writes up to `capacity` entries. kinds receive
+ * pointers valid until the next call on this session. */
+SB_API int32_t sb_session_profile(sb_session* session, int32_t n_inputs, const char* const* in_names,
+                           sb_value* const* in_values, int32_t iters, const char** kinds, double* ms,
+                           int32_t capacity, int32_t* n_steps);
+/* Plan statistics for these inputs: kernel launches per run, tensor-core launches, algorithmic
+ * multiply-accumulates, device bytes (arena + weights), devices used. */
+SB_API int32_t sb_session_stats(sb_session* session, int32_t n_inputs, const char* const* in_names,
+                         sb_value* const* in_values, int64_t* launches, int64_t* tc_launches, double* macs,
+                         int64_t* device_bytes, int32_t* devices_used);
+
+/* ---- Diagnostics (no counterpart in the reference interface) ------------------------------- */
+/* Lowers and fuses the model on the host only (no device needed) for inputs given in session input
+ * order, and writes a summary (one line per device op, then "separable=0|1") into buf as a
+ * NUL-terminated string; *needed receives the full length + 1. */
+SB_API int32_t sb_debug_lower(const uint8_t* model, size_t model_len, int32_t n_inputs, sb_value* const* in_values,
+                              char* buf, size_t capacity, size_t* needed);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SHOROKOO_B200_H_ */

@@ -1,0 +1,335 @@
+// extern "C" entry points declared in include/shorokoo_b200.h.
+#include "../../include/shorokoo_b200.h"
+
+#include <cstring>
+#include <memory>
+#include <string>
+
+#include "session.h"
+
+namespace sb {
+void* host_alloc(size_t bytes, bool& pinned);
+void host_copy(void* dst, const void* src, size_t n);
+}  // namespace sb
+
+using sb::HostValue;
+
+struct sb_session {
+  std::unique_ptr<sb::Session> s;
+  std::vector<std::string> profile_kinds;
+};
+
+struct sb_value {
+  std::shared_ptr<HostValue> v;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int32_t set_error(int32_t code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+template <typename F>
+int32_t guarded(F&& f) {
+  try {
+    g_last_error.clear();
+    return f();
+  } catch (const sb::Error& e) {
+    return set_error(e.code, e.what());
+  } catch (const std::bad_alloc&) {
+    return set_error(SB_STATUS_OUT_OF_MEMORY, "host out of memory");
+  } catch (const std::exception& e) {
+    return set_error(SB_STATUS_INTERNAL, e.what());
+  }
+}
+
+std::vector<int64_t> shape_of(const int64_t* shape, int32_t rank) {
+  SB_CHECK(rank >= 0 && rank <= 16, sb::SB_INVALID_ARGUMENT, "rank out of range");
+  SB_CHECK(rank == 0 || shape != nullptr, sb::SB_INVALID_ARGUMENT, "shape is null");
+  std::vector<int64_t> s(shape, shape + rank);
+  for (int64_t d : s) SB_CHECK(d >= 0, sb::SB_INVALID_ARGUMENT, "negative dimension");
+  return s;
+}
+
+std::vector<std::shared_ptr<HostValue>> ordered_inputs(const sb::Session& s, int32_t n, const char* const* names,
+                                                       sb_value* const* vals) {
+  const auto& want = s.input_names();
+  SB_CHECK(n >= 0 && (n == 0 || (names && vals)), sb::SB_INVALID_ARGUMENT, "null input arrays");
+  std::vector<std::shared_ptr<HostValue>> out(want.size());
+  for (int32_t i = 0; i < n; ++i) {
+    SB_CHECK(names[i] && vals[i], sb::SB_INVALID_ARGUMENT, "null input name or value");
+    size_t k = 0;
+    while (k < want.size() && want[k] != names[i]) ++k;
+    SB_CHECK(k < want.size(), sb::SB_INVALID_ARGUMENT, std::string("unknown input '") + names[i] + "'");
+    SB_CHECK(!out[k], sb::SB_INVALID_ARGUMENT, std::string("input '") + names[i] + "' given twice");
+    out[k] = vals[i]->v;
+  }
+  for (size_t k = 0; k < want.size(); ++k)
+    SB_CHECK(out[k] != nullptr, sb::SB_INVALID_ARGUMENT, "missing input '" + want[k] + "'");
+  return out;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t sb_version(void) { return 100; }
+
+const char* sb_last_error(void) { return g_last_error.c_str(); }
+
+int32_t sb_session_create_ex(const uint8_t* model, size_t len, int32_t, int32_t, int32_t num_devices,
+                             int32_t first_device, sb_session** out) {
+  return guarded([&] {
+    SB_CHECK(out != nullptr, sb::SB_INVALID_ARGUMENT, "out is null");
+    *out = nullptr;
+    sb::SessionOptions o;
+    o.num_devices = num_devices;
+    o.first_device = first_device;
+    auto s = std::make_unique<sb_session>();
+    s->s = std::make_unique<sb::Session>(model, len, o);
+    *out = s.release();
+    return SB_STATUS_OK;
+  });
+}
+
+int32_t sb_session_create(const uint8_t* model, size_t len, int32_t opt, int32_t sev, sb_session** out) {
+  return sb_session_create_ex(model, len, opt, sev, 0, 0, out);
+}
+
+void sb_session_destroy(sb_session* s) { delete s; }
+
+int32_t sb_session_input_count(const sb_session* s) { return s ? int32_t(s->s->input_names().size()) : 0; }
+const char* sb_session_input_name(const sb_session* s, int32_t i) {
+  if (!s || i < 0 || size_t(i) >= s->s->input_names().size()) return nullptr;
+  return s->s->input_names()[size_t(i)].c_str();
+}
+int32_t sb_session_output_count(const sb_session* s) { return s ? int32_t(s->s->output_names().size()) : 0; }
+const char* sb_session_output_name(const sb_session* s, int32_t i) {
+  if (!s || i < 0 || size_t(i) >= s->s->output_names().size()) return nullptr;
+  return s->s->output_names()[size_t(i)].c_str();
+}
+
+int32_t sb_session_run(sb_session* s, int32_t n_in, const char* const* in_names, sb_value* const* in_values,
+                       int32_t n_out, const char* const* out_names, sb_value** out_values) {
+  return guarded([&] {
+    SB_CHECK(s != nullptr, sb::SB_INVALID_ARGUMENT, "session is null");
+    SB_CHECK(n_out >= 0 && (n_out == 0 || (out_names && out_values)), sb::SB_INVALID_ARGUMENT, "null output arrays");
+    for (int32_t j = 0; j < n_out; ++j) out_values[j] = nullptr;
+    auto ins = ordered_inputs(*s->s, n_in, in_names, in_values);
+    const auto& onames = s->s->output_names();
+    std::vector<int> idx;
+    for (int32_t j = 0; j < n_out; ++j) {
+      SB_CHECK(out_names[j] != nullptr, sb::SB_INVALID_ARGUMENT, "null output name");
+      size_t k = 0;
+      while (k < onames.size() && onames[k] != out_names[j]) ++k;
+      SB_CHECK(k < onames.size(), sb::SB_INVALID_ARGUMENT, std::string("unknown output '") + out_names[j] + "'");
+      idx.push_back(int(k));
+    }
+    auto outs = s->s->run(ins, idx);
+    for (int32_t j = 0; j < n_out; ++j) out_values[j] = new sb_value{outs[size_t(j)]};
+    return SB_STATUS_OK;
+  });
+}
+
+int32_t sb_value_create_tensor(int32_t et, const int64_t* shape, int32_t rank, const void* data, size_t nbytes,
+                               sb_value** out) {
+  return guarded([&] {
+    SB_CHECK(out != nullptr, sb::SB_INVALID_ARGUMENT, "out is null");
+    *out = nullptr;
+    SB_CHECK(et != sb::DT_STRING, sb::SB_INVALID_ARGUMENT,
+             "String tensors are variable-length and not byte-stride; use sb_value_create_string_tensor");
+    SB_CHECK(sb::dtype_size(et) != 0, sb::SB_UNSUPPORTED, "element type " + std::to_string(et) + " is not supported");
+    auto s = shape_of(shape, rank);
+    auto v = HostValue::alloc_tensor(et, s);
+    SB_CHECK(nbytes == v->nbytes, sb::SB_INVALID_ARGUMENT,
+             "data is " + std::to_string(nbytes) + " bytes but shape " + sb::shape_str(s) + " needs " +
+                 std::to_string(v->nbytes));
+    SB_CHECK(nbytes == 0 || data != nullptr, sb::SB_INVALID_ARGUMENT, "data is null");
+    if (nbytes) sb::host_copy(v->data, data, nbytes);
+    *out = new sb_value{v};
+    return SB_STATUS_OK;
+  });
+}
+
+int32_t sb_value_wrap_tensor(int32_t et, const int64_t* shape, int32_t rank, void* data, size_t nbytes, sb_value** out) {
+  return guarded([&] {
+    SB_CHECK(out != nullptr, sb::SB_INVALID_ARGUMENT, "out is null");
+    *out = nullptr;
+    SB_CHECK(sb::dtype_size(et) != 0 && et != sb::DT_STRING, sb::SB_UNSUPPORTED,
+             "element type " + std::to_string(et) + " is not supported");
+    auto s = shape_of(shape, rank);
+    auto v = std::make_shared<HostValue>();
+    v->elem_type = et;
+    v->shape = s;
+    v->nbytes = size_t(sb::numel(s)) * sb::dtype_size(et);
+    SB_CHECK(nbytes == v->nbytes, sb::SB_INVALID_ARGUMENT, "data size does not match shape " + sb::shape_str(s));
+    SB_CHECK(nbytes == 0 || data != nullptr, sb::SB_INVALID_ARGUMENT, "data is null");
+    v->data = data;
+    v->owned = false;
+    *out = new sb_value{v};
+    return SB_STATUS_OK;
+  });
+}
+
+int32_t sb_value_create_string_tensor(const char* const* strings, size_t count, const int64_t* shape, int32_t rank,
+                                      sb_value** out) {
+  return guarded([&] {
+    SB_CHECK(out != nullptr, sb::SB_INVALID_ARGUMENT, "out is null");
+    *out = nullptr;
+    auto s = shape_of(shape, rank);
+    SB_CHECK(int64_t(count) == sb::numel(s), sb::SB_INVALID_ARGUMENT, "string count does not match shape");
+    auto v = std::make_shared<HostValue>();
+    v->elem_type = sb::DT_STRING;
+    v->shape = s;
+    for (size_t i = 0; i < count; ++i) {
+      SB_CHECK(strings && strings[i], sb::SB_INVALID_ARGUMENT, "null string");
+      v->strings.emplace_back(strings[i]);
+    }
+    *out = new sb_value{v};
+    return SB_STATUS_OK;
+  });
+}
+
+int32_t sb_value_create_sequence(sb_value* const* values, size_t count, sb_value** out) {
+  return guarded([&] {
+    SB_CHECK(out != nullptr, sb::SB_INVALID_ARGUMENT, "out is null");
+    *out = nullptr;
+    auto v = std::make_shared<HostValue>();
+    v->kind = HostValue::SEQUENCE;
+    for (size_t i = 0; i < count; ++i) {
+      SB_CHECK(values && values[i], sb::SB_INVALID_ARGUMENT, "null sequence element");
+      SB_CHECK(values[i]->v->kind == HostValue::TENSOR, sb::SB_UNSUPPORTED, "sequences of sequences are not supported");
+      if (i) SB_CHECK(values[i]->v->elem_type == v->items[0]->elem_type, sb::SB_INVALID_ARGUMENT,
+                      "sequence elements must share an element type");
+      v->items.push_back(values[i]->v);
+    }
+    v->elem_type = v->items.empty() ? sb::DT_UNDEFINED : v->items[0]->elem_type;
+    *out = new sb_value{v};
+    return SB_STATUS_OK;
+  });
+}
+
+void sb_value_release(sb_value* v) { delete v; }
+
+int32_t sb_value_type(const sb_value* v) { return v ? v->v->kind : 0; }
+int32_t sb_value_elem_type(const sb_value* v) { return v ? v->v->elem_type : 0; }
+int32_t sb_value_rank(const sb_value* v) { return v ? int32_t(v->v->shape.size()) : 0; }
+const int64_t* sb_value_shape(const sb_value* v) { return v ? v->v->shape.data() : nullptr; }
+void* sb_value_data(sb_value* v) { return v ? v->v->data : nullptr; }
+size_t sb_value_nbytes(const sb_value* v) { return v ? v->v->nbytes : 0; }
+size_t sb_value_string_count(const sb_value* v) { return v ? v->v->strings.size() : 0; }
+const char* sb_value_string_at(const sb_value* v, size_t i) {
+  if (!v || i >= v->v->strings.size()) return nullptr;
+  return v->v->strings[i].c_str();
+}
+int32_t sb_value_count(const sb_value* v) { return v ? int32_t(v->v->items.size()) : 0; }
+int32_t sb_value_at(const sb_value* v, int32_t i, sb_value** out) {
+  return guarded([&] {
+    SB_CHECK(v && out && i >= 0 && size_t(i) < v->v->items.size(), sb::SB_INVALID_ARGUMENT, "index out of range");
+    *out = new sb_value{v->v->items[size_t(i)]};
+    return SB_STATUS_OK;
+  });
+}
+int32_t sb_value_sequence_elem_type(const sb_value* v) {
+  return v && v->v->kind == HostValue::SEQUENCE ? v->v->elem_type : 0;
+}
+
+int32_t sb_session_time_device(sb_session* s, int32_t n_in, const char* const* in_names, sb_value* const* in_values,
+                               int32_t warmup, int32_t iters, double* ms, int32_t capacity, int32_t* n_dev) {
+  return guarded([&] {
+    SB_CHECK(s && ms && n_dev && iters > 0, sb::SB_INVALID_ARGUMENT, "bad arguments");
+    auto ins = ordered_inputs(*s->s, n_in, in_names, in_values);
+    auto r = s->s->time_device(ins, warmup, iters);
+    *n_dev = int32_t(r.size());
+    for (size_t i = 0; i < r.size() && int32_t(i) < capacity; ++i) ms[i] = r[i];
+    return SB_STATUS_OK;
+  });
+}
+
+int32_t sb_session_profile(sb_session* s, int32_t n_in, const char* const* in_names, sb_value* const* in_values,
+                           int32_t iters, const char** kinds, double* ms, int32_t capacity, int32_t* n_steps) {
+  return guarded([&] {
+    SB_CHECK(s && kinds && ms && n_steps && iters > 0, sb::SB_INVALID_ARGUMENT, "bad arguments");
+    auto ins = ordered_inputs(*s->s, n_in, in_names, in_values);
+    auto r = s->s->profile_steps(ins, iters);
+    s->profile_kinds.clear();
+    for (auto& p : r) s->profile_kinds.push_back(p.first);
+    *n_steps = int32_t(r.size());
+    for (size_t i = 0; i < r.size() && int32_t(i) < capacity; ++i) {
+      kinds[i] = s->profile_kinds[i].c_str();
+      ms[i] = r[i].second;
+    }
+    return SB_STATUS_OK;
+  });
+}
+
+int32_t sb_session_stats(sb_session* s, int32_t n_in, const char* const* in_names, sb_value* const* in_values,
+                         int64_t* launches, int64_t* tc, double* macs, int64_t* dev_bytes, int32_t* devices) {
+  return guarded([&] {
+    SB_CHECK(s != nullptr, sb::SB_INVALID_ARGUMENT, "session is null");
+    auto ins = ordered_inputs(*s->s, n_in, in_names, in_values);
+    auto st = s->s->stats(ins);
+    if (launches) *launches = st.kernels;
+    if (tc) *tc = st.tc_kernels;
+    if (macs) *macs = st.macs;
+    if (dev_bytes) *dev_bytes = int64_t(st.arena_bytes + st.weight_bytes);
+    if (devices) *devices = s->s->devices_used(ins);
+    return SB_STATUS_OK;
+  });
+}
+
+int32_t sb_debug_lower(const uint8_t* model, size_t len, int32_t n_in, sb_value* const* in_values, char* buf,
+                       size_t cap, size_t* needed) {
+  return guarded([&] {
+    sb::OnnxModel m = sb::parse_onnx(model, len);
+    sb::check_supported_ops(m);
+    std::vector<sb::InputSpec> specs;
+    for (int32_t i = 0; i < n_in; ++i) {
+      SB_CHECK(in_values && in_values[i], sb::SB_INVALID_ARGUMENT, "null input value");
+      const HostValue& v = *in_values[i]->v;
+      sb::InputSpec s;
+      s.dtype = v.elem_type;
+      s.shape = v.shape;
+      if (sb::numel(v.shape) <= sb::kPlanTimeInputMaxElems) {
+        auto h = std::make_shared<sb::HostTensor>(v.elem_type, v.shape);
+        if (v.nbytes) std::memcpy(h->mutable_data(), v.data, v.nbytes);
+        s.value = h;
+      }
+      specs.push_back(s);
+    }
+    sb::LGraph g = sb::lower(m, specs);
+    sb::fuse(g);
+    std::string out;
+    for (const sb::Op& op : g.ops) {
+      if (op.dead) continue;
+      out += op.type;
+      for (int id : op.in)
+        if (id >= 0) out += " " + sb::shape_str(g.vals[size_t(id)].shape) + (g.vals[size_t(id)].is_host ? "h" : "");
+      out += " ->";
+      for (int id : op.out) out += " " + sb::shape_str(g.vals[size_t(id)].shape);
+      if (op.type == "FusedConv")
+        out += " k=" + std::to_string(op.kernel[0]) + "x" + std::to_string(op.kernel[1]) + " s=" +
+               std::to_string(op.strides[0]) + " pads=" + sb::shape_str(op.pads);
+      if (op.act) out += " act=" + std::to_string(op.act);
+      if (op.residual >= 0) out += " residual=" + std::to_string(op.residual_mode);
+      out += "\n";
+    }
+    for (size_t j = 0; j < g.outputs.size(); ++j) {
+      const sb::Value& v = g.vals[size_t(g.outputs[j])];
+      out += "output " + sb::shape_str(v.shape) + (v.is_host ? " host" : " device") + "\n";
+    }
+    out += std::string("separable=") + (sb::batch_separable(g) ? "1" : "0") + "\n";
+    if (needed) *needed = out.size() + 1;
+    if (buf && cap) {
+      size_t n = std::min(cap - 1, out.size());
+      std::memcpy(buf, out.data(), n);
+      buf[n] = 0;
+    }
+    return SB_STATUS_OK;
+  });
+}
+
+}  // extern "C"

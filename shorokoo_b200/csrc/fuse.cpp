@@ -1,0 +1,332 @@
+// Pattern fusion on the lowered graph.
+//
+//  Conv  [Pad folded into pads]  -> (Mul|Add|Sub|Div by per-channel constants)*  -> [Add residual]
+//        -> [Relu|Sigmoid]                                          => FusedConv
+//    The per-channel chain is the reference's inference-mode FrozenBatchNorm, emitted as primitive
+//    ops over initializers (samples/RetinaNet/ResNet.cs:177-201): y = x*scale + shift with
+//    scale = w / sqrt(var + eps), shift = b - mean*scale. It is folded into the conv weights and
+//    bias in double precision: W' = W*scale, b' = b*scale + shift.
+//    The residual may be a same-shape tensor (ResNet.cs:280-329) or the nearest-2x Resize of a
+//    coarser map (FPN top-down add, RetinaNetDetector.cs:375-384,401-450).
+//  MatMul(x, W^T constant) / Gemm -> (+bias) -> [Relu|Sigmoid]  => FusedGemm
+//    (Linear, src/Shorokoo.Modules/Layers/Linear.cs:25-39; DenseBasic, ResNet.cs:102-125).
+//
+// A fused op takes the slot of the last op it absorbed, so operands that the original graph
+// computes later (e.g. the projection shortcut of a bottleneck) are ready when it runs.
+#include <algorithm>
+#include <cmath>
+
+#include "ir.h"
+
+namespace sb {
+
+namespace {
+
+struct Consumers {
+  std::vector<std::vector<int>> ops;   // per value: live consumer op indices
+  std::vector<bool> is_output;
+};
+
+Consumers consumers(const LGraph& g) {
+  Consumers c;
+  c.ops.assign(g.vals.size(), {});
+  c.is_output.assign(g.vals.size(), false);
+  for (size_t i = 0; i < g.ops.size(); ++i) {
+    const Op& op = g.ops[i];
+    if (op.dead) continue;
+    for (int id : op.in)
+      if (id >= 0) c.ops[size_t(id)].push_back(int(i));
+    if (op.residual >= 0) c.ops[size_t(op.residual)].push_back(int(i));
+  }
+  for (int id : g.outputs) c.is_output[size_t(id)] = true;
+  return c;
+}
+
+// Host tensor that broadcasts against an output of `rank` dims and varies at most along `axis`
+// (size `len`); returns the per-index values (length len).
+bool per_axis_values(const HostTensor& h, size_t rank, size_t axis, int64_t len, std::vector<double>& out) {
+  if (h.shape.size() > rank) return false;
+  size_t off = rank - h.shape.size();
+  int64_t along = 1;
+  for (size_t i = 0; i < h.shape.size(); ++i) {
+    size_t d = i + off;
+    if (d == axis) {
+      along = h.shape[i];
+      if (along != 1 && along != len) return false;
+    } else if (h.shape[i] != 1) {
+      return false;
+    }
+  }
+  out.resize(size_t(len));
+  for (int64_t m = 0; m < len; ++m) out[size_t(m)] = h.get_f64(along == 1 ? 0 : m);
+  return true;
+}
+
+std::shared_ptr<HostTensor> to_f32(const HostTensor& h) {
+  auto o = std::make_shared<HostTensor>(DT_FLOAT, h.shape);
+  if (h.dtype == DT_FLOAT) {
+    std::memcpy(o->mutable_data(), h.data(), h.nbytes());
+  } else {
+    float* p = o->mptr<float>();
+    for (int64_t i = 0; i < h.numel(); ++i) p[i] = float(h.get_f64(i));
+  }
+  return o;
+}
+
+// Resize that maps output index o to floor(o/2) on the two spatial axes and is identity elsewhere.
+bool is_nearest_up2(const Op& r, const LGraph& g) {
+  if (r.type != "Resize" || r.dead) return false;
+  if (r.scales.size() != 4 || r.scales[0] != 1.f || r.scales[1] != 1.f || r.scales[2] != 2.f || r.scales[3] != 2.f)
+    return false;
+  const auto& xs = g.vals[size_t(r.in[0])].shape;
+  const auto& ys = g.vals[size_t(r.out[0])].shape;
+  if (xs.size() != 4 || ys[2] != 2 * xs[2] || ys[3] != 2 * xs[3]) return false;
+  bool hp = r.coord_mode == "half_pixel" || r.coord_mode == "pytorch_half_pixel";
+  bool asym = r.coord_mode == "asymmetric";
+  if (hp) return r.nearest_mode == "round_prefer_floor";
+  if (asym) return r.nearest_mode == "floor" || r.nearest_mode == "round_prefer_floor";
+  return false;
+}
+
+}  // namespace
+
+void fuse(LGraph& g) {
+  // ---------------- Conv chains ----------------
+  for (size_t ci = 0; ci < g.ops.size(); ++ci) {
+    if (g.ops[ci].dead || g.ops[ci].type != "Conv") continue;
+    Consumers C = consumers(g);
+    Op conv = g.ops[ci];
+    int x = conv.in[0];
+    // Fold a zero constant Pad on the spatial axes into the conv padding (ResNet stem, ResNet.cs:364).
+    const Value& xv = g.vals[size_t(x)];
+    if (xv.producer >= 0) {
+      const Op& p = g.ops[size_t(xv.producer)];
+      if (!p.dead && p.type == "Pad" && p.alpha == 0.f && p.pads.size() == 8 && p.pads[0] == 0 && p.pads[1] == 0 &&
+          p.pads[4] == 0 && p.pads[5] == 0 && C.ops[size_t(x)].size() == 1 && !C.is_output[size_t(x)]) {
+        conv.pads[0] += p.pads[2];
+        conv.pads[1] += p.pads[3];
+        conv.pads[2] += p.pads[6];
+        conv.pads[3] += p.pads[7];
+        g.ops[size_t(xv.producer)].dead = true;
+        x = p.in[0];
+      }
+    }
+    const HostTensor& W = *g.vals[size_t(conv.in[1])].host;
+    const int64_t M = W.shape[0];
+    Op f;
+    f.type = "FusedConv";
+    f.name = conv.name;
+    f.in = {x};
+    f.kernel = conv.kernel;
+    f.strides = conv.strides;
+    f.pads = conv.pads;
+    f.dilations = conv.dilations;
+    f.group = conv.group;
+    f.weight = to_f32(W);
+    f.bias = std::make_shared<HostTensor>(DT_FLOAT, std::vector<int64_t>{M});
+    std::vector<double> scale(size_t(M), 1.0), shift(size_t(M), 0.0);
+    if (conv.in.size() > 2 && conv.in[2] >= 0) {
+      const HostTensor& b = *g.vals[size_t(conv.in[2])].host;
+      SB_CHECK(b.numel() == M, SB_SHAPE_ERROR, "Conv: bias length mismatch");
+      for (int64_t m = 0; m < M; ++m) shift[size_t(m)] = b.get_f64(m);
+    }
+    int cur = conv.out[0];
+    int slot = int(ci);
+    std::vector<int> absorbed;
+    while (true) {
+      if (C.is_output[size_t(cur)] || C.ops[size_t(cur)].size() != 1) break;
+      int oi = C.ops[size_t(cur)][0];
+      const Op& o = g.ops[size_t(oi)];
+      if (o.residual >= 0) break;
+      auto other_of = [&](const Op& op) { return op.in[0] == cur ? op.in[1] : op.in[0]; };
+      bool done = false;
+      if ((o.type == "Mul" || o.type == "Add" || o.type == "Sub" || o.type == "Div") && o.in.size() == 2 &&
+          f.residual < 0 && f.act == 0) {
+        int other = other_of(o);
+        const Value& ov = g.vals[size_t(other)];
+        std::vector<double> v;
+        if (ov.is_host && per_axis_values(*ov.host, 4, 1, M, v) &&
+            g.vals[size_t(o.out[0])].shape == g.vals[size_t(cur)].shape) {
+          bool cur_first = o.in[0] == cur;
+          for (int64_t m = 0; m < M; ++m) {
+            double k = v[size_t(m)];
+            if (o.type == "Mul") {
+              scale[size_t(m)] *= k;
+              shift[size_t(m)] *= k;
+            } else if (o.type == "Add") {
+              shift[size_t(m)] += k;
+            } else if (o.type == "Sub") {
+              if (cur_first) {
+                shift[size_t(m)] -= k;
+              } else {
+                scale[size_t(m)] = -scale[size_t(m)];
+                shift[size_t(m)] = k - shift[size_t(m)];
+              }
+            } else {   // Div
+              if (!cur_first) { done = true; break; }
+              scale[size_t(m)] /= k;
+              shift[size_t(m)] /= k;
+            }
+          }
+          if (done) break;
+          absorbed.push_back(oi);
+          cur = o.out[0];
+          slot = oi;
+          continue;
+        }
+        if (o.type == "Add" && !ov.is_host && f.residual < 0) {
+          if (ov.shape == g.vals[size_t(cur)].shape) {
+            f.residual = other;
+            f.residual_mode = 0;
+            absorbed.push_back(oi);
+            cur = o.out[0];
+            slot = oi;
+            continue;
+          }
+          if (ov.producer >= 0 && is_nearest_up2(g.ops[size_t(ov.producer)], g) &&
+              g.vals[size_t(o.out[0])].shape == g.vals[size_t(cur)].shape) {
+            const Op& rz = g.ops[size_t(ov.producer)];
+            f.residual = rz.in[0];
+            f.residual_mode = 1;
+            absorbed.push_back(oi);
+            cur = o.out[0];
+            slot = oi;
+            continue;
+          }
+        }
+        break;
+      }
+      if ((o.type == "Relu" || o.type == "Sigmoid") && f.act == 0) {
+        f.act = o.type == "Relu" ? 1 : 2;
+        absorbed.push_back(oi);
+        cur = o.out[0];
+        slot = oi;
+        continue;
+      }
+      break;
+    }
+    // Fold scale/shift into weights and bias.
+    const int64_t per = f.weight->numel() / std::max<int64_t>(M, 1);
+    float* wp = f.weight->mptr<float>();
+    float* bp = f.bias->mptr<float>();
+    for (int64_t m = 0; m < M; ++m) {
+      const double s = scale[size_t(m)];
+      if (s != 1.0)
+        for (int64_t j = 0; j < per; ++j) wp[m * per + j] = float(double(wp[m * per + j]) * s);
+      bp[m] = float(shift[size_t(m)]);
+    }
+    f.out = {cur};
+    g.ops[ci].dead = true;
+    for (int a : absorbed) g.ops[size_t(a)].dead = true;
+    g.vals[size_t(cur)].producer = slot;
+    g.ops[size_t(slot)] = f;
+  }
+
+  // ---------------- MatMul / Gemm chains ----------------
+  for (size_t mi = 0; mi < g.ops.size(); ++mi) {
+    Op& mm0 = g.ops[mi];
+    if (mm0.dead || (mm0.type != "MatMul" && mm0.type != "Gemm")) continue;
+    int bid = mm0.in[1];
+    if (bid < 0 || !g.vals[size_t(bid)].is_host) continue;   // device x device: planned as a generic GEMM
+    if (mm0.type == "Gemm" && mm0.axes[0] != 0) continue;        // transA: planned generically
+    Consumers C = consumers(g);
+    Op mm = mm0;
+    const HostTensor& B = *g.vals[size_t(bid)].host;
+    Op f;
+    f.type = "FusedGemm";
+    f.name = mm.name;
+    f.in = {mm.in[0]};
+    // W = [N, K]
+    bool b_is_nk = mm.type == "Gemm" && mm.axes[1] != 0;
+    if (!b_is_nk && B.transpose_src && !B.buf) {
+      f.weight = to_f32(*B.transpose_src);   // MatMul(x, Transpose(W)): use W directly
+    } else if (b_is_nk) {
+      f.weight = to_f32(B);
+    } else {
+      HostTensor bt = B;
+      auto t = std::make_shared<HostTensor>(B.dtype, std::vector<int64_t>{B.shape[1], B.shape[0]});
+      size_t es = dtype_size(B.dtype);
+      const uint8_t* s = bt.data();
+      uint8_t* d = t->mutable_data();
+      for (int64_t i = 0; i < B.shape[0]; ++i)
+        for (int64_t j = 0; j < B.shape[1]; ++j) std::memcpy(d + (j * B.shape[0] + i) * es, s + (i * B.shape[1] + j) * es, es);
+      f.weight = to_f32(*t);
+    }
+    const int64_t N = f.weight->shape[0];
+    f.bias = std::make_shared<HostTensor>(DT_FLOAT, std::vector<int64_t>{N});
+    std::vector<double> shift(size_t(N), 0.0), scale(size_t(N), 1.0);
+    if (mm.type == "Gemm") {
+      if (mm.alpha != 1.f)
+        for (auto& s : scale) s = mm.alpha;
+      if (mm.in.size() > 2 && mm.in[2] >= 0) {
+        const Value& cv = g.vals[size_t(mm.in[2])];
+        std::vector<double> v;
+        SB_CHECK(cv.is_host && per_axis_values(*cv.host, 2, 1, N, v), SB_UNSUPPORTED,
+                 "Gemm: bias must be a plan-time constant broadcast along columns");
+        for (int64_t n = 0; n < N; ++n) shift[size_t(n)] = double(mm.beta) * v[size_t(n)];
+      }
+    }
+    int cur = mm.out[0];
+    const size_t rank = g.vals[size_t(cur)].shape.size();
+    int slot = int(mi);
+    std::vector<int> absorbed;
+    while (true) {
+      if (C.is_output[size_t(cur)] || C.ops[size_t(cur)].size() != 1) break;
+      int oi = C.ops[size_t(cur)][0];
+      const Op& o = g.ops[size_t(oi)];
+      if (o.residual >= 0) break;
+      if ((o.type == "Add" || o.type == "Mul") && o.in.size() == 2 && f.act == 0 && f.residual < 0) {
+        int other = o.in[0] == cur ? o.in[1] : o.in[0];
+        const Value& ov = g.vals[size_t(other)];
+        std::vector<double> v;
+        if (ov.is_host && per_axis_values(*ov.host, rank, rank - 1, N, v) &&
+            g.vals[size_t(o.out[0])].shape == g.vals[size_t(cur)].shape) {
+          for (int64_t n = 0; n < N; ++n) {
+            if (o.type == "Add") {
+              shift[size_t(n)] += v[size_t(n)];
+            } else {
+              scale[size_t(n)] *= v[size_t(n)];
+              shift[size_t(n)] *= v[size_t(n)];
+            }
+          }
+          absorbed.push_back(oi);
+          cur = o.out[0];
+          slot = oi;
+          continue;
+        }
+        if (o.type == "Add" && !ov.is_host && ov.shape == g.vals[size_t(cur)].shape) {
+          f.residual = other;
+          absorbed.push_back(oi);
+          cur = o.out[0];
+          slot = oi;
+          continue;
+        }
+        break;
+      }
+      if ((o.type == "Relu" || o.type == "Sigmoid") && f.act == 0) {
+        f.act = o.type == "Relu" ? 1 : 2;
+        absorbed.push_back(oi);
+        cur = o.out[0];
+        slot = oi;
+        continue;
+      }
+      break;
+    }
+    const int64_t K = f.weight->shape[1];
+    float* wp = f.weight->mptr<float>();
+    float* bp = f.bias->mptr<float>();
+    for (int64_t n = 0; n < N; ++n) {
+      if (scale[size_t(n)] != 1.0)
+        for (int64_t k = 0; k < K; ++k) wp[n * K + k] = float(double(wp[n * K + k]) * scale[size_t(n)]);
+      bp[n] = float(shift[size_t(n)]);
+    }
+    f.out = {cur};
+    g.ops[mi].dead = true;
+    for (int a : absorbed) g.ops[size_t(a)].dead = true;
+    g.vals[size_t(cur)].producer = slot;
+    g.ops[size_t(slot)] = f;
+  }
+  g.dce();
+}
+
+}  // namespace sb

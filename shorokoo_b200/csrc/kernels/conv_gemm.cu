@@ -1,0 +1,572 @@
+// tcgen05 / TMEM implicit-GEMM kernel for sm_100a: dense MatMul+bias(+ReLU) and Conv2d (folded
+// BatchNorm, fused residual add / nearest-2x upsampled residual, ReLU or Sigmoid epilogue).
+//
+// Persistent, warp-specialised CTA (one per SM):
+//   warp 0      TMA producer: B tiles (weights), and A tiles when A is a plain row matrix
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16 per instr)
+//   warps 2-5   epilogue: tcgen05.ld accumulator -> bias / residual / activation -> global
+//   warps 6-9   (spatial convs) im2col gather producers: cp.async 16B/8B with zero fill, written
+//               into the 128B-swizzled K-major layout the UMMA smem descriptor expects
+// Operand tiles are BM=128 x BK=64 bf16 (one 128-byte swizzle atom per row); the fp32 accumulator
+// is double-buffered in TMEM so the epilogue of tile i overlaps the main loop of tile i+1.
+// Every mbarrier wait is bounded (global timer); a timeout sets a device error word and the CTA
+// drains and frees its TMEM instead of hanging.
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <stdexcept>
+
+#include "kernels.h"
+
+namespace sb {
+namespace k {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr uint64_t kWaitTimeoutNs = 4000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait on an mbarrier phase. Returns false if this CTA is aborting (timeout here or in
+// another role); the first timeout records `code` in the device error word.
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned int* err,
+                                       unsigned int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  uint32_t it = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++it & 127u) == 0) {
+      if (*abort_flag) return false;
+      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+        *abort_flag = 1;
+        if (err) atomicOr(err, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(tm), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_8(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* holder, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D(tmem) (+)= A(smem) * B(smem)^T, kind::f16 (bf16 operands, f32 accumulate).
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// UMMA shared-memory descriptor for a K-major tile with 128-byte swizzle: rows of 128 B, 8-row
+// core groups 1024 B apart (SBO), descriptor version 1 (sm_100), layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr & 0x3FFFFu) >> 4);
+  d |= uint64_t(1) << 16;                 // LBO (unused for swizzled K-major)
+  d |= uint64_t(1024 >> 4) << 32;         // SBO
+  d |= uint64_t(1) << 46;                 // version
+  d |= uint64_t(2) << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: D f32, A/B bf16, both K-major, N>>3 at bit 17, M>>4 at bit 24.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+
+template <int BN>
+struct Cfg {
+  static constexpr int STAGES = BN == 64 ? 8 : (BN == 128 ? 6 : 4);
+  static constexpr uint32_t A_BYTES = BM * BK * 2;
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+};
+
+__device__ __forceinline__ float act_apply(float v, int act) {
+  if (act == 1) return v > 0.f ? v : 0.f;
+  if (act == 2) return 1.f / (1.f + __expf(-v));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Epilogue for one 32-column chunk of one accumulator row.
+__device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint32_t (&r)[32], int m, int n0) {
+  float v[32];
+  const float4* b4 = reinterpret_cast<const float4*>(a.bias + n0);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float4 bb = __ldg(b4 + j);
+    v[4 * j + 0] = __uint_as_float(r[4 * j + 0]) + bb.x;
+    v[4 * j + 1] = __uint_as_float(r[4 * j + 1]) + bb.y;
+    v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + bb.z;
+    v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + bb.w;
+  }
+  const int ncols = min(32, a.Cout - n0);
+  if (a.res) {
+    int64_t rrow = m;
+    if (a.res_mode == 1) {
+      int hw = a.Ho * a.Wo;
+      int n = m / hw, rem = m - n * hw;
+      int ho = rem / a.Wo, wo = rem - ho * a.Wo;
+      rrow = (int64_t(n) * a.Hr + (ho >> 1)) * a.Wr + (wo >> 1);
+    }
+    if (a.res_bf16) {
+      const __nv_bfloat16* rp = reinterpret_cast<const __nv_bfloat16*>(a.res) + rrow * a.ldr + n0;
+      if (ncols == 32 && (reinterpret_cast<uintptr_t>(rp) & 15) == 0) {
+        const uint4* r4 = reinterpret_cast<const uint4*>(rp);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 q = __ldg(r4 + j);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            float2 f = __bfloat1622float2(h[t]);
+            v[8 * j + 2 * t] += f.x;
+            v[8 * j + 2 * t + 1] += f.y;
+          }
+        }
+      } else {
+        for (int j = 0; j < ncols; ++j) v[j] += __bfloat162float(rp[j]);
+      }
+    } else {
+      const float* rp = reinterpret_cast<const float*>(a.res) + rrow * a.ldr + n0;
+      if (ncols == 32 && (reinterpret_cast<uintptr_t>(rp) & 15) == 0) {
+        const float4* r4 = reinterpret_cast<const float4*>(rp);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float4 q = __ldg(r4 + j);
+          v[4 * j] += q.x;
+          v[4 * j + 1] += q.y;
+          v[4 * j + 2] += q.z;
+          v[4 * j + 3] += q.w;
+        }
+      } else {
+        for (int j = 0; j < ncols; ++j) v[j] += rp[j];
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = act_apply(v[j], a.act);
+
+  int64_t orow = a.group_rows ? (int64_t(m / a.group_rows) * a.group_stride + int64_t(m % a.group_rows) * a.ldo)
+                              : int64_t(m) * a.ldo;
+  if (a.out_bf16) {
+    __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(a.out) + orow + n0;
+    if (ncols == 32 && (reinterpret_cast<uintptr_t>(op) & 15) == 0) {
+      uint4* o4 = reinterpret_cast<uint4*>(op);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 q;
+        q.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+        q.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+        q.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+        q.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+        o4[j] = q;
+      }
+    } else {
+      for (int j = 0; j < ncols; ++j) op[j] = __float2bfloat16_rn(v[j]);
+    }
+  } else {
+    float* op = reinterpret_cast<float*>(a.out) + orow + n0;
+    if (ncols == 32 && (reinterpret_cast<uintptr_t>(op) & 15) == 0) {
+      float4* o4 = reinterpret_cast<float4*>(op);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+      for (int j = 0; j < ncols; ++j) op[j] = v[j];
+    }
+  }
+}
+
+// MODE 0: A via TMA; MODE 1: im2col gather in 16-byte units (Cp % 8 == 0); MODE 2: 8-byte units (Cp == 4).
+template <int BN, int MODE>
+__global__ void __launch_bounds__(MODE ? 320 : 192, 1)
+    conv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const ConvGemmArgs a) {
+  using C = Cfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;
+  uint64_t* acce = accf + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acce + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], MODE ? 129u : 1u);
+      mbar_init(&empty[s], 1u);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf[i], 1u);
+      mbar_init(&acce[i], 128u);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    if (MODE == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int tiles_m = (a.M + BM - 1) / BM;
+  const int tiles_n = (a.Cout + BN - 1) / BN;
+  const int total = tiles_m * tiles_n;
+  const int KT = a.Kpad / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        const int mt = t / tiles_n, nt = t - (t / tiles_n) * tiles_n;
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) goto producer_done;
+          mbar_expect_tx(&full[stage], (MODE == 0 ? C::A_BYTES : 0u) + C::B_BYTES);
+          if (MODE == 0) tma_load_2d(sA + stage * C::A_BYTES, &tmA, kt * BK, mt * BM, &full[stage]);
+          tma_load_2d(sB + stage * C::B_BYTES, &tmB, kt * BK, nt * BN, &full[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t aph = uint32_t(it >> 1) & 1u;
+        if (!mbar_wait(&acce[acc], aph ^ 1u, abort_flag, a.err, 2u)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        bool ok = true;
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, a.err, 4u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (MODE) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          const uint64_t ad = sw128_desc(smem_u32(sA + stage * C::A_BYTES));
+          const uint64_t bd = sw128_desc(smem_u32(sB + stage * C::B_BYTES));
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16(d_tmem, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), idesc, (kt | kk) != 0 ? 1u : 0u);
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&accf[acc]);
+      }
+    }
+  } else if (warp < 6) {
+    const int q = warp & 3;   // TMEM lane quarter this warp may access
+    int it = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+      const int mt = t / tiles_n, nt = t - (t / tiles_n) * tiles_n;
+      const int acc = it & 1;
+      const uint32_t aph = uint32_t(it >> 1) & 1u;
+      if (!mbar_wait(&accf[acc], aph, abort_flag, a.err, 8u)) break;
+      tc_fence_after();
+      const int m = mt * BM + q * 32 + lane;
+      const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + uint32_t(c * 32), r);
+        const int n0 = nt * BN + c * 32;
+        if (n0 < a.Cout && m < a.M) epilogue_chunk(a, r, m, n0);
+      }
+      tc_fence_before();
+      mbar_arrive(&acce[acc]);
+    }
+  } else if (MODE != 0) {
+    // ---- im2col gather producers -------------------------------------------------------------
+    const int gt = threadIdx.x - 192;   // 0..127
+    constexpr int TPR = MODE == 1 ? 8 : 16;          // threads per 128-byte row
+    constexpr int ROWS_PER_PASS = 128 / TPR;         // 16 or 8
+    constexpr int PASSES = BM / ROWS_PER_PASS;       // 8 or 16
+    const int sub = gt % TPR;
+    const int rbase = gt / TPR;
+    const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(a.x);
+    const int hw_out = a.Ho * a.Wo;
+    const int ktaps = a.KH * a.KW;
+    const int kreal = ktaps * a.Cp;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const int mt = t / tiles_n;
+      int hb[PASSES], wb[PASSES];
+      int64_t base[PASSES];
+#pragma unroll
+      for (int i = 0; i < PASSES; ++i) {
+        const int m = mt * BM + rbase + i * ROWS_PER_PASS;
+        if (m < a.M) {
+          const int n = m / hw_out, rem = m - n * hw_out;
+          const int ho = rem / a.Wo, wo = rem - ho * a.Wo;
+          hb[i] = ho * a.sh - a.ph;
+          wb[i] = wo * a.sw - a.pw;
+          base[i] = int64_t(n) * a.H * a.W * a.Cp;
+        } else {
+          hb[i] = -(1 << 28);   // forces every tap out of range
+          wb[i] = 0;
+          base[i] = 0;
+        }
+      }
+      for (int kt = 0; kt < KT; ++kt) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 16u)) goto gather_done;
+        const uint32_t sbase = smem_u32(sA + stage * C::A_BYTES);
+        if (MODE == 1) {
+          const int kidx = kt * BK + sub * 8;
+          const int tap = kidx / a.Cp;
+          const int c = kidx - tap * a.Cp;
+          const int kh = tap / a.KW, kw = tap - (tap / a.KW) * a.KW;
+          const bool kvalid = kidx < kreal;
+          const int dh = kh * a.dh, dw = kw * a.dw;
+#pragma unroll
+          for (int i = 0; i < PASSES; ++i) {
+            const int r = rbase + i * ROWS_PER_PASS;
+            const int hi = hb[i] + dh, wi = wb[i] + dw;
+            const bool ok = kvalid && hi >= 0 && hi < a.H && wi >= 0 && wi < a.W;
+            const __nv_bfloat16* src = ok ? x + base[i] + (int64_t(hi) * a.W + wi) * a.Cp + c : x;
+            const uint32_t dst = sbase + uint32_t(r * 128 + ((sub ^ (r & 7)) << 4));
+            cp_async_16(dst, src, ok ? 16u : 0u);
+          }
+        } else {
+          const int tap = kt * (BK / 4) + sub;   // Cp == 4: one tap per 8-byte unit
+          const int kh = tap / a.KW, kw = tap - (tap / a.KW) * a.KW;
+          const bool kvalid = tap < ktaps;
+          const int dh = kh * a.dh, dw = kw * a.dw;
+#pragma unroll
+          for (int i = 0; i < PASSES; ++i) {
+            const int r = rbase + i * ROWS_PER_PASS;
+            const int hi = hb[i] + dh, wi = wb[i] + dw;
+            const bool ok = kvalid && hi >= 0 && hi < a.H && wi >= 0 && wi < a.W;
+            const __nv_bfloat16* src = ok ? x + base[i] + (int64_t(hi) * a.W + wi) * 4 : x;
+            const uint32_t dst = sbase + uint32_t(r * 128 + (((sub >> 1) ^ (r & 7)) << 4) + ((sub & 1) << 3));
+            cp_async_8(dst, src, ok ? 8u : 0u);
+          }
+        }
+        cp_async_arrive_noinc(&full[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  gather_done:
+    cp_async_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool encode_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
+               uint32_t box_outer) {
+  auto fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// The dynamic shared-memory opt-in is a per-device function attribute; it is set while preparing
+// a plan (never during stream capture).
+template <int BN, int MODE>
+cudaError_t ensure_attr() {
+  static std::atomic<uint64_t> done_mask{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = uint64_t(1) << (dev & 63);
+  if (done_mask.load() & bit) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(conv_gemm_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Cfg<BN>::SMEM);
+  if (e == cudaSuccess) done_mask.fetch_or(bit);
+  return e;
+}
+
+template <int BN, int MODE>
+cudaError_t launch_t(const ConvGemmPlan& p, cudaStream_t s) {
+  conv_gemm_kernel<BN, MODE><<<p.grid, MODE ? 320 : 192, Cfg<BN>::SMEM, s>>>(p.tmA, p.tmB, p.args);
+  return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t ensure_attr_mode(int mode) {
+  return mode == 0 ? ensure_attr<BN, 0>() : (mode == 1 ? ensure_attr<BN, 1>() : ensure_attr<BN, 2>());
+}
+
+}  // namespace
+
+void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const void* w, int num_sms) {
+  ConvGemmArgs& a = p.args;
+  // Tile width: widest N tile that still gives at least one tile per SM.
+  auto tiles = [&](int bn) { return int64_t((a.M + BM - 1) / BM) * ((a.Cout + bn - 1) / bn); };
+  int bn = a.Cout <= 64 ? 64 : (a.Cout <= 128 ? 128 : 256);
+  while (bn > 64 && tiles(bn) < num_sms) bn /= 2;
+  p.bn = bn;
+  p.smem = bn == 64 ? Cfg<64>::SMEM : (bn == 128 ? Cfg<128>::SMEM : Cfg<256>::SMEM);
+  int64_t t = tiles(bn);
+  p.grid = int(t < num_sms ? t : num_sms);
+  std::memset(&p.tmA, 0, sizeof(p.tmA));
+  std::memset(&p.tmB, 0, sizeof(p.tmB));
+  bool ok = encode_2d(&p.tmB, w, uint64_t(a.Kpad), uint64_t(a.Cout), uint64_t(a.Kpad) * 2, BK, uint32_t(bn));
+  if (!a.gather) {
+    ok = ok && encode_2d(&p.tmA, a_rows, uint64_t(lda), uint64_t(a.M), uint64_t(lda) * 2, BK, BM);
+  }
+  if (!ok) throw std::runtime_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad layout)");
+  const int mode = a.gather ? (a.Cp == 4 ? 2 : 1) : 0;
+  cudaError_t e = bn == 64 ? ensure_attr_mode<64>(mode) : (bn == 128 ? ensure_attr_mode<128>(mode) : ensure_attr_mode<256>(mode));
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+}
+
+cudaError_t conv_gemm_launch(const ConvGemmPlan& p, cudaStream_t s) {
+  const int mode = p.args.gather ? (p.args.Cp == 4 ? 2 : 1) : 0;
+  switch (p.bn * 4 + mode) {
+    case 64 * 4 + 0: return launch_t<64, 0>(p, s);
+    case 64 * 4 + 1: return launch_t<64, 1>(p, s);
+    case 64 * 4 + 2: return launch_t<64, 2>(p, s);
+    case 128 * 4 + 0: return launch_t<128, 0>(p, s);
+    case 128 * 4 + 1: return launch_t<128, 1>(p, s);
+    case 128 * 4 + 2: return launch_t<128, 2>(p, s);
+    case 256 * 4 + 0: return launch_t<256, 0>(p, s);
+    case 256 * 4 + 1: return launch_t<256, 1>(p, s);
+    case 256 * 4 + 2: return launch_t<256, 2>(p, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace k
+}  // namespace sb

@@ -1,0 +1,103 @@
+// Launch interface of the sm_100a kernels. Plain pointers and sizes only; every launcher takes the
+// stream to run on. Implementations: conv_gemm.cu (tcgen05 tensor-core path), misc.cu (memory-bound).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace sb {
+namespace k {
+
+// ---- tensor-core implicit GEMM --------------------------------------------------------------
+// D[m, n] = act( sum_k A[m, k] * B[n, k] + bias[n] (+ residual[m, n]) )
+//   A = rows of a bf16 matrix (mode TMA) or the im2col of an NHWC bf16 activation (mode GATHER);
+//   B = bf16 weights [Cout, Kpad], K-major, K ordered (kh, kw, c) to match NHWC im2col.
+struct ConvGemmArgs {
+  // geometry of the A operand
+  int gather;              // 0: A rows via TMA (lda = Kpad elements); 1: im2col gather from NHWC
+  const void* x;           // NHWC bf16 [N, H, W, Cp] (gather)
+  int N, H, W, Cp;
+  int Ho, Wo, KH, KW, sh, sw, ph, pw, dh, dw;
+  int M;                   // rows of D (N*Ho*Wo for convs)
+  int Cout;                // columns of D
+  int Kpad;                // padded reduction length (multiple of 64)
+  const float* bias;       // [round_up(Cout, BN)] f32, zero padded (never null)
+  // residual operand
+  const void* res;         // null if none
+  int res_bf16;            // 1: bf16, 0: f32
+  int64_t ldr;             // elements between residual rows
+  int res_mode;            // 0: row m; 1: nearest-2x upsample source (Hr = Ho/2, Wr = Wo/2 rounded up)
+  int Hr, Wr;
+  // output
+  void* out;
+  int out_bf16;
+  int64_t ldo;             // elements between output rows
+  int64_t group_rows;      // rows per output group (0 = contiguous rows)
+  int64_t group_stride;    // elements between output groups
+  int act;                 // 0 none, 1 relu, 2 sigmoid
+  unsigned int* err;       // device error word (bounded-wait timeouts)
+};
+
+struct ConvGemmPlan {
+  CUtensorMap tmA;   // valid when gather == 0
+  CUtensorMap tmB;
+  int bn;            // 64, 128 or 256
+  int grid;
+  int smem;
+  ConvGemmArgs args;
+};
+
+// Builds tensor maps and the launch shape. `a_rows` is the A matrix base (TMA mode) with leading
+// dimension `lda` elements; `w` the weight matrix [Cout_rows >= Cout, Kpad]. Returns false when the
+// driver entry point for tensor-map encoding is unavailable.
+void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const void* w, int num_sms);
+cudaError_t conv_gemm_launch(const ConvGemmPlan& p, cudaStream_t s);
+
+// ---- memory-bound kernels (misc.cu) ------------------------------------------------------------
+constexpr int kMaxRank = 8;
+struct TDesc {
+  int rank;
+  int64_t shape[kMaxRank];
+  int64_t stride[kMaxRank];   // elements
+};
+
+// dst (NHWC bf16 [N,H,W,Cp]) <- src logical [N,C,H,W] with arbitrary strides, f32 or bf16; channels
+// C..Cp-1 are zero.
+cudaError_t to_nhwc_bf16(const void* src, int src_bf16, const int64_t* shape4, const int64_t* stride4,
+                         void* dst, int Cp, cudaStream_t s);
+// dst (bf16 [M, Kp]) <- src logical [M, K] with arbitrary strides; columns K..Kp-1 zero.
+cudaError_t to_rows_bf16(const void* src, int src_bf16, int64_t M, int64_t K, int64_t sm, int64_t sk,
+                         void* dst, int64_t Kp, cudaStream_t s);
+// NHWC bf16 max pooling (padding never wins: out-of-range taps are skipped).
+cudaError_t maxpool_nhwc_bf16(const void* x, void* y, int N, int H, int W, int C, int Ho, int Wo, int kh,
+                              int kw, int sh, int sw, int ph, int pw, int dh, int dw, cudaStream_t s);
+// NHWC (bf16 or f32 with C contiguous, pixel stride ldp) -> [N, C] mean or max, bf16 or f32 output.
+cudaError_t global_pool_nhwc(const void* x, int x_bf16, int N, int HW, int C, int64_t ldp, void* y, int y_bf16,
+                             int is_max, cudaStream_t s);
+// Generic strided copy with dtype conversion: dst[idx] = src[idx] over `shape`.
+cudaError_t strided_copy(const void* src, int src_bf16, const TDesc& sd, void* dst, int dst_bf16, const TDesc& dd,
+                         cudaStream_t s);
+cudaError_t fill_f32(void* dst, int64_t n, float v, cudaStream_t s);
+// Elementwise: y (f32 contiguous over out shape) = f(a [, b]) with broadcasting strides.
+enum EwOp : int {
+  EW_ADD = 0, EW_SUB, EW_MUL, EW_DIV, EW_POW, EW_MAX, EW_MIN,
+  EW_RELU = 16, EW_SIGMOID, EW_TANH, EW_SQRT, EW_NEG, EW_ABS, EW_EXP, EW_LOG, EW_RECIP, EW_FLOOR, EW_CEIL,
+  EW_ERF, EW_LEAKY, EW_CLIP, EW_IDENT
+};
+cudaError_t elementwise(int op, const void* a, int a_bf16, const TDesc& ad, const void* b, int b_bf16,
+                        const TDesc& bd, void* y, int y_bf16, const TDesc& yd, float alpha, float beta,
+                        cudaStream_t s);
+// Softmax over `len` elements spaced `inner` apart, for outer*inner independent rows; f32 in/out
+// contiguous.
+cudaError_t softmax(const float* x, float* y, int64_t outer, int64_t len, int64_t inner, cudaStream_t s);
+// Reduce over the middle axis of a contiguous [outer, len, inner] f32 view. kind: 0 sum, 1 mean, 2 max.
+cudaError_t reduce_mid(const float* x, float* y, int64_t outer, int64_t len, int64_t inner, int kind, cudaStream_t s);
+// Gather along every axis with per-axis index tables (nearest Resize):
+// y[o] = x[sum_d table_d[o_d] * xd.stride[d]]; `tables` holds the per-axis tables back to back
+// (table_d has yd.shape[d] entries).
+cudaError_t gather_axes(const void* x, int x_bf16, const TDesc& xd, const int64_t* tables, void* y, int y_bf16,
+                        const TDesc& yd, cudaStream_t s);
+
+}  // namespace k
+}  // namespace sb

@@ -1,0 +1,347 @@
+// Memory-bound kernels: layout/dtype conversion, NHWC max pooling, global pooling, generic strided
+// elementwise / copy / softmax / reduce / gather. Coalesced along the innermost dimension and
+// 128-bit vectorised where the layout allows; grids are sized in multiples of the SM count.
+#include <cuda_bf16.h>
+
+#include <cmath>
+
+#include "kernels.h"
+
+namespace sb {
+namespace k {
+namespace {
+
+constexpr int kThreads = 256;
+
+inline int grid_for(int64_t n, int threads = kThreads) {
+  int64_t g = (n + threads - 1) / threads;
+  if (g > 148 * 32) g = 148 * 32;   // grid-stride beyond 32 blocks per SM
+  return int(g < 1 ? 1 : g);
+}
+
+__device__ __forceinline__ float ld_any(const void* p, int bf16, int64_t i) {
+  return bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]) : reinterpret_cast<const float*>(p)[i];
+}
+__device__ __forceinline__ void st_any(void* p, int bf16, int64_t i, float v) {
+  if (bf16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else reinterpret_cast<float*>(p)[i] = v;
+}
+
+// linear index -> offset under a strided descriptor
+__device__ __forceinline__ int64_t offset_of(int64_t lin, const TDesc& d) {
+  int64_t off = 0;
+#pragma unroll 1
+  for (int i = d.rank - 1; i >= 0; --i) {
+    const int64_t s = d.shape[i];
+    const int64_t q = lin / s;
+    off += (lin - q * s) * d.stride[i];
+    lin = q;
+  }
+  return off;
+}
+
+// ---- NCHW/any -> NHWC bf16 with channel padding ---------------------------------------------
+// One thread per (pixel, 4-channel group): reads are coalesced across pixels of a channel plane.
+__global__ void to_nhwc_bf16_kernel(const void* __restrict__ src, int src_bf16, int64_t N, int64_t C, int64_t H,
+                                    int64_t W, int64_t s0, int64_t s1, int64_t s2, int64_t s3,
+                                    __nv_bfloat16* __restrict__ dst, int Cp) {
+  const int groups = Cp / 4;
+  const int64_t total = N * H * W * groups;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    // order: pixel fastest within a channel group so that the strided reads coalesce
+    const int64_t pix_total = N * H * W;
+    const int g = int(i / pix_total);
+    const int64_t pix = i - int64_t(g) * pix_total;
+    const int64_t n = pix / (H * W);
+    const int64_t hw = pix - n * H * W;
+    const int64_t h = hw / W, w = hw - (hw / W) * W;
+    const int64_t base = n * s0 + h * s2 + w * s3;
+    __align__(8) __nv_bfloat16 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t c = int64_t(g) * 4 + j;
+      v[j] = __float2bfloat16_rn(c < C ? ld_any(src, src_bf16, base + c * s1) : 0.f);
+    }
+    *reinterpret_cast<uint2*>(dst + pix * Cp + g * 4) = *reinterpret_cast<uint2*>(v);
+  }
+}
+
+__global__ void to_rows_bf16_kernel(const void* __restrict__ src, int src_bf16, int64_t M, int64_t K, int64_t sm,
+                                    int64_t sk, __nv_bfloat16* __restrict__ dst, int64_t Kp) {
+  const int64_t total = M * Kp;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t m = i / Kp, kk = i - m * Kp;
+    dst[i] = __float2bfloat16_rn(kk < K ? ld_any(src, src_bf16, m * sm + kk * sk) : 0.f);
+  }
+}
+
+// ---- NHWC bf16 max pooling, 8 channels (16 bytes) per thread ---------------------------------
+__global__ void maxpool_nhwc_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int N, int H,
+                                    int W, int C, int Ho, int Wo, int kh, int kw, int sh, int sw, int ph, int pw,
+                                    int dh, int dw) {
+  const int cg = C / 8;
+  const int64_t total = int64_t(N) * Ho * Wo * cg;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int g = int(i % cg);
+    int64_t pix = i / cg;
+    const int wo = int(pix % Wo);
+    pix /= Wo;
+    const int ho = int(pix % Ho);
+    const int n = int(pix / Ho);
+    float m[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m[j] = -INFINITY;
+    for (int a = 0; a < kh; ++a) {
+      const int hi = ho * sh - ph + a * dh;
+      if (hi < 0 || hi >= H) continue;
+      for (int b = 0; b < kw; ++b) {
+        const int wi = wo * sw - pw + b * dw;
+        if (wi < 0 || wi >= W) continue;
+        uint4 q = __ldg(reinterpret_cast<const uint4*>(x + ((int64_t(n) * H + hi) * W + wi) * C + g * 8));
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          float2 f = __bfloat1622float2(h[t]);
+          m[2 * t] = fmaxf(m[2 * t], f.x);
+          m[2 * t + 1] = fmaxf(m[2 * t + 1], f.y);
+        }
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) oh[t] = __floats2bfloat162_rn(m[2 * t], m[2 * t + 1]);
+    *reinterpret_cast<uint4*>(y + i * 8) = o;
+  }
+}
+
+// Scalar fallback when C is not a multiple of 8.
+__global__ void maxpool_nhwc_scalar_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int N,
+                                           int H, int W, int C, int Ho, int Wo, int kh, int kw, int sh, int sw, int ph,
+                                           int pw, int dh, int dw) {
+  const int64_t total = int64_t(N) * Ho * Wo * C;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int c = int(i % C);
+    int64_t pix = i / C;
+    const int wo = int(pix % Wo);
+    pix /= Wo;
+    const int ho = int(pix % Ho);
+    const int n = int(pix / Ho);
+    float m = -INFINITY;
+    for (int a = 0; a < kh; ++a) {
+      const int hi = ho * sh - ph + a * dh;
+      if (hi < 0 || hi >= H) continue;
+      for (int b = 0; b < kw; ++b) {
+        const int wi = wo * sw - pw + b * dw;
+        if (wi < 0 || wi >= W) continue;
+        m = fmaxf(m, __bfloat162float(x[((int64_t(n) * H + hi) * W + wi) * C + c]));
+      }
+    }
+    y[i] = __float2bfloat16_rn(m);
+  }
+}
+
+// ---- global average / max pool over NHWC: one thread per (n, channel) -------------------------
+__global__ void global_pool_kernel(const void* __restrict__ x, int x_bf16, int N, int HW, int C, int64_t ldp,
+                                   void* __restrict__ y, int y_bf16, int is_max) {
+  const int64_t total = int64_t(N) * C;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int n = int(i / C), c = int(i - int64_t(i / C) * C);
+    const int64_t base = int64_t(n) * HW * ldp + c;
+    float acc = is_max ? -INFINITY : 0.f;
+    for (int p = 0; p < HW; ++p) {
+      const float v = ld_any(x, x_bf16, base + int64_t(p) * ldp);
+      acc = is_max ? fmaxf(acc, v) : acc + v;
+    }
+    st_any(y, y_bf16, i, is_max ? acc : acc / float(HW));
+  }
+}
+
+__global__ void strided_copy_kernel(const void* __restrict__ src, int src_bf16, TDesc sd, void* __restrict__ dst,
+                                    int dst_bf16, TDesc dd, int64_t total) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x)
+    st_any(dst, dst_bf16, offset_of(i, dd), ld_any(src, src_bf16, offset_of(i, sd)));
+}
+
+__global__ void fill_kernel(float* dst, int64_t n, float v) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+    dst[i] = v;
+}
+
+__device__ __forceinline__ float ew_apply(int op, float a, float b, float alpha, float beta) {
+  switch (op) {
+    case EW_ADD: return a + b;
+    case EW_SUB: return a - b;
+    case EW_MUL: return a * b;
+    case EW_DIV: return a / b;
+    case EW_POW: return powf(a, b);
+    case EW_MAX: return fmaxf(a, b);
+    case EW_MIN: return fminf(a, b);
+    case EW_RELU: return a > 0.f ? a : 0.f;
+    case EW_SIGMOID: return 1.f / (1.f + expf(-a));
+    case EW_TANH: return tanhf(a);
+    case EW_SQRT: return sqrtf(a);
+    case EW_NEG: return -a;
+    case EW_ABS: return fabsf(a);
+    case EW_EXP: return expf(a);
+    case EW_LOG: return logf(a);
+    case EW_RECIP: return 1.f / a;
+    case EW_FLOOR: return floorf(a);
+    case EW_CEIL: return ceilf(a);
+    case EW_ERF: return erff(a);
+    case EW_LEAKY: return a >= 0.f ? a : alpha * a;
+    case EW_CLIP: return fminf(fmaxf(a, alpha), beta);
+    default: return a;
+  }
+}
+
+__global__ void elementwise_kernel(int op, const void* __restrict__ a, int a_bf16, TDesc ad, const void* __restrict__ b,
+                                   int b_bf16, TDesc bd, void* __restrict__ y, int y_bf16, TDesc yd, float alpha,
+                                   float beta, int64_t total) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const float va = ld_any(a, a_bf16, offset_of(i, ad));
+    const float vb = b ? ld_any(b, b_bf16, offset_of(i, bd)) : 0.f;
+    st_any(y, y_bf16, offset_of(i, yd), ew_apply(op, va, vb, alpha, beta));
+  }
+}
+
+// One warp per softmax row; rows are (outer, inner) pairs, elements `inner` apart.
+__global__ void softmax_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t outer, int64_t len,
+                               int64_t inner) {
+  const int64_t rows = outer * inner;
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; r < rows;
+       r += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+    const int64_t o = r / inner, in = r - o * inner;
+    const float* xp = x + o * len * inner + in;
+    float* yp = y + o * len * inner + in;
+    float m = -INFINITY;
+    for (int64_t l = lane; l < len; l += 32) m = fmaxf(m, xp[l * inner]);
+#pragma unroll
+    for (int s = 16; s; s >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
+    float sum = 0.f;
+    for (int64_t l = lane; l < len; l += 32) sum += expf(xp[l * inner] - m);
+#pragma unroll
+    for (int s = 16; s; s >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, s);
+    const float inv = 1.f / sum;
+    for (int64_t l = lane; l < len; l += 32) yp[l * inner] = expf(xp[l * inner] - m) * inv;
+  }
+}
+
+__global__ void reduce_mid_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t outer, int64_t len,
+                                  int64_t inner, int kind) {
+  const int64_t total = outer * inner;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t o = i / inner, in = i - o * inner;
+    const float* xp = x + o * len * inner + in;
+    float acc = kind == 2 ? -INFINITY : 0.f;
+    for (int64_t l = 0; l < len; ++l) acc = kind == 2 ? fmaxf(acc, xp[l * inner]) : acc + xp[l * inner];
+    y[i] = kind == 1 ? acc / float(len) : acc;
+  }
+}
+
+__global__ void gather_axes_kernel(const void* __restrict__ x, int x_bf16, TDesc xd, const int64_t* __restrict__ tables,
+                                   void* __restrict__ y, int y_bf16, TDesc yd, int64_t total) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t lin = i, off = 0, tab = 0;
+    int64_t tab_off[kMaxRank];
+    for (int d = 0; d < yd.rank; ++d) {
+      tab_off[d] = tab;
+      tab += yd.shape[d];
+    }
+    for (int d = yd.rank - 1; d >= 0; --d) {
+      const int64_t q = lin / yd.shape[d];
+      const int64_t idx = lin - q * yd.shape[d];
+      off += tables[tab_off[d] + idx] * xd.stride[d];
+      lin = q;
+    }
+    st_any(y, y_bf16, offset_of(i, yd), ld_any(x, x_bf16, off));
+  }
+}
+
+}  // namespace
+
+cudaError_t to_nhwc_bf16(const void* src, int src_bf16, const int64_t* sh, const int64_t* st, void* dst, int Cp,
+                         cudaStream_t s) {
+  const int64_t total = sh[0] * sh[2] * sh[3] * (Cp / 4);
+  to_nhwc_bf16_kernel<<<grid_for(total), kThreads, 0, s>>>(src, src_bf16, sh[0], sh[1], sh[2], sh[3], st[0], st[1],
+                                                           st[2], st[3], reinterpret_cast<__nv_bfloat16*>(dst), Cp);
+  return cudaGetLastError();
+}
+
+cudaError_t to_rows_bf16(const void* src, int src_bf16, int64_t M, int64_t K, int64_t sm, int64_t sk, void* dst,
+                         int64_t Kp, cudaStream_t s) {
+  to_rows_bf16_kernel<<<grid_for(M * Kp), kThreads, 0, s>>>(src, src_bf16, M, K, sm, sk,
+                                                            reinterpret_cast<__nv_bfloat16*>(dst), Kp);
+  return cudaGetLastError();
+}
+
+cudaError_t maxpool_nhwc_bf16(const void* x, void* y, int N, int H, int W, int C, int Ho, int Wo, int kh, int kw, int sh,
+                              int sw, int ph, int pw, int dh, int dw, cudaStream_t s) {
+  auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto yb = reinterpret_cast<__nv_bfloat16*>(y);
+  if (C % 8 == 0) {
+    maxpool_nhwc_kernel<<<grid_for(int64_t(N) * Ho * Wo * (C / 8)), kThreads, 0, s>>>(xb, yb, N, H, W, C, Ho, Wo, kh, kw,
+                                                                                      sh, sw, ph, pw, dh, dw);
+  } else {
+    maxpool_nhwc_scalar_kernel<<<grid_for(int64_t(N) * Ho * Wo * C), kThreads, 0, s>>>(xb, yb, N, H, W, C, Ho, Wo, kh,
+                                                                                       kw, sh, sw, ph, pw, dh, dw);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t global_pool_nhwc(const void* x, int x_bf16, int N, int HW, int C, int64_t ldp, void* y, int y_bf16,
+                             int is_max, cudaStream_t s) {
+  global_pool_kernel<<<grid_for(int64_t(N) * C), kThreads, 0, s>>>(x, x_bf16, N, HW, C, ldp, y, y_bf16, is_max);
+  return cudaGetLastError();
+}
+
+cudaError_t strided_copy(const void* src, int src_bf16, const TDesc& sd, void* dst, int dst_bf16, const TDesc& dd,
+                         cudaStream_t s) {
+  int64_t total = 1;
+  for (int i = 0; i < dd.rank; ++i) total *= dd.shape[i];
+  if (total == 0) return cudaSuccess;
+  strided_copy_kernel<<<grid_for(total), kThreads, 0, s>>>(src, src_bf16, sd, dst, dst_bf16, dd, total);
+  return cudaGetLastError();
+}
+
+cudaError_t fill_f32(void* dst, int64_t n, float v, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  fill_kernel<<<grid_for(n), kThreads, 0, s>>>(reinterpret_cast<float*>(dst), n, v);
+  return cudaGetLastError();
+}
+
+cudaError_t elementwise(int op, const void* a, int a_bf16, const TDesc& ad, const void* b, int b_bf16, const TDesc& bd,
+                        void* y, int y_bf16, const TDesc& yd, float alpha, float beta, cudaStream_t s) {
+  int64_t total = 1;
+  for (int i = 0; i < yd.rank; ++i) total *= yd.shape[i];
+  if (total == 0) return cudaSuccess;
+  elementwise_kernel<<<grid_for(total), kThreads, 0, s>>>(op, a, a_bf16, ad, b, b_bf16, bd, y, y_bf16, yd, alpha, beta,
+                                                          total);
+  return cudaGetLastError();
+}
+
+cudaError_t softmax(const float* x, float* y, int64_t outer, int64_t len, int64_t inner, cudaStream_t s) {
+  const int64_t rows = outer * inner;
+  if (rows == 0) return cudaSuccess;
+  softmax_kernel<<<grid_for(rows * 32), kThreads, 0, s>>>(x, y, outer, len, inner);
+  return cudaGetLastError();
+}
+
+cudaError_t reduce_mid(const float* x, float* y, int64_t outer, int64_t len, int64_t inner, int kind, cudaStream_t s) {
+  if (outer * inner == 0) return cudaSuccess;
+  reduce_mid_kernel<<<grid_for(outer * inner), kThreads, 0, s>>>(x, y, outer, len, inner, kind);
+  return cudaGetLastError();
+}
+
+cudaError_t gather_axes(const void* x, int x_bf16, const TDesc& xd, const int64_t* tables, void* y, int y_bf16,
+                        const TDesc& yd, cudaStream_t s) {
+  int64_t total = 1;
+  for (int i = 0; i < yd.rank; ++i) total *= yd.shape[i];
+  if (total == 0) return cudaSuccess;
+  gather_axes_kernel<<<grid_for(total), kThreads, 0, s>>>(x, x_bf16, xd, tables, y, y_bf16, yd, total);
+  return cudaGetLastError();
+}
+
+}  // namespace k
+}  // namespace sb

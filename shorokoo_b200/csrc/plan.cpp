@@ -1,0 +1,1033 @@
+// Plan construction: layout / dtype selection, conversion insertion, weight packing, arena
+// allocation (liveness + best fit), launch closures and CUDA-graph capture.
+//
+// Layout policy: activations that feed tensor-core or pooling kernels are stored NHWC bf16 (channel
+// contiguous, so an im2col row of one filter tap is a contiguous 128-byte run); everything a generic
+// op or a graph output reads is fp32. Reshape / Transpose / Slice / Expand are stride views when the
+// memory permits (the NHWC conv output of a RetinaNet head makes its Reshape->Transpose chain a pure
+// view), otherwise a strided copy materialises them.
+#include "plan.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <map>
+#include <numeric>
+#include <optional>
+
+namespace sb {
+
+namespace {
+
+constexpr size_t kAlign = 256;
+
+std::vector<int64_t> contig_strides(const std::vector<int64_t>& s) {
+  std::vector<int64_t> st(s.size());
+  int64_t acc = 1;
+  for (int i = int(s.size()) - 1; i >= 0; --i) {
+    st[size_t(i)] = acc;
+    acc *= std::max<int64_t>(s[size_t(i)], 1);
+  }
+  return st;
+}
+
+bool is_contig(const DevTensor& t) {
+  auto c = contig_strides(t.shape);
+  for (size_t i = 0; i < t.shape.size(); ++i)
+    if (t.shape[i] != 1 && t.strides[i] != c[i]) return false;
+  return true;
+}
+
+// Strides for viewing (shape, strides) as new_shape without copying, if possible (the stride
+// bookkeeping of a reshape over non-contiguous memory: dims are grouped into runs that are
+// contiguous with respect to each other, and every run must split/merge exactly).
+std::optional<std::vector<int64_t>> view_strides(const std::vector<int64_t>& shape, const std::vector<int64_t>& strides,
+                                                 const std::vector<int64_t>& new_shape) {
+  if (numel(shape) == 0) return contig_strides(new_shape);
+  // drop size-1 dims of the source; they do not constrain the view
+  std::vector<int64_t> s, st;
+  for (size_t i = 0; i < shape.size(); ++i)
+    if (shape[i] != 1) {
+      s.push_back(shape[i]);
+      st.push_back(strides[i]);
+    }
+  std::vector<int64_t> out(new_shape.size(), 0);
+  int vi = int(new_shape.size()) - 1;
+  int i = int(s.size()) - 1;
+  while (i >= 0) {
+    // gather a maximal contiguous run of source dims [j..i]
+    int j = i;
+    int64_t run = s[size_t(i)];
+    while (j > 0 && st[size_t(j - 1)] == st[size_t(j)] * s[size_t(j)]) {
+      --j;
+      run *= s[size_t(j)];
+    }
+    // consume new dims covering exactly `run` elements, innermost first
+    int64_t acc = 1;
+    const int64_t base = st[size_t(i)];
+    while (vi >= 0 && (acc < run || new_shape[size_t(vi)] == 1)) {
+      if (new_shape[size_t(vi)] == 1) {
+        out[size_t(vi)] = acc * base;
+        --vi;
+        continue;
+      }
+      out[size_t(vi)] = acc * base;
+      acc *= new_shape[size_t(vi)];
+      --vi;
+    }
+    if (acc != run) return std::nullopt;
+    i = j - 1;
+  }
+  while (vi >= 0) {
+    if (new_shape[size_t(vi)] != 1) return std::nullopt;
+    out[size_t(vi)] = 1;
+    --vi;
+  }
+  return out;
+}
+
+k::TDesc tdesc(const DevTensor& t) {
+  k::TDesc d{};
+  SB_CHECK(t.shape.size() <= size_t(k::kMaxRank), SB_UNSUPPORTED, "tensor rank above 8 is not supported on device");
+  d.rank = int(t.shape.size());
+  for (size_t i = 0; i < t.shape.size(); ++i) {
+    d.shape[i] = t.shape[i];
+    d.stride[i] = t.strides[i];
+  }
+  if (d.rank == 0) {   // scalars: rank-1 of length 1
+    d.rank = 1;
+    d.shape[0] = 1;
+    d.stride[0] = 1;
+  }
+  return d;
+}
+
+// Broadcast view of `t` to `out_shape` (stride 0 on broadcast dims).
+DevTensor broadcast_to(const DevTensor& t, const std::vector<int64_t>& out_shape) {
+  DevTensor r = t;
+  r.shape = out_shape;
+  r.strides.assign(out_shape.size(), 0);
+  size_t off = out_shape.size() - t.shape.size();
+  for (size_t i = 0; i < t.shape.size(); ++i) {
+    if (t.shape[i] == out_shape[i + off]) r.strides[i + off] = t.strides[i];
+    else SB_CHECK(t.shape[i] == 1, SB_SHAPE_ERROR, "broadcast mismatch");
+  }
+  return r;
+}
+
+bool is_view_op(const std::string& t) {
+  return t == "Reshape" || t == "Transpose" || t == "Identity" || t == "Slice" || t == "Expand";
+}
+
+int ew_code(const std::string& t) {
+  static const std::map<std::string, int> m = {
+      {"Add", k::EW_ADD}, {"Sub", k::EW_SUB}, {"Mul", k::EW_MUL}, {"Div", k::EW_DIV}, {"Pow", k::EW_POW},
+      {"Max", k::EW_MAX}, {"Min", k::EW_MIN}, {"Relu", k::EW_RELU}, {"Sigmoid", k::EW_SIGMOID},
+      {"Tanh", k::EW_TANH}, {"Sqrt", k::EW_SQRT}, {"Neg", k::EW_NEG}, {"Abs", k::EW_ABS}, {"Exp", k::EW_EXP},
+      {"Log", k::EW_LOG}, {"Reciprocal", k::EW_RECIP}, {"Floor", k::EW_FLOOR}, {"Ceil", k::EW_CEIL},
+      {"Erf", k::EW_ERF}, {"LeakyRelu", k::EW_LEAKY}, {"Clip", k::EW_CLIP}};
+  auto it = m.find(t);
+  return it == m.end() ? -1 : it->second;
+}
+
+inline void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    if (e == cudaErrorMemoryAllocation) fail(SB_OUT_OF_MEMORY, std::string(what) + ": " + cudaGetErrorString(e));
+    fail(SB_CUDA_ERROR, std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------
+Plan::Plan(LGraph g, int device, int num_sms) : g_(std::move(g)), device_(device), num_sms_(num_sms) {
+  fuse(g_);
+  build();
+  allocate_and_finalize();
+}
+
+Plan::~Plan() {
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device_);
+  if (exec_) cudaGraphExecDestroy(exec_);
+  if (graph_) cudaGraphDestroy(graph_);
+  if (arena_) cudaFree(arena_);
+  if (weights_) cudaFree(weights_);
+  if (err_) cudaFree(err_);
+  if (prev >= 0) cudaSetDevice(prev);
+}
+
+int Plan::new_buffer(size_t bytes) {
+  Buffer b;
+  b.bytes = (bytes + kAlign - 1) / kAlign * kAlign;
+  if (b.bytes == 0) b.bytes = kAlign;
+  bufs_.push_back(b);
+  return int(bufs_.size()) - 1;
+}
+
+DevTensor Plan::alloc_contig(const std::vector<int64_t>& shape, bool bf16) {
+  DevTensor t;
+  t.bf16 = bf16;
+  t.shape = shape;
+  t.strides = contig_strides(shape);
+  t.buf = new_buffer(size_t(numel(shape)) * (bf16 ? 2 : 4));
+  return t;
+}
+
+// NHWC storage for a logical NCHW tensor, channel stride 1 and `cstride` elements per pixel.
+DevTensor Plan::alloc_nhwc(const std::vector<int64_t>& s, bool bf16, int64_t cstride) {
+  DevTensor t;
+  t.bf16 = bf16;
+  t.shape = s;
+  t.strides = {s[2] * s[3] * cstride, 1, s[3] * cstride, cstride};
+  t.buf = new_buffer(size_t(s[0] * s[2] * s[3] * cstride) * (bf16 ? 2 : 4));
+  return t;
+}
+
+int64_t Plan::add_weight_bytes(const void* data, size_t bytes) {
+  size_t off = (wblob_.size() + kAlign - 1) / kAlign * kAlign;
+  wblob_.resize(off + std::max<size_t>(bytes, 1));
+  if (bytes) std::memcpy(wblob_.data() + off, data, bytes);
+  return int64_t(off);
+}
+
+void* Plan::buffer_ptr(int buf) const { return static_cast<uint8_t*>(arena_) + bufs_[size_t(buf)].offset; }
+
+void* Plan::ptr(const DevTensor& t) const {
+  SB_CHECK(t.valid(), SB_INTERNAL, "plan: invalid tensor reference");
+  uint8_t* base = t.buf == -1 ? static_cast<uint8_t*>(weights_) : static_cast<uint8_t*>(arena_) + bufs_[size_t(t.buf)].offset;
+  return base + t.off;
+}
+
+void Plan::add_step(const std::string& kind, std::vector<DevTensor> reads, std::vector<DevTensor> writes,
+                    std::function<std::function<cudaError_t(cudaStream_t)>()> b) {
+  const int idx = int(pending_.size());
+  for (auto* lst : {&reads, &writes})
+    for (auto& t : *lst)
+      if (t.buf >= 0) {
+        bufs_[size_t(t.buf)].first = std::min(bufs_[size_t(t.buf)].first, idx);
+        bufs_[size_t(t.buf)].last = std::max(bufs_[size_t(t.buf)].last, idx);
+      }
+  pending_.push_back({kind, std::move(b), std::move(reads), std::move(writes)});
+  stats_.kernels++;
+}
+
+bool Plan::consumers_accept_bf16(int v) const {
+  if (is_output_[size_t(v)]) return false;
+  if (consumers_[size_t(v)].empty()) return false;
+  for (int oi : consumers_[size_t(v)]) {
+    const Op& op = g_.ops[size_t(oi)];
+    if (op.type == "FusedConv" || op.type == "FusedGemm" || op.type == "MaxPool" ||
+        op.type == "GlobalAveragePool" || op.type == "GlobalMaxPool")
+      continue;
+    if (is_view_op(op.type) && op.in[0] == v) {
+      if (!consumers_accept_bf16(op.out[0])) return false;
+      continue;
+    }
+    return false;
+  }
+  return true;
+}
+
+DevTensor Plan::materialize(const DevTensor& src, bool bf16) {
+  DevTensor dst = alloc_contig(src.shape, bf16);
+  add_step("copy", {src}, {dst}, [this, src, dst]() {
+    void* sp = ptr(src);
+    void* dp = ptr(dst);
+    k::TDesc sd = tdesc(src), dd = tdesc(dst);
+    int sb = src.bf16, db = dst.bf16;
+    return std::function<cudaError_t(cudaStream_t)>(
+        [=](cudaStream_t s) { return k::strided_copy(sp, sb, sd, dp, db, dd, s); });
+  });
+  return dst;
+}
+
+DevTensor Plan::as_f32_contig(int v) {
+  const DevTensor& t = vt_[size_t(v)];
+  if (!t.bf16 && is_contig(t)) return t;
+  return materialize(t, false);
+}
+
+DevTensor Plan::as_nhwc_bf16(int v, int Cp) {
+  const DevTensor& t = vt_[size_t(v)];
+  SB_CHECK(t.shape.size() == 4, SB_SHAPE_ERROR, "expected a rank-4 activation");
+  const int64_t N = t.shape[0], C = t.shape[1], H = t.shape[2], W = t.shape[3];
+  if (t.bf16 && C == Cp && t.strides[1] == 1 && t.strides[3] == Cp && (t.strides[2] == W * Cp || H == 1) &&
+      (t.strides[0] == H * W * Cp || N == 1) && t.off % 16 == 0)
+    return t;
+  auto key = std::make_pair(v, Cp);
+  auto it = conv_cache_.find(key);
+  if (it != conv_cache_.end()) return it->second;
+  DevTensor dst = alloc_nhwc({N, C, H, W}, true, Cp);
+  add_step("to_nhwc_bf16", {t}, {dst}, [this, t, dst, Cp]() {
+    const void* sp = ptr(t);
+    void* dp = ptr(dst);
+    int64_t sh[4] = {t.shape[0], t.shape[1], t.shape[2], t.shape[3]};
+    int64_t st[4] = {t.strides[0], t.strides[1], t.strides[2], t.strides[3]};
+    int sb = t.bf16;
+    return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+      return k::to_nhwc_bf16(sp, sb, sh, st, dp, Cp, s);
+    });
+  });
+  conv_cache_[key] = dst;
+  return dst;
+}
+
+DevTensor Plan::as_rows_bf16(int v, int64_t M, int64_t K) {
+  DevTensor t = vt_[size_t(v)];
+  auto vs = view_strides(t.shape, t.strides, {M, K});
+  if (vs) {
+    DevTensor r = t;
+    r.shape = {M, K};
+    r.strides = *vs;
+    if (t.bf16 && r.strides[1] == 1 && (r.strides[0] == K || M == 1) && K % 8 == 0 && t.off % 16 == 0) {
+      r.strides[0] = K;
+      return r;
+    }
+    t = r;
+  } else {
+    t = materialize(t, false);
+    t.shape = {M, K};
+    t.strides = {K, 1};
+  }
+  auto it = rows_cache_.find(v);
+  if (it != rows_cache_.end()) return it->second;
+  const int64_t Kp = round_up(K, 8);
+  DevTensor dst = alloc_contig({M, Kp}, true);
+  add_step("to_rows_bf16", {t}, {dst}, [this, t, dst, M, K, Kp]() {
+    const void* sp = ptr(t);
+    void* dp = ptr(dst);
+    int64_t sm = t.strides[0], sk = t.strides[1];
+    int sb = t.bf16;
+    return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+      return k::to_rows_bf16(sp, sb, M, K, sm, sk, dp, Kp, s);
+    });
+  });
+  rows_cache_[v] = dst;
+  return dst;
+}
+
+// ---------------------------------------------------------------------------------------------
+void Plan::plan_conv(const Op& op) {
+  const Value& xv = g_.vals[size_t(op.in[0])];
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  SB_CHECK(op.group == 1, SB_UNSUPPORTED, "Conv: group > 1 is not supported");
+  const HostTensor& Wt = *op.weight;
+  const int64_t N = xv.shape[0], C = xv.shape[1], H = xv.shape[2], W = xv.shape[3];
+  const int64_t Cout = Wt.shape[0], KH = Wt.shape[2], KW = Wt.shape[3];
+  const int64_t Ho = yv.shape[2], Wo = yv.shape[3];
+  const int Cp = int(C % 8 == 0 ? C : (C <= 4 ? 4 : round_up(C, 8)));
+  const bool one_by_one = KH == 1 && KW == 1 && op.strides[0] == 1 && op.strides[1] == 1 && op.pads[0] == 0 &&
+                          op.pads[1] == 0 && op.pads[2] == 0 && op.pads[3] == 0 && Cp % 8 == 0;
+  DevTensor x = as_nhwc_bf16(op.in[0], Cp);
+  const int64_t K = KH * KW * Cp;
+  const int64_t Kpad = round_up(K, 64);
+  SB_CHECK(N * Ho * Wo < (int64_t(1) << 31) && N * H * W * Cp < (int64_t(1) << 40), SB_UNSUPPORTED,
+           "Conv: problem too large for 32-bit row indexing");
+  // weights [Cout, Kpad] bf16, K ordered (kh, kw, c)
+  std::vector<uint16_t> wb(size_t(Cout * Kpad), 0);
+  const float* wp = Wt.ptr<float>();
+  for (int64_t m = 0; m < Cout; ++m)
+    for (int64_t c = 0; c < C; ++c)
+      for (int64_t a = 0; a < KH; ++a)
+        for (int64_t b = 0; b < KW; ++b)
+          wb[size_t(m * Kpad + (a * KW + b) * Cp + c)] = f32_to_bf16_rne(wp[((m * C + c) * KH + a) * KW + b]);
+  DevTensor wt;
+  wt.buf = -1;
+  wt.off = add_weight_bytes(wb.data(), wb.size() * 2);
+  std::vector<float> bias(size_t(round_up(Cout, 256)), 0.f);
+  for (int64_t m = 0; m < Cout; ++m) bias[size_t(m)] = op.bias ? op.bias->ptr<float>()[m] : 0.f;
+  DevTensor bt;
+  bt.buf = -1;
+  bt.off = add_weight_bytes(bias.data(), bias.size() * 4);
+
+  const bool out_bf16 = consumers_accept_bf16(op.out[0]);
+  DevTensor y = alloc_nhwc(yv.shape, out_bf16, Cout);
+  vt_[size_t(op.out[0])] = y;
+
+  DevTensor r;
+  int64_t ldr = 0;
+  int Hr = 0, Wr = 0;
+  if (op.residual >= 0) {
+    const DevTensor& rt = vt_[size_t(op.residual)];
+    SB_CHECK(rt.shape.size() == 4 && rt.shape[1] == Cout && rt.shape[0] == N, SB_SHAPE_ERROR, "Conv: residual shape");
+    const int64_t rh = rt.shape[2], rw = rt.shape[3];
+    if (op.residual_mode == 0) SB_CHECK(rh == Ho && rw == Wo, SB_SHAPE_ERROR, "Conv: residual shape");
+    else SB_CHECK(rh * 2 == Ho && rw * 2 == Wo, SB_SHAPE_ERROR, "Conv: upsampled residual shape");
+    const int64_t cs = rt.strides[3];
+    if (rt.strides[1] == 1 && (rt.strides[2] == rw * cs || rh == 1) && (rt.strides[0] == rh * rw * cs || N == 1) &&
+        cs >= Cout) {
+      r = rt;
+      ldr = cs;
+    } else {
+      r = as_nhwc_bf16(op.residual, int(round_up(Cout, 4)));
+      ldr = round_up(Cout, 4);
+    }
+    Hr = int(rh);
+    Wr = int(rw);
+  }
+  stats_.macs += double(N * Ho * Wo) * double(Cout) * double(C * KH * KW);
+  stats_.tc_kernels++;
+  std::vector<DevTensor> reads{x};
+  if (r.valid()) reads.push_back(r);
+  const int sms = num_sms_;
+  add_step("conv", reads, {y}, [=]() {
+    auto p = std::make_shared<k::ConvGemmPlan>();
+    k::ConvGemmArgs& a = p->args;
+    std::memset(&a, 0, sizeof(a));
+    a.gather = one_by_one ? 0 : 1;
+    a.x = ptr(x);
+    a.N = int(N);
+    a.H = int(H);
+    a.W = int(W);
+    a.Cp = Cp;
+    a.Ho = int(Ho);
+    a.Wo = int(Wo);
+    a.KH = int(KH);
+    a.KW = int(KW);
+    a.sh = int(op.strides[0]);
+    a.sw = int(op.strides[1]);
+    a.ph = int(op.pads[0]);
+    a.pw = int(op.pads[1]);
+    a.dh = int(op.dilations[0]);
+    a.dw = int(op.dilations[1]);
+    a.M = int(N * Ho * Wo);
+    a.Cout = int(Cout);
+    a.Kpad = int(Kpad);
+    a.bias = static_cast<const float*>(ptr(bt));
+    a.res = r.valid() ? ptr(r) : nullptr;
+    a.res_bf16 = r.valid() ? int(r.bf16) : 0;
+    a.ldr = ldr;
+    a.res_mode = op.residual_mode;
+    a.Hr = Hr;
+    a.Wr = Wr;
+    a.out = ptr(y);
+    a.out_bf16 = int(y.bf16);
+    a.ldo = Cout;
+    a.act = op.act;
+    a.err = err_;
+    k::conv_gemm_prepare(*p, ptr(x), Cp, ptr(wt), sms);
+    return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::conv_gemm_launch(*p, s); });
+  });
+}
+
+void Plan::plan_gemm(const Op& op) {
+  const Value& xv = g_.vals[size_t(op.in[0])];
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  const HostTensor& Wt = *op.weight;
+  const int64_t Nn = Wt.shape[0], K = Wt.shape[1];
+  SB_CHECK(!xv.shape.empty() && xv.shape.back() == K, SB_SHAPE_ERROR, "Gemm: inner dimension mismatch");
+  const int64_t M = numel(xv.shape) / std::max<int64_t>(K, 1);
+  SB_CHECK(M < (int64_t(1) << 31), SB_UNSUPPORTED, "Gemm: too many rows");
+  DevTensor x = as_rows_bf16(op.in[0], M, K);
+  const int64_t lda = x.strides[0];
+  const int64_t Kpad = round_up(K, 64);
+  std::vector<uint16_t> wb(size_t(Nn * Kpad), 0);
+  const float* wp = Wt.ptr<float>();
+  for (int64_t n = 0; n < Nn; ++n)
+    for (int64_t kk = 0; kk < K; ++kk) wb[size_t(n * Kpad + kk)] = f32_to_bf16_rne(wp[n * K + kk]);
+  DevTensor wt;
+  wt.buf = -1;
+  wt.off = add_weight_bytes(wb.data(), wb.size() * 2);
+  std::vector<float> bias(size_t(round_up(Nn, 256)), 0.f);
+  for (int64_t n = 0; n < Nn; ++n) bias[size_t(n)] = op.bias ? op.bias->ptr<float>()[n] : 0.f;
+  DevTensor bt;
+  bt.buf = -1;
+  bt.off = add_weight_bytes(bias.data(), bias.size() * 4);
+  const bool out_bf16 = consumers_accept_bf16(op.out[0]);
+  DevTensor y = alloc_contig(yv.shape, out_bf16);
+  vt_[size_t(op.out[0])] = y;
+  DevTensor r;
+  if (op.residual >= 0) {
+    r = vt_[size_t(op.residual)];
+    if (!is_contig(r)) r = materialize(r, false);
+  }
+  stats_.macs += double(M) * double(Nn) * double(K);
+  stats_.tc_kernels++;
+  std::vector<DevTensor> reads{x};
+  if (r.valid()) reads.push_back(r);
+  const int sms = num_sms_;
+  add_step("gemm", reads, {y}, [=]() {
+    auto p = std::make_shared<k::ConvGemmPlan>();
+    k::ConvGemmArgs& a = p->args;
+    std::memset(&a, 0, sizeof(a));
+    a.gather = 0;
+    a.N = 1;
+    a.H = a.W = 1;
+    a.Ho = 1;
+    a.Wo = 1;
+    a.KH = a.KW = 1;
+    a.sh = a.sw = 1;
+    a.dh = a.dw = 1;
+    a.Cp = int(K);
+    a.M = int(M);
+    a.Cout = int(Nn);
+    a.Kpad = int(Kpad);
+    a.bias = static_cast<const float*>(ptr(bt));
+    a.res = r.valid() ? ptr(r) : nullptr;
+    a.res_bf16 = r.valid() ? int(r.bf16) : 0;
+    a.ldr = Nn;
+    a.out = ptr(y);
+    a.out_bf16 = int(y.bf16);
+    a.ldo = Nn;
+    a.act = op.act;
+    a.err = err_;
+    k::conv_gemm_prepare(*p, ptr(x), lda, ptr(wt), sms);
+    return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::conv_gemm_launch(*p, s); });
+  });
+}
+
+void Plan::plan_maxpool(const Op& op) {
+  const Value& xv = g_.vals[size_t(op.in[0])];
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  const DevTensor& t = vt_[size_t(op.in[0])];
+  const int64_t C = xv.shape[1];
+  DevTensor x;
+  int64_t cs = t.strides.size() == 4 ? t.strides[3] : 0;
+  if (t.bf16 && t.strides[1] == 1 && cs >= C && t.strides[2] == xv.shape[3] * cs &&
+      t.strides[0] == xv.shape[2] * xv.shape[3] * cs && t.off % 16 == 0 && cs % 4 == 0) {
+    x = t;
+  } else {
+    cs = round_up(C, 4);
+    x = as_nhwc_bf16(op.in[0], int(cs));
+  }
+  DevTensor y = alloc_nhwc(yv.shape, true, cs);
+  vt_[size_t(op.out[0])] = y;
+  const int N = int(xv.shape[0]), H = int(xv.shape[2]), W = int(xv.shape[3]);
+  const int Ho = int(yv.shape[2]), Wo = int(yv.shape[3]);
+  const int Cs = int(cs);
+  add_step("maxpool", {x}, {y}, [=]() {
+    const void* xp = ptr(x);
+    void* yp = ptr(y);
+    return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+      return k::maxpool_nhwc_bf16(xp, yp, N, H, W, Cs, Ho, Wo, int(op.kernel[0]), int(op.kernel[1]),
+                                  int(op.strides[0]), int(op.strides[1]), int(op.pads[0]), int(op.pads[1]),
+                                  int(op.dilations[0]), int(op.dilations[1]), s);
+    });
+  });
+}
+
+void Plan::plan_global_pool(const Op& op) {
+  const Value& xv = g_.vals[size_t(op.in[0])];
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  SB_CHECK(xv.shape.size() == 4, SB_UNSUPPORTED, "GlobalPool: rank-4 input required");
+  const DevTensor& t = vt_[size_t(op.in[0])];
+  const int64_t N = xv.shape[0], C = xv.shape[1], H = xv.shape[2], W = xv.shape[3];
+  DevTensor x = t;
+  int64_t ldp = t.strides[3];
+  bool nhwc = t.strides[1] == 1 && (t.strides[2] == W * ldp || H == 1) && (t.strides[0] == H * W * ldp || N == 1);
+  if (!nhwc) {
+    ldp = round_up(C, 4);
+    x = as_nhwc_bf16(op.in[0], int(ldp));
+  }
+  const bool out_bf16 = consumers_accept_bf16(op.out[0]);
+  DevTensor y = alloc_contig(yv.shape, out_bf16);
+  vt_[size_t(op.out[0])] = y;
+  const int is_max = op.type == "GlobalMaxPool";
+  add_step("global_pool", {x}, {y}, [=]() {
+    const void* xp = ptr(x);
+    void* yp = ptr(y);
+    int xb = x.bf16, yb = y.bf16;
+    return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+      return k::global_pool_nhwc(xp, xb, int(N), int(H * W), int(C), ldp, yp, yb, is_max, s);
+    });
+  });
+}
+
+void Plan::plan_elementwise(const Op& op) {
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  const int code = ew_code(op.type);
+  SB_CHECK(code >= 0, SB_UNSUPPORTED, "no device kernel for " + op.type);
+  std::vector<DevTensor> ins;
+  for (int id : op.in) {
+    if (id < 0) continue;
+    const Value& v = g_.vals[size_t(id)];
+    if (v.is_host) {
+      std::vector<float> f(size_t(v.host->numel()));
+      for (int64_t i = 0; i < v.host->numel(); ++i) f[size_t(i)] = float(v.host->get_f64(i));
+      DevTensor h;
+      h.buf = -1;
+      h.off = add_weight_bytes(f.data(), f.size() * 4);
+      h.shape = v.shape;
+      h.strides = contig_strides(v.shape);
+      ins.push_back(h);
+    } else {
+      ins.push_back(vt_[size_t(id)]);
+    }
+  }
+  // Output follows the physical order of the first same-shape dense input (keeps NHWC as NHWC).
+  DevTensor y;
+  const DevTensor* like = nullptr;
+  for (auto& t : ins)
+    if (t.shape == yv.shape && t.buf >= 0) {
+      like = &t;
+      break;
+    }
+  if (like && yv.shape.size() == 4 && like->strides[1] == 1 && !is_contig(*like)) {
+    const int64_t cs = yv.shape[1];
+    y = alloc_nhwc(yv.shape, false, cs);
+  } else {
+    y = alloc_contig(yv.shape, false);
+  }
+  vt_[size_t(op.out[0])] = y;
+  DevTensor a = broadcast_to(ins[0], yv.shape);
+  DevTensor b;
+  if (ins.size() > 1) b = broadcast_to(ins[1], yv.shape);
+  float alpha = op.alpha, beta = 0.f;
+  if (op.type == "Clip") {
+    alpha = op.fmin;
+    beta = op.fmax;
+  }
+  std::vector<DevTensor> reads{ins[0]};
+  if (ins.size() > 1) reads.push_back(ins[1]);
+  add_step("elementwise:" + op.type, reads, {y}, [=]() {
+    const void* ap = ptr(a);
+    const void* bp = b.valid() ? ptr(b) : nullptr;
+    void* yp = ptr(y);
+    k::TDesc ad = tdesc(a), bd = b.valid() ? tdesc(b) : k::TDesc{}, yd = tdesc(y);
+    int ab = a.bf16, bb = b.valid() ? int(b.bf16) : 0;
+    return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+      return k::elementwise(code, ap, ab, ad, bp, bb, bd, yp, 0, yd, alpha, beta, s);
+    });
+  });
+}
+
+void Plan::plan_view(const Op& op) {
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  DevTensor t = vt_[size_t(op.in[0])];
+  SB_CHECK(t.valid(), SB_INTERNAL, "view of an unplanned value");
+  if (op.type == "Identity") {
+    vt_[size_t(op.out[0])] = t;
+    return;
+  }
+  if (op.type == "Transpose") {
+    DevTensor r = t;
+    r.shape.clear();
+    r.strides.clear();
+    for (auto p : op.perm) {
+      r.shape.push_back(t.shape[size_t(p)]);
+      r.strides.push_back(t.strides[size_t(p)]);
+    }
+    vt_[size_t(op.out[0])] = r;
+    return;
+  }
+  if (op.type == "Slice") {
+    DevTensor r = t;
+    int64_t es = t.bf16 ? 2 : 4;
+    for (size_t d = 0; d < t.shape.size(); ++d) {
+      r.off += op.axes[d] * t.strides[d] * es;
+      r.strides[d] = t.strides[d] * op.strides[d];
+    }
+    r.shape = yv.shape;
+    vt_[size_t(op.out[0])] = r;
+    return;
+  }
+  if (op.type == "Expand") {
+    vt_[size_t(op.out[0])] = broadcast_to(t, yv.shape);
+    return;
+  }
+  // Reshape
+  auto vs = view_strides(t.shape, t.strides, yv.shape);
+  if (!vs) {
+    t = materialize(t, t.bf16);
+    vs = contig_strides(yv.shape);
+  }
+  DevTensor r = t;
+  r.shape = yv.shape;
+  r.strides = *vs;
+  vt_[size_t(op.out[0])] = r;
+}
+
+void Plan::plan_concat(const Op& op) {
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  DevTensor y = alloc_contig(yv.shape, false);
+  vt_[size_t(op.out[0])] = y;
+  int64_t off = 0;
+  for (int id : op.in) {
+    const Value& v = g_.vals[size_t(id)];
+    DevTensor src;
+    if (v.is_host) {
+      std::vector<float> f(size_t(v.host->numel()));
+      for (int64_t i = 0; i < v.host->numel(); ++i) f[size_t(i)] = float(v.host->get_f64(i));
+      src.buf = -1;
+      src.off = add_weight_bytes(f.data(), f.size() * 4);
+      src.shape = v.shape;
+      src.strides = contig_strides(v.shape);
+    } else {
+      src = vt_[size_t(id)];
+    }
+    DevTensor dst = y;
+    dst.shape = v.shape;
+    dst.off = off * y.strides[size_t(op.axis)] * 4;
+    off += v.shape[size_t(op.axis)];
+    if (numel(v.shape) == 0) continue;
+    add_step("concat_copy", {src}, {y}, [this, src, dst]() {
+      const void* sp = ptr(src);
+      void* dp = ptr(dst);
+      k::TDesc sd = tdesc(src), dd = tdesc(dst);
+      int sb = src.bf16;
+      return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+        return k::strided_copy(sp, sb, sd, dp, 0, dd, s);
+      });
+    });
+  }
+}
+
+void Plan::plan_softmax(const Op& op) {
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  DevTensor x = as_f32_contig(op.in[0]);
+  DevTensor y = alloc_contig(yv.shape, false);
+  vt_[size_t(op.out[0])] = y;
+  int64_t outer = 1, inner = 1;
+  for (int64_t d = 0; d < op.axis; ++d) outer *= yv.shape[size_t(d)];
+  for (size_t d = size_t(op.axis) + 1; d < yv.shape.size(); ++d) inner *= yv.shape[d];
+  const int64_t len = yv.shape.empty() ? 1 : yv.shape[size_t(op.axis)];
+  add_step("softmax", {x}, {y}, [=]() {
+    const float* xp = static_cast<const float*>(ptr(x));
+    float* yp = static_cast<float*>(ptr(y));
+    return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+      return k::softmax(xp, yp, outer, len, inner, s);
+    });
+  });
+}
+
+void Plan::plan_reduce(const Op& op) {
+  const Value& xv = g_.vals[size_t(op.in[0])];
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  const int kind = op.type == "ReduceMax" ? 2 : 0;
+  DevTensor cur = as_f32_contig(op.in[0]);
+  std::vector<int64_t> shape = xv.shape;
+  int64_t count = 1;
+  // reduce one axis at a time from the innermost (keepdims), then a mean scale if needed
+  std::vector<int64_t> axes = op.axes;
+  std::sort(axes.rbegin(), axes.rend());
+  for (int64_t a : axes) {
+    int64_t outer = 1, inner = 1;
+    for (int64_t d = 0; d < a; ++d) outer *= shape[size_t(d)];
+    for (size_t d = size_t(a) + 1; d < shape.size(); ++d) inner *= shape[d];
+    const int64_t len = shape[size_t(a)];
+    count *= len;
+    shape[size_t(a)] = 1;
+    DevTensor nx = alloc_contig(shape, false);
+    DevTensor src = cur;
+    add_step("reduce", {src}, {nx}, [=]() {
+      const float* xp = static_cast<const float*>(ptr(src));
+      float* yp = static_cast<float*>(ptr(nx));
+      return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+        return k::reduce_mid(xp, yp, outer, len, inner, kind, s);
+      });
+    });
+    cur = nx;
+  }
+  if (op.type == "ReduceMean" && count > 1) {
+    DevTensor nx = alloc_contig(shape, false);
+    DevTensor src = cur;
+    const float inv = 1.f / float(count);
+    std::vector<float> c{inv};
+    DevTensor ct;
+    ct.buf = -1;
+    ct.off = add_weight_bytes(c.data(), 4);
+    ct.shape = {};
+    ct.strides = {};
+    DevTensor cb = broadcast_to(ct, shape);
+    add_step("reduce_scale", {src}, {nx}, [=]() {
+      const void* xp = ptr(src);
+      const void* cp = ptr(cb);
+      void* yp = ptr(nx);
+      k::TDesc d = tdesc(src), cd = tdesc(cb), yd = tdesc(nx);
+      return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+        return k::elementwise(k::EW_MUL, xp, 0, d, cp, 0, cd, yp, 0, yd, 0.f, 0.f, s);
+      });
+    });
+    cur = nx;
+  }
+  cur.shape = yv.shape;
+  cur.strides = contig_strides(yv.shape);
+  vt_[size_t(op.out[0])] = cur;
+}
+
+void Plan::plan_pad(const Op& op) {
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  DevTensor x = vt_[size_t(op.in[0])];
+  DevTensor y = alloc_contig(yv.shape, false);
+  vt_[size_t(op.out[0])] = y;
+  const int64_t n = numel(yv.shape);
+  const float val = op.alpha;
+  add_step("pad_fill", {}, {y}, [=]() {
+    void* yp = ptr(y);
+    return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) { return k::fill_f32(yp, n, val, s); });
+  });
+  DevTensor dst = y;
+  const size_t r = yv.shape.size();
+  dst.shape = x.shape;
+  for (size_t d = 0; d < r; ++d) dst.off += op.pads[d] * y.strides[d] * 4;
+  add_step("pad_copy", {x}, {y}, [=]() {
+    const void* xp = ptr(x);
+    void* dp = ptr(dst);
+    k::TDesc xd = tdesc(x), dd = tdesc(dst);
+    int xb = x.bf16;
+    return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+      return k::strided_copy(xp, xb, xd, dp, 0, dd, s);
+    });
+  });
+}
+
+void Plan::plan_resize(const Op& op) {
+  const Value& xv = g_.vals[size_t(op.in[0])];
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  DevTensor x = vt_[size_t(op.in[0])];
+  DevTensor y = alloc_contig(yv.shape, false);
+  vt_[size_t(op.out[0])] = y;
+  // per-axis nearest index tables (ONNX Resize, mode=nearest)
+  std::vector<int64_t> tables;
+  for (size_t d = 0; d < yv.shape.size(); ++d) {
+    const int64_t in_len = xv.shape[d], out_len = yv.shape[d];
+    const double scale = double(op.scales[d]);
+    for (int64_t o = 0; o < out_len; ++o) {
+      double xo;
+      if (op.coord_mode == "asymmetric") xo = double(o) / scale;
+      else if (op.coord_mode == "align_corners") xo = out_len > 1 ? double(o) * double(in_len - 1) / double(out_len - 1) : 0.0;
+      else if (op.coord_mode == "pytorch_half_pixel") xo = out_len > 1 ? (double(o) + 0.5) / scale - 0.5 : 0.0;
+      else if (op.coord_mode == "half_pixel") xo = (double(o) + 0.5) / scale - 0.5;
+      else fail(SB_UNSUPPORTED, "Resize: coordinate_transformation_mode " + op.coord_mode);
+      double idx;
+      const double fl = std::floor(xo);
+      if (op.nearest_mode == "floor") idx = fl;
+      else if (op.nearest_mode == "ceil") idx = std::ceil(xo);
+      else if (op.nearest_mode == "round_prefer_ceil") idx = (xo - fl == 0.5) ? fl + 1 : std::nearbyint(xo);
+      else idx = (xo - fl == 0.5) ? fl : std::round(xo);
+      tables.push_back(std::clamp<int64_t>(int64_t(idx), 0, in_len - 1));
+    }
+  }
+  DevTensor tt;
+  tt.buf = -1;
+  tt.off = add_weight_bytes(tables.data(), tables.size() * 8);
+  add_step("resize_nearest", {x}, {y}, [=]() {
+    const void* xp = ptr(x);
+    const int64_t* tp = static_cast<const int64_t*>(ptr(tt));
+    void* yp = ptr(y);
+    k::TDesc xd = tdesc(x), yd = tdesc(y);
+    int xb = x.bf16;
+    return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+      return k::gather_axes(xp, xb, xd, tp, yp, 0, yd, s);
+    });
+  });
+}
+
+// ---------------------------------------------------------------------------------------------
+void Plan::build() {
+  vt_.assign(g_.vals.size(), DevTensor{});
+  consumers_.assign(g_.vals.size(), {});
+  is_output_.assign(g_.vals.size(), false);
+  for (size_t i = 0; i < g_.ops.size(); ++i) {
+    const Op& op = g_.ops[i];
+    if (op.dead) continue;
+    for (int id : op.in)
+      if (id >= 0) consumers_[size_t(id)].push_back(int(i));
+    if (op.residual >= 0) consumers_[size_t(op.residual)].push_back(int(i));
+  }
+  for (int id : g_.outputs) is_output_[size_t(id)] = true;
+
+  // Host-known operands read by device ops (plan-time inputs, folded constants) live in the
+  // weights blob as f32 contiguous tensors.
+  for (const Op& op : g_.ops) {
+    if (op.dead) continue;
+    std::vector<int> ids = op.in;
+    if (op.residual >= 0) ids.push_back(op.residual);
+    for (int id : ids) {
+      if (id < 0 || vt_[size_t(id)].valid()) continue;
+      const Value& v = g_.vals[size_t(id)];
+      if (!v.is_host) continue;
+      std::vector<float> f(size_t(v.host->numel()));
+      for (int64_t i = 0; i < v.host->numel(); ++i) f[size_t(i)] = float(v.host->get_f64(i));
+      DevTensor h;
+      h.buf = -1;
+      h.off = add_weight_bytes(f.data(), f.size() * 4);
+      h.shape = v.shape;
+      h.strides = contig_strides(v.shape);
+      vt_[size_t(id)] = h;
+    }
+  }
+
+  // graph inputs: f32 contiguous buffers filled by H2D
+  for (size_t k = 0; k < g_.inputs.size(); ++k) {
+    const Value& v = g_.vals[size_t(g_.inputs[k])];
+    if (v.is_host) continue;
+    DevTensor t = alloc_contig(v.shape, false);
+    bufs_[size_t(t.buf)].first = -1;
+    vt_[size_t(g_.inputs[k])] = t;
+    inputs_.push_back({int(k), t.buf, size_t(numel(v.shape)) * 4});
+  }
+
+  for (size_t i = 0; i < g_.ops.size(); ++i) {
+    const Op& op = g_.ops[i];
+    if (op.dead) continue;
+    const std::string& t = op.type;
+    if (t == "FusedConv") plan_conv(op);
+    else if (t == "FusedGemm") plan_gemm(op);
+    else if (t == "MaxPool") plan_maxpool(op);
+    else if (t == "GlobalAveragePool" || t == "GlobalMaxPool") plan_global_pool(op);
+    else if (is_view_op(t)) plan_view(op);
+    else if (t == "Concat") plan_concat(op);
+    else if (t == "Softmax") plan_softmax(op);
+    else if (t == "ReduceMean" || t == "ReduceSum" || t == "ReduceMax") plan_reduce(op);
+    else if (t == "Pad") plan_pad(op);
+    else if (t == "Resize") plan_resize(op);
+    else if (ew_code(t) >= 0) plan_elementwise(op);
+    else if (t == "Conv") fail(SB_INTERNAL, "Conv was not fused");
+    else if (t == "MatMul" || t == "Gemm")
+      fail(SB_UNSUPPORTED, t + " with a non-constant weight operand is not supported");
+    else fail(SB_UNSUPPORTED, "no device plan for operator " + t);
+  }
+
+  for (size_t j = 0; j < g_.outputs.size(); ++j) {
+    const int id = g_.outputs[j];
+    const Value& v = g_.vals[size_t(id)];
+    OutputBinding ob;
+    ob.shape = v.shape;
+    if (v.is_host) {
+      ob.host = true;
+      ob.value = v.host;
+    } else {
+      DevTensor t = vt_[size_t(id)];
+      SB_CHECK(t.valid(), SB_INTERNAL, "graph output was not planned");
+      if (t.bf16 || !is_contig(t) || t.buf < 0) t = materialize(t, false);
+      bufs_[size_t(t.buf)].last = 1 << 30;
+      ob.dev = t;
+    }
+    outputs_.push_back(ob);
+  }
+}
+
+void Plan::allocate_and_finalize() {
+  // Best-fit offsets by decreasing size; two buffers may share memory only if their step ranges
+  // [first, last] do not overlap.
+  std::vector<int> order(bufs_.size());
+  std::iota(order.begin(), order.end(), 0);
+  std::sort(order.begin(), order.end(), [&](int a, int b) { return bufs_[size_t(a)].bytes > bufs_[size_t(b)].bytes; });
+  std::vector<int> placed;
+  size_t total = 0;
+  for (int bi : order) {
+    Buffer& b = bufs_[size_t(bi)];
+    if (b.last < b.first) {   // never used (e.g. dead view); still give it a slot at the end
+      b.first = b.last = 1 << 29;
+    }
+    std::vector<std::pair<size_t, size_t>> busy;
+    for (int pj : placed) {
+      const Buffer& o = bufs_[size_t(pj)];
+      if (o.first <= b.last && b.first <= o.last) busy.push_back({o.offset, o.offset + o.bytes});
+    }
+    std::sort(busy.begin(), busy.end());
+    size_t off = 0;
+    size_t best = SIZE_MAX, best_gap = SIZE_MAX;
+    for (auto& iv : busy) {
+      if (iv.first >= off + b.bytes) {
+        size_t gap = iv.first - off;
+        if (gap < best_gap) {
+          best_gap = gap;
+          best = off;
+        }
+      }
+      off = std::max(off, iv.second);
+    }
+    if (best == SIZE_MAX) best = off;
+    b.offset = best;
+    total = std::max(total, best + b.bytes);
+    placed.push_back(bi);
+  }
+  stats_.arena_bytes = total;
+  stats_.weight_bytes = wblob_.size();
+
+  ck(cudaSetDevice(device_), "cudaSetDevice");
+  ck(cudaMalloc(&arena_, std::max<size_t>(total, kAlign)), "arena allocation");
+  ck(cudaMalloc(&weights_, std::max<size_t>(wblob_.size(), kAlign)), "weight allocation");
+  if (!wblob_.empty()) ck(cudaMemcpy(weights_, wblob_.data(), wblob_.size(), cudaMemcpyHostToDevice), "weight upload");
+  wblob_.clear();
+  wblob_.shrink_to_fit();
+  ck(cudaMalloc(&err_, sizeof(unsigned int)), "error word allocation");
+  ck(cudaMemset(err_, 0, sizeof(unsigned int)), "error word init");
+
+  for (auto& p : pending_) {
+    kinds_.push_back(p.kind);
+    steps_.push_back(p.build());
+  }
+  pending_.clear();
+
+  // Capture the kernel sequence once.
+  cudaStream_t s;
+  ck(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream create");
+  bool ok = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+  if (ok) {
+    for (auto& st : steps_)
+      if (st(s) != cudaSuccess) ok = false;
+    cudaGraph_t gph = nullptr;
+    cudaError_t e = cudaStreamEndCapture(s, &gph);
+    if (ok && e == cudaSuccess && gph) {
+      graph_ = gph;
+      if (cudaGraphInstantiate(&exec_, graph_, 0) != cudaSuccess) {
+        exec_ = nullptr;
+      }
+    } else if (gph) {
+      cudaGraphDestroy(gph);
+    }
+  }
+  cudaGetLastError();   // clear capture errors; steps are replayed directly below if needed
+  cudaStreamDestroy(s);
+  if (debug_level() >= 1)
+    std::fprintf(stderr, "[shorokoo_b200] plan dev%d: %zu launches (%lld tensor-core), arena %.1f MB, weights %.1f MB, %s\n",
+                 device_, steps_.size(), (long long)stats_.tc_kernels, double(stats_.arena_bytes) / 1e6,
+                 double(stats_.weight_bytes) / 1e6, exec_ ? "cuda graph" : "direct launches");
+}
+
+void Plan::enqueue_kernels(cudaStream_t stream) {
+  if (exec_) {
+    ck(cudaGraphLaunch(exec_, stream), "graph launch");
+  } else {
+    for (auto& st : steps_) ck(st(stream), "kernel launch");
+  }
+}
+
+void Plan::enqueue(cudaStream_t stream, const std::vector<const void*>& host_in, const std::vector<void*>& host_out) {
+  for (auto& ib : inputs_) {
+    SB_CHECK(size_t(ib.index) < host_in.size() && host_in[size_t(ib.index)], SB_INVALID_ARGUMENT, "missing input data");
+    ck(cudaMemcpyAsync(buffer_ptr(ib.buf), host_in[size_t(ib.index)], ib.bytes, cudaMemcpyHostToDevice, stream), "H2D");
+  }
+  enqueue_kernels(stream);
+  for (size_t j = 0; j < outputs_.size(); ++j) {
+    const OutputBinding& ob = outputs_[j];
+    if (ob.host || !host_out[j]) continue;
+    ck(cudaMemcpyAsync(host_out[j], ptr(ob.dev), size_t(numel(ob.shape)) * 4, cudaMemcpyDeviceToHost, stream), "D2H");
+  }
+}
+
+std::vector<std::pair<std::string, double>> Plan::profile(cudaStream_t stream, int iters) {
+  std::vector<std::pair<std::string, double>> out;
+  cudaEvent_t e0, e1;
+  ck(cudaEventCreate(&e0), "event");
+  ck(cudaEventCreate(&e1), "event");
+  for (size_t i = 0; i < steps_.size(); ++i) {
+    ck(steps_[i](stream), "kernel launch");   // warm
+    ck(cudaEventRecord(e0, stream), "event record");
+    for (int r = 0; r < iters; ++r) ck(steps_[i](stream), "kernel launch");
+    ck(cudaEventRecord(e1, stream), "event record");
+    ck(cudaEventSynchronize(e1), "event sync");
+    float t = 0;
+    ck(cudaEventElapsedTime(&t, e0, e1), "elapsed");
+    out.push_back({kinds_[i], double(t) / std::max(iters, 1)});
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  return out;
+}
+
+void Plan::check_device_error() {
+  unsigned int e = 0;
+  ck(cudaMemcpy(&e, err_, sizeof(e), cudaMemcpyDeviceToHost), "error word read");
+  if (e) {
+    cudaMemset(err_, 0, sizeof(unsigned int));
+    fail(SB_CUDA_ERROR, "device pipeline wait timed out (error word " + std::to_string(e) + ")");
+  }
+}
+
+}  // namespace sb

@@ -1,0 +1,137 @@
+// Execution plan for one device: every live op of the fused graph becomes one or more kernel
+// launches over a static activation arena; weights live in one packed device blob. The launch
+// sequence is captured once into a CUDA graph and replayed per run.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "ir.h"
+#include "kernels/kernels.h"
+
+namespace sb {
+
+void fuse(LGraph& g);
+
+struct DevTensor {
+  int buf = -2;            // arena buffer id; -1 = weights blob; -2 = invalid
+  int64_t off = 0;         // bytes from the buffer start
+  bool bf16 = false;
+  std::vector<int64_t> shape, strides;   // logical shape, element strides
+  bool valid() const { return buf != -2; }
+};
+
+struct PlanStats {
+  int64_t kernels = 0;          // kernel launches per run
+  int64_t tc_kernels = 0;       // tensor-core (tcgen05) launches per run
+  double macs = 0;              // algorithmic multiply-accumulates (Conv/MatMul) per run
+  size_t arena_bytes = 0, weight_bytes = 0;
+};
+
+struct InputBinding {
+  int index;               // session input index
+  int buf;                 // arena buffer receiving the H2D copy
+  size_t bytes;
+};
+
+struct OutputBinding {
+  bool host = false;                 // value folded at plan time
+  std::shared_ptr<HostTensor> value; // when host
+  DevTensor dev;                     // f32 contiguous when !host
+  std::vector<int64_t> shape;
+};
+
+class Plan {
+ public:
+  Plan(LGraph g, int device, int num_sms);
+  ~Plan();
+  Plan(const Plan&) = delete;
+  Plan& operator=(const Plan&) = delete;
+
+  // Enqueues H2D of inputs, the captured kernel graph and D2H of outputs on `stream`.
+  // host_in[i] points at session input i (nullptr for plan-time inputs); host_out[j] receives
+  // output j (device outputs only; host outputs are copied by the caller).
+  void enqueue(cudaStream_t stream, const std::vector<const void*>& host_in, const std::vector<void*>& host_out);
+  // Runs only the kernel sequence (inputs already resident); used for device-side timing.
+  void enqueue_kernels(cudaStream_t stream);
+  // Checks and clears the device error word written by bounded waits.
+  void check_device_error();
+  // Times every launch of the sequence on its own (`iters` repetitions each, CUDA events on
+  // `stream`); returns (kind, milliseconds per launch) in launch order.
+  std::vector<std::pair<std::string, double>> profile(cudaStream_t stream, int iters);
+
+  const std::vector<OutputBinding>& outputs() const { return outputs_; }
+  const std::vector<InputBinding>& inputs() const { return inputs_; }
+  const PlanStats& stats() const { return stats_; }
+  int device() const { return device_; }
+  void* buffer_ptr(int buf) const;
+
+ private:
+  struct Buffer {
+    size_t bytes = 0;
+    int first = 1 << 30, last = -1;
+    size_t offset = 0;
+  };
+  struct PendingStep {
+    std::string kind;
+    std::function<std::function<cudaError_t(cudaStream_t)>()> build;   // run after allocation
+    std::vector<DevTensor> reads, writes;
+  };
+
+  LGraph g_;
+  int device_;
+  int num_sms_;
+  std::vector<DevTensor> vt_;       // per value id
+  std::vector<Buffer> bufs_;
+  std::vector<PendingStep> pending_;
+  std::vector<std::function<cudaError_t(cudaStream_t)>> steps_;
+  std::vector<std::string> kinds_;
+  std::vector<uint8_t> wblob_;      // host staging of the weights blob
+  std::vector<InputBinding> inputs_;
+  std::vector<OutputBinding> outputs_;
+  PlanStats stats_;
+  void* arena_ = nullptr;
+  void* weights_ = nullptr;
+  unsigned int* err_ = nullptr;
+  cudaGraph_t graph_ = nullptr;
+  cudaGraphExec_t exec_ = nullptr;
+  std::vector<std::vector<int>> consumers_;
+  std::vector<bool> is_output_;
+  std::map<std::pair<int, int>, DevTensor> conv_cache_;   // (value, Cp) -> NHWC bf16 copy
+  std::map<int, DevTensor> rows_cache_;                    // value -> bf16 rows copy
+
+  void build();
+  void allocate_and_finalize();
+  int new_buffer(size_t bytes);
+  DevTensor alloc_contig(const std::vector<int64_t>& shape, bool bf16);
+  DevTensor alloc_nhwc(const std::vector<int64_t>& shape_nchw, bool bf16, int64_t cstride);
+  int64_t add_weight_bytes(const void* data, size_t bytes);
+  void* ptr(const DevTensor& t) const;
+  void add_step(const std::string& kind, std::vector<DevTensor> reads, std::vector<DevTensor> writes,
+                std::function<std::function<cudaError_t(cudaStream_t)>()> build);
+
+  bool consumers_accept_bf16(int v) const;
+  DevTensor as_nhwc_bf16(int v, int Cp);
+  DevTensor as_rows_bf16(int v, int64_t M, int64_t K);
+  DevTensor as_f32_contig(int v);
+  DevTensor materialize(const DevTensor& src, bool bf16);
+
+  void plan_conv(const Op& op);
+  void plan_gemm(const Op& op);
+  void plan_maxpool(const Op& op);
+  void plan_global_pool(const Op& op);
+  void plan_elementwise(const Op& op);
+  void plan_view(const Op& op);
+  void plan_concat(const Op& op);
+  void plan_softmax(const Op& op);
+  void plan_reduce(const Op& op);
+  void plan_pad(const Op& op);
+  void plan_resize(const Op& op);
+  void plan_avgpool(const Op& op);
+};
+
+}  // namespace sb

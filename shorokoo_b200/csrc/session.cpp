@@ -1,0 +1,544 @@
+// Session: model parsing at creation (unsupported operators are a hard error here, as the
+// reference's CreateSession contract requires), a plan cache keyed by input shapes and plan-time
+// input values, and batch sharding across devices with replicated weights and no collective.
+#include "session.h"
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <functional>
+#include <set>
+#include <thread>
+
+namespace sb {
+
+int debug_level() {
+  static int lvl = [] {
+    const char* e = std::getenv("SHOROKOO_B200_DEBUG");
+    return e ? std::atoi(e) : 0;
+  }();
+  return lvl;
+}
+
+namespace {
+
+inline void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    if (e == cudaErrorMemoryAllocation) fail(SB_OUT_OF_MEMORY, std::string(what) + ": " + cudaGetErrorString(e));
+    fail(SB_CUDA_ERROR, std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+
+// ---- host memory: pinned (page-locked) when a CUDA device exists, pooled for reuse ------------
+constexpr size_t kPinnedMin = size_t(1) << 20;
+constexpr size_t kPoolMaxBytes = size_t(16) << 30;
+
+struct HostPool {
+  std::mutex mu;
+  std::multimap<size_t, void*> free_blocks;
+  size_t pooled = 0;
+  int cuda_ok = -1;
+
+  bool have_cuda() {
+    if (cuda_ok < 0) {
+      int n = 0;
+      cuda_ok = (cudaGetDeviceCount(&n) == cudaSuccess && n > 0) ? 1 : 0;
+      cudaGetLastError();
+    }
+    return cuda_ok == 1;
+  }
+
+  void* alloc(size_t bytes, bool& pinned) {
+    pinned = false;
+    if (bytes >= kPinnedMin) {
+      size_t sz = (bytes + kPinnedMin - 1) / kPinnedMin * kPinnedMin;
+      {
+        std::lock_guard<std::mutex> l(mu);
+        auto it = free_blocks.lower_bound(sz);
+        if (it != free_blocks.end() && it->first <= sz + sz / 4) {
+          void* p = it->second;
+          pooled -= it->first;
+          free_blocks.erase(it);
+          pinned = true;
+          return p;
+        }
+      }
+      if (have_cuda()) {
+        void* p = nullptr;
+        if (cudaHostAlloc(&p, sz, cudaHostAllocPortable) == cudaSuccess) {
+          pinned = true;
+          return p;
+        }
+        cudaGetLastError();
+      }
+    }
+    void* p = std::aligned_alloc(64, std::max<size_t>((bytes + 63) / 64 * 64, 64));
+    SB_CHECK(p != nullptr, SB_OUT_OF_MEMORY, "host allocation failed");
+    return p;
+  }
+
+  void release(void* p, size_t bytes, bool pinned) {
+    if (!p) return;
+    if (!pinned) {
+      std::free(p);
+      return;
+    }
+    size_t sz = (bytes + kPinnedMin - 1) / kPinnedMin * kPinnedMin;
+    std::lock_guard<std::mutex> l(mu);
+    if (pooled + sz <= kPoolMaxBytes) {
+      free_blocks.emplace(sz, p);
+      pooled += sz;
+    } else {
+      cudaFreeHost(p);
+    }
+  }
+};
+
+HostPool& pool() {
+  static HostPool* p = new HostPool();   // intentionally leaked: outlives static destructors
+  return *p;
+}
+
+// Parallel memcpy for large host copies.
+void par_memcpy(void* dst, const void* src, size_t n) {
+  const size_t chunk = size_t(64) << 20;
+  if (n < 2 * chunk) {
+    std::memcpy(dst, src, n);
+    return;
+  }
+  unsigned nt = std::min<unsigned>(8, std::max(1u, std::thread::hardware_concurrency()));
+  std::vector<std::thread> th;
+  size_t per = (n + nt - 1) / nt;
+  for (unsigned i = 0; i < nt; ++i) {
+    size_t b = i * per, e = std::min(n, b + per);
+    if (b >= e) break;
+    th.emplace_back([=] { std::memcpy(static_cast<uint8_t*>(dst) + b, static_cast<const uint8_t*>(src) + b, e - b); });
+  }
+  for (auto& t : th) t.join();
+}
+
+}  // namespace
+
+void* host_alloc(size_t bytes, bool& pinned) { return pool().alloc(bytes, pinned); }
+void host_release(void* p, size_t bytes, bool pinned) { pool().release(p, bytes, pinned); }
+void host_copy(void* dst, const void* src, size_t n) { par_memcpy(dst, src, n); }
+
+HostValue::~HostValue() {
+  if (owned && data) pool().release(data, nbytes, pinned);
+}
+
+std::shared_ptr<HostValue> HostValue::alloc_tensor(int32_t elem_type, const std::vector<int64_t>& shape) {
+  auto v = std::make_shared<HostValue>();
+  v->kind = TENSOR;
+  v->elem_type = elem_type;
+  v->shape = shape;
+  v->nbytes = size_t(numel(shape)) * dtype_size(elem_type);
+  bool pinned = false;
+  v->data = pool().alloc(std::max<size_t>(v->nbytes, 1), pinned);
+  v->pinned = pinned;
+  v->owned = true;
+  return v;
+}
+
+// ---- batch separability --------------------------------------------------------------------
+// Every device value gets the axis that carries the batch (-1: no batch dependence, -2: mixed).
+// A graph shards cleanly when every op keeps samples independent and every output carries the
+// batch on axis 0.
+bool batch_separable(const LGraph& g) {
+  std::vector<int> ax(g.vals.size(), -1);
+  for (int id : g.inputs) {
+    const Value& v = g.vals[size_t(id)];
+    if (!v.is_host) {
+      if (v.shape.empty()) return false;
+      ax[size_t(id)] = 0;
+    }
+  }
+  auto host_ok = [&](int id, int axis, size_t out_rank) {
+    // a plan-time constant must not vary along the batch axis of the output
+    const Value& v = g.vals[size_t(id)];
+    if (axis < 0) return true;
+    size_t off = out_rank - v.shape.size();
+    if (size_t(axis) < off) return true;
+    return v.shape[size_t(axis) - off] == 1;
+  };
+  for (const Op& op : g.ops) {
+    if (op.dead) continue;
+    const Value& y = g.vals[size_t(op.out[0])];
+    int a0 = op.in.empty() || op.in[0] < 0 ? -1 : ax[size_t(op.in[0])];
+    if (a0 == -2) return false;
+    int out = -2;
+    const std::string& t = op.type;
+    if (t == "FusedConv" || t == "MaxPool" || t == "GlobalAveragePool" || t == "GlobalMaxPool" ||
+        t == "AveragePool") {
+      if (a0 != 0) return false;
+      if (op.residual >= 0 && ax[size_t(op.residual)] != 0) return false;
+      out = 0;
+    } else if (t == "FusedGemm") {
+      if (a0 != 0 || g.vals[size_t(op.in[0])].shape.size() < 2) return false;
+      if (op.residual >= 0 && ax[size_t(op.residual)] != 0) return false;
+      out = 0;
+    } else if (t == "Identity") {
+      out = a0;
+    } else if (t == "Transpose") {
+      out = -1;
+      for (size_t i = 0; i < op.perm.size(); ++i)
+        if (op.perm[i] == a0) out = int(i);
+      if (a0 >= 0 && out < 0) return false;
+    } else if (t == "Reshape") {
+      const auto& xs = g.vals[size_t(op.in[0])].shape;
+      if (a0 < 0) out = -1;
+      else if (a0 == 0 && !y.shape.empty() && y.shape[0] == xs[0]) out = 0;
+      else return false;
+    } else if (t == "Slice") {
+      if (a0 >= 0 && (op.axes[size_t(a0)] != 0 || op.strides[size_t(a0)] != 1 ||
+                      y.shape[size_t(a0)] != g.vals[size_t(op.in[0])].shape[size_t(a0)]))
+        return false;
+      out = a0;
+    } else if (t == "Expand") {
+      out = a0 >= 0 ? a0 + int(y.shape.size() - g.vals[size_t(op.in[0])].shape.size()) : -1;
+    } else if (t == "Concat" || t == "Softmax") {
+      out = -1;
+      for (int id : op.in) {
+        if (id < 0) continue;
+        int ai = ax[size_t(id)];
+        if (ai == -2) return false;
+        if (ai >= 0) {
+          if (out >= 0 && out != ai) return false;
+          out = ai;
+        }
+      }
+      if (out >= 0 && out == int(op.axis)) return false;
+      for (int id : op.in)
+        if (id >= 0 && ax[size_t(id)] < 0 && out >= 0 && !g.vals[size_t(id)].is_host) return false;
+    } else if (t == "Pad") {
+      if (a0 >= 0 && (op.pads[size_t(a0)] != 0 || op.pads[size_t(a0) + y.shape.size()] != 0)) return false;
+      out = a0;
+    } else if (t == "Resize") {
+      if (a0 >= 0 && op.scales[size_t(a0)] != 1.f) return false;
+      out = a0;
+    } else if (t == "ReduceMean" || t == "ReduceSum" || t == "ReduceMax") {
+      if (a0 >= 0 && std::find(op.axes.begin(), op.axes.end(), a0) != op.axes.end()) return false;
+      int removed = 0;
+      if (!op.keepdims)
+        for (auto a : op.axes)
+          if (a < a0) ++removed;
+      out = a0 >= 0 ? a0 - removed : -1;
+    } else {
+      // elementwise (broadcasting)
+      out = -1;
+      for (int id : op.in) {
+        if (id < 0) continue;
+        const Value& v = g.vals[size_t(id)];
+        int ai = ax[size_t(id)];
+        if (ai == -2) return false;
+        if (ai >= 0) {
+          int aligned = ai + int(y.shape.size() - v.shape.size());
+          if (out >= 0 && out != aligned) return false;
+          out = aligned;
+        }
+      }
+      for (int id : op.in)
+        if (id >= 0 && ax[size_t(id)] < 0 && !host_ok(id, out, y.shape.size())) return false;
+    }
+    for (int o : op.out) ax[size_t(o)] = out;
+  }
+  for (int id : g.outputs)
+    if (g.vals[size_t(id)].is_host || ax[size_t(id)] != 0) return false;
+  return true;
+}
+
+// ---- Session -------------------------------------------------------------------------------
+Session::Session(const uint8_t* model, size_t len, const SessionOptions& opt) : opt_(opt) {
+  model_ = parse_onnx(model, len);
+  check_supported_ops(model_);
+  info_ = model_info(model_);
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    fail(SB_CUDA_ERROR, "no CUDA device is available for the B200 backend");
+  }
+  int want = opt.num_devices;
+  if (want <= 0) {
+    const char* e = std::getenv("SHOROKOO_B200_DEVICES");
+    want = e ? std::atoi(e) : count;
+  }
+  want = std::max(1, std::min(want, count - opt.first_device));
+  SB_CHECK(opt.first_device >= 0 && opt.first_device < count, SB_INVALID_ARGUMENT, "first_device out of range");
+  for (int d = 0; d < want; ++d) {
+    const int dev = opt.first_device + d;
+    cudaDeviceProp prop;
+    ck(cudaGetDeviceProperties(&prop, dev), "cudaGetDeviceProperties");
+    SB_CHECK(prop.major == 10 && prop.minor == 0, SB_UNSUPPORTED,
+             std::string("device ") + std::to_string(dev) + " (" + prop.name +
+                 ") is not sm_100; this backend ships sm_100a kernels only");
+    devices_.push_back(dev);
+    sm_counts_.push_back(prop.multiProcessorCount);
+    ck(cudaSetDevice(dev), "cudaSetDevice");
+    cudaStream_t s;
+    ck(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
+    streams_.push_back(s);
+  }
+}
+
+Session::~Session() {
+  cache_.clear();
+  for (size_t i = 0; i < streams_.size(); ++i) {
+    cudaSetDevice(devices_[i]);
+    cudaStreamDestroy(streams_[i]);
+  }
+}
+
+std::vector<InputSpec> Session::specs_for(const std::vector<std::shared_ptr<HostValue>>& inputs, int64_t b0,
+                                          int64_t cnt, bool shard) const {
+  std::vector<InputSpec> specs;
+  for (size_t i = 0; i < inputs.size(); ++i) {
+    const HostValue& v = *inputs[i];
+    InputSpec s;
+    s.dtype = v.elem_type;
+    s.shape = v.shape;
+    if (numel(v.shape) <= kPlanTimeInputMaxElems) {
+      auto h = std::make_shared<HostTensor>(v.elem_type, v.shape);
+      if (v.nbytes) std::memcpy(h->mutable_data(), v.data, v.nbytes);
+      s.value = h;
+    } else if (shard) {
+      s.shape[0] = cnt;
+      (void)b0;
+    }
+    specs.push_back(std::move(s));
+  }
+  return specs;
+}
+
+std::shared_ptr<Session::PlanSet> Session::get_plans(const std::vector<std::shared_ptr<HostValue>>& inputs) {
+  SB_CHECK(inputs.size() == info_.input_names.size(), SB_INVALID_ARGUMENT,
+           "expected " + std::to_string(info_.input_names.size()) + " inputs, got " + std::to_string(inputs.size()));
+  std::string key;
+  for (size_t i = 0; i < inputs.size(); ++i) {
+    const HostValue& v = *inputs[i];
+    SB_CHECK(v.kind == HostValue::TENSOR, SB_UNSUPPORTED, "input '" + info_.input_names[i] + "': sequences are not supported");
+    SB_CHECK(v.elem_type != DT_STRING, SB_UNSUPPORTED, "input '" + info_.input_names[i] + "': string tensors are not supported");
+    if (info_.input_dtypes[i] != DT_UNDEFINED)
+      SB_CHECK(v.elem_type == info_.input_dtypes[i], SB_INVALID_ARGUMENT,
+               "input '" + info_.input_names[i] + "' expects " + dtype_name(info_.input_dtypes[i]) + ", got " +
+                   dtype_name(v.elem_type));
+    if (info_.input_ranks[i] >= 0)
+      SB_CHECK(int(v.shape.size()) == info_.input_ranks[i], SB_INVALID_ARGUMENT,
+               "input '" + info_.input_names[i] + "' expects rank " + std::to_string(info_.input_ranks[i]) +
+                   ", got " + shape_str(v.shape));
+    key += std::to_string(v.elem_type) + shape_str(v.shape);
+    if (numel(v.shape) <= kPlanTimeInputMaxElems)
+      key += "=" + std::string(static_cast<const char*>(v.data), v.nbytes);
+    key += ";";
+  }
+  auto it = cache_.find(key);
+  if (it != cache_.end()) return it->second;
+
+  auto ps = std::make_shared<PlanSet>();
+  LGraph full = lower(model_, specs_for(inputs, 0, 0, false));
+  fuse(full);
+  for (size_t j = 0; j < full.outputs.size(); ++j) {
+    const Value& v = full.vals[size_t(full.outputs[j])];
+    ps->out_shapes.push_back(v.shape);
+    ps->out_host.push_back(v.is_host);
+    ps->out_values.push_back(v.is_host ? v.host : nullptr);
+  }
+  int64_t batch = -1;
+  for (size_t i = 0; i < inputs.size(); ++i)
+    if (numel(inputs[i]->shape) > kPlanTimeInputMaxElems) {
+      if (batch < 0) batch = inputs[i]->shape[0];
+      else if (inputs[i]->shape[0] != batch) batch = -2;
+    }
+  const int nd = int(devices_.size());
+  bool shard = nd > 1 && batch >= 2 && batch_separable(full);
+  if (nd > 1 && !shard && debug_level() >= 1)
+    std::fprintf(stderr, "[shorokoo_b200] graph does not shard on the batch axis; running on one device\n");
+  if (!shard) {
+    ck(cudaSetDevice(devices_[0]), "cudaSetDevice");
+    ps->shards.push_back({0, 0, batch > 0 ? batch : 0, std::make_shared<Plan>(std::move(full), devices_[0], sm_counts_[0])});
+  } else {
+    ps->sharded = true;
+    const int parts = int(std::min<int64_t>(nd, batch));
+    int64_t b0 = 0;
+    for (int d = 0; d < parts; ++d) {
+      int64_t cnt = batch / parts + (d < batch % parts ? 1 : 0);
+      ps->shards.push_back({d, b0, cnt, nullptr});
+      b0 += cnt;
+    }
+    std::vector<std::thread> th;
+    std::vector<std::string> errs(ps->shards.size());
+    std::vector<int32_t> codes(ps->shards.size(), 0);
+    for (size_t si = 0; si < ps->shards.size(); ++si) {
+      th.emplace_back([&, si] {
+        Shard& sh = ps->shards[si];
+        try {
+          cudaSetDevice(devices_[size_t(sh.device)]);
+          LGraph g = lower(model_, specs_for(inputs, sh.begin, sh.count, true));
+          sh.plan = std::make_shared<Plan>(std::move(g), devices_[size_t(sh.device)], sm_counts_[size_t(sh.device)]);
+        } catch (const Error& e) {
+          errs[si] = e.what();
+          codes[si] = e.code;
+        } catch (const std::exception& e) {
+          errs[si] = e.what();
+          codes[si] = SB_INTERNAL;
+        }
+      });
+    }
+    for (auto& t : th) t.join();
+    for (size_t si = 0; si < errs.size(); ++si)
+      if (codes[si]) fail(codes[si], "device " + std::to_string(devices_[size_t(ps->shards[si].device)]) + ": " + errs[si]);
+  }
+  cache_[key] = ps;
+  return ps;
+}
+
+std::vector<std::shared_ptr<HostValue>> Session::run(const std::vector<std::shared_ptr<HostValue>>& inputs,
+                                                     const std::vector<int>& out_idx) {
+  std::lock_guard<std::mutex> lock(mu_);
+  auto ps = get_plans(inputs);
+  const size_t nout = ps->out_shapes.size();
+  std::vector<std::shared_ptr<HostValue>> outs(nout);
+  std::vector<bool> wanted(nout, false);
+  for (int j : out_idx) wanted[size_t(j)] = true;
+  for (size_t j = 0; j < nout; ++j) {
+    if (!wanted[j]) continue;
+    if (ps->out_host[j]) {
+      const HostTensor& h = *ps->out_values[j];
+      outs[j] = HostValue::alloc_tensor(h.dtype, h.shape);
+      if (h.nbytes()) std::memcpy(outs[j]->data, h.data(), h.nbytes());
+    } else {
+      outs[j] = HostValue::alloc_tensor(DT_FLOAT, ps->out_shapes[j]);
+    }
+  }
+  std::vector<std::string> errs(ps->shards.size());
+  std::vector<int32_t> codes(ps->shards.size(), 0);
+  auto work = [&](size_t si) {
+    const Shard& sh = ps->shards[si];
+    try {
+      ck(cudaSetDevice(devices_[size_t(sh.device)]), "cudaSetDevice");
+      std::vector<const void*> hin(inputs.size(), nullptr);
+      for (size_t i = 0; i < inputs.size(); ++i) {
+        const HostValue& v = *inputs[i];
+        if (numel(v.shape) <= kPlanTimeInputMaxElems) continue;
+        size_t row = v.shape.empty() ? 0 : v.nbytes / size_t(std::max<int64_t>(v.shape[0], 1));
+        hin[i] = static_cast<const uint8_t*>(v.data) + (ps->sharded ? size_t(sh.begin) * row : 0);
+      }
+      std::vector<void*> hout(nout, nullptr);
+      for (size_t j = 0; j < nout; ++j) {
+        if (!outs[j] || ps->out_host[j]) continue;
+        size_t row = ps->out_shapes[j].empty() ? 0
+                                                : outs[j]->nbytes / size_t(std::max<int64_t>(ps->out_shapes[j][0], 1));
+        hout[j] = static_cast<uint8_t*>(outs[j]->data) + (ps->sharded ? size_t(sh.begin) * row : 0);
+      }
+      cudaStream_t s = streams_[size_t(sh.device)];
+      sh.plan->enqueue(s, hin, hout);
+      ck(cudaStreamSynchronize(s), "stream synchronize");
+      sh.plan->check_device_error();
+    } catch (const Error& e) {
+      errs[si] = e.what();
+      codes[si] = e.code;
+    } catch (const std::exception& e) {
+      errs[si] = e.what();
+      codes[si] = SB_INTERNAL;
+    }
+  };
+  if (ps->shards.size() == 1) {
+    work(0);
+  } else {
+    std::vector<std::thread> th;
+    for (size_t si = 0; si < ps->shards.size(); ++si) th.emplace_back(work, si);
+    for (auto& t : th) t.join();
+  }
+  for (size_t si = 0; si < errs.size(); ++si)
+    if (codes[si]) fail(codes[si], errs[si]);
+  std::vector<std::shared_ptr<HostValue>> res;
+  for (int j : out_idx) res.push_back(outs[size_t(j)]);
+  return res;
+}
+
+std::vector<double> Session::time_device(const std::vector<std::shared_ptr<HostValue>>& inputs, int warmup, int iters) {
+  std::lock_guard<std::mutex> lock(mu_);
+  auto ps = get_plans(inputs);
+  std::vector<double> ms(ps->shards.size(), 0.0);
+  std::vector<std::string> errs(ps->shards.size());
+  std::vector<int32_t> codes(ps->shards.size(), 0);
+  auto work = [&](size_t si) {
+    const Shard& sh = ps->shards[si];
+    try {
+      ck(cudaSetDevice(devices_[size_t(sh.device)]), "cudaSetDevice");
+      cudaStream_t s = streams_[size_t(sh.device)];
+      std::vector<const void*> hin(inputs.size(), nullptr);
+      for (size_t i = 0; i < inputs.size(); ++i) {
+        const HostValue& v = *inputs[i];
+        if (numel(v.shape) <= kPlanTimeInputMaxElems) continue;
+        size_t row = v.shape.empty() ? 0 : v.nbytes / size_t(std::max<int64_t>(v.shape[0], 1));
+        hin[i] = static_cast<const uint8_t*>(v.data) + (ps->sharded ? size_t(sh.begin) * row : 0);
+      }
+      std::vector<void*> hout(ps->out_shapes.size(), nullptr);
+      sh.plan->enqueue(s, hin, hout);   // inputs resident in HBM from here on
+      for (int w = 0; w < warmup; ++w) sh.plan->enqueue_kernels(s);
+      cudaEvent_t e0, e1;
+      ck(cudaEventCreate(&e0), "event");
+      ck(cudaEventCreate(&e1), "event");
+      ck(cudaStreamSynchronize(s), "sync");
+      ck(cudaEventRecord(e0, s), "event record");
+      for (int i = 0; i < iters; ++i) sh.plan->enqueue_kernels(s);
+      ck(cudaEventRecord(e1, s), "event record");
+      ck(cudaEventSynchronize(e1), "event sync");
+      float t = 0;
+      ck(cudaEventElapsedTime(&t, e0, e1), "elapsed");
+      cudaEventDestroy(e0);
+      cudaEventDestroy(e1);
+      ms[si] = double(t) / std::max(iters, 1);
+      sh.plan->check_device_error();
+    } catch (const Error& e) {
+      errs[si] = e.what();
+      codes[si] = e.code;
+    }
+  };
+  std::vector<std::thread> th;
+  for (size_t si = 0; si < ps->shards.size(); ++si) th.emplace_back(work, si);
+  for (auto& t : th) t.join();
+  for (size_t si = 0; si < errs.size(); ++si)
+    if (codes[si]) fail(codes[si], errs[si]);
+  return ms;
+}
+
+std::vector<std::pair<std::string, double>> Session::profile_steps(const std::vector<std::shared_ptr<HostValue>>& inputs,
+                                                                   int iters) {
+  std::lock_guard<std::mutex> lock(mu_);
+  auto ps = get_plans(inputs);
+  const Shard& sh = ps->shards[0];
+  ck(cudaSetDevice(devices_[size_t(sh.device)]), "cudaSetDevice");
+  cudaStream_t s = streams_[size_t(sh.device)];
+  std::vector<const void*> hin(inputs.size(), nullptr);
+  for (size_t i = 0; i < inputs.size(); ++i)
+    if (numel(inputs[i]->shape) > kPlanTimeInputMaxElems) hin[i] = inputs[i]->data;
+  std::vector<void*> hout(ps->out_shapes.size(), nullptr);
+  sh.plan->enqueue(s, hin, hout);
+  ck(cudaStreamSynchronize(s), "sync");
+  auto r = sh.plan->profile(s, iters);
+  sh.plan->check_device_error();
+  return r;
+}
+
+PlanStats Session::stats(const std::vector<std::shared_ptr<HostValue>>& inputs) {
+  std::lock_guard<std::mutex> lock(mu_);
+  auto ps = get_plans(inputs);
+  PlanStats t;
+  for (auto& sh : ps->shards) {
+    const PlanStats& s = sh.plan->stats();
+    t.kernels += s.kernels;
+    t.tc_kernels += s.tc_kernels;
+    t.macs += s.macs;
+    t.arena_bytes += s.arena_bytes;
+    t.weight_bytes += s.weight_bytes;
+  }
+  return t;
+}
+
+int Session::devices_used(const std::vector<std::shared_ptr<HostValue>>& inputs) {
+  std::lock_guard<std::mutex> lock(mu_);
+  return int(get_plans(inputs)->shards.size());
+}
+
+}  // namespace sb

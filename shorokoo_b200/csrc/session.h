@@ -1,0 +1,90 @@
+// Session runtime behind the C ABI: the native side of IShorokooInferenceSession
+// (src/Shorokoo/Core/Inference/Abstractions/IShorokooInferenceSession.cs:3-13) and of the host
+// tensor values of IShorokooTensorValue (IShorokooTensorValue.cs:8-31).
+#pragma once
+
+#include <atomic>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "ir.h"
+#include "plan.h"
+
+namespace sb {
+
+// Host value: tensor (any byte-stride element type), string tensor, or sequence of values.
+struct HostValue {
+  enum Kind { TENSOR = 1, SEQUENCE = 2 };   // ShorokooOnnxValueType numbering
+  int kind = TENSOR;
+  int32_t elem_type = DT_FLOAT;
+  std::vector<int64_t> shape;
+  // tensor bytes
+  void* data = nullptr;
+  size_t nbytes = 0;
+  bool owned = true;       // false: borrowed caller memory
+  bool pinned = false;
+  std::vector<std::string> strings;
+  std::vector<std::shared_ptr<HostValue>> items;   // sequence elements
+  ~HostValue();
+  static std::shared_ptr<HostValue> alloc_tensor(int32_t elem_type, const std::vector<int64_t>& shape);
+};
+
+struct SessionOptions {
+  int num_devices = 0;   // 0: SHOROKOO_B200_DEVICES or all visible devices
+  int first_device = 0;
+};
+
+class Session {
+ public:
+  Session(const uint8_t* model, size_t len, const SessionOptions& opt);
+  ~Session();
+
+  const std::vector<std::string>& input_names() const { return info_.input_names; }
+  const std::vector<std::string>& output_names() const { return info_.output_names; }
+
+  // Run with inputs in session input order; returns outputs in the order of `out_idx`.
+  std::vector<std::shared_ptr<HostValue>> run(const std::vector<std::shared_ptr<HostValue>>& inputs,
+                                              const std::vector<int>& out_idx);
+  // Device-only timing: uploads inputs once and times `iters` replays of the kernel sequence on
+  // every device; returns per-device milliseconds per run (CUDA events on each device's stream).
+  std::vector<double> time_device(const std::vector<std::shared_ptr<HostValue>>& inputs, int warmup, int iters);
+  // Times each launch of device 0's plan individually (no graph); returns (kind, ms) pairs.
+  std::vector<std::pair<std::string, double>> profile_steps(const std::vector<std::shared_ptr<HostValue>>& inputs,
+                                                            int iters);
+  PlanStats stats(const std::vector<std::shared_ptr<HostValue>>& inputs);
+  int devices_used(const std::vector<std::shared_ptr<HostValue>>& inputs);
+
+ private:
+  struct Shard {
+    int device;
+    int64_t begin, count;   // batch rows
+    std::shared_ptr<Plan> plan;
+  };
+  struct PlanSet {
+    std::vector<Shard> shards;
+    std::vector<std::vector<int64_t>> out_shapes;
+    std::vector<bool> out_host;
+    std::vector<std::shared_ptr<HostTensor>> out_values;
+    bool sharded = false;
+  };
+
+  OnnxModel model_;
+  ModelInfo info_;
+  SessionOptions opt_;
+  std::vector<int> devices_;
+  std::vector<int> sm_counts_;
+  std::vector<cudaStream_t> streams_;
+  std::mutex mu_;
+  std::map<std::string, std::shared_ptr<PlanSet>> cache_;
+
+  std::shared_ptr<PlanSet> get_plans(const std::vector<std::shared_ptr<HostValue>>& inputs);
+  std::vector<InputSpec> specs_for(const std::vector<std::shared_ptr<HostValue>>& inputs, int64_t batch_begin,
+                                   int64_t batch_count, bool shard) const;
+};
+
+bool batch_separable(const LGraph& g);
+
+}  // namespace sb

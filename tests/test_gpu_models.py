@@ -1,0 +1,38 @@
+"""End-to-end GPU parity of the five benchmark graphs (small sizes) against the oracle and, for
+ResNet-18, against the reference's own PyTorch twin (golden fixture)."""
+import os
+
+import numpy as np
+import pytest
+
+from helpers import assert_close, run_backend, run_oracle
+from shorokoo_b200.emit import graphs
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def test_resnet18_matches_reference_pytorch_twin():
+    d = np.load(os.path.join(GOLDEN, "resnet18_torchref.npz"))
+    case = graphs.resnet(**eval(str(d["kwargs"])))
+    got = run_backend(case)[0]
+    assert_close(got, d["logits"], what="resnet18 vs reference PyTorch twin")
+    # same top-1 class per sample
+    assert (got.argmax(1) == d["logits"].argmax(1)).all()
+
+
+@pytest.mark.parametrize("name,kw", [
+    ("stacked_linear", dict(batch=64)),
+    ("stacked_linear", dict(batch=64, live_depth=True, depth=5)),
+    ("mlp", dict(batch=96, widths=(256, 512, 512, 100))),
+    ("resnet50", dict(batch=2, hw=(64, 64), affine_scale=0.1)),
+    ("resnet50", dict(batch=2, hw=(64, 64), live_hypers=True, dead_code=True)),
+    ("resnet50", dict(batch=2, hw=(64, 64), live_hypers=True, apply_softmax=True)),
+    ("retinanet", dict(batch=1, hw=(128, 160), affine_scale=0.1)),
+])
+def test_model_parity(name, kw):
+    case = graphs.build(name, **kw)
+    got = run_backend(case)
+    ref = run_oracle(case)
+    for g, r, o in zip(got, ref, case.output_names):
+        assert_close(g, r, what=f"{name} {kw} output {o}")
