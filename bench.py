@@ -1,0 +1,295 @@
+#!/usr/bin/env python3
+"""Throughput benchmark of the B200 inference backend (one JSON line on rank 0).
+
+Workload (default): ResNet-50 classification forward, batch 512 of 3x224x224 float32 NCHW input
+N(0,1) seed 11, inference-mode BatchNorm, 1000-way FC; synthetic random-init weights (no datasets or
+checkpoints exist offline). With --gpus N (launched by torchrun, one process per GPU) the 512-image
+batch is sharded 512/N per GPU with replicated weights and no collective ("strong" scaling).
+
+  value  device time: inputs resident in HBM, CUDA events around K replays of the captured kernel
+         sequence on the launching stream; whole-job images/s = 512 / max-over-ranks time.
+  e2e    the same metric through the plugin interface (B200InferenceSession.Run) with host
+         buffers: pinned H2D of the input, kernels, D2H of the logits, all inside the timed region.
+
+--impl reference times the oracle (the CPU restatement of the reference's ONNX Runtime CPU path)
+on the host cores instead, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: (emit config, batch, unit label)
+    "resnet50": ("resnet50", 512),
+    "resnet18": ("resnet18", 256),
+    "mlp": ("mlp", 8192),
+    "stacked_linear": ("stacked_linear", 4096),
+    "retinanet": ("retinanet", 16),
+}
+METRIC = "ResNet-50 images/sec at 1/2/4/8 B200; % tensor-pipe peak; vs ORT CPU"
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region (200 ms period)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), f[5], f[6], f[7], f[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        reasons = set()
+        for r in rows:
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), r[2:]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def cpu_baseline(case_fn, batch_total, sample, budget_s=20.0):
+    """The oracle (torch-CPU fp32 restatement of the ORT-CPU path) on `sample` images."""
+    import torch
+    from oracle.interp import Interpreter
+    cores = len(os.sched_getaffinity(0))
+    case = case_fn(sample)
+    it = Interpreter(case.model, "fp32", threads=cores)
+    feed = dict(case.inputs)
+    it.run(feed)   # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        it.run(feed)
+        n += 1
+        if time.perf_counter() - t0 > budget_s / 2 or n >= 3:
+            break
+    dt = (time.perf_counter() - t0) / n
+    return {"value": sample / dt, "unit": "images/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{sample} images of the same workload, oracle/interp.py fp32 (torch CPU), "
+                      f"median of {n} runs"}
+
+
+def make_case(name, batch):
+    from shorokoo_b200.emit import graphs
+    cfg, _ = WORKLOADS[name]
+    return graphs.build(cfg, batch=batch)
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    name = args.workload
+    batch = WORKLOADS[name][1]
+    sample = args.ref_sample
+    import torch
+    from oracle.interp import Interpreter
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    case = make_case(name, sample)
+    it = Interpreter(case.model, "fp32", threads=cores)
+    feed = dict(case.inputs)
+    for _ in range(args.warmup):
+        it.run(feed)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        it.run(feed)
+    dt = (time.perf_counter() - t0) / args.steps
+    val = sample / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "images/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{name} bs{batch} (timed on a {sample}-image sample per step)",
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": val, "unit": "images/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"{sample} images per step; ONNX Runtime is not installable offline, so the "
+                                   f"oracle's torch-CPU fp32 restatement of its CPU path stands in"},
+        "e2e": {"value": val, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="resnet50", choices=sorted(WORKLOADS))
+    ap.add_argument("--ref-sample", type=int, default=8, help="images per step of the CPU reference arm")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("gloo", timeout=timedelta(seconds=600))   # host barrier / max only
+    from shorokoo_b200 import B200InferenceSessionFactory
+
+    name = args.workload
+    total = WORKLOADS[name][1]
+    per = total // world + (1 if rank < total % world else 0)
+    begin = rank * (total // world) + min(rank, total % world)
+    full = make_case(name, total) if world == 1 else None
+    case = full if full is not None else make_case(name, total)
+    # this rank's contiguous shard of the batch
+    inputs = [(n, a[begin:begin + per] if a.ndim and a.shape[0] == total else a) for n, a in case.inputs]
+    f = B200InferenceSessionFactory(num_devices=1, first_device=local)
+    sess = f.CreateSession(case.model)
+    feeds = {n: f.CreateTensor(a) for n, a in inputs}
+    st = sess.stats(feeds)
+    macs_per_img = case.macs / total
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-resident throughput (value) ----
+    barrier()
+    with ClockSampler(local) as clk:
+        ms = sess.time_device(feeds, warmup=args.warmup, iters=args.steps)[0]
+        barrier()
+        # ---- end to end through the plugin interface (e2e) ----
+        for _ in range(args.warmup):
+            outs = sess.Run(feeds, case.output_names)
+            for o in outs:
+                o.Dispose()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            outs = sess.Run(feeds, case.output_names)
+            for o in outs:
+                o.Dispose()
+        torch.cuda.synchronize()
+        e2e_s = (time.perf_counter() - t0) / args.steps
+        barrier()
+    clocks = clk.summary()
+    t_max = ms
+    e_max = e2e_s
+    if world > 1:
+        tt = torch.tensor([ms, e2e_s], dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_max, e_max = float(tt[0]), float(tt[1])
+
+    # ---- roofline of the dominant kernel (tensor-core implicit GEMM), timed per launch ----
+    prof = sess.profile(feeds, iters=3)
+    tc_ms = sum(v for k, v in prof if k in ("conv", "gemm"))
+    tc_launches = sum(1 for k, _ in prof if k in ("conv", "gemm"))
+    all_ms = sum(v for _, v in prof)
+    peak_tflops, peak_hbm, peak_kind = measured_peaks()
+    achieved = 2.0 * st["macs"] / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as fh:
+            traffic = json.load(fh).get(name)
+
+    h2d = sum(a.nbytes for _, a in inputs)
+    outs = sess.Run(feeds, case.output_names)
+    d2h = sum(int(np.prod(o.Shape)) * 4 for o in outs)
+    for o in outs:
+        o.Dispose()
+
+    if rank == 0:
+        value = total / (t_max / 1e3)
+        line = {
+            "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_max, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded inputs, random-init weights)",
+            "config": {"workload": f"{name} forward, batch {total} ({per}/GPU), 3x224x224 fp32 NCHW input"
+                       if name.startswith("resnet") else f"{name} forward, batch {total}",
+                       "global_batch": total, "parallelism": f"batch-sharded x{world}, replicated weights, no collective",
+                       "l2": "inputs larger than L2 (the 308 MB input and a multi-GB activation arena per step)",
+                       "precision": "bf16 operands, fp32 accumulate"},
+            "e2e": {"value": total / e_max, "unit": "images/s", "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world, "timing": "host wall clock around Run (synchronous)"},
+            "gpu_launches": int(st["launches"]) * args.steps,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
+                         "frac": achieved / peak_tflops, "traffic": traffic,
+                         "kernel": f"conv_gemm_kernel (tcgen05 implicit GEMM), {tc_launches} launches/step, "
+                                   f"{tc_ms:.3f} of {all_ms:.3f} ms per step timed per launch with CUDA events",
+                         "peak_kind": f"{peak_kind} bf16 dense (burst)"},
+            "clocks": clocks,
+            "flops_per_image": 2 * macs_per_img,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                line["cpu_baseline"] = cpu_baseline(lambda b: make_case(name, b), total, sample=8)
+            except Exception as e:   # reported, never fatal for the GPU number
+                line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+        print(json.dumps(line), flush=True)
+    sess.Dispose()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

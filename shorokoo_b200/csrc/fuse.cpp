@@ -175,19 +175,20 @@ void fuse(LGraph& g) {
           continue;
         }
         if (o.type == "Add" && !ov.is_host && f.residual < 0) {
-          if (ov.shape == g.vals[size_t(cur)].shape) {
-            f.residual = other;
-            f.residual_mode = 0;
-            absorbed.push_back(oi);
-            cur = o.out[0];
-            slot = oi;
-            continue;
-          }
+          // Nearest-2x upsampled operand: read the coarse map directly in the epilogue.
           if (ov.producer >= 0 && is_nearest_up2(g.ops[size_t(ov.producer)], g) &&
               g.vals[size_t(o.out[0])].shape == g.vals[size_t(cur)].shape) {
             const Op& rz = g.ops[size_t(ov.producer)];
             f.residual = rz.in[0];
             f.residual_mode = 1;
+            absorbed.push_back(oi);
+            cur = o.out[0];
+            slot = oi;
+            continue;
+          }
+          if (ov.shape == g.vals[size_t(cur)].shape) {
+            f.residual = other;
+            f.residual_mode = 0;
             absorbed.push_back(oi);
             cur = o.out[0];
             slot = oi;

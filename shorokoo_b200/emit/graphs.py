@@ -490,12 +490,23 @@ def resnet(depth: int = 50, batch: int = 512, hw: Tuple[int, int] = (224, 224), 
     return ModelCase(f"resnet{depth}", B.model(f"ResNet{depth}"), inputs, [out], B.macs, B.params)
 
 
+def kaiming_uniform_a1(rng, shape):
+    """Kaiming-uniform with negative slope a=1: U(-b, b), b = sqrt(3 / fan_in) (torchvision's FPN init)."""
+    bound = math.sqrt(3.0 / _fan_in(shape))
+    return rng.uniform(-bound, bound, size=shape).astype(np.float32)
+
+
+def head_normal(rng, shape):
+    """N(0, 0.01^2): torchvision's RetinaNet head-conv init."""
+    return (rng.standard_normal(size=shape, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
+
+
 def ret_conv(B: Builder, x: str, filters: int, k: int, stride: int, path: str,
              bias_value: float = 0.0, bias_scale: float = 0.0) -> str:
     """RetConv1x1 / RetConv3x3 / RetConv3x3Stride2 (RetinaNetDetector.cs:282-334): trainable bias,
     3x3 convs use auto_pad SAME_UPPER (asymmetric pads on even inputs)."""
     cin = B.shape[x][1]
-    w = B.init(kaiming_normal(B.rng, (filters, cin, k, k)), path + ".weight")
+    w = B.init(kaiming_uniform_a1(B.rng, (filters, cin, k, k)), path + ".weight")
     bias = np.full(filters, bias_value, np.float32)
     if bias_scale:
         bias = bias + (bias_scale * B.rng.standard_normal(filters)).astype(np.float32)
@@ -509,7 +520,7 @@ class _SharedConv:
     """A conv whose initializers are created once and reused at every pyramid level."""
 
     def __init__(self, B: Builder, cin: int, filters: int, path: str, bias_value=0.0, bias_scale=0.0):
-        self.w = B.init(kaiming_normal(B.rng, (filters, cin, 3, 3)), path + ".weight")
+        self.w = B.init(head_normal(B.rng, (filters, cin, 3, 3)), path + ".weight")
         bias = np.full(filters, bias_value, np.float32)
         if bias_scale:
             bias = bias + (bias_scale * B.rng.standard_normal(filters)).astype(np.float32)
@@ -525,7 +536,10 @@ def retinanet(batch: int = 16, hw: Tuple[int, int] = (800, 1024), seed: int = 13
               backbone_blocks: Sequence[int] = (3, 4, 6, 3)) -> ModelCase:
     """RetinaNetResNet50NoNorm (RetinaNetDetector.cs:828-886) + Sigmoid on the class output.
 
-    The class-head bias starts at -ln(99) (focal-loss prior 0.01, RetInitClsBias :79-99)."""
+    The class-head bias starts at -ln(99) (focal-loss prior 0.01, RetInitClsBias :79-99). FPN convs are
+    Kaiming-uniform(a=1) and head convs N(0, 0.01^2), the initialisation of the torchvision RetinaNet
+    the sample mirrors; the sample's own constant 0.02 fill (RetInitXavier :53-61) would make every
+    output channel identical."""
     rng_in = np.random.Generator(np.random.PCG64(seed))
     x_val = rng_in.standard_normal(size=(batch, 3, hw[0], hw[1]), dtype=np.float32)
     B = Builder(seed + WEIGHT_SEED_OFFSET)

@@ -1,0 +1,149 @@
+"""Host-side tests of the native library (no GPU needed): the C ABI loads and exports exactly what
+include/shorokoo_b200.h declares, host tensor values behave like IShorokooTensorValue, the plan-time
+lowering resolves the reference's emission quirks (shape chains, live-[Hyper] If / Loop, dead
+initializers, FrozenBatchNorm folding, Pad folding, head Reshape/Transpose views), and failures are
+reported as the plugin contract requires (unsupported op = hard error at CreateSession)."""
+import ctypes as C
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from shorokoo_b200 import (B200ArgumentError, B200InferenceSessionFactory, B200InvalidOperationError,
+                           B200NotSupportedError, ShorokooOnnxValueType, ShorokooTensorElementType, _native)
+from shorokoo_b200.emit import graphs
+from shorokoo_b200.emit import onnx_writer as W
+from shorokoo_b200.emit.graphs import Builder
+
+F = B200InferenceSessionFactory()
+
+
+def test_library_exports_exactly_the_header():
+    out = subprocess.run(["nm", "-D", "--defined-only", _native.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    exported = sorted(set(re.findall(r" T (sb_\w+)", out)))
+    assert exported == _native.header_symbols()
+    lib = _native.lib()
+    for name in _native.header_symbols():
+        assert hasattr(lib, name)
+    assert lib.sb_version() >= 100
+
+
+def test_tensor_values_roundtrip():
+    a = np.arange(24, dtype=np.float32).reshape(2, 3, 4)
+    v = F.CreateTensor(a)
+    assert v.ValueType == ShorokooOnnxValueType.Tensor
+    assert v.ElementType == ShorokooTensorElementType.Float
+    assert v.Shape == [2, 3, 4]
+    np.testing.assert_array_equal(v.GetTensorDataAsSpan(), a)
+    v.GetTensorMutableDataAsSpan()[0, 0, 0] = 7
+    assert v.GetTensorDataAsSpan()[0, 0, 0] == 7
+    s = F.CreateTensor(np.array(3, np.int64))
+    assert s.Shape == [] and s.GetTensorDataAsSpan() == 3
+    r = F.CreateTensorFromRawBytes(ShorokooTensorElementType.BFloat16, b"\x80\x3f\x00\x40", [2])
+    assert r.ElementType == ShorokooTensorElementType.BFloat16 and r.Shape == [2]
+    st = F.CreateStringTensor(["a", "bc", ""], [3])
+    assert st.GetStringTensorData() == ["a", "bc", ""]
+    seq = F.CreateSequence([F.CreateTensor(np.zeros(2, np.int64)), F.CreateTensor(np.ones(3, np.int64))])
+    assert seq.ValueType == ShorokooOnnxValueType.Sequence and seq.GetValueCount() == 2
+    assert seq.GetSequenceElementType() == ShorokooTensorElementType.Int64
+    assert seq.GetValue(1).Shape == [3]
+    with pytest.raises(B200ArgumentError):
+        F.CreateTensor(np.zeros(6, np.float32), [4])
+    with pytest.raises(B200NotSupportedError):
+        F.CreateTensorFromRawBytes(ShorokooTensorElementType.String, b"", [0])
+
+
+def lower(case, inputs=None):
+    vals = [F.CreateTensor(a) for _, a in (inputs or case.inputs)]
+    arr = (C.c_void_p * max(len(vals), 1))(*[v._h.value for v in vals])
+    buf = C.create_string_buffer(1 << 22)
+    need = C.c_size_t()
+    st = _native.lib().sb_debug_lower(case.model, len(case.model), len(vals), arr, buf, len(buf), C.byref(need))
+    if st:
+        raise RuntimeError(_native.lib().sb_last_error().decode())
+    lines = buf.value.decode().strip().split("\n")
+    return lines
+
+
+def kinds(lines):
+    from collections import Counter
+    return Counter(l.split()[0] for l in lines if not l.startswith(("output", "separable")))
+
+
+def test_lowering_resnet50_fuses_everything():
+    lines = lower(graphs.resnet(depth=50, batch=2, hw=(64, 64)))
+    k = kinds(lines)
+    assert k == {"FusedConv": 53, "MaxPool": 1, "GlobalAveragePool": 1, "Reshape": 1, "FusedGemm": 1}, k
+    stem = [l for l in lines if l.startswith("FusedConv")][0]
+    assert "k=7x7 s=2 pads=[3,3,3,3]" in stem and "act=1" in stem   # Pad folded, BN folded, ReLU fused
+    assert sum("residual=0" in l for l in lines) == 16                # one residual add per bottleneck
+    assert lines[-1] == "separable=1"
+
+
+def test_lowering_live_hypers_and_dead_code():
+    case = graphs.resnet(depth=50, batch=2, hw=(64, 64), live_hypers=True, dead_code=True)
+    k = kinds(lower(case))
+    assert k["FusedConv"] == 53 and k["FusedGemm"] == 1      # dead shortcut convs pruned
+    case = graphs.resnet(depth=18, batch=2, hw=(64, 64), live_hypers=True, apply_softmax=True)
+    assert kinds(lower(case))["Softmax"] == 1
+    # includeTop=false drops the head entirely
+    case = graphs.resnet(depth=18, batch=2, hw=(64, 64), live_hypers=True, include_top=False)
+    k = kinds(lower(case))
+    assert "FusedGemm" not in k and k["GlobalAveragePool"] == 1
+
+
+def test_lowering_unrolls_live_loop():
+    case = graphs.stacked_linear(batch=8, n=64, depth=5, live_depth=True)
+    k = kinds(lower(case))
+    assert k["FusedGemm"] == 5
+    # a different trip count gives a different plan
+    inputs = [(case.inputs[0][0], np.array(2, np.int64)), case.inputs[1]]
+    assert kinds(lower(case, inputs))["FusedGemm"] == 2
+
+
+def test_lowering_retinanet_heads_are_views():
+    lines = lower(graphs.retinanet(batch=1, hw=(128, 160)))
+    k = kinds(lines)
+    assert k["FusedConv"] == 111
+    assert sum("residual=1" in l for l in lines) == 2        # FPN top-down adds with nearest-2x upsample
+    assert k["Concat"] == 2 and k["Sigmoid"] == 1
+    assert [l for l in lines if l.startswith("output")] == ["output [1,3852,80] device", "output [1,3852,4] device"]
+
+
+def test_unsupported_operator_is_a_hard_error_at_create_session():
+    B = Builder(0)
+    x = B.graph_input(W.FLOAT, 2, (2, 2))
+    y = B.op("NonMaxSuppression", [x])
+    B.outputs.append(W.ValueInfo(y))
+    with pytest.raises(B200NotSupportedError, match="NonMaxSuppression"):
+        F.CreateSession(B.model("bad"))
+
+
+@pytest.mark.parametrize("blob", [b"", b"\x0a\xff\xff\xff\xff\x0f", b"\x3a\x05abc", bytes(range(7, 40))])
+def test_malformed_model_bytes(blob):
+    with pytest.raises((B200ArgumentError, B200NotSupportedError)):
+        F.CreateSession(blob)
+
+
+def test_truncated_model():
+    case = graphs.stacked_linear(batch=2, n=8, depth=2)
+    with pytest.raises(B200ArgumentError):
+        F.CreateSession(case.model[: len(case.model) // 2])
+
+
+def test_no_gpu_reports_cuda_error():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    case = graphs.stacked_linear(batch=2, n=8, depth=2)
+    with pytest.raises(B200InvalidOperationError, match="CUDA"):
+        F.CreateSession(case.model)
+
+
+def test_shape_errors_at_lowering():
+    case = graphs.mlp(batch=4, widths=(16, 8))
+    bad = [(case.inputs[0][0], np.zeros((4, 15), np.float32))]
+    with pytest.raises(RuntimeError, match="inner dimensions|MatMul"):
+        lower(case, bad)
