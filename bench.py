@@ -239,8 +239,8 @@ def main():
 
     # ---- roofline of the dominant kernel (tensor-core implicit GEMM), timed per launch ----
     prof = sess.profile(feeds, iters=3)
-    tc_ms = sum(v for k, v in prof if k in ("conv", "gemm"))
-    tc_launches = sum(1 for k, _ in prof if k in ("conv", "gemm"))
+    tc_ms = sum(v for k, v in prof if k.split()[0] in ("conv", "gemm"))
+    tc_launches = sum(1 for k, _ in prof if k.split()[0] in ("conv", "gemm"))
     all_ms = sum(v for _, v in prof)
     peak_tflops, peak_hbm, peak_kind = measured_peaks()
     achieved = 2.0 * st["macs"] / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0

@@ -372,7 +372,11 @@ void Plan::plan_conv(const Op& op) {
   std::vector<DevTensor> reads{x};
   if (r.valid()) reads.push_back(r);
   const int sms = num_sms_;
-  add_step("conv", reads, {y}, [=]() {
+  const std::string kind = "conv " + std::to_string(KH) + "x" + std::to_string(KW) + "/" +
+                           std::to_string(op.strides[0]) + " " + std::to_string(C) + "->" + std::to_string(Cout) +
+                           " M=" + std::to_string(N * Ho * Wo) + (one_by_one ? " tma" : " gather") +
+                           (op.residual >= 0 ? " +res" : "");
+  add_step(kind, reads, {y}, [=]() {
     auto p = std::make_shared<k::ConvGemmPlan>();
     k::ConvGemmArgs& a = p->args;
     std::memset(&a, 0, sizeof(a));
@@ -448,7 +452,7 @@ void Plan::plan_gemm(const Op& op) {
   std::vector<DevTensor> reads{x};
   if (r.valid()) reads.push_back(r);
   const int sms = num_sms_;
-  add_step("gemm", reads, {y}, [=]() {
+  add_step("gemm " + std::to_string(M) + "x" + std::to_string(K) + "->" + std::to_string(Nn), reads, {y}, [=]() {
     auto p = std::make_shared<k::ConvGemmPlan>();
     k::ConvGemmArgs& a = p->args;
     std::memset(&a, 0, sizeof(a));

@@ -64,6 +64,10 @@ class Builder:
         self.macs = 0
         self.dead_code = dead_code
         self.stack: List[List[W.Node]] = [self.nodes]
+        # Optional BatchNorm calibration: value name -> activation (torch, NCHW) of a small seeded
+        # calibration batch, propagated alongside emission (used by retinanet(calibrate_bn=True)).
+        self.calib: Dict[str, object] = {}
+        self.params_by_name: Dict[str, np.ndarray] = {}
 
     # -- raw emission -------------------------------------------------------------------------
     def _next(self) -> int:
@@ -90,6 +94,7 @@ class Builder:
         name = f"N{k}_T0"
         self.inits.append(W.Tensor(name, np.ascontiguousarray(arr), encoding="raw"))
         self.shape[name] = tuple(arr.shape)
+        self.params_by_name[name] = arr
         if path:
             self.params[path] = arr
         return name
@@ -144,17 +149,35 @@ class Builder:
                     pads=(pads if auto_pad == "NOTSET" else None), strides=[stride, stride])
         self.shape[y] = (n, cout, ho, wo)
         self.macs += n * ho * wo * cout * c * kernel * kernel
+        if x in self.calib:
+            import torch
+            import torch.nn.functional as F
+            xt = self.calib[x]
+            if auto_pad == "SAME_UPPER":
+                ch, cw = xt.shape[2], xt.shape[3]
+                th = max((-(-ch // stride) - 1) * stride + kernel - ch, 0)
+                tw = max((-(-cw // stride) - 1) * stride + kernel - cw, 0)
+                xt = F.pad(xt, (tw // 2, tw - tw // 2, th // 2, th - th // 2))
+            elif pads:
+                xt = F.pad(xt, (pads[1], pads[3], pads[0], pads[2]))
+            wt = torch.from_numpy(self.params_by_name[w])
+            bt = torch.from_numpy(self.params_by_name[b]) if b in self.params_by_name else None
+            self.calib[y] = F.conv2d(xt, wt, bt, stride=stride)
         return y
 
     def unary(self, op: str, x: str) -> str:
         y = self.op(op, [x])
         self.shape[y] = self.shape[x]
+        if x in self.calib and op == "Relu":
+            self.calib[y] = self.calib[x].clamp_min(0)
         return y
 
     def binary(self, op: str, a: str, b: str) -> str:
         y = self.op(op, [a, b])
         if a in self.shape and b in self.shape:
             self.shape[y] = tuple(np.broadcast_shapes(self.shape[a], self.shape[b]))
+        if a in self.calib and b in self.calib and op == "Add":
+            self.calib[y] = self.calib[a] + self.calib[b]
         return y
 
     def model(self, name: str, functions=()) -> bytes:
@@ -322,6 +345,10 @@ def frozen_bn(B: Builder, x: str, path: str, o: ResNetOpts) -> str:
     rng = B.rng
     mean = (rng.standard_normal(C, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
     var = rng.uniform(0.5, 1.5, size=C).astype(np.float32)
+    if x in B.calib:   # frozen statistics of the calibration batch (a trained network's BN state)
+        xt = B.calib[x]
+        mean = xt.mean(dim=(0, 2, 3)).numpy().astype(np.float32)
+        var = (xt.var(dim=(0, 2, 3), unbiased=False) + 1e-3).numpy().astype(np.float32)
     if o.bn_affine_scale > 0:
         gamma = (1.0 + o.bn_affine_scale * rng.standard_normal(C)).astype(np.float32)
         beta = (o.bn_affine_scale * rng.standard_normal(C)).astype(np.float32)
@@ -342,6 +369,11 @@ def frozen_bn(B: Builder, x: str, path: str, o: ResNetOpts) -> str:
     shift = B.op("Sub", [r_b, B.op("Mul", [r_mean, scale])])
     y = B.op("Add", [B.op("Mul", [x, scale]), shift])
     B.shape[y] = B.shape[x]
+    if x in B.calib:
+        import torch
+        sc = gamma / np.sqrt(var + np.float32(o.eps))
+        sh = beta - mean * sc
+        B.calib[y] = B.calib[x] * torch.from_numpy(sc).view(1, -1, 1, 1) + torch.from_numpy(sh).view(1, -1, 1, 1)
     return y
 
 
@@ -393,11 +425,17 @@ def stem(B: Builder, x: str, o: ResNetOpts) -> str:
     xp = B.op("Pad", [x, pads, B.const(np.array(0.0, np.float32))], mode="constant")
     n, c, h, w = B.shape[x]
     B.shape[xp] = (n, c, h + 6, w + 6)
+    if x in B.calib:
+        import torch.nn.functional as F
+        B.calib[xp] = F.pad(B.calib[x], (3, 3, 3, 3))
     y = B.unary("Relu", frozen_bn(B, resnet_conv(B, xp, 64, 7, 2, "conv1"), "bn1", o))
     mp = B.op("MaxPool", [y], ceil_mode=0, dilations=[1, 1], kernel_shape=[3, 3], pads=[1, 1, 1, 1],
               storage_order=0, strides=[2, 2])
     n, c, h, w = B.shape[y]
     B.shape[mp] = (n, c, (h + 2 - 3) // 2 + 1, (w + 2 - 3) // 2 + 1)
+    if y in B.calib:
+        import torch.nn.functional as F
+        B.calib[mp] = F.max_pool2d(B.calib[y], 3, 2, 1)
     return mp
 
 
@@ -533,18 +571,25 @@ class _SharedConv:
 def retinanet(batch: int = 16, hw: Tuple[int, int] = (800, 1024), seed: int = 13, num_classes: int = 80,
               num_anchors: int = 9, fpn: int = 256, sigmoid: bool = True, affine_scale: float = 0.0,
               backbone_widths: Sequence[int] = (64, 128, 256, 512),
-              backbone_blocks: Sequence[int] = (3, 4, 6, 3)) -> ModelCase:
+              backbone_blocks: Sequence[int] = (3, 4, 6, 3), calibrate_bn: bool = True) -> ModelCase:
     """RetinaNetResNet50NoNorm (RetinaNetDetector.cs:828-886) + Sigmoid on the class output.
 
     The class-head bias starts at -ln(99) (focal-loss prior 0.01, RetInitClsBias :79-99). FPN convs are
     Kaiming-uniform(a=1) and head convs N(0, 0.01^2), the initialisation of the torchvision RetinaNet
     the sample mirrors; the sample's own constant 0.02 fill (RetInitXavier :53-61) would make every
-    output channel identical."""
+    output channel identical. With ``calibrate_bn`` the backbone's frozen BatchNorm statistics are the
+    per-channel mean/variance of a seeded 2x3x128x128 calibration batch (the state a trained detector's
+    frozen BN carries); uncalibrated statistics let the un-normalised residual stream grow by orders
+    of magnitude, which turns the sigmoid outputs into a sign test on logits near zero."""
     rng_in = np.random.Generator(np.random.PCG64(seed))
     x_val = rng_in.standard_normal(size=(batch, 3, hw[0], hw[1]), dtype=np.float32)
     B = Builder(seed + WEIGHT_SEED_OFFSET)
     o = ResNetOpts(bn_affine_scale=affine_scale)
     x = B.graph_input(W.FLOAT, 4, x_val.shape)
+    if calibrate_bn:
+        import torch
+        cal = np.random.Generator(np.random.PCG64(seed + 2 * WEIGHT_SEED_OFFSET))
+        B.calib[x] = torch.from_numpy(cal.standard_normal((2, 3, 128, 128), dtype=np.float32))
     h = stem(B, x, o)
     feats = []
     for li, (f, nb) in enumerate(zip(backbone_widths, backbone_blocks)):
