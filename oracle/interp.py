@@ -9,7 +9,10 @@ inference hot path, interpreting the same ONNX bytes the B200 library receives.
 
 * ``precision="fp32"`` computes float tensors in float32 (the stand-in for ORT-CPU's fp32 kernels,
   and the timed CPU baseline);
-* ``precision="fp64"`` promotes every float tensor to float64 (ground truth for error analysis).
+* ``precision="fp64"`` promotes every float tensor to float64 (ground truth for error analysis);
+* ``precision="bf16-operands"`` computes in float32 but rounds both operands of every Conv / MatMul
+  to bfloat16 (round-to-nearest-even), the arithmetic of a bf16 tensor-core path with fp32
+  accumulation. It separates a kernel bug from the precision floor of bf16 operands.
 
 Conv / MatMul use torch CPU kernels (torch.nn.functional.conv2d, torch.matmul) for speed; everything
 else is numpy.  ``oracle/ref_small.c`` re-derives Conv / MaxPool / GEMM with plain loops so the
@@ -44,11 +47,11 @@ def _i(a) -> List[int]:
 
 class Interpreter:
     def __init__(self, model_bytes: bytes, precision: str = "fp32", threads: Optional[int] = None):
-        if precision not in ("fp32", "fp64"):
+        if precision not in ("fp32", "fp64", "bf16-operands"):
             raise ValueError(precision)
         self.model: ModelP = decode_model(model_bytes)
         self.precision = precision
-        self.fdt = np.float32 if precision == "fp32" else np.float64
+        self.fdt = np.float64 if precision == "fp64" else np.float32
         self.functions = {(f.domain, f.name): f for f in self.model.functions}
         self.inits = {t.name: self._cast_float(t.to_numpy()) for t in self.model.graph.initializers}
         if torch is not None:
@@ -375,8 +378,14 @@ class Interpreter:
     def _t(self, a):
         return torch.from_numpy(np.ascontiguousarray(a))
 
+    def _op_round(self, a):
+        """Operand rounding of the bf16 tensor-core path (identity in fp32 / fp64 modes)."""
+        if self.precision != "bf16-operands":
+            return a
+        return torch.from_numpy(np.ascontiguousarray(a, np.float32)).bfloat16().float().numpy()
+
     def op_MatMul(self, n, x, env):
-        a, b = x
+        a, b = self._op_round(x[0]), self._op_round(x[1])
         if torch is not None and a.dtype == b.dtype and a.dtype in (np.float32, np.float64):
             return torch.matmul(self._t(a), self._t(b)).numpy()
         return np.matmul(a, b)
@@ -417,7 +426,7 @@ class Interpreter:
         return list(pads) if pads else [0] * (2 * nd)
 
     def op_Conv(self, n, x, env):
-        X, Wt = x[0], x[1]
+        X, Wt = self._op_round(x[0]), self._op_round(x[1])
         B = x[2] if len(x) > 2 else None
         k = n.attr("kernel_shape") or list(Wt.shape[2:])
         nd = len(k)

@@ -15,6 +15,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -62,7 +63,7 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 
 // Bounded wait on an mbarrier phase. Returns false if this CTA is aborting (timeout here or in
 // another role); the first timeout records `code` in the device error word.
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned int* err,
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned int* err,
                                        unsigned int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
@@ -87,6 +88,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, in
       "l"(tm), "r"(c0), "r"(c1), "r"(smem_u32(bar))
       : "memory");
 }
+
+// TMA store of a swizzled smem box to global (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, int c0, int c1, const void* src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tm), "r"(c0),
+               "r"(c1), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
@@ -161,7 +173,9 @@ struct Cfg {
   static constexpr int STAGES = BN == 64 ? 8 : (BN == 128 ? 6 : 4);
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
-  static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 1024 /*align*/ + 256 /*barriers*/;
+  // Epilogue staging: per epilogue warp a residual slab and an output slab of 32 rows x 128 bytes.
+  static constexpr uint32_t EPI_BYTES = 4 * 2 * 4096;
+  static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
 
@@ -213,7 +227,9 @@ __device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint
           }
         }
       } else {
-        for (int j = 0; j < ncols; ++j) v[j] += __bfloat162float(rp[j]);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < ncols) v[j] += __bfloat162float(rp[j]);
       }
     } else {
       const float* rp = reinterpret_cast<const float*>(a.res) + rrow * a.ldr + n0;
@@ -228,7 +244,9 @@ __device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint
           v[4 * j + 3] += q.w;
         }
       } else {
-        for (int j = 0; j < ncols; ++j) v[j] += rp[j];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < ncols) v[j] += rp[j];
       }
     }
   }
@@ -251,7 +269,9 @@ __device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint
         o4[j] = q;
       }
     } else {
-      for (int j = 0; j < ncols; ++j) op[j] = __float2bfloat16_rn(v[j]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncols) op[j] = __float2bfloat16_rn(v[j]);
     }
   } else {
     float* op = reinterpret_cast<float*>(a.out) + orow + n0;
@@ -260,7 +280,161 @@ __device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint
 #pragma unroll
       for (int j = 0; j < 8; ++j) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     } else {
-      for (int j = 0; j < ncols; ++j) op[j] = v[j];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncols) op[j] = v[j];
+    }
+  }
+}
+
+// Swizzled offset of 16-byte chunk j of row r in a 32-row x 128-byte slab (TMA SWIZZLE_128B layout):
+// conflict-free both for one-row-per-thread and for four-rows-per-warp-instruction access.
+__device__ __forceinline__ uint32_t slab_off(int r, int j) { return uint32_t(r * 128 + ((j ^ (r & 7)) << 4)); }
+
+// Slab epilogue of one warp (32 rows from row0) on one accumulator tile. Columns go in slabs of 128
+// bytes per row (64 bf16 or 32 f32). A same-dtype residual slab is fetched with cp.async into shared
+// memory in coalesced form (each warp instruction covers four full 128-byte rows), one slab ahead,
+// and read back one row per thread; the output slab is written one row per thread into shared
+// memory and leaves with coalesced 16-byte stores (epi 1) or one TMA bulk store (epi 2).
+template <int BN, bool OBF>
+__device__ __forceinline__ void res_prefetch(const ConvGemmArgs& a, uint8_t* sbR, int row0, int n0) {
+  constexpr int EPC = OBF ? 8 : 4;
+  constexpr int ES = OBF ? 2 : 4;
+  const int lane = threadIdx.x & 31;
+  const int xr = lane >> 3, xc = lane & 7;
+  const int nch = min(8, (a.Cout - n0) / EPC);
+  const uint8_t* rbase = reinterpret_cast<const uint8_t*>(a.res) + int64_t(n0) * ES + xc * 16;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int grow = row0 + xr + 4 * i;
+    const bool ok = grow < a.M && xc < nch;
+    const void* src = ok ? static_cast<const void*>(rbase + int64_t(grow) * a.ldr * ES) : a.res;
+    cp_async_16(smem_u32(sbR + slab_off(xr + 4 * i, xc)), src, ok ? 16u : 0u);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int BN, bool OBF>
+__device__ __forceinline__ void epilogue_slabs(const ConvGemmArgs& a, const CUtensorMap* tmOut, uint32_t tbase,
+                                               int row0, int ncol0, uint8_t* ebuf) {
+  constexpr int SC = OBF ? 64 : 32;   // columns per slab
+  constexpr int NS = BN / SC;
+  constexpr int EPC = OBF ? 8 : 4;    // elements per 16-byte chunk
+  constexpr int ES = OBF ? 2 : 4;
+  const int lane = threadIdx.x & 31;
+  const int m = row0 + lane;
+  uint8_t* sbR = ebuf;
+  uint8_t* sbO = ebuf + 4096;
+  const bool cres = a.res != nullptr && a.epi_res;
+  const int xr = lane >> 3, xc = lane & 7;
+  if (cres) res_prefetch<BN, OBF>(a, sbR, row0, ncol0);
+#pragma unroll 1
+  for (int sidx = 0; sidx < NS; ++sidx) {
+    const int n0 = ncol0 + sidx * SC;
+    if (n0 >= a.Cout) break;
+    const int nch = min(8, (a.Cout - n0) / EPC);
+    if (cres) {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      __syncwarp();
+    }
+    if (a.epi == 2 && lane == 0) bulk_wait_read0();   // the previous TMA store has left sbO
+    __syncwarp();
+#pragma unroll 1
+    for (int h = 0; h < SC / 32; ++h) {
+      float v[32];
+      uint32_t r[32];
+      tmem_ld32(tbase + uint32_t(sidx * SC + h * 32), r);
+      const float4* b4 = reinterpret_cast<const float4*>(a.bias + n0 + h * 32);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float4 bb = __ldg(b4 + j);
+        v[4 * j + 0] = __uint_as_float(r[4 * j + 0]) + bb.x;
+        v[4 * j + 1] = __uint_as_float(r[4 * j + 1]) + bb.y;
+        v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + bb.z;
+        v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + bb.w;
+      }
+      constexpr int CH = 32 / EPC;   // chunks in this half
+      if (a.res) {
+        if (cres) {
+#pragma unroll
+          for (int j = 0; j < CH; ++j) {
+            const uint4 qv = *reinterpret_cast<const uint4*>(sbR + slab_off(lane, h * CH + j));
+            if (OBF) {
+              const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&qv);
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                float2 f = __bfloat1622float2(hh[t]);
+                v[8 * j + 2 * t] += f.x;
+                v[8 * j + 2 * t + 1] += f.y;
+              }
+            } else {
+              v[4 * j] += __uint_as_float(qv.x);
+              v[4 * j + 1] += __uint_as_float(qv.y);
+              v[4 * j + 2] += __uint_as_float(qv.z);
+              v[4 * j + 3] += __uint_as_float(qv.w);
+            }
+          }
+        } else if (m < a.M) {
+          const int c0 = n0 + h * 32;
+          const int ncols = max(0, min(32, a.Cout - c0));
+          int64_t rrow = m;
+          if (a.res_mode == 1) {
+            const int hw = a.Ho * a.Wo;
+            const int n = m / hw, rem = m - n * hw;
+            const int ho = rem / a.Wo, wo = rem - ho * a.Wo;
+            rrow = (int64_t(n) * a.Hr + (ho >> 1)) * a.Wr + (wo >> 1);
+          }
+          if (a.res_bf16) {
+            const __nv_bfloat16* rp = reinterpret_cast<const __nv_bfloat16*>(a.res) + rrow * a.ldr + c0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < ncols) v[j] += __bfloat162float(rp[j]);
+          } else {
+            const float* rp = reinterpret_cast<const float*>(a.res) + rrow * a.ldr + c0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < ncols) v[j] += rp[j];
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = act_apply(v[j], a.act);
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {
+        uint4 qv;
+        if (OBF) {
+          qv.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+          qv.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+          qv.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+          qv.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+        } else {
+          qv = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]),
+                          __float_as_uint(v[4 * j + 3]));
+        }
+        *reinterpret_cast<uint4*>(sbO + slab_off(lane, h * CH + j)) = qv;
+      }
+    }
+    if (cres) {   // every lane is done with sbR: fetch the next slab's residual behind the store
+      __syncwarp();
+      if (sidx + 1 < NS && n0 + SC < a.Cout) res_prefetch<BN, OBF>(a, sbR, row0, n0 + SC);
+    }
+    if (a.epi == 2) {
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmOut, n0, row0, sbO);
+        bulk_commit();
+      }
+    } else {
+      __syncwarp();
+      uint8_t* obase = reinterpret_cast<uint8_t*>(a.out) + int64_t(n0) * ES + xc * 16;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int grow = row0 + xr + 4 * i;
+        if (grow < a.M && xc < nch)
+          *reinterpret_cast<uint4*>(obase + int64_t(grow) * a.ldo * ES) =
+              *reinterpret_cast<const uint4*>(sbO + slab_off(xr + 4 * i, xc));
+      }
     }
   }
 }
@@ -269,14 +443,15 @@ __device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint
 template <int BN, int MODE>
 __global__ void __launch_bounds__(MODE ? 320 : 192, 1)
     conv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const ConvGemmArgs a) {
+                     const __grid_constant__ CUtensorMap tmOut, const ConvGemmArgs a) {
   using C = Cfg<BN>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_BYTES);
+  uint8_t* sE = sB + STAGES * C::B_BYTES;   // epilogue slabs (1024-byte aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sE + C::EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* accf = empty + STAGES;
   uint64_t* acce = accf + 2;
@@ -302,6 +477,7 @@ __global__ void __launch_bounds__(MODE ? 320 : 192, 1)
   if (warp == 0 && lane == 0) {
     if (MODE == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+    if (a.epi == 2) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmOut) : "memory");
   }
   if (warp == 1) tmem_alloc(tmem_holder, C::TMEM_COLS);
   tc_fence_before();
@@ -377,18 +553,28 @@ __global__ void __launch_bounds__(MODE ? 320 : 192, 1)
       const uint32_t aph = uint32_t(it >> 1) & 1u;
       if (!mbar_wait(&accf[acc], aph, abort_flag, a.err, 8u)) break;
       tc_fence_after();
-      const int m = mt * BM + q * 32 + lane;
+      const int row0 = mt * BM + q * 32;
+      const int m = row0 + lane;
       const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
+      if (a.epi != 0) {
+        if (row0 < a.M) {   // warp-uniform
+          uint8_t* ebuf = sE + q * 8192;
+          if (a.out_bf16) epilogue_slabs<BN, true>(a, &tmOut, tbase, row0, nt * BN, ebuf);
+          else epilogue_slabs<BN, false>(a, &tmOut, tbase, row0, nt * BN, ebuf);
+        }
+      } else {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tbase + uint32_t(c * 32), r);
-        const int n0 = nt * BN + c * 32;
-        if (n0 < a.Cout && m < a.M) epilogue_chunk(a, r, m, n0);
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + uint32_t(c * 32), r);
+          const int n0 = nt * BN + c * 32;
+          if (n0 < a.Cout && m < a.M) epilogue_chunk(a, r, m, n0);
+        }
       }
       tc_fence_before();
       mbar_arrive(&acce[acc]);
     }
+    if (a.epi == 2 && lane == 0) bulk_wait_all();
   } else if (MODE != 0) {
     // ---- im2col gather producers -------------------------------------------------------------
     const int gt = threadIdx.x - 192;   // 0..127
@@ -489,14 +675,15 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 }
 
 bool encode_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
-               uint32_t box_outer) {
+               uint32_t box_outer, bool f32 = false) {
   auto fn = get_encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = fn(tm, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -519,7 +706,7 @@ cudaError_t ensure_attr() {
 
 template <int BN, int MODE>
 cudaError_t launch_t(const ConvGemmPlan& p, cudaStream_t s) {
-  conv_gemm_kernel<BN, MODE><<<p.grid, MODE ? 320 : 192, Cfg<BN>::SMEM, s>>>(p.tmA, p.tmB, p.args);
+  conv_gemm_kernel<BN, MODE><<<p.grid, MODE ? 320 : 192, Cfg<BN>::SMEM, s>>>(p.tmA, p.tmB, p.tmOut, p.args);
   return cudaGetLastError();
 }
 
@@ -545,6 +732,25 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   bool ok = encode_2d(&p.tmB, w, uint64_t(a.Kpad), uint64_t(a.Cout), uint64_t(a.Kpad) * 2, BK, uint32_t(bn));
   if (!a.gather) {
     ok = ok && encode_2d(&p.tmA, a_rows, uint64_t(lda), uint64_t(a.M), uint64_t(lda) * 2, BK, BM);
+  }
+  // Epilogue variant: 0 row-per-thread global stores; 1 slabs through shared memory with coalesced
+  // 16-byte stores; 2 slabs with TMA bulk stores. Slab paths need 16-byte aligned rows and chunks.
+  std::memset(&p.tmOut, 0, sizeof(p.tmOut));
+  const int es = a.out_bf16 ? 2 : 4;
+  const int epc = 16 / es;
+  int want = 2;
+  if (const char* e = std::getenv("SHOROKOO_B200_EPI")) want = std::atoi(e);
+  a.epi = 0;
+  a.epi_res = 0;
+  if (want != 0 && a.group_rows == 0 && a.Cout % epc == 0 && (a.ldo * es) % 16 == 0 &&
+      (reinterpret_cast<uintptr_t>(a.out) & 15) == 0) {
+    a.epi = 1;
+    if (want == 2 && encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldo) * es,
+                               a.out_bf16 ? 64 : 32, 32, !a.out_bf16))
+      a.epi = 2;
+    if (a.res && a.res_mode == 0 && a.res_bf16 == a.out_bf16 && (a.ldr * es) % 16 == 0 &&
+        (reinterpret_cast<uintptr_t>(a.res) & 15) == 0)
+      a.epi_res = 1;
   }
   if (!ok) throw std::runtime_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad layout)");
   const int mode = a.gather ? (a.Cp == 4 ? 2 : 1) : 0;

@@ -334,6 +334,7 @@ def mlp(batch: int = 8192, widths: Sequence[int] = (1024, 4096, 4096, 4096, 4096
 class ResNetOpts:
     eps_input: Optional[str] = None         # live bnEps graph input, else folded constant
     eps: float = 1e-5
+    calibrate_bn: bool = False              # running stats from the calibration batch (tests only)
     bn_affine_scale: float = 0.0            # >0 draws gamma/beta around 1/0 (tests only)
 
 
@@ -345,7 +346,7 @@ def frozen_bn(B: Builder, x: str, path: str, o: ResNetOpts) -> str:
     rng = B.rng
     mean = (rng.standard_normal(C, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
     var = rng.uniform(0.5, 1.5, size=C).astype(np.float32)
-    if x in B.calib:   # frozen statistics of the calibration batch (a trained network's BN state)
+    if x in B.calib and o.calibrate_bn:   # frozen statistics of the calibration batch
         xt = B.calib[x]
         mean = xt.mean(dim=(0, 2, 3)).numpy().astype(np.float32)
         var = (xt.var(dim=(0, 2, 3), unbiased=False) + 1e-3).numpy().astype(np.float32)
@@ -540,11 +541,14 @@ def head_normal(rng, shape):
 
 
 def ret_conv(B: Builder, x: str, filters: int, k: int, stride: int, path: str,
-             bias_value: float = 0.0, bias_scale: float = 0.0) -> str:
+             bias_value: float = 0.0, bias_scale: float = 0.0, normalize_input: bool = False) -> str:
     """RetConv1x1 / RetConv3x3 / RetConv3x3Stride2 (RetinaNetDetector.cs:282-334): trainable bias,
     3x3 convs use auto_pad SAME_UPPER (asymmetric pads on even inputs)."""
     cin = B.shape[x][1]
-    w = B.init(kaiming_uniform_a1(B.rng, (filters, cin, k, k)), path + ".weight")
+    wv = kaiming_uniform_a1(B.rng, (filters, cin, k, k))
+    if normalize_input and x in B.calib:   # data-dependent scale: unit-variance lateral outputs
+        wv = (wv / np.float32(float(B.calib[x].std()))).astype(np.float32)
+    w = B.init(wv, path + ".weight")
     bias = np.full(filters, bias_value, np.float32)
     if bias_scale:
         bias = bias + (bias_scale * B.rng.standard_normal(filters)).astype(np.float32)
@@ -557,8 +561,8 @@ def ret_conv(B: Builder, x: str, filters: int, k: int, stride: int, path: str,
 class _SharedConv:
     """A conv whose initializers are created once and reused at every pyramid level."""
 
-    def __init__(self, B: Builder, cin: int, filters: int, path: str, bias_value=0.0, bias_scale=0.0):
-        self.w = B.init(head_normal(B.rng, (filters, cin, 3, 3)), path + ".weight")
+    def __init__(self, B: Builder, cin: int, filters: int, path: str, bias_value=0.0, bias_scale=0.0, init=None):
+        self.w = B.init((init or head_normal)(B.rng, (filters, cin, 3, 3)), path + ".weight")
         bias = np.full(filters, bias_value, np.float32)
         if bias_scale:
             bias = bias + (bias_scale * B.rng.standard_normal(filters)).astype(np.float32)
@@ -571,7 +575,7 @@ class _SharedConv:
 def retinanet(batch: int = 16, hw: Tuple[int, int] = (800, 1024), seed: int = 13, num_classes: int = 80,
               num_anchors: int = 9, fpn: int = 256, sigmoid: bool = True, affine_scale: float = 0.0,
               backbone_widths: Sequence[int] = (64, 128, 256, 512),
-              backbone_blocks: Sequence[int] = (3, 4, 6, 3), calibrate_bn: bool = True) -> ModelCase:
+              backbone_blocks: Sequence[int] = (3, 4, 6, 3), calibrate_bn: bool = False) -> ModelCase:
     """RetinaNetResNet50NoNorm (RetinaNetDetector.cs:828-886) + Sigmoid on the class output.
 
     The class-head bias starts at -ln(99) (focal-loss prior 0.01, RetInitClsBias :79-99). FPN convs are
@@ -584,9 +588,9 @@ def retinanet(batch: int = 16, hw: Tuple[int, int] = (800, 1024), seed: int = 13
     rng_in = np.random.Generator(np.random.PCG64(seed))
     x_val = rng_in.standard_normal(size=(batch, 3, hw[0], hw[1]), dtype=np.float32)
     B = Builder(seed + WEIGHT_SEED_OFFSET)
-    o = ResNetOpts(bn_affine_scale=affine_scale)
+    o = ResNetOpts(bn_affine_scale=affine_scale, calibrate_bn=calibrate_bn)
     x = B.graph_input(W.FLOAT, 4, x_val.shape)
-    if calibrate_bn:
+    if True:   # seeded calibration batch: FPN input scales (and BN statistics with calibrate_bn)
         import torch
         cal = np.random.Generator(np.random.PCG64(seed + 2 * WEIGHT_SEED_OFFSET))
         B.calib[x] = torch.from_numpy(cal.standard_normal((2, 3, 128, 128), dtype=np.float32))
@@ -599,9 +603,9 @@ def retinanet(batch: int = 16, hw: Tuple[int, int] = (800, 1024), seed: int = 13
         feats.append(h)
     c3, c4, c5 = feats[1], feats[2], feats[3]
     # FPN (RetFeaturePyramidNetworkFull, :401-450)
-    p5_1 = ret_conv(B, c5, fpn, 1, 1, "fpn.inner5", bias_scale=affine_scale)
-    p4_1 = ret_conv(B, c4, fpn, 1, 1, "fpn.inner4", bias_scale=affine_scale)
-    p3_1 = ret_conv(B, c3, fpn, 1, 1, "fpn.inner3", bias_scale=affine_scale)
+    p5_1 = ret_conv(B, c5, fpn, 1, 1, "fpn.inner5", bias_scale=affine_scale, normalize_input=True)
+    p4_1 = ret_conv(B, c4, fpn, 1, 1, "fpn.inner4", bias_scale=affine_scale, normalize_input=True)
+    p3_1 = ret_conv(B, c3, fpn, 1, 1, "fpn.inner3", bias_scale=affine_scale, normalize_input=True)
 
     def up2(v):   # RetUpsampleNearest (:375-384): Resize nearest, scales [1,1,2,2], default attrs
         y = B.op("Resize", [v, "", B.const(np.array([1.0, 1.0, 2.0, 2.0], np.float32))], mode="nearest")
@@ -618,10 +622,12 @@ def retinanet(batch: int = 16, hw: Tuple[int, int] = (800, 1024), seed: int = 13
     p7 = ret_conv(B, B.unary("Relu", p6), fpn, 3, 2, "fpn.p7", bias_scale=affine_scale)
     levels = [p3, p4, p5, p6, p7]
     # Shared heads (RetClassificationHead :539-571, RetRegressionHead :644-680)
-    cls_convs = [_SharedConv(B, fpn, fpn, f"cls.conv{i}", bias_scale=affine_scale) for i in range(4)]
+    cls_convs = [_SharedConv(B, fpn, fpn, f"cls.conv{i}", bias_scale=affine_scale, init=kaiming_normal)
+                 for i in range(4)]
     cls_out = _SharedConv(B, fpn, num_anchors * num_classes, "cls.logits",
                           bias_value=-math.log(99.0), bias_scale=affine_scale)
-    reg_convs = [_SharedConv(B, fpn, fpn, f"reg.conv{i}", bias_scale=affine_scale) for i in range(4)]
+    reg_convs = [_SharedConv(B, fpn, fpn, f"reg.conv{i}", bias_scale=affine_scale, init=kaiming_normal)
+                 for i in range(4)]
     reg_out = _SharedConv(B, fpn, num_anchors * 4, "reg.deltas", bias_scale=affine_scale)
 
     def head(feat, convs, final, k):
