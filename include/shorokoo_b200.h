@@ -128,6 +128,21 @@ SB_API int32_t sb_session_stats(sb_session* session, int32_t n_inputs, const cha
                          sb_value* const* in_values, int64_t* launches, int64_t* tc_launches, double* macs,
                          int64_t* device_bytes, int32_t* devices_used);
 
+/* ---- Allocation-free dense layer (no counterpart in the reference interface) -------------------
+ * y[M,N] = x[M,K] * w[N,K]^T + bias[N] (ReLU when relu != 0): fp32 device buffers in and out, bf16
+ * tensor-core arithmetic with fp32 accumulation, the same kernels a session uses for Linear layers.
+ * For callers that cannot call cudaMalloc (pre-budgeted device memory, a host runtime that owns the
+ * allocator, allocation-free hot loops): it allocates nothing. Its scratch (bf16 operand copies,
+ * padded bias, error word) is one fixed 16 MiB device array that every GPU loading this library
+ * holds until exit; sizes whose scratch exceeds it (M*round8(K)*2 + N*round64(K)*2 + ~1 KiB) are
+ * rejected with SB_STATUS_INVALID_ARGUMENT. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress), so make that first call before any stream capture. All calls share
+ * the array and the previous call's contents remain in it; calls that overlap on the GPU (other
+ * streams, other threads) race on it. The call runs on `stream` (cudaStream_t, NULL = default) and
+ * returns after it completes. bias may be NULL. */
+SB_API int32_t sb_linear_noalloc(const float* x, const float* w, const float* bias, float* y, int64_t M, int64_t K,
+                                 int64_t N, int32_t relu, void* stream);
+
 /* ---- Diagnostics (no counterpart in the reference interface) ------------------------------- */
 /* Lowers and fuses the model on the host only (no device needed) for inputs given in session input
  * order, and writes a summary (one line per device op, then "separable=0|1") into buf as a

@@ -50,6 +50,7 @@ SIGNATURES = {
     "sb_session_stats": (I32, [P, I32, PSTR, PP, C.POINTER(I64), C.POINTER(I64), C.POINTER(DBL),
                                C.POINTER(I64), C.POINTER(I32)]),
     "sb_debug_lower": (I32, [C.c_char_p, SZ, I32, PP, C.c_char_p, SZ, C.POINTER(SZ)]),
+    "sb_linear_noalloc": (I32, [P, P, P, P, I64, I64, I64, I32, P]),
 }
 
 

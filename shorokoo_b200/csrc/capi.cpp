@@ -74,6 +74,10 @@ std::vector<std::shared_ptr<HostValue>> ordered_inputs(const sb::Session& s, int
 
 }  // namespace
 
+namespace sb {
+void set_thread_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace sb
+
 extern "C" {
 
 int32_t sb_version(void) { return 100; }
