@@ -2,10 +2,12 @@
 // BatchNorm, fused residual add / nearest-2x upsampled residual, ReLU or Sigmoid epilogue).
 //
 // Persistent, warp-specialised CTA (one per SM):
-//   warp 0      TMA producer: B tiles (weights), and A tiles when A is a plain row matrix
+//   warp 0      TMA producer: B tiles (weights), A tiles when A is a plain row matrix, and each
+//               output tile's residual into a shared-memory ring ahead of its operands
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16 per instr)
-//   warps 2-5   epilogue: tcgen05.ld accumulator -> bias / residual / activation -> global
-//   warps 6-9   (spatial convs) im2col gather producers: cp.async 16B/8B with zero fill, written
+//   warps 2-9   epilogue, two warps per TMEM lane quarter: tcgen05.ld accumulator -> bias /
+//               residual / activation -> swizzled smem slab -> TMA bulk store
+//   warps 10-13 (spatial convs) im2col gather producers: cp.async 16B/8B with zero fill, written
 //               into the 128B-swizzled K-major layout the UMMA smem descriptor expects
 // Operand tiles are BM=128 x BK=64 bf16 (one 128-byte swizzle atom per row); the fp32 accumulator
 // is double-buffered in TMEM so the epilogue of tile i overlaps the main loop of tile i+1.
@@ -168,17 +170,6 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
 
-template <int BN>
-struct Cfg {
-  static constexpr int STAGES = BN == 64 ? 8 : (BN == 128 ? 6 : 4);
-  static constexpr uint32_t A_BYTES = BM * BK * 2;
-  static constexpr uint32_t B_BYTES = BN * BK * 2;
-  // Epilogue staging: per epilogue warp a residual slab and an output slab of 32 rows x 128 bytes.
-  static constexpr uint32_t EPI_BYTES = 4 * 2 * 4096;
-  static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
-};
-
 __device__ __forceinline__ float act_apply(float v, int act) {
   if (act == 1) return v > 0.f ? v : 0.f;
   if (act == 2) return 1.f / (1.f + __expf(-v));
@@ -287,175 +278,136 @@ __device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint
   }
 }
 
-// Swizzled offset of 16-byte chunk j of row r in a 32-row x 128-byte slab (TMA SWIZZLE_128B layout):
-// conflict-free both for one-row-per-thread and for four-rows-per-warp-instruction access.
+// Swizzled offset of 16-byte chunk j of row r in a 128-byte-row slab (TMA SWIZZLE_128B layout).
 __device__ __forceinline__ uint32_t slab_off(int r, int j) { return uint32_t(r * 128 + ((j ^ (r & 7)) << 4)); }
 
-// Slab epilogue of one warp (32 rows from row0) on one accumulator tile. Columns go in slabs of 128
-// bytes per row (64 bf16 or 32 f32). A same-dtype residual slab is fetched with cp.async into shared
-// memory in coalesced form (each warp instruction covers four full 128-byte rows), one slab ahead,
-// and read back one row per thread; the output slab is written one row per thread into shared
-// memory and leaves with coalesced 16-byte stores (epi 1) or one TMA bulk store (epi 2).
-template <int BN, bool OBF>
-__device__ __forceinline__ void res_prefetch(const ConvGemmArgs& a, uint8_t* sbR, int row0, int n0) {
-  constexpr int EPC = OBF ? 8 : 4;
-  constexpr int ES = OBF ? 2 : 4;
-  const int lane = threadIdx.x & 31;
-  const int xr = lane >> 3, xc = lane & 7;
-  const int nch = min(8, (a.Cout - n0) / EPC);
-  const uint8_t* rbase = reinterpret_cast<const uint8_t*>(a.res) + int64_t(n0) * ES + xc * 16;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int grow = row0 + xr + 4 * i;
-    const bool ok = grow < a.M && xc < nch;
-    const void* src = ok ? static_cast<const void*>(rbase + int64_t(grow) * a.ldr * ES) : a.res;
-    cp_async_16(smem_u32(sbR + slab_off(xr + 4 * i, xc)), src, ok ? 16u : 0u);
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
+constexpr int kSmemLimit = 232448;        // opt-in maximum dynamic shared memory per block
+constexpr uint32_t kOutStage = 8 * 4096;  // one 32-row x 128-byte output slab per epilogue warp
+constexpr int kMaxStages = 8;
 
-template <int BN, bool OBF>
-__device__ __forceinline__ void epilogue_slabs(const ConvGemmArgs& a, const CUtensorMap* tmOut, uint32_t tbase,
-                                               int row0, int ncol0, uint8_t* ebuf) {
-  constexpr int SC = OBF ? 64 : 32;   // columns per slab
-  constexpr int NS = BN / SC;
-  constexpr int EPC = OBF ? 8 : 4;    // elements per 16-byte chunk
-  constexpr int ES = OBF ? 2 : 4;
+// One output slab (32 rows from row0, 128 bytes of columns from n0) of one epilogue warp:
+// accumulator columns [col0, col0 + SC) of the warp's TMEM lanes -> bias -> residual (from the
+// producer-filled residual slot, or direct rows) -> activation -> swizzled smem -> TMA store.
+template <bool OBF>
+__device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUtensorMap* tmOut, uint32_t tbase,
+                                              int col0, int row0, int n0, uint8_t* sb, const uint8_t* rslab) {
+  constexpr int SC = OBF ? 64 : 32;
+  constexpr int EPC = OBF ? 8 : 4;
+  constexpr int CH = 32 / EPC;   // 16-byte chunks per 32 columns
   const int lane = threadIdx.x & 31;
   const int m = row0 + lane;
-  uint8_t* sbR = ebuf;
-  uint8_t* sbO = ebuf + 4096;
-  const bool cres = a.res != nullptr && a.epi_res;
-  const int xr = lane >> 3, xc = lane & 7;
-  if (cres) res_prefetch<BN, OBF>(a, sbR, row0, ncol0);
+  const int rrow = (row0 & (BM - 1)) + lane;   // row inside the 128-row residual slab
+  if (lane == 0) bulk_wait_read0();             // the previous store from this buffer has been read
+  __syncwarp();
 #pragma unroll 1
-  for (int sidx = 0; sidx < NS; ++sidx) {
-    const int n0 = ncol0 + sidx * SC;
-    if (n0 >= a.Cout) break;
-    const int nch = min(8, (a.Cout - n0) / EPC);
-    if (cres) {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-      __syncwarp();
+  for (int h = 0; h < SC / 32; ++h) {
+    float v[32];
+    uint32_t r[32];
+    tmem_ld32(tbase + uint32_t(col0 + h * 32), r);
+    const float4* b4 = reinterpret_cast<const float4*>(a.bias + n0 + h * 32);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 bb = __ldg(b4 + j);
+      v[4 * j + 0] = __uint_as_float(r[4 * j + 0]) + bb.x;
+      v[4 * j + 1] = __uint_as_float(r[4 * j + 1]) + bb.y;
+      v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + bb.z;
+      v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + bb.w;
     }
-    if (a.epi == 2 && lane == 0) bulk_wait_read0();   // the previous TMA store has left sbO
-    __syncwarp();
-#pragma unroll 1
-    for (int h = 0; h < SC / 32; ++h) {
-      float v[32];
-      uint32_t r[32];
-      tmem_ld32(tbase + uint32_t(sidx * SC + h * 32), r);
-      const float4* b4 = reinterpret_cast<const float4*>(a.bias + n0 + h * 32);
+    if (a.res) {
+      if (rslab) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float4 bb = __ldg(b4 + j);
-        v[4 * j + 0] = __uint_as_float(r[4 * j + 0]) + bb.x;
-        v[4 * j + 1] = __uint_as_float(r[4 * j + 1]) + bb.y;
-        v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + bb.z;
-        v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + bb.w;
-      }
-      constexpr int CH = 32 / EPC;   // chunks in this half
-      if (a.res) {
-        if (cres) {
+        for (int j = 0; j < CH; ++j) {
+          const uint4 qv = *reinterpret_cast<const uint4*>(rslab + slab_off(rrow, h * CH + j));
+          if (OBF) {
+            const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&qv);
 #pragma unroll
-          for (int j = 0; j < CH; ++j) {
-            const uint4 qv = *reinterpret_cast<const uint4*>(sbR + slab_off(lane, h * CH + j));
-            if (OBF) {
-              const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&qv);
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                float2 f = __bfloat1622float2(hh[t]);
-                v[8 * j + 2 * t] += f.x;
-                v[8 * j + 2 * t + 1] += f.y;
-              }
-            } else {
-              v[4 * j] += __uint_as_float(qv.x);
-              v[4 * j + 1] += __uint_as_float(qv.y);
-              v[4 * j + 2] += __uint_as_float(qv.z);
-              v[4 * j + 3] += __uint_as_float(qv.w);
+            for (int t = 0; t < 4; ++t) {
+              float2 f = __bfloat1622float2(hh[t]);
+              v[8 * j + 2 * t] += f.x;
+              v[8 * j + 2 * t + 1] += f.y;
             }
-          }
-        } else if (m < a.M) {
-          const int c0 = n0 + h * 32;
-          const int ncols = max(0, min(32, a.Cout - c0));
-          int64_t rrow = m;
-          if (a.res_mode == 1) {
-            const int hw = a.Ho * a.Wo;
-            const int n = m / hw, rem = m - n * hw;
-            const int ho = rem / a.Wo, wo = rem - ho * a.Wo;
-            rrow = (int64_t(n) * a.Hr + (ho >> 1)) * a.Wr + (wo >> 1);
-          }
-          if (a.res_bf16) {
-            const __nv_bfloat16* rp = reinterpret_cast<const __nv_bfloat16*>(a.res) + rrow * a.ldr + c0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < ncols) v[j] += __bfloat162float(rp[j]);
           } else {
-            const float* rp = reinterpret_cast<const float*>(a.res) + rrow * a.ldr + c0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < ncols) v[j] += rp[j];
+            v[4 * j] += __uint_as_float(qv.x);
+            v[4 * j + 1] += __uint_as_float(qv.y);
+            v[4 * j + 2] += __uint_as_float(qv.z);
+            v[4 * j + 3] += __uint_as_float(qv.w);
           }
         }
-      }
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = act_apply(v[j], a.act);
-#pragma unroll
-      for (int j = 0; j < CH; ++j) {
-        uint4 qv;
-        if (OBF) {
-          qv.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
-          qv.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
-          qv.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
-          qv.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-        } else {
-          qv = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]),
-                          __float_as_uint(v[4 * j + 3]));
+      } else if (m < a.M) {
+        const int c0 = n0 + h * 32;
+        const int ncols = max(0, min(32, a.Cout - c0));
+        int64_t rr = m;
+        if (a.res_mode == 1) {
+          const int hw = a.Ho * a.Wo;
+          const int n = m / hw, rem = m - n * hw;
+          const int ho = rem / a.Wo, wo = rem - ho * a.Wo;
+          rr = (int64_t(n) * a.Hr + (ho >> 1)) * a.Wr + (wo >> 1);
         }
-        *reinterpret_cast<uint4*>(sbO + slab_off(lane, h * CH + j)) = qv;
-      }
-    }
-    if (cres) {   // every lane is done with sbR: fetch the next slab's residual behind the store
-      __syncwarp();
-      if (sidx + 1 < NS && n0 + SC < a.Cout) res_prefetch<BN, OBF>(a, sbR, row0, n0 + SC);
-    }
-    if (a.epi == 2) {
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        tma_store_2d(tmOut, n0, row0, sbO);
-        bulk_commit();
-      }
-    } else {
-      __syncwarp();
-      uint8_t* obase = reinterpret_cast<uint8_t*>(a.out) + int64_t(n0) * ES + xc * 16;
+        if (a.res_bf16) {
+          const __nv_bfloat16* rp = reinterpret_cast<const __nv_bfloat16*>(a.res) + rr * a.ldr + c0;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int grow = row0 + xr + 4 * i;
-        if (grow < a.M && xc < nch)
-          *reinterpret_cast<uint4*>(obase + int64_t(grow) * a.ldo * ES) =
-              *reinterpret_cast<const uint4*>(sbO + slab_off(xr + 4 * i, xc));
+          for (int j = 0; j < 32; ++j)
+            if (j < ncols) v[j] += __bfloat162float(rp[j]);
+        } else {
+          const float* rp = reinterpret_cast<const float*>(a.res) + rr * a.ldr + c0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < ncols) v[j] += rp[j];
+        }
       }
     }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = act_apply(v[j], a.act);
+#pragma unroll
+    for (int j = 0; j < CH; ++j) {
+      uint4 qv;
+      if (OBF) {
+        qv.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+        qv.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+        qv.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+        qv.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+      } else {
+        qv = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]),
+                        __float_as_uint(v[4 * j + 3]));
+      }
+      *reinterpret_cast<uint4*>(sb + slab_off(lane, h * CH + j)) = qv;
+    }
+  }
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmOut, n0, row0, sb);
+    bulk_commit();
   }
 }
 
 // MODE 0: A via TMA; MODE 1: im2col gather in 16-byte units (Cp % 8 == 0); MODE 2: 8-byte units (Cp == 4).
+// Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-9 epilogue (two per TMEM lane quarter,
+// splitting the column slabs), 10-13 im2col gather (MODE 1/2).
 template <int BN, int MODE>
-__global__ void __launch_bounds__(MODE ? 320 : 192, 1)
+__global__ void __launch_bounds__(MODE ? 448 : 320, 1)
     conv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmOut, const ConvGemmArgs a) {
-  using C = Cfg<BN>;
-  constexpr int STAGES = C::STAGES;
+                     const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
+                     const ConvGemmArgs a) {
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  const int STAGES = a.stages;
+  const int RS = a.res_slots;
+  const uint32_t RSB = uint32_t(a.res_slot_bytes);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * C::A_BYTES;
-  uint8_t* sE = sB + STAGES * C::B_BYTES;   // epilogue slabs (1024-byte aligned)
-  uint64_t* full = reinterpret_cast<uint64_t*>(sE + C::EPI_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* accf = empty + STAGES;
+  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* sOut = sB + STAGES * B_BYTES;
+  uint8_t* sRes = sOut + kOutStage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sRes + RS * RSB);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* accf = empty + kMaxStages;
   uint64_t* acce = accf + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acce + 2);
+  uint64_t* resf = acce + 2;
+  uint64_t* rese = resf + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rese + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -468,7 +420,9 @@ __global__ void __launch_bounds__(MODE ? 320 : 192, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf[i], 1u);
-      mbar_init(&acce[i], 128u);
+      mbar_init(&acce[i], 8u);
+      mbar_init(&resf[i], 1u);
+      mbar_init(&rese[i], 8u);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -478,8 +432,9 @@ __global__ void __launch_bounds__(MODE ? 320 : 192, 1)
     if (MODE == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
     if (a.epi == 2) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmOut) : "memory");
+    if (RS) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmRes) : "memory");
   }
-  if (warp == 1) tmem_alloc(tmem_holder, C::TMEM_COLS);
+  if (warp == 1) tmem_alloc(tmem_holder, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -489,18 +444,32 @@ __global__ void __launch_bounds__(MODE ? 320 : 192, 1)
   const int tiles_n = (a.Cout + BN - 1) / BN;
   const int total = tiles_m * tiles_n;
   const int KT = a.Kpad / BK;
+  const int SC = a.out_bf16 ? 64 : 32;   // output columns per 128-byte slab
+  const int NS = BN / SC;
 
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      int it = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
         const int mt = t / tiles_n, nt = t - (t / tiles_n) * tiles_n;
+        if (RS) {   // the tile's residual, into a ring slot, ahead of its operands
+          const int slot = it % RS;
+          const uint32_t rph = uint32_t(it / RS) & 1u;
+          if (!mbar_wait(&rese[slot], rph ^ 1u, abort_flag, a.err, 64u)) goto producer_done;
+          int nsl = 0;
+          for (int s2 = 0; s2 < NS; ++s2)
+            if (nt * BN + s2 * SC < a.Cout) ++nsl;
+          mbar_expect_tx(&resf[slot], uint32_t(nsl) * 128u * 128u);
+          for (int s2 = 0; s2 < nsl; ++s2)
+            tma_load_2d(sRes + slot * RSB + s2 * 128 * 128, &tmRes, nt * BN + s2 * SC, mt * BM, &resf[slot]);
+        }
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) goto producer_done;
-          mbar_expect_tx(&full[stage], (MODE == 0 ? C::A_BYTES : 0u) + C::B_BYTES);
-          if (MODE == 0) tma_load_2d(sA + stage * C::A_BYTES, &tmA, kt * BK, mt * BM, &full[stage]);
-          tma_load_2d(sB + stage * C::B_BYTES, &tmB, kt * BK, nt * BN, &full[stage]);
+          mbar_expect_tx(&full[stage], (MODE == 0 ? A_BYTES : 0u) + B_BYTES);
+          if (MODE == 0) tma_load_2d(sA + stage * A_BYTES, &tmA, kt * BK, mt * BM, &full[stage]);
+          tma_load_2d(sB + stage * B_BYTES, &tmB, kt * BK, nt * BN, &full[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -529,8 +498,8 @@ __global__ void __launch_bounds__(MODE ? 320 : 192, 1)
           }
           tc_fence_after();
           if (MODE) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          const uint64_t ad = sw128_desc(smem_u32(sA + stage * C::A_BYTES));
-          const uint64_t bd = sw128_desc(smem_u32(sB + stage * C::B_BYTES));
+          const uint64_t ad = sw128_desc(smem_u32(sA + stage * A_BYTES));
+          const uint64_t bd = sw128_desc(smem_u32(sB + stage * B_BYTES));
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
             umma_bf16(d_tmem, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), idesc, (kt | kk) != 0 ? 1u : 0u);
@@ -544,8 +513,10 @@ __global__ void __launch_bounds__(MODE ? 320 : 192, 1)
         umma_commit(&accf[acc]);
       }
     }
-  } else if (warp < 6) {
-    const int q = warp & 3;   // TMEM lane quarter this warp may access
+  } else if (warp < 10) {
+    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    const int hsel = (warp - 2) >> 2; // which of the two warps of this quarter
+    uint8_t* sb = sOut + (warp - 2) * 4096;
     int it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
       const int mt = t / tiles_n, nt = t - (t / tiles_n) * tiles_n;
@@ -554,30 +525,40 @@ __global__ void __launch_bounds__(MODE ? 320 : 192, 1)
       if (!mbar_wait(&accf[acc], aph, abort_flag, a.err, 8u)) break;
       tc_fence_after();
       const int row0 = mt * BM + q * 32;
-      const int m = row0 + lane;
       const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
-      if (a.epi != 0) {
-        if (row0 < a.M) {   // warp-uniform
-          uint8_t* ebuf = sE + q * 8192;
-          if (a.out_bf16) epilogue_slabs<BN, true>(a, &tmOut, tbase, row0, nt * BN, ebuf);
-          else epilogue_slabs<BN, false>(a, &tmOut, tbase, row0, nt * BN, ebuf);
-        }
-      } else {
+      const int slot = RS ? it % RS : 0;
+      if (RS && !mbar_wait(&resf[slot], uint32_t(it / RS) & 1u, abort_flag, a.err, 32u)) break;
+      if (row0 < a.M) {   // warp-uniform
+        if (a.epi == 2) {
+          for (int s2 = hsel; s2 < NS; s2 += 2) {
+            const int n0 = nt * BN + s2 * SC;
+            if (n0 >= a.Cout) break;
+            const uint8_t* rslab = RS ? sRes + slot * RSB + s2 * 128 * 128 : nullptr;
+            if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab);
+            else epilogue_slab<false>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab);
+          }
+        } else {
+          const int m = row0 + lane;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tbase + uint32_t(c * 32), r);
-          const int n0 = nt * BN + c * 32;
-          if (n0 < a.Cout && m < a.M) epilogue_chunk(a, r, m, n0);
+          for (int c = hsel; c < BN / 32; c += 2) {
+            uint32_t r[32];
+            tmem_ld32(tbase + uint32_t(c * 32), r);
+            const int n0 = nt * BN + c * 32;
+            if (n0 < a.Cout && m < a.M) epilogue_chunk(a, r, m, n0);
+          }
         }
       }
       tc_fence_before();
-      mbar_arrive(&acce[acc]);
+      __syncwarp();
+      if (lane == 0) {
+        if (RS) mbar_arrive(&rese[slot]);
+        mbar_arrive(&acce[acc]);
+      }
     }
-    if (a.epi == 2 && lane == 0) bulk_wait_all();
+    if (lane == 0) bulk_wait_all();
   } else if (MODE != 0) {
     // ---- im2col gather producers -------------------------------------------------------------
-    const int gt = threadIdx.x - 192;   // 0..127
+    const int gt = threadIdx.x - 320;   // 0..127
     constexpr int TPR = MODE == 1 ? 8 : 16;          // threads per 128-byte row
     constexpr int ROWS_PER_PASS = 128 / TPR;         // 16 or 8
     constexpr int PASSES = BM / ROWS_PER_PASS;       // 8 or 16
@@ -610,7 +591,7 @@ __global__ void __launch_bounds__(MODE ? 320 : 192, 1)
       }
       for (int kt = 0; kt < KT; ++kt) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 16u)) goto gather_done;
-        const uint32_t sbase = smem_u32(sA + stage * C::A_BYTES);
+        const uint32_t sbase = smem_u32(sA + stage * A_BYTES);
         if (MODE == 1) {
           const int kidx = kt * BK + sub * 8;
           const int tap = kidx / a.Cp;
@@ -657,7 +638,7 @@ __global__ void __launch_bounds__(MODE ? 320 : 192, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -683,9 +664,8 @@ bool encode_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(tm, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                  const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -698,15 +678,15 @@ cudaError_t ensure_attr() {
   cudaGetDevice(&dev);
   const uint64_t bit = uint64_t(1) << (dev & 63);
   if (done_mask.load() & bit) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(conv_gemm_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       Cfg<BN>::SMEM);
+  cudaError_t e =
+      cudaFuncSetAttribute(conv_gemm_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
   if (e == cudaSuccess) done_mask.fetch_or(bit);
   return e;
 }
 
 template <int BN, int MODE>
 cudaError_t launch_t(const ConvGemmPlan& p, cudaStream_t s) {
-  conv_gemm_kernel<BN, MODE><<<p.grid, MODE ? 320 : 192, Cfg<BN>::SMEM, s>>>(p.tmA, p.tmB, p.tmOut, p.args);
+  conv_gemm_kernel<BN, MODE><<<p.grid, MODE ? 448 : 320, p.smem, s>>>(p.tmA, p.tmB, p.tmOut, p.tmRes, p.args);
   return cudaGetLastError();
 }
 
@@ -719,40 +699,57 @@ cudaError_t ensure_attr_mode(int mode) {
 
 void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const void* w, int num_sms) {
   ConvGemmArgs& a = p.args;
-  // Tile width: widest N tile that still gives at least one tile per SM.
-  auto tiles = [&](int bn) { return int64_t((a.M + BM - 1) / BM) * ((a.Cout + bn - 1) / bn); };
-  int bn = a.Cout <= 64 ? 64 : (a.Cout <= 128 ? 128 : 256);
-  while (bn > 64 && tiles(bn) < num_sms) bn /= 2;
-  p.bn = bn;
-  p.smem = bn == 64 ? Cfg<64>::SMEM : (bn == 128 ? Cfg<128>::SMEM : Cfg<256>::SMEM);
-  int64_t t = tiles(bn);
-  p.grid = int(t < num_sms ? t : num_sms);
   std::memset(&p.tmA, 0, sizeof(p.tmA));
   std::memset(&p.tmB, 0, sizeof(p.tmB));
-  bool ok = encode_2d(&p.tmB, w, uint64_t(a.Kpad), uint64_t(a.Cout), uint64_t(a.Kpad) * 2, BK, uint32_t(bn));
-  if (!a.gather) {
-    ok = ok && encode_2d(&p.tmA, a_rows, uint64_t(lda), uint64_t(a.M), uint64_t(lda) * 2, BK, BM);
-  }
-  // Epilogue variant: 0 row-per-thread global stores; 1 slabs through shared memory with coalesced
-  // 16-byte stores; 2 slabs with TMA bulk stores. Slab paths need 16-byte aligned rows and chunks.
   std::memset(&p.tmOut, 0, sizeof(p.tmOut));
+  std::memset(&p.tmRes, 0, sizeof(p.tmRes));
+  // Epilogue: TMA bulk stores when rows and 16-byte chunks are aligned (else direct row stores);
+  // a same-dtype, same-shape residual is then streamed into shared memory by the producer warp.
   const int es = a.out_bf16 ? 2 : 4;
   const int epc = 16 / es;
+  const uint32_t sc = a.out_bf16 ? 64 : 32;
+  a.epi = 0;
+  a.res_slots = 0;
+  a.res_slot_bytes = 0;
   int want = 2;
   if (const char* e = std::getenv("SHOROKOO_B200_EPI")) want = std::atoi(e);
-  a.epi = 0;
-  a.epi_res = 0;
-  if (want != 0 && a.group_rows == 0 && a.Cout % epc == 0 && (a.ldo * es) % 16 == 0 &&
-      (reinterpret_cast<uintptr_t>(a.out) & 15) == 0) {
-    a.epi = 1;
-    if (want == 2 && encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldo) * es,
-                               a.out_bf16 ? 64 : 32, 32, !a.out_bf16))
-      a.epi = 2;
-    if (a.res && a.res_mode == 0 && a.res_bf16 == a.out_bf16 && (a.ldr * es) % 16 == 0 &&
-        (reinterpret_cast<uintptr_t>(a.res) & 15) == 0)
-      a.epi_res = 1;
-  }
+  const bool out_ok = want != 0 && a.group_rows == 0 && a.Cout % epc == 0 && (a.ldo * es) % 16 == 0 &&
+                      (reinterpret_cast<uintptr_t>(a.out) & 15) == 0;
+  const bool res_ring = out_ok && a.res && a.res_mode == 0 && a.res_bf16 == a.out_bf16 && (a.ldr * es) % 16 == 0 &&
+                        (reinterpret_cast<uintptr_t>(a.res) & 15) == 0;
+  // Tile width: widest N tile that still gives at least one tile per SM; residual convs use at most
+  // 128 so two residual tiles fit beside a deep operand pipeline.
+  auto tiles = [&](int bn) { return int64_t((a.M + BM - 1) / BM) * ((a.Cout + bn - 1) / bn); };
+  int bn = a.Cout <= 64 ? 64 : (a.Cout <= 128 || res_ring ? 128 : 256);
+  while (bn > 64 && tiles(bn) < num_sms) bn /= 2;
+  p.bn = bn;
+  const int stage_bytes = BM * BK * 2 + bn * BK * 2;
+  const int fixed = int(kOutStage) + 1024 + 512;
+  const int rsb = 128 * bn * es;
+  int rs = 0;
+  if (res_ring) rs = (kSmemLimit - fixed - 2 * rsb) / stage_bytes >= 3 ? 2 : 1;
+  int stages = std::min(kMaxStages, (kSmemLimit - fixed - rs * rsb) / stage_bytes);
+  if (stages < 2) throw std::runtime_error("conv_gemm: shared-memory plan leaves fewer than 2 stages");
+  a.stages = stages;
+  p.smem = stages * stage_bytes + fixed + rs * rsb;
+  int64_t t = tiles(bn);
+  p.grid = int(t < num_sms ? t : num_sms);
+  bool ok = encode_2d(&p.tmB, w, uint64_t(a.Kpad), uint64_t(a.Cout), uint64_t(a.Kpad) * 2, BK, uint32_t(bn));
+  if (!a.gather) ok = ok && encode_2d(&p.tmA, a_rows, uint64_t(lda), uint64_t(a.M), uint64_t(lda) * 2, BK, BM);
   if (!ok) throw std::runtime_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad layout)");
+  if (out_ok &&
+      encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldo) * es, sc, 32, !a.out_bf16)) {
+    a.epi = 2;
+    if (rs && encode_2d(&p.tmRes, a.res, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldr) * es, sc, 128,
+                        !a.out_bf16)) {
+      a.res_slots = rs;
+      a.res_slot_bytes = rsb;
+    } else {
+      // no ring: restore the operand stages the ring would have used
+      a.stages = std::min(kMaxStages, (kSmemLimit - fixed) / stage_bytes);
+      p.smem = a.stages * stage_bytes + fixed;
+    }
+  }
   const int mode = a.gather ? (a.Cp == 4 ? 2 : 1) : 0;
   cudaError_t e = bn == 64 ? ensure_attr_mode<64>(mode) : (bn == 128 ? ensure_attr_mode<128>(mode) : ensure_attr_mode<256>(mode));
   if (e != cudaSuccess) throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));

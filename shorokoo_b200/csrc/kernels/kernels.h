@@ -37,14 +37,18 @@ struct ConvGemmArgs {
   int64_t group_stride;    // elements between output groups
   int act;                 // 0 none, 1 relu, 2 sigmoid
   unsigned int* err;       // device error word (bounded-wait timeouts)
-  int epi;                 // set by conv_gemm_prepare: epilogue variant (0 direct, 1 smem slabs, 2 TMA store)
-  int epi_res;             // set by conv_gemm_prepare: residual read as coalesced slabs
+  // set by conv_gemm_prepare:
+  int epi;                 // epilogue: 0 direct row stores, 2 TMA bulk stores from smem slabs
+  int stages;              // operand pipeline depth
+  int res_slots;           // residual ring slots filled by the producer warp (0: direct residual reads)
+  int res_slot_bytes;
 };
 
 struct ConvGemmPlan {
   CUtensorMap tmA;   // valid when gather == 0
   CUtensorMap tmB;
   CUtensorMap tmOut;   // valid when args.epi == 2
+  CUtensorMap tmRes;   // valid when args.res_slots > 0
   int bn;            // 64, 128 or 256
   int grid;
   int smem;
