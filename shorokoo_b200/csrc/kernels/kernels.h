@@ -73,6 +73,10 @@ struct TDesc {
 // C..Cp-1 are zero.
 cudaError_t to_nhwc_bf16(const void* src, int src_bf16, const int64_t* shape4, const int64_t* stride4,
                          void* dst, int Cp, cudaStream_t s);
+// 2x2 space-to-depth: dst (NHWC bf16 [N, Hs, Ws, 16]) <- src logical [N, C<=4, H, W] (any strides):
+// dst[n, hs, ws, (p*2+q)*C + c] = src[n, c, 2hs+p, 2ws+q], zero outside the image and in channels 4C..15.
+cudaError_t to_s2d_bf16(const void* src, int src_bf16, const int64_t* shape4, const int64_t* stride4, void* dst,
+                        int64_t Hs, int64_t Ws, cudaStream_t s);
 // dst (bf16 [M, Kp]) <- src logical [M, K] with arbitrary strides; columns K..Kp-1 zero.
 cudaError_t to_rows_bf16(const void* src, int src_bf16, int64_t M, int64_t K, int64_t sm, int64_t sk,
                          void* dst, int64_t Kp, cudaStream_t s);

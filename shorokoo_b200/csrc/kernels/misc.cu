@@ -66,6 +66,34 @@ __global__ void to_nhwc_bf16_kernel(const void* __restrict__ src, int src_bf16, 
   }
 }
 
+// 2x2 space-to-depth into NHWC bf16 with 16 channels: dst[n, hs, ws, (p*2+q)*C + c] =
+// src[n, c, 2hs+p, 2ws+q] (zero outside the image; channels 4C..15 zero). One thread per pixel.
+__global__ void to_s2d_bf16_kernel(const void* __restrict__ src, int src_bf16, int64_t N, int64_t C, int64_t H,
+                                   int64_t W, int64_t s0, int64_t s1, int64_t s2, int64_t s3,
+                                   __nv_bfloat16* __restrict__ dst, int64_t Hs, int64_t Ws) {
+  const int64_t total = N * Hs * Ws;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t n = i / (Hs * Ws);
+    const int64_t r = i - n * Hs * Ws;
+    const int64_t hs = r / Ws, ws = r - (r / Ws) * Ws;
+    __align__(16) __nv_bfloat16 v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __float2bfloat16_rn(0.f);
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int64_t h = 2 * hs + p, w = 2 * ws + q;
+        if (h >= H || w >= W) continue;
+        for (int64_t c = 0; c < C; ++c)
+          v[(p * 2 + q) * C + c] = __float2bfloat16_rn(ld_any(src, src_bf16, n * s0 + c * s1 + h * s2 + w * s3));
+      }
+    uint4* d = reinterpret_cast<uint4*>(dst + i * 16);
+    d[0] = reinterpret_cast<const uint4*>(v)[0];
+    d[1] = reinterpret_cast<const uint4*>(v)[1];
+  }
+}
+
 __global__ void to_rows_bf16_kernel(const void* __restrict__ src, int src_bf16, int64_t M, int64_t K, int64_t sm,
                                     int64_t sk, __nv_bfloat16* __restrict__ dst, int64_t Kp) {
   const int64_t total = M * Kp;
@@ -266,6 +294,15 @@ cudaError_t to_nhwc_bf16(const void* src, int src_bf16, const int64_t* sh, const
   const int64_t total = sh[0] * sh[2] * sh[3] * (Cp / 4);
   to_nhwc_bf16_kernel<<<grid_for(total), kThreads, 0, s>>>(src, src_bf16, sh[0], sh[1], sh[2], sh[3], st[0], st[1],
                                                            st[2], st[3], reinterpret_cast<__nv_bfloat16*>(dst), Cp);
+  return cudaGetLastError();
+}
+
+cudaError_t to_s2d_bf16(const void* src, int src_bf16, const int64_t* sh, const int64_t* st, void* dst, int64_t Hs,
+                        int64_t Ws, cudaStream_t s) {
+  if (sh[1] > 4) return cudaErrorInvalidValue;
+  to_s2d_bf16_kernel<<<grid_for(sh[0] * Hs * Ws), kThreads, 0, s>>>(src, src_bf16, sh[0], sh[1], sh[2], sh[3], st[0],
+                                                                    st[1], st[2], st[3],
+                                                                    reinterpret_cast<__nv_bfloat16*>(dst), Hs, Ws);
   return cudaGetLastError();
 }
 

@@ -317,22 +317,76 @@ void Plan::plan_conv(const Op& op) {
   const int64_t N = xv.shape[0], C = xv.shape[1], H = xv.shape[2], W = xv.shape[3];
   const int64_t Cout = Wt.shape[0], KH = Wt.shape[2], KW = Wt.shape[3];
   const int64_t Ho = yv.shape[2], Wo = yv.shape[3];
-  const int Cp = int(C % 8 == 0 ? C : (C <= 4 ? 4 : round_up(C, 8)));
-  const bool one_by_one = KH == 1 && KW == 1 && op.strides[0] == 1 && op.strides[1] == 1 && op.pads[0] == 0 &&
+  // Strided convs on at most 4 input channels (the ResNet stem) run as a stride-1 conv over the 2x2
+  // space-to-depth image: out(ho) reads original rows i = 2*ho - pt + kh; with e = pt % 2 and
+  // u = kh + e = 2a + p this is s2d row ho - (pt+e)/2 + a, parity p, so the kernel becomes
+  // ceil((KH+e)/2) taps over 16 channels (p, q, c) with zero weights where kh falls outside [0, KH).
+  const bool s2d = op.strides[0] == 2 && op.strides[1] == 2 && op.dilations[0] == 1 && op.dilations[1] == 1 &&
+                   C <= 4 && KH >= 3 && KW >= 3;
+  int64_t gH = H, gW = W, gKH = KH, gKW = KW, gsh = op.strides[0], gsw = op.strides[1];
+  int64_t gph = op.pads[0], gpw = op.pads[1], gdh = op.dilations[0], gdw = op.dilations[1];
+  int Cp = int(C % 8 == 0 ? C : (C <= 4 ? 4 : round_up(C, 8)));
+  int64_t et = 0, el = 0;
+  if (s2d) {
+    et = op.pads[0] % 2;
+    el = op.pads[1] % 2;
+    gH = ceil_div(H, 2);
+    gW = ceil_div(W, 2);
+    gKH = ceil_div(KH + et, 2);
+    gKW = ceil_div(KW + el, 2);
+    gsh = gsw = 1;
+    gph = (op.pads[0] + et) / 2;
+    gpw = (op.pads[1] + el) / 2;
+    gdh = gdw = 1;
+    Cp = 16;
+  }
+  const bool one_by_one = !s2d && KH == 1 && KW == 1 && op.strides[0] == 1 && op.strides[1] == 1 && op.pads[0] == 0 &&
                           op.pads[1] == 0 && op.pads[2] == 0 && op.pads[3] == 0 && Cp % 8 == 0;
-  DevTensor x = as_nhwc_bf16(op.in[0], Cp);
-  const int64_t K = KH * KW * Cp;
+  DevTensor x;
+  if (s2d) {
+    auto key = std::make_pair(op.in[0], -16);
+    auto it = conv_cache_.find(key);
+    if (it != conv_cache_.end()) {
+      x = it->second;
+    } else {
+      const DevTensor t = vt_[size_t(op.in[0])];
+      x = alloc_nhwc({N, 16, gH, gW}, true, 16);
+      const int64_t Hs = gH, Ws = gW;
+      add_step("to_s2d_bf16", {t}, {x}, [this, t, x, Hs, Ws]() {
+        const void* sp = ptr(t);
+        void* dp = ptr(x);
+        int64_t sh[4] = {t.shape[0], t.shape[1], t.shape[2], t.shape[3]};
+        int64_t st[4] = {t.strides[0], t.strides[1], t.strides[2], t.strides[3]};
+        int sb = t.bf16;
+        return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+          return k::to_s2d_bf16(sp, sb, sh, st, dp, Hs, Ws, s);
+        });
+      });
+      conv_cache_[key] = x;
+    }
+  } else {
+    x = as_nhwc_bf16(op.in[0], Cp);
+  }
+  const int64_t K = gKH * gKW * Cp;
   const int64_t Kpad = round_up(K, 64);
-  SB_CHECK(N * Ho * Wo < (int64_t(1) << 31) && N * H * W * Cp < (int64_t(1) << 40), SB_UNSUPPORTED,
+  SB_CHECK(N * Ho * Wo < (int64_t(1) << 31) && N * gH * gW * Cp < (int64_t(1) << 40), SB_UNSUPPORTED,
            "Conv: problem too large for 32-bit row indexing");
-  // weights [Cout, Kpad] bf16, K ordered (kh, kw, c)
+  // weights [Cout, Kpad] bf16, K ordered (kh, kw, c) of the kernel as run
   std::vector<uint16_t> wb(size_t(Cout * Kpad), 0);
   const float* wp = Wt.ptr<float>();
   for (int64_t m = 0; m < Cout; ++m)
     for (int64_t c = 0; c < C; ++c)
       for (int64_t a = 0; a < KH; ++a)
-        for (int64_t b = 0; b < KW; ++b)
-          wb[size_t(m * Kpad + (a * KW + b) * Cp + c)] = f32_to_bf16_rne(wp[((m * C + c) * KH + a) * KW + b]);
+        for (int64_t b = 0; b < KW; ++b) {
+          int64_t kidx;
+          if (s2d) {
+            const int64_t u = a + et, v = b + el;   // u = 2*a' + p, v = 2*b' + q
+            kidx = ((u / 2) * gKW + (v / 2)) * Cp + ((u % 2) * 2 + (v % 2)) * C + c;
+          } else {
+            kidx = (a * KW + b) * Cp + c;
+          }
+          wb[size_t(m * Kpad + kidx)] = f32_to_bf16_rne(wp[((m * C + c) * KH + a) * KW + b]);
+        }
   DevTensor wt;
   wt.buf = -1;
   wt.off = add_weight_bytes(wb.data(), wb.size() * 2);
@@ -374,7 +428,7 @@ void Plan::plan_conv(const Op& op) {
   const int sms = num_sms_;
   const std::string kind = "conv " + std::to_string(KH) + "x" + std::to_string(KW) + "/" +
                            std::to_string(op.strides[0]) + " " + std::to_string(C) + "->" + std::to_string(Cout) +
-                           " M=" + std::to_string(N * Ho * Wo) + (one_by_one ? " tma" : " gather") +
+                           " M=" + std::to_string(N * Ho * Wo) + (one_by_one ? " tma" : (s2d ? " s2d" : " gather")) +
                            (op.residual >= 0 ? " +res" : "");
   add_step(kind, reads, {y}, [=]() {
     auto p = std::make_shared<k::ConvGemmPlan>();
@@ -383,19 +437,19 @@ void Plan::plan_conv(const Op& op) {
     a.gather = one_by_one ? 0 : 1;
     a.x = ptr(x);
     a.N = int(N);
-    a.H = int(H);
-    a.W = int(W);
+    a.H = int(gH);
+    a.W = int(gW);
     a.Cp = Cp;
     a.Ho = int(Ho);
     a.Wo = int(Wo);
-    a.KH = int(KH);
-    a.KW = int(KW);
-    a.sh = int(op.strides[0]);
-    a.sw = int(op.strides[1]);
-    a.ph = int(op.pads[0]);
-    a.pw = int(op.pads[1]);
-    a.dh = int(op.dilations[0]);
-    a.dw = int(op.dilations[1]);
+    a.KH = int(gKH);
+    a.KW = int(gKW);
+    a.sh = int(gsh);
+    a.sw = int(gsw);
+    a.ph = int(gph);
+    a.pw = int(gpw);
+    a.dh = int(gdh);
+    a.dw = int(gdw);
     a.M = int(N * Ho * Wo);
     a.Cout = int(Cout);
     a.Kpad = int(Kpad);

@@ -39,6 +39,11 @@ def test_gemm(m, k, n, relu):
     dict(c=64, cout=36, k=3, auto_pad="SAME_UPPER", h=13, w=16),                # reg head
     dict(c=128, cout=64, k=1, pads=[0, 0, 0, 0], h=10, w=16, upsample_residual=True),  # FPN lateral
     dict(n=1, c=8, cout=8, k=3, h=1, w=1),
+    # strided convs on <= 4 channels run over the 2x2 space-to-depth image
+    dict(c=3, cout=64, k=7, stride=2, pads=[3, 2, 2, 3], h=31, w=33, bn=True, relu=True),
+    dict(c=1, cout=16, k=3, stride=2, pads=[1, 1, 1, 1], h=9, w=12),
+    dict(c=4, cout=24, k=5, stride=2, pads=[0, 0, 0, 0], h=17, w=16),
+    dict(c=2, cout=8, k=3, stride=2, auto_pad="SAME_UPPER", h=10, w=7),
 ])
 def test_conv(kw):
     case = conv_case(**kw)
