@@ -176,6 +176,8 @@ def main():
     ap.add_argument("--workload", default="resnet50", choices=sorted(WORKLOADS))
     ap.add_argument("--ref-sample", type=int, default=8, help="images per step of the CPU reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the workload's global batch (small cases for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -192,7 +194,7 @@ def main():
     from shorokoo_b200 import B200InferenceSessionFactory
 
     name = args.workload
-    total = WORKLOADS[name][1]
+    total = args.batch or WORKLOADS[name][1]
     per = total // world + (1 if rank < total % world else 0)
     begin = rank * (total // world) + min(rank, total % world)
     full = make_case(name, total) if world == 1 else None

@@ -6,9 +6,13 @@
 //               output tile's residual into a shared-memory ring ahead of its operands
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16 per instr)
 //   warps 2-9   epilogue, two warps per TMEM lane quarter: tcgen05.ld accumulator -> bias /
-//               residual / activation -> swizzled smem slab -> TMA bulk store
-//   warps 10-13 (spatial convs) im2col gather producers: cp.async 16B/8B with zero fill, written
-//               into the 128B-swizzled K-major layout the UMMA smem descriptor expects
+//               residual / activation -> swizzled smem slab (two per warp, alternating) -> TMA
+//               bulk store
+//   warps 10-13 (gather modes only) im2col gather producers: cp.async 16B/8B with zero fill,
+//               written into the 128B-swizzled K-major layout the UMMA smem descriptor expects
+// Spatial convolutions whose activation channels come in 64s (or 16s) instead take the A operand
+// with TMA in im2col mode: one load per k-tile brings 128 consecutive output pixels x 64
+// channels of one filter tap, zero-filled outside the image, straight into the swizzled layout.
 // Operand tiles are BM=128 x BK=64 bf16 (one 128-byte swizzle atom per row); the fp32 accumulator
 // is double-buffered in TMEM so the epilogue of tile i overlaps the main loop of tile i+1.
 // Every mbarrier wait is bounded (global timer); a timeout sets a device error word and the CTA
@@ -91,6 +95,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, in
       : "memory");
 }
 
+// im2col TMA load: 4D activation (C, W, H, N); (c, w, h, n) is the channel block and the top-left
+// input corner of the filter window of the first output pixel, (ow, oh) the filter tap offset.
+__device__ __forceinline__ void tma_load_im2col(void* dst, const CUtensorMap* tm, int c, int w, int h, int n,
+                                                uint16_t ow, uint16_t oh, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(smem_u32(dst)),
+      "l"(tm), "r"(c), "r"(w), "r"(h), "r"(n), "r"(smem_u32(bar)), "h"(ow), "h"(oh)
+      : "memory");
+}
+
 // TMA store of a swizzled smem box to global (bulk-group completion).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, int c0, int c1, const void* src) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tm), "r"(c0),
@@ -98,7 +113,7 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, int c0, int 
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -162,6 +177,18 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   d |= uint64_t(1024 >> 4) << 32;         // SBO
   d |= uint64_t(1) << 46;                 // version
   d |= uint64_t(2) << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+// The same for a 32-byte swizzle (rows of 32 B = 16 bf16, 8-row groups 256 B apart, layout type 6):
+// one such tile is exactly the K=16 slice a single MMA consumes.
+__device__ __forceinline__ uint64_t sw32_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr & 0x3FFFFu) >> 4);
+  d |= uint64_t(1) << 16;
+  d |= uint64_t(256 >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(6) << 61;                 // SWIZZLE_32B
   return d;
 }
 
@@ -282,7 +309,7 @@ __device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint
 __device__ __forceinline__ uint32_t slab_off(int r, int j) { return uint32_t(r * 128 + ((j ^ (r & 7)) << 4)); }
 
 constexpr int kSmemLimit = 232448;        // opt-in maximum dynamic shared memory per block
-constexpr uint32_t kOutStage = 8 * 4096;  // one 32-row x 128-byte output slab per epilogue warp
+constexpr uint32_t kOutStage = 16 * 4096;  // two 32-row x 128-byte output slabs per epilogue warp
 constexpr int kMaxStages = 8;
 
 // One output slab (32 rows from row0, 128 bytes of columns from n0) of one epilogue warp:
@@ -297,7 +324,7 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
   const int lane = threadIdx.x & 31;
   const int m = row0 + lane;
   const int rrow = (row0 & (BM - 1)) + lane;   // row inside the 128-row residual slab
-  if (lane == 0) bulk_wait_read0();             // the previous store from this buffer has been read
+  if (lane == 0) bulk_wait_read1();             // the store before the last one (same buffer) has been read
   __syncwarp();
 #pragma unroll 1
   for (int h = 0; h < SC / 32; ++h) {
@@ -381,17 +408,23 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
   }
 }
 
-// MODE 0: A via TMA; MODE 1: im2col gather in 16-byte units (Cp % 8 == 0); MODE 2: 8-byte units (Cp == 4).
+// MODE is a ConvAMode: 0 A rows via TMA; 1 / 2 im2col gather by cp.async in 16 / 8-byte units;
+// 3 / 4 im2col by TMA with 64 / 16 channels per pixel.
 // Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-9 epilogue (two per TMEM lane quarter,
 // splitting the column slabs), 10-13 im2col gather (MODE 1/2).
+template <int MODE>
+constexpr int kThreads = (MODE == 1 || MODE == 2) ? 448 : 320;
+
 template <int BN, int MODE>
-__global__ void __launch_bounds__(MODE ? 448 : 320, 1)
+__global__ void __launch_bounds__(kThreads<MODE>, 1)
     conv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
                      const ConvGemmArgs a) {
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BN * BK * 2;
   constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr bool GATHER = MODE == 1 || MODE == 2;
+  constexpr bool A_TMA = !GATHER;
   const int STAGES = a.stages;
   const int RS = a.res_slots;
   const uint32_t RSB = uint32_t(a.res_slot_bytes);
@@ -415,7 +448,7 @@ __global__ void __launch_bounds__(MODE ? 448 : 320, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], MODE ? 129u : 1u);
+      mbar_init(&full[s], GATHER ? 129u : 1u);
       mbar_init(&empty[s], 1u);
     }
     for (int i = 0; i < 2; ++i) {
@@ -429,7 +462,7 @@ __global__ void __launch_bounds__(MODE ? 448 : 320, 1)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   if (warp == 0 && lane == 0) {
-    if (MODE == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+    if (A_TMA) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
     if (a.epi == 2) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmOut) : "memory");
     if (RS) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmRes) : "memory");
@@ -451,9 +484,21 @@ __global__ void __launch_bounds__(MODE ? 448 : 320, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      const int hw_out = a.Ho * a.Wo;
+      const int cblocks = a.Cp / BK;   // 64-channel blocks per filter tap (MODE 3)
       int it = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
         const int mt = t / tiles_n, nt = t - (t / tiles_n) * tiles_n;
+        // im2col: image and top-left input corner of the tile's first output pixel
+        int img = 0, cw = 0, ch = 0;
+        if (MODE == 3 || MODE == 4) {
+          const int m0 = mt * BM;
+          img = m0 / hw_out;
+          const int rem = m0 - img * hw_out;
+          const int ho = rem / a.Wo;
+          ch = ho * a.sh - a.ph;
+          cw = (rem - ho * a.Wo) * a.sw - a.pw;
+        }
         if (RS) {   // the tile's residual, into a ring slot, ahead of its operands
           const int slot = it % RS;
           const uint32_t rph = uint32_t(it / RS) & 1u;
@@ -467,8 +512,23 @@ __global__ void __launch_bounds__(MODE ? 448 : 320, 1)
         }
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) goto producer_done;
-          mbar_expect_tx(&full[stage], (MODE == 0 ? A_BYTES : 0u) + B_BYTES);
+          mbar_expect_tx(&full[stage], (A_TMA ? A_BYTES : 0u) + B_BYTES);
           if (MODE == 0) tma_load_2d(sA + stage * A_BYTES, &tmA, kt * BK, mt * BM, &full[stage]);
+          if (MODE == 3) {
+            const int tap = kt / cblocks, cb = kt - tap * cblocks;
+            const int kh = tap / a.KW, kw = tap - (tap / a.KW) * a.KW;
+            tma_load_im2col(sA + stage * A_BYTES, &tmA, cb * BK, cw, ch, img, uint16_t(kw * a.dw),
+                            uint16_t(kh * a.dh), &full[stage]);
+          }
+          if (MODE == 4) {   // four 16-channel taps, one 4 KB sub-tile each
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int tap = kt * 4 + j;
+              const int kh = tap / a.KW, kw = tap - (tap / a.KW) * a.KW;
+              tma_load_im2col(sA + stage * A_BYTES + j * (BM * 32), &tmA, 0, cw, ch, img, uint16_t(kw * a.dw),
+                              uint16_t(kh * a.dh), &full[stage]);
+            }
+          }
           tma_load_2d(sB + stage * B_BYTES, &tmB, kt * BK, nt * BN, &full[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -497,12 +557,15 @@ __global__ void __launch_bounds__(MODE ? 448 : 320, 1)
             break;
           }
           tc_fence_after();
-          if (MODE) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          if (GATHER) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           const uint64_t ad = sw128_desc(smem_u32(sA + stage * A_BYTES));
           const uint64_t bd = sw128_desc(smem_u32(sB + stage * B_BYTES));
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            umma_bf16(d_tmem, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), idesc, (kt | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t akk = MODE == 4 ? sw32_desc(smem_u32(sA + stage * A_BYTES + kk * (BM * 32)))
+                                           : ad + uint64_t(kk * 2);
+            umma_bf16(d_tmem, akk, bd + uint64_t(kk * 2), idesc, (kt | kk) != 0 ? 1u : 0u);
+          }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -516,7 +579,8 @@ __global__ void __launch_bounds__(MODE ? 448 : 320, 1)
   } else if (warp < 10) {
     const int q = warp & 3;          // TMEM lane quarter this warp may access
     const int hsel = (warp - 2) >> 2; // which of the two warps of this quarter
-    uint8_t* sb = sOut + (warp - 2) * 4096;
+    uint8_t* sb0 = sOut + (warp - 2) * 8192;
+    int nslab = 0;   // slabs stored by this warp so far (selects the buffer)
     int it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
       const int mt = t / tiles_n, nt = t - (t / tiles_n) * tiles_n;
@@ -534,6 +598,7 @@ __global__ void __launch_bounds__(MODE ? 448 : 320, 1)
             const int n0 = nt * BN + s2 * SC;
             if (n0 >= a.Cout) break;
             const uint8_t* rslab = RS ? sRes + slot * RSB + s2 * 128 * 128 : nullptr;
+            uint8_t* sb = sb0 + (nslab++ & 1) * 4096;
             if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab);
             else epilogue_slab<false>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab);
           }
@@ -556,7 +621,7 @@ __global__ void __launch_bounds__(MODE ? 448 : 320, 1)
       }
     }
     if (lane == 0) bulk_wait_all();
-  } else if (MODE != 0) {
+  } else if constexpr (GATHER) {
     // ---- im2col gather producers -------------------------------------------------------------
     const int gt = threadIdx.x - 320;   // 0..127
     constexpr int TPR = MODE == 1 ? 8 : 16;          // threads per 128-byte row
@@ -669,6 +734,40 @@ bool encode_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer
   return r == CUDA_SUCCESS;
 }
 
+PFN_cuTensorMapEncodeIm2col_v12000 get_encode_im2col_fn() {
+  static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(p);
+  });
+  return fn;
+}
+
+// Bounding box of the filter-window corners one output row sweeps: the first corner is -pad, the
+// last (Wo-1)*stride - pad; the map encodes the last as an offset from the far edge (W-1).
+inline int im2col_upper(int W, int Wo, int s, int pad) { return (Wo - 1) * s - pad - (W - 1); }
+
+// im2col tensor map over the NHWC activation a.x (pitch Cp channels): each load is 128 output
+// pixels (traversed W, then H, then N with the conv strides) x `cpp` channels, zero outside.
+bool encode_im2col(CUtensorMap* tm, const ConvGemmArgs& a, int cpp) {
+  auto fn = get_encode_im2col_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {cuuint64_t(a.Cp), cuuint64_t(a.W), cuuint64_t(a.H), cuuint64_t(a.N)};
+  cuuint64_t strides[3] = {cuuint64_t(a.Cp) * 2, cuuint64_t(a.W) * a.Cp * 2, cuuint64_t(a.H) * a.W * a.Cp * 2};
+  int lower[2] = {-a.pw, -a.ph};
+  int upper[2] = {im2col_upper(a.W, a.Wo, a.sw, a.pw), im2col_upper(a.H, a.Ho, a.sh, a.ph)};
+  cuuint32_t estr[4] = {1, cuuint32_t(a.sw), cuuint32_t(a.sh), 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(a.x), dims, strides, lower, upper,
+                  cuuint32_t(cpp), cuuint32_t(BM), estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  cpp == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // The dynamic shared-memory opt-in is a per-device function attribute; it is set while preparing
 // a plan (never during stream capture).
 template <int BN, int MODE>
@@ -686,16 +785,54 @@ cudaError_t ensure_attr() {
 
 template <int BN, int MODE>
 cudaError_t launch_t(const ConvGemmPlan& p, cudaStream_t s) {
-  conv_gemm_kernel<BN, MODE><<<p.grid, MODE ? 448 : 320, p.smem, s>>>(p.tmA, p.tmB, p.tmOut, p.tmRes, p.args);
+  conv_gemm_kernel<BN, MODE><<<p.grid, kThreads<MODE>, p.smem, s>>>(p.tmA, p.tmB, p.tmOut, p.tmRes, p.args);
   return cudaGetLastError();
 }
 
 template <int BN>
 cudaError_t ensure_attr_mode(int mode) {
-  return mode == 0 ? ensure_attr<BN, 0>() : (mode == 1 ? ensure_attr<BN, 1>() : ensure_attr<BN, 2>());
+  switch (mode) {
+    case 0: return ensure_attr<BN, 0>();
+    case 1: return ensure_attr<BN, 1>();
+    case 2: return ensure_attr<BN, 2>();
+    case 3: return ensure_attr<BN, 3>();
+    case 4: return ensure_attr<BN, 4>();
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int BN>
+cudaError_t launch_mode(const ConvGemmPlan& p, cudaStream_t s) {
+  switch (p.mode) {
+    case 0: return launch_t<BN, 0>(p, s);
+    case 1: return launch_t<BN, 1>(p, s);
+    case 2: return launch_t<BN, 2>(p, s);
+    case 3: return launch_t<BN, 3>(p, s);
+    case 4: return launch_t<BN, 4>(p, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace
+
+int conv_gemm_a_mode(const ConvGemmArgs& a) {
+  if (!a.gather) return kARows;
+  // TMA im2col: the corner box must fit the map's signed 8-bit corner fields and the tap offsets
+  // its 8-bit offset fields; activations under 128 KiB keep the cp.async gather.
+  static const bool im2col_on = [] {
+    const char* e = std::getenv("SHOROKOO_B200_IM2COL");
+    return !(e && e[0] == '0');
+  }();
+  const int up_w = im2col_upper(a.W, a.Wo, a.sw, a.pw), up_h = im2col_upper(a.H, a.Ho, a.sh, a.ph);
+  const bool box_ok = a.pw <= 128 && a.ph <= 128 && up_w >= -128 && up_w <= 127 && up_h >= -128 && up_h <= 127 &&
+                      (a.KW - 1) * a.dw <= 255 && (a.KH - 1) * a.dh <= 255 && a.sw <= 8 && a.sh <= 8;
+  const bool big = int64_t(a.N) * a.H * a.W * a.Cp * 2 >= (int64_t(1) << 17);
+  if (im2col_on && box_ok && big) {
+    if (a.Cp % 64 == 0) return kAIm2col64;
+    if (a.Cp == 16 && (a.KH * a.KW) % 4 == 0) return kAIm2col16;
+  }
+  return a.Cp == 4 ? kAGather8 : kAGather16;
+}
 
 void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const void* w, int num_sms) {
   ConvGemmArgs& a = p.args;
@@ -734,9 +871,12 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   p.smem = stages * stage_bytes + fixed + rs * rsb;
   int64_t t = tiles(bn);
   p.grid = int(t < num_sms ? t : num_sms);
+  p.mode = conv_gemm_a_mode(a);
   bool ok = encode_2d(&p.tmB, w, uint64_t(a.Kpad), uint64_t(a.Cout), uint64_t(a.Kpad) * 2, BK, uint32_t(bn));
-  if (!a.gather) ok = ok && encode_2d(&p.tmA, a_rows, uint64_t(lda), uint64_t(a.M), uint64_t(lda) * 2, BK, BM);
+  if (p.mode == kARows) ok = ok && encode_2d(&p.tmA, a_rows, uint64_t(lda), uint64_t(a.M), uint64_t(lda) * 2, BK, BM);
   if (!ok) throw std::runtime_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad layout)");
+  if ((p.mode == kAIm2col64 || p.mode == kAIm2col16) && !encode_im2col(&p.tmA, a, p.mode == kAIm2col64 ? 64 : 16))
+    throw std::runtime_error("cuTensorMapEncodeIm2col failed (driver entry point missing or bad layout)");
   if (out_ok &&
       encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldo) * es, sc, 32, !a.out_bf16)) {
     a.epi = 2;
@@ -750,23 +890,16 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
       p.smem = a.stages * stage_bytes + fixed;
     }
   }
-  const int mode = a.gather ? (a.Cp == 4 ? 2 : 1) : 0;
+  const int mode = p.mode;
   cudaError_t e = bn == 64 ? ensure_attr_mode<64>(mode) : (bn == 128 ? ensure_attr_mode<128>(mode) : ensure_attr_mode<256>(mode));
   if (e != cudaSuccess) throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
 }
 
 cudaError_t conv_gemm_launch(const ConvGemmPlan& p, cudaStream_t s) {
-  const int mode = p.args.gather ? (p.args.Cp == 4 ? 2 : 1) : 0;
-  switch (p.bn * 4 + mode) {
-    case 64 * 4 + 0: return launch_t<64, 0>(p, s);
-    case 64 * 4 + 1: return launch_t<64, 1>(p, s);
-    case 64 * 4 + 2: return launch_t<64, 2>(p, s);
-    case 128 * 4 + 0: return launch_t<128, 0>(p, s);
-    case 128 * 4 + 1: return launch_t<128, 1>(p, s);
-    case 128 * 4 + 2: return launch_t<128, 2>(p, s);
-    case 256 * 4 + 0: return launch_t<256, 0>(p, s);
-    case 256 * 4 + 1: return launch_t<256, 1>(p, s);
-    case 256 * 4 + 2: return launch_t<256, 2>(p, s);
+  switch (p.bn) {
+    case 64: return launch_mode<64>(p, s);
+    case 128: return launch_mode<128>(p, s);
+    case 256: return launch_mode<256>(p, s);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -15,8 +15,8 @@ namespace k {
 //   B = bf16 weights [Cout, Kpad], K-major, K ordered (kh, kw, c) to match NHWC im2col.
 struct ConvGemmArgs {
   // geometry of the A operand
-  int gather;              // 0: A rows via TMA (lda = Kpad elements); 1: im2col gather from NHWC
-  const void* x;           // NHWC bf16 [N, H, W, Cp] (gather)
+  int gather;              // 0: A rows via TMA (lda = Kpad elements); 1: im2col from NHWC
+  const void* x;           // NHWC bf16 [N, H, W, Cp] (im2col)
   int N, H, W, Cp;
   int Ho, Wo, KH, KW, sh, sw, ph, pw, dh, dw;
   int M;                   // rows of D (N*Ho*Wo for convs)
@@ -44,12 +44,22 @@ struct ConvGemmArgs {
   int res_slot_bytes;
 };
 
+// How the kernel fetches its A operand (chosen from the geometry by conv_gemm_a_mode):
+//   0  A is a row matrix: 2D TMA tiles
+//   1  im2col by cp.async in 16-byte units (Cp % 8 == 0)
+//   2  im2col by cp.async in 8-byte units (Cp == 4)
+//   3  im2col by TMA (im2col tensor map, 64 channels x 128 output pixels per load; Cp % 64 == 0)
+//   4  im2col by TMA, 16 channels x 128 pixels per load, four taps per k-tile (Cp == 16)
+enum ConvAMode { kARows = 0, kAGather16 = 1, kAGather8 = 2, kAIm2col64 = 3, kAIm2col16 = 4 };
+int conv_gemm_a_mode(const ConvGemmArgs& a);
+
 struct ConvGemmPlan {
-  CUtensorMap tmA;   // valid when gather == 0
+  CUtensorMap tmA;   // 2D tiles (mode 0) or im2col map (modes 3, 4)
   CUtensorMap tmB;
   CUtensorMap tmOut;   // valid when args.epi == 2
   CUtensorMap tmRes;   // valid when args.res_slots > 0
   int bn;            // 64, 128 or 256
+  int mode;          // ConvAMode
   int grid;
   int smem;
   ConvGemmArgs args;

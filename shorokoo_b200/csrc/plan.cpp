@@ -10,6 +10,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <cstdio>
 #include <map>
 #include <numeric>
@@ -426,10 +427,28 @@ void Plan::plan_conv(const Op& op) {
   std::vector<DevTensor> reads{x};
   if (r.valid()) reads.push_back(r);
   const int sms = num_sms_;
+  k::ConvGemmArgs geo;   // geometry only: how the kernel will fetch A (for the step's label)
+  std::memset(&geo, 0, sizeof(geo));
+  geo.gather = one_by_one ? 0 : 1;
+  geo.N = int(N);
+  geo.H = int(gH);
+  geo.W = int(gW);
+  geo.Cp = Cp;
+  geo.Ho = int(Ho);
+  geo.Wo = int(Wo);
+  geo.KH = int(gKH);
+  geo.KW = int(gKW);
+  geo.sh = int(gsh);
+  geo.sw = int(gsw);
+  geo.ph = int(gph);
+  geo.pw = int(gpw);
+  geo.dh = int(gdh);
+  geo.dw = int(gdw);
+  static const char* kAModeName[] = {"tma", "gather", "gather8", "im2col", "im2col16"};
   const std::string kind = "conv " + std::to_string(KH) + "x" + std::to_string(KW) + "/" +
                            std::to_string(op.strides[0]) + " " + std::to_string(C) + "->" + std::to_string(Cout) +
-                           " M=" + std::to_string(N * Ho * Wo) + (one_by_one ? " tma" : (s2d ? " s2d" : " gather")) +
-                           (op.residual >= 0 ? " +res" : "");
+                           " M=" + std::to_string(N * Ho * Wo) + " " + kAModeName[k::conv_gemm_a_mode(geo)] +
+                           (s2d ? " s2d" : "") + (op.residual >= 0 ? " +res" : "");
   add_step(kind, reads, {y}, [=]() {
     auto p = std::make_shared<k::ConvGemmPlan>();
     k::ConvGemmArgs& a = p->args;

@@ -52,6 +52,38 @@ def test_conv(kw):
     assert_close(got, ref, what=f"conv {kw}")
 
 
+# Activations of at least 128 KiB whose channels come in 64s (or the 16-channel space-to-depth stem
+# image) take the A operand by TMA in im2col mode; the step labels say which path ran.
+@pytest.mark.parametrize("kw,path", [
+    (dict(n=2, c=64, cout=64, k=3, h=32, w=32, bn=True, relu=True), "im2col"),
+    (dict(n=3, c=128, cout=96, k=3, h=17, w=23), "im2col"),                       # M tail across images
+    (dict(n=2, c=64, cout=128, k=3, stride=2, h=33, w=30), "im2col"),             # stride 2, odd H
+    (dict(n=2, c=128, cout=256, k=1, stride=2, pads=[0, 0, 0, 0], h=28, w=28), "im2col"),
+    (dict(n=2, c=64, cout=64, k=3, dil=2, pads=[2, 2, 2, 2], h=24, w=24), "im2col"),
+    (dict(n=2, c=64, cout=48, k=3, stride=2, auto_pad="SAME_UPPER", h=25, w=32), "im2col"),
+    (dict(n=2, c=64, cout=32, k=5, pads=[1, 2, 3, 0], h=20, w=30), "im2col"),     # asymmetric pads
+    (dict(n=2, c=64, cout=64, k=3, h=32, w=32, bn=True, residual=True, relu=True), "im2col"),
+    (dict(n=2, c=192, cout=256, k=3, h=16, w=16, sigmoid=True), "im2col"),        # 3 channel blocks
+    (dict(n=2, c=3, cout=64, k=7, stride=2, pads=[3, 3, 3, 3], h=96, w=96, bn=True, relu=True), "im2col16"),
+    (dict(n=2, c=3, cout=64, k=7, stride=2, pads=[3, 2, 2, 3], h=97, w=95), "im2col16"),
+])
+def test_conv_im2col(kw, path):
+    from shorokoo_b200 import B200InferenceSessionFactory
+    case = conv_case(**kw)
+    f = B200InferenceSessionFactory(num_devices=1)
+    sess = f.CreateSession(case.model)
+    feeds = {name: f.CreateTensor(arr) for name, arr in case.inputs}
+    kinds = [k for k, _ in sess.profile(feeds, iters=1) if k.startswith("conv")]
+    assert len(kinds) == 1 and path in kinds[0].split(), kinds
+    outs = sess.Run(feeds, case.output_names)
+    got = outs[0].numpy()
+    for o in outs:
+        o.Dispose()
+    sess.Dispose()
+    ref = run_oracle(case)[0]
+    assert_close(got, ref, what=f"conv {kw}")
+
+
 def test_maxpool_and_gap():
     case = graphs.resnet(depth=18, batch=2, hw=(40, 40), seed=5, include_top=False)
     got = run_backend(case)[0]
