@@ -197,10 +197,16 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
 
-__device__ __forceinline__ float act_apply(float v, int act) {
-  if (act == 1) return v > 0.f ? v : 0.f;
-  if (act == 2) return 1.f / (1.f + __expf(-v));
-  return v;
+// Activation of 32 accumulator values; the switch is outside the element loop so each case is one
+// straight run. Sigmoid uses the fast reciprocal (a few ulp, far below the bf16 output rounding).
+__device__ __forceinline__ void act_apply32(float (&v)[32], int act) {
+  if (act == 1) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = v[j] > 0.f ? v[j] : 0.f;
+  } else if (act == 2) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __fdividef(1.f, 1.f + __expf(-v[j]));
+  }
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
@@ -268,8 +274,7 @@ __device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint
       }
     }
   }
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = act_apply(v[j], a.act);
+  act_apply32(v, a.act);
 
   int64_t orow = a.group_rows ? (int64_t(m / a.group_rows) * a.group_stride + int64_t(m % a.group_rows) * a.ldo)
                               : int64_t(m) * a.ldo;
@@ -310,14 +315,17 @@ __device__ __forceinline__ uint32_t slab_off(int r, int j) { return uint32_t(r *
 
 constexpr int kSmemLimit = 232448;        // opt-in maximum dynamic shared memory per block
 constexpr uint32_t kOutStage = 16 * 4096;  // two 32-row x 128-byte output slabs per epilogue warp
+constexpr uint32_t kBiasStage = 8 * 512;   // each epilogue warp's bias columns of the current tile
 constexpr int kMaxStages = 8;
 
 // One output slab (32 rows from row0, 128 bytes of columns from n0) of one epilogue warp:
-// accumulator columns [col0, col0 + SC) of the warp's TMEM lanes -> bias -> residual (from the
-// producer-filled residual slot, or direct rows) -> activation -> swizzled smem -> TMA store.
+// accumulator columns [col0, col0 + SC) of the warp's TMEM lanes -> bias (SC floats staged in
+// shared memory at bsl) -> residual (from the producer-filled residual slot, or direct rows) ->
+// activation -> swizzled smem -> TMA store.
 template <bool OBF>
 __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUtensorMap* tmOut, uint32_t tbase,
-                                              int col0, int row0, int n0, uint8_t* sb, const uint8_t* rslab) {
+                                              int col0, int row0, int n0, uint8_t* sb, const uint8_t* rslab,
+                                              const float* bsl) {
   constexpr int SC = OBF ? 64 : 32;
   constexpr int EPC = OBF ? 8 : 4;
   constexpr int CH = 32 / EPC;   // 16-byte chunks per 32 columns
@@ -331,10 +339,10 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
     float v[32];
     uint32_t r[32];
     tmem_ld32(tbase + uint32_t(col0 + h * 32), r);
-    const float4* b4 = reinterpret_cast<const float4*>(a.bias + n0 + h * 32);
+    const float4* b4 = reinterpret_cast<const float4*>(bsl + h * 32);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      float4 bb = __ldg(b4 + j);
+      const float4 bb = b4[j];
       v[4 * j + 0] = __uint_as_float(r[4 * j + 0]) + bb.x;
       v[4 * j + 1] = __uint_as_float(r[4 * j + 1]) + bb.y;
       v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + bb.z;
@@ -383,8 +391,7 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
         }
       }
     }
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = act_apply(v[j], a.act);
+    act_apply32(v, a.act);
 #pragma unroll
     for (int j = 0; j < CH; ++j) {
       uint4 qv;
@@ -433,7 +440,8 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_BYTES;
   uint8_t* sOut = sB + STAGES * B_BYTES;
-  uint8_t* sRes = sOut + kOutStage;
+  float* sBias = reinterpret_cast<float*>(sOut + kOutStage);
+  uint8_t* sRes = sOut + kOutStage + kBiasStage;
   uint64_t* full = reinterpret_cast<uint64_t*>(sRes + RS * RSB);
   uint64_t* empty = full + kMaxStages;
   uint64_t* accf = empty + kMaxStages;
@@ -580,6 +588,21 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
     const int q = warp & 3;          // TMEM lane quarter this warp may access
     const int hsel = (warp - 2) >> 2; // which of the two warps of this quarter
     uint8_t* sb0 = sOut + (warp - 2) * 8192;
+    float* wbias = sBias + (warp - 2) * 128;
+    const int HPS = SC / 32;   // 32-column halves per slab
+    // Bias of this warp's columns of tile t (slabs hsel, hsel+2, ...; at most 4 x 32 floats),
+    // lane-strided into registers one tile ahead of use and staged through wbias. The bias array
+    // is padded to a multiple of 256 columns.
+    auto load_bias = [&](int t, float (&b)[4]) {
+      const int nt = t % tiles_n;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int s2 = hsel + 2 * (i / HPS);
+        b[i] = (t < total && s2 < NS) ? __ldg(a.bias + nt * BN + s2 * SC + (i % HPS) * 32 + lane) : 0.f;
+      }
+    };
+    float bpre[4];
+    load_bias(blockIdx.x, bpre);
     int nslab = 0;   // slabs stored by this warp so far (selects the buffer)
     int it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
@@ -588,6 +611,10 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
       const uint32_t aph = uint32_t(it >> 1) & 1u;
       if (!mbar_wait(&accf[acc], aph, abort_flag, a.err, 8u)) break;
       tc_fence_after();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) wbias[i * 32 + lane] = bpre[i];
+      __syncwarp();
+      load_bias(t + gridDim.x, bpre);   // next tile's bias, consumed one tile from now
       const int row0 = mt * BM + q * 32;
       const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
       const int slot = RS ? it % RS : 0;
@@ -599,8 +626,9 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
             if (n0 >= a.Cout) break;
             const uint8_t* rslab = RS ? sRes + slot * RSB + s2 * 128 * 128 : nullptr;
             uint8_t* sb = sb0 + (nslab++ & 1) * 4096;
-            if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab);
-            else epilogue_slab<false>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab);
+            const float* bsl = wbias + ((s2 - hsel) >> 1) * SC;
+            if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl);
+            else epilogue_slab<false>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl);
           }
         } else {
           const int m = row0 + lane;
@@ -614,7 +642,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         }
       }
       tc_fence_before();
-      __syncwarp();
+      __syncwarp();   // also: every lane is done reading wbias before the next tile rewrites it
       if (lane == 0) {
         if (RS) mbar_arrive(&rese[slot]);
         mbar_arrive(&acce[acc]);
@@ -861,10 +889,10 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   while (bn > 64 && tiles(bn) < num_sms) bn /= 2;
   p.bn = bn;
   const int stage_bytes = BM * BK * 2 + bn * BK * 2;
-  const int fixed = int(kOutStage) + 1024 + 512;
+  const int fixed = int(kOutStage + kBiasStage) + 1024 + 512;
   const int rsb = 128 * bn * es;
   int rs = 0;
-  if (res_ring) rs = (kSmemLimit - fixed - 2 * rsb) / stage_bytes >= 3 ? 2 : 1;
+  if (res_ring) rs = (kSmemLimit - fixed - 2 * rsb) / stage_bytes >= 2 ? 2 : 1;
   int stages = std::min(kMaxStages, (kSmemLimit - fixed - rs * rsb) / stage_bytes);
   if (stages < 2) throw std::runtime_error("conv_gemm: shared-memory plan leaves fewer than 2 stages");
   a.stages = stages;
