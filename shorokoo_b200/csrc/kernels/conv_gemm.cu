@@ -418,9 +418,12 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
 // MODE is a ConvAMode: 0 A rows via TMA; 1 / 2 im2col gather by cp.async in 16 / 8-byte units;
 // 3 / 4 im2col by TMA with 64 / 16 channels per pixel.
 // Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-9 epilogue (two per TMEM lane quarter,
-// splitting the column slabs), 10-13 im2col gather (MODE 1/2).
+// splitting the column slabs), 10-13 im2col gather (MODE 1/2) or 10-11 two more TMA producers.
+// One thread keeps only a few hundred cycles' worth of TMA loads moving at a time, so the k-tiles
+// are dealt round-robin to the producer threads; with at least as many stages as producers no
+// producer can run two phases ahead on a stage's barrier.
 template <int MODE>
-constexpr int kThreads = (MODE == 1 || MODE == 2) ? 448 : 320;
+constexpr int kThreads = (MODE == 1 || MODE == 2) ? 448 : 384;
 
 template <int BN, int MODE>
 __global__ void __launch_bounds__(kThreads<MODE>, 1)
@@ -488,10 +491,13 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
   const int SC = a.out_bf16 ? 64 : 32;   // output columns per 128-byte slab
   const int NS = BN / SC;
 
-  if (warp == 0) {
-    if (lane == 0) {
+  const int NP = GATHER ? 1 : min(3, STAGES);   // TMA producer threads
+  const int pid = warp == 0 ? 0 : warp - 9;     // producer index of warps 0, 10, 11
+  if (warp == 0 || (A_TMA && warp >= 10)) {
+    if (lane == 0 && pid < NP) {
       int stage = 0;
       uint32_t phase = 0;
+      int g = 0;   // k-tile sequence number (all tiles of this CTA); producer g % NP loads it
       const int hw_out = a.Ho * a.Wo;
       const int cblocks = a.Cp / BK;   // 64-channel blocks per filter tap (MODE 3)
       int it = 0;
@@ -507,7 +513,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
           ch = ho * a.sh - a.ph;
           cw = (rem - ho * a.Wo) * a.sw - a.pw;
         }
-        if (RS) {   // the tile's residual, into a ring slot, ahead of its operands
+        if (RS && pid == 0) {   // the tile's residual, into a ring slot, ahead of its operands
           const int slot = it % RS;
           const uint32_t rph = uint32_t(it / RS) & 1u;
           if (!mbar_wait(&rese[slot], rph ^ 1u, abort_flag, a.err, 64u)) goto producer_done;
@@ -518,7 +524,14 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
           for (int s2 = 0; s2 < nsl; ++s2)
             tma_load_2d(sRes + slot * RSB + s2 * 128 * 128, &tmRes, nt * BN + s2 * SC, mt * BM, &resf[slot]);
         }
-        for (int kt = 0; kt < KT; ++kt) {
+        for (int kt = 0; kt < KT; ++kt, ++g) {
+          if (g % NP != pid) {
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) goto producer_done;
           mbar_expect_tx(&full[stage], (A_TMA ? A_BYTES : 0u) + B_BYTES);
           if (MODE == 0) tma_load_2d(sA + stage * A_BYTES, &tmA, kt * BK, mt * BM, &full[stage]);

@@ -1071,9 +1071,13 @@ void Plan::enqueue(cudaStream_t stream, const std::vector<const void*>& host_in,
     ck(cudaMemcpyAsync(buffer_ptr(ib.buf), host_in[size_t(ib.index)], ib.bytes, cudaMemcpyHostToDevice, stream), "H2D");
   }
   enqueue_kernels(stream);
+  enqueue_outputs(stream, host_out);
+}
+
+void Plan::enqueue_outputs(cudaStream_t stream, const std::vector<void*>& host_out) {
   for (size_t j = 0; j < outputs_.size(); ++j) {
     const OutputBinding& ob = outputs_[j];
-    if (ob.host || !host_out[j]) continue;
+    if (ob.host || j >= host_out.size() || !host_out[j]) continue;
     ck(cudaMemcpyAsync(host_out[j], ptr(ob.dev), size_t(numel(ob.shape)) * 4, cudaMemcpyDeviceToHost, stream), "D2H");
   }
 }

@@ -58,6 +58,8 @@ class Plan {
   void enqueue(cudaStream_t stream, const std::vector<const void*>& host_in, const std::vector<void*>& host_out);
   // Runs only the kernel sequence (inputs already resident); used for device-side timing.
   void enqueue_kernels(cudaStream_t stream);
+  // Enqueues only the D2H copies of the device outputs (host_out[j] as in enqueue).
+  void enqueue_outputs(cudaStream_t stream, const std::vector<void*>& host_out);
   // Checks and clears the device error word written by bounded waits.
   void check_device_error();
   // Times every launch of the sequence on its own (`iters` repetitions each, CUDA events on

@@ -349,7 +349,9 @@ std::shared_ptr<Session::PlanSet> Session::get_plans(const std::vector<std::shar
       else if (inputs[i]->shape[0] != batch) batch = -2;
     }
   const int nd = int(devices_.size());
-  bool shard = nd > 1 && batch >= 2 && batch_separable(full);
+  ps->batch = batch;
+  ps->separable = batch >= 2 && batch_separable(full);
+  bool shard = nd > 1 && ps->separable;
   if (nd > 1 && !shard && debug_level() >= 1)
     std::fprintf(stderr, "[shorokoo_b200] graph does not shard on the batch axis; running on one device\n");
   if (!shard) {
@@ -391,6 +393,102 @@ std::shared_ptr<Session::PlanSet> Session::get_plans(const std::vector<std::shar
   return ps;
 }
 
+Session::Pipeline::~Pipeline() {
+  cudaSetDevice(device);
+  for (auto& slot : staging)
+    for (void* p : slot) cudaFree(p);
+  for (int i = 0; i < 2; ++i) {
+    if (h2d_done[i]) cudaEventDestroy(h2d_done[i]);
+    if (consumed[i]) cudaEventDestroy(consumed[i]);
+  }
+  if (copy) cudaStreamDestroy(copy);
+}
+
+void Session::maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs) {
+  if (ps.pipe_checked) return;
+  ps.pipe_checked = true;
+  if (ps.sharded || ps.shards.size() != 1 || !ps.separable || ps.batch < 2) return;
+  // Chunks of at least kPipeMinChunk rows keep the kernels near their full-batch efficiency;
+  // below kPipeMinBytes of device input the copy is too short to be worth hiding.
+  constexpr int64_t kPipeMinChunk = 128;
+  constexpr size_t kPipeMinBytes = size_t(64) << 20;
+  int chunks = int(std::min<int64_t>(4, ps.batch / kPipeMinChunk));
+  if (const char* e = std::getenv("SHOROKOO_B200_PIPELINE")) chunks = e[0] == '0' ? 0 : std::min(chunks, std::atoi(e));
+  size_t dev_bytes = 0;
+  for (const auto& v : inputs)
+    if (numel(v->shape) > kPlanTimeInputMaxElems) dev_bytes += v->nbytes;
+  if (dev_bytes < kPipeMinBytes) return;
+  while (chunks >= 2 && ps.batch % chunks) --chunks;
+  if (chunks < 2) return;
+  auto P = std::make_shared<Pipeline>();
+  P->device = devices_[0];
+  P->chunks = chunks;
+  P->chunk = ps.batch / chunks;
+  try {
+    ck(cudaSetDevice(P->device), "cudaSetDevice");
+    LGraph g = lower(model_, specs_for(inputs, 0, P->chunk, true));
+    P->plan = std::make_shared<Plan>(std::move(g), P->device, sm_counts_[0]);
+    const auto& outs = P->plan->outputs();
+    for (size_t j = 0; j < outs.size(); ++j)
+      if (!outs[j].host && (outs[j].shape.empty() || outs[j].shape[0] != P->chunk || ps.out_shapes[j].empty() ||
+                            ps.out_shapes[j][0] != ps.batch))
+        return;   // an output is not cut along the batch: keep the single full-batch plan
+    for (int slot = 0; slot < 2; ++slot) {
+      for (const auto& b : P->plan->inputs()) {
+        void* d = nullptr;
+        ck(cudaMalloc(&d, std::max<size_t>(b.bytes, 16)), "cudaMalloc (pipeline staging)");
+        P->staging[slot].push_back(d);
+      }
+      ck(cudaEventCreateWithFlags(&P->h2d_done[slot], cudaEventDisableTiming), "event");
+      ck(cudaEventCreateWithFlags(&P->consumed[slot], cudaEventDisableTiming), "event");
+    }
+    ck(cudaStreamCreateWithFlags(&P->copy, cudaStreamNonBlocking), "cudaStreamCreate");
+  } catch (const Error& e) {
+    if (debug_level() >= 1) std::fprintf(stderr, "[shorokoo_b200] no micro-batch pipeline: %s\n", e.what());
+    return;
+  }
+  if (debug_level() >= 1)
+    std::fprintf(stderr, "[shorokoo_b200] run pipeline: %d chunks of %lld rows\n", chunks, (long long)P->chunk);
+  ps.pipe = P;
+}
+
+void Session::run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs,
+                            const std::vector<std::shared_ptr<HostValue>>& outs) {
+  Pipeline& P = *ps.pipe;
+  ck(cudaSetDevice(P.device), "cudaSetDevice");
+  cudaStream_t cs = streams_[0];
+  const auto& binds = P.plan->inputs();
+  std::vector<void*> hout(outs.size(), nullptr);
+  for (int c = 0; c < P.chunks; ++c) {
+    const int slot = c & 1;
+    if (c >= 2) ck(cudaStreamWaitEvent(P.copy, P.consumed[slot], 0), "stream wait");
+    for (size_t bi = 0; bi < binds.size(); ++bi) {
+      const HostValue& v = *inputs[size_t(binds[bi].index)];
+      const size_t row = v.nbytes / size_t(std::max<int64_t>(v.shape[0], 1));
+      const uint8_t* src = static_cast<const uint8_t*>(v.data) + size_t(c) * size_t(P.chunk) * row;
+      ck(cudaMemcpyAsync(P.staging[slot][bi], src, binds[bi].bytes, cudaMemcpyHostToDevice, P.copy), "H2D");
+    }
+    ck(cudaEventRecord(P.h2d_done[slot], P.copy), "event record");
+    ck(cudaStreamWaitEvent(cs, P.h2d_done[slot], 0), "stream wait");
+    for (size_t bi = 0; bi < binds.size(); ++bi)
+      ck(cudaMemcpyAsync(P.plan->buffer_ptr(binds[bi].buf), P.staging[slot][bi], binds[bi].bytes,
+                         cudaMemcpyDeviceToDevice, cs),
+         "D2D");
+    ck(cudaEventRecord(P.consumed[slot], cs), "event record");
+    P.plan->enqueue_kernels(cs);
+    for (size_t j = 0; j < outs.size(); ++j) {
+      hout[j] = nullptr;
+      if (!outs[j] || ps.out_host[j]) continue;
+      const size_t row = outs[j]->nbytes / size_t(std::max<int64_t>(ps.out_shapes[j][0], 1));
+      hout[j] = static_cast<uint8_t*>(outs[j]->data) + size_t(c) * size_t(P.chunk) * row;
+    }
+    P.plan->enqueue_outputs(cs, hout);
+  }
+  ck(cudaStreamSynchronize(cs), "stream synchronize");
+  ck(cudaStreamSynchronize(P.copy), "stream synchronize");
+  P.plan->check_device_error();
+}
+
 std::vector<std::shared_ptr<HostValue>> Session::run(const std::vector<std::shared_ptr<HostValue>>& inputs,
                                                      const std::vector<int>& out_idx) {
   std::lock_guard<std::mutex> lock(mu_);
@@ -408,6 +506,13 @@ std::vector<std::shared_ptr<HostValue>> Session::run(const std::vector<std::shar
     } else {
       outs[j] = HostValue::alloc_tensor(DT_FLOAT, ps->out_shapes[j]);
     }
+  }
+  maybe_build_pipeline(*ps, inputs);
+  if (ps->pipe) {
+    run_pipelined(*ps, inputs, outs);
+    std::vector<std::shared_ptr<HostValue>> res;
+    for (int j : out_idx) res.push_back(outs[size_t(j)]);
+    return res;
   }
   std::vector<std::string> errs(ps->shards.size());
   std::vector<int32_t> codes(ps->shards.size(), 0);

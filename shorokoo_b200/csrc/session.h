@@ -63,12 +63,32 @@ class Session {
     int64_t begin, count;   // batch rows
     std::shared_ptr<Plan> plan;
   };
+  // Single-device micro-batch pipeline for run(): the batch is cut into `chunks` equal chunks
+  // that all run through one plan built for the chunk size. Chunk c is copied host->device on
+  // the copy stream into staging slot c % 2 while chunk c-1 computes; the compute stream then
+  // moves it into the plan's input buffers (device->device), runs the kernels and copies the
+  // chunk's outputs back.
+  struct Pipeline {
+    int device = 0;
+    int chunks = 0;
+    int64_t chunk = 0;
+    std::shared_ptr<Plan> plan;
+    std::vector<void*> staging[2];                // per plan input binding
+    cudaEvent_t h2d_done[2] = {nullptr, nullptr};  // staging slot filled
+    cudaEvent_t consumed[2] = {nullptr, nullptr};  // staging slot read by the compute stream
+    cudaStream_t copy = nullptr;
+    ~Pipeline();
+  };
   struct PlanSet {
     std::vector<Shard> shards;
     std::vector<std::vector<int64_t>> out_shapes;
     std::vector<bool> out_host;
     std::vector<std::shared_ptr<HostTensor>> out_values;
     bool sharded = false;
+    int64_t batch = -1;        // common leading dimension of the device inputs (-1 none, -2 mixed)
+    bool separable = false;    // the graph treats batch rows independently
+    bool pipe_checked = false;
+    std::shared_ptr<Pipeline> pipe;
   };
 
   OnnxModel model_;
@@ -81,6 +101,9 @@ class Session {
   std::map<std::string, std::shared_ptr<PlanSet>> cache_;
 
   std::shared_ptr<PlanSet> get_plans(const std::vector<std::shared_ptr<HostValue>>& inputs);
+  void maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs);
+  void run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs,
+                     const std::vector<std::shared_ptr<HostValue>>& outs);
   std::vector<InputSpec> specs_for(const std::vector<std::shared_ptr<HostValue>>& inputs, int64_t batch_begin,
                                    int64_t batch_count, bool shard) const;
 };

@@ -1,0 +1,68 @@
+"""GPU test of the single-device micro-batch pipeline behind Run: large batch-separable inputs are
+cut into chunks whose host->device copies overlap the previous chunk's kernels. The pipelined Run
+must give exactly the single full-batch plan's result (the chunk plan runs the same per-row
+arithmetic), and the oracle's on a slice of the batch.
+
+Runs in a child process so the backend's debug switch (read once per process) reports the
+pipeline it built."""
+import json
+import os
+import subprocess
+import sys
+import textwrap
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+CHILD = textwrap.dedent("""
+    import json, os, sys
+    import numpy as np
+    sys.path.insert(0, {root!r})
+    sys.path.insert(0, os.path.join({root!r}, "tests"))
+    from helpers import run_backend
+    from shorokoo_b200.emit import graphs
+    case = {case}
+    os.environ["SHOROKOO_B200_PIPELINE"] = "0"
+    ref = run_backend(case)[0]
+    del os.environ["SHOROKOO_B200_PIPELINE"]
+    got = run_backend(case)[0]
+    np.save(os.path.join({out!r}, "ref.npy"), ref)
+    np.save(os.path.join({out!r}, "got.npy"), got)
+""")
+
+
+def _run_child(tmp_path, case_expr):
+    code = CHILD.format(root=ROOT, case=case_expr, out=str(tmp_path))
+    env = dict(os.environ, SHOROKOO_B200_DEBUG="1")
+    env.pop("SHOROKOO_B200_PIPELINE", None)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    return np.load(tmp_path / "ref.npy"), np.load(tmp_path / "got.npy"), r.stderr
+
+
+@pytest.mark.parametrize("case_expr,chunks", [
+    ("graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)", 4),
+    ("graphs.resnet(depth=18, batch=256, hw=(160, 160), seed=9)", 2),
+])
+def test_pipelined_run_matches_full_batch_plan(tmp_path, case_expr, chunks):
+    ref, got, log = _run_child(tmp_path, case_expr)
+    assert f"run pipeline: {chunks} chunks" in log, log[-2000:]
+    assert got.shape == ref.shape
+    assert np.array_equal(got, ref), float(np.abs(got - ref).max())
+
+
+def test_pipelined_run_matches_oracle_on_a_slice(tmp_path):
+    from helpers import assert_close, run_oracle
+    from shorokoo_b200.emit import graphs
+    expr = "graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)"
+    _, got, _ = _run_child(tmp_path, expr)
+    small = graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)
+    rows = np.r_[0:64, 4096 - 32:4096 + 32, 16384 - 64:16384]   # first, a chunk seam, last
+    x = small.inputs[0][1][rows]
+    ref = run_oracle(graphs.ModelCase(small.name, small.model, [(small.inputs[0][0], x)], small.output_names,
+                                      small.macs))[0]
+    assert_close(got[rows], ref, what="pipelined mlp rows vs oracle")
