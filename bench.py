@@ -271,7 +271,7 @@ def main():
                        "precision": "bf16 operands, fp32 accumulate"},
             "e2e": {"value": total / e_max, "unit": "images/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "timing": "host wall clock around Run (synchronous)"},
-            "gpu_launches": int(st["launches"]) * args.steps,
+            "gpu_launches": int(st["launches"]) * args.steps * world,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
                          "frac": achieved / peak_tflops, "traffic": traffic,
                          "kernel": f"conv_gemm_kernel (tcgen05 implicit GEMM), {tc_launches} launches/step, "
