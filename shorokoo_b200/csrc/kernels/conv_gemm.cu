@@ -6,8 +6,7 @@
 //               output tile's residual into a shared-memory ring ahead of its operands
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16 per instr)
 //   warps 2-9   epilogue, two warps per TMEM lane quarter: tcgen05.ld accumulator -> bias /
-//               residual / activation -> swizzled smem slab (two per warp, alternating) -> TMA
-//               bulk store
+//               residual / activation -> swizzled smem slab -> TMA bulk store
 //   warps 10-13 (gather modes only) im2col gather producers: cp.async 16B/8B with zero fill,
 //               written into the 128B-swizzled K-major layout the UMMA smem descriptor expects
 // Spatial convolutions whose activation channels come in 64s (or 16s) instead take the A operand
@@ -113,6 +112,7 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, int c0, int 
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -166,6 +166,21 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Accumulator columns [taddr, taddr + 32) of this warp's TMEM lanes summed over the split-K
+// partial accumulators, which sit `pstride` columns apart.
+__device__ __forceinline__ void tmem_ld_sum(uint32_t taddr, int parts, int pstride, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld32(taddr, r);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+#pragma unroll 1
+  for (int p = 1; p < parts; ++p) {
+    tmem_ld32(taddr + uint32_t(p * pstride), r);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(r[j]);
+  }
 }
 
 // UMMA shared-memory descriptor for a K-major tile with 128-byte swizzle: rows of 128 B, 8-row
@@ -314,7 +329,7 @@ __device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint
 __device__ __forceinline__ uint32_t slab_off(int r, int j) { return uint32_t(r * 128 + ((j ^ (r & 7)) << 4)); }
 
 constexpr int kSmemLimit = 232448;        // opt-in maximum dynamic shared memory per block
-constexpr uint32_t kOutStage = 16 * 4096;  // two 32-row x 128-byte output slabs per epilogue warp
+constexpr uint32_t kOutSlab = 4096;        // one 32-row x 128-byte output slab
 constexpr uint32_t kBiasStage = 8 * 512;   // each epilogue warp's bias columns of the current tile
 constexpr int kMaxStages = 8;
 
@@ -325,28 +340,30 @@ constexpr int kMaxStages = 8;
 template <bool OBF>
 __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUtensorMap* tmOut, uint32_t tbase,
                                               int col0, int row0, int n0, uint8_t* sb, const uint8_t* rslab,
-                                              const float* bsl) {
+                                              const float* bsl, bool dbl, int parts, int pstride) {
   constexpr int SC = OBF ? 64 : 32;
   constexpr int EPC = OBF ? 8 : 4;
   constexpr int CH = 32 / EPC;   // 16-byte chunks per 32 columns
   const int lane = threadIdx.x & 31;
   const int m = row0 + lane;
   const int rrow = (row0 & (BM - 1)) + lane;   // row inside the 128-row residual slab
-  if (lane == 0) bulk_wait_read1();             // the store before the last one (same buffer) has been read
+  if (lane == 0) {   // the last store from this buffer has been read
+    if (dbl) bulk_wait_read1();
+    else bulk_wait_read0();
+  }
   __syncwarp();
 #pragma unroll 1
   for (int h = 0; h < SC / 32; ++h) {
     float v[32];
-    uint32_t r[32];
-    tmem_ld32(tbase + uint32_t(col0 + h * 32), r);
+    tmem_ld_sum(tbase + uint32_t(col0 + h * 32), parts, pstride, v);
     const float4* b4 = reinterpret_cast<const float4*>(bsl + h * 32);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float4 bb = b4[j];
-      v[4 * j + 0] = __uint_as_float(r[4 * j + 0]) + bb.x;
-      v[4 * j + 1] = __uint_as_float(r[4 * j + 1]) + bb.y;
-      v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + bb.z;
-      v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + bb.w;
+      v[4 * j + 0] += bb.x;
+      v[4 * j + 1] += bb.y;
+      v[4 * j + 2] += bb.z;
+      v[4 * j + 3] += bb.w;
     }
     if (a.res) {
       if (rslab) {
@@ -418,12 +435,15 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
 // MODE is a ConvAMode: 0 A rows via TMA; 1 / 2 im2col gather by cp.async in 16 / 8-byte units;
 // 3 / 4 im2col by TMA with 64 / 16 channels per pixel.
 // Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-9 epilogue (two per TMEM lane quarter,
-// splitting the column slabs), 10-13 im2col gather (MODE 1/2) or 10-11 two more TMA producers.
-// One thread keeps only a few hundred cycles' worth of TMA loads moving at a time, so the k-tiles
-// are dealt round-robin to the producer threads; with at least as many stages as producers no
-// producer can run two phases ahead on a stage's barrier.
+// splitting the column slabs), then either 10-13 im2col gather (MODE 1/2) or 10-12 more TMA
+// producers and 13-15 more MMA issuers. One thread keeps only one TMA load per few hundred cycles
+// and one tcgen05.mma per ~164 cycles in flight, whatever the tile shape, so the k-tiles are
+// dealt round-robin to Q producer threads and P MMA-issuing threads (each in its own warp). The stage count is a
+// multiple of both, so each stage's full and empty barriers have exactly one producer and one
+// consumer, each moving through the stage's phases in order: no waiter can face a barrier two
+// phases behind (which a parity wait would mistake for done).
 template <int MODE>
-constexpr int kThreads = (MODE == 1 || MODE == 2) ? 448 : 384;
+constexpr int kThreads = (MODE == 1 || MODE == 2) ? 448 : 512;
 
 template <int BN, int MODE>
 __global__ void __launch_bounds__(kThreads<MODE>, 1)
@@ -432,7 +452,9 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
                      const ConvGemmArgs a) {
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BN * BK * 2;
-  constexpr uint32_t TMEM_COLS = 2 * BN;
+  const int PL = a.mma_lanes;                 // split-K partial accumulators per tile
+  const uint32_t TMEM_COLS = uint32_t(2 * PL * BN);
+  const int PE = PL;                          // at most KT, so every partial gets a k-tile
   constexpr bool GATHER = MODE == 1 || MODE == 2;
   constexpr bool A_TMA = !GATHER;
   const int STAGES = a.stages;
@@ -440,18 +462,22 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
   const uint32_t RSB = uint32_t(a.res_slot_bytes);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int KT = a.Kpad / BK;
+  const bool BRES = A_TMA && a.b_resident;   // weights loaded once: slot kt holds k-tile kt
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_BYTES;
-  uint8_t* sOut = sB + STAGES * B_BYTES;
-  float* sBias = reinterpret_cast<float*>(sOut + kOutStage);
-  uint8_t* sRes = sOut + kOutStage + kBiasStage;
+  uint8_t* sOut = sB + (BRES ? KT : STAGES) * B_BYTES;
+  const int OB = a.out_bufs;
+  float* sBias = reinterpret_cast<float*>(sOut + 8 * OB * kOutSlab);
+  uint8_t* sRes = sOut + 8 * OB * kOutSlab + kBiasStage;
   uint64_t* full = reinterpret_cast<uint64_t*>(sRes + RS * RSB);
   uint64_t* empty = full + kMaxStages;
   uint64_t* accf = empty + kMaxStages;
   uint64_t* acce = accf + 2;
   uint64_t* resf = acce + 2;
   uint64_t* rese = resf + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rese + 2);
+  uint64_t* bfull = rese + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bfull + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -463,11 +489,12 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
       mbar_init(&empty[s], 1u);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&accf[i], 1u);
+      mbar_init(&accf[i], uint32_t(PE));
       mbar_init(&acce[i], 8u);
       mbar_init(&resf[i], 1u);
       mbar_init(&rese[i], 8u);
     }
+    mbar_init(bfull, 1u);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -487,19 +514,22 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
   const int tiles_m = (a.M + BM - 1) / BM;
   const int tiles_n = (a.Cout + BN - 1) / BN;
   const int total = tiles_m * tiles_n;
-  const int KT = a.Kpad / BK;
   const int SC = a.out_bf16 ? 64 : 32;   // output columns per 128-byte slab
   const int NS = BN / SC;
 
-  const int NP = GATHER ? 1 : min(3, STAGES);   // TMA producer threads
-  const int pid = warp == 0 ? 0 : warp - 9;     // producer index of warps 0, 10, 11
-  if (warp == 0 || (A_TMA && warp >= 10)) {
+  const int NP = GATHER ? 1 : a.producers;      // TMA producer threads
+  const int pid = warp == 0 ? 0 : warp - 9;     // producer index of warps 0, 10, 11, 12
+  if (warp == 0 || (A_TMA && warp >= 10 && warp <= 12)) {
     if (lane == 0 && pid < NP) {
       int stage = 0;
       uint32_t phase = 0;
-      int g = 0;   // k-tile sequence number (all tiles of this CTA); producer g % NP loads it
+      int owner = 0;   // producer of the current k-tile (k-tiles are dealt round-robin)
       const int hw_out = a.Ho * a.Wo;
       const int cblocks = a.Cp / BK;   // 64-channel blocks per filter tap (MODE 3)
+      if (BRES && pid == 0) {   // the whole weight matrix, once (a single N tile)
+        mbar_expect_tx(bfull, uint32_t(KT) * B_BYTES);
+        for (int kt = 0; kt < KT; ++kt) tma_load_2d(sB + kt * B_BYTES, &tmB, kt * BK, 0, bfull);
+      }
       int it = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
         const int mt = t / tiles_n, nt = t - (t / tiles_n) * tiles_n;
@@ -524,8 +554,10 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
           for (int s2 = 0; s2 < nsl; ++s2)
             tma_load_2d(sRes + slot * RSB + s2 * 128 * 128, &tmRes, nt * BN + s2 * SC, mt * BM, &resf[slot]);
         }
-        for (int kt = 0; kt < KT; ++kt, ++g) {
-          if (g % NP != pid) {
+        for (int kt = 0; kt < KT; ++kt) {
+          const bool mine = owner == pid;
+          if (++owner == NP) owner = 0;
+          if (!mine) {
             if (++stage == STAGES) {
               stage = 0;
               phase ^= 1u;
@@ -533,7 +565,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
             continue;
           }
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) goto producer_done;
-          mbar_expect_tx(&full[stage], (A_TMA ? A_BYTES : 0u) + B_BYTES);
+          mbar_expect_tx(&full[stage], (A_TMA ? A_BYTES : 0u) + (BRES ? 0u : B_BYTES));
           if (MODE == 0) tma_load_2d(sA + stage * A_BYTES, &tmA, kt * BK, mt * BM, &full[stage]);
           if (MODE == 3) {
             const int tap = kt / cblocks, cb = kt - tap * cblocks;
@@ -550,7 +582,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
                               uint16_t(kh * a.dh), &full[stage]);
             }
           }
-          tma_load_2d(sB + stage * B_BYTES, &tmB, kt * BK, nt * BN, &full[stage]);
+          if (!BRES) tma_load_2d(sB + stage * B_BYTES, &tmB, kt * BK, nt * BN, &full[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -559,20 +591,31 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
       }
     producer_done:;
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
+  } else if (warp == 1 || (A_TMA && warp >= 13)) {
+    // Issuer `mid` (lane 0 of warp 1, 13, 14 or 15) issues the MMAs of the k-tiles with sequence
+    // number g = mid (mod PE) into its own partial accumulator: one thread sustains only about one
+    // tcgen05.mma per ~164 cycles whatever the shape, so N=64/128 tiles need several issuing
+    // threads to keep the tensor pipe busy. Each issuer commits its own k-tiles' stages and
+    // arrives once per tile on the accumulator-full barrier.
+    const int mid = warp == 1 ? 0 : warp - 12;
+    if (lane == 0 && mid < PE) {
       constexpr uint32_t idesc = idesc_bf16(BM, BN);
-      int stage = 0;
-      uint32_t phase = 0;
       int it = 0;
-      for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+      int g0 = 0;   // sequence number of the tile's first k-tile (the producers' numbering)
+      // this issuer's next k-tile g (= mid mod PE) and its stage / phase, advanced by PE steps
+      int g = mid, stage = mid;
+      uint32_t phase = 0;
+      if (BRES && !mbar_wait(bfull, 0u, abort_flag, a.err, 128u)) goto mma_done;
+      for (int t = blockIdx.x; t < total; t += gridDim.x, ++it, g0 += KT) {
         const int acc = it & 1;
         const uint32_t aph = uint32_t(it >> 1) & 1u;
         if (!mbar_wait(&acce[acc], aph ^ 1u, abort_flag, a.err, 2u)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        const uint32_t d_tmem = tmem_base + uint32_t((acc * PL + mid) * BN);
         bool ok = true;
-        for (int kt = 0; kt < KT; ++kt) {
+        // this issuer's k-tiles of the tile: g0 <= g < g0 + KT with g = mid (mod PE)
+        for (bool first = true; g < g0 + KT; first = false) {
+          const int kt = g - g0;
           if (!mbar_wait(&full[stage], phase, abort_flag, a.err, 4u)) {
             ok = false;
             break;
@@ -580,27 +623,30 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
           tc_fence_after();
           if (GATHER) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           const uint64_t ad = sw128_desc(smem_u32(sA + stage * A_BYTES));
-          const uint64_t bd = sw128_desc(smem_u32(sB + stage * B_BYTES));
+          const uint64_t bd = sw128_desc(smem_u32(sB + (BRES ? kt : stage) * B_BYTES));
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t akk = MODE == 4 ? sw32_desc(smem_u32(sA + stage * A_BYTES + kk * (BM * 32)))
                                            : ad + uint64_t(kk * 2);
-            umma_bf16(d_tmem, akk, bd + uint64_t(kk * 2), idesc, (kt | kk) != 0 ? 1u : 0u);
+            umma_bf16(d_tmem, akk, bd + uint64_t(kk * 2), idesc, (!first || kk != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
+          g += PE;
+          stage += PE;
+          if (stage >= STAGES) {   // STAGES is a multiple of PE (or PE == 1)
+            stage -= STAGES;
             phase ^= 1u;
           }
         }
         if (!ok) break;
         umma_commit(&accf[acc]);
       }
+    mma_done:;
     }
   } else if (warp < 10) {
     const int q = warp & 3;          // TMEM lane quarter this warp may access
     const int hsel = (warp - 2) >> 2; // which of the two warps of this quarter
-    uint8_t* sb0 = sOut + (warp - 2) * 8192;
+    uint8_t* sb0 = sOut + (warp - 2) * OB * kOutSlab;
     float* wbias = sBias + (warp - 2) * 128;
     const int HPS = SC / 32;   // 32-column halves per slab
     // Bias of this warp's columns of tile t (slabs hsel, hsel+2, ...; at most 4 x 32 floats),
@@ -629,7 +675,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
       __syncwarp();
       load_bias(t + gridDim.x, bpre);   // next tile's bias, consumed one tile from now
       const int row0 = mt * BM + q * 32;
-      const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
+      const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * PL * BN);
       const int slot = RS ? it % RS : 0;
       if (RS && !mbar_wait(&resf[slot], uint32_t(it / RS) & 1u, abort_flag, a.err, 32u)) break;
       if (row0 < a.M) {   // warp-uniform
@@ -638,17 +684,20 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
             const int n0 = nt * BN + s2 * SC;
             if (n0 >= a.Cout) break;
             const uint8_t* rslab = RS ? sRes + slot * RSB + s2 * 128 * 128 : nullptr;
-            uint8_t* sb = sb0 + (nslab++ & 1) * 4096;
+            uint8_t* sb = sb0 + (OB == 2 ? (nslab++ & 1) * kOutSlab : 0);
             const float* bsl = wbias + ((s2 - hsel) >> 1) * SC;
-            if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl);
-            else epilogue_slab<false>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl);
+            if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl, OB == 2, PE, BN);
+            else epilogue_slab<false>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl, OB == 2, PE, BN);
           }
         } else {
           const int m = row0 + lane;
 #pragma unroll 1
           for (int c = hsel; c < BN / 32; c += 2) {
+            float fv[32];
+            tmem_ld_sum(tbase + uint32_t(c * 32), PE, BN, fv);
             uint32_t r[32];
-            tmem_ld32(tbase + uint32_t(c * 32), r);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(fv[j]);
             const int n0 = nt * BN + c * 32;
             if (n0 < a.Cout && m < a.M) epilogue_chunk(a, r, m, n0);
           }
@@ -901,18 +950,75 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   int bn = a.Cout <= 64 ? 64 : (a.Cout <= 128 || res_ring ? 128 : 256);
   while (bn > 64 && tiles(bn) < num_sms) bn /= 2;
   p.bn = bn;
-  const int stage_bytes = BM * BK * 2 + bn * BK * 2;
-  const int fixed = int(kOutStage + kBiasStage) + 1024 + 512;
+  p.mode = conv_gemm_a_mode(a);
+  // Weights stay resident when the conv has one N tile and all its k-tiles fit in 96 KB: every
+  // pipeline stage then carries only the activation tile (half the TMA loads for N=64 layers).
+  const int KT = a.Kpad / BK;
+  const int64_t w_bytes = int64_t(KT) * bn * BK * 2;
+  bool bres = p.mode != kAGather16 && p.mode != kAGather8 && a.Cout <= bn && w_bytes <= 96 * 1024;
+  if (const char* e = std::getenv("SHOROKOO_B200_BRES"))
+    if (e[0] == '0') bres = false;
+  a.b_resident = bres ? 1 : 0;
+  // MMA-issuing threads: as many split-K partial accumulators as double-buffered TMEM holds, at
+  // most the number of k-tiles.
+  const bool gather = p.mode == kAGather16 || p.mode == kAGather8;
+  // Measured on ResNet-50: two issuers beat one on N=64/128 im2col tiles (3x3 convs, the stem),
+  // four starve on operands, and the row-matrix 1x1 convs lose more to the stage rounding (their
+  // residual ring leaves room for only two or three stages) than they gain.
+  const bool im2col = p.mode == kAIm2col64 || p.mode == kAIm2col16;
+  int pl = im2col && bn <= 128 ? 2 : 1;
+  if (const char* e = std::getenv("SHOROKOO_B200_MMA_LANES")) pl = std::max(1, std::min(pl, std::atoi(e)));
+  while (pl > KT) pl /= 2;
+  a.mma_lanes = pl;
+  const int stage_bytes = BM * BK * 2 + (bres ? 0 : bn * BK * 2);
   const int rsb = 128 * bn * es;
-  int rs = 0;
-  if (res_ring) rs = (kSmemLimit - fixed - 2 * rsb) / stage_bytes >= 2 ? 2 : 1;
-  int stages = std::min(kMaxStages, (kSmemLimit - fixed - rs * rsb) / stage_bytes);
+  // Shared memory: operand stages + output slabs (one per epilogue warp by default) + bias +
+  // residual ring (two slots when two operand stages still fit beside them). A second output
+  // buffer per warp lets a slab's store drain while the next slab is computed, but measured on
+  // ResNet-50 the operand stages it costs are worth more, so it is opt-in (SHOROKOO_B200_OUTBUF=2).
+  auto fixed_for = [&](int ob) { return int(8 * ob * kOutSlab + kBiasStage) + 1024 + 512 + (bres ? int(w_bytes) : 0); };
+  auto ring_for = [&](int ob) {
+    if (!res_ring) return 0;
+    return (kSmemLimit - fixed_for(ob) - 2 * rsb) / stage_bytes >= 2 ? 2 : 1;
+  };
+  auto stages_for = [&](int ob, int rs) { return std::min(kMaxStages, (kSmemLimit - fixed_for(ob) - rs * rsb) / stage_bytes); };
+  int ob = 1;
+  if (const char* e = std::getenv("SHOROKOO_B200_OUTBUF")) ob = std::atoi(e) == 2 ? 2 : 1;
+  int rs = ring_for(ob);
+  const int smax = stages_for(ob, rs);
+  // Producers and stages. With one MMA issuer the stages are consumed in order, and at least as
+  // many stages as producers keeps every barrier wait within one phase. With several issuers the
+  // stage count must be a multiple of both counts (one producer and one consumer per stage).
+  // Prefer three or four producers (TMA issue rate), then the deepest ring.
+  auto lcm = [](int x, int y) { int g = x, h = y; while (h) { int r = g % h; g = h; h = r; } return x / g * y; };
+  int np = 1, stages = (smax / pl) * pl;
+  if (!gather && pl == 1) {
+    np = std::min(3, smax);
+    stages = smax;
+  } else if (!gather) {
+    int best_np = 0, best_s = 0;
+    for (int q : {3, 4, 2, 1}) {
+      const int l = lcm(q, pl);
+      const int s_q = (smax / l) * l;
+      if (s_q < std::max(2, l)) continue;
+      if (best_np == 0 || (std::min(q, 3) > std::min(best_np, 3)) ||
+          (std::min(q, 3) == std::min(best_np, 3) && s_q > best_s)) {
+        best_np = q;
+        best_s = s_q;
+      }
+    }
+    if (best_np == 0) throw std::runtime_error("conv_gemm: no producer/stage split fits shared memory");
+    np = best_np;
+    stages = best_s;
+  }
+  a.producers = np;
   if (stages < 2) throw std::runtime_error("conv_gemm: shared-memory plan leaves fewer than 2 stages");
+  const int fixed = fixed_for(ob);
+  a.out_bufs = ob;
   a.stages = stages;
   p.smem = stages * stage_bytes + fixed + rs * rsb;
   int64_t t = tiles(bn);
   p.grid = int(t < num_sms ? t : num_sms);
-  p.mode = conv_gemm_a_mode(a);
   bool ok = encode_2d(&p.tmB, w, uint64_t(a.Kpad), uint64_t(a.Cout), uint64_t(a.Kpad) * 2, BK, uint32_t(bn));
   if (p.mode == kARows) ok = ok && encode_2d(&p.tmA, a_rows, uint64_t(lda), uint64_t(a.M), uint64_t(lda) * 2, BK, BM);
   if (!ok) throw std::runtime_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad layout)");
@@ -926,8 +1032,10 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
       a.res_slots = rs;
       a.res_slot_bytes = rsb;
     } else {
-      // no ring: restore the operand stages the ring would have used
-      a.stages = std::min(kMaxStages, (kSmemLimit - fixed) / stage_bytes);
+      // no ring: restore the operand stages the ring would have used (a multiple of P and Q
+      // when several MMA threads issue)
+      const int l = a.mma_lanes == 1 ? 1 : lcm(a.producers, a.mma_lanes);
+      a.stages = std::max(a.stages, (std::min(kMaxStages, (kSmemLimit - fixed) / stage_bytes) / l) * l);
       p.smem = a.stages * stage_bytes + fixed;
     }
   }

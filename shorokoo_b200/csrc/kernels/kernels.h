@@ -42,6 +42,13 @@ struct ConvGemmArgs {
   int stages;              // operand pipeline depth
   int res_slots;           // residual ring slots filled by the producer warp (0: direct residual reads)
   int res_slot_bytes;
+  int out_bufs;            // output slab buffers per epilogue warp (1, or 2 to overlap stores)
+  int b_resident;          // 1: every weight k-tile is loaded once and stays in shared memory
+  int mma_lanes;           // MMA-issuing threads P (1, 2 or 4, one per warp): issuer p accumulates
+                           // the k-tiles g = p mod P into its own partial accumulator
+  int producers;           // TMA producer threads Q (1-4): thread q loads k-tiles g = q mod Q
+                           // (stages is a multiple of P and Q, so every stage has one producer
+                           // and one consumer, each in order)
 };
 
 // How the kernel fetches its A operand (chosen from the geometry by conv_gemm_a_mode):

@@ -143,6 +143,53 @@ __global__ void maxpool_nhwc_kernel(const __nv_bfloat16* __restrict__ x, __nv_bf
   }
 }
 
+// K x K window, dilation 1 (the ResNet stem's 3x3/2 pool): all K*K loads of a thread are issued
+// before the max chain, so the window's rows are in flight together.
+template <int K>
+__global__ void maxpool_k_nhwc_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int N,
+                                      int H, int W, int C, int Ho, int Wo, int sh, int sw, int ph, int pw) {
+  const int cg = C / 8;
+  const int64_t total = int64_t(N) * Ho * Wo * cg;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int g = int(i % cg);
+    int64_t pix = i / cg;
+    const int wo = int(pix % Wo);
+    pix /= Wo;
+    const int ho = int(pix % Ho);
+    const int n = int(pix / Ho);
+    const int h0 = ho * sh - ph, w0 = wo * sw - pw;
+    const __nv_bfloat16* base = x + int64_t(n) * H * W * C + g * 8;
+    uint4 q[K * K];
+#pragma unroll
+    for (int a = 0; a < K; ++a)
+#pragma unroll
+      for (int b = 0; b < K; ++b) {
+        const int hi = h0 + a, wi = w0 + b;
+        const bool ok = hi >= 0 && hi < H && wi >= 0 && wi < W;
+        q[a * K + b] = ok ? __ldg(reinterpret_cast<const uint4*>(base + (int64_t(hi) * W + wi) * C))
+                          : make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);   // bf16 -inf
+      }
+    float m[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m[j] = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < K * K; ++k) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q[k]);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = __bfloat1622float2(h[t]);
+        m[2 * t] = fmaxf(m[2 * t], f.x);
+        m[2 * t + 1] = fmaxf(m[2 * t + 1], f.y);
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) oh[t] = __floats2bfloat162_rn(m[2 * t], m[2 * t + 1]);
+    *reinterpret_cast<uint4*>(y + i * 8) = o;
+  }
+}
+
 // Scalar fallback when C is not a multiple of 8.
 __global__ void maxpool_nhwc_scalar_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int N,
                                            int H, int W, int C, int Ho, int Wo, int kh, int kw, int sh, int sw, int ph,
@@ -317,7 +364,10 @@ cudaError_t maxpool_nhwc_bf16(const void* x, void* y, int N, int H, int W, int C
                               int sw, int ph, int pw, int dh, int dw, cudaStream_t s) {
   auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
   auto yb = reinterpret_cast<__nv_bfloat16*>(y);
-  if (C % 8 == 0) {
+  if (C % 8 == 0 && kh == 3 && kw == 3 && dh == 1 && dw == 1) {
+    maxpool_k_nhwc_kernel<3><<<grid_for(int64_t(N) * Ho * Wo * (C / 8)), kThreads, 0, s>>>(xb, yb, N, H, W, C, Ho, Wo,
+                                                                                           sh, sw, ph, pw);
+  } else if (C % 8 == 0) {
     maxpool_nhwc_kernel<<<grid_for(int64_t(N) * Ho * Wo * (C / 8)), kThreads, 0, s>>>(xb, yb, N, H, W, C, Ho, Wo, kh, kw,
                                                                                       sh, sw, ph, pw, dh, dw);
   } else {

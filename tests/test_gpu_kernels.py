@@ -84,6 +84,33 @@ def test_conv_im2col(kw, path):
     assert_close(got, ref, what=f"conv {kw}")
 
 
+@pytest.mark.parametrize("n,c,h,w,k,stride,pads", [
+    (2, 64, 112, 112, 3, 2, [1, 1, 1, 1]),    # the ResNet stem pool (3x3 fast path)
+    (3, 32, 17, 23, 3, 2, [1, 0, 0, 1]),      # odd sizes, asymmetric pads
+    (2, 16, 9, 9, 3, 1, [0, 0, 0, 0]),
+    (2, 24, 10, 12, 2, 2, [0, 0, 0, 0]),      # general window
+    (1, 5, 7, 7, 3, 2, [1, 1, 1, 1]),         # channels not a multiple of 8
+])
+def test_maxpool(n, c, h, w, k, stride, pads):
+    from shorokoo_b200.emit import onnx_writer as W
+    from shorokoo_b200.emit.graphs import Builder, ModelCase
+    rng = np.random.Generator(np.random.PCG64(17))
+    x = rng.standard_normal((n, c, h, w), dtype=np.float32)
+    B = Builder(18)
+    xi = B.graph_input(W.FLOAT, 4, x.shape)
+    y = B.op("MaxPool", [xi], ceil_mode=0, dilations=[1, 1], kernel_shape=[k, k], pads=pads,
+             strides=[stride, stride])
+    ho = (h + pads[0] + pads[2] - k) // stride + 1
+    wo = (w + pads[1] + pads[3] - k) // stride + 1
+    B.shape[y] = (n, c, ho, wo)
+    B.outputs.append(W.ValueInfo(y))
+    case = ModelCase("maxpool", B.model("maxpool"), [(xi, x)], [y], 0)
+    got = run_backend(case)[0]
+    ref = run_oracle(case)[0]
+    assert got.shape == (n, c, ho, wo)
+    assert_close(got, ref, what=f"maxpool {n}x{c}x{h}x{w} k{k}/s{stride} {pads}")
+
+
 def test_maxpool_and_gap():
     case = graphs.resnet(depth=18, batch=2, hw=(40, 40), seed=5, include_top=False)
     got = run_backend(case)[0]

@@ -1,7 +1,9 @@
 """GPU test of the single-device micro-batch pipeline behind Run: large batch-separable inputs are
 cut into chunks whose host->device copies overlap the previous chunk's kernels. The pipelined Run
-must give exactly the single full-batch plan's result (the chunk plan runs the same per-row
-arithmetic), and the oracle's on a slice of the batch.
+must give the single full-batch plan's result up to summation order (the chunk plan may pick
+another tile width and with it another split of K across the MMA-issuing lanes, and a changed
+fp32 partial sum can flip the bf16 rounding of an intermediate activation), and the oracle's on a
+slice of the batch.
 
 Runs in a child process so the backend's debug switch (read once per process) reports the
 pipeline it built."""
@@ -13,6 +15,8 @@ import textwrap
 
 import numpy as np
 import pytest
+
+from helpers import assert_close
 
 pytestmark = pytest.mark.gpu
 
@@ -52,11 +56,11 @@ def test_pipelined_run_matches_full_batch_plan(tmp_path, case_expr, chunks):
     ref, got, log = _run_child(tmp_path, case_expr)
     assert f"run pipeline: {chunks} chunks" in log, log[-2000:]
     assert got.shape == ref.shape
-    assert np.array_equal(got, ref), float(np.abs(got - ref).max())
+    assert_close(got, ref, what="pipelined run vs full-batch plan")
 
 
 def test_pipelined_run_matches_oracle_on_a_slice(tmp_path):
-    from helpers import assert_close, run_oracle
+    from helpers import run_oracle
     from shorokoo_b200.emit import graphs
     expr = "graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)"
     _, got, _ = _run_child(tmp_path, expr)
