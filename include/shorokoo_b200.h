@@ -59,10 +59,18 @@ SB_API const char* sb_last_error(void);
  * Devices: SHOROKOO_B200_DEVICES (default: all visible CUDA devices); batches shard across them. */
 SB_API int32_t sb_session_create(const uint8_t* model, size_t model_len, int32_t graph_optimization,
                           int32_t log_severity, sb_session** out);
-/* Same, with an explicit device range [first_device, first_device + num_devices). */
+/* Same, with an explicit device range [first_device, first_device + num_devices) and the
+ * tensor-core precision: SB_PRECISION_BF16 (bf16 operands, fp32 accumulation; the throughput mode,
+ * normwise error <= 1e-2), SB_PRECISION_TF32 (fp32 operands read as TF32; the accuracy mode,
+ * <= 2e-3), or SB_PRECISION_DEFAULT (SHOROKOO_B200_PRECISION=bf16|tf32, else bf16).
+ * sb_session_create uses SB_PRECISION_DEFAULT. No counterpart in the reference, whose ORT CUDA
+ * provider computes in fp32 (OrtSessionFactory.cs:23-42). */
+#define SB_PRECISION_DEFAULT (-1)
+#define SB_PRECISION_BF16 0
+#define SB_PRECISION_TF32 1
 SB_API int32_t sb_session_create_ex(const uint8_t* model, size_t model_len, int32_t graph_optimization,
                              int32_t log_severity, int32_t num_devices, int32_t first_device,
-                             sb_session** out);
+                             int32_t precision, sb_session** out);
 /* IShorokooInferenceSession.Dispose (IDisposable). */
 SB_API void sb_session_destroy(sb_session* session);
 

@@ -12,7 +12,9 @@ inference hot path, interpreting the same ONNX bytes the B200 library receives.
 * ``precision="fp64"`` promotes every float tensor to float64 (ground truth for error analysis);
 * ``precision="bf16-operands"`` computes in float32 but rounds both operands of every Conv / MatMul
   to bfloat16 (round-to-nearest-even), the arithmetic of a bf16 tensor-core path with fp32
-  accumulation. It separates a kernel bug from the precision floor of bf16 operands.
+  accumulation. It separates a kernel bug from the precision floor of bf16 operands;
+* ``precision="tf32-operands"`` does the same with TF32 operands (fp32 rounded to 10 explicit
+  mantissa bits, nearest even): the arithmetic of the TF32 accuracy mode.
 
 Conv / MatMul use torch CPU kernels (torch.nn.functional.conv2d, torch.matmul) for speed; everything
 else is numpy.  ``oracle/ref_small.c`` re-derives Conv / MaxPool / GEMM with plain loops so the
@@ -47,7 +49,7 @@ def _i(a) -> List[int]:
 
 class Interpreter:
     def __init__(self, model_bytes: bytes, precision: str = "fp32", threads: Optional[int] = None):
-        if precision not in ("fp32", "fp64", "bf16-operands"):
+        if precision not in ("fp32", "fp64", "bf16-operands", "tf32-operands"):
             raise ValueError(precision)
         self.model: ModelP = decode_model(model_bytes)
         self.precision = precision
@@ -379,10 +381,15 @@ class Interpreter:
         return torch.from_numpy(np.ascontiguousarray(a))
 
     def _op_round(self, a):
-        """Operand rounding of the bf16 tensor-core path (identity in fp32 / fp64 modes)."""
-        if self.precision != "bf16-operands":
-            return a
-        return torch.from_numpy(np.ascontiguousarray(a, np.float32)).bfloat16().float().numpy()
+        """Operand rounding of the bf16 / TF32 tensor-core paths (identity in fp32 / fp64 modes)."""
+        if self.precision == "bf16-operands":
+            return torch.from_numpy(np.ascontiguousarray(a, np.float32)).bfloat16().float().numpy()
+        if self.precision == "tf32-operands":
+            u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+            finite = (u & np.uint32(0x7F800000)) != np.uint32(0x7F800000)
+            r = (u + np.uint32(0xFFF) + ((u >> np.uint32(13)) & np.uint32(1))) & np.uint32(0xFFFFE000)
+            return np.where(finite, r, u).view(np.float32)
+        return a
 
     def op_MatMul(self, n, x, env):
         a, b = self._op_round(x[0]), self._op_round(x[1])

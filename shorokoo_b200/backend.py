@@ -274,11 +274,18 @@ class B200InferenceSession:
 class B200InferenceSessionFactory:
     """IShorokooInferenceSessionFactory for the Shorokoo.LinuxGPU slot (OrtSessionFactory.cs:14-106).
 
-    ``num_devices`` = 0 uses SHOROKOO_B200_DEVICES or every visible GPU; batches shard across them."""
+    ``num_devices`` = 0 uses SHOROKOO_B200_DEVICES or every visible GPU; batches shard across them.
+    ``precision``: "bf16" (throughput mode), "tf32" (accuracy mode: fp32 operands read as TF32) or
+    None for SHOROKOO_B200_PRECISION (default bf16)."""
 
-    def __init__(self, num_devices: int = 0, first_device: int = 0):
+    _PRECISIONS = {None: -1, "bf16": 0, "tf32": 1}
+
+    def __init__(self, num_devices: int = 0, first_device: int = 0, precision: Optional[str] = None):
+        if precision not in self._PRECISIONS:
+            raise ValueError(f"precision must be 'bf16', 'tf32' or None, got {precision!r}")
         self.num_devices = num_devices
         self.first_device = first_device
+        self.precision = precision
 
     def CreateSession(self, modelBytes: bytes,
                       graphOptimization: ShorokooGraphOptimization = ShorokooGraphOptimization.EnableAll,
@@ -286,7 +293,8 @@ class B200InferenceSessionFactory:
         out = C.c_void_p()
         b = bytes(modelBytes)
         _check(_native.lib().sb_session_create_ex(b, len(b), int(graphOptimization), int(logSeverity),
-                                                  self.num_devices, self.first_device, C.byref(out)))
+                                                  self.num_devices, self.first_device,
+                                                  self._PRECISIONS[self.precision], C.byref(out)))
         return B200InferenceSession(out.value)
 
     def CreateTensor(self, data, shape: Optional[Sequence[int]] = None) -> B200TensorValue:

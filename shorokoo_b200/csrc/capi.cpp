@@ -85,13 +85,16 @@ int32_t sb_version(void) { return 100; }
 const char* sb_last_error(void) { return g_last_error.c_str(); }
 
 int32_t sb_session_create_ex(const uint8_t* model, size_t len, int32_t, int32_t, int32_t num_devices,
-                             int32_t first_device, sb_session** out) {
+                             int32_t first_device, int32_t precision, sb_session** out) {
   return guarded([&] {
     SB_CHECK(out != nullptr, sb::SB_INVALID_ARGUMENT, "out is null");
     *out = nullptr;
+    SB_CHECK(precision >= SB_PRECISION_DEFAULT && precision <= SB_PRECISION_TF32, sb::SB_INVALID_ARGUMENT,
+             "precision must be SB_PRECISION_DEFAULT, _BF16 or _TF32");
     sb::SessionOptions o;
     o.num_devices = num_devices;
     o.first_device = first_device;
+    o.precision = precision;
     auto s = std::make_unique<sb_session>();
     s->s = std::make_unique<sb::Session>(model, len, o);
     *out = s.release();
@@ -100,7 +103,7 @@ int32_t sb_session_create_ex(const uint8_t* model, size_t len, int32_t, int32_t,
 }
 
 int32_t sb_session_create(const uint8_t* model, size_t len, int32_t opt, int32_t sev, sb_session** out) {
-  return sb_session_create_ex(model, len, opt, sev, 0, 0, out);
+  return sb_session_create_ex(model, len, opt, sev, 0, 0, SB_PRECISION_DEFAULT, out);
 }
 
 void sb_session_destroy(sb_session* s) { delete s; }

@@ -12,7 +12,8 @@
 // Spatial convolutions whose activation channels come in 64s (or 16s) instead take the A operand
 // with TMA in im2col mode: one load per k-tile brings 128 consecutive output pixels x 64
 // channels of one filter tap, zero-filled outside the image, straight into the swizzled layout.
-// Operand tiles are BM=128 x BK=64 bf16 (one 128-byte swizzle atom per row); the fp32 accumulator
+// Operand tiles are BM=128 rows x 128 bytes (64 bf16, or 32 fp32 in the TF32 accuracy mode: one
+// 128-byte swizzle atom per row); the fp32 accumulator
 // is double-buffered in TMEM so the epilogue of tile i overlaps the main loop of tile i+1.
 // Every mbarrier wait is bounded (global timer); a timeout sets a device error word and the CTA
 // drains and frees its TMEM instead of hanging.
@@ -33,7 +34,7 @@ namespace k {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BK = 64;
+constexpr int BK = 64;   // bf16 elements per 128-byte k-tile row (32 for TF32 operands)
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -150,6 +151,16 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint6
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D(tmem) (+)= A(smem) * B(smem)^T, kind::tf32 (fp32 operands read as TF32, f32 accumulate, K=8).
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -207,9 +218,18 @@ __device__ __forceinline__ uint64_t sw32_desc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor: D f32, A/B bf16, both K-major, N>>3 at bit 17, M>>4 at bit 24.
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+// Instruction descriptor: D f32, A/B format (1 = bf16 for kind::f16, 2 = TF32 for kind::tf32) at
+// bits 7 and 10, both K-major, N>>3 at bit 17, M>>4 at bit 24.
+__host__ __device__ constexpr uint32_t idesc_mma(int M, int N, bool tf32) {
+  return (1u << 4) | ((tf32 ? 2u : 1u) << 7) | ((tf32 ? 2u : 1u) << 10) | (uint32_t(N >> 3) << 17) |
+         (uint32_t(M >> 4) << 24);
+}
+
+// fp32 rounded to the TF32 grid (nearest, ties away): activations that feed TF32 MMAs.
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
 }
 
 // Activation of 32 accumulator values; the switch is outside the element loop so each case is one
@@ -312,6 +332,10 @@ __device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint
         if (j < ncols) op[j] = __float2bfloat16_rn(v[j]);
     }
   } else {
+    if (a.round_tf32) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = tf32_rna(v[j]);
+    }
     float* op = reinterpret_cast<float*>(a.out) + orow + n0;
     if (ncols == 32 && (reinterpret_cast<uintptr_t>(op) & 15) == 0) {
       float4* o4 = reinterpret_cast<float4*>(op);
@@ -409,6 +433,10 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
       }
     }
     act_apply32(v, a.act);
+    if (!OBF && a.round_tf32) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = tf32_rna(v[j]);
+    }
 #pragma unroll
     for (int j = 0; j < CH; ++j) {
       uint4 qv;
@@ -445,13 +473,15 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
 template <int MODE>
 constexpr int kThreads = (MODE == 1 || MODE == 2) ? 448 : 512;
 
-template <int BN, int MODE>
+template <int BN, int MODE, bool TF32>
 __global__ void __launch_bounds__(kThreads<MODE>, 1)
     conv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
                      const ConvGemmArgs a) {
-  constexpr uint32_t A_BYTES = BM * BK * 2;
-  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr int EB = TF32 ? 4 : 2;        // operand element bytes
+  constexpr int BKE = 128 / EB;           // operand elements per 128-byte k-tile row
+  constexpr uint32_t A_BYTES = BM * 128;
+  constexpr uint32_t B_BYTES = BN * 128;
   const int PL = a.mma_lanes;                 // split-K partial accumulators per tile
   const uint32_t TMEM_COLS = uint32_t(2 * PL * BN);
   const int PE = PL;                          // at most KT, so every partial gets a k-tile
@@ -462,7 +492,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
   const uint32_t RSB = uint32_t(a.res_slot_bytes);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int KT = a.Kpad / BK;
+  const int KT = a.Kpad / BKE;
   const bool BRES = A_TMA && a.b_resident;   // weights loaded once: slot kt holds k-tile kt
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_BYTES;
@@ -525,10 +555,10 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
       uint32_t phase = 0;
       int owner = 0;   // producer of the current k-tile (k-tiles are dealt round-robin)
       const int hw_out = a.Ho * a.Wo;
-      const int cblocks = a.Cp / BK;   // 64-channel blocks per filter tap (MODE 3)
+      const int cblocks = a.Cp / BKE;   // 128-byte channel blocks per filter tap (MODE 3)
       if (BRES && pid == 0) {   // the whole weight matrix, once (a single N tile)
         mbar_expect_tx(bfull, uint32_t(KT) * B_BYTES);
-        for (int kt = 0; kt < KT; ++kt) tma_load_2d(sB + kt * B_BYTES, &tmB, kt * BK, 0, bfull);
+        for (int kt = 0; kt < KT; ++kt) tma_load_2d(sB + kt * B_BYTES, &tmB, kt * BKE, 0, bfull);
       }
       int it = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
@@ -566,11 +596,11 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
           }
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) goto producer_done;
           mbar_expect_tx(&full[stage], (A_TMA ? A_BYTES : 0u) + (BRES ? 0u : B_BYTES));
-          if (MODE == 0) tma_load_2d(sA + stage * A_BYTES, &tmA, kt * BK, mt * BM, &full[stage]);
+          if (MODE == 0) tma_load_2d(sA + stage * A_BYTES, &tmA, kt * BKE, mt * BM, &full[stage]);
           if (MODE == 3) {
             const int tap = kt / cblocks, cb = kt - tap * cblocks;
             const int kh = tap / a.KW, kw = tap - (tap / a.KW) * a.KW;
-            tma_load_im2col(sA + stage * A_BYTES, &tmA, cb * BK, cw, ch, img, uint16_t(kw * a.dw),
+            tma_load_im2col(sA + stage * A_BYTES, &tmA, cb * BKE, cw, ch, img, uint16_t(kw * a.dw),
                             uint16_t(kh * a.dh), &full[stage]);
           }
           if (MODE == 4) {   // four 16-channel taps, one 4 KB sub-tile each
@@ -582,7 +612,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
                               uint16_t(kh * a.dh), &full[stage]);
             }
           }
-          if (!BRES) tma_load_2d(sB + stage * B_BYTES, &tmB, kt * BK, nt * BN, &full[stage]);
+          if (!BRES) tma_load_2d(sB + stage * B_BYTES, &tmB, kt * BKE, nt * BN, &full[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -599,7 +629,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
     // arrives once per tile on the accumulator-full barrier.
     const int mid = warp == 1 ? 0 : warp - 12;
     if (lane == 0 && mid < PE) {
-      constexpr uint32_t idesc = idesc_bf16(BM, BN);
+      constexpr uint32_t idesc = idesc_mma(BM, BN, TF32);
       int it = 0;
       int g0 = 0;   // sequence number of the tile's first k-tile (the producers' numbering)
       // this issuer's next k-tile g (= mid mod PE) and its stage / phase, advanced by PE steps
@@ -625,10 +655,11 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
           const uint64_t ad = sw128_desc(smem_u32(sA + stage * A_BYTES));
           const uint64_t bd = sw128_desc(smem_u32(sB + (BRES ? kt : stage) * B_BYTES));
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
+          for (int kk = 0; kk < 4; ++kk) {   // four 32-byte K slices per 128-byte row
             const uint64_t akk = MODE == 4 ? sw32_desc(smem_u32(sA + stage * A_BYTES + kk * (BM * 32)))
                                            : ad + uint64_t(kk * 2);
-            umma_bf16(d_tmem, akk, bd + uint64_t(kk * 2), idesc, (!first || kk != 0) ? 1u : 0u);
+            if (TF32) umma_tf32(d_tmem, akk, bd + uint64_t(kk * 2), idesc, (!first || kk != 0) ? 1u : 0u);
+            else umma_bf16(d_tmem, akk, bd + uint64_t(kk * 2), idesc, (!first || kk != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           g += PE;
@@ -719,7 +750,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
     constexpr int PASSES = BM / ROWS_PER_PASS;       // 8 or 16
     const int sub = gt % TPR;
     const int rbase = gt / TPR;
-    const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(a.x);
+    const uint8_t* xb = reinterpret_cast<const uint8_t*>(a.x);
     const int hw_out = a.Ho * a.Wo;
     const int ktaps = a.KH * a.KW;
     const int kreal = ktaps * a.Cp;
@@ -748,7 +779,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 16u)) goto gather_done;
         const uint32_t sbase = smem_u32(sA + stage * A_BYTES);
         if (MODE == 1) {
-          const int kidx = kt * BK + sub * 8;
+          const int kidx = kt * BKE + sub * (16 / EB);
           const int tap = kidx / a.Cp;
           const int c = kidx - tap * a.Cp;
           const int kh = tap / a.KW, kw = tap - (tap / a.KW) * a.KW;
@@ -759,12 +790,12 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
             const int r = rbase + i * ROWS_PER_PASS;
             const int hi = hb[i] + dh, wi = wb[i] + dw;
             const bool ok = kvalid && hi >= 0 && hi < a.H && wi >= 0 && wi < a.W;
-            const __nv_bfloat16* src = ok ? x + base[i] + (int64_t(hi) * a.W + wi) * a.Cp + c : x;
+            const uint8_t* src = ok ? xb + (base[i] + (int64_t(hi) * a.W + wi) * a.Cp + c) * EB : xb;
             const uint32_t dst = sbase + uint32_t(r * 128 + ((sub ^ (r & 7)) << 4));
             cp_async_16(dst, src, ok ? 16u : 0u);
           }
         } else {
-          const int tap = kt * (BK / 4) + sub;   // Cp == 4: one tap per 8-byte unit
+          const int tap = kt * (BKE / 4) + sub;   // bf16, Cp == 4: one tap per 8-byte unit
           const int kh = tap / a.KW, kw = tap - (tap / a.KW) * a.KW;
           const bool kvalid = tap < ktaps;
           const int dh = kh * a.dh, dw = kw * a.dw;
@@ -773,7 +804,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
             const int r = rbase + i * ROWS_PER_PASS;
             const int hi = hb[i] + dh, wi = wb[i] + dw;
             const bool ok = kvalid && hi >= 0 && hi < a.H && wi >= 0 && wi < a.W;
-            const __nv_bfloat16* src = ok ? x + base[i] + (int64_t(hi) * a.W + wi) * 4 : x;
+            const uint8_t* src = ok ? xb + (base[i] + (int64_t(hi) * a.W + wi) * 4) * EB : xb;
             const uint32_t dst = sbase + uint32_t(r * 128 + (((sub >> 1) ^ (r & 7)) << 4) + ((sub & 1) << 3));
             cp_async_8(dst, src, ok ? 8u : 0u);
           }
@@ -846,21 +877,23 @@ inline int im2col_upper(int W, int Wo, int s, int pad) { return (Wo - 1) * s - p
 bool encode_im2col(CUtensorMap* tm, const ConvGemmArgs& a, int cpp) {
   auto fn = get_encode_im2col_fn();
   if (!fn) return false;
+  const cuuint64_t eb = a.tf32 ? 4 : 2;
   cuuint64_t dims[4] = {cuuint64_t(a.Cp), cuuint64_t(a.W), cuuint64_t(a.H), cuuint64_t(a.N)};
-  cuuint64_t strides[3] = {cuuint64_t(a.Cp) * 2, cuuint64_t(a.W) * a.Cp * 2, cuuint64_t(a.H) * a.W * a.Cp * 2};
+  cuuint64_t strides[3] = {cuuint64_t(a.Cp) * eb, cuuint64_t(a.W) * a.Cp * eb, cuuint64_t(a.H) * a.W * a.Cp * eb};
   int lower[2] = {-a.pw, -a.ph};
   int upper[2] = {im2col_upper(a.W, a.Wo, a.sw, a.pw), im2col_upper(a.H, a.Ho, a.sh, a.ph)};
   cuuint32_t estr[4] = {1, cuuint32_t(a.sw), cuuint32_t(a.sh), 1};
-  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(a.x), dims, strides, lower, upper,
-                  cuuint32_t(cpp), cuuint32_t(BM), estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  cpp == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B,
+  CUresult r = fn(tm, a.tf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                  const_cast<void*>(a.x), dims, strides, lower, upper, cuuint32_t(cpp), cuuint32_t(BM), estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  cpp * eb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
 // The dynamic shared-memory opt-in is a per-device function attribute; it is set while preparing
 // a plan (never during stream capture).
-template <int BN, int MODE>
+template <int BN, int MODE, bool TF32>
 cudaError_t ensure_attr() {
   static std::atomic<uint64_t> done_mask{0};
   int dev = 0;
@@ -868,37 +901,54 @@ cudaError_t ensure_attr() {
   const uint64_t bit = uint64_t(1) << (dev & 63);
   if (done_mask.load() & bit) return cudaSuccess;
   cudaError_t e =
-      cudaFuncSetAttribute(conv_gemm_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+      cudaFuncSetAttribute(conv_gemm_kernel<BN, MODE, TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
   if (e == cudaSuccess) done_mask.fetch_or(bit);
   return e;
 }
 
-template <int BN, int MODE>
+template <int BN, int MODE, bool TF32>
 cudaError_t launch_t(const ConvGemmPlan& p, cudaStream_t s) {
-  conv_gemm_kernel<BN, MODE><<<p.grid, kThreads<MODE>, p.smem, s>>>(p.tmA, p.tmB, p.tmOut, p.tmRes, p.args);
+  conv_gemm_kernel<BN, MODE, TF32><<<p.grid, kThreads<MODE>, p.smem, s>>>(p.tmA, p.tmB, p.tmOut, p.tmRes, p.args);
   return cudaGetLastError();
 }
 
+// TF32 operands use the row-matrix, 16-byte gather and 128-byte im2col modes only.
 template <int BN>
-cudaError_t ensure_attr_mode(int mode) {
+cudaError_t ensure_attr_mode(int mode, bool tf32) {
+  if (tf32) {
+    switch (mode) {
+      case 0: return ensure_attr<BN, 0, true>();
+      case 1: return ensure_attr<BN, 1, true>();
+      case 3: return ensure_attr<BN, 3, true>();
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (mode) {
-    case 0: return ensure_attr<BN, 0>();
-    case 1: return ensure_attr<BN, 1>();
-    case 2: return ensure_attr<BN, 2>();
-    case 3: return ensure_attr<BN, 3>();
-    case 4: return ensure_attr<BN, 4>();
+    case 0: return ensure_attr<BN, 0, false>();
+    case 1: return ensure_attr<BN, 1, false>();
+    case 2: return ensure_attr<BN, 2, false>();
+    case 3: return ensure_attr<BN, 3, false>();
+    case 4: return ensure_attr<BN, 4, false>();
     default: return cudaErrorInvalidValue;
   }
 }
 
 template <int BN>
 cudaError_t launch_mode(const ConvGemmPlan& p, cudaStream_t s) {
+  if (p.args.tf32) {
+    switch (p.mode) {
+      case 0: return launch_t<BN, 0, true>(p, s);
+      case 1: return launch_t<BN, 1, true>(p, s);
+      case 3: return launch_t<BN, 3, true>(p, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (p.mode) {
-    case 0: return launch_t<BN, 0>(p, s);
-    case 1: return launch_t<BN, 1>(p, s);
-    case 2: return launch_t<BN, 2>(p, s);
-    case 3: return launch_t<BN, 3>(p, s);
-    case 4: return launch_t<BN, 4>(p, s);
+    case 0: return launch_t<BN, 0, false>(p, s);
+    case 1: return launch_t<BN, 1, false>(p, s);
+    case 2: return launch_t<BN, 2, false>(p, s);
+    case 3: return launch_t<BN, 3, false>(p, s);
+    case 4: return launch_t<BN, 4, false>(p, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -916,12 +966,13 @@ int conv_gemm_a_mode(const ConvGemmArgs& a) {
   const int up_w = im2col_upper(a.W, a.Wo, a.sw, a.pw), up_h = im2col_upper(a.H, a.Ho, a.sh, a.ph);
   const bool box_ok = a.pw <= 128 && a.ph <= 128 && up_w >= -128 && up_w <= 127 && up_h >= -128 && up_h <= 127 &&
                       (a.KW - 1) * a.dw <= 255 && (a.KH - 1) * a.dh <= 255 && a.sw <= 8 && a.sh <= 8;
-  const bool big = int64_t(a.N) * a.H * a.W * a.Cp * 2 >= (int64_t(1) << 17);
+  const int eb = a.tf32 ? 4 : 2;
+  const bool big = int64_t(a.N) * a.H * a.W * a.Cp * eb >= (int64_t(1) << 17);
   if (im2col_on && box_ok && big) {
-    if (a.Cp % 64 == 0) return kAIm2col64;
-    if (a.Cp == 16 && (a.KH * a.KW) % 4 == 0) return kAIm2col16;
+    if ((a.Cp * eb) % 128 == 0) return kAIm2col64;   // 128-byte channel blocks
+    if (!a.tf32 && a.Cp == 16 && (a.KH * a.KW) % 4 == 0) return kAIm2col16;
   }
-  return a.Cp == 4 ? kAGather8 : kAGather16;
+  return !a.tf32 && a.Cp == 4 ? kAGather8 : kAGather16;
 }
 
 void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const void* w, int num_sms) {
@@ -953,8 +1004,10 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   p.mode = conv_gemm_a_mode(a);
   // Weights stay resident when the conv has one N tile and all its k-tiles fit in 96 KB: every
   // pipeline stage then carries only the activation tile (half the TMA loads for N=64 layers).
-  const int KT = a.Kpad / BK;
-  const int64_t w_bytes = int64_t(KT) * bn * BK * 2;
+  const int bke = a.tf32 ? BK / 2 : BK;   // operand elements per 128-byte k-tile row
+  if (a.Kpad % bke) throw std::runtime_error("conv_gemm: reduction length not padded to a whole k-tile");
+  const int KT = a.Kpad / bke;
+  const int64_t w_bytes = int64_t(KT) * bn * 128;
   bool bres = p.mode != kAGather16 && p.mode != kAGather8 && a.Cout <= bn && w_bytes <= 96 * 1024;
   if (const char* e = std::getenv("SHOROKOO_B200_BRES"))
     if (e[0] == '0') bres = false;
@@ -970,7 +1023,7 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   if (const char* e = std::getenv("SHOROKOO_B200_MMA_LANES")) pl = std::max(1, std::min(pl, std::atoi(e)));
   while (pl > KT) pl /= 2;
   a.mma_lanes = pl;
-  const int stage_bytes = BM * BK * 2 + (bres ? 0 : bn * BK * 2);
+  const int stage_bytes = BM * 128 + (bres ? 0 : bn * 128);
   const int rsb = 128 * bn * es;
   // Shared memory: operand stages + output slabs (one per epilogue warp by default) + bias +
   // residual ring (two slots when two operand stages still fit beside them). A second output
@@ -1019,10 +1072,13 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   p.smem = stages * stage_bytes + fixed + rs * rsb;
   int64_t t = tiles(bn);
   p.grid = int(t < num_sms ? t : num_sms);
-  bool ok = encode_2d(&p.tmB, w, uint64_t(a.Kpad), uint64_t(a.Cout), uint64_t(a.Kpad) * 2, BK, uint32_t(bn));
-  if (p.mode == kARows) ok = ok && encode_2d(&p.tmA, a_rows, uint64_t(lda), uint64_t(a.M), uint64_t(lda) * 2, BK, BM);
+  const int eb = a.tf32 ? 4 : 2;
+  bool ok = encode_2d(&p.tmB, w, uint64_t(a.Kpad), uint64_t(a.Cout), uint64_t(a.Kpad) * eb, uint32_t(bke), uint32_t(bn),
+                      a.tf32 != 0);
+  if (p.mode == kARows)
+    ok = ok && encode_2d(&p.tmA, a_rows, uint64_t(lda), uint64_t(a.M), uint64_t(lda) * eb, uint32_t(bke), BM, a.tf32 != 0);
   if (!ok) throw std::runtime_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad layout)");
-  if ((p.mode == kAIm2col64 || p.mode == kAIm2col16) && !encode_im2col(&p.tmA, a, p.mode == kAIm2col64 ? 64 : 16))
+  if ((p.mode == kAIm2col64 || p.mode == kAIm2col16) && !encode_im2col(&p.tmA, a, p.mode == kAIm2col64 ? bke : 16))
     throw std::runtime_error("cuTensorMapEncodeIm2col failed (driver entry point missing or bad layout)");
   if (out_ok &&
       encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldo) * es, sc, 32, !a.out_bf16)) {
@@ -1040,7 +1096,9 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
     }
   }
   const int mode = p.mode;
-  cudaError_t e = bn == 64 ? ensure_attr_mode<64>(mode) : (bn == 128 ? ensure_attr_mode<128>(mode) : ensure_attr_mode<256>(mode));
+  const bool tf = a.tf32 != 0;
+  cudaError_t e = bn == 64 ? ensure_attr_mode<64>(mode, tf)
+                           : (bn == 128 ? ensure_attr_mode<128>(mode, tf) : ensure_attr_mode<256>(mode, tf));
   if (e != cudaSuccess) throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
 }
 

@@ -46,6 +46,9 @@ struct ConvGemmArgs {
   int b_resident;          // 1: every weight k-tile is loaded once and stays in shared memory
   int mma_lanes;           // MMA-issuing threads P (1, 2 or 4, one per warp): issuer p accumulates
                            // the k-tiles g = p mod P into its own partial accumulator
+  int tf32;                // 0: bf16 operands (kind::f16, 64 per k-tile row); 1: fp32 operands
+                           // multiplied as TF32 (kind::tf32, 32 per 128-byte k-tile row)
+  int round_tf32;          // fp32 output rounded to the TF32 grid (it feeds TF32 MMAs)
   int producers;           // TMA producer threads Q (1-4): thread q loads k-tiles g = q mod Q
                            // (stages is a multiple of P and Q, so every stage has one producer
                            // and one consumer, each in order)
@@ -94,6 +97,15 @@ cudaError_t to_nhwc_bf16(const void* src, int src_bf16, const int64_t* shape4, c
 // dst[n, hs, ws, (p*2+q)*C + c] = src[n, c, 2hs+p, 2ws+q], zero outside the image and in channels 4C..15.
 cudaError_t to_s2d_bf16(const void* src, int src_bf16, const int64_t* shape4, const int64_t* stride4, void* dst,
                         int64_t Hs, int64_t Ws, cudaStream_t s);
+// The same conversions into fp32 operands for the TF32 path (values rounded to the TF32 grid):
+// NHWC fp32 [N,H,W,Cp] (Cp % 4 == 0) and rows fp32 [M, Kp].
+cudaError_t to_nhwc_f32(const void* src, int src_bf16, const int64_t* shape4, const int64_t* stride4, void* dst,
+                        int Cp, cudaStream_t s);
+cudaError_t to_rows_f32(const void* src, int src_bf16, int64_t M, int64_t K, int64_t sm, int64_t sk, void* dst,
+                        int64_t Kp, cudaStream_t s);
+// NHWC fp32 max pooling (C % 4 == 0).
+cudaError_t maxpool_nhwc_f32(const void* x, void* y, int N, int H, int W, int C, int Ho, int Wo, int kh, int kw,
+                             int sh, int sw, int ph, int pw, int dh, int dw, cudaStream_t s);
 // dst (bf16 [M, Kp]) <- src logical [M, K] with arbitrary strides; columns K..Kp-1 zero.
 cudaError_t to_rows_bf16(const void* src, int src_bf16, int64_t M, int64_t K, int64_t sm, int64_t sk,
                          void* dst, int64_t Kp, cudaStream_t s);

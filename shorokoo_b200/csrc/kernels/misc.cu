@@ -94,6 +94,78 @@ __global__ void to_s2d_bf16_kernel(const void* __restrict__ src, int src_bf16, i
   }
 }
 
+// fp32 rounded to the TF32 grid (10 explicit mantissa bits, nearest, ties away): the operands the
+// TF32 tensor-core path multiplies, rounded once here instead of truncated by the MMA.
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// dst (NHWC fp32 [N,H,W,Cp], TF32-rounded) <- src logical [N,C,H,W], 4 channels per thread.
+__global__ void to_nhwc_f32_kernel(const void* __restrict__ src, int src_bf16, int64_t N, int64_t C, int64_t H,
+                                   int64_t W, int64_t s0, int64_t s1, int64_t s2, int64_t s3, float* __restrict__ dst,
+                                   int Cp) {
+  const int groups = Cp / 4;
+  const int64_t total = N * H * W * groups;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t pix_total = N * H * W;
+    const int g = int(i / pix_total);
+    const int64_t pix = i - int64_t(g) * pix_total;
+    const int64_t n = pix / (H * W);
+    const int64_t hw = pix - n * H * W;
+    const int64_t h = hw / W, w = hw - (hw / W) * W;
+    const int64_t base = n * s0 + h * s2 + w * s3;
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t c = int64_t(g) * 4 + j;
+      v[j] = tf32_rna(c < C ? ld_any(src, src_bf16, base + c * s1) : 0.f);
+    }
+    *reinterpret_cast<float4*>(dst + pix * Cp + g * 4) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+__global__ void to_rows_f32_kernel(const void* __restrict__ src, int src_bf16, int64_t M, int64_t K, int64_t sm,
+                                   int64_t sk, float* __restrict__ dst, int64_t Kp) {
+  const int64_t total = M * Kp;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t m = i / Kp, kk = i - m * Kp;
+    dst[i] = tf32_rna(kk < K ? ld_any(src, src_bf16, m * sm + kk * sk) : 0.f);
+  }
+}
+
+// NHWC fp32 max pooling, 4 channels (16 bytes) per thread (padding never wins).
+__global__ void maxpool_nhwc_f32_kernel(const float* __restrict__ x, float* __restrict__ y, int N, int H, int W, int C,
+                                        int Ho, int Wo, int kh, int kw, int sh, int sw, int ph, int pw, int dh,
+                                        int dw) {
+  const int cg = C / 4;
+  const int64_t total = int64_t(N) * Ho * Wo * cg;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int g = int(i % cg);
+    int64_t pix = i / cg;
+    const int wo = int(pix % Wo);
+    pix /= Wo;
+    const int ho = int(pix % Ho);
+    const int n = int(pix / Ho);
+    float4 m = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    for (int a = 0; a < kh; ++a) {
+      const int hi = ho * sh - ph + a * dh;
+      if (hi < 0 || hi >= H) continue;
+      for (int b = 0; b < kw; ++b) {
+        const int wi = wo * sw - pw + b * dw;
+        if (wi < 0 || wi >= W) continue;
+        const float4 q = __ldg(reinterpret_cast<const float4*>(x + ((int64_t(n) * H + hi) * W + wi) * C + g * 4));
+        m.x = fmaxf(m.x, q.x);
+        m.y = fmaxf(m.y, q.y);
+        m.z = fmaxf(m.z, q.z);
+        m.w = fmaxf(m.w, q.w);
+      }
+    }
+    *reinterpret_cast<float4*>(y + i * 4) = m;
+  }
+}
+
 __global__ void to_rows_bf16_kernel(const void* __restrict__ src, int src_bf16, int64_t M, int64_t K, int64_t sm,
                                     int64_t sk, __nv_bfloat16* __restrict__ dst, int64_t Kp) {
   const int64_t total = M * Kp;
@@ -341,6 +413,29 @@ cudaError_t to_nhwc_bf16(const void* src, int src_bf16, const int64_t* sh, const
   const int64_t total = sh[0] * sh[2] * sh[3] * (Cp / 4);
   to_nhwc_bf16_kernel<<<grid_for(total), kThreads, 0, s>>>(src, src_bf16, sh[0], sh[1], sh[2], sh[3], st[0], st[1],
                                                            st[2], st[3], reinterpret_cast<__nv_bfloat16*>(dst), Cp);
+  return cudaGetLastError();
+}
+
+cudaError_t to_nhwc_f32(const void* src, int src_bf16, const int64_t* sh, const int64_t* st, void* dst, int Cp,
+                        cudaStream_t s) {
+  if (Cp % 4) return cudaErrorInvalidValue;
+  const int64_t total = sh[0] * sh[2] * sh[3] * (Cp / 4);
+  to_nhwc_f32_kernel<<<grid_for(total), kThreads, 0, s>>>(src, src_bf16, sh[0], sh[1], sh[2], sh[3], st[0], st[1], st[2],
+                                                          st[3], reinterpret_cast<float*>(dst), Cp);
+  return cudaGetLastError();
+}
+
+cudaError_t to_rows_f32(const void* src, int src_bf16, int64_t M, int64_t K, int64_t sm, int64_t sk, void* dst,
+                        int64_t Kp, cudaStream_t s) {
+  to_rows_f32_kernel<<<grid_for(M * Kp), kThreads, 0, s>>>(src, src_bf16, M, K, sm, sk, reinterpret_cast<float*>(dst), Kp);
+  return cudaGetLastError();
+}
+
+cudaError_t maxpool_nhwc_f32(const void* x, void* y, int N, int H, int W, int C, int Ho, int Wo, int kh, int kw, int sh,
+                             int sw, int ph, int pw, int dh, int dw, cudaStream_t s) {
+  if (C % 4) return cudaErrorInvalidValue;
+  maxpool_nhwc_f32_kernel<<<grid_for(int64_t(N) * Ho * Wo * (C / 4)), kThreads, 0, s>>>(
+      reinterpret_cast<const float*>(x), reinterpret_cast<float*>(y), N, H, W, C, Ho, Wo, kh, kw, sh, sw, ph, pw, dh, dw);
   return cudaGetLastError();
 }
 

@@ -2,8 +2,9 @@
 // allocation (liveness + best fit), launch closures and CUDA-graph capture.
 //
 // Layout policy: activations that feed tensor-core or pooling kernels are stored NHWC bf16 (channel
-// contiguous, so an im2col row of one filter tap is a contiguous 128-byte run); everything a generic
-// op or a graph output reads is fp32. Reshape / Transpose / Slice / Expand are stride views when the
+// contiguous, so an im2col row of one filter tap is a contiguous 128-byte run), or NHWC fp32 rounded
+// to the TF32 grid in the TF32 accuracy mode; everything a generic op or a graph output reads is
+// fp32. Reshape / Transpose / Slice / Expand are stride views when the
 // memory permits (the NHWC conv output of a RetinaNet head makes its Reshape->Transpose chain a pure
 // view), otherwise a strided copy materialises them.
 #include "plan.h"
@@ -141,7 +142,8 @@ inline void ck(cudaError_t e, const char* what) {
 }  // namespace
 
 // ---------------------------------------------------------------------------------------------
-Plan::Plan(LGraph g, int device, int num_sms) : g_(std::move(g)), device_(device), num_sms_(num_sms) {
+Plan::Plan(LGraph g, int device, int num_sms, bool tf32)
+    : g_(std::move(g)), device_(device), num_sms_(num_sms), tf32_(tf32) {
   fuse(g_);
   build();
   allocate_and_finalize();
@@ -186,6 +188,24 @@ DevTensor Plan::alloc_nhwc(const std::vector<int64_t>& s, bool bf16, int64_t cst
   return t;
 }
 
+// Tensor-core weights in the operand dtype: bf16 (round to nearest even), or fp32 rounded to the
+// TF32 grid (10 explicit mantissa bits, nearest even) so the MMA's read of them is exact.
+int64_t Plan::add_operand_weights(const std::vector<float>& w) {
+  if (!tf32_) {
+    std::vector<uint16_t> b(w.size());
+    for (size_t i = 0; i < w.size(); ++i) b[i] = f32_to_bf16_rne(w[i]);
+    return add_weight_bytes(b.data(), b.size() * 2);
+  }
+  std::vector<uint32_t> f(w.size());
+  for (size_t i = 0; i < w.size(); ++i) {
+    uint32_t u;
+    std::memcpy(&u, &w[i], 4);
+    if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0xFFFu + ((u >> 13) & 1u)) & ~0x1FFFu;   // finite values only
+    f[i] = u;
+  }
+  return add_weight_bytes(f.data(), f.size() * 4);
+}
+
 int64_t Plan::add_weight_bytes(const void* data, size_t bytes) {
   size_t off = (wblob_.size() + kAlign - 1) / kAlign * kAlign;
   wblob_.resize(off + std::max<size_t>(bytes, 1));
@@ -214,7 +234,9 @@ void Plan::add_step(const std::string& kind, std::vector<DevTensor> reads, std::
   stats_.kernels++;
 }
 
-bool Plan::consumers_accept_bf16(int v) const {
+// True when every reader of v (through views) is a tensor-core or pooling op: v can be stored in
+// the operand dtype (bf16, or TF32-rounded fp32).
+bool Plan::feeds_tensor_ops(int v) const {
   if (is_output_[size_t(v)]) return false;
   if (consumers_[size_t(v)].empty()) return false;
   for (int oi : consumers_[size_t(v)]) {
@@ -223,13 +245,15 @@ bool Plan::consumers_accept_bf16(int v) const {
         op.type == "GlobalAveragePool" || op.type == "GlobalMaxPool")
       continue;
     if (is_view_op(op.type) && op.in[0] == v) {
-      if (!consumers_accept_bf16(op.out[0])) return false;
+      if (!feeds_tensor_ops(op.out[0])) return false;
       continue;
     }
     return false;
   }
   return true;
 }
+
+bool Plan::consumers_accept_bf16(int v) const { return !tf32_ && feeds_tensor_ops(v); }
 
 DevTensor Plan::materialize(const DevTensor& src, bool bf16) {
   DevTensor dst = alloc_contig(src.shape, bf16);
@@ -250,39 +274,43 @@ DevTensor Plan::as_f32_contig(int v) {
   return materialize(t, false);
 }
 
-DevTensor Plan::as_nhwc_bf16(int v, int Cp) {
+// NHWC copy of v in the operand dtype (bf16, or TF32-rounded fp32) with Cp channels per pixel.
+DevTensor Plan::as_nhwc_op(int v, int Cp) {
   const DevTensor& t = vt_[size_t(v)];
   SB_CHECK(t.shape.size() == 4, SB_SHAPE_ERROR, "expected a rank-4 activation");
   const int64_t N = t.shape[0], C = t.shape[1], H = t.shape[2], W = t.shape[3];
-  if (t.bf16 && C == Cp && t.strides[1] == 1 && t.strides[3] == Cp && (t.strides[2] == W * Cp || H == 1) &&
+  if (t.bf16 == !tf32_ && C == Cp && t.strides[1] == 1 && t.strides[3] == Cp && (t.strides[2] == W * Cp || H == 1) &&
       (t.strides[0] == H * W * Cp || N == 1) && t.off % 16 == 0)
     return t;
   auto key = std::make_pair(v, Cp);
   auto it = conv_cache_.find(key);
   if (it != conv_cache_.end()) return it->second;
-  DevTensor dst = alloc_nhwc({N, C, H, W}, true, Cp);
-  add_step("to_nhwc_bf16", {t}, {dst}, [this, t, dst, Cp]() {
+  DevTensor dst = alloc_nhwc({N, C, H, W}, !tf32_, Cp);
+  const bool f32 = tf32_;
+  add_step(f32 ? "to_nhwc_f32" : "to_nhwc_bf16", {t}, {dst}, [this, t, dst, Cp, f32]() {
     const void* sp = ptr(t);
     void* dp = ptr(dst);
     int64_t sh[4] = {t.shape[0], t.shape[1], t.shape[2], t.shape[3]};
     int64_t st[4] = {t.strides[0], t.strides[1], t.strides[2], t.strides[3]};
     int sb = t.bf16;
     return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
-      return k::to_nhwc_bf16(sp, sb, sh, st, dp, Cp, s);
+      return f32 ? k::to_nhwc_f32(sp, sb, sh, st, dp, Cp, s) : k::to_nhwc_bf16(sp, sb, sh, st, dp, Cp, s);
     });
   });
   conv_cache_[key] = dst;
   return dst;
 }
 
-DevTensor Plan::as_rows_bf16(int v, int64_t M, int64_t K) {
+// Row matrix [M, Kp] of v in the operand dtype, rows 16-byte aligned.
+DevTensor Plan::as_rows_op(int v, int64_t M, int64_t K) {
   DevTensor t = vt_[size_t(v)];
   auto vs = view_strides(t.shape, t.strides, {M, K});
   if (vs) {
     DevTensor r = t;
     r.shape = {M, K};
     r.strides = *vs;
-    if (t.bf16 && r.strides[1] == 1 && (r.strides[0] == K || M == 1) && K % 8 == 0 && t.off % 16 == 0) {
+    if (t.bf16 == !tf32_ && r.strides[1] == 1 && (r.strides[0] == K || M == 1) && K % (tf32_ ? 4 : 8) == 0 &&
+        t.off % 16 == 0) {
       r.strides[0] = K;
       return r;
     }
@@ -294,15 +322,16 @@ DevTensor Plan::as_rows_bf16(int v, int64_t M, int64_t K) {
   }
   auto it = rows_cache_.find(v);
   if (it != rows_cache_.end()) return it->second;
-  const int64_t Kp = round_up(K, 8);
-  DevTensor dst = alloc_contig({M, Kp}, true);
-  add_step("to_rows_bf16", {t}, {dst}, [this, t, dst, M, K, Kp]() {
+  const int64_t Kp = round_up(K, tf32_ ? 4 : 8);
+  DevTensor dst = alloc_contig({M, Kp}, !tf32_);
+  const bool f32 = tf32_;
+  add_step(f32 ? "to_rows_f32" : "to_rows_bf16", {t}, {dst}, [this, t, dst, M, K, Kp, f32]() {
     const void* sp = ptr(t);
     void* dp = ptr(dst);
     int64_t sm = t.strides[0], sk = t.strides[1];
     int sb = t.bf16;
     return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
-      return k::to_rows_bf16(sp, sb, M, K, sm, sk, dp, Kp, s);
+      return f32 ? k::to_rows_f32(sp, sb, M, K, sm, sk, dp, Kp, s) : k::to_rows_bf16(sp, sb, M, K, sm, sk, dp, Kp, s);
     });
   });
   rows_cache_[v] = dst;
@@ -322,11 +351,11 @@ void Plan::plan_conv(const Op& op) {
   // space-to-depth image: out(ho) reads original rows i = 2*ho - pt + kh; with e = pt % 2 and
   // u = kh + e = 2a + p this is s2d row ho - (pt+e)/2 + a, parity p, so the kernel becomes
   // ceil((KH+e)/2) taps over 16 channels (p, q, c) with zero weights where kh falls outside [0, KH).
-  const bool s2d = op.strides[0] == 2 && op.strides[1] == 2 && op.dilations[0] == 1 && op.dilations[1] == 1 &&
-                   C <= 4 && KH >= 3 && KW >= 3;
+  const bool s2d = !tf32_ && op.strides[0] == 2 && op.strides[1] == 2 && op.dilations[0] == 1 &&
+                   op.dilations[1] == 1 && C <= 4 && KH >= 3 && KW >= 3;
   int64_t gH = H, gW = W, gKH = KH, gKW = KW, gsh = op.strides[0], gsw = op.strides[1];
   int64_t gph = op.pads[0], gpw = op.pads[1], gdh = op.dilations[0], gdw = op.dilations[1];
-  int Cp = int(C % 8 == 0 ? C : (C <= 4 ? 4 : round_up(C, 8)));
+  int Cp = int(tf32_ ? round_up(C, 4) : (C % 8 == 0 ? C : (C <= 4 ? 4 : round_up(C, 8))));
   int64_t et = 0, el = 0;
   if (s2d) {
     et = op.pads[0] % 2;
@@ -342,7 +371,7 @@ void Plan::plan_conv(const Op& op) {
     Cp = 16;
   }
   const bool one_by_one = !s2d && KH == 1 && KW == 1 && op.strides[0] == 1 && op.strides[1] == 1 && op.pads[0] == 0 &&
-                          op.pads[1] == 0 && op.pads[2] == 0 && op.pads[3] == 0 && Cp % 8 == 0;
+                          op.pads[1] == 0 && op.pads[2] == 0 && op.pads[3] == 0 && Cp % (tf32_ ? 4 : 8) == 0;
   DevTensor x;
   if (s2d) {
     auto key = std::make_pair(op.in[0], -16);
@@ -366,14 +395,14 @@ void Plan::plan_conv(const Op& op) {
       conv_cache_[key] = x;
     }
   } else {
-    x = as_nhwc_bf16(op.in[0], Cp);
+    x = as_nhwc_op(op.in[0], Cp);
   }
   const int64_t K = gKH * gKW * Cp;
-  const int64_t Kpad = round_up(K, 64);
+  const int64_t Kpad = round_up(K, tf32_ ? 32 : 64);   // whole 128-byte k-tile rows
   SB_CHECK(N * Ho * Wo < (int64_t(1) << 31) && N * gH * gW * Cp < (int64_t(1) << 40), SB_UNSUPPORTED,
            "Conv: problem too large for 32-bit row indexing");
-  // weights [Cout, Kpad] bf16, K ordered (kh, kw, c) of the kernel as run
-  std::vector<uint16_t> wb(size_t(Cout * Kpad), 0);
+  // weights [Cout, Kpad] bf16 (or TF32-rounded fp32), K ordered (kh, kw, c) of the kernel as run
+  std::vector<float> wf(size_t(Cout * Kpad), 0.f);
   const float* wp = Wt.ptr<float>();
   for (int64_t m = 0; m < Cout; ++m)
     for (int64_t c = 0; c < C; ++c)
@@ -386,11 +415,11 @@ void Plan::plan_conv(const Op& op) {
           } else {
             kidx = (a * KW + b) * Cp + c;
           }
-          wb[size_t(m * Kpad + kidx)] = f32_to_bf16_rne(wp[((m * C + c) * KH + a) * KW + b]);
+          wf[size_t(m * Kpad + kidx)] = wp[((m * C + c) * KH + a) * KW + b];
         }
   DevTensor wt;
   wt.buf = -1;
-  wt.off = add_weight_bytes(wb.data(), wb.size() * 2);
+  wt.off = add_operand_weights(wf);
   std::vector<float> bias(size_t(round_up(Cout, 256)), 0.f);
   for (int64_t m = 0; m < Cout; ++m) bias[size_t(m)] = op.bias ? op.bias->ptr<float>()[m] : 0.f;
   DevTensor bt;
@@ -416,7 +445,7 @@ void Plan::plan_conv(const Op& op) {
       r = rt;
       ldr = cs;
     } else {
-      r = as_nhwc_bf16(op.residual, int(round_up(Cout, 4)));
+      r = as_nhwc_op(op.residual, int(round_up(Cout, 4)));
       ldr = round_up(Cout, 4);
     }
     Hr = int(rh);
@@ -427,6 +456,8 @@ void Plan::plan_conv(const Op& op) {
   std::vector<DevTensor> reads{x};
   if (r.valid()) reads.push_back(r);
   const int sms = num_sms_;
+  const bool f32 = tf32_;
+  const bool round_out = tf32_ && feeds_tensor_ops(op.out[0]);   // next MMA reads it as TF32
   k::ConvGemmArgs geo;   // geometry only: how the kernel will fetch A (for the step's label)
   std::memset(&geo, 0, sizeof(geo));
   geo.gather = one_by_one ? 0 : 1;
@@ -484,6 +515,8 @@ void Plan::plan_conv(const Op& op) {
     a.ldo = Cout;
     a.act = op.act;
     a.err = err_;
+    a.tf32 = f32;
+    a.round_tf32 = round_out;
     k::conv_gemm_prepare(*p, ptr(x), Cp, ptr(wt), sms);
     return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::conv_gemm_launch(*p, s); });
   });
@@ -497,16 +530,16 @@ void Plan::plan_gemm(const Op& op) {
   SB_CHECK(!xv.shape.empty() && xv.shape.back() == K, SB_SHAPE_ERROR, "Gemm: inner dimension mismatch");
   const int64_t M = numel(xv.shape) / std::max<int64_t>(K, 1);
   SB_CHECK(M < (int64_t(1) << 31), SB_UNSUPPORTED, "Gemm: too many rows");
-  DevTensor x = as_rows_bf16(op.in[0], M, K);
+  DevTensor x = as_rows_op(op.in[0], M, K);
   const int64_t lda = x.strides[0];
-  const int64_t Kpad = round_up(K, 64);
-  std::vector<uint16_t> wb(size_t(Nn * Kpad), 0);
+  const int64_t Kpad = round_up(K, tf32_ ? 32 : 64);
+  std::vector<float> wf(size_t(Nn * Kpad), 0.f);
   const float* wp = Wt.ptr<float>();
   for (int64_t n = 0; n < Nn; ++n)
-    for (int64_t kk = 0; kk < K; ++kk) wb[size_t(n * Kpad + kk)] = f32_to_bf16_rne(wp[n * K + kk]);
+    for (int64_t kk = 0; kk < K; ++kk) wf[size_t(n * Kpad + kk)] = wp[n * K + kk];
   DevTensor wt;
   wt.buf = -1;
-  wt.off = add_weight_bytes(wb.data(), wb.size() * 2);
+  wt.off = add_operand_weights(wf);
   std::vector<float> bias(size_t(round_up(Nn, 256)), 0.f);
   for (int64_t n = 0; n < Nn; ++n) bias[size_t(n)] = op.bias ? op.bias->ptr<float>()[n] : 0.f;
   DevTensor bt;
@@ -525,6 +558,8 @@ void Plan::plan_gemm(const Op& op) {
   std::vector<DevTensor> reads{x};
   if (r.valid()) reads.push_back(r);
   const int sms = num_sms_;
+  const bool f32 = tf32_;
+  const bool round_out = tf32_ && feeds_tensor_ops(op.out[0]);   // next MMA reads it as TF32
   add_step("gemm " + std::to_string(M) + "x" + std::to_string(K) + "->" + std::to_string(Nn), reads, {y}, [=]() {
     auto p = std::make_shared<k::ConvGemmPlan>();
     k::ConvGemmArgs& a = p->args;
@@ -550,6 +585,8 @@ void Plan::plan_gemm(const Op& op) {
     a.ldo = Nn;
     a.act = op.act;
     a.err = err_;
+    a.tf32 = f32;
+    a.round_tf32 = round_out;
     k::conv_gemm_prepare(*p, ptr(x), lda, ptr(wt), sms);
     return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::conv_gemm_launch(*p, s); });
   });
@@ -562,25 +599,26 @@ void Plan::plan_maxpool(const Op& op) {
   const int64_t C = xv.shape[1];
   DevTensor x;
   int64_t cs = t.strides.size() == 4 ? t.strides[3] : 0;
-  if (t.bf16 && t.strides[1] == 1 && cs >= C && t.strides[2] == xv.shape[3] * cs &&
+  if (t.bf16 == !tf32_ && t.strides[1] == 1 && cs >= C && t.strides[2] == xv.shape[3] * cs &&
       t.strides[0] == xv.shape[2] * xv.shape[3] * cs && t.off % 16 == 0 && cs % 4 == 0) {
     x = t;
   } else {
     cs = round_up(C, 4);
-    x = as_nhwc_bf16(op.in[0], int(cs));
+    x = as_nhwc_op(op.in[0], int(cs));
   }
-  DevTensor y = alloc_nhwc(yv.shape, true, cs);
+  DevTensor y = alloc_nhwc(yv.shape, !tf32_, cs);
   vt_[size_t(op.out[0])] = y;
   const int N = int(xv.shape[0]), H = int(xv.shape[2]), W = int(xv.shape[3]);
   const int Ho = int(yv.shape[2]), Wo = int(yv.shape[3]);
   const int Cs = int(cs);
+  const bool f32 = tf32_;
   add_step("maxpool", {x}, {y}, [=]() {
     const void* xp = ptr(x);
     void* yp = ptr(y);
     return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
-      return k::maxpool_nhwc_bf16(xp, yp, N, H, W, Cs, Ho, Wo, int(op.kernel[0]), int(op.kernel[1]),
-                                  int(op.strides[0]), int(op.strides[1]), int(op.pads[0]), int(op.pads[1]),
-                                  int(op.dilations[0]), int(op.dilations[1]), s);
+      auto fn = f32 ? k::maxpool_nhwc_f32 : k::maxpool_nhwc_bf16;
+      return fn(xp, yp, N, H, W, Cs, Ho, Wo, int(op.kernel[0]), int(op.kernel[1]), int(op.strides[0]),
+                int(op.strides[1]), int(op.pads[0]), int(op.pads[1]), int(op.dilations[0]), int(op.dilations[1]), s);
     });
   });
 }
@@ -596,7 +634,7 @@ void Plan::plan_global_pool(const Op& op) {
   bool nhwc = t.strides[1] == 1 && (t.strides[2] == W * ldp || H == 1) && (t.strides[0] == H * W * ldp || N == 1);
   if (!nhwc) {
     ldp = round_up(C, 4);
-    x = as_nhwc_bf16(op.in[0], int(ldp));
+    x = as_nhwc_op(op.in[0], int(ldp));
   }
   const bool out_bf16 = consumers_accept_bf16(op.out[0]);
   DevTensor y = alloc_contig(yv.shape, out_bf16);

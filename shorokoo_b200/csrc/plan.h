@@ -47,7 +47,8 @@ struct OutputBinding {
 
 class Plan {
  public:
-  Plan(LGraph g, int device, int num_sms);
+  // tf32: tensor-core operands are fp32 (TF32 MMA, the accuracy mode) instead of bf16.
+  Plan(LGraph g, int device, int num_sms, bool tf32 = false);
   ~Plan();
   Plan(const Plan&) = delete;
   Plan& operator=(const Plan&) = delete;
@@ -87,6 +88,7 @@ class Plan {
   LGraph g_;
   int device_;
   int num_sms_;
+  bool tf32_ = false;   // operand dtype of the tensor-core path: fp32 (TF32 MMA) instead of bf16
   std::vector<DevTensor> vt_;       // per value id
   std::vector<Buffer> bufs_;
   std::vector<PendingStep> pending_;
@@ -111,14 +113,16 @@ class Plan {
   int new_buffer(size_t bytes);
   DevTensor alloc_contig(const std::vector<int64_t>& shape, bool bf16);
   DevTensor alloc_nhwc(const std::vector<int64_t>& shape_nchw, bool bf16, int64_t cstride);
+  int64_t add_operand_weights(const std::vector<float>& w);
   int64_t add_weight_bytes(const void* data, size_t bytes);
   void* ptr(const DevTensor& t) const;
   void add_step(const std::string& kind, std::vector<DevTensor> reads, std::vector<DevTensor> writes,
                 std::function<std::function<cudaError_t(cudaStream_t)>()> build);
 
+  bool feeds_tensor_ops(int v) const;
   bool consumers_accept_bf16(int v) const;
-  DevTensor as_nhwc_bf16(int v, int Cp);
-  DevTensor as_rows_bf16(int v, int64_t M, int64_t K);
+  DevTensor as_nhwc_op(int v, int Cp);
+  DevTensor as_rows_op(int v, int64_t M, int64_t K);
   DevTensor as_f32_contig(int v);
   DevTensor materialize(const DevTensor& src, bool bf16);
 

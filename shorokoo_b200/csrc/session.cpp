@@ -257,6 +257,14 @@ Session::Session(const uint8_t* model, size_t len, const SessionOptions& opt) : 
     cudaGetLastError();
     fail(SB_CUDA_ERROR, "no CUDA device is available for the B200 backend");
   }
+  int prec = opt.precision;
+  if (prec < 0) {
+    const char* e = std::getenv("SHOROKOO_B200_PRECISION");
+    const std::string v = e ? e : "bf16";
+    SB_CHECK(v == "bf16" || v == "tf32", SB_INVALID_ARGUMENT, "SHOROKOO_B200_PRECISION must be bf16 or tf32");
+    prec = v == "tf32" ? 1 : 0;
+  }
+  tf32_ = prec == 1;
   int want = opt.num_devices;
   if (want <= 0) {
     const char* e = std::getenv("SHOROKOO_B200_DEVICES");
@@ -356,7 +364,7 @@ std::shared_ptr<Session::PlanSet> Session::get_plans(const std::vector<std::shar
     std::fprintf(stderr, "[shorokoo_b200] graph does not shard on the batch axis; running on one device\n");
   if (!shard) {
     ck(cudaSetDevice(devices_[0]), "cudaSetDevice");
-    ps->shards.push_back({0, 0, batch > 0 ? batch : 0, std::make_shared<Plan>(std::move(full), devices_[0], sm_counts_[0])});
+    ps->shards.push_back({0, 0, batch > 0 ? batch : 0, std::make_shared<Plan>(std::move(full), devices_[0], sm_counts_[0], tf32_)});
   } else {
     ps->sharded = true;
     const int parts = int(std::min<int64_t>(nd, batch));
@@ -375,7 +383,7 @@ std::shared_ptr<Session::PlanSet> Session::get_plans(const std::vector<std::shar
         try {
           cudaSetDevice(devices_[size_t(sh.device)]);
           LGraph g = lower(model_, specs_for(inputs, sh.begin, sh.count, true));
-          sh.plan = std::make_shared<Plan>(std::move(g), devices_[size_t(sh.device)], sm_counts_[size_t(sh.device)]);
+          sh.plan = std::make_shared<Plan>(std::move(g), devices_[size_t(sh.device)], sm_counts_[size_t(sh.device)], tf32_);
         } catch (const Error& e) {
           errs[si] = e.what();
           codes[si] = e.code;
@@ -427,7 +435,7 @@ void Session::maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_pt
   try {
     ck(cudaSetDevice(P->device), "cudaSetDevice");
     LGraph g = lower(model_, specs_for(inputs, 0, P->chunk, true));
-    P->plan = std::make_shared<Plan>(std::move(g), P->device, sm_counts_[0]);
+    P->plan = std::make_shared<Plan>(std::move(g), P->device, sm_counts_[0], tf32_);
     const auto& outs = P->plan->outputs();
     for (size_t j = 0; j < outs.size(); ++j)
       if (!outs[j].host && (outs[j].shape.empty() || outs[j].shape[0] != P->chunk || ps.out_shapes[j].empty() ||

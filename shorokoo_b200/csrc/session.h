@@ -35,6 +35,7 @@ struct HostValue {
 struct SessionOptions {
   int num_devices = 0;   // 0: SHOROKOO_B200_DEVICES or all visible devices
   int first_device = 0;
+  int precision = -1;    // -1: SHOROKOO_B200_PRECISION (bf16 | tf32, default bf16); 0 bf16; 1 tf32
 };
 
 class Session {
@@ -94,6 +95,7 @@ class Session {
   OnnxModel model_;
   ModelInfo info_;
   SessionOptions opt_;
+  bool tf32_ = false;   // tensor-core operands fp32 read as TF32 (the accuracy mode)
   std::vector<int> devices_;
   std::vector<int> sm_counts_;
   std::vector<cudaStream_t> streams_;

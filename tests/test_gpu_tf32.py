@@ -1,0 +1,76 @@
+"""GPU parity of the TF32 accuracy mode (precision="tf32": fp32 operands read as TF32 by
+tcgen05.mma kind::tf32, fp32 accumulation, fp32 activations rounded to the TF32 grid) against the
+fp32 oracle at the TF32 gate, normwise max|gpu - ref| / max|ref| <= 2e-3 per output, and against
+the oracle with TF32-rounded operands (the mode's own arithmetic) more tightly."""
+import numpy as np
+import pytest
+
+from helpers import assert_close, conv_case, run_oracle
+from shorokoo_b200 import B200InferenceSessionFactory
+from shorokoo_b200.emit import graphs
+from helpers import run_backend
+
+pytestmark = pytest.mark.gpu
+
+TF32_TOL = 2e-3
+
+
+def _tf32(case):
+    return run_backend(case, factory=B200InferenceSessionFactory(num_devices=1, precision="tf32"))
+
+
+@pytest.mark.parametrize("m,k,n,relu", [
+    (300, 200, 100, True), (1000, 96, 1000, False), (513, 1024, 4096, True), (2, 2048, 1000, False),
+])
+def test_tf32_gemm(m, k, n, relu):
+    widths = (k, n) if not relu else (k, n, n)
+    case = graphs.mlp(batch=m, widths=widths, seed=3, bias_scale=0.5)
+    got = _tf32(case)[0]
+    assert_close(got, run_oracle(case)[0], tol=TF32_TOL, what=f"tf32 gemm {m}x{k}x{n}")
+
+
+@pytest.mark.parametrize("kw", [
+    dict(c=64, cout=64, k=1, pads=[0, 0, 0, 0]),                                   # row-matrix 1x1
+    dict(c=64, cout=256, k=1, pads=[0, 0, 0, 0], bn=True, residual=True, relu=True),
+    dict(c=24, cout=40, k=3, h=11, w=7),                                           # gather, 16-byte units
+    dict(c=3, cout=64, k=7, stride=2, pads=[3, 3, 3, 3], h=32, w=32, bn=True, relu=True),  # stem
+    dict(c=32, cout=48, k=3, stride=2, auto_pad="SAME_UPPER", h=25, w=32),
+    dict(c=64, cout=720, k=3, auto_pad="SAME_UPPER", h=7, w=8, sigmoid=True),
+    dict(n=2, c=64, cout=64, k=3, h=32, w=32, bn=True, relu=True),                 # im2col (128-byte pixels)
+    dict(n=2, c=128, cout=256, k=1, stride=2, pads=[0, 0, 0, 0], h=28, w=28),
+    dict(n=2, c=64, cout=32, k=5, pads=[1, 2, 3, 0], h=20, w=30),
+    dict(c=128, cout=64, k=1, pads=[0, 0, 0, 0], h=10, w=16, upsample_residual=True),
+])
+def test_tf32_conv(kw):
+    case = conv_case(**kw)
+    got = _tf32(case)[0]
+    assert_close(got, run_oracle(case)[0], tol=TF32_TOL, what=f"tf32 conv {kw}")
+    assert_close(got, run_oracle(case, "tf32-operands")[0], tol=5e-4, what=f"tf32 conv {kw} vs tf32 oracle")
+
+
+@pytest.mark.parametrize("name,kw", [
+    ("resnet50", dict(batch=2, hw=(64, 64), affine_scale=0.1)),
+    ("resnet18", dict(batch=3, hw=(96, 96))),
+    ("stacked_linear", dict(batch=64)),
+])
+def test_tf32_model_parity(name, kw):
+    case = graphs.build(name, **kw)
+    got = _tf32(case)
+    ref = run_oracle(case)
+    for g, r, o in zip(got, ref, case.output_names):
+        assert_close(g, r, tol=TF32_TOL, what=f"tf32 {name} {kw} output {o}")
+
+
+def test_tf32_retinanet_meets_the_tf32_gate():
+    """The detection graph whose per-pixel outputs sit above the 1e-2 gate with bf16 operands: with
+    TF32 operands both outputs (class scores after the sigmoid, box regressions) meet 2e-3."""
+    case = graphs.retinanet(batch=1, hw=(128, 160))
+    got = _tf32(case)
+    ref = run_oracle(case)
+    for g, r, o in zip(got, ref, case.output_names):
+        assert_close(g, r, tol=TF32_TOL, what=f"tf32 retinanet {o}")
+
+
+def test_precision_is_validated():
+    with pytest.raises(ValueError):
+        B200InferenceSessionFactory(precision="fp8")

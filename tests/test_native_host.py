@@ -133,6 +133,18 @@ def test_truncated_model():
         F.CreateSession(case.model[: len(case.model) // 2])
 
 
+def test_precision_argument_is_validated_before_any_device_work():
+    import ctypes as C
+    from shorokoo_b200 import _native
+    case = graphs.stacked_linear(batch=2, n=8, depth=2)
+    out = C.c_void_p()
+    st = _native.lib().sb_session_create_ex(case.model, len(case.model), 0, 0, 0, 0, 7, C.byref(out))
+    assert st == 1 and out.value is None
+    assert "precision" in _native.lib().sb_last_error().decode()
+    with pytest.raises(ValueError):
+        B200InferenceSessionFactory(precision="fp16")
+
+
 def test_no_gpu_reports_cuda_error():
     import torch
     if torch.cuda.is_available():
