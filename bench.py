@@ -176,6 +176,8 @@ def main():
     ap.add_argument("--workload", default="resnet50", choices=sorted(WORKLOADS))
     ap.add_argument("--ref-sample", type=int, default=8, help="images per step of the CPU reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "tf32"],
+                    help="tensor-core operand precision (tf32: the accuracy mode)")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the workload's global batch (small cases for profiler captures)")
     args = ap.parse_args()
@@ -201,7 +203,7 @@ def main():
     case = full if full is not None else make_case(name, total)
     # this rank's contiguous shard of the batch
     inputs = [(n, a[begin:begin + per] if a.ndim and a.shape[0] == total else a) for n, a in case.inputs]
-    f = B200InferenceSessionFactory(num_devices=1, first_device=local)
+    f = B200InferenceSessionFactory(num_devices=1, first_device=local, precision=args.precision)
     sess = f.CreateSession(case.model)
     feeds = {n: f.CreateTensor(a) for n, a in inputs}
     st = sess.stats(feeds)
@@ -245,6 +247,10 @@ def main():
     tc_launches = sum(1 for k, _ in prof if k.split()[0] in ("conv", "gemm"))
     all_ms = sum(v for _, v in prof)
     peak_tflops, peak_hbm, peak_kind = measured_peaks()
+    peak_note = f"{peak_kind} bf16 dense (burst)"
+    if args.precision == "tf32":   # the dense TF32 tensor rate is half the bf16 rate
+        peak_tflops /= 2
+        peak_note = f"half the {peak_kind} bf16 dense burst (TF32 dense rate)"
     achieved = 2.0 * st["macs"] / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
@@ -263,12 +269,13 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded inputs, random-init weights)",
+            "vs_baseline": None, "dtype": args.precision, "data": "synthetic (seeded inputs, random-init weights)",
             "config": {"workload": f"{name} forward, batch {total} ({per}/GPU), 3x224x224 fp32 NCHW input"
                        if name.startswith("resnet") else f"{name} forward, batch {total}",
                        "global_batch": total, "parallelism": f"batch-sharded x{world}, replicated weights, no collective",
                        "l2": "inputs larger than L2 (the 308 MB input and a multi-GB activation arena per step)",
-                       "precision": "bf16 operands, fp32 accumulate"},
+                       "precision": ("bf16 operands" if args.precision == "bf16" else
+                                     "fp32 operands read as TF32") + ", fp32 accumulate"},
             "e2e": {"value": total / e_max, "unit": "images/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "timing": "host wall clock around Run (synchronous)"},
             "gpu_launches": int(st["launches"]) * args.steps * world,
@@ -276,7 +283,7 @@ def main():
                          "frac": achieved / peak_tflops, "traffic": traffic,
                          "kernel": f"conv_gemm_kernel (tcgen05 implicit GEMM), {tc_launches} launches/step, "
                                    f"{tc_ms:.3f} of {all_ms:.3f} ms per step timed per launch with CUDA events",
-                         "peak_kind": f"{peak_kind} bf16 dense (burst)"},
+                         "peak_kind": peak_note},
             "clocks": clocks,
             "flops_per_image": 2 * macs_per_img,
         }
