@@ -73,6 +73,12 @@ SB_API int32_t sb_session_create_ex(const uint8_t* model, size_t model_len, int3
                              int32_t precision, sb_session** out);
 /* IShorokooInferenceSession.Dispose (IDisposable). */
 SB_API void sb_session_destroy(sb_session* session);
+/* Sessions are cached per process by model content (128-bit hash of the bytes, which are not
+ * retained), device range and precision, so ComputeContext.Execute's session-per-call pattern
+ * (ComputeContext.cs:318-359) reuses plans already built. Up to SHOROKOO_B200_SESSION_CACHE
+ * (default 2; 0 disables) sessions stay cached after their last handle is destroyed. This
+ * releases them and returns how many were cached. No counterpart in the reference. */
+SB_API int32_t sb_session_cache_clear(void);
 
 /* IShorokooInferenceSession.InputNames / OutputNames (IShorokooInferenceSession.cs:5-6).
  * Inputs are reported in graph-input order (ComputeContext.cs:209-211 maps them positionally). */

@@ -23,6 +23,7 @@ SIGNATURES = {
     "sb_last_error": (CSTR, []),
     "sb_session_create": (I32, [C.c_char_p, SZ, I32, I32, PP]),
     "sb_session_create_ex": (I32, [C.c_char_p, SZ, I32, I32, I32, I32, I32, PP]),
+    "sb_session_cache_clear": (I32, []),
     "sb_session_destroy": (None, [P]),
     "sb_session_input_count": (I32, [P]),
     "sb_session_input_name": (CSTR, [P, I32]),

@@ -287,6 +287,12 @@ class B200InferenceSessionFactory:
         self.first_device = first_device
         self.precision = precision
 
+    @staticmethod
+    def ClearSessionCache() -> int:
+        """Releases the sessions the library keeps cached by model content (so a new session on the
+        same model bytes reuses its plans); returns how many were cached."""
+        return int(_native.lib().sb_session_cache_clear())
+
     def CreateSession(self, modelBytes: bytes,
                       graphOptimization: ShorokooGraphOptimization = ShorokooGraphOptimization.EnableAll,
                       logSeverity: ShorokooLogSeverity = ShorokooLogSeverity.Fatal) -> B200InferenceSession:

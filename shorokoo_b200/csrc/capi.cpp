@@ -1,11 +1,17 @@
 // extern "C" entry points declared in include/shorokoo_b200.h.
 #include "../../include/shorokoo_b200.h"
 
+#include <algorithm>
+#include <cstdlib>
 #include <cstring>
+#include <list>
 #include <memory>
+#include <mutex>
 #include <string>
 
 #include "session.h"
+
+extern char** environ;
 
 namespace sb {
 void* host_alloc(size_t bytes, bool& pinned);
@@ -15,7 +21,7 @@ void host_copy(void* dst, const void* src, size_t n);
 using sb::HostValue;
 
 struct sb_session {
-  std::unique_ptr<sb::Session> s;
+  std::shared_ptr<sb::Session> s;   // shared with the session cache and other handles on the same model
   std::vector<std::string> profile_kinds;
 };
 
@@ -72,6 +78,66 @@ std::vector<std::shared_ptr<HostValue>> ordered_inputs(const sb::Session& s, int
   return out;
 }
 
+// Process-wide session cache: ComputeContext.Execute creates a new session per call
+// (ComputeContext.cs:318-359), so a handle created for model bytes already seen (same 128-bit
+// content hash and length, device range, precision and SHOROKOO_B200_* settings, which plans
+// read when they are built) shares the existing session and with it every plan built so far. The bytes themselves are not retained. The last
+// SHOROKOO_B200_SESSION_CACHE (default 2, 0 disables) distinct sessions stay cached after their
+// handles are destroyed; sb_session_cache_clear releases them.
+struct CacheKey {
+  uint64_t h1, h2;
+  size_t len;
+  int32_t num_devices, first_device, precision;
+  std::string env;   // SHOROKOO_B200_* settings in effect
+  bool operator==(const CacheKey& o) const {
+    return h1 == o.h1 && h2 == o.h2 && len == o.len && num_devices == o.num_devices &&
+           first_device == o.first_device && precision == o.precision && env == o.env;
+  }
+};
+
+// Two independent 64-bit multiply-xorshift hashes over 8-byte words (with the tail zero-padded).
+void content_hash(const uint8_t* p, size_t n, uint64_t& h1, uint64_t& h2) {
+  uint64_t a = 0x243F6A8885A308D3ull ^ n, b = 0x13198A2E03707344ull + n;
+  size_t i = 0;
+  auto mix = [](uint64_t h, uint64_t w, uint64_t k) {
+    h ^= w * k;
+    h = (h << 27) | (h >> 37);
+    return h * 0x9E3779B97F4A7C15ull + 0x632BE59BD9B4E019ull;
+  };
+  for (; i + 8 <= n; i += 8) {
+    uint64_t w;
+    std::memcpy(&w, p + i, 8);
+    a = mix(a, w, 0xC2B2AE3D27D4EB4Full);
+    b = mix(b, w ^ 0xA0761D6478BD642Full, 0x165667B19E3779F9ull);
+  }
+  uint64_t w = 0;
+  if (i < n) std::memcpy(&w, p + i, n - i);
+  a = mix(a, w, 0xC2B2AE3D27D4EB4Full);
+  b = mix(b, w ^ 0xA0761D6478BD642Full, 0x165667B19E3779F9ull);
+  a ^= a >> 33;
+  b ^= b >> 29;
+  h1 = a * 0xFF51AFD7ED558CCDull;
+  h2 = b * 0xC4CEB9FE1A85EC53ull;
+}
+
+std::mutex g_cache_mu;
+std::list<std::pair<CacheKey, std::shared_ptr<sb::Session>>> g_cache;   // most recent first
+
+std::string backend_env() {
+  std::string r;
+  for (char** e = environ; e && *e; ++e)
+    if (std::strncmp(*e, "SHOROKOO_B200_", 14) == 0 && std::strncmp(*e, "SHOROKOO_B200_SESSION_CACHE=", 28) != 0) {
+      r += *e;
+      r += '\n';
+    }
+  return r;
+}
+
+size_t cache_capacity() {
+  const char* e = std::getenv("SHOROKOO_B200_SESSION_CACHE");
+  return e ? size_t(std::max(0, std::atoi(e))) : 2;
+}
+
 }  // namespace
 
 namespace sb {
@@ -91,12 +157,37 @@ int32_t sb_session_create_ex(const uint8_t* model, size_t len, int32_t, int32_t,
     *out = nullptr;
     SB_CHECK(precision >= SB_PRECISION_DEFAULT && precision <= SB_PRECISION_TF32, sb::SB_INVALID_ARGUMENT,
              "precision must be SB_PRECISION_DEFAULT, _BF16 or _TF32");
+    SB_CHECK(model != nullptr || len == 0, sb::SB_INVALID_ARGUMENT, "model is null");
     sb::SessionOptions o;
     o.num_devices = num_devices;
     o.first_device = first_device;
-    o.precision = precision;
+    o.precision = sb::resolve_precision(precision);
+    CacheKey key;
+    content_hash(model, len, key.h1, key.h2);
+    key.len = len;
+    key.num_devices = num_devices;
+    key.first_device = first_device;
+    key.precision = o.precision;
+    key.env = backend_env();
     auto s = std::make_unique<sb_session>();
-    s->s = std::make_unique<sb::Session>(model, len, o);
+    const size_t cap = cache_capacity();
+    if (cap > 0) {
+      std::lock_guard<std::mutex> l(g_cache_mu);
+      for (auto it = g_cache.begin(); it != g_cache.end(); ++it)
+        if (it->first == key) {
+          s->s = it->second;
+          g_cache.splice(g_cache.begin(), g_cache, it);
+          break;
+        }
+    }
+    if (!s->s) {
+      s->s = std::make_shared<sb::Session>(model, len, o);
+      if (cap > 0) {
+        std::lock_guard<std::mutex> l(g_cache_mu);
+        g_cache.emplace_front(key, s->s);
+        while (g_cache.size() > cap) g_cache.pop_back();
+      }
+    }
     *out = s.release();
     return SB_STATUS_OK;
   });
@@ -107,6 +198,15 @@ int32_t sb_session_create(const uint8_t* model, size_t len, int32_t opt, int32_t
 }
 
 void sb_session_destroy(sb_session* s) { delete s; }
+
+int32_t sb_session_cache_clear(void) {
+  std::list<std::pair<CacheKey, std::shared_ptr<sb::Session>>> drop;
+  {
+    std::lock_guard<std::mutex> l(g_cache_mu);
+    drop.swap(g_cache);
+  }
+  return int32_t(drop.size());   // the sessions are released here unless a handle still holds one
+}
 
 int32_t sb_session_input_count(const sb_session* s) { return s ? int32_t(s->s->input_names().size()) : 0; }
 const char* sb_session_input_name(const sb_session* s, int32_t i) {

@@ -143,8 +143,6 @@ class Lowerer {
     }
     // Ops that read only metadata of a device value.
     if (n.op_type == "Shape" || n.op_type == "Size") {
-      HostTensor tmp(DT_FLOAT, V(in[0]).shape);
-      tmp.buf.reset();
       std::vector<HostTensor> hout;
       HostTensor shape_only;
       shape_only.dtype = DT_FLOAT;

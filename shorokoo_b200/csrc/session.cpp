@@ -257,14 +257,7 @@ Session::Session(const uint8_t* model, size_t len, const SessionOptions& opt) : 
     cudaGetLastError();
     fail(SB_CUDA_ERROR, "no CUDA device is available for the B200 backend");
   }
-  int prec = opt.precision;
-  if (prec < 0) {
-    const char* e = std::getenv("SHOROKOO_B200_PRECISION");
-    const std::string v = e ? e : "bf16";
-    SB_CHECK(v == "bf16" || v == "tf32", SB_INVALID_ARGUMENT, "SHOROKOO_B200_PRECISION must be bf16 or tf32");
-    prec = v == "tf32" ? 1 : 0;
-  }
-  tf32_ = prec == 1;
+  tf32_ = resolve_precision(opt.precision) == 1;
   int want = opt.num_devices;
   if (want <= 0) {
     const char* e = std::getenv("SHOROKOO_B200_DEVICES");
@@ -286,6 +279,14 @@ Session::Session(const uint8_t* model, size_t len, const SessionOptions& opt) : 
     ck(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
     streams_.push_back(s);
   }
+}
+
+int resolve_precision(int requested) {
+  if (requested >= 0) return requested;
+  const char* e = std::getenv("SHOROKOO_B200_PRECISION");
+  const std::string v = e ? e : "bf16";
+  SB_CHECK(v == "bf16" || v == "tf32", SB_INVALID_ARGUMENT, "SHOROKOO_B200_PRECISION must be bf16 or tf32");
+  return v == "tf32" ? 1 : 0;
 }
 
 Session::~Session() {

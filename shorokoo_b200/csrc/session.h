@@ -111,5 +111,7 @@ class Session {
 };
 
 bool batch_separable(const LGraph& g);
+// SB_PRECISION_DEFAULT (-1) -> SHOROKOO_B200_PRECISION (bf16 | tf32, default bf16); 0 bf16; 1 tf32.
+int resolve_precision(int requested);
 
 }  // namespace sb
