@@ -364,16 +364,16 @@ constexpr int kMaxStages = 8;
 template <bool OBF>
 __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUtensorMap* tmOut, uint32_t tbase,
                                               int col0, int row0, int n0, uint8_t* sb, const uint8_t* rslab,
-                                              const float* bsl, bool dbl, int parts, int pstride) {
+                                              const float* bsl, int wait_mode, int parts, int pstride) {
   constexpr int SC = OBF ? 64 : 32;
   constexpr int EPC = OBF ? 8 : 4;
   constexpr int CH = 32 / EPC;   // 16-byte chunks per 32 columns
   const int lane = threadIdx.x & 31;
   const int m = row0 + lane;
   const int rrow = (row0 & (BM - 1)) + lane;   // row inside the 128-row residual slab
-  if (lane == 0) {   // the last store from this buffer has been read
-    if (dbl) bulk_wait_read1();
-    else bulk_wait_read0();
+  if (lane == 0) {   // the last store from this buffer has been read (1: one buffer, 2: two)
+    if (wait_mode == 2) bulk_wait_read1();
+    else if (wait_mode == 1) bulk_wait_read0();
   }
   __syncwarp();
 #pragma unroll 1
@@ -715,10 +715,16 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
             const int n0 = nt * BN + s2 * SC;
             if (n0 >= a.Cout) break;
             const uint8_t* rslab = RS ? sRes + slot * RSB + s2 * 128 * 128 : nullptr;
-            uint8_t* sb = sb0 + (OB == 2 ? (nslab++ & 1) * kOutSlab : 0);
+            // With a residual ring and no output slabs (OB == 0) the output is written in place
+            // over this warp's 32-row band of the residual slab and stored from there; the slot is
+            // released once that store has read it. Otherwise the warp's own output slab(s).
+            const bool inplace = RS && OB == 0;
+            uint8_t* sb = inplace ? sRes + slot * RSB + s2 * 128 * 128 + q * 32 * 128
+                                  : sb0 + (OB == 2 ? (nslab++ & 1) * kOutSlab : 0);
+            const int wm = inplace ? 0 : OB;
             const float* bsl = wbias + ((s2 - hsel) >> 1) * SC;
-            if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl, OB == 2, PE, BN);
-            else epilogue_slab<false>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl, OB == 2, PE, BN);
+            if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl, wm, PE, BN);
+            else epilogue_slab<false>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl, wm, PE, BN);
           }
         } else {
           const int m = row0 + lane;
@@ -737,8 +743,11 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
       tc_fence_before();
       __syncwarp();   // also: every lane is done reading wbias before the next tile rewrites it
       if (lane == 0) {
-        if (RS) mbar_arrive(&rese[slot]);
         mbar_arrive(&acce[acc]);
+        if (RS) {
+          if (OB == 0) bulk_wait_read0();   // in place: this warp's stores have read the slot
+          mbar_arrive(&rese[slot]);
+        }
       }
     }
     if (lane == 0) bulk_wait_all();
@@ -1019,24 +1028,42 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   // four starve on operands, and the row-matrix 1x1 convs lose more to the stage rounding (their
   // residual ring leaves room for only two or three stages) than they gain.
   const bool im2col = p.mode == kAIm2col64 || p.mode == kAIm2col16;
-  int pl = im2col && bn <= 128 ? 2 : 1;
+  // Residual convs with a long reduction (>= 8 k-tiles) write their output in place in the residual
+  // ring: the output slabs' shared memory becomes a fourth operand stage, which also lets two MMA
+  // threads issue. The short ones (HBM-bound) keep separate output slabs, releasing each ring slot
+  // without waiting for the stores (measured on ResNet-50: in place there costs 5-6%).
+  const bool inplace_hint = res_ring && out_ok && KT >= 8;
+  // (the cp.async gather modes have no spare warps: their warps 10-13 gather, so one issuer)
+  int pl = !gather && (im2col || inplace_hint) && bn <= 128 ? 2 : 1;
   if (const char* e = std::getenv("SHOROKOO_B200_MMA_LANES")) pl = std::max(1, std::min(pl, std::atoi(e)));
   while (pl > KT) pl /= 2;
+  if (gather && pl != 1) throw std::runtime_error("conv_gemm: gather modes have a single MMA issuer");
   a.mma_lanes = pl;
   const int stage_bytes = BM * 128 + (bres ? 0 : bn * 128);
   const int rsb = 128 * bn * es;
-  // Shared memory: operand stages + output slabs (one per epilogue warp by default) + bias +
-  // residual ring (two slots when two operand stages still fit beside them). A second output
-  // buffer per warp lets a slab's store drain while the next slab is computed, but measured on
-  // ResNet-50 the operand stages it costs are worth more, so it is opt-in (SHOROKOO_B200_OUTBUF=2).
+  // Output and residual tensor maps first: whether the epilogue stores through TMA and streams the
+  // residual through a ring decides the shared-memory plan.
+  bool ring = false;
+  if (out_ok &&
+      encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldo) * es, sc, 32, !a.out_bf16)) {
+    a.epi = 2;
+    ring = res_ring && encode_2d(&p.tmRes, a.res, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldr) * es, sc, 128,
+                                 !a.out_bf16);
+  }
+  // Shared memory: operand stages + output slabs + bias + residual ring (two slots when two
+  // operand stages still fit beside them). In-place residual convs have no output slabs;
+  // otherwise one slab per epilogue warp. A second slab per warp lets a store
+  // drain while the next slab is computed, but measured on ResNet-50 the operand stages it costs
+  // are worth more, so it is opt-in (SHOROKOO_B200_OUTBUF=2).
   auto fixed_for = [&](int ob) { return int(8 * ob * kOutSlab + kBiasStage) + 1024 + 512 + (bres ? int(w_bytes) : 0); };
   auto ring_for = [&](int ob) {
-    if (!res_ring) return 0;
+    if (!ring) return 0;
     return (kSmemLimit - fixed_for(ob) - 2 * rsb) / stage_bytes >= 2 ? 2 : 1;
   };
   auto stages_for = [&](int ob, int rs) { return std::min(kMaxStages, (kSmemLimit - fixed_for(ob) - rs * rsb) / stage_bytes); };
-  int ob = 1;
-  if (const char* e = std::getenv("SHOROKOO_B200_OUTBUF")) ob = std::atoi(e) == 2 ? 2 : 1;
+  int ob = ring && KT >= 8 ? 0 : 1;
+  if (ob != 0)
+    if (const char* e = std::getenv("SHOROKOO_B200_OUTBUF")) ob = std::atoi(e) == 2 ? 2 : 1;
   int rs = ring_for(ob);
   const int smax = stages_for(ob, rs);
   // Producers and stages. With one MMA issuer the stages are consumed in order, and at least as
@@ -1080,21 +1107,8 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   if (!ok) throw std::runtime_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad layout)");
   if ((p.mode == kAIm2col64 || p.mode == kAIm2col16) && !encode_im2col(&p.tmA, a, p.mode == kAIm2col64 ? bke : 16))
     throw std::runtime_error("cuTensorMapEncodeIm2col failed (driver entry point missing or bad layout)");
-  if (out_ok &&
-      encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldo) * es, sc, 32, !a.out_bf16)) {
-    a.epi = 2;
-    if (rs && encode_2d(&p.tmRes, a.res, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldr) * es, sc, 128,
-                        !a.out_bf16)) {
-      a.res_slots = rs;
-      a.res_slot_bytes = rsb;
-    } else {
-      // no ring: restore the operand stages the ring would have used (a multiple of P and Q
-      // when several MMA threads issue)
-      const int l = a.mma_lanes == 1 ? 1 : lcm(a.producers, a.mma_lanes);
-      a.stages = std::max(a.stages, (std::min(kMaxStages, (kSmemLimit - fixed) / stage_bytes) / l) * l);
-      p.smem = a.stages * stage_bytes + fixed;
-    }
-  }
+  a.res_slots = rs;
+  a.res_slot_bytes = rs ? rsb : 0;
   const int mode = p.mode;
   const bool tf = a.tf32 != 0;
   cudaError_t e = bn == 64 ? ensure_attr_mode<64>(mode, tf)
