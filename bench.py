@@ -176,7 +176,7 @@ def main():
     ap.add_argument("--workload", default="resnet50", choices=sorted(WORKLOADS))
     ap.add_argument("--ref-sample", type=int, default=8, help="images per step of the CPU reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--precision", default="bf16", choices=["bf16", "tf32"],
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "tf32", "tf32x3"],
                     help="tensor-core operand precision (tf32: the accuracy mode)")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the workload's global batch (small cases for profiler captures)")
@@ -248,9 +248,12 @@ def main():
     all_ms = sum(v for _, v in prof)
     peak_tflops, peak_hbm, peak_kind = measured_peaks()
     peak_note = f"{peak_kind} bf16 dense (burst)"
-    if args.precision == "tf32":   # the dense TF32 tensor rate is half the bf16 rate
+    if args.precision in ("tf32", "tf32x3"):   # the dense TF32 tensor rate is half the bf16 rate
         peak_tflops /= 2
         peak_note = f"half the {peak_kind} bf16 dense burst (TF32 dense rate)"
+        if args.precision == "tf32x3":   # three MMAs per algorithmic one
+            peak_tflops /= 3
+            peak_note += ", divided by the three MMAs per K slice of TF32x3"
     achieved = 2.0 * st["macs"] / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
@@ -274,8 +277,9 @@ def main():
                        if name.startswith("resnet") else f"{name} forward, batch {total}",
                        "global_batch": total, "parallelism": f"batch-sharded x{world}, replicated weights, no collective",
                        "l2": "inputs larger than L2 (the 308 MB input and a multi-GB activation arena per step)",
-                       "precision": ("bf16 operands" if args.precision == "bf16" else
-                                     "fp32 operands read as TF32") + ", fp32 accumulate"},
+                       "precision": {"bf16": "bf16 operands", "tf32": "fp32 operands read as TF32",
+                                     "tf32x3": "error-compensated TF32 (hi*hi + hi*lo + lo*hi)"}[args.precision]
+                                    + ", fp32 accumulate"},
             "e2e": {"value": total / e_max, "unit": "images/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "timing": "host wall clock around Run (synchronous)"},
             "gpu_launches": int(st["launches"]) * args.steps * world,

@@ -61,13 +61,16 @@ SB_API int32_t sb_session_create(const uint8_t* model, size_t model_len, int32_t
                           int32_t log_severity, sb_session** out);
 /* Same, with an explicit device range [first_device, first_device + num_devices) and the
  * tensor-core precision: SB_PRECISION_BF16 (bf16 operands, fp32 accumulation; the throughput mode,
- * normwise error <= 1e-2), SB_PRECISION_TF32 (fp32 operands read as TF32; the accuracy mode,
- * <= 2e-3), or SB_PRECISION_DEFAULT (SHOROKOO_B200_PRECISION=bf16|tf32, else bf16).
+ * normwise error <= 1e-2), SB_PRECISION_TF32 (fp32 operands read as TF32; <= 2e-3 except where
+ * deep per-pixel outputs sit at the TF32 floor), SB_PRECISION_TF32X3 (error-compensated TF32:
+ * three MMAs per K slice, close to fp32 accuracy, at a third of the TF32 rate), or
+ * SB_PRECISION_DEFAULT (SHOROKOO_B200_PRECISION=bf16|tf32|tf32x3, else bf16).
  * sb_session_create uses SB_PRECISION_DEFAULT. No counterpart in the reference, whose ORT CUDA
  * provider computes in fp32 (OrtSessionFactory.cs:23-42). */
 #define SB_PRECISION_DEFAULT (-1)
 #define SB_PRECISION_BF16 0
 #define SB_PRECISION_TF32 1
+#define SB_PRECISION_TF32X3 2
 SB_API int32_t sb_session_create_ex(const uint8_t* model, size_t model_len, int32_t graph_optimization,
                              int32_t log_severity, int32_t num_devices, int32_t first_device,
                              int32_t precision, sb_session** out);

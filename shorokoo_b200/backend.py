@@ -275,14 +275,14 @@ class B200InferenceSessionFactory:
     """IShorokooInferenceSessionFactory for the Shorokoo.LinuxGPU slot (OrtSessionFactory.cs:14-106).
 
     ``num_devices`` = 0 uses SHOROKOO_B200_DEVICES or every visible GPU; batches shard across them.
-    ``precision``: "bf16" (throughput mode), "tf32" (accuracy mode: fp32 operands read as TF32) or
-    None for SHOROKOO_B200_PRECISION (default bf16)."""
+    ``precision``: "bf16" (throughput mode), "tf32" (fp32 operands read as TF32), "tf32x3"
+    (error-compensated TF32, close to fp32) or None for SHOROKOO_B200_PRECISION (default bf16)."""
 
-    _PRECISIONS = {None: -1, "bf16": 0, "tf32": 1}
+    _PRECISIONS = {None: -1, "bf16": 0, "tf32": 1, "tf32x3": 2}
 
     def __init__(self, num_devices: int = 0, first_device: int = 0, precision: Optional[str] = None):
         if precision not in self._PRECISIONS:
-            raise ValueError(f"precision must be 'bf16', 'tf32' or None, got {precision!r}")
+            raise ValueError(f"precision must be 'bf16', 'tf32', 'tf32x3' or None, got {precision!r}")
         self.num_devices = num_devices
         self.first_device = first_device
         self.precision = precision

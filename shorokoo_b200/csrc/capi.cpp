@@ -155,8 +155,8 @@ int32_t sb_session_create_ex(const uint8_t* model, size_t len, int32_t, int32_t,
   return guarded([&] {
     SB_CHECK(out != nullptr, sb::SB_INVALID_ARGUMENT, "out is null");
     *out = nullptr;
-    SB_CHECK(precision >= SB_PRECISION_DEFAULT && precision <= SB_PRECISION_TF32, sb::SB_INVALID_ARGUMENT,
-             "precision must be SB_PRECISION_DEFAULT, _BF16 or _TF32");
+    SB_CHECK(precision >= SB_PRECISION_DEFAULT && precision <= SB_PRECISION_TF32X3, sb::SB_INVALID_ARGUMENT,
+             "precision must be SB_PRECISION_DEFAULT, _BF16, _TF32 or _TF32X3");
     SB_CHECK(model != nullptr || len == 0, sb::SB_INVALID_ARGUMENT, "model is null");
     sb::SessionOptions o;
     o.num_devices = num_devices;

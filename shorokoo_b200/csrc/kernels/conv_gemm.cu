@@ -470,18 +470,27 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
 // multiple of both, so each stage's full and empty barriers have exactly one producer and one
 // consumer, each moving through the stage's phases in order: no waiter can face a barrier two
 // phases behind (which a parity wait would mistake for done).
-template <int MODE>
-constexpr int kThreads = (MODE == 1 || MODE == 2) ? 448 : 512;
+// PREC: 0 bf16 operands (kind::f16); 1 fp32 operands read as TF32 (kind::tf32); 2 error-
+// compensated TF32 ("TF32x3"): every operand x = hi + lo with hi its TF32 truncation, three MMAs
+// per K slice (hi*hi + hi*lo + lo*hi) give close to fp32 accuracy. The weights' hi / lo matrices
+// come from the host (lo rows start at a.w_lo_row); the activation's lo tile is computed per stage
+// in shared memory by warps 14-15 once the stage has landed.
+template <int MODE, int PREC>
+constexpr int kThreads = ((MODE == 1 || MODE == 2) && PREC != 2) ? 448 : 512;
 
-template <int BN, int MODE, bool TF32>
-__global__ void __launch_bounds__(kThreads<MODE>, 1)
+template <int BN, int MODE, int PREC>
+__global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
     conv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
                      const ConvGemmArgs a) {
+  constexpr bool TF32 = PREC >= 1;
+  constexpr bool X3 = PREC == 2;
   constexpr int EB = TF32 ? 4 : 2;        // operand element bytes
   constexpr int BKE = 128 / EB;           // operand elements per 128-byte k-tile row
   constexpr uint32_t A_BYTES = BM * 128;
   constexpr uint32_t B_BYTES = BN * 128;
+  constexpr uint32_t A_STAGE = X3 ? 2 * A_BYTES : A_BYTES;   // X3: hi tile, then its lo tile
+  constexpr uint32_t B_STAGE = X3 ? 2 * B_BYTES : B_BYTES;
   const int PL = a.mma_lanes;                 // split-K partial accumulators per tile
   const uint32_t TMEM_COLS = uint32_t(2 * PL * BN);
   const int PE = PL;                          // at most KT, so every partial gets a k-tile
@@ -495,8 +504,8 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
   const int KT = a.Kpad / BKE;
   const bool BRES = A_TMA && a.b_resident;   // weights loaded once: slot kt holds k-tile kt
   uint8_t* sA = smem;
-  uint8_t* sB = sA + STAGES * A_BYTES;
-  uint8_t* sOut = sB + (BRES ? KT : STAGES) * B_BYTES;
+  uint8_t* sB = sA + STAGES * A_STAGE;
+  uint8_t* sOut = sB + (BRES ? KT * B_BYTES : STAGES * B_STAGE);
   const int OB = a.out_bufs;
   float* sBias = reinterpret_cast<float*>(sOut + 8 * OB * kOutSlab);
   uint8_t* sRes = sOut + 8 * OB * kOutSlab + kBiasStage;
@@ -507,7 +516,8 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
   uint64_t* resf = acce + 2;
   uint64_t* rese = resf + 2;
   uint64_t* bfull = rese + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bfull + 1);
+  uint64_t* split = bfull + 1;   // X3: the stage's activation lo tile is ready
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(split + kMaxStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -525,6 +535,8 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
       mbar_init(&rese[i], 8u);
     }
     mbar_init(bfull, 1u);
+    if (X3)
+      for (int s = 0; s < STAGES; ++s) mbar_init(&split[s], 64u);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -595,12 +607,12 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
             continue;
           }
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) goto producer_done;
-          mbar_expect_tx(&full[stage], (A_TMA ? A_BYTES : 0u) + (BRES ? 0u : B_BYTES));
-          if (MODE == 0) tma_load_2d(sA + stage * A_BYTES, &tmA, kt * BKE, mt * BM, &full[stage]);
+          mbar_expect_tx(&full[stage], (A_TMA ? A_BYTES : 0u) + (BRES ? 0u : B_STAGE));
+          if (MODE == 0) tma_load_2d(sA + stage * A_STAGE, &tmA, kt * BKE, mt * BM, &full[stage]);
           if (MODE == 3) {
             const int tap = kt / cblocks, cb = kt - tap * cblocks;
             const int kh = tap / a.KW, kw = tap - (tap / a.KW) * a.KW;
-            tma_load_im2col(sA + stage * A_BYTES, &tmA, cb * BKE, cw, ch, img, uint16_t(kw * a.dw),
+            tma_load_im2col(sA + stage * A_STAGE, &tmA, cb * BKE, cw, ch, img, uint16_t(kw * a.dw),
                             uint16_t(kh * a.dh), &full[stage]);
           }
           if (MODE == 4) {   // four 16-channel taps, one 4 KB sub-tile each
@@ -608,11 +620,12 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
             for (int j = 0; j < 4; ++j) {
               const int tap = kt * 4 + j;
               const int kh = tap / a.KW, kw = tap - (tap / a.KW) * a.KW;
-              tma_load_im2col(sA + stage * A_BYTES + j * (BM * 32), &tmA, 0, cw, ch, img, uint16_t(kw * a.dw),
+              tma_load_im2col(sA + stage * A_STAGE + j * (BM * 32), &tmA, 0, cw, ch, img, uint16_t(kw * a.dw),
                               uint16_t(kh * a.dh), &full[stage]);
             }
           }
-          if (!BRES) tma_load_2d(sB + stage * B_BYTES, &tmB, kt * BKE, nt * BN, &full[stage]);
+          if (!BRES) tma_load_2d(sB + stage * B_STAGE, &tmB, kt * BKE, nt * BN, &full[stage]);
+          if (X3) tma_load_2d(sB + stage * B_STAGE + B_BYTES, &tmB, kt * BKE, a.w_lo_row + nt * BN, &full[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -621,6 +634,40 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
       }
     producer_done:;
     }
+  } else if (X3 && warp >= 14) {
+    // ---- X3: activation lo tiles. x = hi + lo with hi = x truncated to TF32 (what the MMA reads
+    // from the fp32 tile) and lo = x - hi (exact in fp32), stored rounded to TF32 so the MMA's read
+    // of it is exact and the dropped part is unbiased (a truncated lo would bias every product
+    // toward zero, an error growing with K). Infinities / NaNs get lo = 0. ----------------------
+    const int sid = threadIdx.x - 14 * 32;   // 0..63
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      for (int kt = 0; kt < KT; ++kt) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, a.err, 256u)) goto split_done;
+        const uint4* src = reinterpret_cast<const uint4*>(sA + stage * A_STAGE);
+        uint4* dst = reinterpret_cast<uint4*>(sA + stage * A_STAGE + A_BYTES);
+#pragma unroll 4
+        for (int i = sid; i < int(A_BYTES / 16); i += 64) {
+          const uint4 u = src[i];
+          uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float x = __uint_as_float(w[j]);
+            const float hi = __uint_as_float(w[j] & 0xFFFFE000u);
+            w[j] = (w[j] & 0x7F800000u) == 0x7F800000u ? 0u : __float_as_uint(tf32_rna(x - hi));
+          }
+          dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        fence_async_smem();   // generic writes -> the MMA's async-proxy reads
+        mbar_arrive(&split[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  split_done:;
   } else if (warp == 1 || (A_TMA && warp >= 13)) {
     // Issuer `mid` (lane 0 of warp 1, 13, 14 or 15) issues the MMAs of the k-tiles with sequence
     // number g = mid (mod PE) into its own partial accumulator: one thread sustains only about one
@@ -646,20 +693,31 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
         // this issuer's k-tiles of the tile: g0 <= g < g0 + KT with g = mid (mod PE)
         for (bool first = true; g < g0 + KT; first = false) {
           const int kt = g - g0;
-          if (!mbar_wait(&full[stage], phase, abort_flag, a.err, 4u)) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, a.err, 4u) ||
+              (X3 && !mbar_wait(&split[stage], phase, abort_flag, a.err, 512u))) {
             ok = false;
             break;
           }
           tc_fence_after();
           if (GATHER) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          const uint64_t ad = sw128_desc(smem_u32(sA + stage * A_BYTES));
-          const uint64_t bd = sw128_desc(smem_u32(sB + (BRES ? kt : stage) * B_BYTES));
+          const uint64_t ad = sw128_desc(smem_u32(sA + stage * A_STAGE));
+          const uint64_t bd = sw128_desc(smem_u32(BRES ? sB + kt * B_BYTES : sB + stage * B_STAGE));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {   // four 32-byte K slices per 128-byte row
-            const uint64_t akk = MODE == 4 ? sw32_desc(smem_u32(sA + stage * A_BYTES + kk * (BM * 32)))
+            const uint64_t akk = MODE == 4 ? sw32_desc(smem_u32(sA + stage * A_STAGE + kk * (BM * 32)))
                                            : ad + uint64_t(kk * 2);
-            if (TF32) umma_tf32(d_tmem, akk, bd + uint64_t(kk * 2), idesc, (!first || kk != 0) ? 1u : 0u);
-            else umma_bf16(d_tmem, akk, bd + uint64_t(kk * 2), idesc, (!first || kk != 0) ? 1u : 0u);
+            const uint32_t accum = (!first || kk != 0) ? 1u : 0u;
+            if (X3) {
+              const uint64_t alo = sw128_desc(smem_u32(sA + stage * A_STAGE + A_BYTES)) + uint64_t(kk * 2);
+              const uint64_t blo = sw128_desc(smem_u32(sB + stage * B_STAGE + B_BYTES)) + uint64_t(kk * 2);
+              umma_tf32(d_tmem, akk, bd + uint64_t(kk * 2), idesc, accum);
+              umma_tf32(d_tmem, akk, blo, idesc, 1u);
+              umma_tf32(d_tmem, alo, bd + uint64_t(kk * 2), idesc, 1u);
+            } else if (TF32) {
+              umma_tf32(d_tmem, akk, bd + uint64_t(kk * 2), idesc, accum);
+            } else {
+              umma_bf16(d_tmem, akk, bd + uint64_t(kk * 2), idesc, accum);
+            }
           }
           umma_commit(&empty[stage]);
           g += PE;
@@ -786,7 +844,7 @@ __global__ void __launch_bounds__(kThreads<MODE>, 1)
       }
       for (int kt = 0; kt < KT; ++kt) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 16u)) goto gather_done;
-        const uint32_t sbase = smem_u32(sA + stage * A_BYTES);
+        const uint32_t sbase = smem_u32(sA + stage * A_STAGE);
         if (MODE == 1) {
           const int kidx = kt * BKE + sub * (16 / EB);
           const int tap = kidx / a.Cp;
@@ -902,7 +960,7 @@ bool encode_im2col(CUtensorMap* tm, const ConvGemmArgs& a, int cpp) {
 
 // The dynamic shared-memory opt-in is a per-device function attribute; it is set while preparing
 // a plan (never during stream capture).
-template <int BN, int MODE, bool TF32>
+template <int BN, int MODE, int PREC>
 cudaError_t ensure_attr() {
   static std::atomic<uint64_t> done_mask{0};
   int dev = 0;
@@ -910,54 +968,61 @@ cudaError_t ensure_attr() {
   const uint64_t bit = uint64_t(1) << (dev & 63);
   if (done_mask.load() & bit) return cudaSuccess;
   cudaError_t e =
-      cudaFuncSetAttribute(conv_gemm_kernel<BN, MODE, TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+      cudaFuncSetAttribute(conv_gemm_kernel<BN, MODE, PREC>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
   if (e == cudaSuccess) done_mask.fetch_or(bit);
   return e;
 }
 
-template <int BN, int MODE, bool TF32>
+template <int BN, int MODE, int PREC>
 cudaError_t launch_t(const ConvGemmPlan& p, cudaStream_t s) {
-  conv_gemm_kernel<BN, MODE, TF32><<<p.grid, kThreads<MODE>, p.smem, s>>>(p.tmA, p.tmB, p.tmOut, p.tmRes, p.args);
+  conv_gemm_kernel<BN, MODE, PREC><<<p.grid, kThreads<MODE, PREC>, p.smem, s>>>(p.tmA, p.tmB, p.tmOut, p.tmRes, p.args);
   return cudaGetLastError();
 }
 
-// TF32 operands use the row-matrix, 16-byte gather and 128-byte im2col modes only.
-template <int BN>
-cudaError_t ensure_attr_mode(int mode, bool tf32) {
-  if (tf32) {
-    switch (mode) {
-      case 0: return ensure_attr<BN, 0, true>();
-      case 1: return ensure_attr<BN, 1, true>();
-      case 3: return ensure_attr<BN, 3, true>();
-      default: return cudaErrorInvalidValue;
-    }
-  }
+// TF32 / TF32x3 operands use the row-matrix, 16-byte gather and 128-byte im2col modes only.
+template <int BN, int PREC>
+cudaError_t ensure_attr_f32(int mode) {
   switch (mode) {
-    case 0: return ensure_attr<BN, 0, false>();
-    case 1: return ensure_attr<BN, 1, false>();
-    case 2: return ensure_attr<BN, 2, false>();
-    case 3: return ensure_attr<BN, 3, false>();
-    case 4: return ensure_attr<BN, 4, false>();
+    case 0: return ensure_attr<BN, 0, PREC>();
+    case 1: return ensure_attr<BN, 1, PREC>();
+    case 3: return ensure_attr<BN, 3, PREC>();
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int BN>
+cudaError_t ensure_attr_mode(int mode, int prec) {
+  if (prec == 1) return ensure_attr_f32<BN, 1>(mode);
+  if (prec == 2) return ensure_attr_f32<BN, 2>(mode);
+  switch (mode) {
+    case 0: return ensure_attr<BN, 0, 0>();
+    case 1: return ensure_attr<BN, 1, 0>();
+    case 2: return ensure_attr<BN, 2, 0>();
+    case 3: return ensure_attr<BN, 3, 0>();
+    case 4: return ensure_attr<BN, 4, 0>();
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int BN, int PREC>
+cudaError_t launch_f32(const ConvGemmPlan& p, cudaStream_t s) {
+  switch (p.mode) {
+    case 0: return launch_t<BN, 0, PREC>(p, s);
+    case 1: return launch_t<BN, 1, PREC>(p, s);
+    case 3: return launch_t<BN, 3, PREC>(p, s);
     default: return cudaErrorInvalidValue;
   }
 }
 
 template <int BN>
 cudaError_t launch_mode(const ConvGemmPlan& p, cudaStream_t s) {
-  if (p.args.tf32) {
-    switch (p.mode) {
-      case 0: return launch_t<BN, 0, true>(p, s);
-      case 1: return launch_t<BN, 1, true>(p, s);
-      case 3: return launch_t<BN, 3, true>(p, s);
-      default: return cudaErrorInvalidValue;
-    }
-  }
+  if (p.args.tf32) return p.args.x3 ? launch_f32<BN, 2>(p, s) : launch_f32<BN, 1>(p, s);
   switch (p.mode) {
-    case 0: return launch_t<BN, 0, false>(p, s);
-    case 1: return launch_t<BN, 1, false>(p, s);
-    case 2: return launch_t<BN, 2, false>(p, s);
-    case 3: return launch_t<BN, 3, false>(p, s);
-    case 4: return launch_t<BN, 4, false>(p, s);
+    case 0: return launch_t<BN, 0, 0>(p, s);
+    case 1: return launch_t<BN, 1, 0>(p, s);
+    case 2: return launch_t<BN, 2, 0>(p, s);
+    case 3: return launch_t<BN, 3, 0>(p, s);
+    case 4: return launch_t<BN, 4, 0>(p, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -1007,7 +1072,8 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   // Tile width: widest N tile that still gives at least one tile per SM; residual convs use at most
   // 128 so two residual tiles fit beside a deep operand pipeline.
   auto tiles = [&](int bn) { return int64_t((a.M + BM - 1) / BM) * ((a.Cout + bn - 1) / bn); };
-  int bn = a.Cout <= 64 ? 64 : (a.Cout <= 128 || res_ring ? 128 : 256);
+  // (TF32x3 stages hold hi and lo tiles: at most 128 columns so two stages fit)
+  int bn = a.Cout <= 64 ? 64 : (a.Cout <= 128 || res_ring || a.x3 ? 128 : 256);
   while (bn > 64 && tiles(bn) < num_sms) bn /= 2;
   p.bn = bn;
   p.mode = conv_gemm_a_mode(a);
@@ -1017,7 +1083,7 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   if (a.Kpad % bke) throw std::runtime_error("conv_gemm: reduction length not padded to a whole k-tile");
   const int KT = a.Kpad / bke;
   const int64_t w_bytes = int64_t(KT) * bn * 128;
-  bool bres = p.mode != kAGather16 && p.mode != kAGather8 && a.Cout <= bn && w_bytes <= 96 * 1024;
+  bool bres = !a.x3 && p.mode != kAGather16 && p.mode != kAGather8 && a.Cout <= bn && w_bytes <= 96 * 1024;
   if (const char* e = std::getenv("SHOROKOO_B200_BRES"))
     if (e[0] == '0') bres = false;
   a.b_resident = bres ? 1 : 0;
@@ -1034,12 +1100,12 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   // without waiting for the stores (measured on ResNet-50: in place there costs 5-6%).
   const bool inplace_hint = res_ring && out_ok && KT >= 8;
   // (the cp.async gather modes have no spare warps: their warps 10-13 gather, so one issuer)
-  int pl = !gather && (im2col || inplace_hint) && bn <= 128 ? 2 : 1;
+  int pl = !a.x3 && !gather && (im2col || inplace_hint) && bn <= 128 ? 2 : 1;   // X3: warps 13-15 split
   if (const char* e = std::getenv("SHOROKOO_B200_MMA_LANES")) pl = std::max(1, std::min(pl, std::atoi(e)));
   while (pl > KT) pl /= 2;
   if (gather && pl != 1) throw std::runtime_error("conv_gemm: gather modes have a single MMA issuer");
   a.mma_lanes = pl;
-  const int stage_bytes = BM * 128 + (bres ? 0 : bn * 128);
+  const int stage_bytes = (BM * 128 + (bres ? 0 : bn * 128)) * (a.x3 ? 2 : 1);
   const int rsb = 128 * bn * es;
   // Output and residual tensor maps first: whether the epilogue stores through TMA and streams the
   // residual through a ring decides the shared-memory plan.
@@ -1056,15 +1122,17 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   // drain while the next slab is computed, but measured on ResNet-50 the operand stages it costs
   // are worth more, so it is opt-in (SHOROKOO_B200_OUTBUF=2).
   auto fixed_for = [&](int ob) { return int(8 * ob * kOutSlab + kBiasStage) + 1024 + 512 + (bres ? int(w_bytes) : 0); };
-  auto ring_for = [&](int ob) {
+  auto ring_for = [&](int ob) {   // residual slots that still leave two operand stages (0: direct reads)
     if (!ring) return 0;
-    return (kSmemLimit - fixed_for(ob) - 2 * rsb) / stage_bytes >= 2 ? 2 : 1;
+    if ((kSmemLimit - fixed_for(ob) - 2 * rsb) / stage_bytes >= 2) return 2;
+    return (kSmemLimit - fixed_for(ob) - rsb) / stage_bytes >= 2 ? 1 : 0;
   };
   auto stages_for = [&](int ob, int rs) { return std::min(kMaxStages, (kSmemLimit - fixed_for(ob) - rs * rsb) / stage_bytes); };
   int ob = ring && KT >= 8 ? 0 : 1;
   if (ob != 0)
     if (const char* e = std::getenv("SHOROKOO_B200_OUTBUF")) ob = std::atoi(e) == 2 ? 2 : 1;
   int rs = ring_for(ob);
+  if (rs == 0 && ob == 0) ob = 1;   // writing in place needs a residual ring
   const int smax = stages_for(ob, rs);
   // Producers and stages. With one MMA issuer the stages are consumed in order, and at least as
   // many stages as producers keeps every barrier wait within one phase. With several issuers the
@@ -1100,8 +1168,10 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   int64_t t = tiles(bn);
   p.grid = int(t < num_sms ? t : num_sms);
   const int eb = a.tf32 ? 4 : 2;
-  bool ok = encode_2d(&p.tmB, w, uint64_t(a.Kpad), uint64_t(a.Cout), uint64_t(a.Kpad) * eb, uint32_t(bke), uint32_t(bn),
-                      a.tf32 != 0);
+  if (a.x3 && (a.w_lo_row < a.Cout || a.w_lo_row % bn))
+    throw std::runtime_error("conv_gemm: TF32x3 weights need their lo rows after a BN-padded hi block");
+  bool ok = encode_2d(&p.tmB, w, uint64_t(a.Kpad), uint64_t(a.x3 ? 2 * a.w_lo_row : a.Cout), uint64_t(a.Kpad) * eb,
+                      uint32_t(bke), uint32_t(bn), a.tf32 != 0);
   if (p.mode == kARows)
     ok = ok && encode_2d(&p.tmA, a_rows, uint64_t(lda), uint64_t(a.M), uint64_t(lda) * eb, uint32_t(bke), BM, a.tf32 != 0);
   if (!ok) throw std::runtime_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad layout)");
@@ -1110,9 +1180,9 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   a.res_slots = rs;
   a.res_slot_bytes = rs ? rsb : 0;
   const int mode = p.mode;
-  const bool tf = a.tf32 != 0;
-  cudaError_t e = bn == 64 ? ensure_attr_mode<64>(mode, tf)
-                           : (bn == 128 ? ensure_attr_mode<128>(mode, tf) : ensure_attr_mode<256>(mode, tf));
+  const int prec = a.tf32 ? (a.x3 ? 2 : 1) : 0;
+  cudaError_t e = bn == 64 ? ensure_attr_mode<64>(mode, prec)
+                           : (bn == 128 ? ensure_attr_mode<128>(mode, prec) : ensure_attr_mode<256>(mode, prec));
   if (e != cudaSuccess) throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
 }
 

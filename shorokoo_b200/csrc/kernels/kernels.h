@@ -49,6 +49,8 @@ struct ConvGemmArgs {
   int tf32;                // 0: bf16 operands (kind::f16, 64 per k-tile row); 1: fp32 operands
                            // multiplied as TF32 (kind::tf32, 32 per 128-byte k-tile row)
   int round_tf32;          // fp32 output rounded to the TF32 grid (it feeds TF32 MMAs)
+  int x3;                  // with tf32: error-compensated TF32 (hi*hi + hi*lo + lo*hi per K slice)
+  int w_lo_row;            // x3: row of the weights' lo matrix (hi rows 0..Cout-1, zero to w_lo_row)
   int producers;           // TMA producer threads Q (1-4): thread q loads k-tiles g = q mod Q
                            // (stages is a multiple of P and Q, so every stage has one producer
                            // and one consumer, each in order)
@@ -97,12 +99,13 @@ cudaError_t to_nhwc_bf16(const void* src, int src_bf16, const int64_t* shape4, c
 // dst[n, hs, ws, (p*2+q)*C + c] = src[n, c, 2hs+p, 2ws+q], zero outside the image and in channels 4C..15.
 cudaError_t to_s2d_bf16(const void* src, int src_bf16, const int64_t* shape4, const int64_t* stride4, void* dst,
                         int64_t Hs, int64_t Ws, cudaStream_t s);
-// The same conversions into fp32 operands for the TF32 path (values rounded to the TF32 grid):
-// NHWC fp32 [N,H,W,Cp] (Cp % 4 == 0) and rows fp32 [M, Kp].
+// The same conversions into fp32 operands for the TF32 paths: NHWC fp32 [N,H,W,Cp] (Cp % 4 == 0)
+// and rows fp32 [M, Kp]; values rounded to the TF32 grid when round_tf32 (single-pass TF32), kept
+// exact for TF32x3.
 cudaError_t to_nhwc_f32(const void* src, int src_bf16, const int64_t* shape4, const int64_t* stride4, void* dst,
-                        int Cp, cudaStream_t s);
+                        int Cp, int round_tf32, cudaStream_t s);
 cudaError_t to_rows_f32(const void* src, int src_bf16, int64_t M, int64_t K, int64_t sm, int64_t sk, void* dst,
-                        int64_t Kp, cudaStream_t s);
+                        int64_t Kp, int round_tf32, cudaStream_t s);
 // NHWC fp32 max pooling (C % 4 == 0).
 cudaError_t maxpool_nhwc_f32(const void* x, void* y, int N, int H, int W, int C, int Ho, int Wo, int kh, int kw,
                              int sh, int sw, int ph, int pw, int dh, int dw, cudaStream_t s);

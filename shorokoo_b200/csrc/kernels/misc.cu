@@ -105,7 +105,7 @@ __device__ __forceinline__ float tf32_rna(float x) {
 // dst (NHWC fp32 [N,H,W,Cp], TF32-rounded) <- src logical [N,C,H,W], 4 channels per thread.
 __global__ void to_nhwc_f32_kernel(const void* __restrict__ src, int src_bf16, int64_t N, int64_t C, int64_t H,
                                    int64_t W, int64_t s0, int64_t s1, int64_t s2, int64_t s3, float* __restrict__ dst,
-                                   int Cp) {
+                                   int Cp, int rnd) {
   const int groups = Cp / 4;
   const int64_t total = N * H * W * groups;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
@@ -120,18 +120,20 @@ __global__ void to_nhwc_f32_kernel(const void* __restrict__ src, int src_bf16, i
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int64_t c = int64_t(g) * 4 + j;
-      v[j] = tf32_rna(c < C ? ld_any(src, src_bf16, base + c * s1) : 0.f);
+      const float x = c < C ? ld_any(src, src_bf16, base + c * s1) : 0.f;
+      v[j] = rnd ? tf32_rna(x) : x;
     }
     *reinterpret_cast<float4*>(dst + pix * Cp + g * 4) = make_float4(v[0], v[1], v[2], v[3]);
   }
 }
 
 __global__ void to_rows_f32_kernel(const void* __restrict__ src, int src_bf16, int64_t M, int64_t K, int64_t sm,
-                                   int64_t sk, float* __restrict__ dst, int64_t Kp) {
+                                   int64_t sk, float* __restrict__ dst, int64_t Kp, int rnd) {
   const int64_t total = M * Kp;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t m = i / Kp, kk = i - m * Kp;
-    dst[i] = tf32_rna(kk < K ? ld_any(src, src_bf16, m * sm + kk * sk) : 0.f);
+    const float x = kk < K ? ld_any(src, src_bf16, m * sm + kk * sk) : 0.f;
+    dst[i] = rnd ? tf32_rna(x) : x;
   }
 }
 
@@ -417,17 +419,18 @@ cudaError_t to_nhwc_bf16(const void* src, int src_bf16, const int64_t* sh, const
 }
 
 cudaError_t to_nhwc_f32(const void* src, int src_bf16, const int64_t* sh, const int64_t* st, void* dst, int Cp,
-                        cudaStream_t s) {
+                        int round_tf32, cudaStream_t s) {
   if (Cp % 4) return cudaErrorInvalidValue;
   const int64_t total = sh[0] * sh[2] * sh[3] * (Cp / 4);
   to_nhwc_f32_kernel<<<grid_for(total), kThreads, 0, s>>>(src, src_bf16, sh[0], sh[1], sh[2], sh[3], st[0], st[1], st[2],
-                                                          st[3], reinterpret_cast<float*>(dst), Cp);
+                                                          st[3], reinterpret_cast<float*>(dst), Cp, round_tf32);
   return cudaGetLastError();
 }
 
 cudaError_t to_rows_f32(const void* src, int src_bf16, int64_t M, int64_t K, int64_t sm, int64_t sk, void* dst,
-                        int64_t Kp, cudaStream_t s) {
-  to_rows_f32_kernel<<<grid_for(M * Kp), kThreads, 0, s>>>(src, src_bf16, M, K, sm, sk, reinterpret_cast<float*>(dst), Kp);
+                        int64_t Kp, int round_tf32, cudaStream_t s) {
+  to_rows_f32_kernel<<<grid_for(M * Kp), kThreads, 0, s>>>(src, src_bf16, M, K, sm, sk, reinterpret_cast<float*>(dst), Kp,
+                                                           round_tf32);
   return cudaGetLastError();
 }
 

@@ -142,8 +142,8 @@ inline void ck(cudaError_t e, const char* what) {
 }  // namespace
 
 // ---------------------------------------------------------------------------------------------
-Plan::Plan(LGraph g, int device, int num_sms, bool tf32)
-    : g_(std::move(g)), device_(device), num_sms_(num_sms), tf32_(tf32) {
+Plan::Plan(LGraph g, int device, int num_sms, int precision)
+    : g_(std::move(g)), device_(device), num_sms_(num_sms), tf32_(precision >= 1), x3_(precision == 2) {
   fuse(g_);
   build();
   allocate_and_finalize();
@@ -188,21 +188,41 @@ DevTensor Plan::alloc_nhwc(const std::vector<int64_t>& s, bool bf16, int64_t cst
   return t;
 }
 
-// Tensor-core weights in the operand dtype: bf16 (round to nearest even), or fp32 rounded to the
-// TF32 grid (10 explicit mantissa bits, nearest even) so the MMA's read of them is exact.
-int64_t Plan::add_operand_weights(const std::vector<float>& w) {
+// Tensor-core weights [rows, K] in the operand dtype: bf16 (round to nearest even), or fp32
+// rounded to the TF32 grid (10 explicit mantissa bits, nearest even) so the MMA's read of them is
+// exact. TF32x3: the TF32-rounded hi matrix, zero rows up to *lo_row (rows rounded up to 256),
+// then the lo matrix w - hi rounded to TF32 (unbiased, and read exactly by the MMA).
+int64_t Plan::add_operand_weights(const std::vector<float>& w, int64_t rows, int64_t* lo_row) {
+  if (lo_row) *lo_row = 0;
   if (!tf32_) {
     std::vector<uint16_t> b(w.size());
     for (size_t i = 0; i < w.size(); ++i) b[i] = f32_to_bf16_rne(w[i]);
     return add_weight_bytes(b.data(), b.size() * 2);
   }
-  std::vector<uint32_t> f(w.size());
-  for (size_t i = 0; i < w.size(); ++i) {
+  auto tf32_rne = [](float x) {
     uint32_t u;
-    std::memcpy(&u, &w[i], 4);
+    std::memcpy(&u, &x, 4);
     if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0xFFFu + ((u >> 13) & 1u)) & ~0x1FFFu;   // finite values only
-    f[i] = u;
+    float r;
+    std::memcpy(&r, &u, 4);
+    return r;
+  };
+  if (!x3_) {
+    std::vector<float> f(w.size());
+    for (size_t i = 0; i < w.size(); ++i) f[i] = tf32_rne(w[i]);
+    return add_weight_bytes(f.data(), f.size() * 4);
   }
+  const int64_t K = rows ? int64_t(w.size()) / rows : 0;
+  const int64_t lo = round_up(rows, 256);
+  std::vector<float> f(size_t(2 * lo * K), 0.f);
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t k = 0; k < K; ++k) {
+      const float x = w[size_t(r * K + k)];
+      const float hi = tf32_rne(x);
+      f[size_t(r * K + k)] = hi;
+      f[size_t((lo + r) * K + k)] = std::isfinite(x) ? tf32_rne(x - hi) : 0.f;   // lo, itself on the TF32 grid
+    }
+  if (lo_row) *lo_row = lo;
   return add_weight_bytes(f.data(), f.size() * 4);
 }
 
@@ -287,14 +307,15 @@ DevTensor Plan::as_nhwc_op(int v, int Cp) {
   if (it != conv_cache_.end()) return it->second;
   DevTensor dst = alloc_nhwc({N, C, H, W}, !tf32_, Cp);
   const bool f32 = tf32_;
-  add_step(f32 ? "to_nhwc_f32" : "to_nhwc_bf16", {t}, {dst}, [this, t, dst, Cp, f32]() {
+  const int rnd = tf32_ && !x3_;
+  add_step(f32 ? "to_nhwc_f32" : "to_nhwc_bf16", {t}, {dst}, [this, t, dst, Cp, f32, rnd]() {
     const void* sp = ptr(t);
     void* dp = ptr(dst);
     int64_t sh[4] = {t.shape[0], t.shape[1], t.shape[2], t.shape[3]};
     int64_t st[4] = {t.strides[0], t.strides[1], t.strides[2], t.strides[3]};
     int sb = t.bf16;
     return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
-      return f32 ? k::to_nhwc_f32(sp, sb, sh, st, dp, Cp, s) : k::to_nhwc_bf16(sp, sb, sh, st, dp, Cp, s);
+      return f32 ? k::to_nhwc_f32(sp, sb, sh, st, dp, Cp, rnd, s) : k::to_nhwc_bf16(sp, sb, sh, st, dp, Cp, s);
     });
   });
   conv_cache_[key] = dst;
@@ -325,13 +346,14 @@ DevTensor Plan::as_rows_op(int v, int64_t M, int64_t K) {
   const int64_t Kp = round_up(K, tf32_ ? 4 : 8);
   DevTensor dst = alloc_contig({M, Kp}, !tf32_);
   const bool f32 = tf32_;
-  add_step(f32 ? "to_rows_f32" : "to_rows_bf16", {t}, {dst}, [this, t, dst, M, K, Kp, f32]() {
+  const int rnd = tf32_ && !x3_;
+  add_step(f32 ? "to_rows_f32" : "to_rows_bf16", {t}, {dst}, [this, t, dst, M, K, Kp, f32, rnd]() {
     const void* sp = ptr(t);
     void* dp = ptr(dst);
     int64_t sm = t.strides[0], sk = t.strides[1];
     int sb = t.bf16;
     return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
-      return f32 ? k::to_rows_f32(sp, sb, M, K, sm, sk, dp, Kp, s) : k::to_rows_bf16(sp, sb, M, K, sm, sk, dp, Kp, s);
+      return f32 ? k::to_rows_f32(sp, sb, M, K, sm, sk, dp, Kp, rnd, s) : k::to_rows_bf16(sp, sb, M, K, sm, sk, dp, Kp, s);
     });
   });
   rows_cache_[v] = dst;
@@ -419,7 +441,8 @@ void Plan::plan_conv(const Op& op) {
         }
   DevTensor wt;
   wt.buf = -1;
-  wt.off = add_operand_weights(wf);
+  int64_t w_lo_row = 0;
+  wt.off = add_operand_weights(wf, Cout, &w_lo_row);
   std::vector<float> bias(size_t(round_up(Cout, 256)), 0.f);
   for (int64_t m = 0; m < Cout; ++m) bias[size_t(m)] = op.bias ? op.bias->ptr<float>()[m] : 0.f;
   DevTensor bt;
@@ -457,7 +480,8 @@ void Plan::plan_conv(const Op& op) {
   if (r.valid()) reads.push_back(r);
   const int sms = num_sms_;
   const bool f32 = tf32_;
-  const bool round_out = tf32_ && feeds_tensor_ops(op.out[0]);   // next MMA reads it as TF32
+  const bool round_out = tf32_ && !x3_ && feeds_tensor_ops(op.out[0]);   // next MMA reads it as TF32
+  const int x3 = x3_;
   k::ConvGemmArgs geo;   // geometry only: how the kernel will fetch A (for the step's label)
   std::memset(&geo, 0, sizeof(geo));
   geo.gather = one_by_one ? 0 : 1;
@@ -517,6 +541,8 @@ void Plan::plan_conv(const Op& op) {
     a.err = err_;
     a.tf32 = f32;
     a.round_tf32 = round_out;
+    a.x3 = x3;
+    a.w_lo_row = int(w_lo_row);
     k::conv_gemm_prepare(*p, ptr(x), Cp, ptr(wt), sms);
     return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::conv_gemm_launch(*p, s); });
   });
@@ -539,7 +565,8 @@ void Plan::plan_gemm(const Op& op) {
     for (int64_t kk = 0; kk < K; ++kk) wf[size_t(n * Kpad + kk)] = wp[n * K + kk];
   DevTensor wt;
   wt.buf = -1;
-  wt.off = add_operand_weights(wf);
+  int64_t w_lo_row = 0;
+  wt.off = add_operand_weights(wf, Nn, &w_lo_row);
   std::vector<float> bias(size_t(round_up(Nn, 256)), 0.f);
   for (int64_t n = 0; n < Nn; ++n) bias[size_t(n)] = op.bias ? op.bias->ptr<float>()[n] : 0.f;
   DevTensor bt;
@@ -559,7 +586,8 @@ void Plan::plan_gemm(const Op& op) {
   if (r.valid()) reads.push_back(r);
   const int sms = num_sms_;
   const bool f32 = tf32_;
-  const bool round_out = tf32_ && feeds_tensor_ops(op.out[0]);   // next MMA reads it as TF32
+  const bool round_out = tf32_ && !x3_ && feeds_tensor_ops(op.out[0]);   // next MMA reads it as TF32
+  const int x3 = x3_;
   add_step("gemm " + std::to_string(M) + "x" + std::to_string(K) + "->" + std::to_string(Nn), reads, {y}, [=]() {
     auto p = std::make_shared<k::ConvGemmPlan>();
     k::ConvGemmArgs& a = p->args;
@@ -587,6 +615,8 @@ void Plan::plan_gemm(const Op& op) {
     a.err = err_;
     a.tf32 = f32;
     a.round_tf32 = round_out;
+    a.x3 = x3;
+    a.w_lo_row = int(w_lo_row);
     k::conv_gemm_prepare(*p, ptr(x), lda, ptr(wt), sms);
     return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::conv_gemm_launch(*p, s); });
   });

@@ -47,8 +47,8 @@ struct OutputBinding {
 
 class Plan {
  public:
-  // tf32: tensor-core operands are fp32 (TF32 MMA, the accuracy mode) instead of bf16.
-  Plan(LGraph g, int device, int num_sms, bool tf32 = false);
+  // precision: 0 bf16 operands; 1 fp32 operands read as TF32; 2 TF32x3 (error-compensated).
+  Plan(LGraph g, int device, int num_sms, int precision = 0);
   ~Plan();
   Plan(const Plan&) = delete;
   Plan& operator=(const Plan&) = delete;
@@ -89,6 +89,7 @@ class Plan {
   int device_;
   int num_sms_;
   bool tf32_ = false;   // operand dtype of the tensor-core path: fp32 (TF32 MMA) instead of bf16
+  bool x3_ = false;     // TF32x3: operands kept exact in fp32, weights split into hi / lo
   std::vector<DevTensor> vt_;       // per value id
   std::vector<Buffer> bufs_;
   std::vector<PendingStep> pending_;
@@ -113,7 +114,7 @@ class Plan {
   int new_buffer(size_t bytes);
   DevTensor alloc_contig(const std::vector<int64_t>& shape, bool bf16);
   DevTensor alloc_nhwc(const std::vector<int64_t>& shape_nchw, bool bf16, int64_t cstride);
-  int64_t add_operand_weights(const std::vector<float>& w);
+  int64_t add_operand_weights(const std::vector<float>& w, int64_t rows, int64_t* lo_row);
   int64_t add_weight_bytes(const void* data, size_t bytes);
   void* ptr(const DevTensor& t) const;
   void add_step(const std::string& kind, std::vector<DevTensor> reads, std::vector<DevTensor> writes,

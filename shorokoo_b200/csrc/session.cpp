@@ -257,7 +257,7 @@ Session::Session(const uint8_t* model, size_t len, const SessionOptions& opt) : 
     cudaGetLastError();
     fail(SB_CUDA_ERROR, "no CUDA device is available for the B200 backend");
   }
-  tf32_ = resolve_precision(opt.precision) == 1;
+  precision_ = resolve_precision(opt.precision);
   int want = opt.num_devices;
   if (want <= 0) {
     const char* e = std::getenv("SHOROKOO_B200_DEVICES");
@@ -285,8 +285,9 @@ int resolve_precision(int requested) {
   if (requested >= 0) return requested;
   const char* e = std::getenv("SHOROKOO_B200_PRECISION");
   const std::string v = e ? e : "bf16";
-  SB_CHECK(v == "bf16" || v == "tf32", SB_INVALID_ARGUMENT, "SHOROKOO_B200_PRECISION must be bf16 or tf32");
-  return v == "tf32" ? 1 : 0;
+  SB_CHECK(v == "bf16" || v == "tf32" || v == "tf32x3", SB_INVALID_ARGUMENT,
+           "SHOROKOO_B200_PRECISION must be bf16, tf32 or tf32x3");
+  return v == "tf32" ? 1 : (v == "tf32x3" ? 2 : 0);
 }
 
 Session::~Session() {
@@ -365,7 +366,7 @@ std::shared_ptr<Session::PlanSet> Session::get_plans(const std::vector<std::shar
     std::fprintf(stderr, "[shorokoo_b200] graph does not shard on the batch axis; running on one device\n");
   if (!shard) {
     ck(cudaSetDevice(devices_[0]), "cudaSetDevice");
-    ps->shards.push_back({0, 0, batch > 0 ? batch : 0, std::make_shared<Plan>(std::move(full), devices_[0], sm_counts_[0], tf32_)});
+    ps->shards.push_back({0, 0, batch > 0 ? batch : 0, std::make_shared<Plan>(std::move(full), devices_[0], sm_counts_[0], precision_)});
   } else {
     ps->sharded = true;
     const int parts = int(std::min<int64_t>(nd, batch));
@@ -384,7 +385,7 @@ std::shared_ptr<Session::PlanSet> Session::get_plans(const std::vector<std::shar
         try {
           cudaSetDevice(devices_[size_t(sh.device)]);
           LGraph g = lower(model_, specs_for(inputs, sh.begin, sh.count, true));
-          sh.plan = std::make_shared<Plan>(std::move(g), devices_[size_t(sh.device)], sm_counts_[size_t(sh.device)], tf32_);
+          sh.plan = std::make_shared<Plan>(std::move(g), devices_[size_t(sh.device)], sm_counts_[size_t(sh.device)], precision_);
         } catch (const Error& e) {
           errs[si] = e.what();
           codes[si] = e.code;
@@ -436,7 +437,7 @@ void Session::maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_pt
   try {
     ck(cudaSetDevice(P->device), "cudaSetDevice");
     LGraph g = lower(model_, specs_for(inputs, 0, P->chunk, true));
-    P->plan = std::make_shared<Plan>(std::move(g), P->device, sm_counts_[0], tf32_);
+    P->plan = std::make_shared<Plan>(std::move(g), P->device, sm_counts_[0], precision_);
     const auto& outs = P->plan->outputs();
     for (size_t j = 0; j < outs.size(); ++j)
       if (!outs[j].host && (outs[j].shape.empty() || outs[j].shape[0] != P->chunk || ps.out_shapes[j].empty() ||

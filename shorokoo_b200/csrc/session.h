@@ -35,7 +35,7 @@ struct HostValue {
 struct SessionOptions {
   int num_devices = 0;   // 0: SHOROKOO_B200_DEVICES or all visible devices
   int first_device = 0;
-  int precision = -1;    // -1: SHOROKOO_B200_PRECISION (bf16 | tf32, default bf16); 0 bf16; 1 tf32
+  int precision = -1;    // -1: SHOROKOO_B200_PRECISION (bf16 | tf32 | tf32x3, default bf16); 0, 1, 2
 };
 
 class Session {
@@ -95,7 +95,7 @@ class Session {
   OnnxModel model_;
   ModelInfo info_;
   SessionOptions opt_;
-  bool tf32_ = false;   // tensor-core operands fp32 read as TF32 (the accuracy mode)
+  int precision_ = 0;   // 0 bf16 operands, 1 TF32, 2 TF32x3 (the accuracy modes)
   std::vector<int> devices_;
   std::vector<int> sm_counts_;
   std::vector<cudaStream_t> streams_;
@@ -111,7 +111,8 @@ class Session {
 };
 
 bool batch_separable(const LGraph& g);
-// SB_PRECISION_DEFAULT (-1) -> SHOROKOO_B200_PRECISION (bf16 | tf32, default bf16); 0 bf16; 1 tf32.
+// SB_PRECISION_DEFAULT (-1) -> SHOROKOO_B200_PRECISION (bf16 | tf32 | tf32x3, default bf16);
+// 0 bf16; 1 tf32; 2 tf32x3.
 int resolve_precision(int requested);
 
 }  // namespace sb

@@ -1,4 +1,4 @@
-"""GPU parity of the TF32 accuracy mode (precision="tf32": fp32 operands read as TF32 by
+"""GPU parity of the TF32 accuracy modes (precision="tf32": fp32 operands read as TF32 by
 tcgen05.mma kind::tf32, fp32 accumulation, fp32 activations rounded to the TF32 grid) against the
 fp32 oracle at the TF32 gate, normwise max|gpu - ref| / max|ref| <= 2e-3 per output, and against
 the oracle with TF32-rounded operands (the mode's own arithmetic) more tightly."""
@@ -80,3 +80,41 @@ def test_tf32_retinanet_at_the_tf32_floor():
 def test_precision_is_validated():
     with pytest.raises(ValueError):
         B200InferenceSessionFactory(precision="fp8")
+
+
+# ---- TF32x3: error-compensated TF32 (x = hi + lo, hi*hi + hi*lo + lo*hi per K slice) ----------
+X3_TOL = 5e-5   # single convs / GEMMs land at 1e-6 - 3e-5 (fp32-accumulation bound)
+
+
+def _x3(case):
+    return run_backend(case, factory=B200InferenceSessionFactory(num_devices=1, precision="tf32x3"))
+
+
+@pytest.mark.parametrize("kw", [
+    dict(c=64, cout=256, k=1, pads=[0, 0, 0, 0], bn=True, residual=True, relu=True),  # rows + residual
+    dict(c=24, cout=40, k=3, h=11, w=7),                                           # gather
+    dict(n=2, c=64, cout=64, k=3, h=32, w=32, bn=True, relu=True),                 # im2col
+    dict(c=3, cout=64, k=7, stride=2, pads=[3, 3, 3, 3], h=32, w=32),              # stem
+    dict(c=128, cout=64, k=1, pads=[0, 0, 0, 0], h=10, w=16, upsample_residual=True),
+])
+def test_tf32x3_conv(kw):
+    case = conv_case(**kw)
+    got = _x3(case)[0]
+    assert_close(got, run_oracle(case)[0], tol=X3_TOL, what=f"tf32x3 conv {kw}")
+
+
+def test_tf32x3_gemm():
+    case = graphs.mlp(batch=513, widths=(1024, 4096, 100), seed=3, bias_scale=0.5)
+    assert_close(_x3(case)[0], run_oracle(case)[0], tol=X3_TOL, what="tf32x3 mlp")
+
+
+def test_tf32x3_retinanet_meets_the_tf32_gate():
+    """The graph at the single-pass TF32 floor: with error-compensated TF32 both detection outputs
+    meet the 2e-3 TF32 gate with margin (measured 4.5e-4 / 2.2e-4). Single convs land at 1e-6 -
+    5e-6; what remains on deep graphs is the tensor core's fp32 accumulation, whose error grows
+    with the reduction length (3e-5 on one K=4096 GEMM with exact hi / lo operands)."""
+    case = graphs.retinanet(batch=1, hw=(128, 160))
+    got = _x3(case)
+    ref = run_oracle(case)
+    for g, r, o in zip(got, ref, case.output_names):
+        assert_close(g, r, tol=1e-3, what=f"tf32x3 retinanet {o} (2e-3 gate with margin)")
