@@ -418,33 +418,39 @@ void Session::maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_pt
   if (ps.pipe_checked) return;
   ps.pipe_checked = true;
   if (ps.sharded || ps.shards.size() != 1 || !ps.separable || ps.batch < 2) return;
-  // Chunks of at least kPipeMinChunk rows keep the kernels near their full-batch efficiency;
-  // below kPipeMinBytes of device input the copy is too short to be worth hiding.
-  constexpr int64_t kPipeMinChunk = 128;
+  // Below kPipeMinBytes of device input the copy is too short to be worth hiding. The head is a
+  // sixteenth of the batch (its copy is the one nothing overlaps); the rest is three equal body
+  // chunks, each long enough that the next chunk's copy finishes while it computes.
   constexpr size_t kPipeMinBytes = size_t(64) << 20;
-  int chunks = int(std::min<int64_t>(4, ps.batch / kPipeMinChunk));
-  if (const char* e = std::getenv("SHOROKOO_B200_PIPELINE")) chunks = e[0] == '0' ? 0 : std::min(chunks, std::atoi(e));
+  if (const char* e = std::getenv("SHOROKOO_B200_PIPELINE"))
+    if (e[0] == '0') return;
   size_t dev_bytes = 0;
   for (const auto& v : inputs)
     if (numel(v->shape) > kPlanTimeInputMaxElems) dev_bytes += v->nbytes;
-  if (dev_bytes < kPipeMinBytes) return;
-  while (chunks >= 2 && ps.batch % chunks) --chunks;
-  if (chunks < 2) return;
+  if (dev_bytes < kPipeMinBytes || ps.batch < 32) return;
+  const int64_t body = (ps.batch - std::max<int64_t>(1, ps.batch / 16)) / 3;
+  const int64_t head = ps.batch - 3 * body;
+  if (body < head || body < 8) return;
   auto P = std::make_shared<Pipeline>();
   P->device = devices_[0];
-  P->chunks = chunks;
-  P->chunk = ps.batch / chunks;
+  P->rows = {head, body, body, body};
   try {
     ck(cudaSetDevice(P->device), "cudaSetDevice");
-    LGraph g = lower(model_, specs_for(inputs, 0, P->chunk, true));
-    P->plan = std::make_shared<Plan>(std::move(g), P->device, sm_counts_[0], precision_);
-    const auto& outs = P->plan->outputs();
-    for (size_t j = 0; j < outs.size(); ++j)
-      if (!outs[j].host && (outs[j].shape.empty() || outs[j].shape[0] != P->chunk || ps.out_shapes[j].empty() ||
-                            ps.out_shapes[j][0] != ps.batch))
-        return;   // an output is not cut along the batch: keep the single full-batch plan
+    auto build = [&](int64_t n) {
+      LGraph g = lower(model_, specs_for(inputs, 0, n, true));
+      auto plan = std::make_shared<Plan>(std::move(g), P->device, sm_counts_[0], precision_);
+      const auto& outs = plan->outputs();
+      for (size_t j = 0; j < outs.size(); ++j)
+        if (!outs[j].host && (outs[j].shape.empty() || outs[j].shape[0] != n || ps.out_shapes[j].empty() ||
+                              ps.out_shapes[j][0] != ps.batch))
+          return std::shared_ptr<Plan>();   // an output is not cut along the batch
+      return plan;
+    };
+    P->body = build(body);
+    P->head = head == body ? P->body : build(head);
+    if (!P->body || !P->head) return;   // keep the single full-batch plan
     for (int slot = 0; slot < 2; ++slot) {
-      for (const auto& b : P->plan->inputs()) {
+      for (const auto& b : P->body->inputs()) {   // body bindings are the largest
         void* d = nullptr;
         ck(cudaMalloc(&d, std::max<size_t>(b.bytes, 16)), "cudaMalloc (pipeline staging)");
         P->staging[slot].push_back(d);
@@ -458,7 +464,8 @@ void Session::maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_pt
     return;
   }
   if (debug_level() >= 1)
-    std::fprintf(stderr, "[shorokoo_b200] run pipeline: %d chunks of %lld rows\n", chunks, (long long)P->chunk);
+    std::fprintf(stderr, "[shorokoo_b200] run pipeline: 4 chunks of %lld + 3 x %lld rows\n", (long long)head,
+                 (long long)body);
   ps.pipe = P;
 }
 
@@ -467,36 +474,39 @@ void Session::run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostV
   Pipeline& P = *ps.pipe;
   ck(cudaSetDevice(P.device), "cudaSetDevice");
   cudaStream_t cs = streams_[0];
-  const auto& binds = P.plan->inputs();
   std::vector<void*> hout(outs.size(), nullptr);
-  for (int c = 0; c < P.chunks; ++c) {
-    const int slot = c & 1;
+  int64_t r0 = 0;   // first batch row of the chunk
+  for (size_t c = 0; c < P.rows.size(); r0 += P.rows[c], ++c) {
+    Plan& plan = c == 0 ? *P.head : *P.body;
+    const auto& binds = plan.inputs();
+    const int slot = int(c & 1);
     if (c >= 2) ck(cudaStreamWaitEvent(P.copy, P.consumed[slot], 0), "stream wait");
     for (size_t bi = 0; bi < binds.size(); ++bi) {
       const HostValue& v = *inputs[size_t(binds[bi].index)];
       const size_t row = v.nbytes / size_t(std::max<int64_t>(v.shape[0], 1));
-      const uint8_t* src = static_cast<const uint8_t*>(v.data) + size_t(c) * size_t(P.chunk) * row;
+      const uint8_t* src = static_cast<const uint8_t*>(v.data) + size_t(r0) * row;
       ck(cudaMemcpyAsync(P.staging[slot][bi], src, binds[bi].bytes, cudaMemcpyHostToDevice, P.copy), "H2D");
     }
     ck(cudaEventRecord(P.h2d_done[slot], P.copy), "event record");
     ck(cudaStreamWaitEvent(cs, P.h2d_done[slot], 0), "stream wait");
     for (size_t bi = 0; bi < binds.size(); ++bi)
-      ck(cudaMemcpyAsync(P.plan->buffer_ptr(binds[bi].buf), P.staging[slot][bi], binds[bi].bytes,
+      ck(cudaMemcpyAsync(plan.buffer_ptr(binds[bi].buf), P.staging[slot][bi], binds[bi].bytes,
                          cudaMemcpyDeviceToDevice, cs),
          "D2D");
     ck(cudaEventRecord(P.consumed[slot], cs), "event record");
-    P.plan->enqueue_kernels(cs);
+    plan.enqueue_kernels(cs);
     for (size_t j = 0; j < outs.size(); ++j) {
       hout[j] = nullptr;
       if (!outs[j] || ps.out_host[j]) continue;
       const size_t row = outs[j]->nbytes / size_t(std::max<int64_t>(ps.out_shapes[j][0], 1));
-      hout[j] = static_cast<uint8_t*>(outs[j]->data) + size_t(c) * size_t(P.chunk) * row;
+      hout[j] = static_cast<uint8_t*>(outs[j]->data) + size_t(r0) * row;
     }
-    P.plan->enqueue_outputs(cs, hout);
+    plan.enqueue_outputs(cs, hout);
   }
   ck(cudaStreamSynchronize(cs), "stream synchronize");
   ck(cudaStreamSynchronize(P.copy), "stream synchronize");
-  P.plan->check_device_error();
+  P.head->check_device_error();
+  if (P.body != P.head) P.body->check_device_error();
 }
 
 std::vector<std::shared_ptr<HostValue>> Session::run(const std::vector<std::shared_ptr<HostValue>>& inputs,

@@ -64,16 +64,16 @@ class Session {
     int64_t begin, count;   // batch rows
     std::shared_ptr<Plan> plan;
   };
-  // Single-device micro-batch pipeline for run(): the batch is cut into `chunks` equal chunks
-  // that all run through one plan built for the chunk size. Chunk c is copied host->device on
-  // the copy stream into staging slot c % 2 while chunk c-1 computes; the compute stream then
-  // moves it into the plan's input buffers (device->device), runs the kernels and copies the
-  // chunk's outputs back.
+  // Single-device micro-batch pipeline for run(): the batch is cut into a small head chunk and
+  // three equal body chunks (rows[0], rows[1..3]), each running through a plan built for its size.
+  // Chunk c is copied host->device on the copy stream into staging slot c % 2 while chunk c-1
+  // computes; the compute stream then moves it into the plan's input buffers (device->device),
+  // runs the kernels and copies the chunk's outputs back. The small head keeps the one copy that
+  // nothing overlaps short.
   struct Pipeline {
     int device = 0;
-    int chunks = 0;
-    int64_t chunk = 0;
-    std::shared_ptr<Plan> plan;
+    std::vector<int64_t> rows;          // chunk sizes, head first
+    std::shared_ptr<Plan> head, body;   // body also runs the head when the sizes are equal
     std::vector<void*> staging[2];                // per plan input binding
     cudaEvent_t h2d_done[2] = {nullptr, nullptr};  // staging slot filled
     cudaEvent_t consumed[2] = {nullptr, nullptr};  // staging slot read by the compute stream

@@ -1,5 +1,6 @@
 """GPU test of the single-device micro-batch pipeline behind Run: large batch-separable inputs are
-cut into chunks whose host->device copies overlap the previous chunk's kernels. The pipelined Run
+cut into a small head chunk and three equal body chunks whose host->device copies overlap the
+previous chunk's kernels. The pipelined Run
 must give the single full-batch plan's result up to summation order (the chunk plan may pick
 another tile width and with it another split of K across the MMA-issuing lanes, and a changed
 fp32 partial sum can flip the bf16 rounding of an intermediate activation), and the oracle's on a
@@ -48,13 +49,13 @@ def _run_child(tmp_path, case_expr):
     return np.load(tmp_path / "ref.npy"), np.load(tmp_path / "got.npy"), r.stderr
 
 
-@pytest.mark.parametrize("case_expr,chunks", [
-    ("graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)", 4),
-    ("graphs.resnet(depth=18, batch=256, hw=(160, 160), seed=9)", 2),
+@pytest.mark.parametrize("case_expr,schedule", [
+    ("graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)", "1024 + 3 x 5120"),
+    ("graphs.resnet(depth=18, batch=256, hw=(160, 160), seed=9)", "16 + 3 x 80"),
 ])
-def test_pipelined_run_matches_full_batch_plan(tmp_path, case_expr, chunks):
+def test_pipelined_run_matches_full_batch_plan(tmp_path, case_expr, schedule):
     ref, got, log = _run_child(tmp_path, case_expr)
-    assert f"run pipeline: {chunks} chunks" in log, log[-2000:]
+    assert f"run pipeline: 4 chunks of {schedule} rows" in log, log[-2000:]
     assert got.shape == ref.shape
     assert_close(got, ref, what="pipelined run vs full-batch plan")
 
@@ -65,7 +66,7 @@ def test_pipelined_run_matches_oracle_on_a_slice(tmp_path):
     expr = "graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)"
     _, got, _ = _run_child(tmp_path, expr)
     small = graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)
-    rows = np.r_[0:64, 4096 - 32:4096 + 32, 16384 - 64:16384]   # first, a chunk seam, last
+    rows = np.r_[0:64, 1024 - 32:1024 + 32, 6144 - 32:6144 + 32, 16384 - 64:16384]   # first, seams, last
     x = small.inputs[0][1][rows]
     ref = run_oracle(graphs.ModelCase(small.name, small.model, [(small.inputs[0][0], x)], small.output_names,
                                       small.macs))[0]
