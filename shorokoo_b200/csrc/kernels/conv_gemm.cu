@@ -179,6 +179,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// v[j] += (x, y) for the pair j, j + 1, as one packed fp32 add.
+__device__ __forceinline__ void add_pair(float (&v)[32], int j, float x, float y) {
+  const float2 s = __fadd2_rn(make_float2(v[j], v[j + 1]), make_float2(x, y));
+  v[j] = s.x;
+  v[j + 1] = s.y;
+}
 // Accumulator columns [taddr, taddr + 32) of this warp's TMEM lanes summed over the split-K
 // partial accumulators, which sit `pstride` columns apart.
 __device__ __forceinline__ void tmem_ld_sum(uint32_t taddr, int parts, int pstride, float (&v)[32]) {
@@ -190,7 +196,7 @@ __device__ __forceinline__ void tmem_ld_sum(uint32_t taddr, int parts, int pstri
   for (int p = 1; p < parts; ++p) {
     tmem_ld32(taddr + uint32_t(p * pstride), r);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(r[j]);
+    for (int j = 0; j < 32; j += 2) add_pair(v, j, __uint_as_float(r[j]), __uint_as_float(r[j + 1]));
   }
 }
 
@@ -247,6 +253,12 @@ __device__ __forceinline__ void act_apply32(float (&v)[32], int act) {
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+// max(a, 0) and max(b, 0) rounded to bf16 in one conversion (a in the low half).
+__device__ __forceinline__ uint32_t pack_bf16x2_relu(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
 }
 
 // Epilogue for one 32-column chunk of one accumulator row.
@@ -357,14 +369,20 @@ constexpr uint32_t kOutSlab = 4096;        // one 32-row x 128-byte output slab
 constexpr uint32_t kBiasStage = 8 * 512;   // each epilogue warp's bias columns of the current tile
 constexpr int kMaxStages = 8;
 
+// 64-byte swizzled slab (32 rows of 64 bytes, the TMA SWIZZLE_64B pattern): 16-byte chunk j of row r.
+__device__ __forceinline__ uint32_t slab64_off(int r, int j) { return uint32_t(r * 64 + ((j ^ ((r >> 1) & 3)) << 4)); }
+
 // One output slab (32 rows from row0, 128 bytes of columns from n0) of one epilogue warp:
 // accumulator columns [col0, col0 + SC) of the warp's TMEM lanes -> bias (SC floats staged in
 // shared memory at bsl) -> residual (from the producer-filled residual slot, or direct rows) ->
-// activation -> swizzled smem -> TMA store.
+// activation -> swizzled smem -> TMA store. With half >= 0 (bf16 output only) the warp does only
+// the slab's 32-column half `half` (bias at bsl[0..32)), laid out as a 64-byte swizzled slab and
+// stored through a 32x32 box.
 template <bool OBF>
 __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUtensorMap* tmOut, uint32_t tbase,
                                               int col0, int row0, int n0, uint8_t* sb, const uint8_t* rslab,
-                                              const float* bsl, int wait_mode, int parts, int pstride) {
+                                              const float* bsl, int wait_mode, int parts, int pstride,
+                                              int half = -1) {
   constexpr int SC = OBF ? 64 : 32;
   constexpr int EPC = OBF ? 8 : 4;
   constexpr int CH = 32 / EPC;   // 16-byte chunks per 32 columns
@@ -376,18 +394,16 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
     else if (wait_mode == 1) bulk_wait_read0();
   }
   __syncwarp();
-#pragma unroll 1
-  for (int h = 0; h < SC / 32; ++h) {
-    float v[32];
-    tmem_ld_sum(tbase + uint32_t(col0 + h * 32), parts, pstride, v);
-    const float4* b4 = reinterpret_cast<const float4*>(bsl + h * 32);
+  const int h_begin = half >= 0 ? half : 0;
+  const int h_end = half >= 0 ? half + 1 : SC / 32;
+  // bias, residual, activation, bf16 / fp32 conversion and the swizzled slab store of half h
+  auto finish_half = [&](int h, float(&v)[32]) {
+    const float4* b4 = reinterpret_cast<const float4*>(bsl + (h - h_begin) * 32);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float4 bb = b4[j];
-      v[4 * j + 0] += bb.x;
-      v[4 * j + 1] += bb.y;
-      v[4 * j + 2] += bb.z;
-      v[4 * j + 3] += bb.w;
+      add_pair(v, 4 * j, bb.x, bb.y);
+      add_pair(v, 4 * j + 2, bb.z, bb.w);
     }
     if (a.res) {
       if (rslab) {
@@ -398,15 +414,12 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
             const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&qv);
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
-              float2 f = __bfloat1622float2(hh[t]);
-              v[8 * j + 2 * t] += f.x;
-              v[8 * j + 2 * t + 1] += f.y;
+              const float2 f = __bfloat1622float2(hh[t]);
+              add_pair(v, 8 * j + 2 * t, f.x, f.y);
             }
           } else {
-            v[4 * j] += __uint_as_float(qv.x);
-            v[4 * j + 1] += __uint_as_float(qv.y);
-            v[4 * j + 2] += __uint_as_float(qv.z);
-            v[4 * j + 3] += __uint_as_float(qv.w);
+            add_pair(v, 4 * j, __uint_as_float(qv.x), __uint_as_float(qv.y));
+            add_pair(v, 4 * j + 2, __uint_as_float(qv.z), __uint_as_float(qv.w));
           }
         }
       } else if (m < a.M) {
@@ -432,7 +445,9 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
         }
       }
     }
-    act_apply32(v, a.act);
+    // bf16 output folds ReLU into the conversion
+    const bool relu_pack = OBF && a.act == 1;
+    if (!relu_pack) act_apply32(v, a.act);
     if (!OBF && a.round_tf32) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = tf32_rna(v[j]);
@@ -440,7 +455,12 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
 #pragma unroll
     for (int j = 0; j < CH; ++j) {
       uint4 qv;
-      if (OBF) {
+      if (OBF && relu_pack) {
+        qv.x = pack_bf16x2_relu(v[8 * j + 0], v[8 * j + 1]);
+        qv.y = pack_bf16x2_relu(v[8 * j + 2], v[8 * j + 3]);
+        qv.z = pack_bf16x2_relu(v[8 * j + 4], v[8 * j + 5]);
+        qv.w = pack_bf16x2_relu(v[8 * j + 6], v[8 * j + 7]);
+      } else if (OBF) {
         qv.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
         qv.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
         qv.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
@@ -449,13 +469,19 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
         qv = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]),
                         __float_as_uint(v[4 * j + 3]));
       }
-      *reinterpret_cast<uint4*>(sb + slab_off(lane, h * CH + j)) = qv;
+      *reinterpret_cast<uint4*>(sb + (half >= 0 ? slab64_off(lane, j) : slab_off(lane, h * CH + j))) = qv;
     }
+  };
+#pragma unroll
+  for (int h = h_begin; h < h_end; ++h) {   // unrolled: the halves' independent work interleaves
+    float v[32];
+    tmem_ld_sum(tbase + uint32_t(col0 + h * 32), parts, pstride, v);
+    finish_half(h, v);
   }
   fence_async_smem();
   __syncwarp();
   if (lane == 0) {
-    tma_store_2d(tmOut, n0, row0, sb);
+    tma_store_2d(tmOut, n0 + h_begin * 32 * (half >= 0), row0, sb);
     bulk_commit();
   }
 }
@@ -741,12 +767,15 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
     // Bias of this warp's columns of tile t (slabs hsel, hsel+2, ...; at most 4 x 32 floats),
     // lane-strided into registers one tile ahead of use and staged through wbias. The bias array
     // is padded to a multiple of 256 columns.
+    // With epi_half the warp's columns are the tile's 32-column half hsel.
+    const bool ehalf = BN == 64 && a.epi_half != 0 && OB != 0;
     auto load_bias = [&](int t, float (&b)[4]) {
       const int nt = t % tiles_n;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int s2 = hsel + 2 * (i / HPS);
-        b[i] = (t < total && s2 < NS) ? __ldg(a.bias + nt * BN + s2 * SC + (i % HPS) * 32 + lane) : 0.f;
+        if (ehalf) b[i] = (t < total && i == 0) ? __ldg(a.bias + nt * BN + hsel * 32 + lane) : 0.f;
+        else b[i] = (t < total && s2 < NS) ? __ldg(a.bias + nt * BN + s2 * SC + (i % HPS) * 32 + lane) : 0.f;
       }
     };
     float bpre[4];
@@ -768,7 +797,13 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
       const int slot = RS ? it % RS : 0;
       if (RS && !mbar_wait(&resf[slot], uint32_t(it / RS) & 1u, abort_flag, a.err, 32u)) break;
       if (row0 < a.M) {   // warp-uniform
-        if (a.epi == 2) {
+        if (a.epi == 2 && ehalf) {   // bf16 output, one 64-column slab: both warps, a half each
+          if (nt * BN + hsel * 32 < a.Cout) {
+            const uint8_t* rslab = RS ? sRes + slot * RSB : nullptr;
+            uint8_t* sb = sb0 + (OB == 2 ? (nslab++ & 1) * kOutSlab : 0);
+            epilogue_slab<true>(a, &tmOut, tbase, 0, row0, nt * BN, sb, rslab, wbias, OB, PE, BN, hsel);
+          }
+        } else if (a.epi == 2) {
           for (int s2 = hsel; s2 < NS; s2 += 2) {
             const int n0 = nt * BN + s2 * SC;
             if (n0 >= a.Cout) break;
@@ -909,7 +944,7 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 }
 
 bool encode_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
-               uint32_t box_outer, bool f32 = false) {
+               uint32_t box_outer, bool f32 = false, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = get_encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {inner, outer};
@@ -917,8 +952,8 @@ bool encode_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(tm, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -1111,7 +1146,9 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   const bool inplace_hint = res_ring && out_ok && KT >= 8;
   // (the cp.async gather modes have no spare warps: their warps 10-13 gather, so one issuer)
   int pl = !a.x3 && !gather && (im2col || inplace_hint) && bn <= 128 ? 2 : 1;   // X3: warps 13-15 split
-  if (const char* e = std::getenv("SHOROKOO_B200_MMA_LANES")) pl = std::max(1, std::min(pl, std::atoi(e)));
+  if (const char* e = std::getenv("SHOROKOO_B200_MMA_LANES"))   // 1, 2 or 4 where TMEM holds them
+    if (!a.x3 && !gather) pl = std::atoi(e) >= 4 ? 4 : (std::atoi(e) >= 2 ? 2 : 1);
+  while (pl > 1 && 2 * pl * bn > 512) pl /= 2;
   while (pl > KT) pl /= 2;
   if (gather && pl != 1) throw std::runtime_error("conv_gemm: gather modes have a single MMA issuer");
   a.mma_lanes = pl;
@@ -1173,6 +1210,21 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   if (stages < 2) throw std::runtime_error("conv_gemm: shared-memory plan leaves fewer than 2 stages");
   const int fixed = fixed_for(ob);
   a.out_bufs = ob;
+  // bf16 output of 64-column tiles is one 128-byte slab per 32 rows, which would leave one of each
+  // TMEM quarter's two epilogue warps idle: split it into two 32-column halves, one per warp, each
+  // stored from its own slab through a 32x32 box (not for in-place output, whose slab is the
+  // residual ring's 128-byte layout).
+  a.epi_half = 0;
+  static const bool half_on = [] {
+    const char* e = std::getenv("SHOROKOO_B200_EPI_HALF");
+    return !(e && e[0] == '0');
+  }();
+  if (half_on && a.epi == 2 && a.out_bf16 && bn == 64 && ob != 0) {
+    if (!encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldo) * es, 32, 32, false,
+                   CU_TENSOR_MAP_SWIZZLE_64B))
+      throw std::runtime_error("conv_gemm: output tensor map (32x32 box) rejected");
+    a.epi_half = 1;
+  }
   a.stages = stages;
   p.smem = stages * stage_bytes + fixed + rs * rsb;
   int64_t t = tiles(bn);

@@ -43,6 +43,8 @@ struct ConvGemmArgs {
   int res_slots;           // residual ring slots filled by the producer warp (0: direct residual reads)
   int res_slot_bytes;
   int out_bufs;            // output slab buffers per epilogue warp (1, or 2 to overlap stores)
+  int epi_half;            // 1: bf16 output of 64-column tiles; each of a TMEM quarter's two epilogue
+                           // warps stores its own 32-column half (64-byte swizzled slab, 32x32 box)
   int b_resident;          // 1: every weight k-tile is loaded once and stays in shared memory
   int mma_lanes;           // MMA-issuing threads P (1, 2 or 4, one per warp): issuer p accumulates
                            // the k-tiles g = p mod P into its own partial accumulator

@@ -66,6 +66,9 @@ def test_conv(kw):
     (dict(n=2, c=192, cout=256, k=3, h=16, w=16, sigmoid=True), "im2col"),        # 3 channel blocks
     (dict(n=2, c=3, cout=64, k=7, stride=2, pads=[3, 3, 3, 3], h=96, w=96, bn=True, relu=True), "im2col16"),
     (dict(n=2, c=3, cout=64, k=7, stride=2, pads=[3, 2, 2, 3], h=97, w=95), "im2col16"),
+    (dict(n=2, c=1, cout=32, k=3, stride=2, pads=[1, 1, 1, 1], h=160, w=150), "im2col16"),   # 2x2 s2d taps
+    (dict(n=2, c=4, cout=24, k=7, stride=2, pads=[2, 2, 2, 2], h=129, w=128), "im2col16"),
+    (dict(n=2, c=4, cout=24, k=5, stride=2, pads=[0, 0, 0, 0], h=129, w=128), "s2d"),   # 3x3 taps: gather
 ])
 def test_conv_im2col(kw, path):
     from shorokoo_b200 import B200InferenceSessionFactory
@@ -117,3 +120,40 @@ def test_maxpool_and_gap():
     ref = run_oracle(case)[0]
     assert got.shape == (2, 512, 1, 1)
     assert_close(got, ref, what="resnet18 trunk + GAP")
+
+
+def _conv(B, x, cin, cout, k, relu=False, res=None):
+    from shorokoo_b200.emit.graphs import kaiming_normal
+    w = B.init(kaiming_normal(B.rng, (cout, cin, k, k)), "w")
+    b = B.init((0.3 * B.rng.standard_normal(cout)).astype(np.float32), "b")
+    y = B.op("Conv", [x, w, b], auto_pad="NOTSET", dilations=[1, 1], group=1, kernel_shape=[k, k],
+             pads=[k // 2] * 4, strides=[1, 1])
+    if res is not None:
+        y = B.op("Add", [y, res])
+    return B.op("Relu", [y]) if relu else y
+
+
+# Convs whose bf16 output feeds another conv and whose tile is 64 columns wide split each 32-row
+# output slab between the TMEM quarter's two epilogue warps (one 32-column half each): ragged
+# channel counts (48: the second half is partly outside; 24: the second half is empty) and a
+# residual streamed through the ring (one k-tile, so not written in place).
+@pytest.mark.parametrize("cmid", [64, 48, 24])
+def test_conv_chain_64_column_tiles(cmid):
+    from shorokoo_b200.emit import onnx_writer as W
+    from shorokoo_b200.emit.graphs import Builder, ModelCase
+    rng = np.random.Generator(np.random.PCG64(23))
+    n, c, h, w = 2, 32, 48, 40
+    x = rng.standard_normal((n, c, h, w), dtype=np.float32)
+    B = Builder(24)
+    xi = B.graph_input(W.FLOAT, 4, x.shape)
+    y1 = _conv(B, xi, c, cmid, 3, relu=True)
+    y2 = _conv(B, y1, cmid, cmid, 1, relu=True, res=y1)
+    y3 = _conv(B, y2, cmid, 16, 3)
+    for t, ch in ((y1, cmid), (y2, cmid), (y3, 16)):
+        B.shape[t] = (n, ch, h, w)
+    B.outputs.append(W.ValueInfo(y3))
+    case = ModelCase("conv_chain", B.model("conv_chain"), [(xi, x)], [y3], 0)
+    got = run_backend(case)[0]
+    ref = run_oracle(case)[0]
+    assert got.shape == (n, 16, h, w)
+    assert_close(got, ref, what=f"conv chain through {cmid} channels")
