@@ -281,7 +281,7 @@ __device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint
     v[4 * j + 3] = __uint_as_float(r[4 * j + 3]) + bb.w;
   }
   const int ncols = min(32, a.Cout - n0);
-  if (a.res) {
+  if (a.res && !a.res_mma) {   // (res_mma: the MMA added it)
     int64_t rrow = m;
     if (a.res_mode == 1) {
       int hw = a.Ho * a.Wo;
@@ -375,6 +375,7 @@ constexpr int kSmemLimit = 232448;        // opt-in maximum dynamic shared memor
 constexpr uint32_t kOutSlab = 4096;        // one 32-row x 128-byte output slab
 constexpr uint32_t kBiasStage = 8 * 512;   // each epilogue warp's bias columns of the current tile
 constexpr int kMaxStages = 8;
+constexpr uint32_t kIdBytes = 64 * 128;   // 64x64 bf16 identity, K-major, 128-byte swizzle
 
 // 64-byte swizzled slab (32 rows of 64 bytes, the TMA SWIZZLE_64B pattern): 16-byte chunk j of row r.
 __device__ __forceinline__ uint32_t slab64_off(int r, int j) { return uint32_t(r * 64 + ((j ^ ((r >> 1) & 3)) << 4)); }
@@ -412,7 +413,7 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
       add_pair(v, 4 * j, bb.x, bb.y);
       add_pair(v, 4 * j + 2, bb.z, bb.w);
     }
-    if (a.res) {
+    if (a.res && !a.res_mma) {   // (res_mma: the MMA added it)
       if (rslab) {
 #pragma unroll
         for (int j = 0; j < CH; ++j) {
@@ -535,6 +536,9 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int KT = a.Kpad / BKE;
+  // residual k-tiles (res_mma): k-tile KT + j adds residual channels [64j, 64j + 64) of the tile
+  const bool RESM = A_TMA && MODE != 4 && PREC == 0 && a.res_mma;
+  const int KTE = KT + (RESM ? BN / 64 : 0);
   const bool BRES = A_TMA && a.b_resident;   // weights loaded once: slot kt holds k-tile kt
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_STAGE;
@@ -542,7 +546,8 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
   const int OB = a.out_bufs;
   float* sBias = reinterpret_cast<float*>(sOut + 8 * OB * kOutSlab);
   uint8_t* sRes = sOut + 8 * OB * kOutSlab + kBiasStage;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sRes + RS * RSB);
+  uint8_t* sId = sRes + RS * RSB;   // RESM: the identity operand
+  uint64_t* full = reinterpret_cast<uint64_t*>(sId + (RESM ? kIdBytes : 0u));
   uint64_t* empty = full + kMaxStages;
   uint64_t* accf = empty + kMaxStages;
   uint64_t* acce = accf + 2;
@@ -578,7 +583,17 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
     if (A_TMA) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
     if (a.epi == 2) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmOut) : "memory");
-    if (RS) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmRes) : "memory");
+    if (RS || RESM) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmRes) : "memory");
+  }
+  if (RESM) {   // identity rows n: 1.0 at k = n; 16-byte chunk c holds row c / 8, logical chunk (c % 8) ^ (row % 8)
+    for (int c = threadIdx.x; c < int(kIdBytes / 16); c += blockDim.x) {
+      const int n = c >> 3, lc = (c & 7) ^ (n & 7);
+      const int word = (n >> 3) == lc ? (n & 7) >> 1 : -1;   // the 32-bit word holding element n
+      const uint32_t one = (n & 1) ? 0x3F800000u : 0x00003F80u;
+      reinterpret_cast<uint4*>(sId)[c] =
+          make_uint4(word == 0 ? one : 0u, word == 1 ? one : 0u, word == 2 ? one : 0u, word == 3 ? one : 0u);
+    }
+    fence_async_smem();   // generic writes -> the MMA's async-proxy reads
   }
   if (warp == 1) tmem_alloc(tmem_holder, TMEM_COLS);
   tc_fence_before();
@@ -629,7 +644,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
           for (int s2 = 0; s2 < nsl; ++s2)
             tma_load_2d(sRes + slot * RSB + s2 * 128 * 128, &tmRes, nt * BN + s2 * SC, mt * BM, &resf[slot]);
         }
-        for (int kt = 0; kt < KT; ++kt) {
+        for (int kt = 0; kt < KTE; ++kt) {
           const bool mine = owner == pid;
           if (++owner == NP) owner = 0;
           if (!mine) {
@@ -640,6 +655,15 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
             continue;
           }
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) goto producer_done;
+          if (kt >= KT) {   // residual k-tile: 128 rows x 64 channels of the residual, no weights
+            mbar_expect_tx(&full[stage], A_BYTES);
+            tma_load_2d(sA + stage * A_STAGE, &tmRes, nt * BN + (kt - KT) * 64, mt * BM, &full[stage]);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
           mbar_expect_tx(&full[stage], (A_TMA ? A_BYTES : 0u) + (BRES ? 0u : B_STAGE));
           if (MODE == 0) tma_load_2d(sA + stage * A_STAGE, &tmA, kt * BKE, mt * BM, &full[stage]);
           if (MODE == 3) {
@@ -710,21 +734,23 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
     const int mid = warp == 1 ? 0 : warp - 12;
     if (lane == 0 && mid < PE) {
       constexpr uint32_t idesc = idesc_mma(BM, BN, TF32);
+      constexpr uint32_t idesc64 = idesc_mma(BM, 64, TF32);   // residual k-tiles: 64 columns each
       int it = 0;
       int g0 = 0;   // sequence number of the tile's first k-tile (the producers' numbering)
       // this issuer's next k-tile g (= mid mod PE) and its stage / phase, advanced by PE steps
       int g = mid, stage = mid;
       uint32_t phase = 0;
       if (BRES && !mbar_wait(bfull, 0u, abort_flag, a.err, 128u)) goto mma_done;
-      for (int t = blockIdx.x; t < total; t += gridDim.x, ++it, g0 += KT) {
+      for (int t = blockIdx.x; t < total; t += gridDim.x, ++it, g0 += KTE) {
         const int acc = it & 1;
         const uint32_t aph = uint32_t(it >> 1) & 1u;
         if (!mbar_wait(&acce[acc], aph ^ 1u, abort_flag, a.err, 2u)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t((acc * PL + mid) * BN);
         bool ok = true;
-        // this issuer's k-tiles of the tile: g0 <= g < g0 + KT with g = mid (mod PE)
-        for (bool first = true; g < g0 + KT; first = false) {
+        // this issuer's k-tiles of the tile: g0 <= g < g0 + KTE with g = mid (mod PE); the first
+        // is always a weight k-tile (PE <= KT), which initialises every column of the partial
+        for (bool first = true; g < g0 + KTE; first = false) {
           const int kt = g - g0;
           if (!mbar_wait(&full[stage], phase, abort_flag, a.err, 4u) ||
               (X3 && !mbar_wait(&split[stage], phase, abort_flag, a.err, 512u))) {
@@ -734,22 +760,29 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
           tc_fence_after();
           if (GATHER) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           const uint64_t ad = sw128_desc(smem_u32(sA + stage * A_STAGE));
-          const uint64_t bd = sw128_desc(smem_u32(BRES ? sB + kt * B_BYTES : sB + stage * B_STAGE));
+          if (RESM && kt >= KT) {   // residual k-tile: D[:, 64j .. 64j + 64) += R_j * I
+            const uint64_t idd = sw128_desc(smem_u32(sId));
+            const uint32_t dcol = d_tmem + uint32_t((kt - KT) * 64);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {   // four 32-byte K slices per 128-byte row
-            const uint64_t akk = MODE == 4 ? sw32_desc(smem_u32(sA + stage * A_STAGE + kk * (BM * 32)))
-                                           : ad + uint64_t(kk * 2);
-            const uint32_t accum = (!first || kk != 0) ? 1u : 0u;
-            if (X3) {
-              const uint64_t alo = sw128_desc(smem_u32(sA + stage * A_STAGE + A_BYTES)) + uint64_t(kk * 2);
-              const uint64_t blo = sw128_desc(smem_u32(sB + stage * B_STAGE + B_BYTES)) + uint64_t(kk * 2);
-              umma_tf32(d_tmem, akk, bd + uint64_t(kk * 2), idesc, accum);
-              umma_tf32(d_tmem, akk, blo, idesc, 1u);
-              umma_tf32(d_tmem, alo, bd + uint64_t(kk * 2), idesc, 1u);
-            } else if (TF32) {
-              umma_tf32(d_tmem, akk, bd + uint64_t(kk * 2), idesc, accum);
-            } else {
-              umma_bf16(d_tmem, akk, bd + uint64_t(kk * 2), idesc, accum);
+            for (int kk = 0; kk < 4; ++kk) umma_bf16(dcol, ad + uint64_t(kk * 2), idd + uint64_t(kk * 2), idesc64, 1u);
+          } else {
+            const uint64_t bd = sw128_desc(smem_u32(BRES ? sB + kt * B_BYTES : sB + stage * B_STAGE));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {   // four 32-byte K slices per 128-byte row
+              const uint64_t akk = MODE == 4 ? sw32_desc(smem_u32(sA + stage * A_STAGE + kk * (BM * 32)))
+                                             : ad + uint64_t(kk * 2);
+              const uint32_t accum = (!first || kk != 0) ? 1u : 0u;
+              if (X3) {
+                const uint64_t alo = sw128_desc(smem_u32(sA + stage * A_STAGE + A_BYTES)) + uint64_t(kk * 2);
+                const uint64_t blo = sw128_desc(smem_u32(sB + stage * B_STAGE + B_BYTES)) + uint64_t(kk * 2);
+                umma_tf32(d_tmem, akk, bd + uint64_t(kk * 2), idesc, accum);
+                umma_tf32(d_tmem, akk, blo, idesc, 1u);
+                umma_tf32(d_tmem, alo, bd + uint64_t(kk * 2), idesc, 1u);
+              } else if (TF32) {
+                umma_tf32(d_tmem, akk, bd + uint64_t(kk * 2), idesc, accum);
+              } else {
+                umma_bf16(d_tmem, akk, bd + uint64_t(kk * 2), idesc, accum);
+              }
             }
           }
           umma_commit(&empty[stage]);
@@ -1109,10 +1142,23 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   if (const char* e = std::getenv("SHOROKOO_B200_EPI")) want = std::atoi(e);
   const bool out_ok = want != 0 && a.group_rows == 0 && a.Cout % epc == 0 && (a.ldo * es) % 16 == 0 &&
                       (reinterpret_cast<uintptr_t>(a.out) & 15) == 0;
-  const bool res_ring = out_ok && a.res && a.res_mode == 0 && a.res_bf16 == a.out_bf16 && (a.ldr * es) % 16 == 0 &&
-                        (reinterpret_cast<uintptr_t>(a.res) & 15) == 0;
-  // Tile width: residual convs use at most 128 columns so two residual tiles fit beside a deep
-  // operand pipeline.
+  p.mode = conv_gemm_a_mode(a);
+  // A bf16 residual of a bf16 conv whose A operand comes by TMA is added by the tensor core (one
+  // extra k-tile per 64 channels against an identity operand), which takes the residual off the
+  // epilogue's per-element work; otherwise it streams through a shared-memory ring (below) or is
+  // read directly by the epilogue.
+  static const bool res_mma_on = [] {
+    const char* e = std::getenv("SHOROKOO_B200_RES_MMA");
+    return !(e && e[0] == '0');
+  }();
+  const bool res_mma = res_mma_on && out_ok && a.res && a.res_mode == 0 && a.res_bf16 && !a.tf32 && !a.x3 &&
+                       (p.mode == kARows || p.mode == kAIm2col64) && (a.ldr * 2) % 16 == 0 &&
+                       (reinterpret_cast<uintptr_t>(a.res) & 15) == 0;
+  a.res_mma = 0;
+  const bool res_ring = !res_mma && out_ok && a.res && a.res_mode == 0 && a.res_bf16 == a.out_bf16 &&
+                        (a.ldr * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.res) & 15) == 0;
+  // Tile width: residual convs with a ring use at most 128 columns so two residual tiles fit beside
+  // a deep operand pipeline.
   auto tiles = [&](int bn) { return int64_t((a.M + BM - 1) / BM) * ((a.Cout + bn - 1) / bn); };
   // (TF32x3 stages hold hi and lo tiles: at most 128 columns so two stages fit)
   int bn = a.Cout <= 64 ? 64 : (a.Cout <= 128 || res_ring || a.x3 ? 128 : 256);
@@ -1128,7 +1174,6 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
     bn = best;
   }
   p.bn = bn;
-  p.mode = conv_gemm_a_mode(a);
   // Weights stay resident when the conv has one N tile and all its k-tiles fit in 96 KB: every
   // pipeline stage then carries only the activation tile (half the TMA loads for N=64 layers).
   const int bke = a.tf32 ? BK / 2 : BK;   // operand elements per 128-byte k-tile row
@@ -1167,6 +1212,8 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   if (out_ok &&
       encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldo) * es, sc, 32, !a.out_bf16)) {
     a.epi = 2;
+    if (res_mma)   // residual k-tiles: 128 rows x 64 channels, the A operand's layout
+      a.res_mma = encode_2d(&p.tmRes, a.res, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldr) * 2, 64, 128) ? 1 : 0;
     ring = res_ring && encode_2d(&p.tmRes, a.res, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldr) * es, sc, 128,
                                  !a.out_bf16);
   }
@@ -1175,7 +1222,9 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   // otherwise one slab per epilogue warp. A second slab per warp lets a store
   // drain while the next slab is computed, but measured on ResNet-50 the operand stages it costs
   // are worth more, so it is opt-in (SHOROKOO_B200_OUTBUF=2).
-  auto fixed_for = [&](int ob) { return int(8 * ob * kOutSlab + kBiasStage) + 1024 + 512 + (bres ? int(w_bytes) : 0); };
+  auto fixed_for = [&](int ob) {
+    return int(8 * ob * kOutSlab + kBiasStage) + 1024 + 512 + (bres ? int(w_bytes) : 0) + (a.res_mma ? int(kIdBytes) : 0);
+  };
   auto ring_for = [&](int ob) {   // residual slots that still leave two operand stages (0: direct reads)
     if (!ring) return 0;
     if ((kSmemLimit - fixed_for(ob) - 2 * rsb) / stage_bytes >= 2) return 2;

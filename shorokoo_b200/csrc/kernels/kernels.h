@@ -43,6 +43,9 @@ struct ConvGemmArgs {
   int res_slots;           // residual ring slots filled by the producer warp (0: direct residual reads)
   int res_slot_bytes;
   int out_bufs;            // output slab buffers per epilogue warp (1, or 2 to overlap stores)
+  int res_mma;             // 1: the tensor core adds the bf16 residual: after the tile's k-tiles come
+                           // one k-tile per 64 residual channels, A = the residual rows (TMA), B = a
+                           // 64x64 identity in shared memory, accumulated into those 64 columns
   int epi_half;            // 1: bf16 output of 64-column tiles; each of a TMEM quarter's two epilogue
                            // warps stores its own 32-column half (64-byte swizzled slab, 32x32 box)
   int b_resident;          // 1: every weight k-tile is loaded once and stays in shared memory

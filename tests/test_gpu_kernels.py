@@ -135,9 +135,10 @@ def _conv(B, x, cin, cout, k, relu=False, res=None):
 
 # Convs whose bf16 output feeds another conv and whose tile is 64 columns wide split each 32-row
 # output slab between the TMEM quarter's two epilogue warps (one 32-column half each): ragged
-# channel counts (48: the second half is partly outside; 24: the second half is empty) and a
-# residual streamed through the ring (one k-tile, so not written in place).
-@pytest.mark.parametrize("cmid", [64, 48, 24])
+# channel counts (48: the second half is partly outside; 24: the second half is empty). The middle
+# conv's bf16 residual is added by the tensor core as one extra k-tile per 64 channels (96: the
+# second residual k-tile is partly outside the tensor; 200: four of them, the last partly outside).
+@pytest.mark.parametrize("cmid", [64, 48, 24, 96, 200])
 def test_conv_chain_64_column_tiles(cmid):
     from shorokoo_b200.emit import onnx_writer as W
     from shorokoo_b200.emit.graphs import Builder, ModelCase
