@@ -274,7 +274,7 @@ __device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint
   const float4* b4 = reinterpret_cast<const float4*>(a.bias + n0);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    float4 bb = __ldg(b4 + j);
+    float4 bb = a.bias_mma ? make_float4(0.f, 0.f, 0.f, 0.f) : __ldg(b4 + j);   // (bias_mma: in the accumulator)
     v[4 * j + 0] = __uint_as_float(r[4 * j + 0]) + bb.x;
     v[4 * j + 1] = __uint_as_float(r[4 * j + 1]) + bb.y;
     v[4 * j + 2] = __uint_as_float(r[4 * j + 2]) + bb.z;
@@ -376,6 +376,7 @@ constexpr uint32_t kOutSlab = 4096;        // one 32-row x 128-byte output slab
 constexpr uint32_t kBiasStage = 8 * 512;   // each epilogue warp's bias columns of the current tile
 constexpr int kMaxStages = 8;
 constexpr uint32_t kIdBytes = 64 * 128;   // 64x64 bf16 identity, K-major, 128-byte swizzle
+constexpr uint32_t kOnesBytes = 128 * 32; // bias_mma: 128 x 16 bf16 A tile, 1.0 at k = 0 and 1, 32-byte swizzle
 
 // 64-byte swizzled slab (32 rows of 64 bytes, the TMA SWIZZLE_64B pattern): 16-byte chunk j of row r.
 __device__ __forceinline__ uint32_t slab64_off(int r, int j) { return uint32_t(r * 64 + ((j ^ ((r >> 1) & 3)) << 4)); }
@@ -406,12 +407,14 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
   const int h_end = half >= 0 ? half + 1 : SC / 32;
   // bias, residual, activation, bf16 / fp32 conversion and the swizzled slab store of half h
   auto finish_half = [&](int h, float(&v)[32]) {
-    const float4* b4 = reinterpret_cast<const float4*>(bsl + (h - h_begin) * 32);
+    if (!a.bias_mma) {   // (bias_mma: the accumulator started at the bias)
+      const float4* b4 = reinterpret_cast<const float4*>(bsl + (h - h_begin) * 32);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 bb = b4[j];
-      add_pair(v, 4 * j, bb.x, bb.y);
-      add_pair(v, 4 * j + 2, bb.z, bb.w);
+      for (int j = 0; j < 8; ++j) {
+        const float4 bb = b4[j];
+        add_pair(v, 4 * j, bb.x, bb.y);
+        add_pair(v, 4 * j + 2, bb.z, bb.w);
+      }
     }
     if (a.res && !a.res_mma) {   // (res_mma: the MMA added it)
       if (rslab) {
@@ -547,7 +550,12 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
   float* sBias = reinterpret_cast<float*>(sOut + 8 * OB * kOutSlab);
   uint8_t* sRes = sOut + 8 * OB * kOutSlab + kBiasStage;
   uint8_t* sId = sRes + RS * RSB;   // RESM: the identity operand
-  uint64_t* full = reinterpret_cast<uint64_t*>(sId + (RESM ? kIdBytes : 0u));
+  // bias_mma: the ones tile, then the bias rows of every N tile (hi, lo at k = 0, 1)
+  const bool BMMA = PREC == 0 && a.bias_mma;
+  uint8_t* sOnes = sId + (RESM ? kIdBytes : 0u);
+  uint8_t* sBiasT = sOnes + kOnesBytes;
+  const int bias_rows = ((a.Cout + BN - 1) / BN) * BN;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOnes + (BMMA ? kOnesBytes + uint32_t(bias_rows) * 32u : 0u));
   uint64_t* empty = full + kMaxStages;
   uint64_t* accf = empty + kMaxStages;
   uint64_t* acce = accf + 2;
@@ -594,6 +602,24 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
           make_uint4(word == 0 ? one : 0u, word == 1 ? one : 0u, word == 2 ? one : 0u, word == 3 ? one : 0u);
     }
     fence_async_smem();   // generic writes -> the MMA's async-proxy reads
+  }
+  if (BMMA) {
+    // 32-byte swizzle, K-major: row r's 16-byte chunk c sits at chunk position c ^ ((r / 4) % 2).
+    // Ones tile: 1.0 at k = 0, 1 of every row. Bias tile: row n holds hi = bf16(b[n]) at k = 0 and
+    // lo = bf16(b[n] - hi) at k = 1, so hi + lo matches the fp32 bias to about 2^-17 of it.
+    for (int c = threadIdx.x; c < int(kOnesBytes / 16); c += blockDim.x) {
+      const int r = c >> 1, pos = c & 1;
+      reinterpret_cast<uint4*>(sOnes)[c] = make_uint4(pos == ((r >> 2) & 1) ? 0x3F803F80u : 0u, 0u, 0u, 0u);
+    }
+    for (int c = threadIdx.x; c < bias_rows * 2; c += blockDim.x) {
+      const int r = c >> 1, pos = c & 1;
+      const float b = a.bias[r];
+      const __nv_bfloat16 hi = __float2bfloat16_rn(b);
+      const __nv_bfloat16 lo = __float2bfloat16_rn(b - __bfloat162float(hi));
+      const uint32_t w = uint32_t(__bfloat16_as_ushort(hi)) | (uint32_t(__bfloat16_as_ushort(lo)) << 16);
+      reinterpret_cast<uint4*>(sBiasT)[c] = make_uint4(pos == ((r >> 2) & 1) ? w : 0u, 0u, 0u, 0u);
+    }
+    fence_async_smem();
   }
   if (warp == 1) tmem_alloc(tmem_holder, TMEM_COLS);
   tc_fence_before();
@@ -767,11 +793,17 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
             for (int kk = 0; kk < 4; ++kk) umma_bf16(dcol, ad + uint64_t(kk * 2), idd + uint64_t(kk * 2), idesc64, 1u);
           } else {
             const uint64_t bd = sw128_desc(smem_u32(BRES ? sB + kt * B_BYTES : sB + stage * B_STAGE));
+            // bias_mma: issuer 0 starts the tile's accumulator at the bias (the other issuers'
+            // partials start at zero)
+            const bool bias_first = BMMA && first && mid == 0;
+            if (bias_first)
+              umma_bf16(d_tmem, sw32_desc(smem_u32(sOnes)), sw32_desc(smem_u32(sBiasT + (t % tiles_n) * BN * 32)),
+                        idesc, 0u);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {   // four 32-byte K slices per 128-byte row
               const uint64_t akk = MODE == 4 ? sw32_desc(smem_u32(sA + stage * A_STAGE + kk * (BM * 32)))
                                              : ad + uint64_t(kk * 2);
-              const uint32_t accum = (!first || kk != 0) ? 1u : 0u;
+              const uint32_t accum = (!first || kk != 0 || bias_first) ? 1u : 0u;
               if (X3) {
                 const uint64_t alo = sw128_desc(smem_u32(sA + stage * A_STAGE + A_BYTES)) + uint64_t(kk * 2);
                 const uint64_t blo = sw128_desc(smem_u32(sB + stage * B_STAGE + B_BYTES)) + uint64_t(kk * 2);
@@ -814,7 +846,8 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int s2 = hsel + 2 * (i / HPS);
-        if (ehalf) b[i] = (t < total && i == 0) ? __ldg(a.bias + nt * BN + hsel * 32 + lane) : 0.f;
+        if (a.bias_mma) b[i] = 0.f;   // (the accumulator starts at the bias)
+        else if (ehalf) b[i] = (t < total && i == 0) ? __ldg(a.bias + nt * BN + hsel * 32 + lane) : 0.f;
         else b[i] = (t < total && s2 < NS) ? __ldg(a.bias + nt * BN + s2 * SC + (i % HPS) * 32 + lane) : 0.f;
       }
     };
@@ -1179,6 +1212,16 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   const int bke = a.tf32 ? BK / 2 : BK;   // operand elements per 128-byte k-tile row
   if (a.Kpad % bke) throw std::runtime_error("conv_gemm: reduction length not padded to a whole k-tile");
   const int KT = a.Kpad / bke;
+  // bf16 convs with a single weight k-tile (the 1x1 convs from 64 channels, whose epilogue sets the
+  // pace) start each accumulator at the bias with one extra MMA, so the epilogue adds none. Measured
+  // on ResNet-50 bs512: 1x1 64->64 0.118 -> 0.107 ms, 64->256 -17%; convs with more k-tiles or
+  // wider bias tiles lost 1-7% (the extra MMA on the issue path, the bias tile's shared memory).
+  static const bool bias_mma_on = [] {
+    const char* e = std::getenv("SHOROKOO_B200_BIAS_MMA");
+    return !(e && e[0] == '0');
+  }();
+  const int bias_rows = int((a.Cout + bn - 1) / bn) * bn;
+  a.bias_mma = bias_mma_on && !a.tf32 && !a.x3 && a.bias && KT == 1 && bias_rows <= 256 ? 1 : 0;
   const int64_t w_bytes = int64_t(KT) * bn * 128;
   bool bres = !a.x3 && p.mode != kAGather16 && p.mode != kAGather8 && a.Cout <= bn && w_bytes <= 96 * 1024;
   if (const char* e = std::getenv("SHOROKOO_B200_BRES"))
@@ -1223,7 +1266,8 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   // drain while the next slab is computed, but measured on ResNet-50 the operand stages it costs
   // are worth more, so it is opt-in (SHOROKOO_B200_OUTBUF=2).
   auto fixed_for = [&](int ob) {
-    return int(8 * ob * kOutSlab + kBiasStage) + 1024 + 512 + (bres ? int(w_bytes) : 0) + (a.res_mma ? int(kIdBytes) : 0);
+    return int(8 * ob * kOutSlab + kBiasStage) + 1024 + 512 + (bres ? int(w_bytes) : 0) + (a.res_mma ? int(kIdBytes) : 0) +
+           (a.bias_mma ? int(kOnesBytes) + bias_rows * 32 : 0);
   };
   auto ring_for = [&](int ob) {   // residual slots that still leave two operand stages (0: direct reads)
     if (!ring) return 0;

@@ -46,6 +46,8 @@ struct ConvGemmArgs {
   int res_mma;             // 1: the tensor core adds the bf16 residual: after the tile's k-tiles come
                            // one k-tile per 64 residual channels, A = the residual rows (TMA), B = a
                            // 64x64 identity in shared memory, accumulated into those 64 columns
+  int bias_mma;            // 1: the tensor core starts every accumulator at the bias: one K=16 MMA of
+                           // a ones tile (A) and the bias split into bf16 hi + lo (B) per tile
   int epi_half;            // 1: bf16 output of 64-column tiles; each of a TMEM quarter's two epilogue
                            // warps stores its own 32-column half (64-byte swizzled slab, 32x32 box)
   int b_resident;          // 1: every weight k-tile is loaded once and stays in shared memory
