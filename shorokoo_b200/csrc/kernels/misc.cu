@@ -94,6 +94,45 @@ __global__ void to_s2d_bf16_kernel(const void* __restrict__ src, int src_bf16, i
   }
 }
 
+// The same for the common case: fp32 NCHW stored contiguously, even width, C (1-4) known at compile
+// time. Each thread builds its 16-value pixel in registers from float2 loads of its two input rows
+// (consecutive threads read consecutive 8-byte pairs of a row) and stores it as two 16-byte words.
+template <int C>
+__global__ void to_s2d_bf16_f32_kernel(const float* __restrict__ src, int64_t N, int64_t H, int64_t W,
+                                       __nv_bfloat16* __restrict__ dst, int64_t Hs, int64_t Ws) {
+  const int64_t total = N * Hs * Ws;
+  const int64_t plane = H * W;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t n = i / (Hs * Ws);
+    const int64_t r = i - n * Hs * Ws;
+    const int64_t hs = r / Ws, ws = r - (r / Ws) * Ws;
+    float f[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) f[j] = 0.f;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int64_t h = 2 * hs + p;
+      if (h < H) {   // (the width is even: both columns of the pair exist)
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+          const float2 x = __ldg(reinterpret_cast<const float2*>(src + (n * C + c) * plane + h * W + 2 * ws));
+          f[(p * 2) * C + c] = x.x;
+          f[(p * 2 + 1) * C + c] = x.y;
+        }
+      }
+    }
+    uint32_t w[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+      w[j] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+    uint4* d = reinterpret_cast<uint4*>(dst + i * 16);
+    d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
 // fp32 rounded to the TF32 grid (10 explicit mantissa bits, nearest, ties away): the operands the
 // TF32 tensor-core path multiplies, rounded once here instead of truncated by the MMA.
 __device__ __forceinline__ float tf32_rna(float x) {
@@ -261,6 +300,53 @@ __global__ void maxpool_k_nhwc_kernel(const __nv_bfloat16* __restrict__ x, __nv_
 #pragma unroll
     for (int t = 0; t < 4; ++t) oh[t] = __floats2bfloat162_rn(m[2 * t], m[2 * t + 1]);
     *reinterpret_cast<uint4*>(y + i * 8) = o;
+  }
+}
+
+// 3x3 stride-2 max pool (the ResNet stem pool), NHWC bf16, C % 8 == 0: one block per output row.
+// The block first takes, for every input column its row needs, the max over the window's three input
+// rows (16 bytes of channels at a time) into shared memory, then for each output pixel the max over
+// three adjacent columns. Each input row is read by 1.5 blocks (instead of each pixel by 2.25
+// threads). The max of bf16 values is one of them, so this equals the per-pixel kernel exactly.
+__device__ __forceinline__ uint4 bf16x8_max(uint4 a, uint4 b) {
+  const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&b);
+  uint4 r;
+  __nv_bfloat162* z = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+  for (int t = 0; t < 4; ++t) z[t] = __hmax2(x[t], y[t]);
+  return r;
+}
+__global__ void maxpool3s2_row_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int H,
+                                      int W, int C, int Ho, int Wo, int ph, int pw) {
+  extern __shared__ uint4 colmax[];   // [2 * Wo + 1][C / 8]: column w - pw's max over the three rows
+  const int cg = C / 8;
+  const int Wv = 2 * Wo + 1;
+  const int row = blockIdx.x;   // n * Ho + ho
+  const int n = row / Ho, ho = row - n * Ho;
+  const int h0 = 2 * ho - ph;
+  const __nv_bfloat16* img = x + int64_t(n) * H * W * C;
+  const uint4 ninf = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);   // bf16 -inf
+  for (int i = threadIdx.x; i < Wv * cg; i += blockDim.x) {
+    const int wi = i / cg, g = i - wi * cg;
+    const int w = wi - pw;
+    uint4 m = ninf;
+    if (w >= 0 && w < W) {
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        const int h = h0 + a;
+        if (h >= 0 && h < H)
+          m = bf16x8_max(m, __ldg(reinterpret_cast<const uint4*>(img + (int64_t(h) * W + w) * C + g * 8)));
+      }
+    }
+    colmax[i] = m;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < Wo * cg; i += blockDim.x) {
+    const int wo = i / cg, g = i - wo * cg;
+    const uint4 m = bf16x8_max(bf16x8_max(colmax[(2 * wo) * cg + g], colmax[(2 * wo + 1) * cg + g]),
+                               colmax[(2 * wo + 2) * cg + g]);
+    *reinterpret_cast<uint4*>(y + (int64_t(row) * Wo + wo) * C + g * 8) = m;
   }
 }
 
@@ -445,6 +531,21 @@ cudaError_t maxpool_nhwc_f32(const void* x, void* y, int N, int H, int W, int C,
 cudaError_t to_s2d_bf16(const void* src, int src_bf16, const int64_t* sh, const int64_t* st, void* dst, int64_t Hs,
                         int64_t Ws, cudaStream_t s) {
   if (sh[1] > 4) return cudaErrorInvalidValue;
+  const bool packed = !src_bf16 && st[3] == 1 && st[2] == sh[3] && st[1] == sh[2] * sh[3] &&
+                      st[0] == sh[1] * sh[2] * sh[3] && sh[3] % 2 == 0 && 2 * Ws == sh[3] && 2 * Hs >= sh[2] &&
+                      2 * Hs <= sh[2] + 1 && (reinterpret_cast<uintptr_t>(src) & 7) == 0;
+  if (packed) {
+    const float* f = reinterpret_cast<const float*>(src);
+    auto d = reinterpret_cast<__nv_bfloat16*>(dst);
+    const auto g = grid_for(sh[0] * Hs * Ws);
+    switch (sh[1]) {
+      case 1: to_s2d_bf16_f32_kernel<1><<<g, kThreads, 0, s>>>(f, sh[0], sh[2], sh[3], d, Hs, Ws); break;
+      case 2: to_s2d_bf16_f32_kernel<2><<<g, kThreads, 0, s>>>(f, sh[0], sh[2], sh[3], d, Hs, Ws); break;
+      case 3: to_s2d_bf16_f32_kernel<3><<<g, kThreads, 0, s>>>(f, sh[0], sh[2], sh[3], d, Hs, Ws); break;
+      default: to_s2d_bf16_f32_kernel<4><<<g, kThreads, 0, s>>>(f, sh[0], sh[2], sh[3], d, Hs, Ws); break;
+    }
+    return cudaGetLastError();
+  }
   to_s2d_bf16_kernel<<<grid_for(sh[0] * Hs * Ws), kThreads, 0, s>>>(src, src_bf16, sh[0], sh[1], sh[2], sh[3], st[0],
                                                                     st[1], st[2], st[3],
                                                                     reinterpret_cast<__nv_bfloat16*>(dst), Hs, Ws);
@@ -462,7 +563,10 @@ cudaError_t maxpool_nhwc_bf16(const void* x, void* y, int N, int H, int W, int C
                               int sw, int ph, int pw, int dh, int dw, cudaStream_t s) {
   auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
   auto yb = reinterpret_cast<__nv_bfloat16*>(y);
-  if (C % 8 == 0 && kh == 3 && kw == 3 && dh == 1 && dw == 1) {
+  const size_t row_smem = size_t(2 * Wo + 1) * (C / 8) * 16;
+  if (C % 8 == 0 && kh == 3 && kw == 3 && sh == 2 && sw == 2 && dh == 1 && dw == 1 && row_smem <= 48 * 1024) {
+    maxpool3s2_row_kernel<<<int64_t(N) * Ho, 256, row_smem, s>>>(xb, yb, H, W, C, Ho, Wo, ph, pw);
+  } else if (C % 8 == 0 && kh == 3 && kw == 3 && dh == 1 && dw == 1) {
     maxpool_k_nhwc_kernel<3><<<grid_for(int64_t(N) * Ho * Wo * (C / 8)), kThreads, 0, s>>>(xb, yb, N, H, W, C, Ho, Wo,
                                                                                            sh, sw, ph, pw);
   } else if (C % 8 == 0) {
