@@ -547,8 +547,10 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
   uint8_t* sB = sA + STAGES * A_STAGE;
   uint8_t* sOut = sB + (BRES ? KT * B_BYTES : STAGES * B_STAGE);
   const int OB = a.out_bufs;
-  float* sBias = reinterpret_cast<float*>(sOut + 8 * OB * kOutSlab);
-  uint8_t* sRes = sOut + 8 * OB * kOutSlab + kBiasStage;
+  // per-warp output slab: 32 rows x 128 bytes, or 32 x 64 bytes when each warp stores a half
+  const uint32_t SLAB = a.epi_half ? kOutSlab / 2 : kOutSlab;
+  float* sBias = reinterpret_cast<float*>(sOut + 8 * OB * SLAB);
+  uint8_t* sRes = sOut + 8 * OB * SLAB + kBiasStage;
   uint8_t* sId = sRes + RS * RSB;   // RESM: the identity operand
   // bias_mma: the ones tile, then the bias rows of every N tile (hi, lo at k = 0, 1)
   const bool BMMA = PREC == 0 && a.bias_mma;
@@ -833,7 +835,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
   } else if (warp < 10) {
     const int q = warp & 3;          // TMEM lane quarter this warp may access
     const int hsel = (warp - 2) >> 2; // which of the two warps of this quarter
-    uint8_t* sb0 = sOut + (warp - 2) * OB * kOutSlab;
+    uint8_t* sb0 = sOut + (warp - 2) * OB * SLAB;
     float* wbias = sBias + (warp - 2) * 128;
     const int HPS = SC / 32;   // 32-column halves per slab
     // Bias of this warp's columns of tile t (slabs hsel, hsel+2, ...; at most 4 x 32 floats),
@@ -873,7 +875,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
         if (a.epi == 2 && ehalf) {   // bf16 output, one 64-column slab: both warps, a half each
           if (nt * BN + hsel * 32 < a.Cout) {
             const uint8_t* rslab = RS ? sRes + slot * RSB : nullptr;
-            uint8_t* sb = sb0 + (OB == 2 ? (nslab++ & 1) * kOutSlab : 0);
+            uint8_t* sb = sb0 + (OB == 2 ? (nslab++ & 1) * SLAB : 0);
             epilogue_slab<true>(a, &tmOut, tbase, 0, row0, nt * BN, sb, rslab, wbias, OB, PE, BN, hsel);
           }
         } else if (a.epi == 2) {
@@ -886,7 +888,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
             // released once that store has read it. Otherwise the warp's own output slab(s).
             const bool inplace = RS && OB == 0;
             uint8_t* sb = inplace ? sRes + slot * RSB + s2 * 128 * 128 + q * 32 * 128
-                                  : sb0 + (OB == 2 ? (nslab++ & 1) * kOutSlab : 0);
+                                  : sb0 + (OB == 2 ? (nslab++ & 1) * SLAB : 0);
             const int wm = inplace ? 0 : OB;
             const float* bsl = wbias + ((s2 - hsel) >> 1) * SC;
             if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl, wm, PE, BN);
@@ -1265,8 +1267,17 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   // otherwise one slab per epilogue warp. A second slab per warp lets a store
   // drain while the next slab is computed, but measured on ResNet-50 the operand stages it costs
   // are worth more, so it is opt-in (SHOROKOO_B200_OUTBUF=2).
+  // bf16 output of 64-column tiles is one 128-byte slab per 32 rows, which would leave one of each
+  // TMEM quarter's two epilogue warps idle: it is split into two 32-column halves, one per warp,
+  // each stored from its own 64-byte slab through a 32x32 box (not for in-place output, whose slab
+  // is the residual ring's 128-byte layout). The halved slabs also leave room for more stages.
+  static const bool half_on = [] {
+    const char* e = std::getenv("SHOROKOO_B200_EPI_HALF");
+    return !(e && e[0] == '0');
+  }();
+  auto half_for = [&](int ob) { return half_on && a.epi == 2 && a.out_bf16 && bn == 64 && ob != 0; };
   auto fixed_for = [&](int ob) {
-    return int(8 * ob * kOutSlab + kBiasStage) + 1024 + 512 + (bres ? int(w_bytes) : 0) + (a.res_mma ? int(kIdBytes) : 0) +
+    return int(8 * ob * (half_for(ob) ? kOutSlab / 2 : kOutSlab) + kBiasStage) + 1024 + 512 + (bres ? int(w_bytes) : 0) + (a.res_mma ? int(kIdBytes) : 0) +
            (a.bias_mma ? int(kOnesBytes) + bias_rows * 32 : 0);
   };
   auto ring_for = [&](int ob) {   // residual slots that still leave two operand stages (0: direct reads)
@@ -1310,16 +1321,8 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   if (stages < 2) throw std::runtime_error("conv_gemm: shared-memory plan leaves fewer than 2 stages");
   const int fixed = fixed_for(ob);
   a.out_bufs = ob;
-  // bf16 output of 64-column tiles is one 128-byte slab per 32 rows, which would leave one of each
-  // TMEM quarter's two epilogue warps idle: split it into two 32-column halves, one per warp, each
-  // stored from its own slab through a 32x32 box (not for in-place output, whose slab is the
-  // residual ring's 128-byte layout).
   a.epi_half = 0;
-  static const bool half_on = [] {
-    const char* e = std::getenv("SHOROKOO_B200_EPI_HALF");
-    return !(e && e[0] == '0');
-  }();
-  if (half_on && a.epi == 2 && a.out_bf16 && bn == 64 && ob != 0) {
+  if (half_for(ob)) {
     if (!encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldo) * es, 32, 32, false,
                    CU_TENSOR_MAP_SWIZZLE_64B))
       throw std::runtime_error("conv_gemm: output tensor map (32x32 box) rejected");
