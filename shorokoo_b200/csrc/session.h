@@ -72,8 +72,8 @@ class Session {
   // nothing overlaps short.
   struct Pipeline {
     int device = 0;
-    std::vector<int64_t> rows;          // chunk sizes, head first
-    std::shared_ptr<Plan> head, body;   // body also runs the head when the sizes are equal
+    std::vector<int64_t> rows;                 // chunk sizes, in batch order
+    std::vector<std::shared_ptr<Plan>> plans;  // plan of each chunk (chunks of one size share it)
     std::vector<void*> staging[2];                // per plan input binding
     cudaEvent_t h2d_done[2] = {nullptr, nullptr};  // staging slot filled
     cudaEvent_t consumed[2] = {nullptr, nullptr};  // staging slot read by the compute stream

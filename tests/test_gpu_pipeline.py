@@ -1,6 +1,6 @@
 """GPU test of the single-device micro-batch pipeline behind Run: large batch-separable inputs are
-cut into a small head chunk and three equal body chunks whose host->device copies overlap the
-previous chunk's kernels. The pipelined Run
+cut into two small head chunks (an eighth of the batch each) and two body chunks whose host->device
+copies overlap the previous chunk's kernels. The pipelined Run
 must give the single full-batch plan's result up to summation order (the chunk plan may pick
 another tile width and with it another split of K across the MMA-issuing lanes, and a changed
 fp32 partial sum can flip the bf16 rounding of an intermediate activation), and the oracle's on a
@@ -50,8 +50,8 @@ def _run_child(tmp_path, case_expr):
 
 
 @pytest.mark.parametrize("case_expr,schedule", [
-    ("graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)", "1024 + 3 x 5120"),
-    ("graphs.resnet(depth=18, batch=256, hw=(160, 160), seed=9)", "16 + 3 x 80"),
+    ("graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)", "2048 + 2048 + 6144 + 6144"),
+    ("graphs.resnet(depth=18, batch=256, hw=(160, 160), seed=9)", "32 + 32 + 96 + 96"),
 ])
 def test_pipelined_run_matches_full_batch_plan(tmp_path, case_expr, schedule):
     ref, got, log = _run_child(tmp_path, case_expr)
@@ -66,7 +66,8 @@ def test_pipelined_run_matches_oracle_on_a_slice(tmp_path):
     expr = "graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)"
     _, got, _ = _run_child(tmp_path, expr)
     small = graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)
-    rows = np.r_[0:64, 1024 - 32:1024 + 32, 6144 - 32:6144 + 32, 16384 - 64:16384]   # first, seams, last
+    rows = np.r_[0:64, 2048 - 32:2048 + 32, 4096 - 32:4096 + 32, 10240 - 32:10240 + 32,
+                 16384 - 64:16384]   # first, seams, last
     x = small.inputs[0][1][rows]
     ref = run_oracle(graphs.ModelCase(small.name, small.model, [(small.inputs[0][0], x)], small.output_names,
                                       small.macs))[0]
