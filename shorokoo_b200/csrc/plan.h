@@ -72,6 +72,8 @@ class Plan {
   const PlanStats& stats() const { return stats_; }
   int device() const { return device_; }
   void* buffer_ptr(int buf) const;
+  // Device address of output j (f32 contiguous; device outputs only).
+  void* output_ptr(size_t j) const { return ptr(outputs_[j].dev); }
 
  private:
   struct Buffer {

@@ -48,9 +48,9 @@ struct HostPool {
     return cuda_ok == 1;
   }
 
-  void* alloc(size_t bytes, bool& pinned) {
+  void* alloc(size_t bytes, bool& pinned, bool force_pin = false) {
     pinned = false;
-    if (bytes >= kPinnedMin) {
+    if (bytes >= kPinnedMin || force_pin) {
       size_t sz = (bytes + kPinnedMin - 1) / kPinnedMin * kPinnedMin;
       {
         std::lock_guard<std::mutex> l(mu);
@@ -127,14 +127,14 @@ HostValue::~HostValue() {
   if (owned && data) pool().release(data, nbytes, pinned);
 }
 
-std::shared_ptr<HostValue> HostValue::alloc_tensor(int32_t elem_type, const std::vector<int64_t>& shape) {
+std::shared_ptr<HostValue> HostValue::alloc_tensor(int32_t elem_type, const std::vector<int64_t>& shape, bool pin) {
   auto v = std::make_shared<HostValue>();
   v->kind = TENSOR;
   v->elem_type = elem_type;
   v->shape = shape;
   v->nbytes = size_t(numel(shape)) * dtype_size(elem_type);
   bool pinned = false;
-  v->data = pool().alloc(std::max<size_t>(v->nbytes, 1), pinned);
+  v->data = pool().alloc(std::max<size_t>(v->nbytes, 1), pinned, pin);
   v->pinned = pinned;
   v->owned = true;
   return v;
@@ -407,11 +407,16 @@ Session::Pipeline::~Pipeline() {
   cudaSetDevice(device);
   for (auto& slot : staging)
     for (void* p : slot) cudaFree(p);
+  for (auto& slot : out_staging)
+    for (void* p : slot) cudaFree(p);
   for (int i = 0; i < 2; ++i) {
     if (h2d_done[i]) cudaEventDestroy(h2d_done[i]);
     if (consumed[i]) cudaEventDestroy(consumed[i]);
+    if (out_ready[i]) cudaEventDestroy(out_ready[i]);
+    if (out_free[i]) cudaEventDestroy(out_free[i]);
   }
   if (copy) cudaStreamDestroy(copy);
+  if (d2h) cudaStreamDestroy(d2h);
 }
 
 void Session::maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs) {
@@ -427,16 +432,31 @@ void Session::maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_pt
   constexpr size_t kPipeMinBytes = size_t(64) << 20;
   if (const char* e = std::getenv("SHOROKOO_B200_PIPELINE"))
     if (e[0] == '0') return;
-  size_t dev_bytes = 0;
+  // (input and output copies both overlap the chunks' kernels: outputs such as a detector's dense
+  // per-anchor maps can outweigh the inputs)
+  size_t in_bytes = 0, out_bytes = 0;
   for (const auto& v : inputs)
-    if (numel(v->shape) > kPlanTimeInputMaxElems) dev_bytes += v->nbytes;
-  if (dev_bytes < kPipeMinBytes || ps.batch < 32) return;
+    if (numel(v->shape) > kPlanTimeInputMaxElems) in_bytes += v->nbytes;
+  for (size_t j = 0; j < ps.out_shapes.size(); ++j)
+    if (!ps.out_host[j]) out_bytes += size_t(numel(ps.out_shapes[j])) * 4;
+  if (in_bytes + out_bytes < kPipeMinBytes || ps.batch < 8) return;
   const int64_t head = std::max<int64_t>(1, ps.batch / 8);
-  const int64_t body = (ps.batch - 2 * head) / 2;
-  if (body < head || body < 8) return;
   auto P = std::make_shared<Pipeline>();
   P->device = devices_[0];
-  P->rows = {head, head, body, ps.batch - 2 * head - body};
+  if (out_bytes > in_bytes) {
+    // Output-bound (device->host copies outlast the kernels): once the first chunk's outputs start
+    // copying back the copy stream should never wait, and the last chunk's copy is the one nothing
+    // overlaps, so after two small chunks the rest goes in quarters (RetinaNet bs16: 2 + 2 + 4 +
+    // 4 + 4 took 825 MB of outputs back in about the time of the copy alone).
+    const int64_t quarter = std::max<int64_t>(1, ps.batch / 4);
+    const int64_t last = ps.batch - 2 * head - 2 * quarter;
+    if (last < 1) return;
+    P->rows = {head, head, quarter, quarter, last};
+  } else {
+    const int64_t body = (ps.batch - 2 * head) / 2;
+    if (body < head || body < 2) return;
+    P->rows = {head, head, body, ps.batch - 2 * head - body};
+  }
   try {
     ck(cudaSetDevice(P->device), "cudaSetDevice");
     auto build = [&](int64_t n) {
@@ -461,16 +481,29 @@ void Session::maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_pt
       }
       P->plans.push_back(plan);
     }
+    size_t big = 0;   // the largest chunk: its plan's bindings size the staging slots
+    for (size_t c = 1; c < P->rows.size(); ++c)
+      if (P->rows[c] > P->rows[big]) big = c;
     for (int slot = 0; slot < 2; ++slot) {
-      for (const auto& b : P->plans.back()->inputs()) {   // the largest chunk's bindings
+      for (const auto& b : P->plans[big]->inputs()) {
         void* d = nullptr;
         ck(cudaMalloc(&d, std::max<size_t>(b.bytes, 16)), "cudaMalloc (pipeline staging)");
         P->staging[slot].push_back(d);
       }
+      const auto& louts = P->plans[big]->outputs();
+      for (size_t j = 0; j < louts.size(); ++j) {
+        void* d = nullptr;
+        if (!louts[j].host)
+          ck(cudaMalloc(&d, std::max<size_t>(size_t(numel(louts[j].shape)) * 4, 16)), "cudaMalloc (output staging)");
+        P->out_staging[slot].push_back(d);
+      }
       ck(cudaEventCreateWithFlags(&P->h2d_done[slot], cudaEventDisableTiming), "event");
       ck(cudaEventCreateWithFlags(&P->consumed[slot], cudaEventDisableTiming), "event");
+      ck(cudaEventCreateWithFlags(&P->out_ready[slot], cudaEventDisableTiming), "event");
+      ck(cudaEventCreateWithFlags(&P->out_free[slot], cudaEventDisableTiming), "event");
     }
     ck(cudaStreamCreateWithFlags(&P->copy, cudaStreamNonBlocking), "cudaStreamCreate");
+    ck(cudaStreamCreateWithFlags(&P->d2h, cudaStreamNonBlocking), "cudaStreamCreate");
   } catch (const Error& e) {
     if (debug_level() >= 1) std::fprintf(stderr, "[shorokoo_b200] no micro-batch pipeline: %s\n", e.what());
     return;
@@ -509,16 +542,31 @@ void Session::run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostV
          "D2D");
     ck(cudaEventRecord(P.consumed[slot], cs), "event record");
     plan.enqueue_kernels(cs);
+    // outputs: into output slot `slot` on the compute stream (once its previous host copy is done),
+    // then to the host on the d2h stream, overlapping the next chunks
+    if (c >= 2) ck(cudaStreamWaitEvent(cs, P.out_free[slot], 0), "stream wait");
     for (size_t j = 0; j < outs.size(); ++j) {
       hout[j] = nullptr;
       if (!outs[j] || ps.out_host[j]) continue;
       const size_t row = outs[j]->nbytes / size_t(std::max<int64_t>(ps.out_shapes[j][0], 1));
       hout[j] = static_cast<uint8_t*>(outs[j]->data) + size_t(r0) * row;
+      ck(cudaMemcpyAsync(P.out_staging[slot][j], plan.output_ptr(j), row * size_t(P.rows[c]),
+                         cudaMemcpyDeviceToDevice, cs),
+         "D2D (outputs)");
     }
-    plan.enqueue_outputs(cs, hout);
+    ck(cudaEventRecord(P.out_ready[slot], cs), "event record");
+    ck(cudaStreamWaitEvent(P.d2h, P.out_ready[slot], 0), "stream wait");
+    for (size_t j = 0; j < outs.size(); ++j)
+      if (hout[j])
+        ck(cudaMemcpyAsync(hout[j], P.out_staging[slot][j],
+                           outs[j]->nbytes / size_t(std::max<int64_t>(ps.out_shapes[j][0], 1)) * size_t(P.rows[c]),
+                           cudaMemcpyDeviceToHost, P.d2h),
+           "D2H");
+    ck(cudaEventRecord(P.out_free[slot], P.d2h), "event record");
   }
   ck(cudaStreamSynchronize(cs), "stream synchronize");
   ck(cudaStreamSynchronize(P.copy), "stream synchronize");
+  ck(cudaStreamSynchronize(P.d2h), "stream synchronize");
   for (size_t c = 0; c < P.plans.size(); ++c)
     if (c == 0 || P.plans[c] != P.plans[c - 1]) P.plans[c]->check_device_error();
 }
@@ -531,6 +579,11 @@ std::vector<std::shared_ptr<HostValue>> Session::run(const std::vector<std::shar
   std::vector<std::shared_ptr<HostValue>> outs(nout);
   std::vector<bool> wanted(nout, false);
   for (int j : out_idx) wanted[size_t(j)] = true;
+  maybe_build_pipeline(*ps, inputs);
+  // A pipelined run copies each chunk's outputs back while later chunks still copy in and compute:
+  // a copy into pageable memory would block the host until the chunk is done, serialising the
+  // pipeline, so those outputs are page-locked whatever their size.
+  const bool pin_outputs = ps->pipe != nullptr;
   for (size_t j = 0; j < nout; ++j) {
     if (!wanted[j]) continue;
     if (ps->out_host[j]) {
@@ -538,10 +591,9 @@ std::vector<std::shared_ptr<HostValue>> Session::run(const std::vector<std::shar
       outs[j] = HostValue::alloc_tensor(h.dtype, h.shape);
       if (h.nbytes()) std::memcpy(outs[j]->data, h.data(), h.nbytes());
     } else {
-      outs[j] = HostValue::alloc_tensor(DT_FLOAT, ps->out_shapes[j]);
+      outs[j] = HostValue::alloc_tensor(DT_FLOAT, ps->out_shapes[j], pin_outputs);
     }
   }
-  maybe_build_pipeline(*ps, inputs);
   if (ps->pipe) {
     run_pipelined(*ps, inputs, outs);
     std::vector<std::shared_ptr<HostValue>> res;

@@ -29,7 +29,10 @@ struct HostValue {
   std::vector<std::string> strings;
   std::vector<std::shared_ptr<HostValue>> items;   // sequence elements
   ~HostValue();
-  static std::shared_ptr<HostValue> alloc_tensor(int32_t elem_type, const std::vector<int64_t>& shape);
+  // pin: page-locked even below the pool's size threshold (outputs of a pipelined Run, whose
+  // per-chunk device->host copies must not block the host)
+  static std::shared_ptr<HostValue> alloc_tensor(int32_t elem_type, const std::vector<int64_t>& shape,
+                                                 bool pin = false);
 };
 
 struct SessionOptions {
@@ -78,6 +81,12 @@ class Session {
     cudaEvent_t h2d_done[2] = {nullptr, nullptr};  // staging slot filled
     cudaEvent_t consumed[2] = {nullptr, nullptr};  // staging slot read by the compute stream
     cudaStream_t copy = nullptr;
+    // outputs: the compute stream copies chunk c's outputs into slot c mod 2 (per output, sized for
+    // the largest chunk); the d2h stream copies the slot to the host while later chunks compute
+    std::vector<void*> out_staging[2];
+    cudaEvent_t out_ready[2] = {nullptr, nullptr};   // slot filled by the compute stream
+    cudaEvent_t out_free[2] = {nullptr, nullptr};    // slot copied to the host
+    cudaStream_t d2h = nullptr;
     ~Pipeline();
   };
   struct PlanSet {
