@@ -1202,10 +1202,13 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
     // the issuing thread about the same whatever its N, so a narrower tile only pays when it cuts
     // the number of waves (measured on ResNet-50 bs64: 1.41 -> 1.39 ms against halving N until
     // every SM has a tile).
+    // Among equal wave counts the tile that fills the most SMs wins (ties: the widest): a small batch
+    // whose widest tiles occupy a third of the SMs in one wave runs twice as many CTAs at half the
+    // width, each also free to use two MMA issuers.
     auto waves = [&](int b) { return (tiles(b) + num_sms - 1) / num_sms; };
     int best = bn;
     for (int b = bn; b >= 64; b /= 2)
-      if (waves(b) < waves(best)) best = b;
+      if (waves(b) < waves(best) || (waves(b) == waves(best) && tiles(b) > tiles(best))) best = b;
     bn = best;
   }
   p.bn = bn;

@@ -18,7 +18,7 @@ import textwrap
 import numpy as np
 import pytest
 
-from helpers import assert_close
+from helpers import BF16_TOL, assert_close
 
 pytestmark = pytest.mark.gpu
 
@@ -50,18 +50,22 @@ def _run_child(tmp_path, case_expr):
     return np.load(tmp_path / "ref.npy"), np.load(tmp_path / "got.npy"), r.stderr
 
 
-@pytest.mark.parametrize("case_expr,schedule", [
-    ("graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)", "2048 + 2048 + 6144 + 6144"),
-    ("graphs.resnet(depth=18, batch=256, hw=(160, 160), seed=9)", "32 + 32 + 96 + 96"),
+@pytest.mark.parametrize("case_expr,schedule,tol", [
+    ("graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)", "2048 + 2048 + 6144 + 6144",
+     BF16_TOL),
+    ("graphs.resnet(depth=18, batch=256, hw=(160, 160), seed=9)", "32 + 32 + 96 + 96", BF16_TOL),
     # a detector whose per-anchor outputs (~200 MB) outweigh its input: pipelined below batch 32,
-    # the output copies overlapping later chunks through the output staging slots
-    ("graphs.retinanet(batch=16, hw=(384, 512), seed=5)", "2 + 2 + 4 + 4 + 4"),
+    # the output copies overlapping later chunks through the output staging slots. Its chunks pick
+    # other tiles than the full batch, and through RetinaNet's depth that change of summation order
+    # moves the bf16 result by as much as the bf16 floor the RetinaNet parity tests allow against
+    # the fp32 oracle (3.5e-2).
+    ("graphs.retinanet(batch=16, hw=(384, 512), seed=5)", "2 + 2 + 4 + 4 + 4", 3.5e-2),
 ])
-def test_pipelined_run_matches_full_batch_plan(tmp_path, case_expr, schedule):
+def test_pipelined_run_matches_full_batch_plan(tmp_path, case_expr, schedule, tol):
     ref, got, log = _run_child(tmp_path, case_expr)
     assert f"chunks of {schedule} rows" in log, log[-2000:]
     assert got.shape == ref.shape
-    assert_close(got, ref, what="pipelined run vs full-batch plan")
+    assert_close(got, ref, tol=tol, what="pipelined run vs full-batch plan")
 
 
 def test_pipelined_run_matches_oracle_on_a_slice(tmp_path):
