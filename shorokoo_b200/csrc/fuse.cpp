@@ -37,9 +37,66 @@ Consumers consumers(const LGraph& g) {
     for (int id : op.in)
       if (id >= 0) c.ops[size_t(id)].push_back(int(i));
     if (op.residual >= 0) c.ops[size_t(op.residual)].push_back(int(i));
+    if (op.concat >= 0) c.ops[size_t(op.concat)].push_back(int(i));
   }
   for (int id : g.outputs) c.is_output[size_t(id)] = true;
   return c;
+}
+
+// A FusedConv that is a plain 1x1, stride-1, unpadded, ungrouped conv (no second operand yet).
+bool pointwise_conv(const Op& o) {
+  if (o.dead || o.type != "FusedConv" || o.group != 1 || o.concat >= 0 || !o.weight) return false;
+  const auto& w = o.weight->shape;
+  if (w.size() != 4 || w[2] != 1 || w[3] != 1) return false;
+  for (int64_t s : o.strides)
+    if (s != 1) return false;
+  for (int64_t d : o.dilations)
+    if (d != 1) return false;
+  for (int64_t p : o.pads)
+    if (p != 0) return false;
+  return true;
+}
+
+// Projection shortcut merged into the conv that adds it (the first bottleneck of a ResNet stage
+// whose shortcut is a 1x1 stride-1 conv, ResNet.cs:280-329): y = act(X1*W1 + b1 + (X0*Ws + bs)) is
+// one GEMM over X1's and X0's channels side by side, y = act([X1 X0] * [W1; Ws] + (b1 + bs)), so
+// the shortcut's output is neither written nor read back. Both channel counts must be multiples
+// of 64, so each operand fills whole k-tiles in every precision.
+void merge_projection_shortcuts(LGraph& g) {
+  const Consumers cons = consumers(g);
+  for (size_t i = 0; i < g.ops.size(); ++i) {
+    Op& f = g.ops[i];
+    if (!pointwise_conv(f) || f.residual < 0 || f.residual_mode != 0) continue;
+    const int r = f.residual;
+    const int pi = g.vals[size_t(r)].producer;
+    if (pi < 0 || pi >= int(g.ops.size())) continue;
+    Op& p = g.ops[size_t(pi)];
+    if (!pointwise_conv(p) || p.act != 0 || p.residual >= 0 || p.out.size() != 1 || p.out[0] != r) continue;
+    if (cons.is_output[size_t(r)] || cons.ops[size_t(r)].size() != 1) continue;
+    const Value& x1 = g.vals[size_t(f.in[0])];
+    const Value& x0 = g.vals[size_t(p.in[0])];
+    if (x1.is_host || x0.is_host || x1.shape.size() != 4 || x0.shape.size() != 4) continue;
+    if (x1.shape[0] != x0.shape[0] || x1.shape[2] != x0.shape[2] || x1.shape[3] != x0.shape[3]) continue;
+    const int64_t M = f.weight->shape[0], C1 = f.weight->shape[1], C0 = p.weight->shape[1];
+    if (p.weight->shape[0] != M || C1 != x1.shape[1] || C0 != x0.shape[1] || C1 % 64 || C0 % 64) continue;
+    auto w = std::make_shared<HostTensor>(DT_FLOAT, std::vector<int64_t>{M, C1 + C0, 1, 1});
+    const float* w1 = f.weight->ptr<float>();
+    const float* w0 = p.weight->ptr<float>();
+    float* wp = w->mptr<float>();
+    for (int64_t m = 0; m < M; ++m) {
+      for (int64_t c = 0; c < C1; ++c) wp[m * (C1 + C0) + c] = w1[m * C1 + c];
+      for (int64_t c = 0; c < C0; ++c) wp[m * (C1 + C0) + C1 + c] = w0[m * C0 + c];
+    }
+    auto b = std::make_shared<HostTensor>(DT_FLOAT, std::vector<int64_t>{M});
+    float* bp = b->mptr<float>();
+    for (int64_t m = 0; m < M; ++m)
+      bp[m] = (f.bias ? f.bias->ptr<float>()[m] : 0.f) + (p.bias ? p.bias->ptr<float>()[m] : 0.f);
+    f.weight = w;
+    f.bias = b;
+    f.concat = p.in[0];
+    f.residual = -1;
+    p.dead = true;
+  }
 }
 
 // Host tensor that broadcasts against an output of `rank` dims and varies at most along `axis`
@@ -327,6 +384,7 @@ void fuse(LGraph& g) {
     g.vals[size_t(cur)].producer = slot;
     g.ops[size_t(slot)] = f;
   }
+  merge_projection_shortcuts(g);
   g.dce();
 }
 

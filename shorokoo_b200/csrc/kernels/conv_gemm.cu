@@ -541,6 +541,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
   const int KT = a.Kpad / BKE;
   // residual k-tiles (res_mma): k-tile KT + j adds residual channels [64j, 64j + 64) of the tile
   const bool RESM = A_TMA && MODE != 4 && PREC == 0 && a.res_mma;
+  const bool A2 = MODE == 0 && a.a2 != nullptr;   // second A operand (uses the tmRes map)
   const int KTE = KT + (RESM ? BN / 64 : 0);
   const bool BRES = A_TMA && a.b_resident;   // weights loaded once: slot kt holds k-tile kt
   uint8_t* sA = smem;
@@ -593,7 +594,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
     if (A_TMA) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
     if (a.epi == 2) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmOut) : "memory");
-    if (RS || RESM) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmRes) : "memory");
+    if (RS || RESM || A2) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmRes) : "memory");
   }
   if (RESM) {   // identity rows n: 1.0 at k = n; 16-byte chunk c holds row c / 8, logical chunk (c % 8) ^ (row % 8)
     for (int c = threadIdx.x; c < int(kIdBytes / 16); c += blockDim.x) {
@@ -693,7 +694,10 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
             continue;
           }
           mbar_expect_tx(&full[stage], (A_TMA ? A_BYTES : 0u) + (BRES ? 0u : B_STAGE));
-          if (MODE == 0) tma_load_2d(sA + stage * A_STAGE, &tmA, kt * BKE, mt * BM, &full[stage]);
+          if (MODE == 0) {   // (k-tiles from a2_kt on come from the second operand, through tmRes)
+            if (A2 && kt >= a.a2_kt) tma_load_2d(sA + stage * A_STAGE, &tmRes, (kt - a.a2_kt) * BKE, mt * BM, &full[stage]);
+            else tma_load_2d(sA + stage * A_STAGE, &tmA, kt * BKE, mt * BM, &full[stage]);
+          }
           if (MODE == 3) {
             const int tap = kt / cblocks, cb = kt - tap * cblocks;
             const int kh = tap / a.KW, kw = tap - (tap / a.KW) * a.KW;
@@ -1342,6 +1346,12 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
                       uint32_t(bke), uint32_t(bn), a.tf32 != 0);
   if (p.mode == kARows)
     ok = ok && encode_2d(&p.tmA, a_rows, uint64_t(lda), uint64_t(a.M), uint64_t(lda) * eb, uint32_t(bke), BM, a.tf32 != 0);
+  if (a.a2) {   // second A operand: a row matrix like the first, through the (then unused) tmRes map
+    if (p.mode != kARows || a.res || a.a2_kt <= 0 || a.a2_kt >= KT)
+      throw std::runtime_error("conv_gemm: a second A operand needs row-matrix A, no residual, a split inside K");
+    ok = ok && encode_2d(&p.tmRes, a.a2, uint64_t(a.lda2), uint64_t(a.M), uint64_t(a.lda2) * eb, uint32_t(bke), BM,
+                         a.tf32 != 0);
+  }
   if (!ok) throw std::runtime_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad layout)");
   if ((p.mode == kAIm2col64 || p.mode == kAIm2col16) && !encode_im2col(&p.tmA, a, p.mode == kAIm2col64 ? bke : 16))
     throw std::runtime_error("cuTensorMapEncodeIm2col failed (driver entry point missing or bad layout)");

@@ -43,6 +43,10 @@ struct ConvGemmArgs {
   int res_slots;           // residual ring slots filled by the producer warp (0: direct residual reads)
   int res_slot_bytes;
   int out_bufs;            // output slab buffers per epilogue warp (1, or 2 to overlap stores)
+  const void* a2;          // second A operand (a row matrix like the first, row mode only) supplying
+                           // k-tiles a2_kt.. (a merged projection shortcut's input), or null
+  int64_t lda2;            // its row pitch in elements
+  int a2_kt;               // first k-tile read from a2 (k-tile kt reads its k-tile kt - a2_kt)
   int res_mma;             // 1: the tensor core adds the bf16 residual: after the tile's k-tiles come
                            // one k-tile per 64 residual channels, A = the residual rows (TMA), B = a
                            // 64x64 identity in shared memory, accumulated into those 64 columns

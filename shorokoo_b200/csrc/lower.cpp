@@ -631,6 +631,7 @@ std::vector<int> LGraph::use_counts() const {
     for (int id : op.in)
       if (id >= 0) c[size_t(id)]++;
     if (op.residual >= 0) c[size_t(op.residual)]++;
+    if (op.concat >= 0) c[size_t(op.concat)]++;
   }
   for (int id : outputs) c[size_t(id)]++;
   return c;
@@ -652,6 +653,7 @@ void LGraph::dce() {
     for (int id : op.in)
       if (id >= 0) live[size_t(id)] = true;
     if (op.residual >= 0) live[size_t(op.residual)] = true;
+    if (op.concat >= 0) live[size_t(op.concat)] = true;
   }
 }
 

@@ -419,14 +419,29 @@ void Plan::plan_conv(const Op& op) {
   } else {
     x = as_nhwc_op(op.in[0], Cp);
   }
-  const int64_t K = gKH * gKW * Cp;
+  // A merged projection shortcut's input (op.concat): its C2 channels follow X's in the reduction,
+  // read by the kernel from its own row matrix (k-tiles from Cp / k-tile width on).
+  DevTensor x2;
+  int64_t C2 = 0;
+  if (op.concat >= 0) {
+    C2 = Wt.shape[1] - C;
+    const Value& cv = g_.vals[size_t(op.concat)];
+    SB_CHECK(one_by_one && Cp == C && C % 64 == 0 && C2 > 0 && C2 % 64 == 0 && cv.shape.size() == 4 &&
+                 cv.shape[0] == N && cv.shape[1] == C2 && cv.shape[2] == H && cv.shape[3] == W,
+             SB_UNSUPPORTED, "Conv: concatenated operand layout");
+    x2 = as_nhwc_op(op.concat, int(C2));
+  }
+  const int64_t K = gKH * gKW * Cp + C2;
   const int64_t Kpad = round_up(K, tf32_ ? 32 : 64);   // whole 128-byte k-tile rows
   SB_CHECK(N * Ho * Wo < (int64_t(1) << 31) && N * gH * gW * Cp < (int64_t(1) << 40), SB_UNSUPPORTED,
            "Conv: problem too large for 32-bit row indexing");
   // weights [Cout, Kpad] bf16 (or TF32-rounded fp32), K ordered (kh, kw, c) of the kernel as run
   std::vector<float> wf(size_t(Cout * Kpad), 0.f);
   const float* wp = Wt.ptr<float>();
-  for (int64_t m = 0; m < Cout; ++m)
+  if (op.concat >= 0)   // 1x1 over [X, X2]: k = channel
+    for (int64_t m = 0; m < Cout; ++m)
+      for (int64_t c = 0; c < C + C2; ++c) wf[size_t(m * Kpad + c)] = wp[m * (C + C2) + c];
+  for (int64_t m = 0; m < Cout && op.concat < 0; ++m)
     for (int64_t c = 0; c < C; ++c)
       for (int64_t a = 0; a < KH; ++a)
         for (int64_t b = 0; b < KW; ++b) {
@@ -474,10 +489,11 @@ void Plan::plan_conv(const Op& op) {
     Hr = int(rh);
     Wr = int(rw);
   }
-  stats_.macs += double(N * Ho * Wo) * double(Cout) * double(C * KH * KW);
+  stats_.macs += double(N * Ho * Wo) * double(Cout) * double(C * KH * KW + C2);
   stats_.tc_kernels++;
   std::vector<DevTensor> reads{x};
   if (r.valid()) reads.push_back(r);
+  if (x2.valid()) reads.push_back(x2);
   const int sms = num_sms_;
   const bool f32 = tf32_;
   const bool round_out = tf32_ && !x3_ && feeds_tensor_ops(op.out[0]);   // next MMA reads it as TF32
@@ -503,7 +519,8 @@ void Plan::plan_conv(const Op& op) {
   const std::string kind = "conv " + std::to_string(KH) + "x" + std::to_string(KW) + "/" +
                            std::to_string(op.strides[0]) + " " + std::to_string(C) + "->" + std::to_string(Cout) +
                            " M=" + std::to_string(N * Ho * Wo) + " " + kAModeName[k::conv_gemm_a_mode(geo)] +
-                           (s2d ? " s2d" : "") + (op.residual >= 0 ? " +res" : "");
+                           (s2d ? " s2d" : "") + (op.residual >= 0 ? " +res" : "") +
+                           (op.concat >= 0 ? " +proj " + std::to_string(C2) : "");
   add_step(kind, reads, {y}, [=]() {
     auto p = std::make_shared<k::ConvGemmPlan>();
     k::ConvGemmArgs& a = p->args;
@@ -543,6 +560,11 @@ void Plan::plan_conv(const Op& op) {
     a.round_tf32 = round_out;
     a.x3 = x3;
     a.w_lo_row = int(w_lo_row);
+    if (x2.valid()) {
+      a.a2 = ptr(x2);
+      a.lda2 = C2;
+      a.a2_kt = int(Cp / (f32 ? 32 : 64));
+    }
     k::conv_gemm_prepare(*p, ptr(x), Cp, ptr(wt), sms);
     return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::conv_gemm_launch(*p, s); });
   });
@@ -971,6 +993,7 @@ void Plan::build() {
     for (int id : op.in)
       if (id >= 0) consumers_[size_t(id)].push_back(int(i));
     if (op.residual >= 0) consumers_[size_t(op.residual)].push_back(int(i));
+    if (op.concat >= 0) consumers_[size_t(op.concat)].push_back(int(i));
   }
   for (int id : g_.outputs) is_output_[size_t(id)] = true;
 
@@ -980,6 +1003,7 @@ void Plan::build() {
     if (op.dead) continue;
     std::vector<int> ids = op.in;
     if (op.residual >= 0) ids.push_back(op.residual);
+    if (op.concat >= 0) ids.push_back(op.concat);
     for (int id : ids) {
       if (id < 0 || vt_[size_t(id)].valid()) continue;
       const Value& v = g_.vals[size_t(id)];

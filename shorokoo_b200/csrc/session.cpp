@@ -172,6 +172,7 @@ bool batch_separable(const LGraph& g) {
         t == "AveragePool") {
       if (a0 != 0) return false;
       if (op.residual >= 0 && ax[size_t(op.residual)] != 0) return false;
+      if (op.concat >= 0 && ax[size_t(op.concat)] != 0) return false;
       out = 0;
     } else if (t == "FusedGemm") {
       if (a0 != 0 || g.vals[size_t(op.in[0])].shape.size() < 2) return false;
