@@ -422,7 +422,7 @@ int32_t sb_debug_lower(const uint8_t* model, size_t len, int32_t n_in, sb_value*
                std::to_string(op.strides[0]) + " pads=" + sb::shape_str(op.pads);
       if (op.act) out += " act=" + std::to_string(op.act);
       if (op.residual >= 0) out += " residual=" + std::to_string(op.residual_mode);
-      if (op.concat >= 0) out += " concat";
+      if (op.concat >= 0) out += " concat/" + std::to_string(op.concat_stride);
       out += "\n";
     }
     for (size_t j = 0; j < g.outputs.size(); ++j) {

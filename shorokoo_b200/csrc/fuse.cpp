@@ -43,13 +43,14 @@ Consumers consumers(const LGraph& g) {
   return c;
 }
 
-// A FusedConv that is a plain 1x1, stride-1, unpadded, ungrouped conv (no second operand yet).
-bool pointwise_conv(const Op& o) {
+// A FusedConv that is a plain 1x1, unpadded, ungrouped conv with stride 1 (or `stride` in both
+// dimensions) and no second operand yet.
+bool pointwise_conv(const Op& o, int64_t stride = 1) {
   if (o.dead || o.type != "FusedConv" || o.group != 1 || o.concat >= 0 || !o.weight) return false;
   const auto& w = o.weight->shape;
   if (w.size() != 4 || w[2] != 1 || w[3] != 1) return false;
   for (int64_t s : o.strides)
-    if (s != 1) return false;
+    if (s != stride) return false;
   for (int64_t d : o.dilations)
     if (d != 1) return false;
   for (int64_t p : o.pads)
@@ -57,11 +58,12 @@ bool pointwise_conv(const Op& o) {
   return true;
 }
 
-// Projection shortcut merged into the conv that adds it (the first bottleneck of a ResNet stage
-// whose shortcut is a 1x1 stride-1 conv, ResNet.cs:280-329): y = act(X1*W1 + b1 + (X0*Ws + bs)) is
-// one GEMM over X1's and X0's channels side by side, y = act([X1 X0] * [W1; Ws] + (b1 + bs)), so
-// the shortcut's output is neither written nor read back. Both channel counts must be multiples
-// of 64, so each operand fills whole k-tiles in every precision.
+// Projection shortcut merged into the conv that adds it (the first bottleneck of a ResNet stage,
+// ResNet.cs:280-329): y = act(X1*W1 + b1 + (X0*Ws + bs)) is one GEMM over X1's and X0's channels
+// side by side, y = act([X1 X0] * [W1; Ws] + (b1 + bs)), so the shortcut's output is neither
+// written nor read back. The shortcut may be strided (1x1 stride 2: X0 is then read at every other
+// pixel). Both channel counts must be multiples of 64, so each operand fills whole k-tiles in
+// every precision.
 void merge_projection_shortcuts(LGraph& g) {
   const Consumers cons = consumers(g);
   for (size_t i = 0; i < g.ops.size(); ++i) {
@@ -71,12 +73,17 @@ void merge_projection_shortcuts(LGraph& g) {
     const int pi = g.vals[size_t(r)].producer;
     if (pi < 0 || pi >= int(g.ops.size())) continue;
     Op& p = g.ops[size_t(pi)];
-    if (!pointwise_conv(p) || p.act != 0 || p.residual >= 0 || p.out.size() != 1 || p.out[0] != r) continue;
+    const int64_t ps = p.strides.empty() ? 1 : p.strides[0];
+    if ((ps != 1 && ps != 2) || !pointwise_conv(p, ps) || p.act != 0 || p.residual >= 0 || p.out.size() != 1 ||
+        p.out[0] != r)
+      continue;
     if (cons.is_output[size_t(r)] || cons.ops[size_t(r)].size() != 1) continue;
     const Value& x1 = g.vals[size_t(f.in[0])];
     const Value& x0 = g.vals[size_t(p.in[0])];
     if (x1.is_host || x0.is_host || x1.shape.size() != 4 || x0.shape.size() != 4) continue;
-    if (x1.shape[0] != x0.shape[0] || x1.shape[2] != x0.shape[2] || x1.shape[3] != x0.shape[3]) continue;
+    if (x1.shape[0] != x0.shape[0] || (x0.shape[2] - 1) / ps + 1 != x1.shape[2] ||
+        (x0.shape[3] - 1) / ps + 1 != x1.shape[3])
+      continue;
     const int64_t M = f.weight->shape[0], C1 = f.weight->shape[1], C0 = p.weight->shape[1];
     if (p.weight->shape[0] != M || C1 != x1.shape[1] || C0 != x0.shape[1] || C1 % 64 || C0 % 64) continue;
     auto w = std::make_shared<HostTensor>(DT_FLOAT, std::vector<int64_t>{M, C1 + C0, 1, 1});
@@ -94,6 +101,7 @@ void merge_projection_shortcuts(LGraph& g) {
     f.weight = w;
     f.bias = b;
     f.concat = p.in[0];
+    f.concat_stride = int(ps);
     f.residual = -1;
     p.dead = true;
   }

@@ -41,6 +41,7 @@ struct Op {
   int residual_mode = 0;         // 0 same shape, 1 nearest-2x upsampled source
   int concat = -1;               // FusedConv 1x1/s1: value id of a second activation whose channels
                                  // follow in[0]'s in the reduction (weight holds both blocks)
+  int concat_stride = 1;         // stride at which the second activation is sampled (1 or 2)
   std::shared_ptr<HostTensor> weight;   // folded weights (FusedConv: [M,C,KH,KW] f32; FusedGemm: [N,K] f32)
   std::shared_ptr<HostTensor> bias;     // folded bias [M] f32 (may be null)
 };

@@ -695,8 +695,17 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
           }
           mbar_expect_tx(&full[stage], (A_TMA ? A_BYTES : 0u) + (BRES ? 0u : B_STAGE));
           if (MODE == 0) {   // (k-tiles from a2_kt on come from the second operand, through tmRes)
-            if (A2 && kt >= a.a2_kt) tma_load_2d(sA + stage * A_STAGE, &tmRes, (kt - a.a2_kt) * BKE, mt * BM, &full[stage]);
-            else tma_load_2d(sA + stage * A_STAGE, &tmA, kt * BKE, mt * BM, &full[stage]);
+            if (A2 && kt >= a.a2_kt && a.a2_s > 0) {   // strided image: im2col of a 1x1 conv at stride s
+              const int m0 = mt * BM;
+              const int im = m0 / hw_out, rem = m0 - (m0 / hw_out) * hw_out;
+              const int ho = rem / a.Wo, wo = rem - (rem / a.Wo) * a.Wo;
+              tma_load_im2col(sA + stage * A_STAGE, &tmRes, (kt - a.a2_kt) * BKE, wo * a.a2_s, ho * a.a2_s, im, 0, 0,
+                              &full[stage]);
+            } else if (A2 && kt >= a.a2_kt) {
+              tma_load_2d(sA + stage * A_STAGE, &tmRes, (kt - a.a2_kt) * BKE, mt * BM, &full[stage]);
+            } else {
+              tma_load_2d(sA + stage * A_STAGE, &tmA, kt * BKE, mt * BM, &full[stage]);
+            }
           }
           if (MODE == 3) {
             const int tap = kt / cblocks, cb = kt - tap * cblocks;
@@ -1349,8 +1358,22 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   if (a.a2) {   // second A operand: a row matrix like the first, through the (then unused) tmRes map
     if (p.mode != kARows || a.res || a.a2_kt <= 0 || a.a2_kt >= KT)
       throw std::runtime_error("conv_gemm: a second A operand needs row-matrix A, no residual, a split inside K");
-    ok = ok && encode_2d(&p.tmRes, a.a2, uint64_t(a.lda2), uint64_t(a.M), uint64_t(a.lda2) * eb, uint32_t(bke), BM,
-                         a.tf32 != 0);
+    if (a.a2_s > 0) {   // an NHWC image read at stride a2_s: im2col map of a 1x1 conv, no padding
+      ConvGemmArgs t = a;
+      t.x = a.a2;
+      t.H = a.a2_H;
+      t.W = a.a2_W;
+      t.Cp = int(a.lda2);
+      t.KH = t.KW = 1;
+      t.sh = t.sw = a.a2_s;
+      t.ph = t.pw = 0;
+      t.dh = t.dw = 1;
+      if (!encode_im2col(&p.tmRes, t, bke))
+        throw std::runtime_error("cuTensorMapEncodeIm2col failed for the second A operand");
+    } else {
+      ok = ok && encode_2d(&p.tmRes, a.a2, uint64_t(a.lda2), uint64_t(a.M), uint64_t(a.lda2) * eb, uint32_t(bke), BM,
+                           a.tf32 != 0);
+    }
   }
   if (!ok) throw std::runtime_error("cuTensorMapEncodeTiled failed (driver entry point missing or bad layout)");
   if ((p.mode == kAIm2col64 || p.mode == kAIm2col16) && !encode_im2col(&p.tmA, a, p.mode == kAIm2col64 ? bke : 16))

@@ -47,6 +47,9 @@ struct ConvGemmArgs {
                            // k-tiles a2_kt.. (a merged projection shortcut's input), or null
   int64_t lda2;            // its row pitch in elements
   int a2_kt;               // first k-tile read from a2 (k-tile kt reads its k-tile kt - a2_kt)
+  int a2_s;                // 0: a2 is a row matrix [M, lda2]; s > 0: a2 is an NHWC image
+                           // [N, a2_H, a2_W, lda2] read at stride s (output pixel (ho, wo) -> (s ho, s wo))
+  int a2_H, a2_W;
   int res_mma;             // 1: the tensor core adds the bf16 residual: after the tile's k-tiles come
                            // one k-tile per 64 residual channels, A = the residual rows (TMA), B = a
                            // 64x64 identity in shared memory, accumulated into those 64 columns

@@ -426,8 +426,10 @@ void Plan::plan_conv(const Op& op) {
   if (op.concat >= 0) {
     C2 = Wt.shape[1] - C;
     const Value& cv = g_.vals[size_t(op.concat)];
+    const int64_t cs = op.concat_stride;
     SB_CHECK(one_by_one && Cp == C && C % 64 == 0 && C2 > 0 && C2 % 64 == 0 && cv.shape.size() == 4 &&
-                 cv.shape[0] == N && cv.shape[1] == C2 && cv.shape[2] == H && cv.shape[3] == W,
+                 cv.shape[0] == N && cv.shape[1] == C2 && (cs == 1 || cs == 2) && (cv.shape[2] - 1) / cs + 1 == H &&
+                 (cv.shape[3] - 1) / cs + 1 == W,
              SB_UNSUPPORTED, "Conv: concatenated operand layout");
     x2 = as_nhwc_op(op.concat, int(C2));
   }
@@ -564,6 +566,9 @@ void Plan::plan_conv(const Op& op) {
       a.a2 = ptr(x2);
       a.lda2 = C2;
       a.a2_kt = int(Cp / (f32 ? 32 : 64));
+      a.a2_s = op.concat_stride > 1 ? int(op.concat_stride) : 0;
+      a.a2_H = int(x2.shape[2]);
+      a.a2_W = int(x2.shape[3]);
     }
     k::conv_gemm_prepare(*p, ptr(x), Cp, ptr(wt), sms);
     return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::conv_gemm_launch(*p, s); });

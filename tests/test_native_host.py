@@ -75,20 +75,22 @@ def kinds(lines):
 def test_lowering_resnet50_fuses_everything():
     lines = lower(graphs.resnet(depth=50, batch=2, hw=(64, 64)))
     k = kinds(lines)
-    # 53 convs, less the stage-1 projection shortcut (1x1 stride 1), merged into the conv that adds it
-    assert k == {"FusedConv": 52, "MaxPool": 1, "GlobalAveragePool": 1, "Reshape": 1, "FusedGemm": 1}, k
+    # 53 convs, less the four projection shortcuts (1x1, stride 1 in stage 1 and 2 after it), each
+    # merged into the conv that adds it
+    assert k == {"FusedConv": 49, "MaxPool": 1, "GlobalAveragePool": 1, "Reshape": 1, "FusedGemm": 1}, k
     stem = [l for l in lines if l.startswith("FusedConv")][0]
     assert "k=7x7 s=2 pads=[3,3,3,3]" in stem and "act=1" in stem   # Pad folded, BN folded, ReLU fused
-    assert sum("residual=0" in l for l in lines) == 15                # one residual add per other bottleneck
+    assert sum("residual=0" in l for l in lines) == 12                # one residual add per other bottleneck
     merged = [l for l in lines if "concat" in l]
-    assert len(merged) == 1 and "k=1x1 s=1" in merged[0] and "act=1" in merged[0], merged
+    assert len(merged) == 4 and all("k=1x1 s=1" in l and "act=1" in l for l in merged), merged
+    assert sum("concat/1" in l for l in merged) == 1 and sum("concat/2" in l for l in merged) == 3
     assert lines[-1] == "separable=1"
 
 
 def test_lowering_live_hypers_and_dead_code():
     case = graphs.resnet(depth=50, batch=2, hw=(64, 64), live_hypers=True, dead_code=True)
     k = kinds(lower(case))
-    assert k["FusedConv"] == 52 and k["FusedGemm"] == 1      # dead shortcut convs pruned
+    assert k["FusedConv"] == 49 and k["FusedGemm"] == 1      # dead shortcut convs pruned
     case = graphs.resnet(depth=18, batch=2, hw=(64, 64), live_hypers=True, apply_softmax=True)
     assert kinds(lower(case))["Softmax"] == 1
     # includeTop=false drops the head entirely
@@ -109,7 +111,7 @@ def test_lowering_unrolls_live_loop():
 def test_lowering_retinanet_heads_are_views():
     lines = lower(graphs.retinanet(batch=1, hw=(128, 160)))
     k = kinds(lines)
-    assert k["FusedConv"] == 110                             # (the backbone's stage-1 shortcut merged)
+    assert k["FusedConv"] == 107                             # (the backbone's four shortcuts merged)
     assert sum("residual=1" in l for l in lines) == 2        # FPN top-down adds with nearest-2x upsample
     assert k["Concat"] == 2 and k["Sigmoid"] == 1
     assert [l for l in lines if l.startswith("output")] == ["output [1,3852,80] device", "output [1,3852,4] device"]
