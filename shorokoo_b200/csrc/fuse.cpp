@@ -66,29 +66,44 @@ bool pointwise_conv(const Op& o, int64_t stride = 1) {
 // every precision.
 void merge_projection_shortcuts(LGraph& g) {
   const Consumers cons = consumers(g);
+  auto uniform_stride = [](const Op& o) -> int64_t {
+    if (o.strides.empty()) return 1;
+    for (int64_t s : o.strides)
+      if (s != o.strides[0]) return 0;
+    return o.strides[0];
+  };
   for (size_t i = 0; i < g.ops.size(); ++i) {
-    Op& f = g.ops[i];
-    if (!pointwise_conv(f) || f.residual < 0 || f.residual_mode != 0) continue;
+    Op& f = g.ops[i];   // the conv that absorbed the Add (its residual is the other conv's output)
+    const int64_t sf = f.dead ? 0 : uniform_stride(f);
+    if ((sf != 1 && sf != 2) || !pointwise_conv(f, sf) || f.residual < 0 || f.residual_mode != 0) continue;
     const int r = f.residual;
     const int pi = g.vals[size_t(r)].producer;
     if (pi < 0 || pi >= int(g.ops.size())) continue;
     Op& p = g.ops[size_t(pi)];
-    const int64_t ps = p.strides.empty() ? 1 : p.strides[0];
-    if ((ps != 1 && ps != 2) || !pointwise_conv(p, ps) || p.act != 0 || p.residual >= 0 || p.out.size() != 1 ||
+    const int64_t sp = p.dead ? 0 : uniform_stride(p);
+    if ((sp != 1 && sp != 2) || !pointwise_conv(p, sp) || p.act != 0 || p.residual >= 0 || p.out.size() != 1 ||
         p.out[0] != r)
       continue;
     if (cons.is_output[size_t(r)] || cons.ops[size_t(r)].size() != 1) continue;
-    const Value& x1 = g.vals[size_t(f.in[0])];
-    const Value& x0 = g.vals[size_t(p.in[0])];
+    // main: the stride-1 conv (its input X1 is the GEMM's first operand); shortcut: the other (X0,
+    // read at its stride). Either may be the one that absorbed the Add, depending on node order.
+    if (sf != 1 && sp != 1) continue;
+    const bool f_main = sf == 1;
+    const Op& mo = f_main ? f : p;
+    const Op& so = f_main ? p : f;
+    const int64_t ss = f_main ? sp : sf;
+    const int x1id = mo.in[0], x0id = so.in[0];
+    const Value& x1 = g.vals[size_t(x1id)];
+    const Value& x0 = g.vals[size_t(x0id)];
     if (x1.is_host || x0.is_host || x1.shape.size() != 4 || x0.shape.size() != 4) continue;
-    if (x1.shape[0] != x0.shape[0] || (x0.shape[2] - 1) / ps + 1 != x1.shape[2] ||
-        (x0.shape[3] - 1) / ps + 1 != x1.shape[3])
+    if (x1.shape[0] != x0.shape[0] || (x0.shape[2] - 1) / ss + 1 != x1.shape[2] ||
+        (x0.shape[3] - 1) / ss + 1 != x1.shape[3])
       continue;
-    const int64_t M = f.weight->shape[0], C1 = f.weight->shape[1], C0 = p.weight->shape[1];
-    if (p.weight->shape[0] != M || C1 != x1.shape[1] || C0 != x0.shape[1] || C1 % 64 || C0 % 64) continue;
+    const int64_t M = mo.weight->shape[0], C1 = mo.weight->shape[1], C0 = so.weight->shape[1];
+    if (so.weight->shape[0] != M || C1 != x1.shape[1] || C0 != x0.shape[1] || C1 % 64 || C0 % 64) continue;
     auto w = std::make_shared<HostTensor>(DT_FLOAT, std::vector<int64_t>{M, C1 + C0, 1, 1});
-    const float* w1 = f.weight->ptr<float>();
-    const float* w0 = p.weight->ptr<float>();
+    const float* w1 = mo.weight->ptr<float>();
+    const float* w0 = so.weight->ptr<float>();
     float* wp = w->mptr<float>();
     for (int64_t m = 0; m < M; ++m) {
       for (int64_t c = 0; c < C1; ++c) wp[m * (C1 + C0) + c] = w1[m * C1 + c];
@@ -98,10 +113,13 @@ void merge_projection_shortcuts(LGraph& g) {
     float* bp = b->mptr<float>();
     for (int64_t m = 0; m < M; ++m)
       bp[m] = (f.bias ? f.bias->ptr<float>()[m] : 0.f) + (p.bias ? p.bias->ptr<float>()[m] : 0.f);
+    // the merged conv keeps f's slot, output and activation
+    f.in[0] = x1id;
+    f.strides.assign(f.strides.size(), 1);
     f.weight = w;
     f.bias = b;
-    f.concat = p.in[0];
-    f.concat_stride = int(ps);
+    f.concat = x0id;
+    f.concat_stride = int(ss);
     f.residual = -1;
     p.dead = true;
   }

@@ -2,8 +2,9 @@
 
 Shapes cover the edge cases of the tiling: M/N/K tails (not multiples of 128 / 64 / 64), tiny
 problems (fewer tiles than SMs), every N-tile width, TMA-fed 1x1 convs, im2col-gathered spatial
-convs (stride 2, SAME_UPPER asymmetric pads, dilation), the 4-channel stem path, and the fused
-epilogues (folded affine, residual, nearest-2x upsampled residual, ReLU, Sigmoid)."""
+convs (stride 2, SAME_UPPER asymmetric pads, dilation), the 4-channel stem path, the fused
+epilogues (folded affine, residual, nearest-2x upsampled residual, ReLU, Sigmoid), and projection
+shortcuts merged into the conv that adds them."""
 import numpy as np
 import pytest
 
@@ -158,3 +159,42 @@ def test_conv_chain_64_column_tiles(cmid):
     ref = run_oracle(case)[0]
     assert got.shape == (n, 16, h, w)
     assert_close(got, ref, what=f"conv chain through {cmid} channels")
+
+
+def _conv_s(B, x, cin, cout, k, stride=1, relu=False, res=None):
+    from shorokoo_b200.emit.graphs import kaiming_normal
+    w = B.init(kaiming_normal(B.rng, (cout, cin, k, k)), "w")
+    b = B.init((0.3 * B.rng.standard_normal(cout)).astype(np.float32), "b")
+    y = B.op("Conv", [x, w, b], auto_pad="NOTSET", dilations=[1, 1], group=1, kernel_shape=[k, k],
+             pads=[k // 2] * 4, strides=[stride, stride])
+    if res is not None:
+        y = B.op("Add", [y, res])
+    return B.op("Relu", [y]) if relu else y
+
+
+# A bottleneck whose 1x1 projection shortcut (stride 1, or stride 2 over an odd-sized map) is merged
+# into the last 1x1 conv: one GEMM over both operands' channels, the shortcut's input read through
+# a second tensor map (row matrix, or im2col at the shortcut's stride).
+@pytest.mark.parametrize("stride,h,w,cout", [(1, 12, 10, 256), (2, 15, 13, 256), (2, 16, 16, 192)])
+def test_merged_projection_shortcut(stride, h, w, cout):
+    from shorokoo_b200.emit import onnx_writer as W
+    from shorokoo_b200.emit.graphs import Builder, ModelCase
+    rng = np.random.Generator(np.random.PCG64(31))
+    n, c = 2, 128
+    x = rng.standard_normal((n, c, h, w), dtype=np.float32)
+    B = Builder(32)
+    xi = B.graph_input(W.FLOAT, 4, x.shape)
+    ho, wo = (h - 1) // stride + 1, (w - 1) // stride + 1
+    a = _conv_s(B, xi, c, 64, 1, relu=True)
+    bb = _conv_s(B, a, 64, 64, 3, stride=stride, relu=True)
+    sc = _conv_s(B, xi, c, cout, 1, stride=stride)
+    y = _conv_s(B, bb, 64, cout, 1, relu=True, res=sc)
+    z = _conv_s(B, y, cout, 16, 1)   # y feeds a conv, so the merged conv writes bf16
+    for t, ch, hh, ww in ((a, 64, h, w), (bb, 64, ho, wo), (sc, cout, ho, wo), (y, cout, ho, wo), (z, 16, ho, wo)):
+        B.shape[t] = (n, ch, hh, ww)
+    B.outputs.append(W.ValueInfo(z))
+    case = ModelCase("merged_shortcut", B.model("merged_shortcut"), [(xi, x)], [z], 0)
+    got = run_backend(case)[0]
+    ref = run_oracle(case)[0]
+    assert got.shape == (n, 16, ho, wo)
+    assert_close(got, ref, what=f"bottleneck with merged stride-{stride} shortcut {h}x{w}")
