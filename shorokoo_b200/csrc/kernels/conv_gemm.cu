@@ -1230,16 +1230,17 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   const int bke = a.tf32 ? BK / 2 : BK;   // operand elements per 128-byte k-tile row
   if (a.Kpad % bke) throw std::runtime_error("conv_gemm: reduction length not padded to a whole k-tile");
   const int KT = a.Kpad / bke;
-  // bf16 convs with a single weight k-tile (the 1x1 convs from 64 channels, whose epilogue sets the
-  // pace) start each accumulator at the bias with one extra MMA, so the epilogue adds none. Measured
-  // on ResNet-50 bs512: 1x1 64->64 0.118 -> 0.107 ms, 64->256 -17%; convs with more k-tiles or
-  // wider bias tiles lost 1-7% (the extra MMA on the issue path, the bias tile's shared memory).
+  // bf16 convs with one or two weight k-tiles (the 1x1 convs from 64 channels, whose epilogue sets
+  // the pace) start each accumulator at the bias with one extra MMA, so the epilogue adds none.
+  // Measured on ResNet-50 bs512: 1x1 64->64 0.118 -> 0.107 ms, 64->256 -17%, the stage-1 conv with
+  // its merged shortcut (two k-tiles) 0.245 -> 0.210 ms; convs with more k-tiles or wider bias tiles
+  // lost 1-7% (the extra MMA on the issue path, the bias tile's shared memory).
   static const bool bias_mma_on = [] {
     const char* e = std::getenv("SHOROKOO_B200_BIAS_MMA");
     return !(e && e[0] == '0');
   }();
   const int bias_rows = int((a.Cout + bn - 1) / bn) * bn;
-  a.bias_mma = bias_mma_on && !a.tf32 && !a.x3 && a.bias && KT == 1 && bias_rows <= 256 ? 1 : 0;
+  a.bias_mma = bias_mma_on && !a.tf32 && !a.x3 && a.bias && KT <= 2 && bias_rows <= 256 ? 1 : 0;
   const int64_t w_bytes = int64_t(KT) * bn * 128;
   bool bres = !a.x3 && p.mode != kAGather16 && p.mode != kAGather8 && a.Cout <= bn && w_bytes <= 96 * 1024;
   if (const char* e = std::getenv("SHOROKOO_B200_BRES"))
