@@ -1260,6 +1260,9 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   const bool inplace_hint = res_ring && out_ok && KT >= 8;
   // (the cp.async gather modes have no spare warps: their warps 10-13 gather, so one issuer)
   int pl = !a.x3 && !gather && (im2col || inplace_hint) && bn <= 128 ? 2 : 1;   // X3: warps 13-15 split
+  // 64-column im2col convs with 128-byte pixels (ResNet's layer-1 3x3 convs) take four issuers:
+  // 0.203 -> 0.196 ms at bs512 (the 16-channel stem lost 10% with four, its epilogue summing them).
+  if (pl == 2 && p.mode == kAIm2col64 && bn == 64 && KT >= 4) pl = 4;
   if (const char* e = std::getenv("SHOROKOO_B200_MMA_LANES"))   // 1, 2 or 4 where TMEM holds them
     if (!a.x3 && !gather) pl = std::atoi(e) >= 4 ? 4 : (std::atoi(e) >= 2 ? 2 : 1);
   while (pl > 1 && 2 * pl * bn > 512) pl /= 2;
