@@ -164,3 +164,52 @@ def test_shape_errors_at_lowering():
     bad = [(case.inputs[0][0], np.zeros((4, 15), np.float32))]
     with pytest.raises(RuntimeError, match="inner dimensions|MatMul"):
         lower(case, bad)
+
+
+def _bottleneck(c=128, cmid=64, cout=256, stride=2, h=15, w=13, shortcut_relu=False, shortcut_output=False):
+    from shorokoo_b200.emit import onnx_writer as W
+    from shorokoo_b200.emit.graphs import Builder, ModelCase, kaiming_normal
+
+    def conv(B, x, cin, co, k, s=1, relu=False, res=None):
+        wt = B.init(kaiming_normal(B.rng, (co, cin, k, k)), "w")
+        b = B.init(np.zeros(co, np.float32), "b")
+        y = B.op("Conv", [x, wt, b], auto_pad="NOTSET", dilations=[1, 1], group=1, kernel_shape=[k, k],
+                 pads=[k // 2] * 4, strides=[s, s])
+        if res is not None:
+            y = B.op("Add", [y, res])
+        return B.op("Relu", [y]) if relu else y
+
+    x = np.zeros((2, c, h, w), np.float32)
+    B = Builder(5)
+    xi = B.graph_input(W.FLOAT, 4, x.shape)
+    ho, wo = (h - 1) // stride + 1, (w - 1) // stride + 1
+    a = conv(B, xi, c, cmid, 1, relu=True)
+    bb = conv(B, a, cmid, cmid, 3, s=stride, relu=True)
+    sc = conv(B, xi, c, cout, 1, s=stride, relu=shortcut_relu)
+    y = conv(B, bb, cmid, cout, 1, relu=True, res=sc)
+    for t, ch, hh, ww in ((a, cmid, h, w), (bb, cmid, ho, wo), (sc, cout, ho, wo), (y, cout, ho, wo)):
+        B.shape[t] = (2, ch, hh, ww)
+    B.outputs.append(W.ValueInfo(y))
+    outs = [y]
+    if shortcut_output:
+        B.outputs.append(W.ValueInfo(sc))
+        outs.append(sc)
+    return ModelCase("bottleneck", B.model("bottleneck"), [(xi, x)], outs, 0)
+
+
+# The projection shortcut is merged into the conv that adds it only when that is exact and the
+# kernel can read both operands in whole k-tiles.
+@pytest.mark.parametrize("kw,merged", [
+    (dict(), True),                              # stride-2 shortcut over an odd-sized map
+    (dict(stride=1, h=12, w=10), True),
+    (dict(shortcut_output=True), False),         # the shortcut's output is also a graph output
+    (dict(c=96), False),                         # 96 input channels: not whole 64-channel k-tiles
+    (dict(cmid=48), False),
+    (dict(shortcut_relu=True), False),           # an activation of its own: not a linear term
+])
+def test_projection_shortcut_merge_conditions(kw, merged):
+    lines = lower(_bottleneck(**kw))
+    k = kinds(lines)
+    got = [l for l in lines if "concat" in l]
+    assert bool(got) == merged, lines
+    assert k["FusedConv"] == (3 if merged else 4), k
