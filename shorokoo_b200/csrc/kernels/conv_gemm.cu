@@ -114,7 +114,6 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, int c0, int 
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -398,10 +397,7 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
   const int lane = threadIdx.x & 31;
   const int m = row0 + lane;
   const int rrow = (row0 & (BM - 1)) + lane;   // row inside the 128-row residual slab
-  if (lane == 0) {   // the last store from this buffer has been read (1: one buffer, 2: two)
-    if (wait_mode == 2) bulk_wait_read1();
-    else if (wait_mode == 1) bulk_wait_read0();
-  }
+  if (lane == 0 && wait_mode == 1) bulk_wait_read0();   // the last store from this slab has been read
   __syncwarp();
   const int h_begin = half >= 0 ? half : 0;
   const int h_end = half >= 0 ? half + 1 : SC / 32;
@@ -868,7 +864,6 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
     };
     float bpre[4];
     load_bias(blockIdx.x, bpre);
-    int nslab = 0;   // slabs stored by this warp so far (selects the buffer)
     int it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
       const int mt = t / tiles_n, nt = t - (t / tiles_n) * tiles_n;
@@ -888,7 +883,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
         if (a.epi == 2 && ehalf) {   // bf16 output, one 64-column slab: both warps, a half each
           if (nt * BN + hsel * 32 < a.Cout) {
             const uint8_t* rslab = RS ? sRes + slot * RSB : nullptr;
-            uint8_t* sb = sb0 + (OB == 2 ? (nslab++ & 1) * SLAB : 0);
+            uint8_t* sb = sb0;
             epilogue_slab<true>(a, &tmOut, tbase, 0, row0, nt * BN, sb, rslab, wbias, OB, PE, BN, hsel);
           }
         } else if (a.epi == 2) {
@@ -901,7 +896,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
             // released once that store has read it. Otherwise the warp's own output slab(s).
             const bool inplace = RS && OB == 0;
             uint8_t* sb = inplace ? sRes + slot * RSB + s2 * 128 * 128 + q * 32 * 128
-                                  : sb0 + (OB == 2 ? (nslab++ & 1) * SLAB : 0);
+                                  : sb0;
             const int wm = inplace ? 0 : OB;
             const float* bsl = wbias + ((s2 - hsel) >> 1) * SC;
             if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl, wm, PE, BN);
@@ -1156,16 +1151,12 @@ int conv_gemm_a_mode(const ConvGemmArgs& a) {
   if (!a.gather) return kARows;
   // TMA im2col: the corner box must fit the map's signed 8-bit corner fields and the tap offsets
   // its 8-bit offset fields; activations under 128 KiB keep the cp.async gather.
-  static const bool im2col_on = [] {
-    const char* e = std::getenv("SHOROKOO_B200_IM2COL");
-    return !(e && e[0] == '0');
-  }();
   const int up_w = im2col_upper(a.W, a.Wo, a.sw, a.pw), up_h = im2col_upper(a.H, a.Ho, a.sh, a.ph);
   const bool box_ok = a.pw <= 128 && a.ph <= 128 && up_w >= -128 && up_w <= 127 && up_h >= -128 && up_h <= 127 &&
                       (a.KW - 1) * a.dw <= 255 && (a.KH - 1) * a.dh <= 255 && a.sw <= 8 && a.sh <= 8;
   const int eb = a.tf32 ? 4 : 2;
   const bool big = int64_t(a.N) * a.H * a.W * a.Cp * eb >= (int64_t(1) << 17);
-  if (im2col_on && box_ok && big) {
+  if (box_ok && big) {
     if ((a.Cp * eb) % 128 == 0) return kAIm2col64;   // 128-byte channel blocks
     if (!a.tf32 && a.Cp == 16 && (a.KH * a.KW) % 4 == 0) return kAIm2col16;
   }
@@ -1186,20 +1177,14 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   a.epi = 0;
   a.res_slots = 0;
   a.res_slot_bytes = 0;
-  int want = 2;
-  if (const char* e = std::getenv("SHOROKOO_B200_EPI")) want = std::atoi(e);
-  const bool out_ok = want != 0 && a.group_rows == 0 && a.Cout % epc == 0 && (a.ldo * es) % 16 == 0 &&
+  const bool out_ok = a.group_rows == 0 && a.Cout % epc == 0 && (a.ldo * es) % 16 == 0 &&
                       (reinterpret_cast<uintptr_t>(a.out) & 15) == 0;
   p.mode = conv_gemm_a_mode(a);
   // A bf16 residual of a bf16 conv whose A operand comes by TMA is added by the tensor core (one
   // extra k-tile per 64 channels against an identity operand), which takes the residual off the
   // epilogue's per-element work; otherwise it streams through a shared-memory ring (below) or is
   // read directly by the epilogue.
-  static const bool res_mma_on = [] {
-    const char* e = std::getenv("SHOROKOO_B200_RES_MMA");
-    return !(e && e[0] == '0');
-  }();
-  const bool res_mma = res_mma_on && out_ok && a.res && a.res_mode == 0 && a.res_bf16 && !a.tf32 && !a.x3 &&
+  const bool res_mma = out_ok && a.res && a.res_mode == 0 && a.res_bf16 && !a.tf32 && !a.x3 &&
                        (p.mode == kARows || p.mode == kAIm2col64) && (a.ldr * 2) % 16 == 0 &&
                        (reinterpret_cast<uintptr_t>(a.res) & 15) == 0;
   a.res_mma = 0;
@@ -1235,16 +1220,10 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   // Measured on ResNet-50 bs512: 1x1 64->64 0.118 -> 0.107 ms, 64->256 -17%, the stage-1 conv with
   // its merged shortcut (two k-tiles) 0.245 -> 0.210 ms; convs with more k-tiles or wider bias tiles
   // lost 1-7% (the extra MMA on the issue path, the bias tile's shared memory).
-  static const bool bias_mma_on = [] {
-    const char* e = std::getenv("SHOROKOO_B200_BIAS_MMA");
-    return !(e && e[0] == '0');
-  }();
   const int bias_rows = int((a.Cout + bn - 1) / bn) * bn;
-  a.bias_mma = bias_mma_on && !a.tf32 && !a.x3 && a.bias && KT <= 2 && bias_rows <= 256 ? 1 : 0;
+  a.bias_mma = !a.tf32 && !a.x3 && a.bias && KT <= 2 && bias_rows <= 256 ? 1 : 0;
   const int64_t w_bytes = int64_t(KT) * bn * 128;
-  bool bres = !a.x3 && p.mode != kAGather16 && p.mode != kAGather8 && a.Cout <= bn && w_bytes <= 96 * 1024;
-  if (const char* e = std::getenv("SHOROKOO_B200_BRES"))
-    if (e[0] == '0') bres = false;
+  const bool bres = !a.x3 && p.mode != kAGather16 && p.mode != kAGather8 && a.Cout <= bn && w_bytes <= 96 * 1024;
   a.b_resident = bres ? 1 : 0;
   // MMA-issuing threads: as many split-K partial accumulators as double-buffered TMEM holds, at
   // most the number of k-tiles.
@@ -1263,8 +1242,6 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   // 64-column im2col convs with 128-byte pixels (ResNet's layer-1 3x3 convs) take four issuers:
   // 0.203 -> 0.196 ms at bs512 (the 16-channel stem lost 10% with four, its epilogue summing them).
   if (pl == 2 && p.mode == kAIm2col64 && bn == 64 && KT >= 4) pl = 4;
-  if (const char* e = std::getenv("SHOROKOO_B200_MMA_LANES"))   // 1, 2 or 4 where TMEM holds them
-    if (!a.x3 && !gather) pl = std::atoi(e) >= 4 ? 4 : (std::atoi(e) >= 2 ? 2 : 1);
   while (pl > 1 && 2 * pl * bn > 512) pl /= 2;
   while (pl > KT) pl /= 2;
   if (gather && pl != 1) throw std::runtime_error("conv_gemm: gather modes have a single MMA issuer");
@@ -1284,18 +1261,13 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   }
   // Shared memory: operand stages + output slabs + bias + residual ring (two slots when two
   // operand stages still fit beside them). In-place residual convs have no output slabs;
-  // otherwise one slab per epilogue warp. A second slab per warp lets a store
-  // drain while the next slab is computed, but measured on ResNet-50 the operand stages it costs
-  // are worth more, so it is opt-in (SHOROKOO_B200_OUTBUF=2).
+  // otherwise one slab per epilogue warp (a second slab per warp, letting a store drain while the
+  // next slab is computed, measured slower on ResNet-50: the operand stages it costs are worth more).
   // bf16 output of 64-column tiles is one 128-byte slab per 32 rows, which would leave one of each
   // TMEM quarter's two epilogue warps idle: it is split into two 32-column halves, one per warp,
   // each stored from its own 64-byte slab through a 32x32 box (not for in-place output, whose slab
   // is the residual ring's 128-byte layout). The halved slabs also leave room for more stages.
-  static const bool half_on = [] {
-    const char* e = std::getenv("SHOROKOO_B200_EPI_HALF");
-    return !(e && e[0] == '0');
-  }();
-  auto half_for = [&](int ob) { return half_on && a.epi == 2 && a.out_bf16 && bn == 64 && ob != 0; };
+  auto half_for = [&](int ob) { return a.epi == 2 && a.out_bf16 && bn == 64 && ob != 0; };
   auto fixed_for = [&](int ob) {
     return int(8 * ob * (half_for(ob) ? kOutSlab / 2 : kOutSlab) + kBiasStage) + 1024 + 512 + (bres ? int(w_bytes) : 0) + (a.res_mma ? int(kIdBytes) : 0) +
            (a.bias_mma ? int(kOnesBytes) + bias_rows * 32 : 0);
@@ -1307,8 +1279,6 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   };
   auto stages_for = [&](int ob, int rs) { return std::min(kMaxStages, (kSmemLimit - fixed_for(ob) - rs * rsb) / stage_bytes); };
   int ob = ring && KT >= 8 ? 0 : 1;
-  if (ob != 0)
-    if (const char* e = std::getenv("SHOROKOO_B200_OUTBUF")) ob = std::atoi(e) == 2 ? 2 : 1;
   int rs = ring_for(ob);
   if (rs == 0 && ob == 0) ob = 1;   // writing in place needs a residual ring
   const int smax = stages_for(ob, rs);

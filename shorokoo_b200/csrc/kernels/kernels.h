@@ -42,7 +42,8 @@ struct ConvGemmArgs {
   int stages;              // operand pipeline depth
   int res_slots;           // residual ring slots filled by the producer warp (0: direct residual reads)
   int res_slot_bytes;
-  int out_bufs;            // output slab buffers per epilogue warp (1, or 2 to overlap stores)
+  int out_bufs;            // output slabs per epilogue warp: 1, or 0 when the output is written in
+                           // place over the residual ring
   const void* a2;          // second A operand (a row matrix like the first, row mode only) supplying
                            // k-tiles a2_kt.. (a merged projection shortcut's input), or null
   int64_t lda2;            // its row pitch in elements

@@ -10,7 +10,10 @@
 // That scratch is one file-scope device array of kNoAllocScratchBytes (16 MiB), present on every
 // GPU that loads this library until the process exits. Host code cannot use the array's name as a
 // device address (it names a host-side stand-in), so each device's address is looked up once with
-// cudaGetSymbolAddress while that device is current, on the first call for the device.
+// cudaGetSymbolAddress while that device is current, on the first call for the device. The address
+// is cached per device ordinal, which holds for the CUDA runtime's primary context of that device
+// (the context every runtime-API caller uses); a caller that makes its own driver-API context
+// current gets a different per-context address from the lookup, which this cache does not track.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -32,7 +35,8 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-std::atomic<void*> g_scratch_ptr[kMaxDevices];
+std::atomic<void*> g_scratch_ptr[kMaxDevices];   // device address of the array, per device
+std::atomic<int> g_sm_count[kMaxDevices];         // multiprocessors, per device (0: not looked up)
 std::mutex g_setup_mu;
 
 size_t up256(size_t n) { return (n + 255) / 256 * 256; }
@@ -64,14 +68,21 @@ extern "C" int32_t sb_linear_noalloc(const float* x, const float* w, const float
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return fail(SB_STATUS_CUDA_ERROR, "sb_linear_noalloc: no current CUDA device");
   void* base = g_scratch_ptr[dev].load();
-  if (!base) {   // first call on this device: find the device address of the scratch array
+  int sms = g_sm_count[dev].load();
+  if (!base || sms <= 0) {   // first call on this device: the scratch array's address, the SM count
     std::lock_guard<std::mutex> l(g_setup_mu);
     base = g_scratch_ptr[dev].load();
+    sms = g_sm_count[dev].load();
     if (!base) {
       cudaError_t e = cudaGetSymbolAddress(&base, g_noalloc_scratch);
       if (e != cudaSuccess || !base)
         return fail(SB_STATUS_CUDA_ERROR, std::string("sb_linear_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
       g_scratch_ptr[dev].store(base);
+    }
+    if (sms <= 0) {
+      if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+        return fail(SB_STATUS_CUDA_ERROR, "sb_linear_noalloc: cannot read the multiprocessor count");
+      g_sm_count[dev].store(sms);
     }
   }
   uint8_t* p = static_cast<uint8_t*>(base);
@@ -88,9 +99,6 @@ extern "C" int32_t sb_linear_noalloc(const float* x, const float* w, const float
   if (e == cudaSuccess) e = sb::k::to_rows_bf16(w, 0, N, K, K, 1, ws, Kpad, s);
   if (e != cudaSuccess) return fail(SB_STATUS_CUDA_ERROR, std::string("sb_linear_noalloc: ") + cudaGetErrorString(e));
 
-  cudaDeviceProp prop;
-  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess)
-    return fail(SB_STATUS_CUDA_ERROR, "sb_linear_noalloc: cudaGetDeviceProperties failed");
   sb::k::ConvGemmPlan plan;
   std::memset(&plan, 0, sizeof(plan));
   sb::k::ConvGemmArgs& a = plan.args;
@@ -110,7 +118,7 @@ extern "C" int32_t sb_linear_noalloc(const float* x, const float* w, const float
   a.act = relu ? 1 : 0;
   a.err = err;
   try {
-    sb::k::conv_gemm_prepare(plan, xs, Kp, ws, prop.multiProcessorCount);
+    sb::k::conv_gemm_prepare(plan, xs, Kp, ws, sms);
   } catch (const std::exception& ex) {
     return fail(SB_STATUS_CUDA_ERROR, std::string("sb_linear_noalloc: ") + ex.what());
   }

@@ -1,9 +1,9 @@
 #!/usr/bin/env python3
 """Regenerates the golden fixtures in this directory from the reference's own Python references.
 
-Run inside a checkout that has the reference tree (default /root/reference, or --reference PATH):
+Run where the reference tree is checked out, giving its root:
 
-    python tests/golden/gen_golden.py
+    python tests/golden/gen_golden.py --reference PATH/TO/Shorokoo
 
 * ``linear_pytorchref.npz`` — the reference's PyTorch Linear script
   (tests/pytorch-reference/linear.py, the generator behind NNLinearMatchesPyTorch,
@@ -85,7 +85,7 @@ def gen_resnet18(ref_root: str) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of the reference checkout")
     a = ap.parse_args()
     gen_linear(a.reference)
     gen_resnet18(a.reference)
