@@ -103,7 +103,10 @@ SB_API int32_t sb_session_run(sb_session* session, int32_t n_inputs, const char*
 SB_API int32_t sb_value_create_tensor(int32_t elem_type, const int64_t* shape, int32_t rank, const void* data,
                                size_t nbytes, sb_value** out);
 /* Wraps caller memory without copying (ORT aliases managed arrays the same way,
- * OrtSessionFactory.cs:56). The memory must stay valid and unchanged until the value is released. */
+ * OrtSessionFactory.cs:56). The memory must stay valid and unchanged until the value is released.
+ * Page-locked memory is transferred to the device directly; pageable memory (a pinned managed
+ * array, say) is staged by Run through page-locked slots, chunk by chunk, overlapped with the
+ * transfers and kernels of the previous chunks. */
 SB_API int32_t sb_value_wrap_tensor(int32_t elem_type, const int64_t* shape, int32_t rank, void* data,
                              size_t nbytes, sb_value** out);
 /* IShorokooInferenceSessionFactory.CreateStringTensor (IShorokooInferenceSessionFactory.cs:20-22). */
@@ -153,7 +156,9 @@ SB_API int32_t sb_session_stats(sb_session* session, int32_t n_inputs, const cha
  * padded bias, error word) is one fixed 16 MiB device array that every GPU loading this library
  * holds until exit; sizes whose scratch exceeds it (M*round8(K)*2 + N*round64(K)*2 + ~1 KiB) are
  * rejected with SB_STATUS_INVALID_ARGUMENT. The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress), so make that first call before any stream capture. All calls share
+ * address (cudaGetSymbolAddress) and caches it per device for the runtime's primary context (a
+ * caller that makes its own driver-API context current is not supported), so make that first call
+ * before any stream capture. All calls share
  * the array and the previous call's contents remain in it; calls that overlap on the GPU (other
  * streams, other threads) race on it. The call runs on `stream` (cudaStream_t, NULL = default) and
  * returns after it completes. bias may be NULL. */
@@ -163,7 +168,8 @@ SB_API int32_t sb_linear_noalloc(const float* x, const float* w, const float* bi
 /* ---- Diagnostics (no counterpart in the reference interface) ------------------------------- */
 /* Lowers and fuses the model on the host only (no device needed) for inputs given in session input
  * order, and writes a summary (one line per device op, then "separable=0|1") into buf as a
- * NUL-terminated string; *needed receives the full length + 1. */
+ * NUL-terminated string; *needed receives the full length + 1. Each contraction's line ends with
+ * "prec=A/B/C": its operand precision in a bf16 / TF32 / TF32x3 session. */
 SB_API int32_t sb_debug_lower(const uint8_t* model, size_t model_len, int32_t n_inputs, sb_value* const* in_values,
                               char* buf, size_t capacity, size_t* needed);
 

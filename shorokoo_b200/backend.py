@@ -315,6 +315,23 @@ class B200InferenceSessionFactory:
             raise B200ArgumentError(f"shape {shp} does not match {a.size} elements")
         return self._create(int(NP_TO_ELEM[a.dtype]), shp, a.ctypes.data, a.nbytes)
 
+    def WrapTensor(self, data) -> B200TensorValue:
+        """A tensor value over the caller's C-contiguous array without a copy (sb_value_wrap_tensor),
+        the way the reference's CreateTensor<T> aliases a managed array (OrtSessionFactory.cs:56).
+        The array must not change while the value is alive; the value keeps a reference to it."""
+        a = np.asarray(data)
+        if not a.flags.c_contiguous:
+            raise B200ArgumentError("WrapTensor needs a C-contiguous array")
+        if a.dtype not in NP_TO_ELEM:
+            raise B200NotSupportedError(f"element type {a.dtype} is not supported")
+        arr, r = _shape_arr(list(a.shape))
+        out = C.c_void_p()
+        _check(_native.lib().sb_value_wrap_tensor(int(NP_TO_ELEM[a.dtype]), arr, r, C.c_void_p(a.ctypes.data),
+                                                  a.nbytes, C.byref(out)))
+        v = B200TensorValue(out.value)
+        v._keep = a   # the wrapped memory lives as long as the value
+        return v
+
     def CreateTensorFromRawBytes(self, elementType: ShorokooTensorElementType, data: bytes,
                                  shape: Sequence[int]) -> B200TensorValue:
         if int(elementType) == ShorokooTensorElementType.String:

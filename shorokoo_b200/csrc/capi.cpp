@@ -15,6 +15,7 @@ extern char** environ;
 
 namespace sb {
 void* host_alloc(size_t bytes, bool& pinned);
+bool host_is_page_locked(const void* p);
 void host_copy(void* dst, const void* src, size_t n);
 }  // namespace sb
 
@@ -276,6 +277,7 @@ int32_t sb_value_wrap_tensor(int32_t et, const int64_t* shape, int32_t rank, voi
     SB_CHECK(nbytes == 0 || data != nullptr, sb::SB_INVALID_ARGUMENT, "data is null");
     v->data = data;
     v->owned = false;
+    v->pinned = sb::host_is_page_locked(data);
     *out = new sb_value{v};
     return SB_STATUS_OK;
   });
@@ -409,8 +411,16 @@ int32_t sb_debug_lower(const uint8_t* model, size_t len, int32_t n_in, sb_value*
     }
     sb::LGraph g = sb::lower(m, specs);
     sb::fuse(g);
+    // each contraction's operand precision in a bf16 / TF32 / TF32x3 session
+    std::vector<std::vector<int>> precs(3);
+    for (int p = 0; p < 3; ++p) {
+      sb::assign_precision(g, p);
+      for (const sb::Op& op : g.ops) precs[size_t(p)].push_back(op.prec);
+    }
+    static const char* kPrecName[] = {"bf16", "tf32", "tf32x3"};
     std::string out;
-    for (const sb::Op& op : g.ops) {
+    for (size_t oi = 0; oi < g.ops.size(); ++oi) {
+      const sb::Op& op = g.ops[oi];
       if (op.dead) continue;
       out += op.type;
       for (int id : op.in)
@@ -423,6 +433,9 @@ int32_t sb_debug_lower(const uint8_t* model, size_t len, int32_t n_in, sb_value*
       if (op.act) out += " act=" + std::to_string(op.act);
       if (op.residual >= 0) out += " residual=" + std::to_string(op.residual_mode);
       if (op.concat >= 0) out += " concat/" + std::to_string(op.concat_stride);
+      if (op.type == "FusedConv" || op.type == "FusedGemm")
+        out += std::string(" prec=") + kPrecName[precs[0][oi]] + "/" + kPrecName[precs[1][oi]] + "/" +
+               kPrecName[precs[2][oi]];
       out += "\n";
     }
     for (size_t j = 0; j < g.outputs.size(); ++j) {

@@ -44,6 +44,8 @@ struct Op {
   int concat_stride = 1;         // stride at which the second activation is sampled (1 or 2)
   std::shared_ptr<HostTensor> weight;   // folded weights (FusedConv: [M,C,KH,KW] f32; FusedGemm: [N,K] f32)
   std::shared_ptr<HostTensor> bias;     // folded bias [M] f32 (may be null)
+  int prec = 0;                  // FusedConv/FusedGemm operand precision: 0 bf16, 1 TF32, 2 TF32x3
+                                 // (set per op by assign_precision)
 };
 
 struct LGraph {
@@ -92,6 +94,11 @@ ModelInfo model_info(const OnnxModel& m);
 void check_supported_ops(const OnnxModel& m);
 
 LGraph lower(const OnnxModel& m, const std::vector<InputSpec>& inputs);
+
+// Sets Op::prec of every contraction from the session precision (0 bf16, 1 TF32, 2 TF32x3): dense
+// chains of contractions too long for the session's operand precision to meet its accuracy gate
+// get a more precise operand type for part of the chain (precision.cpp).
+void assign_precision(LGraph& g, int session_precision);
 
 // Inputs with at most this many elements are treated as plan-time constants (hyper scalars such
 // as bnEps / includeTop / Loop trip counts); their values key the plan cache.

@@ -143,8 +143,9 @@ inline void ck(cudaError_t e, const char* what) {
 
 // ---------------------------------------------------------------------------------------------
 Plan::Plan(LGraph g, int device, int num_sms, int precision)
-    : g_(std::move(g)), device_(device), num_sms_(num_sms), tf32_(precision >= 1), x3_(precision == 2) {
+    : g_(std::move(g)), device_(device), num_sms_(num_sms) {
   fuse(g_);
+  assign_precision(g_, precision);
   build();
   allocate_and_finalize();
 }
@@ -192,9 +193,9 @@ DevTensor Plan::alloc_nhwc(const std::vector<int64_t>& s, bool bf16, int64_t cst
 // rounded to the TF32 grid (10 explicit mantissa bits, nearest even) so the MMA's read of them is
 // exact. TF32x3: the TF32-rounded hi matrix, zero rows up to *lo_row (rows rounded up to 256),
 // then the lo matrix w - hi rounded to TF32 (unbiased, and read exactly by the MMA).
-int64_t Plan::add_operand_weights(const std::vector<float>& w, int64_t rows, int64_t* lo_row) {
+int64_t Plan::add_operand_weights(const std::vector<float>& w, int64_t rows, int64_t* lo_row, int prec) {
   if (lo_row) *lo_row = 0;
-  if (!tf32_) {
+  if (prec == 0) {
     std::vector<uint16_t> b(w.size());
     for (size_t i = 0; i < w.size(); ++i) b[i] = f32_to_bf16_rne(w[i]);
     return add_weight_bytes(b.data(), b.size() * 2);
@@ -207,7 +208,7 @@ int64_t Plan::add_operand_weights(const std::vector<float>& w, int64_t rows, int
     std::memcpy(&r, &u, 4);
     return r;
   };
-  if (!x3_) {
+  if (prec == 1) {
     std::vector<float> f(w.size());
     for (size_t i = 0; i < w.size(); ++i) f[i] = tf32_rne(w[i]);
     return add_weight_bytes(f.data(), f.size() * 4);
@@ -254,26 +255,35 @@ void Plan::add_step(const std::string& kind, std::vector<DevTensor> reads, std::
   stats_.kernels++;
 }
 
-// True when every reader of v (through views) is a tensor-core or pooling op: v can be stored in
-// the operand dtype (bf16, or TF32-rounded fp32).
-bool Plan::feeds_tensor_ops(int v) const {
-  if (is_output_[size_t(v)]) return false;
-  if (consumers_[size_t(v)].empty()) return false;
+// The dtype v is stored in, from what its readers (through views and max pools) take:
+//   kStoreBf16   every reader is a bf16-operand contraction (operand, residual or second operand);
+//   kStoreTf32   every reader is a single-pass TF32 contraction: fp32 rounded to the TF32 grid;
+//   kStoreF32    anything else (generic ops, graph outputs, TF32x3 readers, mixed precisions).
+// Global pools read either dtype and add no constraint; a value whose readers add none takes
+// `pref`, the class of its producer's operands.
+int Plan::storage_class(int v, int pref) const {
+  if (is_output_[size_t(v)]) return kStoreF32;
+  int cls = -1;
+  auto meet = [&](int c) {
+    if (c < 0) return;
+    cls = cls < 0 ? c : (cls == c ? c : kStoreF32);
+  };
   for (int oi : consumers_[size_t(v)]) {
     const Op& op = g_.ops[size_t(oi)];
-    if (op.type == "FusedConv" || op.type == "FusedGemm" || op.type == "MaxPool" ||
-        op.type == "GlobalAveragePool" || op.type == "GlobalMaxPool")
+    if (op.type == "FusedConv" || op.type == "FusedGemm") {
+      meet(op.prec == 0 ? kStoreBf16 : (op.prec == 1 ? kStoreTf32 : kStoreF32));
+    } else if (op.type == "GlobalAveragePool" || op.type == "GlobalMaxPool") {
       continue;
-    if (is_view_op(op.type) && op.in[0] == v) {
-      if (!feeds_tensor_ops(op.out[0])) return false;
-      continue;
+    } else if (op.type == "MaxPool" || (is_view_op(op.type) && op.in[0] == v)) {
+      const int c = storage_class(op.out[0], -1);
+      meet(c);
+    } else {
+      meet(kStoreF32);
     }
-    return false;
   }
-  return true;
+  if (cls < 0) cls = pref < 0 ? -1 : pref;
+  return cls;
 }
-
-bool Plan::consumers_accept_bf16(int v) const { return !tf32_ && feeds_tensor_ops(v); }
 
 DevTensor Plan::materialize(const DevTensor& src, bool bf16) {
   DevTensor dst = alloc_contig(src.shape, bf16);
@@ -294,20 +304,22 @@ DevTensor Plan::as_f32_contig(int v) {
   return materialize(t, false);
 }
 
-// NHWC copy of v in the operand dtype (bf16, or TF32-rounded fp32) with Cp channels per pixel.
-DevTensor Plan::as_nhwc_op(int v, int Cp) {
+// NHWC copy of v in the operand dtype of a precision-`prec` contraction (bf16, or fp32 rounded to
+// the TF32 grid for single-pass TF32, exact fp32 for TF32x3) with Cp channels per pixel. An fp32
+// tensor that is not on the TF32 grid is read as is by a TF32 contraction (the MMA truncates it).
+DevTensor Plan::as_nhwc_op(int v, int Cp, int prec) {
   const DevTensor& t = vt_[size_t(v)];
   SB_CHECK(t.shape.size() == 4, SB_SHAPE_ERROR, "expected a rank-4 activation");
   const int64_t N = t.shape[0], C = t.shape[1], H = t.shape[2], W = t.shape[3];
-  if (t.bf16 == !tf32_ && C == Cp && t.strides[1] == 1 && t.strides[3] == Cp && (t.strides[2] == W * Cp || H == 1) &&
+  if (t.bf16 == (prec == 0) && C == Cp && t.strides[1] == 1 && t.strides[3] == Cp && (t.strides[2] == W * Cp || H == 1) &&
       (t.strides[0] == H * W * Cp || N == 1) && t.off % 16 == 0)
     return t;
-  auto key = std::make_pair(v, Cp);
+  auto key = std::make_pair(v, Cp * 4 + prec);
   auto it = conv_cache_.find(key);
   if (it != conv_cache_.end()) return it->second;
-  DevTensor dst = alloc_nhwc({N, C, H, W}, !tf32_, Cp);
-  const bool f32 = tf32_;
-  const int rnd = tf32_ && !x3_;
+  DevTensor dst = alloc_nhwc({N, C, H, W}, prec == 0, Cp);
+  const bool f32 = prec != 0;
+  const int rnd = prec == 1;
   add_step(f32 ? "to_nhwc_f32" : "to_nhwc_bf16", {t}, {dst}, [this, t, dst, Cp, f32, rnd]() {
     const void* sp = ptr(t);
     void* dp = ptr(dst);
@@ -322,15 +334,17 @@ DevTensor Plan::as_nhwc_op(int v, int Cp) {
   return dst;
 }
 
-// Row matrix [M, Kp] of v in the operand dtype, rows 16-byte aligned.
-DevTensor Plan::as_rows_op(int v, int64_t M, int64_t K) {
+// Row matrix [M, Kp] of v in the operand dtype of a precision-`prec` contraction, rows 16-byte
+// aligned.
+DevTensor Plan::as_rows_op(int v, int64_t M, int64_t K, int prec) {
+  const bool tf32 = prec != 0;
   DevTensor t = vt_[size_t(v)];
   auto vs = view_strides(t.shape, t.strides, {M, K});
   if (vs) {
     DevTensor r = t;
     r.shape = {M, K};
     r.strides = *vs;
-    if (t.bf16 == !tf32_ && r.strides[1] == 1 && (r.strides[0] == K || M == 1) && K % (tf32_ ? 4 : 8) == 0 &&
+    if (t.bf16 == !tf32 && r.strides[1] == 1 && (r.strides[0] == K || M == 1) && K % (tf32 ? 4 : 8) == 0 &&
         t.off % 16 == 0) {
       r.strides[0] = K;
       return r;
@@ -341,12 +355,12 @@ DevTensor Plan::as_rows_op(int v, int64_t M, int64_t K) {
     t.shape = {M, K};
     t.strides = {K, 1};
   }
-  auto it = rows_cache_.find(v);
+  auto it = rows_cache_.find(std::make_pair(v, prec));
   if (it != rows_cache_.end()) return it->second;
-  const int64_t Kp = round_up(K, tf32_ ? 4 : 8);
-  DevTensor dst = alloc_contig({M, Kp}, !tf32_);
-  const bool f32 = tf32_;
-  const int rnd = tf32_ && !x3_;
+  const int64_t Kp = round_up(K, tf32 ? 4 : 8);
+  DevTensor dst = alloc_contig({M, Kp}, !tf32);
+  const bool f32 = tf32;
+  const int rnd = prec == 1;
   add_step(f32 ? "to_rows_f32" : "to_rows_bf16", {t}, {dst}, [this, t, dst, M, K, Kp, f32, rnd]() {
     const void* sp = ptr(t);
     void* dp = ptr(dst);
@@ -356,7 +370,7 @@ DevTensor Plan::as_rows_op(int v, int64_t M, int64_t K) {
       return f32 ? k::to_rows_f32(sp, sb, M, K, sm, sk, dp, Kp, rnd, s) : k::to_rows_bf16(sp, sb, M, K, sm, sk, dp, Kp, s);
     });
   });
-  rows_cache_[v] = dst;
+  rows_cache_[std::make_pair(v, prec)] = dst;
   return dst;
 }
 
@@ -368,16 +382,18 @@ void Plan::plan_conv(const Op& op) {
   const HostTensor& Wt = *op.weight;
   const int64_t N = xv.shape[0], C = xv.shape[1], H = xv.shape[2], W = xv.shape[3];
   const int64_t Cout = Wt.shape[0], KH = Wt.shape[2], KW = Wt.shape[3];
+  const int prec = op.prec;
+  const bool tf32 = prec != 0;
   const int64_t Ho = yv.shape[2], Wo = yv.shape[3];
   // Strided convs on at most 4 input channels (the ResNet stem) run as a stride-1 conv over the 2x2
   // space-to-depth image: out(ho) reads original rows i = 2*ho - pt + kh; with e = pt % 2 and
   // u = kh + e = 2a + p this is s2d row ho - (pt+e)/2 + a, parity p, so the kernel becomes
   // ceil((KH+e)/2) taps over 16 channels (p, q, c) with zero weights where kh falls outside [0, KH).
-  const bool s2d = !tf32_ && op.strides[0] == 2 && op.strides[1] == 2 && op.dilations[0] == 1 &&
+  const bool s2d = !tf32 && op.strides[0] == 2 && op.strides[1] == 2 && op.dilations[0] == 1 &&
                    op.dilations[1] == 1 && C <= 4 && KH >= 3 && KW >= 3;
   int64_t gH = H, gW = W, gKH = KH, gKW = KW, gsh = op.strides[0], gsw = op.strides[1];
   int64_t gph = op.pads[0], gpw = op.pads[1], gdh = op.dilations[0], gdw = op.dilations[1];
-  int Cp = int(tf32_ ? round_up(C, 4) : (C % 8 == 0 ? C : (C <= 4 ? 4 : round_up(C, 8))));
+  int Cp = int(tf32 ? round_up(C, 4) : (C % 8 == 0 ? C : (C <= 4 ? 4 : round_up(C, 8))));
   int64_t et = 0, el = 0;
   if (s2d) {
     et = op.pads[0] % 2;
@@ -393,7 +409,7 @@ void Plan::plan_conv(const Op& op) {
     Cp = 16;
   }
   const bool one_by_one = !s2d && KH == 1 && KW == 1 && op.strides[0] == 1 && op.strides[1] == 1 && op.pads[0] == 0 &&
-                          op.pads[1] == 0 && op.pads[2] == 0 && op.pads[3] == 0 && Cp % (tf32_ ? 4 : 8) == 0;
+                          op.pads[1] == 0 && op.pads[2] == 0 && op.pads[3] == 0 && Cp % (tf32 ? 4 : 8) == 0;
   DevTensor x;
   if (s2d) {
     auto key = std::make_pair(op.in[0], -16);
@@ -417,7 +433,7 @@ void Plan::plan_conv(const Op& op) {
       conv_cache_[key] = x;
     }
   } else {
-    x = as_nhwc_op(op.in[0], Cp);
+    x = as_nhwc_op(op.in[0], Cp, prec);
   }
   // A merged projection shortcut's input (op.concat): its C2 channels follow X's in the reduction,
   // read by the kernel from its own row matrix (k-tiles from Cp / k-tile width on).
@@ -431,10 +447,10 @@ void Plan::plan_conv(const Op& op) {
                  cv.shape[0] == N && cv.shape[1] == C2 && (cs == 1 || cs == 2) && (cv.shape[2] - 1) / cs + 1 == H &&
                  (cv.shape[3] - 1) / cs + 1 == W,
              SB_UNSUPPORTED, "Conv: concatenated operand layout");
-    x2 = as_nhwc_op(op.concat, int(C2));
+    x2 = as_nhwc_op(op.concat, int(C2), prec);
   }
   const int64_t K = gKH * gKW * Cp + C2;
-  const int64_t Kpad = round_up(K, tf32_ ? 32 : 64);   // whole 128-byte k-tile rows
+  const int64_t Kpad = round_up(K, tf32 ? 32 : 64);   // whole 128-byte k-tile rows
   SB_CHECK(N * Ho * Wo < (int64_t(1) << 31) && N * gH * gW * Cp < (int64_t(1) << 40), SB_UNSUPPORTED,
            "Conv: problem too large for 32-bit row indexing");
   // weights [Cout, Kpad] bf16 (or TF32-rounded fp32), K ordered (kh, kw, c) of the kernel as run
@@ -459,14 +475,15 @@ void Plan::plan_conv(const Op& op) {
   DevTensor wt;
   wt.buf = -1;
   int64_t w_lo_row = 0;
-  wt.off = add_operand_weights(wf, Cout, &w_lo_row);
+  wt.off = add_operand_weights(wf, Cout, &w_lo_row, prec);
   std::vector<float> bias(size_t(round_up(Cout, 256)), 0.f);
   for (int64_t m = 0; m < Cout; ++m) bias[size_t(m)] = op.bias ? op.bias->ptr<float>()[m] : 0.f;
   DevTensor bt;
   bt.buf = -1;
   bt.off = add_weight_bytes(bias.data(), bias.size() * 4);
 
-  const bool out_bf16 = consumers_accept_bf16(op.out[0]);
+  const int out_cls = storage_class(op.out[0], prec == 0 ? kStoreBf16 : (prec == 1 ? kStoreTf32 : kStoreF32));
+  const bool out_bf16 = out_cls == kStoreBf16;
   DevTensor y = alloc_nhwc(yv.shape, out_bf16, Cout);
   vt_[size_t(op.out[0])] = y;
 
@@ -485,21 +502,23 @@ void Plan::plan_conv(const Op& op) {
       r = rt;
       ldr = cs;
     } else {
-      r = as_nhwc_op(op.residual, int(round_up(Cout, 4)));
+      r = as_nhwc_op(op.residual, int(round_up(Cout, 4)), out_bf16 ? 0 : 2);
       ldr = round_up(Cout, 4);
     }
     Hr = int(rh);
     Wr = int(rw);
   }
-  stats_.macs += double(N * Ho * Wo) * double(Cout) * double(C * KH * KW + C2);
+  const double macs = double(N * Ho * Wo) * double(Cout) * double(C * KH * KW + C2);
+  stats_.macs += macs;
+  stats_.macs_by_prec[prec] += macs;
   stats_.tc_kernels++;
   std::vector<DevTensor> reads{x};
   if (r.valid()) reads.push_back(r);
   if (x2.valid()) reads.push_back(x2);
   const int sms = num_sms_;
-  const bool f32 = tf32_;
-  const bool round_out = tf32_ && !x3_ && feeds_tensor_ops(op.out[0]);   // next MMA reads it as TF32
-  const int x3 = x3_;
+  const bool f32 = tf32;
+  const bool round_out = out_cls == kStoreTf32;   // the next MMA reads it as TF32
+  const int x3 = prec == 2;
   k::ConvGemmArgs geo;   // geometry only: how the kernel will fetch A (for the step's label)
   std::memset(&geo, 0, sizeof(geo));
   geo.gather = one_by_one ? 0 : 1;
@@ -522,7 +541,8 @@ void Plan::plan_conv(const Op& op) {
                            std::to_string(op.strides[0]) + " " + std::to_string(C) + "->" + std::to_string(Cout) +
                            " M=" + std::to_string(N * Ho * Wo) + " " + kAModeName[k::conv_gemm_a_mode(geo)] +
                            (s2d ? " s2d" : "") + (op.residual >= 0 ? " +res" : "") +
-                           (op.concat >= 0 ? " +proj " + std::to_string(C2) : "");
+                           (op.concat >= 0 ? " +proj " + std::to_string(C2) : "") +
+                           (prec == 1 ? " tf32" : (prec == 2 ? " tf32x3" : ""));
   add_step(kind, reads, {y}, [=]() {
     auto p = std::make_shared<k::ConvGemmPlan>();
     k::ConvGemmArgs& a = p->args;
@@ -583,9 +603,11 @@ void Plan::plan_gemm(const Op& op) {
   SB_CHECK(!xv.shape.empty() && xv.shape.back() == K, SB_SHAPE_ERROR, "Gemm: inner dimension mismatch");
   const int64_t M = numel(xv.shape) / std::max<int64_t>(K, 1);
   SB_CHECK(M < (int64_t(1) << 31), SB_UNSUPPORTED, "Gemm: too many rows");
-  DevTensor x = as_rows_op(op.in[0], M, K);
+  const int prec = op.prec;
+  const bool tf32 = prec != 0;
+  DevTensor x = as_rows_op(op.in[0], M, K, prec);
   const int64_t lda = x.strides[0];
-  const int64_t Kpad = round_up(K, tf32_ ? 32 : 64);
+  const int64_t Kpad = round_up(K, tf32 ? 32 : 64);
   std::vector<float> wf(size_t(Nn * Kpad), 0.f);
   const float* wp = Wt.ptr<float>();
   for (int64_t n = 0; n < Nn; ++n)
@@ -593,13 +615,14 @@ void Plan::plan_gemm(const Op& op) {
   DevTensor wt;
   wt.buf = -1;
   int64_t w_lo_row = 0;
-  wt.off = add_operand_weights(wf, Nn, &w_lo_row);
+  wt.off = add_operand_weights(wf, Nn, &w_lo_row, prec);
   std::vector<float> bias(size_t(round_up(Nn, 256)), 0.f);
   for (int64_t n = 0; n < Nn; ++n) bias[size_t(n)] = op.bias ? op.bias->ptr<float>()[n] : 0.f;
   DevTensor bt;
   bt.buf = -1;
   bt.off = add_weight_bytes(bias.data(), bias.size() * 4);
-  const bool out_bf16 = consumers_accept_bf16(op.out[0]);
+  const int out_cls = storage_class(op.out[0], prec == 0 ? kStoreBf16 : (prec == 1 ? kStoreTf32 : kStoreF32));
+  const bool out_bf16 = out_cls == kStoreBf16;
   DevTensor y = alloc_contig(yv.shape, out_bf16);
   vt_[size_t(op.out[0])] = y;
   DevTensor r;
@@ -607,15 +630,19 @@ void Plan::plan_gemm(const Op& op) {
     r = vt_[size_t(op.residual)];
     if (!is_contig(r)) r = materialize(r, false);
   }
-  stats_.macs += double(M) * double(Nn) * double(K);
+  const double macs = double(M) * double(Nn) * double(K);
+  stats_.macs += macs;
+  stats_.macs_by_prec[prec] += macs;
   stats_.tc_kernels++;
   std::vector<DevTensor> reads{x};
   if (r.valid()) reads.push_back(r);
   const int sms = num_sms_;
-  const bool f32 = tf32_;
-  const bool round_out = tf32_ && !x3_ && feeds_tensor_ops(op.out[0]);   // next MMA reads it as TF32
-  const int x3 = x3_;
-  add_step("gemm " + std::to_string(M) + "x" + std::to_string(K) + "->" + std::to_string(Nn), reads, {y}, [=]() {
+  const bool f32 = tf32;
+  const bool round_out = out_cls == kStoreTf32;   // the next MMA reads it as TF32
+  const int x3 = prec == 2;
+  add_step("gemm " + std::to_string(M) + "x" + std::to_string(K) + "->" + std::to_string(Nn) +
+               (prec == 1 ? " tf32" : (prec == 2 ? " tf32x3" : "")),
+           reads, {y}, [=]() {
     auto p = std::make_shared<k::ConvGemmPlan>();
     k::ConvGemmArgs& a = p->args;
     std::memset(&a, 0, sizeof(a));
@@ -656,19 +683,22 @@ void Plan::plan_maxpool(const Op& op) {
   const int64_t C = xv.shape[1];
   DevTensor x;
   int64_t cs = t.strides.size() == 4 ? t.strides[3] : 0;
-  if (t.bf16 == !tf32_ && t.strides[1] == 1 && cs >= C && t.strides[2] == xv.shape[3] * cs &&
+  // The pool keeps the dtype its input is stored in (converting to what its readers take if the
+  // input is in no operand layout).
+  if (t.strides[1] == 1 && cs >= C && t.strides[2] == xv.shape[3] * cs &&
       t.strides[0] == xv.shape[2] * xv.shape[3] * cs && t.off % 16 == 0 && cs % 4 == 0) {
     x = t;
   } else {
     cs = round_up(C, 4);
-    x = as_nhwc_op(op.in[0], int(cs));
+    const int cls = storage_class(op.out[0], kStoreF32);
+    x = as_nhwc_op(op.in[0], int(cs), cls == kStoreBf16 ? 0 : (cls == kStoreTf32 ? 1 : 2));
   }
-  DevTensor y = alloc_nhwc(yv.shape, !tf32_, cs);
+  DevTensor y = alloc_nhwc(yv.shape, x.bf16, cs);
   vt_[size_t(op.out[0])] = y;
   const int N = int(xv.shape[0]), H = int(xv.shape[2]), W = int(xv.shape[3]);
   const int Ho = int(yv.shape[2]), Wo = int(yv.shape[3]);
   const int Cs = int(cs);
-  const bool f32 = tf32_;
+  const bool f32 = !x.bf16;
   add_step("maxpool", {x}, {y}, [=]() {
     const void* xp = ptr(x);
     void* yp = ptr(y);
@@ -691,9 +721,9 @@ void Plan::plan_global_pool(const Op& op) {
   bool nhwc = t.strides[1] == 1 && (t.strides[2] == W * ldp || H == 1) && (t.strides[0] == H * W * ldp || N == 1);
   if (!nhwc) {
     ldp = round_up(C, 4);
-    x = as_nhwc_op(op.in[0], int(ldp));
+    x = as_nhwc_op(op.in[0], int(ldp), 2);
   }
-  const bool out_bf16 = consumers_accept_bf16(op.out[0]);
+  const bool out_bf16 = storage_class(op.out[0], kStoreF32) == kStoreBf16;
   DevTensor y = alloc_contig(yv.shape, out_bf16);
   vt_[size_t(op.out[0])] = y;
   const int is_max = op.type == "GlobalMaxPool";

@@ -29,6 +29,7 @@ struct PlanStats {
   int64_t kernels = 0;          // kernel launches per run
   int64_t tc_kernels = 0;       // tensor-core (tcgen05) launches per run
   double macs = 0;              // algorithmic multiply-accumulates (Conv/MatMul) per run
+  double macs_by_prec[3] = {0, 0, 0};   // the same split by operand precision (bf16, TF32, TF32x3)
   size_t arena_bytes = 0, weight_bytes = 0;
 };
 
@@ -47,7 +48,8 @@ struct OutputBinding {
 
 class Plan {
  public:
-  // precision: 0 bf16 operands; 1 fp32 operands read as TF32; 2 TF32x3 (error-compensated).
+  // precision: the session's operand precision (0 bf16; 1 fp32 read as TF32; 2 TF32x3,
+  // error-compensated), turned into one precision per contraction by assign_precision.
   Plan(LGraph g, int device, int num_sms, int precision = 0);
   ~Plan();
   Plan(const Plan&) = delete;
@@ -90,8 +92,6 @@ class Plan {
   LGraph g_;
   int device_;
   int num_sms_;
-  bool tf32_ = false;   // operand dtype of the tensor-core path: fp32 (TF32 MMA) instead of bf16
-  bool x3_ = false;     // TF32x3: operands kept exact in fp32, weights split into hi / lo
   std::vector<DevTensor> vt_;       // per value id
   std::vector<Buffer> bufs_;
   std::vector<PendingStep> pending_;
@@ -108,24 +108,24 @@ class Plan {
   cudaGraphExec_t exec_ = nullptr;
   std::vector<std::vector<int>> consumers_;
   std::vector<bool> is_output_;
-  std::map<std::pair<int, int>, DevTensor> conv_cache_;   // (value, Cp) -> NHWC bf16 copy
-  std::map<int, DevTensor> rows_cache_;                    // value -> bf16 rows copy
+  std::map<std::pair<int, int>, DevTensor> conv_cache_;   // (value, 4 Cp + prec) -> NHWC operand copy
+  std::map<std::pair<int, int>, DevTensor> rows_cache_;   // (value, prec) -> rows operand copy
 
   void build();
   void allocate_and_finalize();
   int new_buffer(size_t bytes);
   DevTensor alloc_contig(const std::vector<int64_t>& shape, bool bf16);
   DevTensor alloc_nhwc(const std::vector<int64_t>& shape_nchw, bool bf16, int64_t cstride);
-  int64_t add_operand_weights(const std::vector<float>& w, int64_t rows, int64_t* lo_row);
+  int64_t add_operand_weights(const std::vector<float>& w, int64_t rows, int64_t* lo_row, int prec);
   int64_t add_weight_bytes(const void* data, size_t bytes);
   void* ptr(const DevTensor& t) const;
   void add_step(const std::string& kind, std::vector<DevTensor> reads, std::vector<DevTensor> writes,
                 std::function<std::function<cudaError_t(cudaStream_t)>()> build);
 
-  bool feeds_tensor_ops(int v) const;
-  bool consumers_accept_bf16(int v) const;
-  DevTensor as_nhwc_op(int v, int Cp);
-  DevTensor as_rows_op(int v, int64_t M, int64_t K);
+  static constexpr int kStoreBf16 = 0, kStoreTf32 = 1, kStoreF32 = 2;
+  int storage_class(int v, int pref) const;
+  DevTensor as_nhwc_op(int v, int Cp, int prec);
+  DevTensor as_rows_op(int v, int64_t M, int64_t K, int prec);
   DevTensor as_f32_contig(int v);
   DevTensor materialize(const DevTensor& src, bool bf16);
 

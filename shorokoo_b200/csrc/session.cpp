@@ -99,21 +99,24 @@ HostPool& pool() {
   return *p;
 }
 
-// Parallel memcpy for large host copies.
+// Parallel memcpy for large host copies: one piece of at least 4 MiB per thread, up to 16 threads
+// (a single thread copies well below the host's memory bandwidth).
 void par_memcpy(void* dst, const void* src, size_t n) {
-  const size_t chunk = size_t(64) << 20;
-  if (n < 2 * chunk) {
+  const size_t piece = size_t(4) << 20;
+  const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+  const unsigned nt = unsigned(std::min<size_t>(std::min(16u, hw), n / piece));
+  if (nt <= 1) {
     std::memcpy(dst, src, n);
     return;
   }
-  unsigned nt = std::min<unsigned>(8, std::max(1u, std::thread::hardware_concurrency()));
   std::vector<std::thread> th;
-  size_t per = (n + nt - 1) / nt;
-  for (unsigned i = 0; i < nt; ++i) {
-    size_t b = i * per, e = std::min(n, b + per);
+  const size_t per = (n / nt + 63) / 64 * 64;
+  for (unsigned i = 1; i < nt; ++i) {
+    const size_t b = i * per, e = std::min(n, b + per);
     if (b >= e) break;
     th.emplace_back([=] { std::memcpy(static_cast<uint8_t*>(dst) + b, static_cast<const uint8_t*>(src) + b, e - b); });
   }
+  std::memcpy(dst, src, std::min(n, per));
   for (auto& t : th) t.join();
 }
 
@@ -122,6 +125,15 @@ void par_memcpy(void* dst, const void* src, size_t n) {
 void* host_alloc(size_t bytes, bool& pinned) { return pool().alloc(bytes, pinned); }
 void host_release(void* p, size_t bytes, bool pinned) { pool().release(p, bytes, pinned); }
 void host_copy(void* dst, const void* src, size_t n) { par_memcpy(dst, src, n); }
+// True when p lies in page-locked host memory the CUDA runtime knows (cudaHostAlloc'd or
+// cudaHostRegister'ed), so a device transfer from it is asynchronous.
+bool host_is_page_locked(const void* p) {
+  if (!p || !pool().have_cuda()) return false;
+  cudaPointerAttributes at;
+  const bool ok = cudaPointerGetAttributes(&at, p) == cudaSuccess && at.type == cudaMemoryTypeHost;
+  cudaGetLastError();
+  return ok;
+}
 
 HostValue::~HostValue() {
   if (owned && data) pool().release(data, nbytes, pinned);
@@ -406,6 +418,9 @@ std::shared_ptr<Session::PlanSet> Session::get_plans(const std::vector<std::shar
 
 Session::Pipeline::~Pipeline() {
   cudaSetDevice(device);
+  for (auto& slot : host_staging)
+    for (void* p : slot)
+      if (p) cudaFreeHost(p);
   for (auto& slot : staging)
     for (void* p : slot) cudaFree(p);
   for (auto& slot : out_staging)
@@ -530,10 +545,27 @@ void Session::run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostV
     const auto& binds = plan.inputs();
     const int slot = int(c & 1);
     if (c >= 2) ck(cudaStreamWaitEvent(P.copy, P.consumed[slot], 0), "stream wait");
+    bool host_slot_free = c < 2;
     for (size_t bi = 0; bi < binds.size(); ++bi) {
       const HostValue& v = *inputs[size_t(binds[bi].index)];
       const size_t row = v.nbytes / size_t(std::max<int64_t>(v.shape[0], 1));
       const uint8_t* src = static_cast<const uint8_t*>(v.data) + size_t(r0) * row;
+      if (!v.pinned) {   // borrowed pageable memory: through page-locked host slot `slot`
+        if (!host_slot_free) {   // chunk c - 2's transfer out of this slot has finished
+          ck(cudaEventSynchronize(P.h2d_done[slot]), "event synchronize");
+          host_slot_free = true;
+        }
+        if (P.host_staging_bytes.size() < binds.size()) P.host_staging_bytes.assign(binds.size(), 0);
+        for (auto& hs : P.host_staging) hs.resize(binds.size(), nullptr);
+        if (!P.host_staging[slot][bi]) {
+          size_t most = 0;   // the largest chunk's bytes of this binding
+          for (size_t c2 = 0; c2 < P.plans.size(); ++c2) most = std::max(most, P.plans[c2]->inputs()[bi].bytes);
+          ck(cudaHostAlloc(&P.host_staging[slot][bi], most, cudaHostAllocPortable), "cudaHostAlloc (input staging)");
+          P.host_staging_bytes[bi] = most;
+        }
+        par_memcpy(P.host_staging[slot][bi], src, binds[bi].bytes);
+        src = static_cast<const uint8_t*>(P.host_staging[slot][bi]);
+      }
       ck(cudaMemcpyAsync(P.staging[slot][bi], src, binds[bi].bytes, cudaMemcpyHostToDevice, P.copy), "H2D");
     }
     ck(cudaEventRecord(P.h2d_done[slot], P.copy), "event record");

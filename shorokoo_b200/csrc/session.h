@@ -87,6 +87,12 @@ class Session {
     cudaEvent_t out_ready[2] = {nullptr, nullptr};   // slot filled by the compute stream
     cudaEvent_t out_free[2] = {nullptr, nullptr};    // slot copied to the host
     cudaStream_t d2h = nullptr;
+    // Inputs in borrowed pageable memory (sb_value_wrap_tensor over a caller's array, the way the
+    // reference's CreateTensor<T> aliases a managed array) go through page-locked host slots: the
+    // host copies chunk c into slot c % 2 while chunk c - 1 is still being transferred, so the
+    // transfer stays asynchronous (a transfer straight from pageable memory blocks the host).
+    std::vector<void*> host_staging[2];             // per plan input binding (allocated on first use)
+    std::vector<size_t> host_staging_bytes;
     ~Pipeline();
   };
   struct PlanSet {

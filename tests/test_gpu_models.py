@@ -5,7 +5,7 @@ import os
 import numpy as np
 import pytest
 
-from helpers import assert_close, run_backend, run_oracle
+from helpers import BF16_TOL, assert_close, run_backend, run_oracle
 from shorokoo_b200.emit import graphs
 
 pytestmark = pytest.mark.gpu
@@ -38,23 +38,22 @@ def test_model_parity(name, kw):
 
 
 def test_retinanet_parity():
-    """RetinaNet's per-pixel detection outputs sit at the precision floor of bf16 operands: the
-    oracle with bf16-rounded Conv operands and fp32 accumulation (precision="bf16-operands") lands
-    2.1e-2 (class) / 1.6e-2 (box) from the fp32 oracle on this graph, and the GPU lands at the same
-    distance. Unlike ResNet's pooled logits, nothing averages the ~1% per-pixel error of ~70 chained
-    convs, so the 1e-2 bf16 gate is not met here; the bound below is that measured floor (x1.5)."""
+    """RetinaNet's per-anchor outputs carry the operand rounding of every conv on a 57-conv chain
+    (nothing pools them): with bf16 operands throughout they land 2.1e-2 (class) / 1.6e-2 (box) from
+    the fp32 oracle. The bf16 session's precision policy keeps bf16 for the first four contractions
+    of such a chain and gives the rest TF32 operands, which meets the 1e-2 bf16 gate."""
     case = graphs.retinanet(batch=1, hw=(128, 160))
     got = run_backend(case)
     ref = run_oracle(case)
     for g, r, o in zip(got, ref, case.output_names):
-        assert_close(g, r, tol=3.5e-2, what=f"retinanet {o} vs fp32 oracle (bf16 floor)")
+        assert_close(g, r, tol=BF16_TOL, what=f"retinanet {o} vs fp32 oracle")
 
 
 def test_retinanet_shallow_parity():
     """Same FPN / shared heads / reshape-transpose-concat / sigmoid machinery on a one-block-per-stage
-    backbone, where the bf16 floor is ~1.1e-2."""
+    backbone (a 20-conv chain, still past the policy's threshold)."""
     case = graphs.retinanet(batch=2, hw=(128, 160), backbone_blocks=(1, 1, 1, 1))
     got = run_backend(case)
     ref = run_oracle(case)
     for g, r, o in zip(got, ref, case.output_names):
-        assert_close(g, r, tol=2e-2, what=f"shallow retinanet {o}")
+        assert_close(g, r, tol=BF16_TOL, what=f"shallow retinanet {o}")

@@ -56,10 +56,8 @@ def _run_child(tmp_path, case_expr):
     ("graphs.resnet(depth=18, batch=256, hw=(160, 160), seed=9)", "32 + 32 + 96 + 96", BF16_TOL),
     # a detector whose per-anchor outputs (~200 MB) outweigh its input: pipelined below batch 32,
     # the output copies overlapping later chunks through the output staging slots. Its chunks pick
-    # other tiles than the full batch, and through RetinaNet's depth that change of summation order
-    # moves the bf16 result by as much as the bf16 floor the RetinaNet parity tests allow against
-    # the fp32 oracle (3.5e-2).
-    ("graphs.retinanet(batch=16, hw=(384, 512), seed=5)", "2 + 2 + 4 + 4 + 4", 3.5e-2),
+    # other tiles than the full batch (another summation order), within the bf16 gate.
+    ("graphs.retinanet(batch=16, hw=(384, 512), seed=5)", "2 + 2 + 4 + 4 + 4", BF16_TOL),
 ])
 def test_pipelined_run_matches_full_batch_plan(tmp_path, case_expr, schedule, tol):
     ref, got, log = _run_child(tmp_path, case_expr)

@@ -61,20 +61,16 @@ def test_tf32_model_parity(name, kw):
         assert_close(g, r, tol=TF32_TOL, what=f"tf32 {name} {kw} output {o}")
 
 
-def test_tf32_retinanet_at_the_tf32_floor():
-    """The detection graph whose per-pixel outputs sit above the 1e-2 gate with bf16 operands. With
-    TF32 operands the oracle itself (precision="tf32-operands", fp32 accumulation) lands 2.4e-3
-    (class) / 1.8e-3 (box) from the fp32 oracle on this graph: single-pass TF32 has a floor at the
-    2e-3 gate here, and the GPU lands 1.6e-3 - 2.0e-3 depending on the summation order of its
-    split-K partials (GPU and TF32 oracle are each ~2e-3 from fp32, in different directions, as
-    operand-rounding differences amplify through ~70 chained convs; the single-conv TF32 tests
-    check the kernels against the TF32 oracle at 5e-4). The fp32 distance is bounded at that floor
-    (x1.25)."""
+def test_tf32_retinanet_meets_the_tf32_gate():
+    """The detection graph whose 57-conv dense chains put single-pass TF32 operands at 2.4e-3 (class)
+    / 1.8e-3 (box) from the fp32 oracle (the oracle with TF32-rounded operands, 2.8e-3 / 2.5e-3 at
+    800x1024): the TF32 session's precision policy runs the contractions past the first 16 of such a
+    chain as TF32x3, which meets the 2e-3 TF32 gate."""
     case = graphs.retinanet(batch=1, hw=(128, 160))
     got = _tf32(case)
     ref = run_oracle(case)
     for g, r, o in zip(got, ref, case.output_names):
-        assert_close(g, r, tol=3e-3, what=f"tf32 retinanet {o} vs fp32 oracle (tf32 floor)")
+        assert_close(g, r, tol=TF32_TOL, what=f"tf32 retinanet {o} vs fp32 oracle")
 
 
 def test_precision_is_validated():
