@@ -173,6 +173,46 @@ bool is_nearest_up2(const Op& r, const LGraph& g) {
 
 }  // namespace
 
+// Sigmoid / Relu of a value that only rearranges the outputs of activation-free contractions
+// (views and concatenations, e.g. the RetinaNet heads' Reshape -> Transpose(0,3,4,1,2) -> Reshape
+// -> Concat over the pyramid levels followed by the class Sigmoid, RetinaNetDetector.cs:539-571)
+// is applied per element in those contractions' epilogues; the elementwise op becomes an Identity.
+// Every value on the way must have that single reader and be no graph output.
+static void push_activation_into_producers(LGraph& g) {
+  Consumers C = consumers(g);
+  for (Op& e : g.ops) {
+    if (e.dead || (e.type != "Sigmoid" && e.type != "Relu") || e.in.size() != 1 || e.in[0] < 0) continue;
+    std::vector<int> producers;
+    bool ok = true;
+    std::vector<int> todo{e.in[0]};
+    while (ok && !todo.empty()) {
+      const int v = todo.back();
+      todo.pop_back();
+      const Value& val = g.vals[size_t(v)];
+      if (val.is_host || C.is_output[size_t(v)] || C.ops[size_t(v)].size() != 1 || val.producer < 0) {
+        ok = false;
+        break;
+      }
+      const Op& p = g.ops[size_t(val.producer)];
+      if (p.dead) {
+        ok = false;
+      } else if (p.type == "FusedConv" || p.type == "FusedGemm") {
+        if (p.act != 0) ok = false;
+        else producers.push_back(val.producer);
+      } else if (p.type == "Reshape" || p.type == "Transpose" || p.type == "Identity") {
+        todo.push_back(p.in[0]);
+      } else if (p.type == "Concat") {
+        for (int id : p.in) todo.push_back(id);
+      } else {
+        ok = false;
+      }
+    }
+    if (!ok || producers.empty()) continue;
+    for (int pi : producers) g.ops[size_t(pi)].act = e.type == "Sigmoid" ? 2 : 1;
+    e.type = "Identity";
+  }
+}
+
 void fuse(LGraph& g) {
   // ---------------- Conv chains ----------------
   for (size_t ci = 0; ci < g.ops.size(); ++ci) {
@@ -411,6 +451,7 @@ void fuse(LGraph& g) {
     g.ops[size_t(slot)] = f;
   }
   merge_projection_shortcuts(g);
+  push_activation_into_producers(g);
   g.dce();
 }
 

@@ -267,6 +267,17 @@ __device__ __forceinline__ uint32_t pack_bf16x2_relu(float a, float b) {
   return r;
 }
 
+// Elementwise max of two groups of 8 bf16 values.
+__device__ __forceinline__ uint4 bf16x8_max(uint4 a, uint4 b) {
+  const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&b);
+  uint4 r;
+  __nv_bfloat162* z = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+  for (int t = 0; t < 4; ++t) z[t] = __hmax2(x[t], y[t]);
+  return r;
+}
+
 // Epilogue for one 32-column chunk of one accumulator row.
 __device__ __forceinline__ void epilogue_chunk(const ConvGemmArgs& a, const uint32_t (&r)[32], int m, int n0) {
   float v[32];
@@ -1013,6 +1024,250 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
   }
 }
 
+// ---- stem convolution + 3x3/2 max pool ----------------------------------------------------------
+// The ResNet stem (7x7/2 conv over 3 channels, run as a 4x4 stride-1 conv over the 2x2
+// space-to-depth image of 16-channel pixels) with bias, ReLU and the following MaxPool 3x3 / stride
+// 2 / pad 1 in one kernel. A tile is one conv output row (Wo <= 128 pixels; the tile's remaining
+// rows see zero fill and are dropped). CTA b walks a contiguous range of pool rows: for each it
+// computes conv rows 2po and 2po + 1 (and, at the start of its range, the halo row 2po - 1), keeps
+// the last three conv rows in a shared-memory ring and, after each odd row, the epilogue warps write
+// one pool row. The conv output (1.6 MB per 224x224 image) never reaches global memory.
+// A operand: k-tile kt is filter column b = kt; one 4D tiled TMA load of 4 image rows x 128 pixels x
+// 16 channels lands as the four 4 KB K=16 sub-tiles of filter rows a = 0..3 (4 loads per tile, where
+// 16 im2col loads of one tap each are needed otherwise). B: the 64 x 256 weights, resident.
+// Warps: 0 and 10-12 TMA producers, 1 and 13-15 MMA issuers (split-K partials in TMEM, as in
+// conv_gemm_kernel), 2-9 epilogue. Every wait is bounded; the epilogue warps synchronise through
+// two mbarriers (ring row written / pool row done), never through an unbounded named barrier.
+constexpr int kStemKT = 4;                      // k-tiles: filter columns
+constexpr uint32_t kStemAStage = 4 * BM * 32;   // 16 KB: four 4 KB sub-tiles
+constexpr uint32_t kStemBBytes = 64 * 128;      // one 64 x 64 bf16 weight k-tile
+constexpr uint32_t kStemRingRow = 128 * 128;    // 128 pixels x 64 bf16 channels
+
+// The conv rows CTA `cta` computes, in order: calls f(n, r, pool) for each, where pool says that the
+// row completes pool row r / 2 (r odd, and not the halo row of the range's first pool row).
+template <typename F>
+__device__ __forceinline__ void stem_rows(const StemPoolArgs& a, int cta, int ctas, F&& f) {
+  const int Hp = a.Ho / 2;
+  const int64_t total = int64_t(a.N) * Hp;
+  const int64_t p0 = total * cta / ctas, p1 = total * (cta + 1) / ctas;
+  for (int64_t p = p0; p < p1; ++p) {
+    const int n = int(p / Hp), po = int(p - int64_t(n) * Hp);
+    if (p == p0 && po > 0)
+      if (!f(n, 2 * po - 1, false)) return;
+    if (!f(n, 2 * po, false)) return;
+    if (!f(n, 2 * po + 1, true)) return;
+  }
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* tm, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(
+          smem_u32(dst)),
+      "l"(tm), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Swizzled 16-byte chunk j (8 channels) of pixel px in a ring row (128-byte pixel rows).
+__device__ __forceinline__ uint32_t ring_off(int px, int j) { return uint32_t(px * 128 + ((j ^ (px & 7)) << 4)); }
+
+__global__ void __launch_bounds__(512, 1)
+    stem_pool_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const StemPoolArgs a) {
+  constexpr uint32_t idesc = idesc_mma(BM, 64, false);
+  const int STAGES = a.stages;
+  const int NP = a.producers;
+  const int PE = a.mma_lanes;
+  const uint32_t TMEM_COLS = uint32_t(2 * PE * 64);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * kStemAStage;
+  uint8_t* ring = sB + kStemKT * kStemBBytes;
+  float* sBias = reinterpret_cast<float*>(ring + 3 * kStemRingRow);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sBias + 64);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* accf = empty + kMaxStages;
+  uint64_t* acce = accf + 2;
+  uint64_t* bfull = acce + 2;
+  uint64_t* ring_full = bfull + 1;   // the 8 epilogue warps wrote the tile's row into the ring
+  uint64_t* pool_done = ring_full + 1;   // the 8 epilogue warps finished reading the ring for the tile
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(pool_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1u);
+      mbar_init(&empty[s], 1u);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf[i], uint32_t(PE));
+      mbar_init(&acce[i], 8u);
+    }
+    mbar_init(bfull, 1u);
+    mbar_init(ring_full, 8u);
+    mbar_init(pool_done, 8u);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (threadIdx.x < 64) sBias[threadIdx.x] = a.bias[threadIdx.x];
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0 || (warp >= 10 && warp <= 12)) {
+    // ---- TMA producers: k-tiles dealt round-robin over NP threads ----
+    const int pid = warp == 0 ? 0 : warp - 9;
+    if (lane == 0 && pid < NP) {
+      if (pid == 0) {
+        mbar_expect_tx(bfull, uint32_t(kStemKT) * kStemBBytes);
+        for (int kt = 0; kt < kStemKT; ++kt) tma_load_2d(sB + kt * kStemBBytes, &tmB, kt * BK, 0, bfull);
+      }
+      int stage = 0, owner = 0;
+      uint32_t phase = 0;
+      stem_rows(a, blockIdx.x, gridDim.x, [&](int n, int r, bool) {
+        for (int kt = 0; kt < kStemKT; ++kt) {
+          const bool mine = owner == pid;
+          if (++owner == NP) owner = 0;
+          if (mine) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) return false;
+            mbar_expect_tx(&full[stage], kStemAStage);
+            // filter column kt, filter rows 0..3: image rows r - ph .. r - ph + 3, pixels kt - pw ..
+            tma_load_4d(sA + stage * kStemAStage, &tmA, 0, kt - a.pw, r - a.ph, n, &full[stage]);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        return true;
+      });
+    }
+  } else if (warp == 1 || warp >= 13) {
+    // ---- MMA issuers: issuer mid takes the k-tiles g = mid (mod PE) into its own partial ----
+    const int mid = warp == 1 ? 0 : warp - 12;
+    if (lane == 0 && mid < PE) {
+      int it = 0, g0 = 0, g = mid, stage = mid;
+      uint32_t phase = 0;
+      if (mbar_wait(bfull, 0u, abort_flag, a.err, 128u)) {
+        stem_rows(a, blockIdx.x, gridDim.x, [&](int, int, bool) {
+          const int acc = it & 1;
+          const uint32_t aph = uint32_t(it >> 1) & 1u;
+          if (!mbar_wait(&acce[acc], aph ^ 1u, abort_flag, a.err, 2u)) return false;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + uint32_t((acc * PE + mid) * 64);
+          for (bool first = true; g < g0 + kStemKT; first = false) {
+            const int kt = g - g0;
+            if (!mbar_wait(&full[stage], phase, abort_flag, a.err, 4u)) return false;
+            tc_fence_after();
+            const uint64_t bd = sw128_desc(smem_u32(sB + kt * kStemBBytes));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16(d_tmem, sw32_desc(smem_u32(sA + stage * kStemAStage + kk * (BM * 32))), bd + uint64_t(kk * 2),
+                        idesc, (!first || kk != 0) ? 1u : 0u);
+            umma_commit(&empty[stage]);
+            g += PE;
+            stage += PE;
+            if (stage >= STAGES) {
+              stage -= STAGES;
+              phase ^= 1u;
+            }
+          }
+          umma_commit(&accf[acc]);
+          ++it;
+          g0 += kStemKT;
+          return true;
+        });
+      }
+    }
+  } else {
+    // ---- epilogue warps 2-9: warp w holds pixels 32 (w & 3) .. + 31 and channels 32 hsel .. + 31 ----
+    const int q = warp & 3, hsel = (warp - 2) >> 2;
+    const int ew = warp - 2;   // 0..7
+    const int Hp = a.Ho / 2, Wp = a.Wo / 2;
+    const int px = q * 32 + lane;
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+    int it = 0;
+    stem_rows(a, blockIdx.x, gridDim.x, [&](int n, int r, bool pool) {
+      const int acc = it & 1;
+      const uint32_t aph = uint32_t(it >> 1) & 1u;
+      if (!mbar_wait(&accf[acc], aph, abort_flag, a.err, 8u)) return false;
+      tc_fence_after();
+      float v[32];
+      tmem_ld_sum(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * PE * 64 + hsel * 32), PE, 64, v);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[acc]);
+      // the previous tile's pool reads of the ring are done before its slot r % 3 is overwritten
+      if (it > 0 && !mbar_wait(pool_done, uint32_t(it - 1) & 1u, abort_flag, a.err, 16u)) return false;
+      if (px < a.Wo) {
+        uint8_t* row = ring + (r % 3) * kStemRingRow;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float t[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) t[e] = v[8 * j + e] + sBias[hsel * 32 + 8 * j + e];
+          uint4 qv;
+          if (a.act == 1) {
+            qv.x = pack_bf16x2_relu(t[0], t[1]);
+            qv.y = pack_bf16x2_relu(t[2], t[3]);
+            qv.z = pack_bf16x2_relu(t[4], t[5]);
+            qv.w = pack_bf16x2_relu(t[6], t[7]);
+          } else {
+            qv.x = pack_bf16x2(t[0], t[1]);
+            qv.y = pack_bf16x2(t[2], t[3]);
+            qv.z = pack_bf16x2(t[4], t[5]);
+            qv.w = pack_bf16x2(t[6], t[7]);
+          }
+          *reinterpret_cast<uint4*>(row + ring_off(px, hsel * 4 + j)) = qv;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ring_full);
+      if (!mbar_wait(ring_full, uint32_t(it) & 1u, abort_flag, a.err, 32u)) return false;
+      if (pool) {   // pool row po = r / 2 from conv rows r - 2 (padding when po = 0), r - 1, r
+        const int po = r >> 1;
+        const uint8_t* rows[3] = {po > 0 ? ring + ((r + 1) % 3) * kStemRingRow : nullptr,
+                                  ring + ((r + 2) % 3) * kStemRingRow, ring + (r % 3) * kStemRingRow};
+        __nv_bfloat16* orow = out + (int64_t(n) * Hp + po) * int64_t(Wp) * 64;
+        for (int i = ew * 32 + lane; i < Wp * 8; i += 256) {
+          const int qo = i >> 3, j = i & 7;
+          uint4 m = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);   // bf16 -inf
+#pragma unroll
+          for (int dr = 0; dr < 3; ++dr) {
+            if (!rows[dr]) continue;
+#pragma unroll
+            for (int dc = -1; dc <= 1; ++dc) {
+              const int c = 2 * qo + dc;
+              if (c < 0 || c >= a.Wo) continue;
+              m = bf16x8_max(m, *reinterpret_cast<const uint4*>(rows[dr] + ring_off(c, j)));
+            }
+          }
+          *reinterpret_cast<uint4*>(orow + qo * 64 + j * 8) = m;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pool_done);
+      ++it;
+      return true;
+    });
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -1359,6 +1614,55 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   cudaError_t e = bn == 64 ? ensure_attr_mode<64>(mode, prec)
                            : (bn == 128 ? ensure_attr_mode<128>(mode, prec) : ensure_attr_mode<256>(mode, prec));
   if (e != cudaSuccess) throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+}
+
+bool stem_pool_supported(int Cout, int Ho, int Wo, int KH, int KW) {
+  return Cout == 64 && Wo <= BM && Ho % 2 == 0 && Wo % 2 == 0 && KH == 4 && KW == 4;
+}
+
+void stem_pool_prepare(StemPoolPlan& p, const void* w, int num_sms) {
+  StemPoolArgs& a = p.args;
+  std::memset(&p.tmA, 0, sizeof(p.tmA));
+  std::memset(&p.tmB, 0, sizeof(p.tmB));
+  auto fn = get_encode_fn();
+  if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled entry point missing");
+  // the space-to-depth image as a 4D tensor (channel, x, y, image); one box = 4 rows x 128 pixels
+  // x 16 channels, 32-byte rows swizzled as the K=16 MMA sub-tiles expect
+  cuuint64_t dims[4] = {16, cuuint64_t(a.Ws), cuuint64_t(a.Hs), cuuint64_t(a.N)};
+  cuuint64_t strides[3] = {32, cuuint64_t(a.Ws) * 32, cuuint64_t(a.Hs) * a.Ws * 32};
+  cuuint32_t box[4] = {16, BM, 4, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(&p.tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(a.x), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed for the stem input");
+  if (!encode_2d(&p.tmB, w, uint64_t(kStemKT) * BK, 64, uint64_t(kStemKT) * BK * 2, BK, 64))
+    throw std::runtime_error("cuTensorMapEncodeTiled failed for the stem weights");
+  // two MMA issuers and two producers; stages a multiple of both
+  a.mma_lanes = 2;
+  a.producers = 2;
+  const int fixed = int(kStemKT * kStemBBytes + 3 * kStemRingRow) + 256 + 1024 + 512;
+  int stages = std::min(kMaxStages, (kSmemLimit - fixed) / int(kStemAStage));
+  stages -= stages % 2;
+  if (stages < 2) throw std::runtime_error("stem_pool: shared-memory plan leaves fewer than 2 stages");
+  a.stages = stages;
+  p.smem = stages * int(kStemAStage) + fixed;
+  const int64_t pool_rows = int64_t(a.N) * (a.Ho / 2);
+  p.grid = int(std::min<int64_t>(num_sms, pool_rows));
+  static std::atomic<uint64_t> done_mask{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = uint64_t(1) << (dev & 63);
+  if (!(done_mask.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(stem_pool_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    done_mask.fetch_or(bit);
+  }
+}
+
+cudaError_t stem_pool_launch(const StemPoolPlan& p, cudaStream_t s) {
+  stem_pool_kernel<<<p.grid, 512, p.smem, s>>>(p.tmA, p.tmB, p.args);
+  return cudaGetLastError();
 }
 
 cudaError_t conv_gemm_launch(const ConvGemmPlan& p, cudaStream_t s) {

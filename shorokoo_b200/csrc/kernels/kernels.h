@@ -98,6 +98,33 @@ struct ConvGemmPlan {
 void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const void* w, int num_sms);
 cudaError_t conv_gemm_launch(const ConvGemmPlan& p, cudaStream_t s);
 
+// ---- stem convolution with its 3x3/2 max pool fused into the epilogue (conv_gemm.cu) ----------
+// y = maxpool3x3/2,pad1( act( conv(x) + bias ) ) for the ResNet stem run as a 4x4 stride-1 conv over
+// the 2x2 space-to-depth image x (NHWC bf16 [N, Hs, Ws, 16]); weights bf16 [64, 256] with K ordered
+// (filter column b, filter row a, channel c); y NHWC bf16 [N, Ho/2, Wo/2, 64]. Requires Cout = 64,
+// Wo <= 128, Ho and Wo even. The conv output itself is never written to global memory.
+struct StemPoolArgs {
+  const void* x;
+  int N, Hs, Ws;           // space-to-depth image
+  int Ho, Wo;              // conv output (before pooling)
+  int ph, pw;              // conv padding in space-to-depth pixels
+  const float* bias;       // [64] f32
+  void* out;               // [N, Ho/2, Wo/2, 64] bf16
+  int act;                 // 0 none, 1 relu
+  unsigned int* err;
+  // set by stem_pool_prepare:
+  int stages, producers, mma_lanes;
+};
+struct StemPoolPlan {
+  CUtensorMap tmA;   // 4D tiled map of x: box 16 channels x 128 pixels x 4 rows
+  CUtensorMap tmB;   // weights, 64 x 64 boxes (one k-tile)
+  int grid, smem;
+  StemPoolArgs args;
+};
+bool stem_pool_supported(int Cout, int Ho, int Wo, int KH, int KW);
+void stem_pool_prepare(StemPoolPlan& p, const void* w, int num_sms);
+cudaError_t stem_pool_launch(const StemPoolPlan& p, cudaStream_t s);
+
 // ---- memory-bound kernels (misc.cu) ------------------------------------------------------------
 constexpr int kMaxRank = 8;
 struct TDesc {

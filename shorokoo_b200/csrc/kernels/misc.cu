@@ -376,7 +376,75 @@ __global__ void maxpool_nhwc_scalar_kernel(const __nv_bfloat16* __restrict__ x, 
   }
 }
 
-// ---- global average / max pool over NHWC: one thread per (n, channel) -------------------------
+// ---- global average / max pool over NHWC -------------------------------------------------------
+// One block per (image, slab of G x V channels): thread t owns channel group g = t % G (V channels,
+// one 128-bit load per pixel) and the pixels p = t / G (mod 256 / G). Each warp's lanes that share a
+// channel group are combined with shuffles (lane bits above log2 G), then the block's warps through
+// shared memory. A warp's loads of one pixel are G consecutive 16-byte chunks (coalesced).
+template <bool BF16>
+__global__ void global_pool_vec_kernel(const void* __restrict__ x, int HW, int C, int64_t ldp, void* __restrict__ y,
+                                       int y_bf16, int is_max, int G) {
+  constexpr int V = BF16 ? 8 : 4;   // channels per 16-byte load
+  __shared__ float part[kThreads / 32][32][V];
+  const int slabs = (C / V + G - 1) / G;
+  const int n = blockIdx.x / slabs, slab = blockIdx.x - n * slabs;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int g = t % G, pslot = t / G, P = kThreads / G;
+  const int cg = slab * G + g;   // channel group
+  const bool valid = cg < C / V;
+  float acc[V];
+#pragma unroll
+  for (int j = 0; j < V; ++j) acc[j] = is_max ? -INFINITY : 0.f;
+  if (valid) {
+    const uint8_t* base = reinterpret_cast<const uint8_t*>(x) + (int64_t(n) * HW * ldp + int64_t(cg) * V) * (BF16 ? 2 : 4);
+    for (int p = pslot; p < HW; p += P) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(base + int64_t(p) * ldp * (BF16 ? 2 : 4)));
+      float v[V];
+      if (BF16) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q);
+#pragma unroll
+        for (int j = 0; j < V / 2; ++j) {
+          const float2 f = __bfloat1622float2(h[j]);
+          v[2 * j] = f.x;
+          v[2 * j + 1] = f.y;
+        }
+      } else {
+        v[0] = __uint_as_float(q.x);
+        v[1] = __uint_as_float(q.y);
+        v[2] = __uint_as_float(q.z);
+        v[3] = __uint_as_float(q.w);
+      }
+#pragma unroll
+      for (int j = 0; j < V; ++j) acc[j] = is_max ? fmaxf(acc[j], v[j]) : acc[j] + v[j];
+    }
+  }
+  // lanes of one warp with the same channel group differ in the lane bits above log2(G)
+  for (int sft = G; sft < 32; sft <<= 1)
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const float o = __shfl_xor_sync(0xffffffffu, acc[j], sft);
+      acc[j] = is_max ? fmaxf(acc[j], o) : acc[j] + o;
+    }
+  // (G is a power of two up to 32, so lane l of every warp holds group l % G: after the shuffles
+  // lanes 0..G-1 hold the warp's partial result of groups 0..G-1)
+  if (lane < G)
+#pragma unroll
+    for (int j = 0; j < V; ++j) part[warp][lane][j] = acc[j];
+  __syncthreads();
+  if (t < G && valid) {
+    float r[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) r[j] = is_max ? -INFINITY : 0.f;
+    for (int w = 0; w < kThreads / 32; ++w)
+#pragma unroll
+      for (int j = 0; j < V; ++j) r[j] = is_max ? fmaxf(r[j], part[w][t][j]) : r[j] + part[w][t][j];
+    const int64_t o = int64_t(n) * C + int64_t(cg) * V;
+#pragma unroll
+    for (int j = 0; j < V; ++j) st_any(y, y_bf16, o + j, is_max ? r[j] : r[j] / float(HW));
+  }
+}
+
+// Scalar global pool (channel counts or pitches without 16-byte alignment): one thread per (n, c).
 __global__ void global_pool_kernel(const void* __restrict__ x, int x_bf16, int N, int HW, int C, int64_t ldp,
                                    void* __restrict__ y, int y_bf16, int is_max) {
   const int64_t total = int64_t(N) * C;
@@ -437,6 +505,61 @@ __global__ void elementwise_kernel(int op, const void* __restrict__ a, int a_bf1
     const float va = ld_any(a, a_bf16, offset_of(i, ad));
     const float vb = b ? ld_any(b, b_bf16, offset_of(i, bd)) : 0.f;
     st_any(y, y_bf16, offset_of(i, yd), ew_apply(op, va, vb, alpha, beta));
+  }
+}
+
+// Four consecutive elements of the innermost dimension per thread (the dimensions having been
+// collapsed on the host so that the innermost one is as long as possible): the outer index is
+// divided out once per four elements, and an operand whose innermost stride is 1 is read / written
+// with one 16-byte (fp32) or 8-byte (bf16) access; stride 0 (a broadcast operand) is one load.
+// L % 4 == 0 and every unit-stride operand is aligned for its vector access.
+struct Vec4Op {
+  const void* p;
+  int bf16;
+  int64_t s_in;   // innermost stride (0, 1 or other)
+  TDesc outer;    // the outer dimensions
+};
+__device__ __forceinline__ void vload4(const Vec4Op& o, int64_t off, float (&v)[4]) {
+  if (o.s_in == 1) {
+    if (o.bf16) {
+      const uint2 q = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(o.p) + off));
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.x));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.y));
+      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    } else {
+      const float4 q = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(o.p) + off));
+      v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+    }
+  } else if (o.s_in == 0) {
+    v[0] = v[1] = v[2] = v[3] = ld_any(o.p, o.bf16, off);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = ld_any(o.p, o.bf16, off + j * o.s_in);
+  }
+}
+__global__ void elementwise_vec4_kernel(int op, Vec4Op a, Vec4Op b, void* __restrict__ y, int y_bf16, int64_t ys_in,
+                                        TDesc youter, int64_t L, float alpha, float beta, int64_t nvec) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < nvec; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t e = i * 4;
+    const int64_t outer = e / L, in = e - outer * L;
+    float va[4], vb[4] = {0.f, 0.f, 0.f, 0.f};
+    vload4(a, offset_of(outer, a.outer) + in * a.s_in, va);
+    if (b.p) vload4(b, offset_of(outer, b.outer) + in * b.s_in, vb);
+    float r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r[j] = op < 0 ? va[j] : ew_apply(op, va[j], vb[j], alpha, beta);
+    const int64_t yo = offset_of(outer, youter) + in * ys_in;
+    if (ys_in == 1 && !y_bf16) {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + yo) = make_float4(r[0], r[1], r[2], r[3]);
+    } else if (ys_in == 1) {
+      uint2 q;
+      *reinterpret_cast<__nv_bfloat162*>(&q.x) = __floats2bfloat162_rn(r[0], r[1]);
+      *reinterpret_cast<__nv_bfloat162*>(&q.y) = __floats2bfloat162_rn(r[2], r[3]);
+      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(y) + yo) = q;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) st_any(y, y_bf16, yo + j * ys_in, r[j]);
+    }
   }
 }
 
@@ -581,15 +704,115 @@ cudaError_t maxpool_nhwc_bf16(const void* x, void* y, int N, int H, int W, int C
 
 cudaError_t global_pool_nhwc(const void* x, int x_bf16, int N, int HW, int C, int64_t ldp, void* y, int y_bf16,
                              int is_max, cudaStream_t s) {
+  const int V = x_bf16 ? 8 : 4;
+  if (C % V == 0 && ldp % V == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && HW > 0) {
+    // channel groups per block: all of them up to 32, else 32 (a warp covers 512 contiguous bytes)
+    int G = 1;
+    while (G < 32 && G < C / V) G <<= 1;
+    const int64_t blocks = int64_t(N) * ((C / V + G - 1) / G);
+    if (x_bf16)
+      global_pool_vec_kernel<true><<<unsigned(blocks), kThreads, 0, s>>>(x, HW, C, ldp, y, y_bf16, is_max, G);
+    else
+      global_pool_vec_kernel<false><<<unsigned(blocks), kThreads, 0, s>>>(x, HW, C, ldp, y, y_bf16, is_max, G);
+    return cudaGetLastError();
+  }
   global_pool_kernel<<<grid_for(int64_t(N) * C), kThreads, 0, s>>>(x, x_bf16, N, HW, C, ldp, y, y_bf16, is_max);
   return cudaGetLastError();
 }
+
+namespace {
+
+// Merges adjacent dimensions that are contiguous with respect to each other in every descriptor
+// (all of the same shape) and drops unit dimensions, so the innermost dimension is as long as
+// possible. Returns the rank after collapsing.
+int collapse_dims(TDesc** d, int n) {
+  const int rank = d[0]->rank;
+  int64_t shape[kMaxRank];
+  int64_t st[4][kMaxRank];
+  int r = 0;
+  for (int i = 0; i < rank; ++i) {
+    const int64_t sz = d[0]->shape[i];
+    if (sz == 1) continue;
+    bool merge = r > 0;
+    for (int k = 0; k < n && merge; ++k) merge = st[k][r - 1] == d[k]->stride[i] * sz;
+    if (merge) {
+      shape[r - 1] *= sz;
+      for (int k = 0; k < n; ++k) st[k][r - 1] = d[k]->stride[i];
+    } else {
+      shape[r] = sz;
+      for (int k = 0; k < n; ++k) st[k][r] = d[k]->stride[i];
+      ++r;
+    }
+  }
+  if (r == 0) {
+    shape[0] = 1;
+    for (int k = 0; k < n; ++k) st[k][0] = 1;
+    r = 1;
+  }
+  for (int k = 0; k < n; ++k) {
+    d[k]->rank = r;
+    for (int i = 0; i < r; ++i) {
+      d[k]->shape[i] = shape[i];
+      d[k]->stride[i] = st[k][i];
+    }
+  }
+  return r;
+}
+
+bool aligned_for(const void* p, int bf16, int64_t s_in, const TDesc& outer) {
+  if (s_in != 1) return true;
+  const int64_t need = 4;   // elements per vector access (8 or 16 bytes)
+  if ((reinterpret_cast<uintptr_t>(p) & (bf16 ? 7 : 15)) != 0) return false;
+  for (int i = 0; i < outer.rank; ++i)
+    if (outer.stride[i] % need) return false;
+  return true;
+}
+
+// The vectorised path when the collapsed innermost length is a multiple of 4 and the accesses are
+// aligned; false to fall back to the per-element kernels.
+bool launch_vec4(int op, const void* a, int a_bf16, TDesc ad, const void* b, int b_bf16, TDesc bd, void* y,
+                 int y_bf16, TDesc yd, float alpha, float beta, cudaStream_t s) {
+  TDesc* ds[3] = {&yd, &ad, &bd};
+  const int r = collapse_dims(ds, b ? 3 : 2);
+  const int64_t L = yd.shape[r - 1];
+  if (L % 4 != 0) return false;
+  auto outer_of = [&](const TDesc& d) {
+    TDesc o{};
+    o.rank = r - 1;
+    for (int i = 0; i < r - 1; ++i) {
+      o.shape[i] = d.shape[i];
+      o.stride[i] = d.stride[i];
+    }
+    if (o.rank == 0) {   // a single row
+      o.rank = 1;
+      o.shape[0] = 1;
+      o.stride[0] = 0;
+    }
+    return o;
+  };
+  Vec4Op va{a, a_bf16, ad.stride[r - 1], outer_of(ad)};
+  Vec4Op vb{b, b_bf16, b ? bd.stride[r - 1] : 0, b ? outer_of(bd) : TDesc{}};
+  const TDesc yo = outer_of(yd);
+  const int64_t ys = yd.stride[r - 1];
+  if (!aligned_for(a, a_bf16, va.s_in, va.outer) || (b && !aligned_for(b, b_bf16, vb.s_in, vb.outer)) ||
+      !aligned_for(y, y_bf16, ys, yo))
+    return false;
+  int64_t total = 1;
+  for (int i = 0; i < r; ++i) total *= yd.shape[i];
+  const int64_t nvec = total / 4;
+  elementwise_vec4_kernel<<<grid_for(nvec), kThreads, 0, s>>>(op, va, vb, y, y_bf16, ys, yo, L, alpha, beta, nvec);
+  return true;
+}
+
+}  // namespace
 
 cudaError_t strided_copy(const void* src, int src_bf16, const TDesc& sd, void* dst, int dst_bf16, const TDesc& dd,
                          cudaStream_t s) {
   int64_t total = 1;
   for (int i = 0; i < dd.rank; ++i) total *= dd.shape[i];
   if (total == 0) return cudaSuccess;
+  if (launch_vec4(-1, src, src_bf16, sd, nullptr, 0, TDesc{}, dst, dst_bf16, dd, 0.f, 0.f, s))
+    return cudaGetLastError();
   strided_copy_kernel<<<grid_for(total), kThreads, 0, s>>>(src, src_bf16, sd, dst, dst_bf16, dd, total);
   return cudaGetLastError();
 }
@@ -605,6 +828,7 @@ cudaError_t elementwise(int op, const void* a, int a_bf16, const TDesc& ad, cons
   int64_t total = 1;
   for (int i = 0; i < yd.rank; ++i) total *= yd.shape[i];
   if (total == 0) return cudaSuccess;
+  if (launch_vec4(op, a, a_bf16, ad, b, b_bf16, bd, y, y_bf16, yd, alpha, beta, s)) return cudaGetLastError();
   elementwise_kernel<<<grid_for(total), kThreads, 0, s>>>(op, a, a_bf16, ad, b, b_bf16, bd, y, y_bf16, yd, alpha, beta,
                                                           total);
   return cudaGetLastError();

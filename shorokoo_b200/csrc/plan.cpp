@@ -374,6 +374,193 @@ DevTensor Plan::as_rows_op(int v, int64_t M, int64_t K, int prec) {
   return dst;
 }
 
+// Storage of conv output v inside the buffer of the Concat it reaches through single-reader views
+// (the RetinaNet heads: NHWC conv output -> Reshape [B,A,K,H,W] -> Transpose(0,3,4,1,2) ->
+// Reshape [B,H*W*A,K] -> Concat on axis 1, RetinaNetDetector.cs:539-571): when those views of NHWC
+// rows placed in the concat's buffer land exactly on the concat's slice for this input, the conv
+// writes its rows there (grouped per image: the image stride is the concat's) and the concat copies
+// nothing. Returns an invalid tensor when the layouts do not line up.
+DevTensor Plan::concat_home(int v, int64_t Cout) {
+  const Value& yv = g_.vals[size_t(v)];
+  if (yv.shape.size() != 4) return {};
+  std::vector<const Op*> chain;
+  const Op* cat = nullptr;
+  int cur = v;
+  while (true) {
+    if (is_output_[size_t(cur)] || consumers_[size_t(cur)].size() != 1) return {};
+    const Op& o = g_.ops[size_t(consumers_[size_t(cur)][0])];
+    if (o.type == "Concat") {
+      cat = &o;
+      break;
+    }
+    if (!((o.type == "Reshape" || o.type == "Transpose" || o.type == "Identity") && o.in[0] == cur)) return {};
+    chain.push_back(&o);
+    cur = o.out[0];
+  }
+  const int cid = cat->out[0];
+  const Value& cv = g_.vals[size_t(cid)];
+  if (cv.shape.empty() || cv.shape[0] != yv.shape[0]) return {};
+  DevTensor& y = concat_out_[cid];
+  if (!y.valid()) y = alloc_contig(cv.shape, false);
+  int64_t off = 0;
+  for (int id : cat->in) {
+    if (id == cur) break;
+    off += g_.vals[size_t(id)].shape[size_t(cat->axis)];
+  }
+  DevTensor dst = y;
+  dst.shape = g_.vals[size_t(cur)].shape;
+  dst.off = off * y.strides[size_t(cat->axis)] * 4;
+  const int64_t W = yv.shape[3];
+  DevTensor t = y;
+  t.shape = yv.shape;
+  t.strides = {y.strides[0], 1, W * Cout, Cout};
+  t.off = dst.off;
+  DevTensor r = t;
+  for (const Op* o : chain) {
+    const Value& ov = g_.vals[size_t(o->out[0])];
+    if (o->type == "Transpose") {
+      DevTensor q = r;
+      q.shape.clear();
+      q.strides.clear();
+      for (auto pp : o->perm) {
+        q.shape.push_back(r.shape[size_t(pp)]);
+        q.strides.push_back(r.strides[size_t(pp)]);
+      }
+      r = q;
+    } else if (o->type == "Reshape") {
+      auto vs = view_strides(r.shape, r.strides, ov.shape);
+      if (!vs) return {};
+      r.shape = ov.shape;
+      r.strides = *vs;
+    }
+  }
+  if (r.shape != dst.shape || r.off != dst.off) return {};
+  for (size_t d = 0; d < r.shape.size(); ++d)
+    if (r.shape[d] != 1 && r.strides[d] != dst.strides[d]) return {};
+  if (y.strides[0] < yv.shape[2] * W * Cout) return {};
+  return t;
+}
+
+// The ResNet stem pattern the fused stem + max-pool kernel runs: a bf16 7x7/2-style conv over at
+// most 4 channels (space-to-depth eligible, a 4x4 kernel after the transform) to 64 channels, no
+// residual, whose only reader is a MaxPool 3x3 / stride 2 / pad 1 (floor mode) with an even, at most
+// 128 pixel wide input and a bf16-stored output.
+void Plan::find_stem_pools() {
+  for (size_t i = 0; i < g_.ops.size(); ++i) {
+    const Op& op = g_.ops[i];
+    if (op.dead || op.type != "FusedConv" || op.prec != 0 || op.residual >= 0 || op.concat >= 0 || op.act > 1)
+      continue;
+    const Value& xv = g_.vals[size_t(op.in[0])];
+    const Value& yv = g_.vals[size_t(op.out[0])];
+    const auto& w = op.weight->shape;
+    if (xv.shape.size() != 4 || w.size() != 4 || xv.shape[1] > 4 || op.group != 1) continue;
+    if (op.strides[0] != 2 || op.strides[1] != 2 || op.dilations[0] != 1 || op.dilations[1] != 1 || w[2] < 3 || w[3] < 3)
+      continue;
+    const int64_t gkh = ceil_div(w[2] + op.pads[0] % 2, 2), gkw = ceil_div(w[3] + op.pads[1] % 2, 2);
+    if (!k::stem_pool_supported(int(w[0]), int(yv.shape[2]), int(yv.shape[3]), int(gkh), int(gkw))) continue;
+    if (is_output_[size_t(op.out[0])] || consumers_[size_t(op.out[0])].size() != 1) continue;
+    const int pi = consumers_[size_t(op.out[0])][0];
+    const Op& mp = g_.ops[size_t(pi)];
+    if (mp.type != "MaxPool" || mp.in[0] != op.out[0] || mp.kernel != std::vector<int64_t>{3, 3} ||
+        mp.strides != std::vector<int64_t>{2, 2} || mp.pads != std::vector<int64_t>{1, 1, 1, 1} || mp.ceil_mode ||
+        (!mp.dilations.empty() && mp.dilations != std::vector<int64_t>{1, 1}))
+      continue;
+    const Value& pv = g_.vals[size_t(mp.out[0])];
+    if (pv.shape.size() != 4 || pv.shape[2] * 2 != yv.shape[2] || pv.shape[3] * 2 != yv.shape[3]) continue;
+    if (storage_class(mp.out[0], kStoreBf16) != kStoreBf16) continue;
+    stem_pool_[int(i)] = pi;
+    pooled_by_conv_.insert(pi);
+  }
+}
+
+// Space-to-depth NHWC bf16 image [N, ceil(H/2), ceil(W/2), 16] of a stride-2 conv's input (shared by
+// every conv that reads the same value this way).
+DevTensor Plan::s2d_input(int v) {
+  auto key = std::make_pair(v, -16);
+  auto it = conv_cache_.find(key);
+  if (it != conv_cache_.end()) return it->second;
+  const DevTensor t = vt_[size_t(v)];
+  const int64_t N = t.shape[0], H = t.shape[2], W = t.shape[3];
+  const int64_t Hs = ceil_div(H, 2), Ws = ceil_div(W, 2);
+  DevTensor x = alloc_nhwc({N, 16, Hs, Ws}, true, 16);
+  add_step("to_s2d_bf16", {t}, {x}, [this, t, x, Hs, Ws]() {
+    const void* sp = ptr(t);
+    void* dp = ptr(x);
+    int64_t sh[4] = {t.shape[0], t.shape[1], t.shape[2], t.shape[3]};
+    int64_t st[4] = {t.strides[0], t.strides[1], t.strides[2], t.strides[3]};
+    int sb = t.bf16;
+    return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+      return k::to_s2d_bf16(sp, sb, sh, st, dp, Hs, Ws, s);
+    });
+  });
+  conv_cache_[key] = x;
+  return x;
+}
+
+// The stem conv and the max pool reading it as one kernel (k::stem_pool_*): the space-to-depth 4x4
+// conv whose K is ordered (filter column, filter row, channel) so that one 4D TMA box of 4 image rows
+// holds a whole k-tile; output = the pool's output, NHWC bf16.
+void Plan::plan_stem_pool(const Op& op, const Op& pool) {
+  const Value& xv = g_.vals[size_t(op.in[0])];
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  const Value& pv = g_.vals[size_t(pool.out[0])];
+  const HostTensor& Wt = *op.weight;
+  const int64_t N = xv.shape[0], C = xv.shape[1], H = xv.shape[2], W = xv.shape[3];
+  const int64_t Cout = Wt.shape[0], KH = Wt.shape[2], KW = Wt.shape[3];
+  const int64_t Ho = yv.shape[2], Wo = yv.shape[3];
+  const int64_t et = op.pads[0] % 2, el = op.pads[1] % 2;
+  const int64_t gKH = ceil_div(KH + et, 2), gKW = ceil_div(KW + el, 2);
+  const int64_t gph = (op.pads[0] + et) / 2, gpw = (op.pads[1] + el) / 2;
+  DevTensor x = s2d_input(op.in[0]);
+  const int64_t Kpad = gKH * gKW * 16;   // 256
+  std::vector<float> wf(size_t(Cout * Kpad), 0.f);
+  const float* wp = Wt.ptr<float>();
+  for (int64_t m = 0; m < Cout; ++m)
+    for (int64_t c = 0; c < C; ++c)
+      for (int64_t a = 0; a < KH; ++a)
+        for (int64_t b = 0; b < KW; ++b) {
+          const int64_t u = a + et, v = b + el;   // u = 2 a' + p, v = 2 b' + q
+          const int64_t kidx = ((v / 2) * gKH + (u / 2)) * 16 + ((u % 2) * 2 + (v % 2)) * C + c;
+          wf[size_t(m * Kpad + kidx)] = wp[((m * C + c) * KH + a) * KW + b];
+        }
+  DevTensor wt;
+  wt.buf = -1;
+  wt.off = add_operand_weights(wf, Cout, nullptr, 0);
+  std::vector<float> bias(size_t(round_up(Cout, 256)), 0.f);
+  for (int64_t m = 0; m < Cout; ++m) bias[size_t(m)] = op.bias ? op.bias->ptr<float>()[m] : 0.f;
+  DevTensor bt;
+  bt.buf = -1;
+  bt.off = add_weight_bytes(bias.data(), bias.size() * 4);
+  DevTensor y = alloc_nhwc(pv.shape, true, Cout);
+  vt_[size_t(pool.out[0])] = y;
+  const double macs = double(N * Ho * Wo) * double(Cout) * double(C * KH * KW);
+  stats_.macs += macs;
+  stats_.macs_by_prec[0] += macs;
+  stats_.tc_kernels++;
+  const int sms = num_sms_;
+  const std::string kind = "conv " + std::to_string(KH) + "x" + std::to_string(KW) + "/2 " + std::to_string(C) + "->" +
+                           std::to_string(Cout) + " M=" + std::to_string(N * Ho * Wo) + " s2d +maxpool3x3/2";
+  add_step(kind, {x}, {y}, [=]() {
+    auto p = std::make_shared<k::StemPoolPlan>();
+    k::StemPoolArgs& a = p->args;
+    std::memset(&a, 0, sizeof(a));
+    a.x = ptr(x);
+    a.N = int(N);
+    a.Hs = int(x.shape[2]);
+    a.Ws = int(x.shape[3]);
+    a.Ho = int(Ho);
+    a.Wo = int(Wo);
+    a.ph = int(gph);
+    a.pw = int(gpw);
+    a.bias = static_cast<const float*>(ptr(bt));
+    a.out = ptr(y);
+    a.act = op.act;
+    a.err = err_;
+    k::stem_pool_prepare(*p, ptr(wt), sms);
+    return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::stem_pool_launch(*p, s); });
+  });
+}
+
 // ---------------------------------------------------------------------------------------------
 void Plan::plan_conv(const Op& op) {
   const Value& xv = g_.vals[size_t(op.in[0])];
@@ -412,26 +599,7 @@ void Plan::plan_conv(const Op& op) {
                           op.pads[1] == 0 && op.pads[2] == 0 && op.pads[3] == 0 && Cp % (tf32 ? 4 : 8) == 0;
   DevTensor x;
   if (s2d) {
-    auto key = std::make_pair(op.in[0], -16);
-    auto it = conv_cache_.find(key);
-    if (it != conv_cache_.end()) {
-      x = it->second;
-    } else {
-      const DevTensor t = vt_[size_t(op.in[0])];
-      x = alloc_nhwc({N, 16, gH, gW}, true, 16);
-      const int64_t Hs = gH, Ws = gW;
-      add_step("to_s2d_bf16", {t}, {x}, [this, t, x, Hs, Ws]() {
-        const void* sp = ptr(t);
-        void* dp = ptr(x);
-        int64_t sh[4] = {t.shape[0], t.shape[1], t.shape[2], t.shape[3]};
-        int64_t st[4] = {t.strides[0], t.strides[1], t.strides[2], t.strides[3]};
-        int sb = t.bf16;
-        return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
-          return k::to_s2d_bf16(sp, sb, sh, st, dp, Hs, Ws, s);
-        });
-      });
-      conv_cache_[key] = x;
-    }
+    x = s2d_input(op.in[0]);
   } else {
     x = as_nhwc_op(op.in[0], Cp, prec);
   }
@@ -484,7 +652,16 @@ void Plan::plan_conv(const Op& op) {
 
   const int out_cls = storage_class(op.out[0], prec == 0 ? kStoreBf16 : (prec == 1 ? kStoreTf32 : kStoreF32));
   const bool out_bf16 = out_cls == kStoreBf16;
-  DevTensor y = alloc_nhwc(yv.shape, out_bf16, Cout);
+  DevTensor y;
+  int64_t grp_rows = 0, grp_stride = 0;   // rows per image and image stride when writing into a concat
+  if (!out_bf16) {
+    y = concat_home(op.out[0], Cout);
+    if (y.valid() && N > 1) {
+      grp_rows = Ho * Wo;
+      grp_stride = y.strides[0];
+    }
+  }
+  if (!y.valid()) y = alloc_nhwc(yv.shape, out_bf16, Cout);
   vt_[size_t(op.out[0])] = y;
 
   DevTensor r;
@@ -576,6 +753,8 @@ void Plan::plan_conv(const Op& op) {
     a.out = ptr(y);
     a.out_bf16 = int(y.bf16);
     a.ldo = Cout;
+    a.group_rows = grp_rows;
+    a.group_stride = grp_stride;
     a.act = op.act;
     a.err = err_;
     a.tf32 = f32;
@@ -843,7 +1022,8 @@ void Plan::plan_view(const Op& op) {
 
 void Plan::plan_concat(const Op& op) {
   const Value& yv = g_.vals[size_t(op.out[0])];
-  DevTensor y = alloc_contig(yv.shape, false);
+  auto home = concat_out_.find(op.out[0]);   // inputs written in place by their convs
+  DevTensor y = home != concat_out_.end() ? home->second : alloc_contig(yv.shape, false);
   vt_[size_t(op.out[0])] = y;
   int64_t off = 0;
   for (int id : op.in) {
@@ -864,6 +1044,12 @@ void Plan::plan_concat(const Op& op) {
     dst.off = off * y.strides[size_t(op.axis)] * 4;
     off += v.shape[size_t(op.axis)];
     if (numel(v.shape) == 0) continue;
+    if (src.buf == dst.buf && src.off == dst.off && src.shape == dst.shape && !src.bf16) {
+      bool same = true;
+      for (size_t d = 0; d < dst.shape.size(); ++d)
+        if (dst.shape[d] != 1 && src.strides[d] != dst.strides[d]) same = false;
+      if (same) continue;   // already in place
+    }
     add_step("concat_copy", {src}, {y}, [this, src, dst]() {
       const void* sp = ptr(src);
       void* dp = ptr(dst);
@@ -1064,10 +1250,17 @@ void Plan::build() {
     inputs_.push_back({int(k), t.buf, size_t(numel(v.shape)) * 4});
   }
 
+  find_stem_pools();
   for (size_t i = 0; i < g_.ops.size(); ++i) {
     const Op& op = g_.ops[i];
     if (op.dead) continue;
     const std::string& t = op.type;
+    auto sp = stem_pool_.find(int(i));
+    if (sp != stem_pool_.end()) {
+      plan_stem_pool(op, g_.ops[size_t(sp->second)]);
+      continue;
+    }
+    if (t == "MaxPool" && pooled_by_conv_.count(int(i))) continue;   // done by the stem kernel
     if (t == "FusedConv") plan_conv(op);
     else if (t == "FusedGemm") plan_gemm(op);
     else if (t == "MaxPool") plan_maxpool(op);
@@ -1190,6 +1383,23 @@ void Plan::enqueue_kernels(cudaStream_t stream) {
   } else {
     for (auto& st : steps_) ck(st(stream), "kernel launch");
   }
+}
+
+double Plan::time_kernels(cudaStream_t stream, int iters) {
+  cudaEvent_t e0, e1;
+  ck(cudaEventCreate(&e0), "event");
+  ck(cudaEventCreate(&e1), "event");
+  enqueue_kernels(stream);
+  ck(cudaEventRecord(e0, stream), "event record");
+  for (int i = 0; i < iters; ++i) enqueue_kernels(stream);
+  ck(cudaEventRecord(e1, stream), "event record");
+  ck(cudaEventSynchronize(e1), "event sync");
+  float t = 0;
+  ck(cudaEventElapsedTime(&t, e0, e1), "elapsed");
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  check_device_error();
+  return double(t) / std::max(iters, 1);
 }
 
 void Plan::enqueue(cudaStream_t stream, const std::vector<const void*>& host_in, const std::vector<void*>& host_out) {

@@ -7,6 +7,7 @@
 
 #include <functional>
 #include <memory>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -61,6 +62,9 @@ class Plan {
   void enqueue(cudaStream_t stream, const std::vector<const void*>& host_in, const std::vector<void*>& host_out);
   // Runs only the kernel sequence (inputs already resident); used for device-side timing.
   void enqueue_kernels(cudaStream_t stream);
+  // Device milliseconds per replay of the kernel sequence (after one warm replay), CUDA events on
+  // `stream`; whatever the input buffers hold (timing only).
+  double time_kernels(cudaStream_t stream, int iters);
   // Enqueues only the D2H copies of the device outputs (host_out[j] as in enqueue).
   void enqueue_outputs(cudaStream_t stream, const std::vector<void*>& host_out);
   // Checks and clears the device error word written by bounded waits.
@@ -110,6 +114,8 @@ class Plan {
   std::vector<bool> is_output_;
   std::map<std::pair<int, int>, DevTensor> conv_cache_;   // (value, 4 Cp + prec) -> NHWC operand copy
   std::map<std::pair<int, int>, DevTensor> rows_cache_;   // (value, prec) -> rows operand copy
+  std::map<int, DevTensor> concat_out_;                    // Concat output value -> its buffer, when
+                                                           // producers write their slices in place
 
   void build();
   void allocate_and_finalize();
@@ -128,6 +134,12 @@ class Plan {
   DevTensor as_rows_op(int v, int64_t M, int64_t K, int prec);
   DevTensor as_f32_contig(int v);
   DevTensor materialize(const DevTensor& src, bool bf16);
+  DevTensor concat_home(int v, int64_t Cout);
+  DevTensor s2d_input(int v);
+  void find_stem_pools();
+  void plan_stem_pool(const Op& conv, const Op& pool);
+  std::map<int, int> stem_pool_;      // stem conv op -> the MaxPool op it absorbs (fused kernel)
+  std::set<int> pooled_by_conv_;      // MaxPool ops done by a fused stem kernel
 
   void plan_conv(const Op& op);
   void plan_gemm(const Op& op);

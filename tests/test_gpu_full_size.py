@@ -49,6 +49,7 @@ def _check(case, rows, chunk, tol=BF16_TOL):
         scale = float(np.abs(r).max())
         per_row = np.abs(g.astype(np.float64) - r).reshape(len(rows), -1).max(1) / scale
         assert per_row.max() <= tol, f"{case.name} output {o}: row {rows[int(per_row.argmax())]} at {per_row.max():.3e}"
+    print(f"{case.name}: normwise error per output " + ", ".join(f"{e:.2e}" for e in errs) + f" (gate {tol:.0e})")
     return errs
 
 

@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 
 from helpers import assert_close, conv_case, run_backend, run_oracle
+from shorokoo_b200 import B200InferenceSessionFactory
 from shorokoo_b200.emit import graphs
 
 pytestmark = pytest.mark.gpu
@@ -113,6 +114,68 @@ def test_maxpool(n, c, h, w, k, stride, pads):
     ref = run_oracle(case)[0]
     assert got.shape == (n, c, ho, wo)
     assert_close(got, ref, what=f"maxpool {n}x{c}x{h}x{w} k{k}/s{stride} {pads}")
+
+
+def _stem_pool_case(n, h, w, seed=29, conv_output_too=False):
+    """ResNet stem: conv 7x7/2 pad 3 over 3 channels + per-channel affine + ReLU + MaxPool 3x3/2 pad 1."""
+    from shorokoo_b200.emit import onnx_writer as W
+    from shorokoo_b200.emit.graphs import Builder, ModelCase, kaiming_normal
+    rng = np.random.Generator(np.random.PCG64(seed))
+    x = rng.standard_normal((n, 3, h, w), dtype=np.float32)
+    B = Builder(seed + 1)
+    xi = B.graph_input(W.FLOAT, 4, x.shape)
+    wt = B.init(kaiming_normal(B.rng, (64, 3, 7, 7)), "w")
+    y = B.conv(xi, wt, None, 7, 2, pads=[3, 3, 3, 3])
+    sc = B.init((1 + 0.2 * B.rng.standard_normal((1, 64, 1, 1))).astype(np.float32), "s")
+    sh = B.init((0.2 * B.rng.standard_normal((1, 64, 1, 1))).astype(np.float32), "t")
+    y = B.unary("Relu", B.binary("Add", B.binary("Mul", y, sc), sh))
+    p = B.op("MaxPool", [y], ceil_mode=0, dilations=[1, 1], kernel_shape=[3, 3], pads=[1, 1, 1, 1], strides=[2, 2])
+    n_, c_, h_, w_ = B.shape[y]
+    B.shape[p] = (n_, c_, (h_ - 1) // 2 + 1, (w_ - 1) // 2 + 1)
+    # a 1x1 conv reads the pool, as ResNet's first bottleneck does (the pool output is then stored in
+    # the bf16 operand layout the fused kernel writes)
+    w2 = B.init(kaiming_normal(B.rng, (64, 64, 1, 1)), "w2")
+    z = B.conv(p, w2, None, 1, 1, pads=[0, 0, 0, 0])
+    B.outputs.append(W.ValueInfo(z))
+    if conv_output_too:
+        B.outputs.append(W.ValueInfo(y))
+    outs = [z, y] if conv_output_too else [z]
+    return ModelCase("stem_pool", B.model("stem_pool"), [(xi, x)], outs, 0)
+
+
+# The stem conv and its 3x3/2 max pool run as one kernel when the conv output rows are even, at most
+# 128 pixels wide and read only by the pool: each CTA computes a contiguous range of pool rows (with
+# the halo conv row at the start of its range), so batches whose ranges start mid-image (3 x 32 pool
+# rows over 148 CTAs: one each; 40 images: ranges across image boundaries) are covered. 230x230
+# (odd conv rows) and 320x288 (144-pixel rows) take the separate conv and pool kernels.
+@pytest.mark.parametrize("n,h,w,fused", [(2, 224, 224, True), (3, 64, 64, True), (5, 96, 128, True),
+                                         (40, 64, 64, True), (1, 256, 96, True), (2, 230, 230, False),
+                                         (1, 320, 288, False)])
+def test_stem_with_fused_max_pool(n, h, w, fused):
+    case = _stem_pool_case(n, h, w)
+    f = B200InferenceSessionFactory(num_devices=1)
+    sess = f.CreateSession(case.model)
+    feeds = {nm: f.CreateTensor(a) for nm, a in case.inputs}
+    kinds = [k for k, _ in sess.profile(feeds, iters=1)]
+    assert any("+maxpool3x3/2" in k for k in kinds) == fused, kinds
+    outs = sess.Run(feeds, case.output_names)
+    got = outs[0].numpy()
+    for o in outs:
+        o.Dispose()
+    sess.Dispose()
+    ref = run_oracle(case)[0]
+    assert got.shape == ref.shape
+    assert_close(got, ref, what=f"stem + max pool {n}x3x{h}x{w}")
+    # the bf16-operand arithmetic of the path: far tighter than the gate
+    assert_close(got, run_oracle(case, "bf16-operands")[0], tol=4e-3, what="stem + pool vs bf16-operand oracle")
+
+
+def test_stem_pool_not_fused_when_the_conv_output_is_also_read():
+    case = _stem_pool_case(2, 64, 64, conv_output_too=True)
+    got = run_backend(case)
+    ref = run_oracle(case)
+    for g, r in zip(got, ref):
+        assert_close(g, r, what="stem with its conv output as a graph output")
 
 
 def test_maxpool_and_gap():

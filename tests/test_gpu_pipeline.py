@@ -1,7 +1,8 @@
 """GPU test of the single-device micro-batch pipeline behind Run: large batch-separable inputs are
 cut into two small head chunks (an eighth of the batch each) and two body chunks whose host->device
 copies overlap the previous chunk's kernels and whose device->host output copies overlap the next
-chunks'. The pipelined Run
+chunks', when a model of that schedule (measured chunk kernel times and copy rate) beats running the
+batch in one piece. The pipelined Run
 must give the single full-batch plan's result up to summation order (the chunk plan may pick
 another tile width and with it another split of K across the MMA-issuing lanes, and a changed
 fp32 partial sum can flip the bf16 rounding of an intermediate activation), and the oracle's on a
@@ -54,14 +55,19 @@ def _run_child(tmp_path, case_expr):
     ("graphs.mlp(batch=16384, widths=(1024, 512, 256), seed=7, bias_scale=0.5)", "2048 + 2048 + 6144 + 6144",
      BF16_TOL),
     ("graphs.resnet(depth=18, batch=256, hw=(160, 160), seed=9)", "32 + 32 + 96 + 96", BF16_TOL),
-    # a detector whose per-anchor outputs (~200 MB) outweigh its input: pipelined below batch 32,
-    # the output copies overlapping later chunks through the output staging slots. Its chunks pick
-    # other tiles than the full batch (another summation order), within the bf16 gate.
-    ("graphs.retinanet(batch=16, hw=(384, 512), seed=5)", "2 + 2 + 4 + 4 + 4", BF16_TOL),
+    # a detector whose per-anchor outputs (~200 MB) outweigh its input: its 2- and 4-image chunk
+    # plans cost more than the copies they would hide (measured: 15.5 ms pipelined against 9.3 ms in
+    # one piece), so the measured schedule model keeps the single full-batch plan. (At 800x1024 the
+    # model pipelines it: tests/test_gpu_full_size.py.)
+    ("graphs.retinanet(batch=16, hw=(384, 512), seed=5)", None, BF16_TOL),
 ])
 def test_pipelined_run_matches_full_batch_plan(tmp_path, case_expr, schedule, tol):
     ref, got, log = _run_child(tmp_path, case_expr)
-    assert f"chunks of {schedule} rows" in log, log[-2000:]
+    assert "pipeline model:" in log, log[-2000:]
+    if schedule is None:
+        assert "chunks of" not in log, log[-2000:]
+    else:
+        assert f"chunks of {schedule} rows" in log, log[-2000:]
     assert got.shape == ref.shape
     assert_close(got, ref, tol=tol, what="pipelined run vs full-batch plan")
 

@@ -113,7 +113,9 @@ def test_lowering_retinanet_heads_are_views():
     k = kinds(lines)
     assert k["FusedConv"] == 107                             # (the backbone's four shortcuts merged)
     assert sum("residual=1" in l for l in lines) == 2        # FPN top-down adds with nearest-2x upsample
-    assert k["Concat"] == 2 and k["Sigmoid"] == 1
+    assert k["Concat"] == 2 and k["Sigmoid"] == 0
+    # the class Sigmoid after the concat is applied by the five class-logit convs' epilogues
+    assert sum(",720," in l.split("->")[1] and "act=2" in l for l in lines if l.startswith("FusedConv")) == 5
     assert [l for l in lines if l.startswith("output")] == ["output [1,3852,80] device", "output [1,3852,4] device"]
 
 
