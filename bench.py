@@ -273,11 +273,13 @@ def main():
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as fh:
-            traffic = json.load(fh).get(name)
+            traffic = json.load(fh).get(name) if not args.batch and args.precision == "bf16" else None
 
-    h2d = sum(a.nbytes for _, a in inputs)
+    wrapped = {n: f.WrapTensor(a) for n, a in inputs}   # the e2e path's inputs
+    h2d, d2h = sess.transfer_bytes(wrapped)
+    for v in wrapped.values():
+        v.Dispose()
     outs = sess.Run(feeds, case.output_names)
-    d2h = sum(int(np.prod(o.Shape)) * 4 for o in outs)
     gpu_head = [o.numpy()[:8] for o in outs]   # this rank's first rows, for the parity check
     for o in outs:
         o.Dispose()
@@ -298,14 +300,19 @@ def main():
             "e2e": {"value": total / e_max, "unit": "images/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world,
                     "timing": "host wall clock per step around WrapTensor of the pageable host batch (no copy, "
-                              "as CreateTensor<T> aliases a managed array) + Run (staging, H2D, kernels, D2H of "
-                              "the outputs into host memory) + release"},
+                              "as CreateTensor<T> aliases a managed array) + Run (staging through page-locked "
+                              "memory, the float32 input converted to bf16 there as the plan only reads it as "
+                              "bf16, H2D, kernels, D2H of the outputs into host memory) + release; byte counts "
+                              "are the copies Run makes"},
             "e2e_pinned_input": {"value": total / e2e[False], "unit": "images/s",
                                  "timing": "Run alone on an input already in library page-locked memory "
                                            "(CreateTensor outside the timed region)"},
             "gpu_launches": int(st["launches"]) * args.steps * world,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
                          "frac": achieved / peak_tflops, "traffic": traffic,
+                         "traffic_note": "DRAM bytes read + written per step by these launches, one ncu capture of "
+                                         "this workload (profiles/resnet50_bs512_dram_launch_list.md); algorithmic "
+                                         "minimum ~23.2e9" if traffic else None,
                          "kernel": f"conv_gemm_kernel (tcgen05 implicit GEMM), {tc_launches} launches/step, "
                                    f"{tc_ms:.3f} of {all_ms:.3f} ms per step timed per launch with CUDA events",
                          "peak_kind": peak_note},

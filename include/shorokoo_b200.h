@@ -96,6 +96,15 @@ SB_API const char* sb_session_output_name(const sb_session* session, int32_t ind
 SB_API int32_t sb_session_run(sb_session* session, int32_t n_inputs, const char* const* in_names,
                        sb_value* const* in_values, int32_t n_outputs, const char* const* out_names,
                        sb_value** out_values);
+/* Run for chained inference (no counterpart in the reference interface, whose Run returns host
+ * tensors): the same as sb_session_run except that the outputs stay in device memory of the
+ * session's first device, with no device->host copy. sb_value_data copies such a value to host
+ * memory on first use; passed as an input of a later run (of this or another session), it is copied
+ * device to device. Inputs that are device-resident are accepted by sb_session_run as well. Runs
+ * with device-resident inputs or outputs do not use the micro-batch pipeline. */
+SB_API int32_t sb_session_run_device(sb_session* session, int32_t n_inputs, const char* const* in_names,
+                              sb_value* const* in_values, int32_t n_outputs, const char* const* out_names,
+                              sb_value** out_values);
 
 /* ---- IShorokooInferenceSessionFactory.CreateTensor<T> / CreateTensorFromRawBytes
  * (IShorokooInferenceSessionFactory.cs:12-18; ORT: OrtSessionFactory.cs:44-91).
@@ -122,7 +131,12 @@ SB_API int32_t sb_value_type(const sb_value* value);      /* ValueType: SB_VALUE
 SB_API int32_t sb_value_elem_type(const sb_value* value); /* ElementType */
 SB_API int32_t sb_value_rank(const sb_value* value);
 SB_API const int64_t* sb_value_shape(const sb_value* value); /* Shape */
-SB_API void* sb_value_data(sb_value* value);               /* GetTensor(Mutable)DataAsSpan: host memory */
+SB_API void* sb_value_data(sb_value* value);               /* GetTensor(Mutable)DataAsSpan: host memory
+                                                            * (NULL and sb_last_error on a failed copy of
+                                                            * a device-resident value) */
+/* Device address of a device-resident value (an output of sb_session_run_device) and its device;
+ * NULL and -1 for host values. No counterpart in the reference interface. */
+SB_API int32_t sb_value_device_ptr(const sb_value* value, void** ptr, int32_t* device);
 SB_API size_t sb_value_nbytes(const sb_value* value);
 SB_API size_t sb_value_string_count(const sb_value* value);           /* GetStringTensorData */
 SB_API const char* sb_value_string_at(const sb_value* value, size_t index);
@@ -147,6 +161,11 @@ SB_API int32_t sb_session_profile(sb_session* session, int32_t n_inputs, const c
 SB_API int32_t sb_session_stats(sb_session* session, int32_t n_inputs, const char* const* in_names,
                          sb_value* const* in_values, int64_t* launches, int64_t* tc_launches, double* macs,
                          int64_t* device_bytes, int32_t* devices_used);
+
+/* Bytes a Run of these inputs copies host->device and device->host (a float32 input that the plan
+ * only reads as bfloat16 and that Run has to stage from pageable memory travels as bfloat16). */
+SB_API int32_t sb_session_transfer_bytes(sb_session* session, int32_t n_inputs, const char* const* in_names,
+                                  sb_value* const* in_values, int64_t* h2d_bytes, int64_t* d2h_bytes);
 
 /* ---- Allocation-free dense layer (no counterpart in the reference interface) -------------------
  * y[M,N] = x[M,K] * w[N,K]^T + bias[N] (ReLU when relu != 0): fp32 device buffers in and out, bf16

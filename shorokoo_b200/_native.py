@@ -30,6 +30,8 @@ SIGNATURES = {
     "sb_session_output_count": (I32, [P]),
     "sb_session_output_name": (CSTR, [P, I32]),
     "sb_session_run": (I32, [P, I32, PSTR, PP, I32, PSTR, PP]),
+    "sb_session_run_device": (I32, [P, I32, PSTR, PP, I32, PSTR, PP]),
+    "sb_value_device_ptr": (I32, [P, PP, C.POINTER(I32)]),
     "sb_value_create_tensor": (I32, [I32, C.POINTER(I64), I32, P, SZ, PP]),
     "sb_value_wrap_tensor": (I32, [I32, C.POINTER(I64), I32, P, SZ, PP]),
     "sb_value_create_string_tensor": (I32, [PSTR, SZ, C.POINTER(I64), I32, PP]),
@@ -51,6 +53,7 @@ SIGNATURES = {
     "sb_session_stats": (I32, [P, I32, PSTR, PP, C.POINTER(I64), C.POINTER(I64), C.POINTER(DBL),
                                C.POINTER(I64), C.POINTER(I32)]),
     "sb_debug_lower": (I32, [C.c_char_p, SZ, I32, PP, C.c_char_p, SZ, C.POINTER(SZ)]),
+    "sb_session_transfer_bytes": (I32, [P, I32, PSTR, PP, C.POINTER(I64), C.POINTER(I64)]),
     "sb_linear_noalloc": (I32, [P, P, P, P, I64, I64, I64, I32, P]),
 }
 

@@ -142,7 +142,10 @@ class B200TensorValue:
         shape = self.Shape
         if n == 0:
             return np.zeros(shape, dt)
-        buf = (C.c_uint8 * n).from_address(L.sb_value_data(self._h))
+        addr = L.sb_value_data(self._h)
+        if not addr:
+            raise B200InvalidOperationError(L.sb_last_error().decode())
+        buf = (C.c_uint8 * n).from_address(addr)
         a = np.frombuffer(buf, dtype=dt).reshape(shape)
         if not writable:
             a.flags.writeable = False
@@ -174,6 +177,13 @@ class B200TensorValue:
         if self._h:
             _native.lib().sb_value_release(self._h)
             self._h = C.c_void_p()
+
+    @property
+    def DevicePointer(self):
+        """(device address, device) of a device-resident value, (None, -1) for host values."""
+        p, d = C.c_void_p(), C.c_int32()
+        _check(_native.lib().sb_value_device_ptr(self._h, C.byref(p), C.byref(d)))
+        return p.value, d.value
 
     # -- conveniences -----------------------------------------------------------------------
     def numpy(self) -> np.ndarray:
@@ -226,6 +236,19 @@ class B200InferenceSession:
         _check(_native.lib().sb_session_run(self._h, n, carr, varr, m, onames, ovals))
         return [B200TensorValue(ovals[i]) for i in range(m)]
 
+    def RunOnDevice(self, inputs: Mapping[str, B200TensorValue], outputNames: Optional[Sequence[str]] = None
+                    ) -> List[B200TensorValue]:
+        """Run whose outputs stay in device memory (sb_session_run_device): for chaining into another
+        Run without host copies; reading a value's data copies it to the host on first use. No
+        counterpart in the reference interface."""
+        outs = list(outputNames) if outputNames is not None else self.OutputNames
+        n, carr, varr = self._marshal_inputs(inputs)
+        m = len(outs)
+        onames = (C.c_char_p * max(m, 1))(*[s.encode() for s in outs])
+        ovals = (C.c_void_p * max(m, 1))()
+        _check(_native.lib().sb_session_run_device(self._h, n, carr, varr, m, onames, ovals))
+        return [B200TensorValue(ovals[i]) for i in range(m)]
+
     # -- measurement (no counterpart in the reference interface) --------------------------------
     def time_device(self, inputs: Mapping[str, B200TensorValue], warmup: int = 3, iters: int = 10) -> List[float]:
         n, carr, varr = self._marshal_inputs(inputs)
@@ -252,6 +275,13 @@ class B200InferenceSession:
                                               C.byref(db), C.byref(dev)))
         return {"launches": la.value, "tc_launches": tc.value, "macs": macs.value, "device_bytes": db.value,
                 "devices": dev.value}
+
+    def transfer_bytes(self, inputs: Mapping[str, B200TensorValue]):
+        """(host->device, device->host) bytes a Run of these inputs copies."""
+        n, carr, varr = self._marshal_inputs(inputs)
+        h, d = C.c_int64(), C.c_int64()
+        _check(_native.lib().sb_session_transfer_bytes(self._h, n, carr, varr, C.byref(h), C.byref(d)))
+        return h.value, d.value
 
     def Dispose(self) -> None:
         if self._h:

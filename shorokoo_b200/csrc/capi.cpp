@@ -220,8 +220,8 @@ const char* sb_session_output_name(const sb_session* s, int32_t i) {
   return s->s->output_names()[size_t(i)].c_str();
 }
 
-int32_t sb_session_run(sb_session* s, int32_t n_in, const char* const* in_names, sb_value* const* in_values,
-                       int32_t n_out, const char* const* out_names, sb_value** out_values) {
+static int32_t run_impl(sb_session* s, int32_t n_in, const char* const* in_names, sb_value* const* in_values,
+                        int32_t n_out, const char* const* out_names, sb_value** out_values, bool keep_on_device) {
   return guarded([&] {
     SB_CHECK(s != nullptr, sb::SB_INVALID_ARGUMENT, "session is null");
     SB_CHECK(n_out >= 0 && (n_out == 0 || (out_names && out_values)), sb::SB_INVALID_ARGUMENT, "null output arrays");
@@ -236,8 +236,27 @@ int32_t sb_session_run(sb_session* s, int32_t n_in, const char* const* in_names,
       SB_CHECK(k < onames.size(), sb::SB_INVALID_ARGUMENT, std::string("unknown output '") + out_names[j] + "'");
       idx.push_back(int(k));
     }
-    auto outs = s->s->run(ins, idx);
+    auto outs = s->s->run(ins, idx, keep_on_device);
     for (int32_t j = 0; j < n_out; ++j) out_values[j] = new sb_value{outs[size_t(j)]};
+    return SB_STATUS_OK;
+  });
+}
+
+int32_t sb_session_run(sb_session* s, int32_t n_in, const char* const* in_names, sb_value* const* in_values,
+                       int32_t n_out, const char* const* out_names, sb_value** out_values) {
+  return run_impl(s, n_in, in_names, in_values, n_out, out_names, out_values, false);
+}
+
+int32_t sb_session_run_device(sb_session* s, int32_t n_in, const char* const* in_names, sb_value* const* in_values,
+                              int32_t n_out, const char* const* out_names, sb_value** out_values) {
+  return run_impl(s, n_in, in_names, in_values, n_out, out_names, out_values, true);
+}
+
+int32_t sb_value_device_ptr(const sb_value* v, void** ptr, int32_t* device) {
+  return guarded([&] {
+    SB_CHECK(v && ptr && device, sb::SB_INVALID_ARGUMENT, "null argument");
+    *ptr = v->v->dev;
+    *device = v->v->dev ? v->v->dev_id : -1;
     return SB_STATUS_OK;
   });
 }
@@ -327,7 +346,15 @@ int32_t sb_value_type(const sb_value* v) { return v ? v->v->kind : 0; }
 int32_t sb_value_elem_type(const sb_value* v) { return v ? v->v->elem_type : 0; }
 int32_t sb_value_rank(const sb_value* v) { return v ? int32_t(v->v->shape.size()) : 0; }
 const int64_t* sb_value_shape(const sb_value* v) { return v ? v->v->shape.data() : nullptr; }
-void* sb_value_data(sb_value* v) { return v ? v->v->data : nullptr; }
+void* sb_value_data(sb_value* v) {
+  if (!v) return nullptr;
+  try {
+    return v->v->host_data();   // (a device-resident value is copied to the host on first use)
+  } catch (const std::exception& e) {
+    sb::set_thread_error(e.what());
+    return nullptr;
+  }
+}
 size_t sb_value_nbytes(const sb_value* v) { return v ? v->v->nbytes : 0; }
 size_t sb_value_string_count(const sb_value* v) { return v ? v->v->strings.size() : 0; }
 const char* sb_value_string_at(const sb_value* v, size_t i) {
@@ -386,6 +413,18 @@ int32_t sb_session_stats(sb_session* s, int32_t n_in, const char* const* in_name
     if (macs) *macs = st.macs;
     if (dev_bytes) *dev_bytes = int64_t(st.arena_bytes + st.weight_bytes);
     if (devices) *devices = s->s->devices_used(ins);
+    return SB_STATUS_OK;
+  });
+}
+
+int32_t sb_session_transfer_bytes(sb_session* s, int32_t n_in, const char* const* in_names, sb_value* const* in_values,
+                                  int64_t* h2d, int64_t* d2h) {
+  return guarded([&] {
+    SB_CHECK(s != nullptr && h2d && d2h, sb::SB_INVALID_ARGUMENT, "null argument");
+    auto ins = ordered_inputs(*s->s, n_in, in_names, in_values);
+    auto r = s->s->transfer_bytes(ins);
+    *h2d = r.first;
+    *d2h = r.second;
     return SB_STATUS_OK;
   });
 }

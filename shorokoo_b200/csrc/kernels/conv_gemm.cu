@@ -1090,8 +1090,8 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* accf = empty + kMaxStages;
   uint64_t* acce = accf + 2;
   uint64_t* bfull = acce + 2;
-  uint64_t* ring_full = bfull + 1;   // the 8 epilogue warps wrote the tile's row into the ring
-  uint64_t* pool_done = ring_full + 1;   // the 8 epilogue warps finished reading the ring for the tile
+  uint64_t* ring_full = bfull + 1;   // the 8 epilogue warps wrote a pool row's conv rows into the ring
+  uint64_t* pool_done = ring_full + 1;   // the 8 epilogue warps finished computing that pool row
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(pool_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1196,6 +1196,7 @@ __global__ void __launch_bounds__(512, 1)
     const int px = q * 32 + lane;
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
     int it = 0;
+    int pc = 0;   // pool rows this CTA has completed
     stem_rows(a, blockIdx.x, gridDim.x, [&](int n, int r, bool pool) {
       const int acc = it & 1;
       const uint32_t aph = uint32_t(it >> 1) & 1u;
@@ -1206,8 +1207,10 @@ __global__ void __launch_bounds__(512, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce[acc]);
-      // the previous tile's pool reads of the ring are done before its slot r % 3 is overwritten
-      if (it > 0 && !mbar_wait(pool_done, uint32_t(it - 1) & 1u, abort_flag, a.err, 16u)) return false;
+      // Ring slot r % 3 held row r - 3, last read by the previous pool row: an even row waits until
+      // every warp has finished that pool row (the odd row after it then reuses a slot that the same
+      // pool row was the last to read; the range's halo row follows no pool row).
+      if (!(r & 1) && pc > 0 && !mbar_wait(pool_done, uint32_t(pc - 1) & 1u, abort_flag, a.err, 16u)) return false;
       if (px < a.Wo) {
         uint8_t* row = ring + (r % 3) * kStemRingRow;
 #pragma unroll
@@ -1230,10 +1233,13 @@ __global__ void __launch_bounds__(512, 1)
           *reinterpret_cast<uint4*>(row + ring_off(px, hsel * 4 + j)) = qv;
         }
       }
+      ++it;
+      if (!pool) return true;
+      // all warps have written the pool row's conv rows r - 2 .. r
       __syncwarp();
       if (lane == 0) mbar_arrive(ring_full);
-      if (!mbar_wait(ring_full, uint32_t(it) & 1u, abort_flag, a.err, 32u)) return false;
-      if (pool) {   // pool row po = r / 2 from conv rows r - 2 (padding when po = 0), r - 1, r
+      if (!mbar_wait(ring_full, uint32_t(pc) & 1u, abort_flag, a.err, 32u)) return false;
+      {   // pool row po = r / 2 from conv rows r - 2 (padding when po = 0), r - 1, r
         const int po = r >> 1;
         const uint8_t* rows[3] = {po > 0 ? ring + ((r + 1) % 3) * kStemRingRow : nullptr,
                                   ring + ((r + 2) % 3) * kStemRingRow, ring + (r % 3) * kStemRingRow};
@@ -1256,7 +1262,7 @@ __global__ void __launch_bounds__(512, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(pool_done);
-      ++it;
+      ++pc;
       return true;
     });
   }
@@ -1638,12 +1644,16 @@ void stem_pool_prepare(StemPoolPlan& p, const void* w, int num_sms) {
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed for the stem input");
   if (!encode_2d(&p.tmB, w, uint64_t(kStemKT) * BK, 64, uint64_t(kStemKT) * BK * 2, BK, 64))
     throw std::runtime_error("cuTensorMapEncodeTiled failed for the stem weights");
-  // two MMA issuers and two producers; stages a multiple of both
+  // two MMA issuers (one: 621 us at ResNet-50 bs512, two: 494, four: 494-499); the producer count
+  // (one to four) made no difference
   a.mma_lanes = 2;
   a.producers = 2;
   const int fixed = int(kStemKT * kStemBBytes + 3 * kStemRingRow) + 256 + 1024 + 512;
   int stages = std::min(kMaxStages, (kSmemLimit - fixed) / int(kStemAStage));
-  stages -= stages % 2;
+  {
+    const int l = std::max(a.mma_lanes, a.producers);   // (both powers of two up to 4)
+    stages -= stages % l;
+  }
   if (stages < 2) throw std::runtime_error("stem_pool: shared-memory plan leaves fewer than 2 stages");
   a.stages = stages;
   p.smem = stages * int(kStemAStage) + fixed;

@@ -164,6 +164,10 @@ cudaError_t global_pool_nhwc(const void* x, int x_bf16, int N, int HW, int C, in
 cudaError_t strided_copy(const void* src, int src_bf16, const TDesc& sd, void* dst, int dst_bf16, const TDesc& dd,
                          cudaStream_t s);
 cudaError_t fill_f32(void* dst, int64_t n, float v, cudaStream_t s);
+// dst f32 [n] <- src IEEE half [n] (16-byte aligned buffers: 8 halves per thread and step).
+cudaError_t f16_to_f32(const void* src, void* dst, int64_t n, cudaStream_t s);
+// dst f32 [n] <- src bfloat16 [n] (exact widening; 16-byte aligned buffers).
+cudaError_t bf16_to_f32(const void* src, void* dst, int64_t n, cudaStream_t s);
 // Elementwise: y (f32 contiguous over out shape) = f(a [, b]) with broadcasting strides.
 enum EwOp : int {
   EW_ADD = 0, EW_SUB, EW_MUL, EW_DIV, EW_POW, EW_MAX, EW_MIN,

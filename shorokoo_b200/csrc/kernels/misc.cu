@@ -2,6 +2,7 @@
 // elementwise / copy / softmax / reduce / gather. Coalesced along the innermost dimension and
 // 128-bit vectorised where the layout allows; grids are sized in multiples of the SM count.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <cmath>
 
@@ -466,6 +467,35 @@ __global__ void strided_copy_kernel(const void* __restrict__ src, int src_bf16, 
     st_any(dst, dst_bf16, offset_of(i, dd), ld_any(src, src_bf16, offset_of(i, sd)));
 }
 
+__global__ void f16_to_f32_kernel(const uint4* __restrict__ src, float4* __restrict__ dst, int64_t n8,
+                                  const __half* __restrict__ tail_src, float* __restrict__ tail_dst, int tail) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
+    const uint4 q = __ldg(src + i);
+    const __half2* h = reinterpret_cast<const __half2*>(&q);
+    const float2 a = __half22float2(h[0]), b = __half22float2(h[1]), c = __half22float2(h[2]), d = __half22float2(h[3]);
+    dst[2 * i] = make_float4(a.x, a.y, b.x, b.y);
+    dst[2 * i + 1] = make_float4(c.x, c.y, d.x, d.y);
+  }
+  if (blockIdx.x == 0 && int(threadIdx.x) < tail) tail_dst[threadIdx.x] = __half2float(tail_src[threadIdx.x]);
+}
+
+__global__ void bf16_to_f32_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int64_t n8,
+                                   const uint16_t* __restrict__ tail_src, uint32_t* __restrict__ tail_dst, int tail) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
+    const uint4 q = __ldg(src + i);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    uint32_t f[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {   // bfloat16 bits are the high half of the float32 bits
+      f[2 * j] = w[j] << 16;
+      f[2 * j + 1] = w[j] & 0xFFFF0000u;
+    }
+    dst[2 * i] = make_uint4(f[0], f[1], f[2], f[3]);
+    dst[2 * i + 1] = make_uint4(f[4], f[5], f[6], f[7]);
+  }
+  if (blockIdx.x == 0 && int(threadIdx.x) < tail) tail_dst[threadIdx.x] = uint32_t(tail_src[threadIdx.x]) << 16;
+}
+
 __global__ void fill_kernel(float* dst, int64_t n, float v) {
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
     dst[i] = v;
@@ -814,6 +844,26 @@ cudaError_t strided_copy(const void* src, int src_bf16, const TDesc& sd, void* d
   if (launch_vec4(-1, src, src_bf16, sd, nullptr, 0, TDesc{}, dst, dst_bf16, dd, 0.f, 0.f, s))
     return cudaGetLastError();
   strided_copy_kernel<<<grid_for(total), kThreads, 0, s>>>(src, src_bf16, sd, dst, dst_bf16, dd, total);
+  return cudaGetLastError();
+}
+
+cudaError_t f16_to_f32(const void* src, void* dst, int64_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  const int64_t n8 = n / 8;
+  const int tail = int(n - n8 * 8);
+  f16_to_f32_kernel<<<grid_for(std::max<int64_t>(n8, 1)), kThreads, 0, s>>>(
+      reinterpret_cast<const uint4*>(src), reinterpret_cast<float4*>(dst), n8,
+      reinterpret_cast<const __half*>(src) + n8 * 8, reinterpret_cast<float*>(dst) + n8 * 8, tail);
+  return cudaGetLastError();
+}
+
+cudaError_t bf16_to_f32(const void* src, void* dst, int64_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  const int64_t n8 = n / 8;
+  const int tail = int(n - n8 * 8);
+  bf16_to_f32_kernel<<<grid_for(std::max<int64_t>(n8, 1)), kThreads, 0, s>>>(
+      reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), n8,
+      reinterpret_cast<const uint16_t*>(src) + n8 * 8, reinterpret_cast<uint32_t*>(dst) + n8 * 8, tail);
   return cudaGetLastError();
 }
 

@@ -73,9 +73,11 @@ class Lowerer {
         v.shape = s.shape;
         v.input_index = int(k);
         v.name = vi.name;
-        SB_CHECK(s.dtype == DT_FLOAT, SB_UNSUPPORTED,
+        // device inputs: float32, or the 16-bit float types a caller creates with CreateTensor<BFloat16 /
+        // Float16> (OrtSessionFactory.cs:46-55), which reach float math through a Cast to float32
+        SB_CHECK(s.dtype == DT_FLOAT || s.dtype == DT_BFLOAT16 || s.dtype == DT_FLOAT16, SB_UNSUPPORTED,
                  std::string("graph input '") + vi.name + "' of type " + dtype_name(s.dtype) +
-                     " must be small enough to be a plan-time value; device inputs are float32");
+                     " must be small enough to be a plan-time value; device inputs are float32, bfloat16 or float16");
         id = g_.add_value(std::move(v));
       }
       root.map[vi.name] = id;
@@ -313,8 +315,8 @@ class Lowerer {
     };
     for (int id : in)
       if (id >= 0 && !V(id).is_host)
-        SB_CHECK(V(id).dtype == DT_FLOAT, SB_UNSUPPORTED,
-                 t + ": device tensors of type " + dtype_name(V(id).dtype) + " are not supported");
+        SB_CHECK(V(id).dtype == DT_FLOAT || (t == "Cast" && (V(id).dtype == DT_BFLOAT16 || V(id).dtype == DT_FLOAT16)),
+                 SB_UNSUPPORTED, t + ": device tensors of type " + dtype_name(V(id).dtype) + " are not supported");
     std::vector<std::vector<int64_t>> oshapes;
 
     if (t == "Conv") {

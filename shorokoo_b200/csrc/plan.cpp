@@ -1240,14 +1240,30 @@ void Plan::build() {
     }
   }
 
-  // graph inputs: f32 contiguous buffers filled by H2D
+  // graph inputs: contiguous buffers filled by H2D in the caller's element type. bfloat16 inputs are
+  // read as they are by every kernel (half the transfer of float32); float16 ones are widened to
+  // float32 on the device first.
   for (size_t k = 0; k < g_.inputs.size(); ++k) {
     const Value& v = g_.vals[size_t(g_.inputs[k])];
     if (v.is_host) continue;
-    DevTensor t = alloc_contig(v.shape, false);
-    bufs_[size_t(t.buf)].first = -1;
+    DevTensor t = alloc_contig(v.shape, v.dtype == DT_BFLOAT16);
+    if (v.dtype == DT_FLOAT16) {
+      DevTensor h = alloc_contig(v.shape, true);   // raw 16-bit storage of the transfer
+      bufs_[size_t(h.buf)].first = -1;
+      inputs_.push_back({int(k), h.buf, size_t(numel(v.shape)) * 2});
+      const int64_t n = numel(v.shape);
+      add_step("f16_to_f32", {h}, {t}, [this, h, t, n]() {
+        const void* sp = ptr(h);
+        void* dp = ptr(t);
+        return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) { return k::f16_to_f32(sp, dp, n, s); });
+      });
+    } else {
+      bufs_[size_t(t.buf)].first = -1;
+      InputBinding ib{int(k), t.buf, size_t(numel(v.shape)) * dtype_size(v.dtype)};
+      ib.bf16_ok = v.dtype == DT_FLOAT && storage_class(g_.inputs[k], kStoreF32) == kStoreBf16;
+      inputs_.push_back(ib);
+    }
     vt_[size_t(g_.inputs[k])] = t;
-    inputs_.push_back({int(k), t.buf, size_t(numel(v.shape)) * 4});
   }
 
   find_stem_pools();
@@ -1405,7 +1421,8 @@ double Plan::time_kernels(cudaStream_t stream, int iters) {
 void Plan::enqueue(cudaStream_t stream, const std::vector<const void*>& host_in, const std::vector<void*>& host_out) {
   for (auto& ib : inputs_) {
     SB_CHECK(size_t(ib.index) < host_in.size() && host_in[size_t(ib.index)], SB_INVALID_ARGUMENT, "missing input data");
-    ck(cudaMemcpyAsync(buffer_ptr(ib.buf), host_in[size_t(ib.index)], ib.bytes, cudaMemcpyHostToDevice, stream), "H2D");
+    // (host or device-resident source: the runtime picks the direction)
+    ck(cudaMemcpyAsync(buffer_ptr(ib.buf), host_in[size_t(ib.index)], ib.bytes, cudaMemcpyDefault, stream), "H2D");
   }
   enqueue_kernels(stream);
   enqueue_outputs(stream, host_out);
@@ -1415,7 +1432,7 @@ void Plan::enqueue_outputs(cudaStream_t stream, const std::vector<void*>& host_o
   for (size_t j = 0; j < outputs_.size(); ++j) {
     const OutputBinding& ob = outputs_[j];
     if (ob.host || j >= host_out.size() || !host_out[j]) continue;
-    ck(cudaMemcpyAsync(host_out[j], ptr(ob.dev), size_t(numel(ob.shape)) * 4, cudaMemcpyDeviceToHost, stream), "D2H");
+    ck(cudaMemcpyAsync(host_out[j], ptr(ob.dev), size_t(numel(ob.shape)) * 4, cudaMemcpyDefault, stream), "D2H");
   }
 }
 

@@ -38,6 +38,8 @@ struct InputBinding {
   int index;               // session input index
   int buf;                 // arena buffer receiving the H2D copy
   size_t bytes;
+  bool bf16_ok = false;    // float32 input whose every reader rounds it to bfloat16 first: its values
+                           // may arrive as bfloat16 (exact after widening back)
 };
 
 struct OutputBinding {

@@ -4,6 +4,7 @@
 #include "session.h"
 
 #include <algorithm>
+#include <chrono>
 #include <cstdlib>
 #include <cstring>
 #include <functional>
@@ -99,13 +100,13 @@ HostPool& pool() {
   return *p;
 }
 
-// Parallel memcpy for large host copies: one piece of at least 4 MiB per thread, up to 8 threads
-// (measured on the B200 host, 308 MB into page-locked memory: 14 GB/s with one thread, 75 GB/s
-// with 8, 48 GB/s with 16).
+// Parallel memcpy for large host copies: one piece of at least 4 MiB per thread, up to 16 threads
+// (one thread copies at ~14 GB/s on the B200 host; the staging copies of a pipelined Run, running
+// beside host->device transfers, measured 34 GB/s with 8 threads and 45 GB/s with 16).
 void par_memcpy(void* dst, const void* src, size_t n) {
   const size_t piece = size_t(4) << 20;
   const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-  const unsigned nt = unsigned(std::min<size_t>(std::min(8u, hw), n / piece));
+  const unsigned nt = unsigned(std::min<size_t>(std::min(16u, hw), n / piece));
   if (nt <= 1) {
     std::memcpy(dst, src, n);
     return;
@@ -118,6 +119,35 @@ void par_memcpy(void* dst, const void* src, size_t n) {
     th.emplace_back([=] { std::memcpy(static_cast<uint8_t*>(dst) + b, static_cast<const uint8_t*>(src) + b, e - b); });
   }
   std::memcpy(dst, src, std::min(n, per));
+  for (auto& t : th) t.join();
+}
+
+// float32 -> bfloat16 (round to nearest even; NaN stays NaN), n elements (vectorised by the compiler
+// at this optimisation level).
+__attribute__((optimize("O3"))) void f32_to_bf16_span(uint16_t* __restrict__ dst, const float* __restrict__ src,
+                                                       size_t n) {
+  for (size_t i = 0; i < n; ++i) {
+    uint32_t u;
+    std::memcpy(&u, src + i, 4);
+    const bool nan = (u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu);
+    const uint32_t r = u + 0x7FFFu + ((u >> 16) & 1u);
+    dst[i] = uint16_t(nan ? (u >> 16) | 0x40u : r >> 16);
+  }
+}
+
+// The same over up to 16 threads (pieces of at least 1 Mi elements).
+void par_f32_to_bf16(uint16_t* dst, const float* src, size_t n) {
+  const size_t piece = size_t(1) << 20;
+  const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+  const unsigned nt = unsigned(std::max<size_t>(1, std::min<size_t>(std::min(16u, hw), n / piece)));
+  const size_t per = (n / nt + 63) / 64 * 64;
+  std::vector<std::thread> th;
+  for (unsigned i = 1; i < nt; ++i) {
+    const size_t b = i * per, e = std::min(n, b + per);
+    if (b >= e) break;
+    th.emplace_back([=] { f32_to_bf16_span(dst + b, src + b, e - b); });
+  }
+  f32_to_bf16_span(dst, src, std::min(n, per));
   for (auto& t : th) t.join();
 }
 
@@ -138,6 +168,31 @@ bool host_is_page_locked(const void* p) {
 
 HostValue::~HostValue() {
   if (owned && data) pool().release(data, nbytes, pinned);
+  if (dev) {
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(dev_id);
+    cudaFree(dev);
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+}
+
+void* HostValue::host_data() {
+  if (!dev || data || !nbytes) return data;
+  std::lock_guard<std::mutex> l(host_mu);
+  if (!data) {
+    bool pin = false;
+    void* h = pool().alloc(nbytes, pin);
+    cudaError_t e = cudaMemcpy(h, dev, nbytes, cudaMemcpyDefault);
+    if (e != cudaSuccess) {
+      pool().release(h, nbytes, pin);
+      fail(SB_CUDA_ERROR, std::string("copy of a device-resident value to the host: ") + cudaGetErrorString(e));
+    }
+    pinned = pin;
+    owned = true;
+    data = h;
+  }
+  return data;
 }
 
 std::shared_ptr<HostValue> HostValue::alloc_tensor(int32_t elem_type, const std::vector<int64_t>& shape, bool pin) {
@@ -322,7 +377,7 @@ std::vector<InputSpec> Session::specs_for(const std::vector<std::shared_ptr<Host
     s.shape = v.shape;
     if (numel(v.shape) <= kPlanTimeInputMaxElems) {
       auto h = std::make_shared<HostTensor>(v.elem_type, v.shape);
-      if (v.nbytes) std::memcpy(h->mutable_data(), v.data, v.nbytes);
+      if (v.nbytes) std::memcpy(h->mutable_data(), const_cast<HostValue&>(v).host_data(), v.nbytes);
       s.value = h;
     } else if (shard) {
       s.shape[0] = cnt;
@@ -351,7 +406,7 @@ std::shared_ptr<Session::PlanSet> Session::get_plans(const std::vector<std::shar
                    ", got " + shape_str(v.shape));
     key += std::to_string(v.elem_type) + shape_str(v.shape);
     if (numel(v.shape) <= kPlanTimeInputMaxElems)
-      key += "=" + std::string(static_cast<const char*>(v.data), v.nbytes);
+      key += "=" + std::string(static_cast<const char*>(const_cast<HostValue&>(v).host_data()), v.nbytes);
     key += ";";
   }
   auto it = cache_.find(key);
@@ -608,6 +663,9 @@ void Session::run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostV
   Pipeline& P = *ps.pipe;
   ck(cudaSetDevice(P.device), "cudaSetDevice");
   cudaStream_t cs = streams_[0];
+  using clk = std::chrono::steady_clock;
+  const auto t_run = clk::now();
+  double ms_copy = 0, ms_wait = 0;   // host time in staging copies / waiting for staging slots
   std::vector<void*> hout(outs.size(), nullptr);
   int64_t r0 = 0;   // first batch row of the chunk
   for (size_t c = 0; c < P.rows.size(); r0 += P.rows[c], ++c) {
@@ -616,13 +674,22 @@ void Session::run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostV
     const int slot = int(c & 1);
     if (c >= 2) ck(cudaStreamWaitEvent(P.copy, P.consumed[slot], 0), "stream wait");
     bool host_slot_free = c < 2;
+    std::vector<bool> narrowed(binds.size(), false);
     for (size_t bi = 0; bi < binds.size(); ++bi) {
       const HostValue& v = *inputs[size_t(binds[bi].index)];
       const size_t row = v.nbytes / size_t(std::max<int64_t>(v.shape[0], 1));
       const uint8_t* src = static_cast<const uint8_t*>(v.data) + size_t(r0) * row;
+      // A float32 input read only as bfloat16 by the plan travels as bfloat16 when it has to be staged
+      // anyway (half the transfer; widened back on the device, where the plan rounds it to bfloat16
+      // again: the same values).
+      const bool narrow = !v.pinned && binds[bi].bf16_ok && v.elem_type == DT_FLOAT;
+      narrowed[bi] = narrow;
+      const size_t xfer = narrow ? binds[bi].bytes / 2 : binds[bi].bytes;
       if (!v.pinned) {   // borrowed pageable memory: through page-locked host slot `slot`
         if (!host_slot_free) {   // chunk c - 2's transfer out of this slot has finished
+          const auto t0 = clk::now();
           ck(cudaEventSynchronize(P.h2d_done[slot]), "event synchronize");
+          ms_wait += std::chrono::duration<double, std::milli>(clk::now() - t0).count();
           host_slot_free = true;
         }
         if (P.host_staging_bytes.size() < binds.size()) P.host_staging_bytes.assign(binds.size(), 0);
@@ -633,17 +700,28 @@ void Session::run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostV
           ck(cudaHostAlloc(&P.host_staging[slot][bi], most, cudaHostAllocPortable), "cudaHostAlloc (input staging)");
           P.host_staging_bytes[bi] = most;
         }
-        par_memcpy(P.host_staging[slot][bi], src, binds[bi].bytes);
+        const auto t0 = clk::now();
+        if (narrow)
+          par_f32_to_bf16(static_cast<uint16_t*>(P.host_staging[slot][bi]), reinterpret_cast<const float*>(src),
+                          binds[bi].bytes / 4);
+        else
+          par_memcpy(P.host_staging[slot][bi], src, binds[bi].bytes);
+        ms_copy += std::chrono::duration<double, std::milli>(clk::now() - t0).count();
         src = static_cast<const uint8_t*>(P.host_staging[slot][bi]);
       }
-      ck(cudaMemcpyAsync(P.staging[slot][bi], src, binds[bi].bytes, cudaMemcpyHostToDevice, P.copy), "H2D");
+      ck(cudaMemcpyAsync(P.staging[slot][bi], src, xfer, cudaMemcpyHostToDevice, P.copy), "H2D");
     }
     ck(cudaEventRecord(P.h2d_done[slot], P.copy), "event record");
     ck(cudaStreamWaitEvent(cs, P.h2d_done[slot], 0), "stream wait");
-    for (size_t bi = 0; bi < binds.size(); ++bi)
-      ck(cudaMemcpyAsync(plan.buffer_ptr(binds[bi].buf), P.staging[slot][bi], binds[bi].bytes,
-                         cudaMemcpyDeviceToDevice, cs),
-         "D2D");
+    for (size_t bi = 0; bi < binds.size(); ++bi) {
+      if (narrowed[bi])
+        ck(k::bf16_to_f32(P.staging[slot][bi], plan.buffer_ptr(binds[bi].buf), int64_t(binds[bi].bytes / 4), cs),
+           "bf16 widening");
+      else
+        ck(cudaMemcpyAsync(plan.buffer_ptr(binds[bi].buf), P.staging[slot][bi], binds[bi].bytes,
+                           cudaMemcpyDeviceToDevice, cs),
+           "D2D");
+    }
     ck(cudaEventRecord(P.consumed[slot], cs), "event record");
     plan.enqueue_kernels(cs);
     // outputs: into output slot `slot` on the compute stream (once its previous host copy is done),
@@ -668,22 +746,108 @@ void Session::run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostV
            "D2H");
     ck(cudaEventRecord(P.out_free[slot], P.d2h), "event record");
   }
+  const double ms_enqueued = std::chrono::duration<double, std::milli>(clk::now() - t_run).count();
   ck(cudaStreamSynchronize(cs), "stream synchronize");
   ck(cudaStreamSynchronize(P.copy), "stream synchronize");
   ck(cudaStreamSynchronize(P.d2h), "stream synchronize");
+  if (debug_level() >= 2)
+    std::fprintf(stderr, "[shorokoo_b200] pipelined run: %.3f ms (all enqueued at %.3f ms; host staging copies %.3f ms, "
+                 "waits for staging slots %.3f ms)\n",
+                 std::chrono::duration<double, std::milli>(clk::now() - t_run).count(), ms_enqueued, ms_copy, ms_wait);
   for (size_t c = 0; c < P.plans.size(); ++c)
     if (c == 0 || P.plans[c] != P.plans[c - 1]) P.plans[c]->check_device_error();
 }
 
+// Runs every shard's plan on its device (one host thread per device when sharded): copies of the
+// inputs in, the kernels, copies of the outputs out; input and output pointers may be host memory or
+// device memory (cudaMemcpyDefault picks the direction).
+void Session::run_shards(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs,
+                         const std::vector<std::shared_ptr<HostValue>>& outs) {
+  const size_t nout = ps.out_shapes.size();
+  std::vector<std::string> errs(ps.shards.size());
+  std::vector<int32_t> codes(ps.shards.size(), 0);
+  auto work = [&](size_t si) {
+    const Shard& sh = ps.shards[si];
+    try {
+      ck(cudaSetDevice(devices_[size_t(sh.device)]), "cudaSetDevice");
+      std::vector<const void*> hin(inputs.size(), nullptr);
+      for (size_t i = 0; i < inputs.size(); ++i) {
+        const HostValue& v = *inputs[i];
+        if (numel(v.shape) <= kPlanTimeInputMaxElems) continue;
+        size_t row = v.shape.empty() ? 0 : v.nbytes / size_t(std::max<int64_t>(v.shape[0], 1));
+        const void* base = v.dev ? v.dev : v.data;   // device-resident: copied device to device
+        hin[i] = static_cast<const uint8_t*>(base) + (ps.sharded ? size_t(sh.begin) * row : 0);
+      }
+      std::vector<void*> hout(nout, nullptr);
+      for (size_t j = 0; j < nout; ++j) {
+        if (!outs[j] || ps.out_host[j]) continue;
+        size_t row = ps.out_shapes[j].empty() ? 0
+                                                : outs[j]->nbytes / size_t(std::max<int64_t>(ps.out_shapes[j][0], 1));
+        void* base = outs[j]->dev ? outs[j]->dev : outs[j]->data;
+        hout[j] = static_cast<uint8_t*>(base) + (ps.sharded ? size_t(sh.begin) * row : 0);
+      }
+      cudaStream_t s = streams_[size_t(sh.device)];
+      sh.plan->enqueue(s, hin, hout);
+      ck(cudaStreamSynchronize(s), "stream synchronize");
+      sh.plan->check_device_error();
+    } catch (const Error& e) {
+      errs[si] = e.what();
+      codes[si] = e.code;
+    } catch (const std::exception& e) {
+      errs[si] = e.what();
+      codes[si] = SB_INTERNAL;
+    }
+  };
+  if (ps.shards.size() == 1) {
+    work(0);
+  } else {
+    std::vector<std::thread> th;
+    for (size_t si = 0; si < ps.shards.size(); ++si) th.emplace_back(work, si);
+    for (auto& t : th) t.join();
+  }
+  for (size_t si = 0; si < errs.size(); ++si)
+    if (codes[si]) fail(codes[si], errs[si]);
+}
+
 std::vector<std::shared_ptr<HostValue>> Session::run(const std::vector<std::shared_ptr<HostValue>>& inputs,
-                                                     const std::vector<int>& out_idx) {
+                                                     const std::vector<int>& out_idx, bool keep_on_device) {
   std::lock_guard<std::mutex> lock(mu_);
   auto ps = get_plans(inputs);
   const size_t nout = ps->out_shapes.size();
   std::vector<std::shared_ptr<HostValue>> outs(nout);
   std::vector<bool> wanted(nout, false);
   for (int j : out_idx) wanted[size_t(j)] = true;
-  maybe_build_pipeline(*ps, inputs);
+  bool dev_inputs = false;
+  for (const auto& v : inputs) dev_inputs = dev_inputs || v->dev != nullptr;
+  if (keep_on_device || dev_inputs) {   // chained runs: no host copies to hide, no micro-batch pipeline
+    for (size_t j = 0; j < nout; ++j) {
+      if (!wanted[j]) continue;
+      if (ps->out_host[j]) {
+        const HostTensor& h = *ps->out_values[j];
+        outs[j] = HostValue::alloc_tensor(h.dtype, h.shape);
+        if (h.nbytes()) std::memcpy(outs[j]->data, h.data(), h.nbytes());
+      } else if (keep_on_device) {
+        auto v = std::make_shared<HostValue>();
+        v->elem_type = DT_FLOAT;
+        v->shape = ps->out_shapes[j];
+        v->nbytes = size_t(numel(v->shape)) * 4;
+        v->dev_id = devices_[0];
+        ck(cudaSetDevice(v->dev_id), "cudaSetDevice");
+        ck(cudaMalloc(&v->dev, std::max<size_t>(v->nbytes, 16)), "cudaMalloc (device-resident output)");
+        outs[j] = v;
+      } else {
+        outs[j] = HostValue::alloc_tensor(DT_FLOAT, ps->out_shapes[j]);
+      }
+    }
+  } else {
+    maybe_build_pipeline(*ps, inputs);
+  }
+  if (keep_on_device || dev_inputs) {
+    run_shards(*ps, inputs, outs);
+    std::vector<std::shared_ptr<HostValue>> res;
+    for (int j : out_idx) res.push_back(outs[size_t(j)]);
+    return res;
+  }
   // A pipelined run copies each chunk's outputs back while later chunks still copy in and compute:
   // a copy into pageable memory would block the host until the chunk is done, serialising the
   // pipeline, so those outputs are page-locked whatever their size.
@@ -704,47 +868,7 @@ std::vector<std::shared_ptr<HostValue>> Session::run(const std::vector<std::shar
     for (int j : out_idx) res.push_back(outs[size_t(j)]);
     return res;
   }
-  std::vector<std::string> errs(ps->shards.size());
-  std::vector<int32_t> codes(ps->shards.size(), 0);
-  auto work = [&](size_t si) {
-    const Shard& sh = ps->shards[si];
-    try {
-      ck(cudaSetDevice(devices_[size_t(sh.device)]), "cudaSetDevice");
-      std::vector<const void*> hin(inputs.size(), nullptr);
-      for (size_t i = 0; i < inputs.size(); ++i) {
-        const HostValue& v = *inputs[i];
-        if (numel(v.shape) <= kPlanTimeInputMaxElems) continue;
-        size_t row = v.shape.empty() ? 0 : v.nbytes / size_t(std::max<int64_t>(v.shape[0], 1));
-        hin[i] = static_cast<const uint8_t*>(v.data) + (ps->sharded ? size_t(sh.begin) * row : 0);
-      }
-      std::vector<void*> hout(nout, nullptr);
-      for (size_t j = 0; j < nout; ++j) {
-        if (!outs[j] || ps->out_host[j]) continue;
-        size_t row = ps->out_shapes[j].empty() ? 0
-                                                : outs[j]->nbytes / size_t(std::max<int64_t>(ps->out_shapes[j][0], 1));
-        hout[j] = static_cast<uint8_t*>(outs[j]->data) + (ps->sharded ? size_t(sh.begin) * row : 0);
-      }
-      cudaStream_t s = streams_[size_t(sh.device)];
-      sh.plan->enqueue(s, hin, hout);
-      ck(cudaStreamSynchronize(s), "stream synchronize");
-      sh.plan->check_device_error();
-    } catch (const Error& e) {
-      errs[si] = e.what();
-      codes[si] = e.code;
-    } catch (const std::exception& e) {
-      errs[si] = e.what();
-      codes[si] = SB_INTERNAL;
-    }
-  };
-  if (ps->shards.size() == 1) {
-    work(0);
-  } else {
-    std::vector<std::thread> th;
-    for (size_t si = 0; si < ps->shards.size(); ++si) th.emplace_back(work, si);
-    for (auto& t : th) t.join();
-  }
-  for (size_t si = 0; si < errs.size(); ++si)
-    if (codes[si]) fail(codes[si], errs[si]);
+  run_shards(*ps, inputs, outs);
   std::vector<std::shared_ptr<HostValue>> res;
   for (int j : out_idx) res.push_back(outs[size_t(j)]);
   return res;
@@ -766,7 +890,7 @@ std::vector<double> Session::time_device(const std::vector<std::shared_ptr<HostV
         const HostValue& v = *inputs[i];
         if (numel(v.shape) <= kPlanTimeInputMaxElems) continue;
         size_t row = v.shape.empty() ? 0 : v.nbytes / size_t(std::max<int64_t>(v.shape[0], 1));
-        hin[i] = static_cast<const uint8_t*>(v.data) + (ps->sharded ? size_t(sh.begin) * row : 0);
+        hin[i] = static_cast<const uint8_t*>(v.dev ? v.dev : v.data) + (ps->sharded ? size_t(sh.begin) * row : 0);
       }
       std::vector<void*> hout(ps->out_shapes.size(), nullptr);
       sh.plan->enqueue(s, hin, hout);   // inputs resident in HBM from here on
@@ -807,7 +931,7 @@ std::vector<std::pair<std::string, double>> Session::profile_steps(const std::ve
   cudaStream_t s = streams_[size_t(sh.device)];
   std::vector<const void*> hin(inputs.size(), nullptr);
   for (size_t i = 0; i < inputs.size(); ++i)
-    if (numel(inputs[i]->shape) > kPlanTimeInputMaxElems) hin[i] = inputs[i]->data;
+    if (numel(inputs[i]->shape) > kPlanTimeInputMaxElems) hin[i] = inputs[i]->dev ? inputs[i]->dev : inputs[i]->data;
   std::vector<void*> hout(ps->out_shapes.size(), nullptr);
   sh.plan->enqueue(s, hin, hout);
   ck(cudaStreamSynchronize(s), "sync");
@@ -829,6 +953,22 @@ PlanStats Session::stats(const std::vector<std::shared_ptr<HostValue>>& inputs) 
     t.weight_bytes += s.weight_bytes;
   }
   return t;
+}
+
+std::pair<int64_t, int64_t> Session::transfer_bytes(const std::vector<std::shared_ptr<HostValue>>& inputs) {
+  std::lock_guard<std::mutex> lock(mu_);
+  auto ps = get_plans(inputs);
+  maybe_build_pipeline(*ps, inputs);
+  int64_t h2d = 0, d2h = 0;
+  for (const auto& sh : ps->shards)
+    for (const auto& b : sh.plan->inputs()) {
+      const HostValue& v = *inputs[size_t(b.index)];
+      const bool narrow = ps->pipe && !v.pinned && !v.dev && b.bf16_ok && v.elem_type == DT_FLOAT;
+      h2d += int64_t(narrow ? b.bytes / 2 : b.bytes);
+    }
+  for (size_t j = 0; j < ps->out_shapes.size(); ++j)
+    if (!ps->out_host[j]) d2h += numel(ps->out_shapes[j]) * 4;
+  return {h2d, d2h};
 }
 
 int Session::devices_used(const std::vector<std::shared_ptr<HostValue>>& inputs) {

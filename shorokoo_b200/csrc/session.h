@@ -26,6 +26,12 @@ struct HostValue {
   size_t nbytes = 0;
   bool owned = true;       // false: borrowed caller memory
   bool pinned = false;
+  // Device-resident tensor (an output of a run that kept its outputs on the device): `dev` holds
+  // the nbytes on device `dev_id`; `data` stays null until host_data() copies them to the host.
+  void* dev = nullptr;
+  int dev_id = -1;
+  std::mutex host_mu;
+  void* host_data();       // data, copying a device-resident tensor to host memory on first use
   std::vector<std::string> strings;
   std::vector<std::shared_ptr<HostValue>> items;   // sequence elements
   ~HostValue();
@@ -49,9 +55,11 @@ class Session {
   const std::vector<std::string>& input_names() const { return info_.input_names; }
   const std::vector<std::string>& output_names() const { return info_.output_names; }
 
-  // Run with inputs in session input order; returns outputs in the order of `out_idx`.
+  // Run with inputs in session input order; returns outputs in the order of `out_idx`. With
+  // keep_on_device the device outputs stay in device memory (no device->host copy); inputs that are
+  // device-resident are copied device to device.
   std::vector<std::shared_ptr<HostValue>> run(const std::vector<std::shared_ptr<HostValue>>& inputs,
-                                              const std::vector<int>& out_idx);
+                                              const std::vector<int>& out_idx, bool keep_on_device = false);
   // Device-only timing: uploads inputs once and times `iters` replays of the kernel sequence on
   // every device; returns per-device milliseconds per run (CUDA events on each device's stream).
   std::vector<double> time_device(const std::vector<std::shared_ptr<HostValue>>& inputs, int warmup, int iters);
@@ -59,6 +67,9 @@ class Session {
   std::vector<std::pair<std::string, double>> profile_steps(const std::vector<std::shared_ptr<HostValue>>& inputs,
                                                             int iters);
   PlanStats stats(const std::vector<std::shared_ptr<HostValue>>& inputs);
+  // Bytes a run() of these inputs moves host->device and device->host (float32 inputs staged as
+  // bfloat16 count as such).
+  std::pair<int64_t, int64_t> transfer_bytes(const std::vector<std::shared_ptr<HostValue>>& inputs);
   int devices_used(const std::vector<std::shared_ptr<HostValue>>& inputs);
 
  private:
@@ -119,6 +130,8 @@ class Session {
 
   std::shared_ptr<PlanSet> get_plans(const std::vector<std::shared_ptr<HostValue>>& inputs);
   void maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs);
+  void run_shards(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs,
+                  const std::vector<std::shared_ptr<HostValue>>& outs);
   void run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs,
                      const std::vector<std::shared_ptr<HostValue>>& outs);
   std::vector<InputSpec> specs_for(const std::vector<std::shared_ptr<HostValue>>& inputs, int64_t batch_begin,

@@ -472,7 +472,7 @@ def classification_head(B: Builder, x: str, num_classes: int, o: ResNetOpts,
     return top if include_top else g
 
 
-def _resnet_inputs(B: Builder, live: bool, num_classes: int, x_shape):
+def _resnet_inputs(B: Builder, live: bool, num_classes: int, x_shape, x_elem: int = W.FLOAT):
     """Hyper inputs come first when not specialised (RealCheckpointPredictionTests.cs:29-37)."""
     o = ResNetOpts()
     hyper_vals = []
@@ -487,18 +487,39 @@ def _resnet_inputs(B: Builder, live: bool, num_classes: int, x_shape):
                       (eps, np.array(1e-5, np.float32)), (it, np.array(True)), (sm, np.array(False))]
         o.eps_input = eps
         include_top, apply_softmax = it, sm
-    x = B.graph_input(W.FLOAT, 4, x_shape)
+    x = B.graph_input(x_elem, 4, x_shape)
     return x, o, hyper_vals, include_top, apply_softmax
+
+
+def round_to(x: np.ndarray, dtype: str) -> np.ndarray:
+    """float32 values rounded to bfloat16 / float16 (nearest even), still as float32."""
+    if dtype == "float16":
+        return x.astype(np.float16).astype(np.float32)
+    if dtype == "bfloat16":
+        u = np.ascontiguousarray(x, np.float32).view(np.uint32)
+        r = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000))
+        return r.view(np.float32)
+    return x
 
 
 def resnet(depth: int = 50, batch: int = 512, hw: Tuple[int, int] = (224, 224), seed: int = 11,
            num_classes: int = 1000, live_hypers: bool = False, dead_code: bool = False,
            affine_scale: float = 0.0, apply_softmax: Optional[bool] = None,
-           include_top: Optional[bool] = None) -> ModelCase:
+           include_top: Optional[bool] = None, input_dtype: str = "float32") -> ModelCase:
+    """``input_dtype`` "bfloat16" / "float16": the image arrives as a 16-bit float tensor (a caller's
+    CreateTensor<BFloat16 / Float16>) and a Cast to float32 feeds the stem; the case's input array
+    holds the 16-bit values widened to float32."""
     rng_in = np.random.Generator(np.random.PCG64(seed))
     x_val = rng_in.standard_normal(size=(batch, 3, hw[0], hw[1]), dtype=np.float32)
     B = Builder(seed + WEIGHT_SEED_OFFSET, dead_code=dead_code)
-    x, o, hyper_vals, inc_top, app_sm = _resnet_inputs(B, live_hypers, num_classes, x_val.shape)
+    x, o, hyper_vals, inc_top, app_sm = _resnet_inputs(B, live_hypers, num_classes, x_val.shape,
+                                                       {"float32": W.FLOAT, "bfloat16": W.BFLOAT16,
+                                                        "float16": W.FLOAT16}[input_dtype])
+    x_in = x
+    if input_dtype != "float32":
+        x_val = round_to(x_val, input_dtype)
+        x = B.op("Cast", [x_in], to=W.FLOAT)
+        B.shape[x] = x_val.shape
     o.bn_affine_scale = affine_scale
     if apply_softmax is not None:
         if live_hypers:
@@ -525,7 +546,7 @@ def resnet(depth: int = 50, batch: int = 512, hw: Tuple[int, int] = (224, 224), 
         raise ValueError(depth)
     out = classification_head(B, h, num_classes, o, inc_top, app_sm)
     B.outputs.append(W.ValueInfo(out))
-    inputs = hyper_vals + [(x, x_val)]
+    inputs = hyper_vals + [(x_in, x_val)]
     return ModelCase(f"resnet{depth}", B.model(f"ResNet{depth}"), inputs, [out], B.macs, B.params)
 
 

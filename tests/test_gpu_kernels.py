@@ -166,8 +166,10 @@ def test_stem_with_fused_max_pool(n, h, w, fused):
     ref = run_oracle(case)[0]
     assert got.shape == ref.shape
     assert_close(got, ref, what=f"stem + max pool {n}x3x{h}x{w}")
-    # the bf16-operand arithmetic of the path: far tighter than the gate
-    assert_close(got, run_oracle(case, "bf16-operands")[0], tol=4e-3, what="stem + pool vs bf16-operand oracle")
+    if fused:   # against the separate conv and pool kernels (same weights, the conv output also read):
+        # the two differ only in the conv's summation order, far below the gate
+        other = run_backend(_stem_pool_case(n, h, w, conv_output_too=True))[0]
+        assert_close(got, other, tol=2e-3, what="fused stem + pool vs separate kernels")
 
 
 def test_stem_pool_not_fused_when_the_conv_output_is_also_read():
