@@ -488,6 +488,16 @@ class Interpreter:
         X = x[0]
         return np.max(X, axis=tuple(range(2, X.ndim)), keepdims=True)
 
+    def op_SequenceConstruct(self, n, x, env):
+        return [list(x)]
+
+    def op_SequenceAt(self, n, x, env):
+        k = int(np.asarray(x[1]).reshape(-1)[0])
+        return x[0][k]
+
+    def op_SequenceLength(self, n, x, env):
+        return np.array(len(x[0]), np.int64)
+
     def op_Pad(self, n, x, env):
         X = x[0]
         mode = n.attr("mode", b"constant")

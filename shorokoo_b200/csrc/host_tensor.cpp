@@ -369,7 +369,8 @@ static const char* kHostOps[] = {
     "Concat", "Reshape", "Flatten", "Transpose", "Expand", "Cast", "Range", "ReduceProd", "ReduceSum",
     "ReduceMean", "ReduceMax", "ReduceMin", "Add", "Sub", "Mul", "Div", "Pow", "Max", "Min", "Equal", "Less",
     "Greater", "LessOrEqual", "GreaterOrEqual", "Not", "And", "Or", "Where", "Sqrt", "Neg", "Abs", "Exp",
-    "Log", "Reciprocal", "Relu", "Sigmoid", "Tanh", "Floor", "Ceil", "MatMul", "Softmax"};
+    "Log", "Reciprocal", "Relu", "Sigmoid", "Tanh", "Floor", "Ceil", "MatMul", "Softmax", "Pad",
+    "SequenceConstruct", "SequenceAt", "SequenceLength"};
 
 bool host_eval_supported(const std::string& op) {
   for (const char* s : kHostOps)
@@ -417,6 +418,71 @@ bool host_eval(const OnnxNode& n, const std::vector<const HostTensor*>& in, std:
     return true;
   }
   if (op == "Identity") { out.push_back(I(0)); return true; }
+  // Sequences (the reference's module-stage graphs hold a module's parameters in one and pick them
+  // by computed index: SequenceConstruct -> SequenceAt, FastOnnxModelBuilder.cs:1116-1190).
+  if (op == "SequenceConstruct") {
+    HostTensor s;
+    s.seq = std::make_shared<std::vector<HostTensor>>();
+    for (size_t i = 0; i < in.size(); ++i) {
+      SB_CHECK(in[i] && !in[i]->seq, SB_INVALID_ARGUMENT, "SequenceConstruct: tensor inputs expected");
+      s.seq->push_back(*in[i]);
+    }
+    out.push_back(s);
+    return true;
+  }
+  if (op == "SequenceAt" || op == "SequenceLength") {
+    SB_CHECK(I(0).seq != nullptr, SB_INVALID_ARGUMENT, op + ": input 0 is not a sequence");
+    const auto& items = *I(0).seq;
+    if (op == "SequenceLength") {
+      out.push_back(HostTensor::scalar_i64(int64_t(items.size())));
+      return true;
+    }
+    int64_t k = I(1).get_i64(0);
+    if (k < 0) k += int64_t(items.size());
+    SB_CHECK(k >= 0 && k < int64_t(items.size()), SB_INVALID_ARGUMENT, "SequenceAt: index out of range");
+    out.push_back(items[size_t(k)]);
+    return true;
+  }
+  if (op == "Pad") {   // constant mode only (the mode the reference emits)
+    std::string mode = n.attr_s("mode", "constant");
+    SB_CHECK(mode == "constant", SB_UNSUPPORTED, "Pad: only constant mode on the host");
+    const HostTensor& x = I(0);
+    const int64_t r = int64_t(x.shape.size());
+    auto pads = I(1).to_i64_vec();
+    std::vector<int64_t> axes;
+    if (has(3)) {
+      for (int64_t a : I(3).to_i64_vec()) axes.push_back(a < 0 ? a + r : a);
+    } else {
+      for (int64_t a = 0; a < r; ++a) axes.push_back(a);
+    }
+    SB_CHECK(pads.size() == 2 * axes.size(), SB_SHAPE_ERROR, "Pad: pads length");
+    std::vector<int64_t> lo(static_cast<size_t>(r), 0), hi(static_cast<size_t>(r), 0);
+    for (size_t j = 0; j < axes.size(); ++j) {
+      lo[size_t(axes[j])] = pads[j];
+      hi[size_t(axes[j])] = pads[j + axes.size()];
+      SB_CHECK(pads[j] >= 0 && pads[j + axes.size()] >= 0, SB_UNSUPPORTED, "Pad: negative pads");
+    }
+    std::vector<int64_t> os(static_cast<size_t>(r), 0);
+    for (int64_t d = 0; d < r; ++d) os[size_t(d)] = x.shape[size_t(d)] + lo[size_t(d)] + hi[size_t(d)];
+    HostTensor o(x.dtype, os);
+    const double cv = has(2) && I(2).numel() ? I(2).get_f64(0) : 0.0;
+    const bool fl = x.is_float();
+    for (int64_t i = 0; i < o.numel(); ++i) {   // every output element: copy or fill
+      int64_t rem = i, src = 0, stride = 1;
+      bool inside = true;
+      for (int64_t d = r - 1; d >= 0; --d) {
+        const int64_t c = rem % os[size_t(d)] - lo[size_t(d)];
+        rem /= os[size_t(d)];
+        if (c < 0 || c >= x.shape[size_t(d)]) inside = false;
+        src += c * stride;
+        stride *= x.shape[size_t(d)];
+      }
+      if (fl) o.set_f64(i, inside ? x.get_f64(src) : cv);
+      else o.set_i64(i, inside ? x.get_i64(src) : int64_t(cv));
+    }
+    out.push_back(o);
+    return true;
+  }
   if (op == "Shape") {
     auto s = I(0).shape;
     int64_t r = int64_t(s.size());
@@ -729,10 +795,17 @@ bool host_eval(const OnnxNode& n, const std::vector<const HostTensor*>& in, std:
   if (op == "Ceil") { out.push_back(unary(I(0), [](double v) { return std::ceil(v); })); return true; }
   if (op == "MatMul") {
     const HostTensor &a = I(0), &b = I(1);
-    SB_CHECK(a.shape.size() == 2 && b.shape.size() == 2, SB_UNSUPPORTED, "host MatMul: rank-2 only");
-    int64_t M = a.shape[0], K = a.shape[1], N = b.shape[1];
-    SB_CHECK(b.shape[0] == K, SB_SHAPE_ERROR, "MatMul: inner dims differ");
-    HostTensor o(a.dtype, {M, N});
+    // rank 2 x rank 2; a rank-1 operand is a row (left) or a column (right) vector whose unit
+    // dimension is dropped from the result (numpy matmul)
+    SB_CHECK(a.shape.size() >= 1 && a.shape.size() <= 2 && b.shape.size() >= 1 && b.shape.size() <= 2, SB_UNSUPPORTED,
+             "host MatMul: operands of rank 1 or 2 only");
+    const bool av = a.shape.size() == 1, bv = b.shape.size() == 1;
+    int64_t M = av ? 1 : a.shape[0], K = av ? a.shape[0] : a.shape[1], N = bv ? 1 : b.shape[1];
+    SB_CHECK((bv ? b.shape[0] : b.shape[0]) == K, SB_SHAPE_ERROR, "MatMul: inner dims differ");
+    std::vector<int64_t> os;
+    if (!av) os.push_back(M);
+    if (!bv) os.push_back(N);
+    HostTensor o(a.dtype, os);
     for (int64_t i = 0; i < M; ++i)
       for (int64_t j = 0; j < N; ++j) {
         double acc = 0;

@@ -21,6 +21,8 @@ struct HostTensor {
   // Lazy transpose of a rank-2 host tensor: lets MatMul(x, Transpose(W)) use W [N,K] directly
   // without copying a large weight twice.
   std::shared_ptr<HostTensor> transpose_src;
+  // A sequence of tensors (SequenceConstruct; dtype undefined, no shape) when set.
+  std::shared_ptr<std::vector<HostTensor>> seq;
 
   HostTensor() = default;
   HostTensor(int32_t dt, std::vector<int64_t> s);
