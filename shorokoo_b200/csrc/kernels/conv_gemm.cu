@@ -1274,6 +1274,190 @@ __global__ void __launch_bounds__(512, 1)
   }
 }
 
+// ---- 3x3 / stride 1 / pad 1 convolution from halo tiles ------------------------------------------
+// A tile is R output rows x Wp pixels of one image (Wp the power of two >= W + 2, R = 128 / Wp),
+// i.e. the 128 accumulator rows are the pixels p = r * Wp + c. One 4D TMA box brings the tile's
+// (R + 2) x Wp input halo (64 channels, starting at input row r0 - 1 and column -1, zero outside the
+// image) into shared memory in the 128-byte-swizzled K-major layout, and tap (kh, kw) reads it as a
+// 128-row window starting kh * Wp + kw rows in: halo row (r + kh) * Wp + c + kw is input pixel
+// (r0 + r + kh - 1, c + kw - 1). Pixels c >= W (and rows past H) are junk: computed, never stored
+// (their windows may run two rows past the halo, into slack rows of the stage). One load of
+// (R + 2) * Wp * 128 bytes per tile replaces nine 16 KB im2col loads; the 64 x 576 weights stay
+// resident. Warps: 0 TMA producer, 1 and 13-15 MMA issuers (tap t goes to issuer t mod P, each
+// into its own TMEM partial), 2-9 epilogue (TMA stores through a 4D output map that clips the junk).
+constexpr uint32_t kHaloBBytes = 64 * 128;   // one 64 x 64 bf16 weight k-tile
+constexpr int kHaloTaps = 9;
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* tm, int c0, int c1, int c2, int c3, const void* src) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(tm),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(src))
+               : "memory");
+}
+
+__host__ __device__ inline uint32_t halo_stage_bytes(int Wp, int R) {
+  return (uint32_t((R + 2) * Wp + 2) * 128u + 1023u) & ~1023u;   // + the two slack rows, 1 KB aligned
+}
+
+__global__ void __launch_bounds__(512, 1)
+    conv3x3_halo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmOut, const Conv3x3Args a) {
+  constexpr uint32_t idesc = idesc_mma(BM, 64, false);
+  const int STAGES = a.stages;
+  const int PE = a.mma_lanes;
+  const uint32_t TMEM_COLS = uint32_t(2 * PE * 64);
+  const int Wp = a.Wp, R = a.R;
+  const uint32_t HALO_BYTES = uint32_t((R + 2) * Wp) * 128u;
+  const uint32_t HALO_STAGE = halo_stage_bytes(Wp, R);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * HALO_STAGE;
+  uint8_t* sOut = sB + kHaloTaps * kHaloBBytes;
+  float* sBias = reinterpret_cast<float*>(sOut + 8 * (kOutSlab / 2));
+  uint64_t* full = reinterpret_cast<uint64_t*>(sBias + 64);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* accf = empty + kMaxStages;
+  uint64_t* acce = accf + 2;
+  uint64_t* bfull = acce + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bfull + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1u);
+      mbar_init(&empty[s], uint32_t(PE));   // every issuer reads every stage
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf[i], uint32_t(PE));
+      mbar_init(&acce[i], 8u);
+    }
+    mbar_init(bfull, 1u);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (threadIdx.x < 64) sBias[threadIdx.x] = a.bias[threadIdx.x];
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmOut) : "memory");
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int tpi = (a.H + R - 1) / R;   // tiles per image
+  const int total = a.N * tpi;
+
+  if (warp == 0) {
+    if (lane == 0) {   // ---- producer: the weights once, then one halo box per tile ----
+      mbar_expect_tx(bfull, uint32_t(kHaloTaps) * kHaloBBytes);
+      for (int t = 0; t < kHaloTaps; ++t) tma_load_2d(sB + t * kHaloBBytes, &tmB, t * BK, 0, bfull);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        const int n = t / tpi, r0 = (t - n * tpi) * R;
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) break;
+        mbar_expect_tx(&full[stage], HALO_BYTES);
+        tma_load_4d(sA + stage * HALO_STAGE, &tmA, 0, -1, r0 - 1, n, &full[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1 || warp >= 13) {
+    // ---- MMA issuers: issuer mid takes the taps mid, mid + P, ... of every tile ----
+    const int mid = warp == 1 ? 0 : warp - 12;
+    if (lane == 0 && mid < PE && mbar_wait(bfull, 0u, abort_flag, a.err, 128u)) {
+      int stage = 0, it = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t aph = uint32_t(it >> 1) & 1u;
+        if (!mbar_wait(&acce[acc], aph ^ 1u, abort_flag, a.err, 2u)) break;
+        if (!mbar_wait(&full[stage], phase, abort_flag, a.err, 4u)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t((acc * PE + mid) * 64);
+        const uint32_t halo = smem_u32(sA + stage * HALO_STAGE);
+        bool first = true;
+        for (int tap = mid; tap < kHaloTaps; tap += PE, first = false) {
+          const int kh = tap / 3, kw = tap - 3 * (tap / 3);
+          const uint32_t win = halo + uint32_t(kh * Wp + kw) * 128u;
+          const uint64_t ad = sw128_desc(win);   // the swizzle follows the address bits: no base offset
+          const uint64_t bd = sw128_desc(smem_u32(sB + tap * kHaloBBytes));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(d_tmem, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), idesc, (!first || kk != 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[stage]);
+        umma_commit(&accf[acc]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp >= 2 && warp < 10) {
+    // ---- epilogue: warp w holds tile pixels 32 (w & 3) .. + 31, channels 32 hsel .. + 31 ----
+    const int q = warp & 3, hsel = (warp - 2) >> 2;
+    uint8_t* slab = sOut + (warp - 2) * (kOutSlab / 2);
+    int it = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+      const int n = t / tpi, r0 = (t - n * tpi) * R;
+      const int acc = it & 1;
+      const uint32_t aph = uint32_t(it >> 1) & 1u;
+      if (!mbar_wait(&accf[acc], aph, abort_flag, a.err, 8u)) break;
+      tc_fence_after();
+      float v[32];
+      tmem_ld_sum(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * PE * 64 + hsel * 32), PE, 64, v);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&acce[acc]);
+        bulk_wait_read0();   // the previous store from this slab has read it
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float x[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = v[8 * j + e] + sBias[hsel * 32 + 8 * j + e];
+        uint4 qv;
+        if (a.act == 1) {
+          qv.x = pack_bf16x2_relu(x[0], x[1]);
+          qv.y = pack_bf16x2_relu(x[2], x[3]);
+          qv.z = pack_bf16x2_relu(x[4], x[5]);
+          qv.w = pack_bf16x2_relu(x[6], x[7]);
+        } else {
+          qv.x = pack_bf16x2(x[0], x[1]);
+          qv.y = pack_bf16x2(x[2], x[3]);
+          qv.z = pack_bf16x2(x[4], x[5]);
+          qv.w = pack_bf16x2(x[6], x[7]);
+        }
+        *reinterpret_cast<uint4*>(slab + slab64_off(lane, j)) = qv;
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int p0 = q * 32;
+        tma_store_4d(&tmOut, hsel * 32, p0 % Wp, r0 + p0 / Wp, n, slab);
+        bulk_commit();
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -1620,6 +1804,65 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   cudaError_t e = bn == 64 ? ensure_attr_mode<64>(mode, prec)
                            : (bn == 128 ? ensure_attr_mode<128>(mode, prec) : ensure_attr_mode<256>(mode, prec));
   if (e != cudaSuccess) throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+}
+
+int conv3x3_tile_width(int H, int W) {
+  int Wp = 1;
+  while (Wp < W + 2) Wp <<= 1;
+  if (Wp > BM) return 0;
+  const int R = BM / Wp;
+  const int tiles = (H + R - 1) / R;
+  // at least 70% of the computed pixels are real ones (a 7-row map in 8-row tiles is not worth it)
+  if (double(H) * W < 0.7 * double(tiles) * R * Wp) return 0;
+  return Wp;
+}
+
+void conv3x3_prepare(Conv3x3Plan& p, const void* w, int num_sms) {
+  Conv3x3Args& a = p.args;
+  std::memset(&p.tmA, 0, sizeof(p.tmA));
+  std::memset(&p.tmB, 0, sizeof(p.tmB));
+  std::memset(&p.tmOut, 0, sizeof(p.tmOut));
+  auto fn = get_encode_fn();
+  if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled entry point missing");
+  cuuint64_t dims[4] = {64, cuuint64_t(a.W), cuuint64_t(a.H), cuuint64_t(a.N)};
+  cuuint64_t strides[3] = {128, cuuint64_t(a.W) * 128, cuuint64_t(a.H) * a.W * 128};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  cuuint32_t box_in[4] = {64, cuuint32_t(a.Wp), cuuint32_t(a.R + 2), 1};
+  CUresult r = fn(&p.tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(a.x), dims, strides, box_in, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed for the 3x3 halo input");
+  const cuuint32_t spx = cuuint32_t(std::min(a.Wp, 32));
+  cuuint32_t box_out[4] = {32, spx, 32 / spx, 1};
+  r = fn(&p.tmOut, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, a.out, dims, strides, box_out, estr,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed for the 3x3 halo output");
+  if (!encode_2d(&p.tmB, w, uint64_t(kHaloTaps) * BK, 64, uint64_t(kHaloTaps) * BK * 2, BK, 64))
+    throw std::runtime_error("cuTensorMapEncodeTiled failed for the 3x3 weights");
+  a.mma_lanes = 4;
+  const int fixed = int(kHaloTaps * kHaloBBytes + 8 * (kOutSlab / 2)) + 256 + 1024 + 512;
+  const int stage = int(halo_stage_bytes(a.Wp, a.R));
+  int stages = std::min(kMaxStages, (kSmemLimit - fixed) / stage);
+  if (stages < 2) throw std::runtime_error("conv3x3: shared-memory plan leaves fewer than 2 stages");
+  a.stages = stages;
+  p.smem = stages * stage + fixed;
+  const int64_t tiles = int64_t(a.N) * ((a.H + a.R - 1) / a.R);
+  p.grid = int(std::min<int64_t>(num_sms, tiles));
+  static std::atomic<uint64_t> done_mask{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = uint64_t(1) << (dev & 63);
+  if (!(done_mask.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(conv3x3_halo_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    done_mask.fetch_or(bit);
+  }
+}
+
+cudaError_t conv3x3_launch(const Conv3x3Plan& p, cudaStream_t s) {
+  conv3x3_halo_kernel<<<p.grid, 512, p.smem, s>>>(p.tmA, p.tmB, p.tmOut, p.args);
+  return cudaGetLastError();
 }
 
 bool stem_pool_supported(int Cout, int Ho, int Wo, int KH, int KW) {

@@ -125,6 +125,35 @@ bool stem_pool_supported(int Cout, int Ho, int Wo, int KH, int KW);
 void stem_pool_prepare(StemPoolPlan& p, const void* w, int num_sms);
 cudaError_t stem_pool_launch(const StemPoolPlan& p, cudaStream_t s);
 
+// ---- 3x3 / stride 1 / pad 1 convolution from halo tiles (conv_gemm.cu) ---------------------------
+// y = act(conv3x3(x) + bias) over NHWC bf16 x [N, H, W, 64] with 64 output channels, y NHWC bf16.
+// A tile is R output rows x Wp pixels (Wp the power of two >= W + 2, R = 128 / Wp; pixels past W and
+// rows past H are computed and dropped): one 4D TMA box loads the tile's (R + 2) x Wp input halo
+// (zero outside the image) and the nine taps read it through shared-memory descriptors shifted by
+// kh * Wp + kw rows, instead of nine im2col loads. Weights bf16 [64, 576], K ordered (kh, kw, c).
+struct Conv3x3Args {
+  const void* x;
+  int N, H, W;
+  int Wp, R;               // tile geometry
+  const float* bias;       // [64]
+  void* out;
+  int act;                 // 0 none, 1 relu
+  unsigned int* err;
+  // set by conv3x3_prepare:
+  int stages, mma_lanes;
+};
+struct Conv3x3Plan {
+  CUtensorMap tmA;   // 4D tiled map of x, box 64 channels x Wp pixels x (R + 2) rows
+  CUtensorMap tmB;   // weights, 64 x 64 boxes
+  CUtensorMap tmOut; // 4D tiled map of y, box 32 channels x min(32, Wp) pixels x rows
+  int grid, smem;
+  Conv3x3Args args;
+};
+// The tile width for an output width W (0 when none fits: W + 2 > 128 or too few valid pixels).
+int conv3x3_tile_width(int H, int W);
+void conv3x3_prepare(Conv3x3Plan& p, const void* w, int num_sms);
+cudaError_t conv3x3_launch(const Conv3x3Plan& p, cudaStream_t s);
+
 // ---- memory-bound kernels (misc.cu) ------------------------------------------------------------
 constexpr int kMaxRank = 8;
 struct TDesc {

@@ -713,6 +713,35 @@ void Plan::plan_conv(const Op& op) {
   geo.pw = int(gpw);
   geo.dh = int(gdh);
   geo.dw = int(gdw);
+  // 3x3 / stride 1 / pad 1 convs from 64 to 64 channels with a bf16 output and no residual run from
+  // halo tiles (one TMA box of input rows per tile instead of nine im2col boxes).
+  const int halo_wp = (prec == 0 && !s2d && KH == 3 && KW == 3 && op.strides[0] == 1 && op.strides[1] == 1 &&
+                       op.dilations[0] == 1 && op.dilations[1] == 1 && op.pads[0] == 1 && op.pads[1] == 1 &&
+                       op.pads[2] == 1 && op.pads[3] == 1 && C == 64 && Cp == 64 && Cout == 64 && op.residual < 0 &&
+                       op.concat < 0 && out_bf16 && grp_rows == 0 && op.act <= 1 && x.strides[3] == 64 && x.off % 16 == 0)
+                          ? k::conv3x3_tile_width(int(H), int(W))
+                          : 0;
+  if (halo_wp) {
+    const std::string hkind = "conv 3x3/1 64->64 M=" + std::to_string(N * Ho * Wo) + " halo";
+    add_step(hkind, reads, {y}, [=]() {
+      auto p = std::make_shared<k::Conv3x3Plan>();
+      k::Conv3x3Args& a = p->args;
+      std::memset(&a, 0, sizeof(a));
+      a.x = ptr(x);
+      a.N = int(N);
+      a.H = int(H);
+      a.W = int(W);
+      a.Wp = halo_wp;
+      a.R = 128 / halo_wp;
+      a.bias = static_cast<const float*>(ptr(bt));
+      a.out = ptr(y);
+      a.act = op.act;
+      a.err = err_;
+      k::conv3x3_prepare(*p, ptr(wt), sms);
+      return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::conv3x3_launch(*p, s); });
+    });
+    return;
+  }
   static const char* kAModeName[] = {"tma", "gather", "gather8", "im2col", "im2col16"};
   const std::string kind = "conv " + std::to_string(KH) + "x" + std::to_string(KW) + "/" +
                            std::to_string(op.strides[0]) + " " + std::to_string(C) + "->" + std::to_string(Cout) +

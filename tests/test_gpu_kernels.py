@@ -180,6 +180,53 @@ def test_stem_pool_not_fused_when_the_conv_output_is_also_read():
         assert_close(g, r, what="stem with its conv output as a graph output")
 
 
+def _halo_case(n, h, w, relu, seed=41):
+    """Two chained 3x3 / stride 1 / pad 1 convs over 64 channels (+ per-channel affine, the first with
+    ReLU when asked) and a 1x1 conv reading the second (so both 3x3 outputs are bf16 activations)."""
+    from shorokoo_b200.emit import onnx_writer as W
+    from shorokoo_b200.emit.graphs import Builder, ModelCase, kaiming_normal
+    rng = np.random.Generator(np.random.PCG64(seed))
+    x = rng.standard_normal((n, 64, h, w), dtype=np.float32)
+    B = Builder(seed + 1)
+    xi = B.graph_input(W.FLOAT, 4, x.shape)
+    y = xi
+    for i in range(2):
+        wt = B.init(kaiming_normal(B.rng, (64, 64, 3, 3)), f"w{i}")
+        y = B.conv(y, wt, None, 3, 1, pads=[1, 1, 1, 1])
+        sc = B.init((1 + 0.2 * B.rng.standard_normal((1, 64, 1, 1))).astype(np.float32), f"s{i}")
+        sh = B.init((0.2 * B.rng.standard_normal((1, 64, 1, 1))).astype(np.float32), f"t{i}")
+        y = B.binary("Add", B.binary("Mul", y, sc), sh)
+        if relu and i == 0:
+            y = B.unary("Relu", y)
+    w2 = B.init(kaiming_normal(B.rng, (32, 64, 1, 1)), "w2")
+    z = B.conv(y, w2, None, 1, 1, pads=[0, 0, 0, 0])
+    B.outputs.append(W.ValueInfo(z))
+    return ModelCase("halo", B.model("halo"), [(xi, x)], [z], 0)
+
+
+# 3x3 / stride 1 / pad 1 convs from 64 to 64 channels with bf16 outputs run from halo tiles (R rows x
+# Wp pixels, one 4D TMA box of R + 2 input rows per tile, the taps read through row-shifted
+# shared-memory descriptors): map widths giving tile widths 64 (R = 2), 32 (R = 4), 16 (R = 8) and
+# 128 (R = 1), heights not a multiple of R, widths not a power of two, with and without ReLU; the
+# 17x23 map (too many junk pixels in 32-wide tiles) takes the im2col kernel.
+@pytest.mark.parametrize("n,h,w,relu,halo", [(2, 56, 56, True, True), (3, 28, 28, True, True),
+                                             (2, 14, 14, False, True), (2, 30, 50, True, True),
+                                             (4, 9, 100, True, True), (2, 17, 23, True, False)])
+def test_conv3x3_halo_tiles(n, h, w, relu, halo):
+    case = _halo_case(n, h, w, relu)
+    f = B200InferenceSessionFactory(num_devices=1)
+    sess = f.CreateSession(case.model)
+    feeds = {nm: f.CreateTensor(a) for nm, a in case.inputs}
+    kinds = [k for k, _ in sess.profile(feeds, iters=1)]
+    assert sum(k.endswith(" halo") for k in kinds) == (2 if halo else 0), kinds
+    outs = sess.Run(feeds, case.output_names)
+    got = outs[0].numpy()
+    for o in outs:
+        o.Dispose()
+    sess.Dispose()
+    assert_close(got, run_oracle(case)[0], what=f"3x3 halo convs {n}x64x{h}x{w}")
+
+
 def test_maxpool_and_gap():
     case = graphs.resnet(depth=18, batch=2, hw=(40, 40), seed=5, include_top=False)
     got = run_backend(case)[0]
