@@ -182,12 +182,17 @@ def main():
                     help="tensor-core operand precision (tf32: the accuracy mode)")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the workload's global batch (small cases for profiler captures)")
+    ap.add_argument("--devices", type=int, default=1,
+                    help="one session over this many GPUs of this process (the library's own batch sharding, "
+                         "one host thread per device; what SHOROKOO_B200_DEVICES gives a plugin caller)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     rank, world, local = dist_env()
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.devices > 1 and world > 1:
+        ap.error("--devices N runs one process over N GPUs; do not combine it with torchrun ranks")
 
     import torch
     import torch.distributed as dist
@@ -205,11 +210,12 @@ def main():
     case = full if full is not None else make_case(name, total)
     # this rank's contiguous shard of the batch
     inputs = [(n, a[begin:begin + per] if a.ndim and a.shape[0] == total else a) for n, a in case.inputs]
-    f = B200InferenceSessionFactory(num_devices=1, first_device=local, precision=args.precision)
+    f = B200InferenceSessionFactory(num_devices=args.devices, first_device=local, precision=args.precision)
     sess = f.CreateSession(case.model)
     feeds = {n: f.CreateTensor(a) for n, a in inputs}
     st = sess.stats(feeds)
     macs_per_img = case.macs / total
+    n_dev = int(st["devices"])   # devices the session's plans run on (1 unless --devices)
 
     def barrier():
         torch.cuda.synchronize()
@@ -219,7 +225,7 @@ def main():
     # ---- device-resident throughput (value) ----
     barrier()
     with ClockSampler(local) as clk:
-        ms = sess.time_device(feeds, warmup=args.warmup, iters=args.steps)[0]
+        ms = max(sess.time_device(feeds, warmup=args.warmup, iters=args.steps))   # max over the session's devices
         barrier()
         # ---- end to end through the plugin interface (e2e): every step hands the host batch to the
         # library the way the reference's CreateTensor<T> does (aliasing the caller's array, no
@@ -268,7 +274,8 @@ def main():
         if args.precision == "tf32x3":   # three MMAs per algorithmic one
             peak_tflops /= 3
             peak_note += ", divided by the three MMAs per K slice of TF32x3"
-    achieved = 2.0 * st["macs"] / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0
+    # (the profile times device 0's plan: its share of the session's MACs)
+    achieved = 2.0 * st["macs"] / n_dev / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
@@ -287,12 +294,16 @@ def main():
     if rank == 0:
         value = total / (t_max / 1e3)
         line = {
-            "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world * n_dev, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": args.precision, "data": "synthetic (seeded inputs, random-init weights)",
-            "config": {"workload": f"{name} forward, batch {total} ({per}/GPU), 3x224x224 fp32 NCHW input"
+            "config": {"workload": f"{name} forward, batch {total} ({-(-per // n_dev)}/GPU), 3x224x224 fp32 NCHW input"
                        if name.startswith("resnet") else f"{name} forward, batch {total}",
-                       "global_batch": total, "parallelism": f"batch-sharded x{world}, replicated weights, no collective",
+                       "global_batch": total,
+                       "parallelism": (f"batch-sharded x{world}, replicated weights, no collective" if n_dev == 1 else
+                                       f"one session over {n_dev} devices in one process: the library shards the "
+                                       f"batch (contiguous rows, replicated weights, no collective), one host thread "
+                                       f"and one staging pipeline per device"),
                        "l2": "inputs larger than L2 (the 308 MB input and a multi-GB activation arena per step)",
                        "precision": {"bf16": "bf16 operands", "tf32": "fp32 operands read as TF32",
                                      "tf32x3": "error-compensated TF32 (hi*hi + hi*lo + lo*hi)"}[args.precision]
@@ -307,7 +318,7 @@ def main():
             "e2e_pinned_input": {"value": total / e2e[False], "unit": "images/s",
                                  "timing": "Run alone on an input already in library page-locked memory "
                                            "(CreateTensor outside the timed region)"},
-            "gpu_launches": int(st["launches"]) * args.steps * world,
+            "gpu_launches": int(st["launches"]) * args.steps * world,   # (summed over the session's devices)
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
                          "frac": achieved / peak_tflops, "traffic": traffic,
                          "traffic_note": "DRAM bytes read + written per step by these launches, one ncu capture of "

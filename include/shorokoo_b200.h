@@ -192,6 +192,11 @@ SB_API int32_t sb_linear_noalloc(const float* x, const float* w, const float* bi
 SB_API int32_t sb_debug_lower(const uint8_t* model, size_t model_len, int32_t n_inputs, sb_value* const* in_values,
                               char* buf, size_t capacity, size_t* needed);
 
+/* The host narrowing a Run applies to a float32 input in pageable memory that the plan only reads
+ * as bfloat16 (round to nearest even, NaN kept as a quiet NaN; the device's own rounding of a float32
+ * operand, so the narrowed batch gives the same results): n values, up to `threads` host threads. */
+SB_API int32_t sb_debug_narrow_bf16(const float* src, uint16_t* dst, size_t n, int32_t threads);
+
 #ifdef __cplusplus
 }
 #endif

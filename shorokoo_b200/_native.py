@@ -53,6 +53,7 @@ SIGNATURES = {
     "sb_session_stats": (I32, [P, I32, PSTR, PP, C.POINTER(I64), C.POINTER(I64), C.POINTER(DBL),
                                C.POINTER(I64), C.POINTER(I32)]),
     "sb_debug_lower": (I32, [C.c_char_p, SZ, I32, PP, C.c_char_p, SZ, C.POINTER(SZ)]),
+    "sb_debug_narrow_bf16": (I32, [C.c_void_p, C.c_void_p, SZ, I32]),
     "sb_session_transfer_bytes": (I32, [P, I32, PSTR, PP, C.POINTER(I64), C.POINTER(I64)]),
     "sb_linear_noalloc": (I32, [P, P, P, P, I64, I64, I64, I32, P]),
 }
@@ -63,7 +64,7 @@ def header_symbols() -> list:
     import re
     hdr = os.path.join(os.path.dirname(HERE), "include", "shorokoo_b200.h")
     with open(hdr) as f:
-        return sorted(set(re.findall(r"\b(sb_[a-z_]+)\s*\(", f.read())))
+        return sorted(set(re.findall(r"\b(sb_[a-z0-9_]+)\s*\(", f.read())))
 
 
 def lib():

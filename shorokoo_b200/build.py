@@ -24,7 +24,7 @@ INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CXXFLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wno-sign-compare", "-fvisibility=hidden",
+CXXFLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wno-sign-compare", "-Wno-psabi", "-fvisibility=hidden",
             f"-I{CUDA_HOME}/include", f"-I{INCLUDE}", f"-I{CSRC}"]
 NVFLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
                   f"-I{INCLUDE}", f"-I{CSRC}", "--expt-relaxed-constexpr"]

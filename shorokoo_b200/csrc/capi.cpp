@@ -17,6 +17,7 @@ namespace sb {
 void* host_alloc(size_t bytes, bool& pinned);
 bool host_is_page_locked(const void* p);
 void host_copy(void* dst, const void* src, size_t n);
+void host_narrow_bf16(uint16_t* dst, const float* src, size_t n, unsigned threads);
 }  // namespace sb
 
 using sb::HostValue;
@@ -488,6 +489,14 @@ int32_t sb_debug_lower(const uint8_t* model, size_t len, int32_t n_in, sb_value*
       std::memcpy(buf, out.data(), n);
       buf[n] = 0;
     }
+    return SB_STATUS_OK;
+  });
+}
+
+int32_t sb_debug_narrow_bf16(const float* src, uint16_t* dst, size_t n, int32_t threads) {
+  return guarded([&] {
+    SB_CHECK((src && dst) || n == 0, sb::SB_INVALID_ARGUMENT, "null buffer");
+    sb::host_narrow_bf16(dst, src, n, unsigned(std::max(1, threads)));
     return SB_STATUS_OK;
   });
 }

@@ -11,6 +11,8 @@
 #include <set>
 #include <thread>
 
+#include <immintrin.h>
+
 namespace sb {
 
 int debug_level() {
@@ -103,10 +105,10 @@ HostPool& pool() {
 // Parallel memcpy for large host copies: one piece of at least 4 MiB per thread, up to 16 threads
 // (one thread copies at ~14 GB/s on the B200 host; the staging copies of a pipelined Run, running
 // beside host->device transfers, measured 34 GB/s with 8 threads and 45 GB/s with 16).
-void par_memcpy(void* dst, const void* src, size_t n) {
+void par_memcpy(void* dst, const void* src, size_t n, unsigned max_threads = 16) {
   const size_t piece = size_t(4) << 20;
   const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-  const unsigned nt = unsigned(std::min<size_t>(std::min(16u, hw), n / piece));
+  const unsigned nt = unsigned(std::min<size_t>(std::min(std::max(1u, max_threads), hw), n / piece));
   if (nt <= 1) {
     std::memcpy(dst, src, n);
     return;
@@ -122,10 +124,9 @@ void par_memcpy(void* dst, const void* src, size_t n) {
   for (auto& t : th) t.join();
 }
 
-// float32 -> bfloat16 (round to nearest even; NaN stays NaN), n elements (vectorised by the compiler
-// at this optimisation level).
-__attribute__((optimize("O3"))) void f32_to_bf16_span(uint16_t* __restrict__ dst, const float* __restrict__ src,
-                                                       size_t n) {
+// float32 -> bfloat16 (round to nearest even; NaN stays NaN, quieted), n elements: the rounding the
+// device applies when it reads a float32 operand as bfloat16, so narrowing on the host is exact.
+void f32_to_bf16_scalar(uint16_t* __restrict__ dst, const float* __restrict__ src, size_t n) {
   for (size_t i = 0; i < n; ++i) {
     uint32_t u;
     std::memcpy(&u, src + i, 4);
@@ -135,11 +136,49 @@ __attribute__((optimize("O3"))) void f32_to_bf16_span(uint16_t* __restrict__ dst
   }
 }
 
-// The same over up to 16 threads (pieces of at least 1 Mi elements).
-void par_f32_to_bf16(uint16_t* dst, const float* src, size_t n) {
+// The same, 16 elements per step with AVX2, written with non-temporal stores: the destination is a
+// page-locked staging slot the copy engine reads next, so its lines are not read for ownership or
+// kept in the host caches (the narrowing of a 308 MB batch is bound by host memory traffic).
+__attribute__((target("avx2"))) inline __m256i bf16_round8(__m256i u) {
+  const __m256i r = _mm256_srli_epi32(_mm256_add_epi32(_mm256_add_epi32(u, _mm256_set1_epi32(0x7FFF)),
+                                                       _mm256_and_si256(_mm256_srli_epi32(u, 16), _mm256_set1_epi32(1))),
+                                      16);
+  const __m256i nan = _mm256_cmpgt_epi32(_mm256_and_si256(u, _mm256_set1_epi32(0x7FFFFFFF)), _mm256_set1_epi32(0x7F800000));
+  return _mm256_blendv_epi8(r, _mm256_or_si256(_mm256_srli_epi32(u, 16), _mm256_set1_epi32(0x40)), nan);
+}
+
+__attribute__((target("avx2"))) void f32_to_bf16_avx2(uint16_t* __restrict__ dst, const float* __restrict__ src,
+                                                       size_t n) {
+  size_t i = 0;
+  while (i < n && (reinterpret_cast<uintptr_t>(dst + i) & 31u)) {   // to a 32-byte destination boundary
+    f32_to_bf16_scalar(dst + i, src + i, 1);
+    ++i;
+  }
+  for (; i + 16 <= n; i += 16) {
+    const __m256i a = bf16_round8(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(src + i)));
+    const __m256i b = bf16_round8(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(src + i + 8)));
+    // packus interleaves the 128-bit halves: a0-3 b0-3 a4-7 b4-7 -> a0-7 b0-7
+    const __m256i p = _mm256_permute4x64_epi64(_mm256_packus_epi32(a, b), 0xD8);
+    _mm256_stream_si256(reinterpret_cast<__m256i*>(dst + i), p);
+  }
+  _mm_sfence();
+  if (i < n) f32_to_bf16_scalar(dst + i, src + i, n - i);
+}
+
+void f32_to_bf16_span(uint16_t* dst, const float* src, size_t n) {
+  static const bool avx2 = __builtin_cpu_supports("avx2");
+  if (avx2)
+    f32_to_bf16_avx2(dst, src, n);
+  else
+    f32_to_bf16_scalar(dst, src, n);
+}
+
+// The same over up to max_threads threads (pieces of at least 1 Mi elements).
+void par_f32_to_bf16(uint16_t* dst, const float* src, size_t n, unsigned max_threads = 16) {
   const size_t piece = size_t(1) << 20;
   const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-  const unsigned nt = unsigned(std::max<size_t>(1, std::min<size_t>(std::min(16u, hw), n / piece)));
+  const unsigned nt =
+      unsigned(std::max<size_t>(1, std::min<size_t>(std::min(std::max(1u, max_threads), hw), n / piece)));
   const size_t per = (n / nt + 63) / 64 * 64;
   std::vector<std::thread> th;
   for (unsigned i = 1; i < nt; ++i) {
@@ -156,6 +195,9 @@ void par_f32_to_bf16(uint16_t* dst, const float* src, size_t n) {
 void* host_alloc(size_t bytes, bool& pinned) { return pool().alloc(bytes, pinned); }
 void host_release(void* p, size_t bytes, bool pinned) { pool().release(p, bytes, pinned); }
 void host_copy(void* dst, const void* src, size_t n) { par_memcpy(dst, src, n); }
+void host_narrow_bf16(uint16_t* dst, const float* src, size_t n, unsigned threads) {
+  par_f32_to_bf16(dst, src, n, threads);
+}
 // True when p lies in page-locked host memory the CUDA runtime knows (cudaHostAlloc'd or
 // cudaHostRegister'ed), so a device transfer from it is asynchronous.
 bool host_is_page_locked(const void* p) {
@@ -533,17 +575,41 @@ Session::Pipeline::~Pipeline() {
 void Session::maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs) {
   if (ps.pipe_checked) return;
   ps.pipe_checked = true;
-  if (ps.sharded || ps.shards.size() != 1 || !ps.separable || ps.batch < 2) return;
+  if (!ps.separable || ps.batch < 2) return;
+  bool may_cut = true;
+  if (const char* e = std::getenv("SHOROKOO_B200_PIPELINE"))
+    if (e[0] == '0') may_cut = false;
+  // Every shard builds its pipeline on its own device (in parallel, like the shards' plans); the
+  // host staging copies of concurrent shards share the host's threads.
+  const size_t n = ps.shards.size();
+  const unsigned threads = std::max(2u, 16u / unsigned(n));
+  std::vector<std::shared_ptr<Pipeline>> pipes(n);
+  if (n == 1) {
+    pipes[0] = build_pipeline(ps, 0, inputs, may_cut, threads);
+  } else {
+    std::vector<std::thread> th;
+    for (size_t si = 0; si < n; ++si)
+      th.emplace_back([&, si] { pipes[si] = build_pipeline(ps, si, inputs, may_cut, threads); });
+    for (auto& t : th) t.join();
+  }
+  for (const auto& p : pipes)
+    if (!p) return;   // (a shard whose pipeline could not be set up: every shard runs unstaged)
+  ps.pipes = std::move(pipes);
+}
+
+std::shared_ptr<Session::Pipeline> Session::build_pipeline(PlanSet& ps, size_t si,
+                                                           const std::vector<std::shared_ptr<HostValue>>& inputs,
+                                                           bool may_cut, unsigned host_threads) {
+  const Shard& sh = ps.shards[si];
+  const int64_t rows_total = ps.sharded ? sh.count : ps.batch;
   // Below kPipeMinBytes of copies (in + out) they are too short to be worth hiding (at 32 MiB the
   // 8192-row MLP gains 30% end to end, 2.22 -> 1.71 ms per run). Chunks: two head
-  // chunks of an eighth of the batch, then two body chunks of the rest. The first chunk's copy is
+  // chunks of an eighth of the rows, then two body chunks of the rest. The first chunk's copy is
   // the one nothing overlaps, so it is small; each chunk's compute must outlast the next chunk's
   // copy, so sizes grow. Measured for ResNet-50 bs512 on B200 (device ms at batch 32 / 64 / 160 /
   // 192: 1.01 / 1.38 / 2.68 / 3.02; PCIe 10.85 us per image): 64 + 64 + 192 + 192 models 9.6 ms
   // per run against 10.2 ms for the earlier 32 + 3 x 160.
   constexpr size_t kPipeMinBytes = size_t(32) << 20;
-  if (const char* e = std::getenv("SHOROKOO_B200_PIPELINE"))
-    if (e[0] == '0') return;
   // (input and output copies both overlap the chunks' kernels: outputs such as a detector's dense
   // per-anchor maps can outweigh the inputs)
   size_t in_bytes = 0, out_bytes = 0;
@@ -551,123 +617,164 @@ void Session::maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_pt
     if (numel(v->shape) > kPlanTimeInputMaxElems) in_bytes += v->nbytes;
   for (size_t j = 0; j < ps.out_shapes.size(); ++j)
     if (!ps.out_host[j]) out_bytes += size_t(numel(ps.out_shapes[j])) * 4;
-  if (in_bytes + out_bytes < kPipeMinBytes || ps.batch < 8) return;
-  const int64_t head = std::max<int64_t>(1, ps.batch / 8);
+  in_bytes = size_t(double(in_bytes) * double(rows_total) / double(ps.batch));   // this shard's share
+  out_bytes = size_t(double(out_bytes) * double(rows_total) / double(ps.batch));
   auto P = std::make_shared<Pipeline>();
-  P->device = devices_[0];
-  if (out_bytes > in_bytes) {
-    // Output-bound (device->host copies outlast the kernels): once the first chunk's outputs start
-    // copying back the copy stream should never wait, and the last chunk's copy is the one nothing
-    // overlaps, so after two small chunks the rest goes in quarters (RetinaNet bs16: 2 + 2 + 4 +
-    // 4 + 4 took 825 MB of outputs back in about the time of the copy alone).
-    const int64_t quarter = std::max<int64_t>(1, ps.batch / 4);
-    const int64_t last = ps.batch - 2 * head - 2 * quarter;
-    if (last < 1) return;
-    P->rows = {head, head, quarter, quarter, last};
-  } else {
-    const int64_t body = (ps.batch - 2 * head) / 2;
-    if (body < head || body < 2) return;
-    P->rows = {head, head, body, ps.batch - 2 * head - body};
+  P->device = devices_[size_t(sh.device)];
+  P->host_threads = host_threads;
+  const int64_t head = std::max<int64_t>(1, rows_total / 8);
+  if (may_cut && in_bytes + out_bytes >= kPipeMinBytes && rows_total >= 8) {
+    if (out_bytes > in_bytes) {
+      // Output-bound (device->host copies outlast the kernels): once the first chunk's outputs start
+      // copying back the copy stream should never wait, and the last chunk's copy is the one nothing
+      // overlaps, so after two small chunks the rest goes in quarters (RetinaNet bs16: 2 + 2 + 4 +
+      // 4 + 4 took 825 MB of outputs back in about the time of the copy alone).
+      const int64_t quarter = std::max<int64_t>(1, rows_total / 4);
+      const int64_t last = rows_total - 2 * head - 2 * quarter;
+      if (last >= 1) P->rows = {head, head, quarter, quarter, last};
+    } else {
+      const int64_t body = (rows_total - 2 * head) / 2;
+      if (body >= head && body >= 2) P->rows = {head, head, body, rows_total - 2 * head - body};
+    }
   }
+  cudaStream_t cs = streams_[size_t(sh.device)];
   try {
     ck(cudaSetDevice(P->device), "cudaSetDevice");
-    auto build = [&](int64_t n) {
-      LGraph g = lower(model_, specs_for(inputs, 0, n, true));
-      auto plan = std::make_shared<Plan>(std::move(g), P->device, sm_counts_[0], precision_);
-      const auto& outs = plan->outputs();
-      for (size_t j = 0; j < outs.size(); ++j)
-        if (!outs[j].host && (outs[j].shape.empty() || outs[j].shape[0] != n || ps.out_shapes[j].empty() ||
-                              ps.out_shapes[j][0] != ps.batch))
-          return std::shared_ptr<Plan>();   // an output is not cut along the batch
-      return plan;
-    };
-    std::vector<std::pair<int64_t, std::shared_ptr<Plan>>> built;   // one plan per distinct size
-    for (int64_t n : P->rows) {
-      std::shared_ptr<Plan> plan;
-      for (const auto& kv : built)
-        if (kv.first == n) plan = kv.second;
-      if (!plan) {
-        plan = build(n);
-        if (!plan) return;   // keep the single full-batch plan
-        built.emplace_back(n, plan);
-      }
-      P->plans.push_back(plan);
-    }
-    size_t big = 0;   // the largest chunk: its plan's bindings size the staging slots
-    for (size_t c = 1; c < P->rows.size(); ++c)
-      if (P->rows[c] > P->rows[big]) big = c;
+    ck(cudaStreamCreateWithFlags(&P->copy, cudaStreamNonBlocking), "cudaStreamCreate");
+    ck(cudaStreamCreateWithFlags(&P->d2h, cudaStreamNonBlocking), "cudaStreamCreate");
     for (int slot = 0; slot < 2; ++slot) {
-      for (const auto& b : P->plans[big]->inputs()) {
-        void* d = nullptr;
-        ck(cudaMalloc(&d, std::max<size_t>(b.bytes, 16)), "cudaMalloc (pipeline staging)");
-        P->staging[slot].push_back(d);
-      }
-      const auto& louts = P->plans[big]->outputs();
-      for (size_t j = 0; j < louts.size(); ++j) {
-        void* d = nullptr;
-        if (!louts[j].host)
-          ck(cudaMalloc(&d, std::max<size_t>(size_t(numel(louts[j].shape)) * 4, 16)), "cudaMalloc (output staging)");
-        P->out_staging[slot].push_back(d);
-      }
       ck(cudaEventCreateWithFlags(&P->h2d_done[slot], cudaEventDisableTiming), "event");
       ck(cudaEventCreateWithFlags(&P->consumed[slot], cudaEventDisableTiming), "event");
       ck(cudaEventCreateWithFlags(&P->out_ready[slot], cudaEventDisableTiming), "event");
       ck(cudaEventCreateWithFlags(&P->out_free[slot], cudaEventDisableTiming), "event");
     }
-    ck(cudaStreamCreateWithFlags(&P->copy, cudaStreamNonBlocking), "cudaStreamCreate");
-    ck(cudaStreamCreateWithFlags(&P->d2h, cudaStreamNonBlocking), "cudaStreamCreate");
-    // Keep the pipeline only where it pays: small chunks leave SMs idle (a 64-image ResNet-50
-    // batch cut into 8 + 8 + 24 + 24 ran 2.70 ms end to end against 2.03 ms unpipelined), so the
-    // schedule is simulated with measured chunk kernel times and the measured copy rate against
-    // one copy in, the full-batch kernels and one copy out.
-    const double t_full = ps.shards[0].plan->time_kernels(streams_[0], 3);
-    std::vector<double> t_chunk;
-    for (size_t c = 0; c < P->rows.size(); ++c) {
-      double t = -1;
-      for (size_t c2 = 0; c2 < c; ++c2)
-        if (P->plans[c2] == P->plans[c]) t = t_chunk[c2];
-      t_chunk.push_back(t >= 0 ? t : P->plans[c]->time_kernels(streams_[0], 3));
+    if (!P->rows.empty()) {
+      auto build = [&](int64_t n) {
+        LGraph g = lower(model_, specs_for(inputs, 0, n, true));
+        auto plan = std::make_shared<Plan>(std::move(g), P->device, sm_counts_[size_t(sh.device)], precision_);
+        const auto& outs = plan->outputs();
+        for (size_t j = 0; j < outs.size(); ++j)
+          if (!outs[j].host && (outs[j].shape.empty() || outs[j].shape[0] != n || ps.out_shapes[j].empty() ||
+                                ps.out_shapes[j][0] != ps.batch))
+            return std::shared_ptr<Plan>();   // an output is not cut along the batch
+        return plan;
+      };
+      std::vector<std::pair<int64_t, std::shared_ptr<Plan>>> built;   // one plan per distinct size
+      for (int64_t n : P->rows) {
+        std::shared_ptr<Plan> plan;
+        for (const auto& kv : built)
+          if (kv.first == n) plan = kv.second;
+        if (!plan) {
+          plan = build(n);
+          if (!plan) break;
+          built.emplace_back(n, plan);
+        }
+        P->plans.push_back(plan);
+      }
+      if (P->plans.size() != P->rows.size()) {
+        P->rows.clear();
+        P->plans.clear();
+      }
     }
-    const double ms_per_byte = copy_ms_per_byte(P->copy);
-    const double rows = double(ps.batch);
-    double copy_end = 0, comp_end = 0, back_end = 0;
-    std::vector<double> comp_ends;
-    for (size_t c = 0; c < P->rows.size(); ++c) {
-      const double share = double(P->rows[c]) / rows;
-      double start = copy_end;
-      if (c >= 2) start = std::max(start, comp_ends[c - 2]);   // its staging slot is free
-      copy_end = start + share * double(in_bytes) * ms_per_byte;
-      comp_end = std::max(comp_end, copy_end) + t_chunk[c];
-      comp_ends.push_back(comp_end);
-      back_end = std::max(back_end, comp_end) + share * double(out_bytes) * ms_per_byte;
+    if (!P->rows.empty()) {
+      // Keep the cut only where it pays: small chunks leave SMs idle (a 64-image ResNet-50 batch
+      // cut into 8 + 8 + 24 + 24 ran 2.70 ms end to end against 2.03 ms unpipelined), so the
+      // schedule is simulated with measured chunk kernel times and the measured copy rate against
+      // one copy in, the whole shard's kernels and one copy out.
+      const double t_full = sh.plan->time_kernels(cs, 3);
+      std::vector<double> t_chunk;
+      for (size_t c = 0; c < P->rows.size(); ++c) {
+        double t = -1;
+        for (size_t c2 = 0; c2 < c; ++c2)
+          if (P->plans[c2] == P->plans[c]) t = t_chunk[c2];
+        t_chunk.push_back(t >= 0 ? t : P->plans[c]->time_kernels(cs, 3));
+      }
+      const double ms_per_byte = copy_ms_per_byte(P->copy);
+      const double rows = double(rows_total);
+      double copy_end = 0, comp_end = 0, back_end = 0;
+      std::vector<double> comp_ends;
+      for (size_t c = 0; c < P->rows.size(); ++c) {
+        const double share = double(P->rows[c]) / rows;
+        double start = copy_end;
+        if (c >= 2) start = std::max(start, comp_ends[c - 2]);   // its staging slot is free
+        copy_end = start + share * double(in_bytes) * ms_per_byte;
+        comp_end = std::max(comp_end, copy_end) + t_chunk[c];
+        comp_ends.push_back(comp_end);
+        back_end = std::max(back_end, comp_end) + share * double(out_bytes) * ms_per_byte;
+      }
+      const double t_seq = double(in_bytes + out_bytes) * ms_per_byte + t_full;
+      if (debug_level() >= 1)
+        std::fprintf(stderr, "[shorokoo_b200] pipeline model: %.3f ms pipelined vs %.3f ms in one piece (device %d)\n",
+                     back_end, t_seq, P->device);
+      if (back_end >= 0.97 * t_seq) {
+        P->rows.clear();
+        P->plans.clear();
+      }
     }
-    const double t_seq = double(in_bytes + out_bytes) * ms_per_byte + t_full;
-    if (debug_level() >= 1)
-      std::fprintf(stderr, "[shorokoo_b200] pipeline model: %.3f ms pipelined vs %.3f ms in one piece\n", back_end,
-                   t_seq);
-    if (back_end >= 0.97 * t_seq) return;
+    if (P->rows.empty()) {   // one chunk: the shard's own plan
+      P->rows = {rows_total};
+      P->plans = {sh.plan};
+    }
+    // device staging: per chunk slot and input binding (a one-chunk pipeline copies straight into
+    // the plan's buffers and stages only inputs that may travel as bf16, at their bf16 size)
+    const bool one = P->rows.size() == 1;
+    size_t big = 0;   // the largest chunk: its plan's bindings size the staging slots
+    for (size_t c = 1; c < P->rows.size(); ++c)
+      if (P->rows[c] > P->rows[big]) big = c;
+    for (int slot = 0; slot < (one ? 1 : 2); ++slot) {
+      for (const auto& b : P->plans[big]->inputs()) {
+        void* d = nullptr;
+        const size_t bytes = one ? (b.bf16_ok ? b.bytes / 2 : 0) : b.bytes;
+        if (bytes) ck(cudaMalloc(&d, std::max<size_t>(bytes, 16)), "cudaMalloc (pipeline staging)");
+        P->staging[slot].push_back(d);
+      }
+      const auto& louts = P->plans[big]->outputs();
+      for (size_t j = 0; j < louts.size(); ++j) {
+        void* d = nullptr;
+        if (!louts[j].host && !one)
+          ck(cudaMalloc(&d, std::max<size_t>(size_t(numel(louts[j].shape)) * 4, 16)), "cudaMalloc (output staging)");
+        P->out_staging[slot].push_back(d);
+      }
+    }
   } catch (const Error& e) {
     if (debug_level() >= 1) std::fprintf(stderr, "[shorokoo_b200] no micro-batch pipeline: %s\n", e.what());
-    return;
+    return nullptr;
   }
   if (debug_level() >= 1) {
     std::string sched;
     for (size_t c = 0; c < P->rows.size(); ++c) sched += (c ? " + " : "") + std::to_string(P->rows[c]);
-    std::fprintf(stderr, "[shorokoo_b200] run pipeline: %zu chunks of %s rows\n", P->rows.size(), sched.c_str());
+    if (P->rows.size() > 1)
+      std::fprintf(stderr, "[shorokoo_b200] run pipeline: %zu chunks of %s rows (device %d)\n", P->rows.size(),
+                   sched.c_str(), P->device);
+    else
+      std::fprintf(stderr, "[shorokoo_b200] run staging: one piece of %s rows (device %d)\n", sched.c_str(), P->device);
   }
-  ps.pipe = P;
+  return P;
 }
 
-void Session::run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs,
+// The pipelines run when they cut a shard into chunks, or when an input sits in pageable memory
+// (staged through page-locked memory either way).
+bool Session::use_pipelines(const PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs) const {
+  if (ps.pipes.empty()) return false;
+  for (const auto& p : ps.pipes)
+    if (p->rows.size() > 1) return true;
+  for (const auto& v : inputs)
+    if (numel(v->shape) > kPlanTimeInputMaxElems && !v->pinned && !v->dev) return true;
+  return false;
+}
+
+void Session::run_pipelined(PlanSet& ps, size_t si, const std::vector<std::shared_ptr<HostValue>>& inputs,
                             const std::vector<std::shared_ptr<HostValue>>& outs) {
-  Pipeline& P = *ps.pipe;
+  Pipeline& P = *ps.pipes[si];
+  const Shard& sh = ps.shards[si];
   ck(cudaSetDevice(P.device), "cudaSetDevice");
-  cudaStream_t cs = streams_[0];
+  cudaStream_t cs = streams_[size_t(sh.device)];
+  const bool one = P.rows.size() == 1;
   using clk = std::chrono::steady_clock;
   const auto t_run = clk::now();
   double ms_copy = 0, ms_wait = 0;   // host time in staging copies / waiting for staging slots
   std::vector<void*> hout(outs.size(), nullptr);
-  int64_t r0 = 0;   // first batch row of the chunk
+  int64_t r0 = ps.sharded ? sh.begin : 0;   // first batch row of the chunk
   for (size_t c = 0; c < P.rows.size(); r0 += P.rows[c], ++c) {
     Plan& plan = *P.plans[c];
     const auto& binds = plan.inputs();
@@ -703,13 +810,14 @@ void Session::run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostV
         const auto t0 = clk::now();
         if (narrow)
           par_f32_to_bf16(static_cast<uint16_t*>(P.host_staging[slot][bi]), reinterpret_cast<const float*>(src),
-                          binds[bi].bytes / 4);
+                          binds[bi].bytes / 4, P.host_threads);
         else
-          par_memcpy(P.host_staging[slot][bi], src, binds[bi].bytes);
+          par_memcpy(P.host_staging[slot][bi], src, binds[bi].bytes, P.host_threads);
         ms_copy += std::chrono::duration<double, std::milli>(clk::now() - t0).count();
         src = static_cast<const uint8_t*>(P.host_staging[slot][bi]);
       }
-      ck(cudaMemcpyAsync(P.staging[slot][bi], src, xfer, cudaMemcpyHostToDevice, P.copy), "H2D");
+      void* dst = (one && !narrow) ? plan.buffer_ptr(binds[bi].buf) : P.staging[slot][bi];
+      ck(cudaMemcpyAsync(dst, src, xfer, cudaMemcpyHostToDevice, P.copy), "H2D");
     }
     ck(cudaEventRecord(P.h2d_done[slot], P.copy), "event record");
     ck(cudaStreamWaitEvent(cs, P.h2d_done[slot], 0), "stream wait");
@@ -717,7 +825,7 @@ void Session::run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostV
       if (narrowed[bi])
         ck(k::bf16_to_f32(P.staging[slot][bi], plan.buffer_ptr(binds[bi].buf), int64_t(binds[bi].bytes / 4), cs),
            "bf16 widening");
-      else
+      else if (!one)
         ck(cudaMemcpyAsync(plan.buffer_ptr(binds[bi].buf), P.staging[slot][bi], binds[bi].bytes,
                            cudaMemcpyDeviceToDevice, cs),
            "D2D");
@@ -725,22 +833,24 @@ void Session::run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostV
     ck(cudaEventRecord(P.consumed[slot], cs), "event record");
     plan.enqueue_kernels(cs);
     // outputs: into output slot `slot` on the compute stream (once its previous host copy is done),
-    // then to the host on the d2h stream, overlapping the next chunks
+    // then to the host on the d2h stream, overlapping the next chunks (one chunk: straight from the
+    // plan's output buffers)
     if (c >= 2) ck(cudaStreamWaitEvent(cs, P.out_free[slot], 0), "stream wait");
     for (size_t j = 0; j < outs.size(); ++j) {
       hout[j] = nullptr;
       if (!outs[j] || ps.out_host[j]) continue;
       const size_t row = outs[j]->nbytes / size_t(std::max<int64_t>(ps.out_shapes[j][0], 1));
       hout[j] = static_cast<uint8_t*>(outs[j]->data) + size_t(r0) * row;
-      ck(cudaMemcpyAsync(P.out_staging[slot][j], plan.output_ptr(j), row * size_t(P.rows[c]),
-                         cudaMemcpyDeviceToDevice, cs),
-         "D2D (outputs)");
+      if (!one)
+        ck(cudaMemcpyAsync(P.out_staging[slot][j], plan.output_ptr(j), row * size_t(P.rows[c]),
+                           cudaMemcpyDeviceToDevice, cs),
+           "D2D (outputs)");
     }
     ck(cudaEventRecord(P.out_ready[slot], cs), "event record");
     ck(cudaStreamWaitEvent(P.d2h, P.out_ready[slot], 0), "stream wait");
     for (size_t j = 0; j < outs.size(); ++j)
       if (hout[j])
-        ck(cudaMemcpyAsync(hout[j], P.out_staging[slot][j],
+        ck(cudaMemcpyAsync(hout[j], one ? plan.output_ptr(j) : P.out_staging[slot][j],
                            outs[j]->nbytes / size_t(std::max<int64_t>(ps.out_shapes[j][0], 1)) * size_t(P.rows[c]),
                            cudaMemcpyDeviceToHost, P.d2h),
            "D2H");
@@ -751,9 +861,10 @@ void Session::run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostV
   ck(cudaStreamSynchronize(P.copy), "stream synchronize");
   ck(cudaStreamSynchronize(P.d2h), "stream synchronize");
   if (debug_level() >= 2)
-    std::fprintf(stderr, "[shorokoo_b200] pipelined run: %.3f ms (all enqueued at %.3f ms; host staging copies %.3f ms, "
-                 "waits for staging slots %.3f ms)\n",
-                 std::chrono::duration<double, std::milli>(clk::now() - t_run).count(), ms_enqueued, ms_copy, ms_wait);
+    std::fprintf(stderr, "[shorokoo_b200] pipelined run (device %d): %.3f ms (all enqueued at %.3f ms; host staging "
+                 "copies %.3f ms, waits for staging slots %.3f ms)\n",
+                 P.device, std::chrono::duration<double, std::milli>(clk::now() - t_run).count(), ms_enqueued, ms_copy,
+                 ms_wait);
   for (size_t c = 0; c < P.plans.size(); ++c)
     if (c == 0 || P.plans[c] != P.plans[c - 1]) P.plans[c]->check_device_error();
 }
@@ -851,7 +962,8 @@ std::vector<std::shared_ptr<HostValue>> Session::run(const std::vector<std::shar
   // A pipelined run copies each chunk's outputs back while later chunks still copy in and compute:
   // a copy into pageable memory would block the host until the chunk is done, serialising the
   // pipeline, so those outputs are page-locked whatever their size.
-  const bool pin_outputs = ps->pipe != nullptr;
+  const bool pipes = use_pipelines(*ps, inputs);
+  const bool pin_outputs = pipes;
   for (size_t j = 0; j < nout; ++j) {
     if (!wanted[j]) continue;
     if (ps->out_host[j]) {
@@ -862,8 +974,29 @@ std::vector<std::shared_ptr<HostValue>> Session::run(const std::vector<std::shar
       outs[j] = HostValue::alloc_tensor(DT_FLOAT, ps->out_shapes[j], pin_outputs);
     }
   }
-  if (ps->pipe) {
-    run_pipelined(*ps, inputs, outs);
+  if (pipes) {
+    if (ps->pipes.size() == 1) {
+      run_pipelined(*ps, 0, inputs, outs);
+    } else {   // one host thread per device
+      std::vector<std::string> errs(ps->pipes.size());
+      std::vector<int32_t> codes(ps->pipes.size(), 0);
+      std::vector<std::thread> th;
+      for (size_t si = 0; si < ps->pipes.size(); ++si)
+        th.emplace_back([&, si] {
+          try {
+            run_pipelined(*ps, si, inputs, outs);
+          } catch (const Error& e) {
+            errs[si] = e.what();
+            codes[si] = e.code;
+          } catch (const std::exception& e) {
+            errs[si] = e.what();
+            codes[si] = SB_INTERNAL;
+          }
+        });
+      for (auto& t : th) t.join();
+      for (size_t si = 0; si < errs.size(); ++si)
+        if (codes[si]) fail(codes[si], errs[si]);
+    }
     std::vector<std::shared_ptr<HostValue>> res;
     for (int j : out_idx) res.push_back(outs[size_t(j)]);
     return res;
@@ -963,7 +1096,7 @@ std::pair<int64_t, int64_t> Session::transfer_bytes(const std::vector<std::share
   for (const auto& sh : ps->shards)
     for (const auto& b : sh.plan->inputs()) {
       const HostValue& v = *inputs[size_t(b.index)];
-      const bool narrow = ps->pipe && !v.pinned && !v.dev && b.bf16_ok && v.elem_type == DT_FLOAT;
+      const bool narrow = !ps->pipes.empty() && !v.pinned && !v.dev && b.bf16_ok && v.elem_type == DT_FLOAT;
       h2d += int64_t(narrow ? b.bytes / 2 : b.bytes);
     }
   for (size_t j = 0; j < ps->out_shapes.size(); ++j)

@@ -78,14 +78,17 @@ class Session {
     int64_t begin, count;   // batch rows
     std::shared_ptr<Plan> plan;
   };
-  // Single-device micro-batch pipeline for run(): the batch is cut into a small head chunk and
-  // three equal body chunks (rows[0], rows[1..3]), each running through a plan built for its size.
-  // Chunk c is copied host->device on the copy stream into staging slot c % 2 while chunk c-1
-  // computes; the compute stream then moves it into the plan's input buffers (device->device),
-  // runs the kernels and copies the chunk's outputs back. The small head keeps the one copy that
-  // nothing overlaps short.
+  // Micro-batch pipeline of one shard for run() (every shard has its own, on its own device): the
+  // shard's rows are cut into small head chunks and larger body chunks (rows), each running
+  // through a plan built for its size. Chunk c is copied host->device on the copy stream into
+  // staging slot c % 2 while chunk c-1 computes; the compute stream then moves it into the plan's
+  // input buffers (device->device), runs the kernels and copies the chunk's outputs back. The small
+  // head keeps the one copy that nothing overlaps short. A one-chunk pipeline (rows = {shard rows},
+  // the shard's own plan) is what a run with inputs in pageable memory takes when cutting does not
+  // pay: it still stages them through page-locked memory (and narrows float32 read as bf16).
   struct Pipeline {
-    int device = 0;
+    int device = 0;                            // CUDA device ordinal
+    unsigned host_threads = 16;                // threads of the host staging copies
     std::vector<int64_t> rows;                 // chunk sizes, in batch order
     std::vector<std::shared_ptr<Plan>> plans;  // plan of each chunk (chunks of one size share it)
     std::vector<void*> staging[2];                // per plan input binding
@@ -115,7 +118,7 @@ class Session {
     int64_t batch = -1;        // common leading dimension of the device inputs (-1 none, -2 mixed)
     bool separable = false;    // the graph treats batch rows independently
     bool pipe_checked = false;
-    std::shared_ptr<Pipeline> pipe;
+    std::vector<std::shared_ptr<Pipeline>> pipes;   // one per shard, or none
   };
 
   OnnxModel model_;
@@ -130,9 +133,12 @@ class Session {
 
   std::shared_ptr<PlanSet> get_plans(const std::vector<std::shared_ptr<HostValue>>& inputs);
   void maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs);
+  std::shared_ptr<Pipeline> build_pipeline(PlanSet& ps, size_t si, const std::vector<std::shared_ptr<HostValue>>& inputs,
+                                           bool may_cut, unsigned host_threads);
+  bool use_pipelines(const PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs) const;
   void run_shards(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs,
                   const std::vector<std::shared_ptr<HostValue>>& outs);
-  void run_pipelined(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs,
+  void run_pipelined(PlanSet& ps, size_t si, const std::vector<std::shared_ptr<HostValue>>& inputs,
                      const std::vector<std::shared_ptr<HostValue>>& outs);
   std::vector<InputSpec> specs_for(const std::vector<std::shared_ptr<HostValue>>& inputs, int64_t batch_begin,
                                    int64_t batch_count, bool shard) const;
