@@ -37,6 +37,7 @@ WORKLOADS = {
     "mlp": ("mlp", 8192),
     "stacked_linear": ("stacked_linear", 4096),
     "retinanet": ("retinanet", 16),
+    "retinanet_gn": ("retinanet_gn", 16),   # adjacent model: GroupNorm heads (RetinaNetResNet50)
 }
 METRIC = "ResNet-50 images/sec at 1/2/4/8 B200; % tensor-pipe peak; vs ORT CPU"
 
@@ -332,7 +333,7 @@ def main():
         }
         if world == 1 and not args.no_cpu_baseline:
             try:
-                sample = 1 if name == "retinanet" else min(8, total)   # (RetinaNet: ~15 s per image on CPU)
+                sample = 1 if name.startswith("retinanet") else min(8, total)   # (RetinaNet: ~15 s per image on CPU)
                 line["cpu_baseline"], ref = cpu_baseline(case, sample=sample)
                 gate = 1e-2 if args.precision == "bf16" else 2e-3
                 errs = {}

@@ -10,6 +10,8 @@
 //    coarser map (FPN top-down add, RetinaNetDetector.cs:375-384,401-450).
 //  MatMul(x, W^T constant) / Gemm -> (+bias) -> [Relu|Sigmoid]  => FusedGemm
 //    (Linear, src/Shorokoo.Modules/Layers/Linear.cs:25-39; DenseBasic, ResNet.cs:102-125).
+//  Reshape -> ReduceMean -> Sub / Mul / ReduceMean / Add(eps) / Sqrt / Div -> Reshape
+//    -> (per-channel Mul|Add) -> [Relu]                           => GroupNorm (fuse_group_norms)
 //
 // A fused op takes the slot of the last op it absorbed, so operands that the original graph
 // computes later (e.g. the projection shortcut of a bottleneck) are ready when it runs.
@@ -210,6 +212,148 @@ static void push_activation_into_producers(LGraph& g) {
     if (!ok || producers.empty()) continue;
     for (int pi : producers) g.ops[size_t(pi)].act = e.type == "Sigmoid" ? 2 : 1;
     e.type = "Identity";
+  }
+}
+
+// GroupNorm written out in primitives, as the exporter emits RetGroupNorm
+// (samples/RetinaNet/RetinaNetDetector.cs:337-372) and the GroupNorm layer
+// (src/Shorokoo.Modules/Layers/Normalization.cs:278-310):
+//   xr  = Reshape(x [N, C, H, W] -> [N, G, ...])       (a split of the channel axis)
+//   mu  = ReduceMean(xr, axes 2.., keepdims)
+//   d_i = Sub(xr, mu)                                   (one or more such nodes)
+//   var = ReduceMean(Mul(d_a, d_b), axes 2.., keepdims)
+//   y   = Reshape(Div(d_c, Sqrt(Add(var, eps))) -> [N, C, H, W])
+//   then per-channel Mul / Add / Sub / Div by constants (gamma, beta) and an optional Relu
+// => GroupNorm(x): group = G, alpha = eps, weight / bias = the per-channel scale and shift, act.
+static void fuse_group_norms(LGraph& g) {
+  for (size_t mi = 0; mi < g.ops.size(); ++mi) {
+    if (g.ops[mi].dead || g.ops[mi].type != "ReduceMean" || !g.ops[mi].keepdims) continue;
+    Consumers C = consumers(g);
+    const Op m1 = g.ops[mi];
+    const int xr = m1.in[0];
+    const Value& xrv = g.vals[size_t(xr)];
+    if (xrv.producer < 0 || C.is_output[size_t(xr)]) continue;
+    const int r1i = xrv.producer;
+    const Op& r1 = g.ops[size_t(r1i)];
+    if (r1.dead || r1.type != "Reshape") continue;
+    const int x = r1.in[0];
+    const Value& xv = g.vals[size_t(x)];
+    if (xv.is_host || xv.shape.size() != 4) continue;
+    const int64_t N = xv.shape[0], Ch = xv.shape[1], H = xv.shape[2], W = xv.shape[3];
+    const auto& rs = xrv.shape;
+    if (rs.size() < 3 || rs[0] != N || rs[1] < 1 || Ch % rs[1] != 0) continue;
+    const int64_t G = rs[1];
+    int64_t rest = 1;
+    for (size_t i = 2; i < rs.size(); ++i) rest *= rs[i];
+    if (rest != (Ch / G) * H * W) continue;
+    // the reduced axes are exactly 2 .. rank-1
+    bool ok = m1.axes.size() == rs.size() - 2;
+    for (size_t i = 0; ok && i < m1.axes.size(); ++i) ok = m1.axes[i] == int64_t(i + 2);
+    if (!ok) continue;
+    const int mu = m1.out[0];
+    if (C.is_output[size_t(mu)]) continue;
+    // mu feeds only Sub(xr, mu) nodes; xr feeds only m1 and those
+    std::vector<int> subs, sub_outs;
+    for (int oi : C.ops[size_t(mu)]) {
+      const Op& o = g.ops[size_t(oi)];
+      if (o.type != "Sub" || o.in.size() != 2 || o.in[0] != xr || o.in[1] != mu) ok = false;
+      subs.push_back(oi);
+      sub_outs.push_back(o.out[0]);
+    }
+    if (!ok || subs.empty() || C.ops[size_t(xr)].size() != subs.size() + 1) continue;
+    auto is_sub_out = [&](int v) { return std::find(sub_outs.begin(), sub_outs.end(), v) != sub_outs.end(); };
+    // the square and the normalising division, reading only sub outputs
+    int sq = -1, dv = -1;
+    for (int so : sub_outs) {
+      if (C.is_output[size_t(so)]) ok = false;
+      for (int oi : C.ops[size_t(so)]) {
+        const Op& o = g.ops[size_t(oi)];
+        if (o.type == "Mul" && o.in.size() == 2 && is_sub_out(o.in[0]) && is_sub_out(o.in[1]) && (sq < 0 || sq == oi))
+          sq = oi;
+        else if (o.type == "Div" && o.in.size() == 2 && is_sub_out(o.in[0]) && (dv < 0 || dv == oi))
+          dv = oi;
+        else
+          ok = false;
+      }
+    }
+    if (!ok || sq < 0 || dv < 0) continue;
+    auto single = [&](int v) -> int {   // the one consumer of v (-1 when none, several or an output)
+      if (C.is_output[size_t(v)] || C.ops[size_t(v)].size() != 1) return -1;
+      return C.ops[size_t(v)][0];
+    };
+    const int m2 = single(g.ops[size_t(sq)].out[0]);
+    if (m2 < 0 || g.ops[size_t(m2)].type != "ReduceMean" || g.ops[size_t(m2)].axes != m1.axes ||
+        !g.ops[size_t(m2)].keepdims)
+      continue;
+    const int ad = single(g.ops[size_t(m2)].out[0]);
+    if (ad < 0 || g.ops[size_t(ad)].type != "Add" || g.ops[size_t(ad)].in.size() != 2) continue;
+    const Op& add = g.ops[size_t(ad)];
+    const int ev = add.in[0] == g.ops[size_t(m2)].out[0] ? add.in[1] : add.in[0];
+    if (!g.vals[size_t(ev)].is_host || g.vals[size_t(ev)].host->numel() != 1) continue;
+    const double eps = g.vals[size_t(ev)].host->get_f64(0);
+    const int sr = single(add.out[0]);
+    if (sr < 0 || g.ops[size_t(sr)].type != "Sqrt") continue;
+    if (single(g.ops[size_t(sr)].out[0]) != dv || g.ops[size_t(dv)].in[1] != g.ops[size_t(sr)].out[0]) continue;
+    const int r2 = single(g.ops[size_t(dv)].out[0]);
+    if (r2 < 0 || g.ops[size_t(r2)].type != "Reshape" || g.vals[size_t(g.ops[size_t(r2)].out[0])].shape != xv.shape)
+      continue;
+    // per-channel affine and activation after the normalisation
+    std::vector<double> scale(size_t(Ch), 1.0), shift(size_t(Ch), 0.0);
+    int cur = g.ops[size_t(r2)].out[0];
+    int slot = r2;
+    std::vector<int> absorbed = {r1i, int(mi), sq, m2, ad, sr, dv, r2};
+    absorbed.insert(absorbed.end(), subs.begin(), subs.end());
+    int act = 0;
+    while (true) {
+      const int oi = single(cur);
+      if (oi < 0) break;
+      const Op& o = g.ops[size_t(oi)];
+      if ((o.type == "Mul" || o.type == "Add" || o.type == "Sub" || o.type == "Div") && o.in.size() == 2 && act == 0) {
+        const bool cur_first = o.in[0] == cur;
+        const Value& ov = g.vals[size_t(cur_first ? o.in[1] : o.in[0])];
+        std::vector<double> v;
+        if (!ov.is_host || !per_axis_values(*ov.host, 4, 1, Ch, v) || g.vals[size_t(o.out[0])].shape != xv.shape) break;
+        if ((o.type == "Sub" || o.type == "Div") && !cur_first) break;
+        for (int64_t c = 0; c < Ch; ++c) {
+          const double k = v[size_t(c)];
+          if (o.type == "Mul") {
+            scale[size_t(c)] *= k;
+            shift[size_t(c)] *= k;
+          } else if (o.type == "Add") {
+            shift[size_t(c)] += k;
+          } else if (o.type == "Sub") {
+            shift[size_t(c)] -= k;
+          } else {
+            scale[size_t(c)] /= k;
+            shift[size_t(c)] /= k;
+          }
+        }
+      } else if (o.type == "Relu" && act == 0) {
+        act = 1;
+      } else {
+        break;
+      }
+      absorbed.push_back(oi);
+      cur = o.out[0];
+      slot = oi;
+    }
+    Op f;
+    f.type = "GroupNorm";
+    f.name = m1.name;
+    f.in = {x};
+    f.out = {cur};
+    f.group = G;
+    f.alpha = float(eps);
+    f.act = act;
+    f.weight = std::make_shared<HostTensor>(DT_FLOAT, std::vector<int64_t>{Ch});
+    f.bias = std::make_shared<HostTensor>(DT_FLOAT, std::vector<int64_t>{Ch});
+    for (int64_t c = 0; c < Ch; ++c) {
+      f.weight->mptr<float>()[c] = float(scale[size_t(c)]);
+      f.bias->mptr<float>()[c] = float(shift[size_t(c)]);
+    }
+    for (int a : absorbed) g.ops[size_t(a)].dead = true;
+    g.vals[size_t(cur)].producer = slot;
+    g.ops[size_t(slot)] = f;
   }
 }
 
@@ -451,6 +595,7 @@ void fuse(LGraph& g) {
     g.ops[size_t(slot)] = f;
   }
   merge_projection_shortcuts(g);
+  fuse_group_norms(g);
   push_activation_into_producers(g);
   g.dce();
 }

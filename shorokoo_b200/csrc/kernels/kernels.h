@@ -187,6 +187,15 @@ cudaError_t to_rows_bf16(const void* src, int src_bf16, int64_t M, int64_t K, in
 cudaError_t maxpool_nhwc_bf16(const void* x, void* y, int N, int H, int W, int C, int Ho, int Wo, int kh,
                               int kw, int sh, int sw, int ph, int pw, int dh, int dw, cudaStream_t s);
 // NHWC (bf16 or f32 with C contiguous, pixel stride ldp) -> [N, C] mean or max, bf16 or f32 output.
+// Group normalisation over NHWC x [N, HW, ldc] (bf16 or fp32; C channels in G groups, C / G <= 64,
+// C a multiple of the 16-byte vector with C / vector dividing 256): y = act(((x - mean) * rstd) *
+// gamma + beta) per (n, group), stored with pitch ldy as bf16 (y_mode 0), fp32 on the TF32 grid (1)
+// or fp32 (2). Scratch: partial [N * per_img * 2 * C] and ab [N * 2 * C] floats (norm.cu).
+bool group_norm_supported(int C, int G, int x_bf16);
+int group_norm_blocks_per_image(int N, int64_t HW, int num_sms);
+cudaError_t group_norm(const void* x, int x_bf16, int N, int64_t HW, int C, int64_t ldc, int G, float eps,
+                       const float* gamma, const float* beta, void* y, int y_mode, int64_t ldy, int relu, int per_img,
+                       float* partial, float* ab, cudaStream_t s);
 cudaError_t global_pool_nhwc(const void* x, int x_bf16, int N, int HW, int C, int64_t ldp, void* y, int y_bf16,
                              int is_max, cudaStream_t s);
 // Generic strided copy with dtype conversion: dst[idx] = src[idx] over `shape`.

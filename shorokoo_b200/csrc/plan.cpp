@@ -259,8 +259,8 @@ void Plan::add_step(const std::string& kind, std::vector<DevTensor> reads, std::
 //   kStoreBf16   every reader is a bf16-operand contraction (operand, residual or second operand);
 //   kStoreTf32   every reader is a single-pass TF32 contraction: fp32 rounded to the TF32 grid;
 //   kStoreF32    anything else (generic ops, graph outputs, TF32x3 readers, mixed precisions).
-// Global pools read either dtype and add no constraint; a value whose readers add none takes
-// `pref`, the class of its producer's operands.
+// Global pools and group norms read either dtype and add no constraint; a value whose readers add
+// none takes `pref`, the class of its producer's operands.
 int Plan::storage_class(int v, int pref) const {
   if (is_output_[size_t(v)]) return kStoreF32;
   int cls = -1;
@@ -272,7 +272,7 @@ int Plan::storage_class(int v, int pref) const {
     const Op& op = g_.ops[size_t(oi)];
     if (op.type == "FusedConv" || op.type == "FusedGemm") {
       meet(op.prec == 0 ? kStoreBf16 : (op.prec == 1 ? kStoreTf32 : kStoreF32));
-    } else if (op.type == "GlobalAveragePool" || op.type == "GlobalMaxPool") {
+    } else if (op.type == "GlobalAveragePool" || op.type == "GlobalMaxPool" || op.type == "GroupNorm") {
       continue;
     } else if (op.type == "MaxPool" || (is_view_op(op.type) && op.in[0] == v)) {
       const int c = storage_class(op.out[0], -1);
@@ -945,6 +945,62 @@ void Plan::plan_global_pool(const Op& op) {
   });
 }
 
+// GroupNorm (fused from its primitives): reads its input NHWC in the dtype it is stored in (a conv
+// output: bf16, or fp32 for TF32 / TF32x3 convs) and writes what its readers take, so the
+// normalisation sits between two contractions at one read for the statistics and one read and one
+// write for the affine + ReLU pass.
+void Plan::plan_group_norm(const Op& op) {
+  const Value& xv = g_.vals[size_t(op.in[0])];
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  SB_CHECK(xv.shape.size() == 4, SB_UNSUPPORTED, "GroupNorm: rank-4 input required");
+  const int64_t N = xv.shape[0], C = xv.shape[1], H = xv.shape[2], W = xv.shape[3];
+  const int G = int(op.group);
+  const DevTensor& t = vt_[size_t(op.in[0])];
+  DevTensor x = t;
+  int64_t ldc = t.strides.size() == 4 ? t.strides[3] : 0;
+  const int vec = t.bf16 ? 8 : 4;
+  const bool nhwc = t.strides.size() == 4 && t.strides[1] == 1 && ldc >= C && (t.strides[2] == W * ldc || H == 1) &&
+                    (t.strides[0] == H * W * ldc || N == 1) && t.off % 16 == 0 && ldc % vec == 0 &&
+                    k::group_norm_supported(int(C), G, t.bf16);
+  if (!nhwc) {
+    ldc = round_up(C, 4);
+    x = as_nhwc_op(op.in[0], int(ldc), 2);
+  }
+  SB_CHECK(k::group_norm_supported(int(C), G, x.bf16) && ldc % (x.bf16 ? 8 : 4) == 0, SB_UNSUPPORTED,
+           "GroupNorm: " + std::to_string(C) + " channels in " + std::to_string(G) + " groups");
+  const int cls = storage_class(op.out[0], x.bf16 ? kStoreBf16 : kStoreF32);
+  const int ymode = cls == kStoreBf16 ? 0 : (cls == kStoreTf32 ? 1 : 2);
+  const int64_t ldy = round_up(C, 8);
+  DevTensor y = alloc_nhwc(yv.shape, ymode == 0, ldy);
+  vt_[size_t(op.out[0])] = y;
+  std::vector<float> gb(size_t(2 * C));
+  for (int64_t c = 0; c < C; ++c) {
+    gb[size_t(c)] = op.weight->ptr<float>()[c];
+    gb[size_t(C + c)] = op.bias->ptr<float>()[c];
+  }
+  DevTensor gbt;
+  gbt.buf = -1;
+  gbt.off = add_weight_bytes(gb.data(), gb.size() * 4);
+  const int per_img = k::group_norm_blocks_per_image(int(N), H * W, num_sms_);
+  DevTensor partial = alloc_contig({N * per_img * 2 * C}, false);
+  DevTensor ab = alloc_contig({N * 2 * C}, false);
+  const float eps = op.alpha;
+  const int relu = op.act == 1;
+  stats_.kernels += 2;   // (three launches: statistics, their merge, the normalisation)
+  add_step("group_norm " + std::to_string(C) + "/" + std::to_string(G), {x}, {y, partial, ab}, [=]() {
+    const void* xp = ptr(x);
+    const float* gp = static_cast<const float*>(ptr(gbt));
+    void* yp = ptr(y);
+    float* pp = static_cast<float*>(ptr(partial));
+    float* abp = static_cast<float*>(ptr(ab));
+    const int xb = x.bf16;
+    return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+      return k::group_norm(xp, xb, int(N), H * W, int(C), ldc, G, eps, gp, gp + C, yp, ymode, ldy, relu, per_img, pp,
+                           abp, s);
+    });
+  });
+}
+
 void Plan::plan_elementwise(const Op& op) {
   const Value& yv = g_.vals[size_t(op.out[0])];
   const int code = ew_code(op.type);
@@ -1310,6 +1366,7 @@ void Plan::build() {
     else if (t == "FusedGemm") plan_gemm(op);
     else if (t == "MaxPool") plan_maxpool(op);
     else if (t == "GlobalAveragePool" || t == "GlobalMaxPool") plan_global_pool(op);
+    else if (t == "GroupNorm") plan_group_norm(op);
     else if (is_view_op(t)) plan_view(op);
     else if (t == "Concat") plan_concat(op);
     else if (t == "Softmax") plan_softmax(op);

@@ -147,6 +147,7 @@ class Plan {
   void plan_gemm(const Op& op);
   void plan_maxpool(const Op& op);
   void plan_global_pool(const Op& op);
+  void plan_group_norm(const Op& op);
   void plan_elementwise(const Op& op);
   void plan_view(const Op& op);
   void plan_concat(const Op& op);

@@ -279,7 +279,7 @@ bool batch_separable(const LGraph& g) {
     int out = -2;
     const std::string& t = op.type;
     if (t == "FusedConv" || t == "MaxPool" || t == "GlobalAveragePool" || t == "GlobalMaxPool" ||
-        t == "AveragePool") {
+        t == "AveragePool" || t == "GroupNorm") {
       if (a0 != 0) return false;
       if (op.residual >= 0 && ax[size_t(op.residual)] != 0) return false;
       if (op.concat >= 0 && ax[size_t(op.concat)] != 0) return false;

@@ -593,11 +593,60 @@ class _SharedConv:
         return B.conv(x, self.w, self.b, 3, 1, auto_pad="SAME_UPPER")
 
 
+class _GroupNormParams:
+    """gamma / beta of one RetGroupNorm: ones / zeros (RetInitSimple :41-50, RetInitZeros :67-76),
+    perturbed by ``affine_scale`` for the parity tests; created once per head position and shared
+    by every pyramid level, like the head's convs (one head instance is called on each level)."""
+
+    def __init__(self, B: Builder, c: int, path: str, affine_scale: float = 0.0):
+        gv = np.ones(c, np.float32)
+        bv = np.zeros(c, np.float32)
+        if affine_scale:
+            gv = gv + (affine_scale * B.rng.standard_normal(c)).astype(np.float32)
+            bv = bv + (affine_scale * B.rng.standard_normal(c)).astype(np.float32)
+        self.c = c
+        self.gamma = B.init(gv, path + ".weight")
+        self.beta = B.init(bv, path + ".bias")
+
+
+def group_norm(B: Builder, x: str, num_groups: int, params: _GroupNormParams) -> str:
+    """RetGroupNorm (RetinaNetDetector.cs:337-372) as the exporter writes it: x [B, C, H, W] reshaped
+    to [B, G, C/G, H, W] through a runtime shape chain, ReduceMean over axes 2-4 (keepdims), the
+    biased variance as the mean of (x - mean) * (x - mean) (two Sub nodes, as the module writes
+    the difference twice), (x - mean) / Sqrt(var + 1e-5), reshaped back, times gamma reshaped to
+    [1, C, 1, 1] plus beta reshaped to [1, C, 1, 1]."""
+    n, c, hh, ww = B.shape[x]
+    bsz, hd, wd = B.dim(x, 0), B.dim(x, 2), B.dim(x, 3)
+    xr = B.op("Reshape", [x, B.vec([B.unsq(bsz), num_groups, c // num_groups, B.unsq(hd), B.unsq(wd)])])
+    B.shape[xr] = (n, num_groups, c // num_groups, hh, ww)
+    axes = B.const(np.array([2, 3, 4], np.int64))
+    mean = B.op("ReduceMean", [xr, axes], keepdims=1)
+    B.shape[mean] = (n, num_groups, 1, 1, 1)
+    d1, d2 = B.binary("Sub", xr, mean), B.binary("Sub", xr, mean)
+    var = B.op("ReduceMean", [B.binary("Mul", d1, d2), axes], keepdims=1)
+    B.shape[var] = (n, num_groups, 1, 1, 1)
+    eps = B.const(np.array(1e-5, np.float32))
+    B.shape[eps] = ()
+    den = B.unary("Sqrt", B.binary("Add", var, eps))
+    norm = B.binary("Div", B.binary("Sub", xr, mean), den)
+    y = B.op("Reshape", [norm, B.vec([B.unsq(bsz), c, B.unsq(hd), B.unsq(wd)])])
+    B.shape[y] = (n, c, hh, ww)
+    four = B.const(np.array([1, c, 1, 1], np.int64))
+    gamma = B.op("Reshape", [params.gamma, four])
+    beta = B.op("Reshape", [params.beta, four])
+    B.shape[gamma] = B.shape[beta] = (1, c, 1, 1)
+    return B.binary("Add", B.binary("Mul", y, gamma), beta)
+
+
 def retinanet(batch: int = 16, hw: Tuple[int, int] = (800, 1024), seed: int = 13, num_classes: int = 80,
               num_anchors: int = 9, fpn: int = 256, sigmoid: bool = True, affine_scale: float = 0.0,
               backbone_widths: Sequence[int] = (64, 128, 256, 512),
-              backbone_blocks: Sequence[int] = (3, 4, 6, 3), calibrate_bn: bool = False) -> ModelCase:
-    """RetinaNetResNet50NoNorm (RetinaNetDetector.cs:828-886) + Sigmoid on the class output.
+              backbone_blocks: Sequence[int] = (3, 4, 6, 3), calibrate_bn: bool = False,
+              norm_heads: bool = False, num_groups: int = 32) -> ModelCase:
+    """RetinaNetResNet50NoNorm (RetinaNetDetector.cs:828-886) + Sigmoid on the class output; with
+    ``norm_heads`` RetinaNetResNet50 (:957-971): the same backbone and FPN with the GroupNorm heads
+    RetClassificationHeadWithNorm / RetRegressionHeadWithNorm (:492-536, :578-642), each of the four
+    tower convs followed by RetGroupNorm (``num_groups`` groups of the 256 channels) and ReLU.
 
     The class-head bias starts at -ln(99) (focal-loss prior 0.01, RetInitClsBias :79-99). FPN convs are
     Kaiming-uniform(a=1) and head convs N(0, 0.01^2), the initialisation of the torchvision RetinaNet
@@ -651,10 +700,16 @@ def retinanet(batch: int = 16, hw: Tuple[int, int] = (800, 1024), seed: int = 13
                  for i in range(4)]
     reg_out = _SharedConv(B, fpn, num_anchors * 4, "reg.deltas", bias_scale=affine_scale)
 
-    def head(feat, convs, final, k):
+    cls_norms = [_GroupNormParams(B, fpn, f"cls.norm{i}", affine_scale) for i in range(4)] if norm_heads else None
+    reg_norms = [_GroupNormParams(B, fpn, f"reg.norm{i}", affine_scale) for i in range(4)] if norm_heads else None
+
+    def head(feat, convs, final, k, norms):
         v = feat
-        for c in convs:
-            v = B.unary("Relu", c(B, v))
+        for i, c in enumerate(convs):
+            v = c(B, v)
+            if norms:
+                v = group_norm(B, v, num_groups, norms[i])
+            v = B.unary("Relu", v)
         v = final(B, v)
         n, _, hh, ww = B.shape[v]
         bsz, hd, wd = B.dim(v, 0), B.dim(v, 2), B.dim(v, 3)
@@ -663,8 +718,8 @@ def retinanet(batch: int = 16, hw: Tuple[int, int] = (800, 1024), seed: int = 13
         B.shape[t] = (n, hh, ww, num_anchors, k)
         return t
 
-    cls = [head(p, cls_convs, cls_out, num_classes) for p in levels]
-    reg = [head(p, reg_convs, reg_out, 4) for p in levels]
+    cls = [head(p, cls_convs, cls_out, num_classes, cls_norms) for p in levels]
+    reg = [head(p, reg_convs, reg_out, 4, reg_norms) for p in levels]
     bsz = B.dim(cls[0], 0)
     cls = [B.op("Reshape", [c, B.vec([B.unsq(bsz), -1, num_classes])]) for c in cls]
     reg = [B.op("Reshape", [r, B.vec([B.unsq(bsz), -1, 4])]) for r in reg]
@@ -673,7 +728,8 @@ def retinanet(batch: int = 16, hw: Tuple[int, int] = (800, 1024), seed: int = 13
     if sigmoid:
         classifications = B.op("Sigmoid", [classifications])
     B.outputs += [W.ValueInfo(classifications), W.ValueInfo(regressions)]
-    return ModelCase("retinanet", B.model("RetinaNetResNet50NoNorm"), [(x, x_val)],
+    name = "RetinaNetResNet50" if norm_heads else "RetinaNetResNet50NoNorm"
+    return ModelCase("retinanet_gn" if norm_heads else "retinanet", B.model(name), [(x, x_val)],
                      [classifications, regressions], B.macs, B.params)
 
 
@@ -684,6 +740,8 @@ CONFIGS = {
     "resnet18": dict(fn=resnet, kwargs=dict(depth=18, batch=256, seed=7)),
     "resnet50": dict(fn=resnet, kwargs=dict(depth=50, batch=512, seed=11)),
     "retinanet": dict(fn=retinanet, kwargs=dict(batch=16, seed=13)),
+    # adjacent model: the GroupNorm-head detector (RetinaNetResNet50, 32 groups)
+    "retinanet_gn": dict(fn=retinanet, kwargs=dict(batch=16, seed=13, norm_heads=True)),
 }
 
 
