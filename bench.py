@@ -38,6 +38,7 @@ WORKLOADS = {
     "stacked_linear": ("stacked_linear", 4096),
     "retinanet": ("retinanet", 16),
     "retinanet_gn": ("retinanet_gn", 16),   # adjacent model: GroupNorm heads (RetinaNetResNet50)
+    "vit_base": ("vit_base", 1),            # adjacent model: ViT-B/16, batch 1 as its graph allows
 }
 METRIC = "ResNet-50 images/sec at 1/2/4/8 B200; % tensor-pipe peak; vs ORT CPU"
 
@@ -264,8 +265,9 @@ def main():
 
     # ---- roofline of the dominant kernel (tensor-core implicit GEMM), timed per launch ----
     prof = sess.profile(feeds, iters=3)
-    tc_ms = sum(v for k, v in prof if k.split()[0] in ("conv", "gemm"))
-    tc_launches = sum(1 for k, _ in prof if k.split()[0] in ("conv", "gemm"))
+    tc_kinds = ("conv", "gemm", "attention")   # the tcgen05 launches
+    tc_ms = sum(v for k, v in prof if k.split()[0] in tc_kinds)
+    tc_launches = sum(1 for k, _ in prof if k.split()[0] in tc_kinds)
     all_ms = sum(v for _, v in prof)
     peak_tflops, peak_hbm, peak_kind = measured_peaks()
     peak_note = f"{peak_kind} bf16 dense (burst)"

@@ -369,6 +369,23 @@ class Interpreter:
         one = v.dtype.type(1)
         return (one / (one + np.exp(-v))).astype(v.dtype)
 
+    def op_Gelu(self, n, x, env):
+        """ONNX Gelu (opset 20): approximate="none" x * Phi(x) with the error function, "tanh"
+        0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))) (ViTMlp, ViTNet.cs:217-239)."""
+        v = x[0]
+        approx = n.attr("approximate", b"none")
+        if isinstance(approx, bytes):
+            approx = approx.decode()
+        w = v.astype(np.float64)
+        if approx == "tanh":
+            y = 0.5 * w * (1.0 + np.tanh(math.sqrt(2.0 / math.pi) * (w + 0.044715 * w ** 3)))
+        else:
+            y = 0.5 * w * (1.0 + np.vectorize(math.erf)(w / math.sqrt(2.0)))
+        return y.astype(v.dtype)
+
+    def op_Tile(self, n, x, env):
+        return np.tile(x[0], [int(r) for r in x[1]])
+
     def op_Softmax(self, n, x, env):
         axis = n.attr("axis", -1)
         v = x[0]

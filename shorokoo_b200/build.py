@@ -38,6 +38,7 @@ def _sources():
 
 def _headers():
     return (glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "kernels", "*.h")) +
+            glob.glob(os.path.join(CSRC, "kernels", "*.cuh")) +
             glob.glob(os.path.join(INCLUDE, "*.h")))
 
 

@@ -12,6 +12,9 @@
 //    (Linear, src/Shorokoo.Modules/Layers/Linear.cs:25-39; DenseBasic, ResNet.cs:102-125).
 //  Reshape -> ReduceMean -> Sub / Mul / ReduceMean / Add(eps) / Sqrt / Div -> Reshape
 //    -> (per-channel Mul|Add) -> [Relu]                           => GroupNorm (fuse_group_norms)
+//  ReduceMean(last axis) -> Sub / Pow|Mul / ReduceMean / Add(eps) / Sqrt / Div -> (Mul|Add)
+//                                                                 => LayerNorm (fuse_layer_norms)
+//  MatMul(q, Transpose(k)) -> [scale] -> Softmax -> MatMul(., v)  => Attention (fuse_attention)
 //
 // A fused op takes the slot of the last op it absorbed, so operands that the original graph
 // computes later (e.g. the projection shortcut of a bottleneck) are ready when it runs.
@@ -243,6 +246,10 @@ static void fuse_group_norms(LGraph& g) {
     const auto& rs = xrv.shape;
     if (rs.size() < 3 || rs[0] != N || rs[1] < 1 || Ch % rs[1] != 0) continue;
     const int64_t G = rs[1];
+    // the kernel's shapes: channel groups of a power of two up to 32, channels in 16-byte vectors
+    // (other shapes keep the primitives)
+    const int64_t cpg = Ch / G;
+    if (cpg > 32 || (cpg & (cpg - 1)) != 0 || Ch % 8 != 0) continue;
     int64_t rest = 1;
     for (size_t i = 2; i < rs.size(); ++i) rest *= rs[i];
     if (rest != (Ch / G) * H * W) continue;
@@ -357,6 +364,184 @@ static void fuse_group_norms(LGraph& g) {
   }
 }
 
+// LayerNorm written out in primitives (ViTLayerNorm, samples/RetinaNet/ViTNet.cs:51-72):
+//   mu = ReduceMean(x, last axis, keepdims); d_i = Sub(x, mu); var = ReduceMean(Pow(d, 2) or
+//   Mul(d_a, d_b), last axis, keepdims); y = Div(d_c, Sqrt(Add(var, eps))); then Mul / Add / Sub /
+//   Div by constants varying along the last axis (gamma, beta)
+// => LayerNorm(x): alpha = eps, weight / bias = the per-feature scale and shift.
+static void fuse_layer_norms(LGraph& g) {
+  for (size_t mi = 0; mi < g.ops.size(); ++mi) {
+    if (g.ops[mi].dead || g.ops[mi].type != "ReduceMean" || !g.ops[mi].keepdims) continue;
+    Consumers C = consumers(g);
+    const Op m1 = g.ops[mi];
+    const int x = m1.in[0];
+    const Value& xv = g.vals[size_t(x)];
+    if (xv.is_host || xv.shape.size() < 2) continue;
+    const int64_t r = int64_t(xv.shape.size()), D = xv.shape.back();
+    if (m1.axes.size() != 1 || m1.axes[0] != r - 1) continue;
+    const int mu = m1.out[0];
+    if (C.is_output[size_t(mu)]) continue;
+    bool ok = true;
+    std::vector<int> subs, sub_outs;
+    for (int oi : C.ops[size_t(mu)]) {
+      const Op& o = g.ops[size_t(oi)];
+      if (o.type != "Sub" || o.in.size() != 2 || o.in[0] != x || o.in[1] != mu) ok = false;
+      subs.push_back(oi);
+      sub_outs.push_back(o.out[0]);
+    }
+    if (!ok || subs.empty()) continue;
+    auto is_sub_out = [&](int v) { return std::find(sub_outs.begin(), sub_outs.end(), v) != sub_outs.end(); };
+    int sq = -1, dv = -1;
+    for (int so : sub_outs) {
+      if (C.is_output[size_t(so)]) ok = false;
+      for (int oi : C.ops[size_t(so)]) {
+        const Op& o = g.ops[size_t(oi)];
+        const bool square = (o.type == "Mul" && o.in.size() == 2 && is_sub_out(o.in[0]) && is_sub_out(o.in[1])) ||
+                            (o.type == "Pow" && o.in.size() == 2 && is_sub_out(o.in[0]) && g.vals[size_t(o.in[1])].is_host &&
+                             g.vals[size_t(o.in[1])].host->numel() == 1 && g.vals[size_t(o.in[1])].host->get_f64(0) == 2.0);
+        if (square && (sq < 0 || sq == oi))
+          sq = oi;
+        else if (o.type == "Div" && o.in.size() == 2 && is_sub_out(o.in[0]) && (dv < 0 || dv == oi))
+          dv = oi;
+        else
+          ok = false;
+      }
+    }
+    if (!ok || sq < 0 || dv < 0) continue;
+    auto single = [&](int v) -> int {
+      if (C.is_output[size_t(v)] || C.ops[size_t(v)].size() != 1) return -1;
+      return C.ops[size_t(v)][0];
+    };
+    const int m2 = single(g.ops[size_t(sq)].out[0]);
+    if (m2 < 0 || g.ops[size_t(m2)].type != "ReduceMean" || g.ops[size_t(m2)].axes != m1.axes ||
+        !g.ops[size_t(m2)].keepdims)
+      continue;
+    const int ad = single(g.ops[size_t(m2)].out[0]);
+    if (ad < 0 || g.ops[size_t(ad)].type != "Add" || g.ops[size_t(ad)].in.size() != 2) continue;
+    const Op& add = g.ops[size_t(ad)];
+    const int ev = add.in[0] == g.ops[size_t(m2)].out[0] ? add.in[1] : add.in[0];
+    if (!g.vals[size_t(ev)].is_host || g.vals[size_t(ev)].host->numel() != 1) continue;
+    const double eps = g.vals[size_t(ev)].host->get_f64(0);
+    const int sr = single(add.out[0]);
+    if (sr < 0 || g.ops[size_t(sr)].type != "Sqrt") continue;
+    if (single(g.ops[size_t(sr)].out[0]) != dv || g.ops[size_t(dv)].in[1] != g.ops[size_t(sr)].out[0]) continue;
+    std::vector<double> scale(size_t(D), 1.0), shift(size_t(D), 0.0);
+    int cur = g.ops[size_t(dv)].out[0];
+    int slot = dv;
+    std::vector<int> absorbed = {int(mi), sq, m2, ad, sr, dv};
+    absorbed.insert(absorbed.end(), subs.begin(), subs.end());
+    while (true) {
+      const int oi = single(cur);
+      if (oi < 0) break;
+      const Op& o = g.ops[size_t(oi)];
+      if (!((o.type == "Mul" || o.type == "Add" || o.type == "Sub" || o.type == "Div") && o.in.size() == 2)) break;
+      const bool cur_first = o.in[0] == cur;
+      const Value& ov = g.vals[size_t(cur_first ? o.in[1] : o.in[0])];
+      std::vector<double> v;
+      if (!ov.is_host || !per_axis_values(*ov.host, size_t(r), size_t(r - 1), D, v) ||
+          g.vals[size_t(o.out[0])].shape != xv.shape)
+        break;
+      if ((o.type == "Sub" || o.type == "Div") && !cur_first) break;
+      for (int64_t c = 0; c < D; ++c) {
+        const double k = v[size_t(c)];
+        if (o.type == "Mul") {
+          scale[size_t(c)] *= k;
+          shift[size_t(c)] *= k;
+        } else if (o.type == "Add") {
+          shift[size_t(c)] += k;
+        } else if (o.type == "Sub") {
+          shift[size_t(c)] -= k;
+        } else {
+          scale[size_t(c)] /= k;
+          shift[size_t(c)] /= k;
+        }
+      }
+      absorbed.push_back(oi);
+      cur = o.out[0];
+      slot = oi;
+    }
+    Op f;
+    f.type = "LayerNorm";
+    f.name = m1.name;
+    f.in = {x};
+    f.out = {cur};
+    f.alpha = float(eps);
+    f.weight = std::make_shared<HostTensor>(DT_FLOAT, std::vector<int64_t>{D});
+    f.bias = std::make_shared<HostTensor>(DT_FLOAT, std::vector<int64_t>{D});
+    for (int64_t c = 0; c < D; ++c) {
+      f.weight->mptr<float>()[c] = float(scale[size_t(c)]);
+      f.bias->mptr<float>()[c] = float(shift[size_t(c)]);
+    }
+    for (int a : absorbed) g.ops[size_t(a)].dead = true;
+    g.vals[size_t(cur)].producer = slot;
+    g.ops[size_t(slot)] = f;
+  }
+}
+
+// Scaled dot-product attention written out in primitives (ViTAttention, ViTNet.cs:155-207):
+//   s = MatMul(q, Transpose(k, last two axes)) [* or / a scalar]; p = Softmax(s, last axis);
+//   y = MatMul(p, v), with q, k, v [..., S, hd] device tensors
+// => Attention(q, k, v): alpha = the scale on the scores.
+static void fuse_attention(LGraph& g) {
+  for (size_t mi = 0; mi < g.ops.size(); ++mi) {
+    if (g.ops[mi].dead || g.ops[mi].type != "MatMul" || g.ops[mi].in.size() != 2) continue;
+    Consumers C = consumers(g);
+    const Op mm1 = g.ops[mi];
+    const int q = mm1.in[0], kt = mm1.in[1];
+    const Value& qv = g.vals[size_t(q)];
+    const Value& ktv = g.vals[size_t(kt)];
+    if (qv.is_host || ktv.is_host || qv.shape.size() < 3 || ktv.producer < 0) continue;
+    const int ti = ktv.producer;
+    const Op& tr = g.ops[size_t(ti)];
+    if (tr.dead || tr.type != "Transpose") continue;
+    const size_t r = qv.shape.size();
+    bool ok = tr.perm.size() == r;
+    for (size_t i = 0; ok && i < r; ++i)
+      ok = tr.perm[i] == int64_t(i + 2 == r ? r - 1 : (i + 1 == r ? r - 2 : i));
+    if (!ok) continue;
+    const int k = tr.in[0];
+    if (g.vals[size_t(k)].shape != qv.shape) continue;
+    auto single = [&](int v) -> int {
+      if (C.is_output[size_t(v)] || C.ops[size_t(v)].size() != 1) return -1;
+      return C.ops[size_t(v)][0];
+    };
+    int cur = mm1.out[0];
+    double scale = 1.0;
+    std::vector<int> absorbed = {int(mi)};
+    int oi = single(cur);
+    if (oi >= 0 && (g.ops[size_t(oi)].type == "Mul" || g.ops[size_t(oi)].type == "Div") && g.ops[size_t(oi)].in.size() == 2) {
+      const Op& o = g.ops[size_t(oi)];
+      const bool cur_first = o.in[0] == cur;
+      const Value& sv = g.vals[size_t(cur_first ? o.in[1] : o.in[0])];
+      if (sv.is_host && sv.host->numel() == 1 && (o.type == "Mul" || cur_first)) {
+        scale = o.type == "Mul" ? sv.host->get_f64(0) : 1.0 / sv.host->get_f64(0);
+        absorbed.push_back(oi);
+        cur = o.out[0];
+        oi = single(cur);
+      }
+    }
+    if (oi < 0 || g.ops[size_t(oi)].type != "Softmax" || g.ops[size_t(oi)].axis != int64_t(r - 1)) continue;
+    absorbed.push_back(oi);
+    cur = g.ops[size_t(oi)].out[0];
+    const int m2 = single(cur);
+    if (m2 < 0 || g.ops[size_t(m2)].type != "MatMul" || g.ops[size_t(m2)].in[0] != cur) continue;
+    const int v = g.ops[size_t(m2)].in[1];
+    const Value& vv = g.vals[size_t(v)];
+    if (vv.is_host || vv.shape != qv.shape) continue;
+    absorbed.push_back(m2);
+    Op f;
+    f.type = "Attention";
+    f.name = mm1.name;
+    f.in = {q, k, v};
+    f.out = g.ops[size_t(m2)].out;
+    f.alpha = float(scale);
+    for (int a : absorbed) g.ops[size_t(a)].dead = true;
+    if (C.ops[size_t(kt)].size() == 1 && !C.is_output[size_t(kt)]) g.ops[size_t(ti)].dead = true;
+    g.vals[size_t(f.out[0])].producer = m2;
+    g.ops[size_t(m2)] = f;
+  }
+}
+
 void fuse(LGraph& g) {
   // ---------------- Conv chains ----------------
   for (size_t ci = 0; ci < g.ops.size(); ++ci) {
@@ -464,8 +649,8 @@ void fuse(LGraph& g) {
         }
         break;
       }
-      if ((o.type == "Relu" || o.type == "Sigmoid") && f.act == 0) {
-        f.act = o.type == "Relu" ? 1 : 2;
+      if ((o.type == "Relu" || o.type == "Sigmoid" || o.type == "Gelu") && f.act == 0) {
+        f.act = o.type == "Relu" ? 1 : (o.type == "Sigmoid" ? 2 : (o.mode == "tanh" ? 3 : 4));
         absorbed.push_back(oi);
         cur = o.out[0];
         slot = oi;
@@ -571,8 +756,8 @@ void fuse(LGraph& g) {
         }
         break;
       }
-      if ((o.type == "Relu" || o.type == "Sigmoid") && f.act == 0) {
-        f.act = o.type == "Relu" ? 1 : 2;
+      if ((o.type == "Relu" || o.type == "Sigmoid" || o.type == "Gelu") && f.act == 0) {
+        f.act = o.type == "Relu" ? 1 : (o.type == "Sigmoid" ? 2 : (o.mode == "tanh" ? 3 : 4));
         absorbed.push_back(oi);
         cur = o.out[0];
         slot = oi;
@@ -596,6 +781,8 @@ void fuse(LGraph& g) {
   }
   merge_projection_shortcuts(g);
   fuse_group_norms(g);
+  fuse_layer_norms(g);
+  fuse_attention(g);
   push_activation_into_producers(g);
   g.dce();
 }

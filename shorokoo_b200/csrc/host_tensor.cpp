@@ -370,7 +370,7 @@ static const char* kHostOps[] = {
     "ReduceMean", "ReduceMax", "ReduceMin", "Add", "Sub", "Mul", "Div", "Pow", "Max", "Min", "Equal", "Less",
     "Greater", "LessOrEqual", "GreaterOrEqual", "Not", "And", "Or", "Where", "Sqrt", "Neg", "Abs", "Exp",
     "Log", "Reciprocal", "Relu", "Sigmoid", "Tanh", "Floor", "Ceil", "MatMul", "Softmax", "Pad",
-    "SequenceConstruct", "SequenceAt", "SequenceLength"};
+    "SequenceConstruct", "SequenceAt", "SequenceLength", "Tile"};
 
 bool host_eval_supported(const std::string& op) {
   for (const char* s : kHostOps)
@@ -679,6 +679,23 @@ bool host_eval(const OnnxNode& n, const std::vector<const HostTensor*>& in, std:
     out.push_back(gather_bytes(x, shape, [&](const std::vector<int64_t>& idx) {
       int64_t s = 0;
       for (size_t d = 0; d < idx.size(); ++d) s += idx[d] * st[d];
+      return s;
+    }));
+    return true;
+  }
+  if (op == "Tile") {   // out[i] = x[i mod x.shape] with out.shape = x.shape * repeats
+    const HostTensor& x = I(0);
+    auto rep = I(1).to_i64_vec();
+    SB_CHECK(rep.size() == x.shape.size(), SB_SHAPE_ERROR, "Tile: repeats length != rank");
+    std::vector<int64_t> shape(x.shape.size());
+    for (size_t d = 0; d < shape.size(); ++d) {
+      SB_CHECK(rep[d] >= 0, SB_SHAPE_ERROR, "Tile: negative repeat");
+      shape[d] = x.shape[d] * rep[d];
+    }
+    auto st = bstrides(x.shape, x.shape);   // (size-1 dims: stride 0, index 0 anyway)
+    out.push_back(gather_bytes(x, shape, [&](const std::vector<int64_t>& idx) {
+      int64_t s = 0;
+      for (size_t d = 0; d < idx.size(); ++d) s += (idx[d] % x.shape[d]) * st[d];
       return s;
     }));
     return true;

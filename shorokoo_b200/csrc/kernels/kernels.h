@@ -187,6 +187,33 @@ cudaError_t to_rows_bf16(const void* src, int src_bf16, int64_t M, int64_t K, in
 cudaError_t maxpool_nhwc_bf16(const void* x, void* y, int N, int H, int W, int C, int Ho, int Wo, int kh,
                               int kw, int sh, int sw, int ph, int pw, int dh, int dw, cudaStream_t s);
 // NHWC (bf16 or f32 with C contiguous, pixel stride ldp) -> [N, C] mean or max, bf16 or f32 output.
+// Fused attention (attention.cu): y[b, h, s, :] = softmax(scale q k^T) v over q, k, v
+// [B, H, S, hd] strided views (head dim contiguous, 16-byte aligned rows), bf16 or fp32 (read as
+// bf16), S <= 256 and hd = 64; y written at out + b os[0] + h os[1] + s os[2] as bf16 (out_mode 0),
+// fp32 on the TF32 grid (1) or fp32 (2).
+struct AttentionArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  int64_t qs[3], ks[3], vs[3];   // element strides of the batch, head and sequence axes
+  int in_f32;
+  int S, hd;
+  float scale;
+  void* out;
+  int64_t os[3];
+  int out_mode;
+  unsigned int* err;
+};
+bool attention_supported(int S, int hd);
+void attention_prepare();   // once per device, before the first launch (shared-memory attribute)
+cudaError_t attention(const AttentionArgs& a, int B, int H, cudaStream_t s);
+
+// Row-wise layer normalisation (norm.cu): y[r, :] = (x[r, :] - mean) / sqrt(var + eps) * gamma +
+// beta over the last axis of D features, x fp32 rows of pitch ldx, y with pitch ldy as bf16
+// (y_mode 0), fp32 on the TF32 grid (1) or fp32 (2).
+cudaError_t layer_norm(const float* x, int64_t rows, int D, int64_t ldx, float eps, const float* gamma,
+                       const float* beta, void* y, int y_mode, int64_t ldy, cudaStream_t s);
+
 // Group normalisation over NHWC x [N, HW, ldc] (bf16 or fp32; C channels in G groups, C / G <= 64,
 // C a multiple of the 16-byte vector with C / vector dividing 256): y = act(((x - mean) * rstd) *
 // gamma + beta) per (n, group), stored with pitch ldy as bf16 (y_mode 0), fp32 on the TF32 grid (1)
@@ -210,7 +237,7 @@ cudaError_t bf16_to_f32(const void* src, void* dst, int64_t n, cudaStream_t s);
 enum EwOp : int {
   EW_ADD = 0, EW_SUB, EW_MUL, EW_DIV, EW_POW, EW_MAX, EW_MIN,
   EW_RELU = 16, EW_SIGMOID, EW_TANH, EW_SQRT, EW_NEG, EW_ABS, EW_EXP, EW_LOG, EW_RECIP, EW_FLOOR, EW_CEIL,
-  EW_ERF, EW_LEAKY, EW_CLIP, EW_IDENT
+  EW_ERF, EW_LEAKY, EW_CLIP, EW_IDENT, EW_GELU, EW_GELU_TANH
 };
 cudaError_t elementwise(int op, const void* a, int a_bf16, const TDesc& ad, const void* b, int b_bf16,
                         const TDesc& bd, void* y, int y_bf16, const TDesc& yd, float alpha, float beta,

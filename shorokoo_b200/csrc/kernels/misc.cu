@@ -524,6 +524,9 @@ __device__ __forceinline__ float ew_apply(int op, float a, float b, float alpha,
     case EW_ERF: return erff(a);
     case EW_LEAKY: return a >= 0.f ? a : alpha * a;
     case EW_CLIP: return fminf(fmaxf(a, alpha), beta);
+    // GELU (Hendrycks & Gimpel): x Phi(x) with the error function, or its tanh approximation
+    case EW_GELU: return 0.5f * a * (1.f + erff(a * 0.70710678118654752f));
+    case EW_GELU_TANH: return 0.5f * a * (1.f + tanhf(0.79788456080286536f * (a + 0.044715f * a * a * a)));
     default: return a;
   }
 }

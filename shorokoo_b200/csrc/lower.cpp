@@ -23,7 +23,7 @@ const std::set<std::string> kDeviceOps = {
     "Relu", "Sigmoid", "Tanh", "Sqrt", "Neg", "Abs", "Exp", "Log", "Reciprocal", "Floor", "Ceil", "Erf",
     "LeakyRelu", "Clip", "Identity", "Add", "Sub", "Mul", "Div", "Pow", "Max", "Min", "Softmax",
     "Reshape", "Flatten", "Squeeze", "Unsqueeze", "Transpose", "Concat", "Slice", "Pad", "Resize",
-    "ReduceMean", "ReduceSum", "ReduceMax", "Expand", "Shape", "Size", "Cast", "Dropout"};
+    "ReduceMean", "ReduceSum", "ReduceMax", "Expand", "Shape", "Size", "Cast", "Dropout", "Gelu"};
 
 bool is_std_domain(const std::string& d) { return d.empty() || d == "ai.onnx"; }
 
@@ -371,12 +371,16 @@ class Lowerer {
     } else if (t == "MatMul") {
       const Value& a = X(0);
       const Value& b = X(1);
-      SB_CHECK(a.shape.size() >= 2 && b.shape.size() == 2, SB_UNSUPPORTED,
-               "MatMul: supported forms are [...,M,K] x [K,N]");
-      SB_CHECK(a.shape.back() == b.shape[0], SB_SHAPE_ERROR,
+      SB_CHECK(a.shape.size() >= 2 && b.shape.size() >= 2, SB_UNSUPPORTED,
+               "MatMul: supported forms are [...,M,K] x [...,K,N]");
+      const size_t ra = a.shape.size(), rb = b.shape.size();
+      SB_CHECK(a.shape[ra - 1] == b.shape[rb - 2], SB_SHAPE_ERROR,
                "MatMul: inner dimensions differ " + shape_str(a.shape) + " x " + shape_str(b.shape));
-      std::vector<int64_t> os(a.shape.begin(), a.shape.end() - 1);
-      os.push_back(b.shape[1]);
+      // batch dimensions broadcast (a device x device product runs only inside a fused attention)
+      std::vector<int64_t> os = broadcast_shapes(std::vector<int64_t>(a.shape.begin(), a.shape.end() - 2),
+                                                 std::vector<int64_t>(b.shape.begin(), b.shape.end() - 2));
+      os.push_back(a.shape[ra - 2]);
+      os.push_back(b.shape[rb - 1]);
       oshapes.push_back(os);
     } else if (t == "Gemm") {
       const Value& a = X(0);
@@ -396,6 +400,10 @@ class Lowerer {
                t == "Exp" || t == "Log" || t == "Reciprocal" || t == "Floor" || t == "Ceil" || t == "Erf" ||
                t == "Identity" || t == "Dropout") {
       if (t == "Dropout") op.type = "Identity";
+      oshapes.push_back(X(0).shape);
+    } else if (t == "Gelu") {   // approximate: "none" (erf) or "tanh"
+      op.mode = n.attr_s("approximate", "none");
+      SB_CHECK(op.mode == "none" || op.mode == "tanh", SB_UNSUPPORTED, "Gelu: approximate=" + op.mode);
       oshapes.push_back(X(0).shape);
     } else if (t == "LeakyRelu") {
       op.alpha = n.attr_f("alpha", 0.01f);

@@ -127,7 +127,7 @@ int ew_code(const std::string& t) {
       {"Max", k::EW_MAX}, {"Min", k::EW_MIN}, {"Relu", k::EW_RELU}, {"Sigmoid", k::EW_SIGMOID},
       {"Tanh", k::EW_TANH}, {"Sqrt", k::EW_SQRT}, {"Neg", k::EW_NEG}, {"Abs", k::EW_ABS}, {"Exp", k::EW_EXP},
       {"Log", k::EW_LOG}, {"Reciprocal", k::EW_RECIP}, {"Floor", k::EW_FLOOR}, {"Ceil", k::EW_CEIL},
-      {"Erf", k::EW_ERF}, {"LeakyRelu", k::EW_LEAKY}, {"Clip", k::EW_CLIP}};
+      {"Erf", k::EW_ERF}, {"LeakyRelu", k::EW_LEAKY}, {"Clip", k::EW_CLIP}, {"Gelu", k::EW_GELU}};
   auto it = m.find(t);
   return it == m.end() ? -1 : it->second;
 }
@@ -259,8 +259,8 @@ void Plan::add_step(const std::string& kind, std::vector<DevTensor> reads, std::
 //   kStoreBf16   every reader is a bf16-operand contraction (operand, residual or second operand);
 //   kStoreTf32   every reader is a single-pass TF32 contraction: fp32 rounded to the TF32 grid;
 //   kStoreF32    anything else (generic ops, graph outputs, TF32x3 readers, mixed precisions).
-// Global pools and group norms read either dtype and add no constraint; a value whose readers add
-// none takes `pref`, the class of its producer's operands.
+// Global pools, group norms and attention read either dtype and add no constraint; a value whose
+// readers add none takes `pref`, the class of its producer's operands.
 int Plan::storage_class(int v, int pref) const {
   if (is_output_[size_t(v)]) return kStoreF32;
   int cls = -1;
@@ -272,7 +272,8 @@ int Plan::storage_class(int v, int pref) const {
     const Op& op = g_.ops[size_t(oi)];
     if (op.type == "FusedConv" || op.type == "FusedGemm") {
       meet(op.prec == 0 ? kStoreBf16 : (op.prec == 1 ? kStoreTf32 : kStoreF32));
-    } else if (op.type == "GlobalAveragePool" || op.type == "GlobalMaxPool" || op.type == "GroupNorm") {
+    } else if (op.type == "GlobalAveragePool" || op.type == "GlobalMaxPool" || op.type == "GroupNorm" ||
+               op.type == "Attention") {
       continue;
     } else if (op.type == "MaxPool" || (is_view_op(op.type) && op.in[0] == v)) {
       const int c = storage_class(op.out[0], -1);
@@ -1001,9 +1002,114 @@ void Plan::plan_group_norm(const Op& op) {
   });
 }
 
+// LayerNorm over the last axis (fused from its primitives): fp32 rows in, the readers' operand
+// type out (bf16 rows for a bf16 projection), one warp per row.
+void Plan::plan_layer_norm(const Op& op) {
+  const Value& xv = g_.vals[size_t(op.in[0])];
+  const Value& yv = g_.vals[size_t(op.out[0])];
+  const int64_t D = xv.shape.back();
+  const int64_t rows = numel(xv.shape) / std::max<int64_t>(D, 1);
+  DevTensor x = as_f32_contig(op.in[0]);
+  SB_CHECK(D % 4 == 0 && x.off % 16 == 0, SB_UNSUPPORTED, "LayerNorm: " + std::to_string(D) + " features");
+  const int cls = storage_class(op.out[0], kStoreF32);
+  const int ymode = cls == kStoreBf16 ? 0 : (cls == kStoreTf32 ? 1 : 2);
+  DevTensor y = alloc_contig(yv.shape, ymode == 0);
+  vt_[size_t(op.out[0])] = y;
+  std::vector<float> gb(size_t(2 * D));
+  for (int64_t c = 0; c < D; ++c) {
+    gb[size_t(c)] = op.weight->ptr<float>()[c];
+    gb[size_t(D + c)] = op.bias->ptr<float>()[c];
+  }
+  DevTensor gbt;
+  gbt.buf = -1;
+  gbt.off = add_weight_bytes(gb.data(), gb.size() * 4);
+  const float eps = op.alpha;
+  add_step("layer_norm " + std::to_string(D), {x}, {y}, [=]() {
+    const float* xp = static_cast<const float*>(ptr(x));
+    const float* gp = static_cast<const float*>(ptr(gbt));
+    void* yp = ptr(y);
+    return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+      return k::layer_norm(xp, rows, int(D), D, eps, gp, gp + D, yp, ymode, D, s);
+    });
+  });
+}
+
+// Attention (fused q k^T -> scale -> softmax -> v): q, k, v are read where they are (strided views
+// of the QKV projection); the output is laid out [B, S, H, hd], so the Transpose(0, 2, 1, 3) and
+// Reshape to [B, S, H hd] that follow are a plain row matrix for the output projection.
+void Plan::plan_attention(const Op& op) {
+  const Value& qv = g_.vals[size_t(op.in[0])];
+  const size_t r = qv.shape.size();
+  SB_CHECK(r == 3 || r == 4, SB_UNSUPPORTED, "Attention: rank-3 or rank-4 operands required");
+  const int64_t B = qv.shape[0], H = r == 4 ? qv.shape[1] : 1, S = qv.shape[r - 2], hd = qv.shape[r - 1];
+  SB_CHECK(k::attention_supported(int(S), int(hd)), SB_UNSUPPORTED,
+           "Attention: sequences of up to 256 and heads of 64 are supported (got " + std::to_string(S) + " x " +
+               std::to_string(hd) + ")");
+  DevTensor in[3];
+  for (int i = 0; i < 3; ++i) in[i] = vt_[size_t(op.in[size_t(i)])];
+  auto usable = [&](const DevTensor& t) {
+    const int es = t.bf16 ? 2 : 4;
+    if (t.strides.back() != 1 || (t.off % 16) != 0) return false;
+    for (size_t d = 0; d + 1 < r; ++d)
+      if ((t.strides[d] * es) % 16 != 0) return false;
+    return true;
+  };
+  const bool same = in[0].bf16 == in[1].bf16 && in[1].bf16 == in[2].bf16;
+  for (int i = 0; i < 3; ++i)
+    if (!same || !usable(in[i])) in[i] = as_f32_contig(op.in[size_t(i)]);
+  const int cls = storage_class(op.out[0], kStoreF32);
+  const int ymode = cls == kStoreBf16 ? 0 : (cls == kStoreTf32 ? 1 : 2);
+  DevTensor y = alloc_contig({B, S, H, hd}, ymode == 0);
+  DevTensor yl = y;   // the logical [B, H, S, hd] (or [B, S, hd]) view
+  if (r == 4) {
+    yl.shape = {B, H, S, hd};
+    yl.strides = {S * H * hd, hd, H * hd, 1};
+  } else {
+    yl.shape = {B, S, hd};
+    yl.strides = {S * hd, hd, 1};
+  }
+  vt_[size_t(op.out[0])] = yl;
+  auto st3 = [&](const DevTensor& t, int64_t* o) {
+    o[0] = t.strides[0];
+    o[1] = r == 4 ? t.strides[1] : 0;
+    o[2] = t.strides[r - 2];
+  };
+  k::AttentionArgs a;
+  std::memset(&a, 0, sizeof(a));
+  st3(in[0], a.qs);
+  st3(in[1], a.ks);
+  st3(in[2], a.vs);
+  a.in_f32 = in[0].bf16 ? 0 : 1;
+  a.S = int(S);
+  a.hd = int(hd);
+  a.scale = op.alpha;
+  a.os[0] = S * H * hd;
+  a.os[1] = hd;
+  a.os[2] = H * hd;
+  a.out_mode = ymode;
+  a.err = err_;
+  const double macs = 2.0 * double(B * H) * double(S) * double(S) * double(hd);
+  stats_.macs += macs;
+  stats_.macs_by_prec[0] += macs;
+  stats_.tc_kernels++;
+  const DevTensor q = in[0], kk = in[1], v = in[2];
+  add_step("attention " + std::to_string(B * H) + "x" + std::to_string(S) + "x" + std::to_string(hd), {q, kk, v}, {y},
+           [=]() {
+             k::AttentionArgs aa = a;
+             aa.q = ptr(q);
+             aa.k = ptr(kk);
+             aa.v = ptr(v);
+             aa.out = ptr(y);
+             k::attention_prepare();
+             const int nb = int(B), nh = int(H);
+             return std::function<cudaError_t(cudaStream_t)>(
+                 [=](cudaStream_t s) { return k::attention(aa, nb, nh, s); });
+           });
+}
+
 void Plan::plan_elementwise(const Op& op) {
   const Value& yv = g_.vals[size_t(op.out[0])];
-  const int code = ew_code(op.type);
+  const int code = op.type == "Gelu" && op.mode == "tanh" ? int(k::EW_GELU_TANH) : ew_code(op.type);
   SB_CHECK(code >= 0, SB_UNSUPPORTED, "no device kernel for " + op.type);
   std::vector<DevTensor> ins;
   for (int id : op.in) {
@@ -1367,6 +1473,8 @@ void Plan::build() {
     else if (t == "MaxPool") plan_maxpool(op);
     else if (t == "GlobalAveragePool" || t == "GlobalMaxPool") plan_global_pool(op);
     else if (t == "GroupNorm") plan_group_norm(op);
+    else if (t == "LayerNorm") plan_layer_norm(op);
+    else if (t == "Attention") plan_attention(op);
     else if (is_view_op(t)) plan_view(op);
     else if (t == "Concat") plan_concat(op);
     else if (t == "Softmax") plan_softmax(op);

@@ -148,6 +148,8 @@ class Plan {
   void plan_maxpool(const Op& op);
   void plan_global_pool(const Op& op);
   void plan_group_norm(const Op& op);
+  void plan_layer_norm(const Op& op);
+  void plan_attention(const Op& op);
   void plan_elementwise(const Op& op);
   void plan_view(const Op& op);
   void plan_concat(const Op& op);

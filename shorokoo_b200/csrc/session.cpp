@@ -288,6 +288,13 @@ bool batch_separable(const LGraph& g) {
       if (a0 != 0 || g.vals[size_t(op.in[0])].shape.size() < 2) return false;
       if (op.residual >= 0 && ax[size_t(op.residual)] != 0) return false;
       out = 0;
+    } else if (t == "LayerNorm") {   // per row over the last axis
+      if (a0 != 0 || g.vals[size_t(op.in[0])].shape.size() < 2) return false;
+      out = 0;
+    } else if (t == "Attention") {   // per (batch, head): q, k and v sharded alike
+      for (int id : op.in)
+        if (ax[size_t(id)] != 0) return false;
+      out = 0;
     } else if (t == "Identity") {
       out = a0;
     } else if (t == "Transpose") {

@@ -733,6 +733,185 @@ def retinanet(batch: int = 16, hw: Tuple[int, int] = (800, 1024), seed: int = 13
                      [classifications, regressions], B.macs, B.params)
 
 
+# ================================================================================================
+# Adjacent model: Vision Transformer (samples/RetinaNet/ViTNet.cs)
+# ================================================================================================
+
+VIT_VARIANTS = {   # embed_dim, heads, layers, mlp_dim (ViTTiny :310-353, ViTSmall :361-392, ViTBase :403-434)
+    "tiny": (192, 3, 12, 768),
+    "small": (384, 6, 12, 1536),
+    "base": (768, 12, 12, 3072),
+}
+
+
+def _vit_linear(B: Builder, x: str, w: str, b: str, rows: int, k: int, n: int) -> str:
+    """ViTLinear / the attention and MLP projections: MatMul(x, W [in, out]) + b."""
+    y = B.op("MatMul", [x, w])
+    shp = B.shape[x]
+    B.shape[y] = tuple(shp[:-1]) + (n,)
+    B.macs += rows * k * n
+    return B.binary("Add", y, b)
+
+
+class _ViTLayerNormParams:
+    def __init__(self, B: Builder, d: int, path: str, affine_scale: float):
+        gv = np.ones(d, np.float32)
+        bv = np.zeros(d, np.float32)
+        if affine_scale:
+            gv = gv + (affine_scale * B.rng.standard_normal(d)).astype(np.float32)
+            bv = bv + (affine_scale * B.rng.standard_normal(d)).astype(np.float32)
+        self.gamma = B.init(gv, path + ".weight")
+        self.beta = B.init(bv, path + ".bias")
+
+
+def vit_layer_norm(B: Builder, x: str, p: _ViTLayerNormParams, eps: float) -> str:
+    """ViTLayerNorm (ViTNet.cs:51-72): mean over the last axis (keepdims), the biased variance as the
+    mean of Pow(x - mean, 2), (x - mean) / Sqrt(var + eps) (the difference written twice), times
+    gamma plus beta."""
+    axes = B.const(np.array([-1], np.int64))
+    shp = B.shape[x]
+    mean = B.op("ReduceMean", [x, axes], keepdims=1)
+    B.shape[mean] = tuple(shp[:-1]) + (1,)
+    two = B.const(np.array(2.0, np.float32))
+    B.shape[two] = ()
+    var = B.op("ReduceMean", [B.binary("Pow", B.binary("Sub", x, mean), two), axes], keepdims=1)
+    B.shape[var] = B.shape[mean]
+    eps_c = B.const(np.array(eps, np.float32))
+    B.shape[eps_c] = ()
+    den = B.unary("Sqrt", B.binary("Add", var, eps_c))
+    y = B.binary("Div", B.binary("Sub", x, mean), den)
+    B.shape[p.gamma] = B.shape[p.beta] = (shp[-1],)
+    return B.binary("Add", B.binary("Mul", y, p.gamma), p.beta)
+
+
+def vit(variant: str = "base", batch: int = 1, hw: Tuple[int, int] = (224, 224), seed: int = 17,
+        num_classes: int = 1000, apply_softmax: bool = False, affine_scale: float = 0.0, layers: Optional[int] = None,
+        patch: int = 16) -> ModelCase:
+    """ViTTiny / ViTSmall / ViTBase (ViTNet.cs:310-434), batch 1 as the module's graph allows (the
+    [1, 1, D] class token is concatenated to the patch sequence without a batch broadcast).
+
+    Patch embedding (ViTPatchEmbed :80-118): Conv 16x16 / 16 -> Reshape [B, D, P] -> Transpose
+    [0, 2, 1]; class token and positional embedding (initializers); the transformer block
+    (ViTTransformerBlock :247-268) applied ``layers`` times with tied weights (the block model is
+    called inside LoopAPI.Iterate, like StackedLinear; the Loop is unrolled at export): pre-norm
+    LayerNorm -> ViTAttention (:155-207: QKV MatMul + bias, Reshape [B, S, 3, H, hd], Transpose
+    [2, 0, 3, 1, 4], Slice + Squeeze per Q / K / V, Q MatMul Transpose(K) times 1 / sqrt(hd),
+    Softmax(-1), MatMul V, Transpose [0, 2, 1, 3], Reshape [B, S, D], projection MatMul + bias) ->
+    residual Add -> LayerNorm -> ViTMlp (:217-239: MatMul + bias, Gelu(approximate="tanh"), MatMul +
+    bias) -> residual Add; final LayerNorm; ViTClassHead (:275-297: Slice of the class token, Reshape
+    [B, D], MatMul + bias, Softmax when apply_softmax).
+
+    Weights: the sample's ViTInitSimple fills every parameter with 1.0, which makes all channels
+    identical; these are random instead (projections Xavier-uniform, patch conv N(0, 0.02^2), class
+    token and positions N(0, 0.02^2), LayerNorm gamma 1 / beta 0, biases zero unless
+    ``affine_scale`` perturbs them)."""
+    D, H, L, M = VIT_VARIANTS[variant]
+    if layers is not None:
+        L = layers
+    hd = D // H
+    rng_in = np.random.Generator(np.random.PCG64(seed))
+    x_val = rng_in.standard_normal(size=(batch, 3, hw[0], hw[1]), dtype=np.float32)
+    B = Builder(seed + WEIGHT_SEED_OFFSET)
+    x = B.graph_input(W.FLOAT, 4, x_val.shape)
+    eps = 1e-6
+
+    def bias(n, path):
+        v = np.zeros(n, np.float32) if not affine_scale else \
+            (affine_scale * B.rng.standard_normal(n)).astype(np.float32)
+        return B.init(v, path)
+
+    # patch embedding
+    pw = B.init((0.02 * B.rng.standard_normal((D, 3, patch, patch))).astype(np.float32), "patch_embed.weight")
+    pb = bias(D, "patch_embed.bias")
+    pe = B.op("Conv", [x, pw, pb], auto_pad="NOTSET", dilations=[1, 1], group=1, kernel_shape=[patch, patch],
+              pads=[0, 0, 0, 0], strides=[patch, patch])
+    gh, gw = hw[0] // patch, hw[1] // patch
+    B.shape[pe] = (batch, D, gh, gw)
+    B.macs += batch * D * gh * gw * 3 * patch * patch
+    bsz, h_, w_ = B.dim(x, 0), B.dim(x, 2), B.dim(x, 3)
+    ps = B.const(np.array(patch, np.int64))
+    npatch = B.ident(B.op("Mul", [B.op("Div", [h_, ps]), B.op("Div", [w_, ps])]))
+    fl = B.op("Reshape", [pe, B.vec([B.unsq(bsz), D, B.unsq(npatch)])])
+    B.shape[fl] = (batch, D, gh * gw)
+    tok = B.op("Transpose", [fl], perm=[0, 2, 1])
+    S = gh * gw + 1
+    B.shape[tok] = (batch, gh * gw, D)
+    cls = B.init((0.02 * B.rng.standard_normal((1, 1, D))).astype(np.float32), "cls_token")
+    if variant != "tiny":   # ViTSmall / ViTBase tile the token by [1, 1, 1]
+        cls = B.op("Tile", [cls, B.const(np.array([1, 1, 1], np.int64))])
+    B.shape[cls] = (1, 1, D)
+    h = B.op("Concat", [cls, tok], axis=1)
+    B.shape[h] = (batch, S, D)
+    pos = B.init((0.02 * B.rng.standard_normal((1, S, D))).astype(np.float32), "pos_embed")
+    B.shape[pos] = (1, S, D)
+    h = B.binary("Add", h, pos)
+    # one set of block weights (tied across the iterations)
+    ln1 = _ViTLayerNormParams(B, D, "block.norm1", affine_scale)
+    ln2 = _ViTLayerNormParams(B, D, "block.norm2", affine_scale)
+    wqkv = B.init(xavier_uniform(B.rng, (D, 3 * D)), "block.attn.qkv.weight")
+    bqkv = bias(3 * D, "block.attn.qkv.bias")
+    wproj = B.init(xavier_uniform(B.rng, (D, D)), "block.attn.proj.weight")
+    bproj = bias(D, "block.attn.proj.bias")
+    w1 = B.init(xavier_uniform(B.rng, (D, M)), "block.mlp.fc1.weight")
+    b1 = bias(M, "block.mlp.fc1.bias")
+    w2 = B.init(xavier_uniform(B.rng, (M, D)), "block.mlp.fc2.weight")
+    b2 = bias(D, "block.mlp.fc2.bias")
+    scale = B.ident(B.op("Div", [B.const(np.array(1.0, np.float32)),
+                                 B.op("Sqrt", [B.op("Cast", [B.const(np.array(hd, np.int64))], to=W.FLOAT)])]))
+    B.shape[scale] = ()
+    big = np.iinfo(np.int32).max
+    rows = batch * S
+    for _ in range(L):
+        n1 = vit_layer_norm(B, h, ln1, eps)
+        qkv = _vit_linear(B, n1, wqkv, bqkv, rows, D, 3 * D)
+        sb, ss = B.dim(n1, 0), B.dim(n1, 1)
+        r5 = B.op("Reshape", [qkv, B.vec([B.unsq(sb), B.unsq(ss), 3, H, hd])])
+        B.shape[r5] = (batch, S, 3, H, hd)
+        t5 = B.op("Transpose", [r5], perm=[2, 0, 3, 1, 4])
+        B.shape[t5] = (3, batch, H, S, hd)
+        parts = []
+        for i in range(3):
+            sl = B.op("Slice", [t5, B.const(np.array([i, 0, 0, 0, 0], np.int64)),
+                                B.const(np.array([i + 1, big, big, big, big], np.int64))])
+            sq = B.op("Squeeze", [sl, B.const(np.array([0], np.int64))])
+            B.shape[sq] = (batch, H, S, hd)
+            parts.append(sq)
+        q, k, v = parts
+        kt = B.op("Transpose", [k], perm=[0, 1, 3, 2])
+        B.shape[kt] = (batch, H, hd, S)
+        sc = B.op("MatMul", [q, kt])
+        B.shape[sc] = (batch, H, S, S)
+        B.macs += batch * H * S * S * hd
+        sc = B.binary("Mul", sc, scale)
+        att = B.op("Softmax", [sc], axis=-1)
+        B.shape[att] = (batch, H, S, S)
+        ctx = B.op("MatMul", [att, v])
+        B.shape[ctx] = (batch, H, S, hd)
+        B.macs += batch * H * S * S * hd
+        ctx = B.op("Transpose", [ctx], perm=[0, 2, 1, 3])
+        B.shape[ctx] = (batch, S, H, hd)
+        ctx = B.op("Reshape", [ctx, B.vec([B.unsq(sb), B.unsq(ss), D])])
+        B.shape[ctx] = (batch, S, D)
+        h = B.binary("Add", h, _vit_linear(B, ctx, wproj, bproj, rows, D, D))
+        n2 = vit_layer_norm(B, h, ln2, eps)
+        f1 = _vit_linear(B, n2, w1, b1, rows, D, M)
+        g = B.op("Gelu", [f1], approximate="tanh")
+        B.shape[g] = B.shape[f1]
+        h = B.binary("Add", h, _vit_linear(B, g, w2, b2, rows, M, D))
+    h = vit_layer_norm(B, h, _ViTLayerNormParams(B, D, "norm", affine_scale), eps)
+    clsv = B.op("Slice", [h, B.const(np.array([0, 0, 0], np.int64)), B.const(np.array([big, 1, big], np.int64))])
+    B.shape[clsv] = (batch, 1, D)
+    clsv = B.op("Reshape", [clsv, B.vec([B.unsq(B.dim(h, 0)), D])])
+    B.shape[clsv] = (batch, D)
+    wh = B.init(xavier_uniform(B.rng, (D, num_classes)), "head.weight")
+    logits = _vit_linear(B, clsv, wh, bias(num_classes, "head.bias"), batch, D, num_classes)
+    if apply_softmax:
+        logits = B.op("Softmax", [logits], axis=-1)
+    B.outputs.append(W.ValueInfo(logits))
+    name = {"tiny": "ViTTiny", "small": "ViTSmall", "base": "ViTBase"}[variant]
+    return ModelCase(f"vit_{variant}", B.model(name), [(x, x_val)], [logits], B.macs, B.params)
+
+
 # Headline configurations (sizes, seeds) of the five workloads.
 CONFIGS = {
     "stacked_linear": dict(fn=stacked_linear, kwargs=dict(batch=4096, n=1024, depth=8, seed=42)),
@@ -742,6 +921,8 @@ CONFIGS = {
     "retinanet": dict(fn=retinanet, kwargs=dict(batch=16, seed=13)),
     # adjacent model: the GroupNorm-head detector (RetinaNetResNet50, 32 groups)
     "retinanet_gn": dict(fn=retinanet, kwargs=dict(batch=16, seed=13, norm_heads=True)),
+    # adjacent model: ViT-B/16 (ViTBase), batch 1 as its graph allows
+    "vit_base": dict(fn=vit, kwargs=dict(variant="base", batch=1, seed=17)),
 }
 
 
