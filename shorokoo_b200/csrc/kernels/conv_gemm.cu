@@ -351,10 +351,13 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int KT = a.Kpad / BKE;
+  // split-K: tile t is slice t % KS of output tile t / KS, k-tiles [slice * KTS, slice * KTS + KTS)
+  const int KS = a.ksplit > 1 ? a.ksplit : 1;
+  const int KTS = KT / KS;
   // residual k-tiles (res_mma): k-tile KT + j adds residual channels [64j, 64j + 64) of the tile
   const bool RESM = A_TMA && MODE != 4 && PREC == 0 && a.res_mma;
   const bool A2 = MODE == 0 && a.a2 != nullptr;   // second A operand (uses the tmRes map)
-  const int KTE = KT + (RESM ? BN / 64 : 0);
+  const int KTE = KTS + (RESM ? BN / 64 : 0);   // k-tiles per tile (slice)
   const bool BRES = A_TMA && a.b_resident;   // weights loaded once: slot kt holds k-tile kt
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_STAGE;
@@ -444,7 +447,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
 
   const int tiles_m = (a.M + BM - 1) / BM;
   const int tiles_n = (a.Cout + BN - 1) / BN;
-  const int total = tiles_m * tiles_n;
+  const int total = tiles_m * tiles_n * KS;
   const int SC = a.out_bf16 ? 64 : 32;   // output columns per 128-byte slab
   const int NS = BN / SC;
 
@@ -463,7 +466,8 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
       }
       int it = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
-        const int mt = t / tiles_n, nt = t - (t / tiles_n) * tiles_n;
+        const int tmn = t / KS, kt0 = (t - tmn * KS) * KTS;
+        const int mt = tmn / tiles_n, nt = tmn - (tmn / tiles_n) * tiles_n;
         // im2col: image and top-left input corner of the tile's first output pixel
         int img = 0, cw = 0, ch = 0;
         if (MODE == 3 || MODE == 4) {
@@ -485,7 +489,8 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
           for (int s2 = 0; s2 < nsl; ++s2)
             tma_load_2d(sRes + slot * RSB + s2 * 128 * 128, &tmRes, nt * BN + s2 * SC, mt * BM, &resf[slot]);
         }
-        for (int kt = 0; kt < KTE; ++kt) {
+        for (int j = 0; j < KTE; ++j) {
+          const int kt = j < KTS ? kt0 + j : KT + (j - KTS);   // (then the residual k-tiles)
           const bool mine = owner == pid;
           if (++owner == NP) owner = 0;
           if (!mine) {
@@ -553,7 +558,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
     int stage = 0;
     uint32_t phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      for (int kt = 0; kt < KT; ++kt) {
+      for (int kt = 0; kt < KTS; ++kt) {
         if (!mbar_wait(&full[stage], phase, abort_flag, a.err, 256u)) goto split_done;
         const uint4* src = reinterpret_cast<const uint4*>(sA + stage * A_STAGE);
         uint4* dst = reinterpret_cast<uint4*>(sA + stage * A_STAGE + A_BYTES);
@@ -600,11 +605,13 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
         if (!mbar_wait(&acce[acc], aph ^ 1u, abort_flag, a.err, 2u)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t((acc * PL + mid) * BN);
+        const int kt0 = (t % KS) * KTS;
         bool ok = true;
         // this issuer's k-tiles of the tile: g0 <= g < g0 + KTE with g = mid (mod PE); the first
         // is always a weight k-tile (PE <= KT), which initialises every column of the partial
         for (bool first = true; g < g0 + KTE; first = false) {
-          const int kt = g - g0;
+          const int j = g - g0;
+          const int kt = j < KTS ? kt0 + j : KT + (j - KTS);
           if (!mbar_wait(&full[stage], phase, abort_flag, a.err, 4u) ||
               (X3 && !mbar_wait(&split[stage], phase, abort_flag, a.err, 512u))) {
             ok = false;
@@ -624,7 +631,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
             // partials start at zero)
             const bool bias_first = BMMA && first && mid == 0;
             if (bias_first)
-              umma_bf16(d_tmem, sw32_desc(smem_u32(sOnes)), sw32_desc(smem_u32(sBiasT + (t % tiles_n) * BN * 32)),
+              umma_bf16(d_tmem, sw32_desc(smem_u32(sOnes)), sw32_desc(smem_u32(sBiasT + ((t / KS) % tiles_n) * BN * 32)),
                         idesc, 0u);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {   // four 32-byte K slices per 128-byte row
@@ -669,7 +676,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
     // With epi_half the warp's columns are the tile's 32-column half hsel.
     const bool ehalf = BN == 64 && a.epi_half != 0 && OB != 0;
     auto load_bias = [&](int t, float (&b)[4]) {
-      const int nt = t % tiles_n;
+      const int nt = (t / KS) % tiles_n;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int s2 = hsel + 2 * (i / HPS);
@@ -682,7 +689,8 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
     load_bias(blockIdx.x, bpre);
     int it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
-      const int mt = t / tiles_n, nt = t - (t / tiles_n) * tiles_n;
+      const int tmn = t / KS;
+      const int mt = tmn / tiles_n, nt = tmn - (tmn / tiles_n) * tiles_n;
       const int acc = it & 1;
       const uint32_t aph = uint32_t(it >> 1) & 1u;
       if (!mbar_wait(&accf[acc], aph, abort_flag, a.err, 8u)) break;
@@ -692,6 +700,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
       __syncwarp();
       load_bias(t + gridDim.x, bpre);   // next tile's bias, consumed one tile from now
       const int row0 = mt * BM + q * 32;
+      const int srow0 = row0 + (t % KS) * a.Mp;   // (split-K: this slice's rows of the partials)
       const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * PL * BN);
       const int slot = RS ? it % RS : 0;
       if (RS && !mbar_wait(&resf[slot], uint32_t(it / RS) & 1u, abort_flag, a.err, 32u)) break;
@@ -700,7 +709,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
           if (nt * BN + hsel * 32 < a.Cout) {
             const uint8_t* rslab = RS ? sRes + slot * RSB : nullptr;
             uint8_t* sb = sb0;
-            epilogue_slab<true>(a, &tmOut, tbase, 0, row0, nt * BN, sb, rslab, wbias, OB, PE, BN, hsel);
+            epilogue_slab<true>(a, &tmOut, tbase, 0, srow0, nt * BN, sb, rslab, wbias, OB, PE, BN, hsel);
           }
         } else if (a.epi == 2) {
           for (int s2 = hsel; s2 < NS; s2 += 2) {
@@ -715,8 +724,8 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
                                   : sb0;
             const int wm = inplace ? 0 : OB;
             const float* bsl = wbias + ((s2 - hsel) >> 1) * SC;
-            if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl, wm, PE, BN);
-            else epilogue_slab<false>(a, &tmOut, tbase, s2 * SC, row0, n0, sb, rslab, bsl, wm, PE, BN);
+            if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, srow0, n0, sb, rslab, bsl, wm, PE, BN);
+            else epilogue_slab<false>(a, &tmOut, tbase, s2 * SC, srow0, n0, sb, rslab, bsl, wm, PE, BN);
           }
         } else {
           const int m = row0 + lane;
@@ -758,7 +767,8 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
     int stage = 0;
     uint32_t phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      const int mt = t / tiles_n;
+      const int mt = (t / KS) / tiles_n;
+      const int kt0 = (t % KS) * KTS;
       int hb[PASSES], wb[PASSES];
       int64_t base[PASSES];
 #pragma unroll
@@ -776,7 +786,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
           base[i] = 0;
         }
       }
-      for (int kt = 0; kt < KT; ++kt) {
+      for (int kt = kt0; kt < kt0 + KTS; ++kt) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 16u)) goto gather_done;
         const uint32_t sbase = smem_u32(sA + stage * A_STAGE);
         if (MODE == 1) {
@@ -1413,6 +1423,96 @@ int conv_gemm_a_mode(const ConvGemmArgs& a) {
   return !a.tf32 && a.Cp == 4 ? kAGather8 : kAGather16;
 }
 
+namespace {
+
+__device__ __forceinline__ float act1(float v, int act) {
+  switch (act) {
+    case 1: return v > 0.f ? v : 0.f;
+    case 2: return __fdividef(1.f, 1.f + __expf(-v));
+    case 3: return 0.5f * v * (1.f + tanhf(0.79788456080286536f * (v + 0.044715f * v * v * v)));
+    case 4: return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+    default: return v;
+  }
+}
+
+// One thread per 4 output columns of a row: the slices' partials summed in slice order (a fixed
+// order: results do not depend on scheduling), then bias, residual, activation, output type.
+__global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restrict__ ws, int ks, int64_t Mp, int64_t M,
+                                                           int N, const float* __restrict__ bias,
+                                                           const void* __restrict__ res, int res_bf16, int64_t ldr,
+                                                           int act, void* __restrict__ out, int out_bf16, int64_t ldo,
+                                                           int round_tf32) {
+  const int nq = N >> 2;
+  const int64_t total = M * nq;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t m = i / nq;
+    const int n = int(i - m * nq) * 4;
+    float4 v = __ldg(reinterpret_cast<const float4*>(bias + n));
+    for (int s2 = 0; s2 < ks; ++s2) {
+      const float4 p = __ldg(reinterpret_cast<const float4*>(ws + (s2 * Mp + m) * int64_t(N) + n));
+      v.x += p.x;
+      v.y += p.y;
+      v.z += p.z;
+      v.w += p.w;
+    }
+    float o[4] = {v.x, v.y, v.z, v.w};
+    if (res) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        o[j] += res_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(res)[m * ldr + n + j])
+                         : static_cast<const float*>(res)[m * ldr + n + j];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      o[j] = act1(o[j], act);
+      if (round_tf32) o[j] = tf32_rna(o[j]);
+    }
+    if (out_bf16) {
+      __nv_bfloat16* op = static_cast<__nv_bfloat16*>(out) + m * ldo + n;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) op[j] = __float2bfloat16_rn(o[j]);
+    } else {
+      float* op = static_cast<float*>(out) + m * ldo + n;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) op[j] = o[j];
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t conv_gemm_split_reduce(const float* ws, int ks, int64_t Mp, int64_t M, int N, const float* bias,
+                                   const void* res, int res_bf16, int64_t ldr, int act, void* out, int out_bf16,
+                                   int64_t ldo, int round_tf32, cudaStream_t s) {
+  if (N % 4 || (reinterpret_cast<uintptr_t>(ws) & 15u) || (reinterpret_cast<uintptr_t>(bias) & 15u))
+    return cudaErrorInvalidValue;
+  const int64_t total = M * (N / 4);
+  if (total == 0) return cudaSuccess;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  split_reduce_kernel<<<int(blocks), 256, 0, s>>>(ws, ks, Mp, M, N, bias, res, res_bf16, ldr, act, out, out_bf16, ldo,
+                                                  round_tf32);
+  return cudaGetLastError();
+}
+
+int conv_gemm_choose_split(int64_t M, int Cout, int Kpad, int tf32, int x3, int num_sms) {
+  const int bke = tf32 ? BK / 2 : BK;
+  if (Kpad % bke) return 1;
+  const int KT = Kpad / bke;
+  // the widest tile conv_gemm_prepare may pick: the fewest tiles, so the split never overfills a wave
+  const int bn = Cout <= 64 ? 64 : (Cout <= 128 || x3 ? 128 : 256);
+  const int64_t t = ((M + BM - 1) / BM) * ((Cout + bn - 1) / bn);
+  // Measured on B200: ResNet-50 bs64's layer-4 convs (50 tiles, 72 or 32 k-tiles) ran no faster in
+  // two slices (the CTAs' operand traffic sets the pace) and lost the reduce step (+7 us each);
+  // batch-1 ViT-B projections (6-24 tiles) and the bs64 classifier (4 tiles) gained 20-50%. So only
+  // tiles filling under a quarter of the SMs are split, into slices of at least four k-tiles.
+  if (t * 4 > num_sms || KT < 8 || Cout % 4) return 1;
+  int best = 1;
+  for (int d = 2; d <= 16 && d <= KT / 4; ++d)
+    if (KT % d == 0 && t * d <= num_sms) best = d;
+  return best;
+}
+
 void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const void* w, int num_sms) {
   ConvGemmArgs& a = p.args;
   std::memset(&p.tmA, 0, sizeof(p.tmA));
@@ -1421,6 +1521,14 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   std::memset(&p.tmRes, 0, sizeof(p.tmRes));
   // Epilogue: TMA bulk stores when rows and 16-byte chunks are aligned (else direct row stores);
   // a same-dtype, same-shape residual is then streamed into shared memory by the producer warp.
+  // split-K (chosen by the caller with conv_gemm_choose_split): the kernel writes raw fp32 partials
+  // into `out` [ksplit * Mp, ldo] through the TMA-store epilogue; bias, residual, activation and the
+  // output type are conv_gemm_split_reduce's
+  const int KSP = a.ksplit > 1 ? a.ksplit : 1;
+  if (KSP > 1 && (a.out_bf16 || a.res || a.act || a.round_tf32 || a.group_rows || a.Cout % 4 || a.ldo % 4 ||
+                  a.Mp < a.M || a.Mp % BM))
+    throw std::runtime_error("conv_gemm: a split-K launch writes plain fp32 partials (caller error)");
+  const uint64_t out_rows = KSP > 1 ? uint64_t(KSP) * uint64_t(a.Mp) : uint64_t(a.M);
   const int es = a.out_bf16 ? 2 : 4;
   const int epc = 16 / es;
   const uint32_t sc = a.out_bf16 ? 64 : 32;
@@ -1442,7 +1550,7 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
                         (a.ldr * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.res) & 15) == 0;
   // Tile width: residual convs with a ring use at most 128 columns so two residual tiles fit beside
   // a deep operand pipeline.
-  auto tiles = [&](int bn) { return int64_t((a.M + BM - 1) / BM) * ((a.Cout + bn - 1) / bn); };
+  auto tiles = [&](int bn) { return int64_t((a.M + BM - 1) / BM) * ((a.Cout + bn - 1) / bn) * KSP; };
   // (TF32x3 stages hold hi and lo tiles: at most 128 columns so two stages fit)
   int bn = a.Cout <= 64 ? 64 : (a.Cout <= 128 || res_ring || a.x3 ? 128 : 256);
   {
@@ -1465,13 +1573,14 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   const int bke = a.tf32 ? BK / 2 : BK;   // operand elements per 128-byte k-tile row
   if (a.Kpad % bke) throw std::runtime_error("conv_gemm: reduction length not padded to a whole k-tile");
   const int KT = a.Kpad / bke;
+  if (KT % KSP) throw std::runtime_error("conv_gemm: split-K slices must divide the k-tiles");
   // bf16 convs with one or two weight k-tiles (the 1x1 convs from 64 channels, whose epilogue sets
   // the pace) start each accumulator at the bias with one extra MMA, so the epilogue adds none.
   // Measured on ResNet-50 bs512: 1x1 64->64 0.118 -> 0.107 ms, 64->256 -17%, the stage-1 conv with
   // its merged shortcut (two k-tiles) 0.245 -> 0.210 ms; convs with more k-tiles or wider bias tiles
   // lost 1-7% (the extra MMA on the issue path, the bias tile's shared memory).
   const int bias_rows = int((a.Cout + bn - 1) / bn) * bn;
-  a.bias_mma = !a.tf32 && !a.x3 && a.bias && KT <= 2 && bias_rows <= 256 ? 1 : 0;
+  a.bias_mma = !a.tf32 && !a.x3 && a.bias && KT <= 2 && bias_rows <= 256 && KSP == 1 ? 1 : 0;
   const int64_t w_bytes = int64_t(KT) * bn * 128;
   const bool bres = !a.x3 && p.mode != kAGather16 && p.mode != kAGather8 && a.Cout <= bn && w_bytes <= 96 * 1024;
   a.b_resident = bres ? 1 : 0;
@@ -1493,7 +1602,7 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   // 0.203 -> 0.196 ms at bs512 (the 16-channel stem lost 10% with four, its epilogue summing them).
   if (pl == 2 && p.mode == kAIm2col64 && bn == 64 && KT >= 4) pl = 4;
   while (pl > 1 && 2 * pl * bn > 512) pl /= 2;
-  while (pl > KT) pl /= 2;
+  while (pl > KT / KSP) pl /= 2;   // every issuer's partial gets a k-tile of each slice
   if (gather && pl != 1) throw std::runtime_error("conv_gemm: gather modes have a single MMA issuer");
   a.mma_lanes = pl;
   const int stage_bytes = (BM * 128 + (bres ? 0 : bn * 128)) * (a.x3 ? 2 : 1);
@@ -1502,7 +1611,7 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   // residual through a ring decides the shared-memory plan.
   bool ring = false;
   if (out_ok &&
-      encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldo) * es, sc, 32, !a.out_bf16)) {
+      encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), out_rows, uint64_t(a.ldo) * es, sc, 32, !a.out_bf16)) {
     a.epi = 2;
     if (res_mma)   // residual k-tiles: 128 rows x 64 channels, the A operand's layout
       a.res_mma = encode_2d(&p.tmRes, a.res, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldr) * 2, 64, 128) ? 1 : 0;
@@ -1563,11 +1672,12 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   a.out_bufs = ob;
   a.epi_half = 0;
   if (half_for(ob)) {
-    if (!encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), uint64_t(a.M), uint64_t(a.ldo) * es, 32, 32, false,
+    if (!encode_2d(&p.tmOut, a.out, uint64_t(a.Cout), out_rows, uint64_t(a.ldo) * es, 32, 32, false,
                    CU_TENSOR_MAP_SWIZZLE_64B))
       throw std::runtime_error("conv_gemm: output tensor map (32x32 box) rejected");
     a.epi_half = 1;
   }
+  if (KSP > 1 && a.epi != 2) throw std::runtime_error("conv_gemm: split-K partials need the TMA-store epilogue");
   a.stages = stages;
   p.smem = stages * stage_bytes + fixed + rs * rsb;
   int64_t t = tiles(bn);

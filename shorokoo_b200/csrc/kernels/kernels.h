@@ -69,7 +69,21 @@ struct ConvGemmArgs {
   int producers;           // TMA producer threads Q (1-4): thread q loads k-tiles g = q mod Q
                            // (stages is a multiple of P and Q, so every stage has one producer
                            // and one consumer, each in order)
+  int ksplit;              // > 1: split-K over CTAs. Tile (m, n) is computed as ksplit slices of
+                           // Kpad / ksplit each; slice s writes its raw fp32 partial (no bias,
+                           // residual or activation) to rows s * Mp + m of `out` [ksplit * Mp, ldo]
+                           // and conv_gemm_split_reduce finishes the output. 0 or 1: no split.
+  int Mp;                  // ksplit > 1: rows per slice in `out` (M rounded up to 128)
 };
+
+// Slices for split-K: the largest divisor of the k-tile count that keeps the (estimated) tiles in
+// one wave of the SMs, or 1 when the tiles already fill half the SMs or K is short.
+int conv_gemm_choose_split(int64_t M, int Cout, int Kpad, int tf32, int x3, int num_sms);
+// y[m, n] = act(sum_s ws[s * Mp + m, n] + bias[n] (+ res[m, n])) for m < M, n < N (N a multiple of
+// 4), stored as bf16, fp32 or fp32 on the TF32 grid with row pitch ldo (res: bf16 or fp32, pitch ldr).
+cudaError_t conv_gemm_split_reduce(const float* ws, int ks, int64_t Mp, int64_t M, int N, const float* bias,
+                                   const void* res, int res_bf16, int64_t ldr, int act, void* out, int out_bf16,
+                                   int64_t ldo, int round_tf32, cudaStream_t s);
 
 // How the kernel fetches its A operand (chosen from the geometry by conv_gemm_a_mode):
 //   0  A is a row matrix: 2D TMA tiles

@@ -750,7 +750,21 @@ void Plan::plan_conv(const Op& op) {
                            (s2d ? " s2d" : "") + (op.residual >= 0 ? " +res" : "") +
                            (op.concat >= 0 ? " +proj " + std::to_string(C2) : "") +
                            (prec == 1 ? " tf32" : (prec == 2 ? " tf32x3" : ""));
-  add_step(kind, reads, {y}, [=]() {
+  // Split-K when the output tiles leave most SMs idle (small batches, the deep layers): slices of
+  // the reduction run on separate CTAs into fp32 partials, a reduce step finishes the output.
+  const int64_t Mrows = N * Ho * Wo;
+  const int ksplit = grp_rows == 0 && op.residual_mode == 0
+                         ? k::conv_gemm_choose_split(Mrows, int(Cout), int(Kpad), f32, x3, sms)
+                         : 1;
+  const int64_t Mp = round_up(Mrows, 128);
+  DevTensor ws, zb;
+  if (ksplit > 1) {
+    ws = alloc_contig({ksplit * Mp, Cout}, false);
+    std::vector<float> z(size_t(round_up(Cout, 256)), 0.f);
+    zb.buf = -1;
+    zb.off = add_weight_bytes(z.data(), z.size() * 4);
+  }
+  add_step(kind + (ksplit > 1 ? " split" + std::to_string(ksplit) : ""), reads, {ksplit > 1 ? ws : y}, [=]() {
     auto p = std::make_shared<k::ConvGemmPlan>();
     k::ConvGemmArgs& a = p->args;
     std::memset(&a, 0, sizeof(a));
@@ -799,9 +813,42 @@ void Plan::plan_conv(const Op& op) {
       a.a2_H = int(x2.shape[2]);
       a.a2_W = int(x2.shape[3]);
     }
+    if (ksplit > 1) {   // raw partials; bias, residual, activation and output type in the reduce
+      a.ksplit = ksplit;
+      a.Mp = int(Mp);
+      a.out = ptr(ws);
+      a.out_bf16 = 0;
+      a.ldo = Cout;
+      a.bias = static_cast<const float*>(ptr(zb));
+      a.res = nullptr;
+      a.res_bf16 = 0;
+      a.act = 0;
+      a.round_tf32 = 0;
+    }
     k::conv_gemm_prepare(*p, ptr(x), Cp, ptr(wt), sms);
     return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::conv_gemm_launch(*p, s); });
   });
+  if (ksplit > 1) add_split_reduce(ws, ksplit, Mp, Mrows, Cout, bt, r, ldr, op.act, y, round_out);
+}
+
+// The reduce step of a split-K contraction: y = act(sum of the slices' partials + bias (+ residual)).
+void Plan::add_split_reduce(const DevTensor& ws, int ksplit, int64_t Mp, int64_t M, int64_t Cout, const DevTensor& bias,
+                            const DevTensor& res, int64_t ldr, int act, const DevTensor& y, bool round_tf32) {
+  std::vector<DevTensor> reads{ws};
+  if (res.valid()) reads.push_back(res);
+  add_step("split_reduce " + std::to_string(ksplit) + "x" + std::to_string(M) + "x" + std::to_string(Cout), reads, {y},
+           [=]() {
+             const float* wp = static_cast<const float*>(ptr(ws));
+             const float* bp = static_cast<const float*>(ptr(bias));
+             const void* rp = res.valid() ? ptr(res) : nullptr;
+             const int rb = res.valid() ? int(res.bf16) : 0;
+             void* yp = ptr(y);
+             const int yb = int(y.bf16);
+             const int rt = round_tf32 ? 1 : 0;
+             return std::function<cudaError_t(cudaStream_t)>([=](cudaStream_t s) {
+               return k::conv_gemm_split_reduce(wp, ksplit, Mp, M, int(Cout), bp, rp, rb, ldr, act, yp, yb, Cout, rt, s);
+             });
+           });
 }
 
 void Plan::plan_gemm(const Op& op) {
@@ -849,9 +896,18 @@ void Plan::plan_gemm(const Op& op) {
   const bool f32 = tf32;
   const bool round_out = out_cls == kStoreTf32;   // the next MMA reads it as TF32
   const int x3 = prec == 2;
+  const int ksplit = k::conv_gemm_choose_split(M, int(Nn), int(Kpad), f32 ? 1 : 0, x3, sms);
+  const int64_t Mp = round_up(M, 128);
+  DevTensor ws, zb;
+  if (ksplit > 1) {
+    ws = alloc_contig({ksplit * Mp, Nn}, false);
+    std::vector<float> z(size_t(round_up(Nn, 256)), 0.f);
+    zb.buf = -1;
+    zb.off = add_weight_bytes(z.data(), z.size() * 4);
+  }
   add_step("gemm " + std::to_string(M) + "x" + std::to_string(K) + "->" + std::to_string(Nn) +
-               (prec == 1 ? " tf32" : (prec == 2 ? " tf32x3" : "")),
-           reads, {y}, [=]() {
+               (prec == 1 ? " tf32" : (prec == 2 ? " tf32x3" : "")) + (ksplit > 1 ? " split" + std::to_string(ksplit) : ""),
+           reads, {ksplit > 1 ? ws : y}, [=]() {
     auto p = std::make_shared<k::ConvGemmPlan>();
     k::ConvGemmArgs& a = p->args;
     std::memset(&a, 0, sizeof(a));
@@ -880,9 +936,22 @@ void Plan::plan_gemm(const Op& op) {
     a.round_tf32 = round_out;
     a.x3 = x3;
     a.w_lo_row = int(w_lo_row);
+    if (ksplit > 1) {   // raw partials; bias, residual, activation and output type in the reduce
+      a.ksplit = ksplit;
+      a.Mp = int(Mp);
+      a.out = ptr(ws);
+      a.out_bf16 = 0;
+      a.ldo = Nn;
+      a.bias = static_cast<const float*>(ptr(zb));
+      a.res = nullptr;
+      a.res_bf16 = 0;
+      a.act = 0;
+      a.round_tf32 = 0;
+    }
     k::conv_gemm_prepare(*p, ptr(x), lda, ptr(wt), sms);
     return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::conv_gemm_launch(*p, s); });
   });
+  if (ksplit > 1) add_split_reduce(ws, ksplit, Mp, M, Nn, bt, r, Nn, op.act, y, round_out);
 }
 
 void Plan::plan_maxpool(const Op& op) {

@@ -149,6 +149,8 @@ class Plan {
   void plan_global_pool(const Op& op);
   void plan_group_norm(const Op& op);
   void plan_layer_norm(const Op& op);
+  void add_split_reduce(const DevTensor& ws, int ksplit, int64_t Mp, int64_t M, int64_t Cout, const DevTensor& bias,
+                        const DevTensor& res, int64_t ldr, int act, const DevTensor& y, bool round_tf32);
   void plan_attention(const Op& op);
   void plan_elementwise(const Op& op);
   void plan_view(const Op& op);

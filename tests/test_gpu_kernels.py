@@ -8,7 +8,7 @@ shortcuts merged into the conv that adds them."""
 import numpy as np
 import pytest
 
-from helpers import assert_close, conv_case, run_backend, run_oracle
+from helpers import BF16_TOL, assert_close, conv_case, run_backend, run_oracle
 from shorokoo_b200 import B200InferenceSessionFactory
 from shorokoo_b200.emit import graphs
 
@@ -178,6 +178,37 @@ def test_stem_pool_not_fused_when_the_conv_output_is_also_read():
     ref = run_oracle(case)
     for g, r in zip(got, ref):
         assert_close(g, r, what="stem with its conv output as a graph output")
+
+
+# Split-K: contractions whose output tiles would fill under half the SMs run as slices of the
+# reduction on separate CTAs (fp32 partials), then one reduce step adds the bias and residual and
+# applies the activation and output type. Shapes: a batch-1 projection (1 M tile, 16 slices), a
+# ragged M with ReLU, a 1x1 conv with a bf16 residual added in the reduce, a 3x3 conv with Sigmoid
+# over 9 slices, a strided 3x3 512->512 conv over 12 slices, and TF32 operands.
+@pytest.mark.parametrize("kind,kw,prec", [
+    ("gemm", dict(batch=1, widths=(2048, 1000)), "bf16"),
+    ("gemm", dict(batch=197, widths=(768, 3072, 768)), "bf16"),
+    ("conv", dict(n=2, c=512, cout=128, k=1, pads=[0, 0, 0, 0], h=7, w=7, bn=True, residual=True, relu=True), "bf16"),
+    ("conv", dict(n=1, c=128, cout=96, k=3, h=9, w=11, sigmoid=True), "bf16"),
+    ("conv", dict(n=2, c=512, cout=512, k=3, stride=2, h=14, w=14, bn=True, relu=True), "bf16"),
+    ("gemm", dict(batch=200, widths=(1024, 512)), "tf32"),
+])
+def test_split_k(kind, kw, prec):
+    if kind == "gemm":
+        case = graphs.mlp(seed=9, bias_scale=0.5, **kw)
+    else:
+        case = conv_case(seed=19, **kw)
+    f = B200InferenceSessionFactory(num_devices=1, precision=prec)
+    sess = f.CreateSession(case.model)
+    feeds = {nm: f.CreateTensor(a) for nm, a in case.inputs}
+    kinds = [k for k, _ in sess.profile(feeds, iters=1)]
+    assert any(" split" in k for k in kinds) and any(k.startswith("split_reduce") for k in kinds), kinds
+    outs = sess.Run(feeds, case.output_names)
+    got = outs[0].numpy()
+    for o in outs:
+        o.Dispose()
+    sess.Dispose()
+    assert_close(got, run_oracle(case)[0], tol=BF16_TOL if prec == "bf16" else 2e-3, what=f"split-K {kind} {kw}")
 
 
 def _halo_case(n, h, w, relu, seed=41):
