@@ -857,6 +857,9 @@ constexpr int kStemKT = 4;                      // k-tiles: filter columns
 constexpr uint32_t kStemAStage = 4 * BM * 32;   // 16 KB: four 4 KB sub-tiles
 constexpr uint32_t kStemBBytes = 64 * 128;      // one 64 x 64 bf16 weight k-tile
 constexpr uint32_t kStemRingRow = 128 * 128;    // 128 pixels x 64 bf16 channels
+// TMEM accumulators: the MMA issuer may run this many conv rows ahead of the epilogue, whose pool
+// rows come in bursts (every second conv row also computes a 3x3 max over three ring rows)
+constexpr int kStemAcc = 4;
 
 // The conv rows CTA `cta` computes, in order: calls f(n, r, pool) for each, where pool says that the
 // row completes pool row r / 2 (r odd, and not the halo row of the range's first pool row).
@@ -893,7 +896,7 @@ __global__ void __launch_bounds__(512, 1)
   const int STAGES = a.stages;
   const int NP = a.producers;
   const int PE = a.mma_lanes;
-  const uint32_t TMEM_COLS = uint32_t(2 * PE * 64);
+  const uint32_t TMEM_COLS = uint32_t(kStemAcc * PE * 64);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -903,8 +906,8 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sBias + 64);
   uint64_t* empty = full + kMaxStages;
   uint64_t* accf = empty + kMaxStages;
-  uint64_t* acce = accf + 2;
-  uint64_t* bfull = acce + 2;
+  uint64_t* acce = accf + kStemAcc;
+  uint64_t* bfull = acce + kStemAcc;
   uint64_t* ring_full = bfull + 1;   // the 8 epilogue warps wrote a pool row's conv rows into the ring
   uint64_t* pool_done = ring_full + 1;   // the 8 epilogue warps finished computing that pool row
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(pool_done + 1);
@@ -916,7 +919,7 @@ __global__ void __launch_bounds__(512, 1)
       mbar_init(&full[s], 1u);
       mbar_init(&empty[s], 1u);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStemAcc; ++i) {
       mbar_init(&accf[i], uint32_t(PE));
       mbar_init(&acce[i], 8u);
     }
@@ -974,8 +977,8 @@ __global__ void __launch_bounds__(512, 1)
       uint32_t phase = 0;
       if (mbar_wait(bfull, 0u, abort_flag, a.err, 128u)) {
         stem_rows(a, blockIdx.x, gridDim.x, [&](int, int, bool) {
-          const int acc = it & 1;
-          const uint32_t aph = uint32_t(it >> 1) & 1u;
+          const int acc = it % kStemAcc;
+          const uint32_t aph = uint32_t(it / kStemAcc) & 1u;
           if (!mbar_wait(&acce[acc], aph ^ 1u, abort_flag, a.err, 2u)) return false;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + uint32_t((acc * PE + mid) * 64);
@@ -1013,8 +1016,8 @@ __global__ void __launch_bounds__(512, 1)
     int it = 0;
     int pc = 0;   // pool rows this CTA has completed
     stem_rows(a, blockIdx.x, gridDim.x, [&](int n, int r, bool pool) {
-      const int acc = it & 1;
-      const uint32_t aph = uint32_t(it >> 1) & 1u;
+      const int acc = it % kStemAcc;
+      const uint32_t aph = uint32_t(it / kStemAcc) & 1u;
       if (!mbar_wait(&accf[acc], aph, abort_flag, a.err, 8u)) return false;
       tc_fence_after();
       float v[32];
