@@ -579,9 +579,47 @@ Session::Pipeline::~Pipeline() {
   if (d2h) cudaStreamDestroy(d2h);
 }
 
+int Session::staging_mode(const std::vector<std::shared_ptr<HostValue>>& inputs) {
+  for (const auto& v : inputs)
+    if (numel(v->shape) > kPlanTimeInputMaxElems && !v->pinned && !v->dev) return 1;
+  return 0;
+}
+
+// Milliseconds per source byte of the host staging of a pageable input into a page-locked slot
+// (narrowed float32 -> bfloat16, or copied), on `threads` host threads; measured once per process.
+static double host_stage_ms_per_byte(unsigned threads, bool narrow) {
+  static std::mutex mu;
+  static std::map<std::pair<unsigned, bool>, double> cache;
+  std::lock_guard<std::mutex> l(mu);
+  auto key = std::make_pair(threads, narrow);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  const size_t n = size_t(16) << 20;   // floats (64 MB)
+  std::vector<float> src(n, 1.f);
+  void* dst = nullptr;
+  double r = 1.0 / 20e6;   // 20 GB/s if the measurement cannot run
+  if (cudaHostAlloc(&dst, n * 4, cudaHostAllocPortable) == cudaSuccess) {
+    double best = 1e30;
+    for (int rep = 0; rep < 2; ++rep) {
+      const auto t0 = std::chrono::steady_clock::now();
+      if (narrow)
+        par_f32_to_bf16(static_cast<uint16_t*>(dst), src.data(), n, threads);
+      else
+        par_memcpy(dst, src.data(), n * 4, threads);
+      best = std::min(best, std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count());
+    }
+    r = best / double(n * 4);
+    cudaFreeHost(dst);
+  }
+  cudaGetLastError();
+  cache[key] = r;
+  return r;
+}
+
 void Session::maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs) {
-  if (ps.pipe_checked) return;
-  ps.pipe_checked = true;
+  const int mode = staging_mode(inputs);
+  if (ps.pipe_checked[mode]) return;
+  ps.pipe_checked[mode] = true;
   if (!ps.separable || ps.batch < 2) return;
   bool may_cut = true;
   if (const char* e = std::getenv("SHOROKOO_B200_PIPELINE"))
@@ -592,21 +630,21 @@ void Session::maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_pt
   const unsigned threads = std::max(2u, 16u / unsigned(n));
   std::vector<std::shared_ptr<Pipeline>> pipes(n);
   if (n == 1) {
-    pipes[0] = build_pipeline(ps, 0, inputs, may_cut, threads);
+    pipes[0] = build_pipeline(ps, 0, inputs, may_cut, threads, mode == 1);
   } else {
     std::vector<std::thread> th;
     for (size_t si = 0; si < n; ++si)
-      th.emplace_back([&, si] { pipes[si] = build_pipeline(ps, si, inputs, may_cut, threads); });
+      th.emplace_back([&, si] { pipes[si] = build_pipeline(ps, si, inputs, may_cut, threads, mode == 1); });
     for (auto& t : th) t.join();
   }
   for (const auto& p : pipes)
     if (!p) return;   // (a shard whose pipeline could not be set up: every shard runs unstaged)
-  ps.pipes = std::move(pipes);
+  ps.pipes[mode] = std::move(pipes);
 }
 
 std::shared_ptr<Session::Pipeline> Session::build_pipeline(PlanSet& ps, size_t si,
                                                            const std::vector<std::shared_ptr<HostValue>>& inputs,
-                                                           bool may_cut, unsigned host_threads) {
+                                                           bool may_cut, unsigned host_threads, bool pageable) {
   const Shard& sh = ps.shards[si];
   const int64_t rows_total = ps.sharded ? sh.count : ps.batch;
   // Below kPipeMinBytes of copies (in + out) they are too short to be worth hiding (at 32 MiB the
@@ -697,22 +735,35 @@ std::shared_ptr<Session::Pipeline> Session::build_pipeline(PlanSet& ps, size_t s
         t_chunk.push_back(t >= 0 ? t : P->plans[c]->time_kernels(cs, 3));
       }
       const double ms_per_byte = copy_ms_per_byte(P->copy);
+      // Inputs in pageable memory are staged by the host first (narrowed to bf16 where the plan
+      // reads them as bf16, halving the transfer): a pipeline stage of its own, so the host's pass
+      // over chunk c overlaps the transfer and kernels of the chunks before it.
+      double xfer_bytes = 0, host_ms = 0;
+      for (const auto& b : sh.plan->inputs()) {
+        const HostValue& v = *inputs[size_t(b.index)];
+        const bool narrow = pageable && b.bf16_ok && v.elem_type == DT_FLOAT;
+        xfer_bytes += narrow ? double(b.bytes) / 2 : double(b.bytes);
+        if (pageable) host_ms += double(b.bytes) * host_stage_ms_per_byte(host_threads, narrow);
+      }
       const double rows = double(rows_total);
-      double copy_end = 0, comp_end = 0, back_end = 0;
-      std::vector<double> comp_ends;
+      double host_end = 0, copy_end = 0, comp_end = 0, back_end = 0;
+      std::vector<double> copy_ends, comp_ends;
       for (size_t c = 0; c < P->rows.size(); ++c) {
         const double share = double(P->rows[c]) / rows;
-        double start = copy_end;
-        if (c >= 2) start = std::max(start, comp_ends[c - 2]);   // its staging slot is free
-        copy_end = start + share * double(in_bytes) * ms_per_byte;
+        // host slot c % 2 is free once chunk c - 2's transfer out of it is done
+        host_end = std::max(host_end, c >= 2 ? copy_ends[c - 2] : 0.0) + share * host_ms;
+        double start = std::max(copy_end, host_end);
+        if (c >= 2) start = std::max(start, comp_ends[c - 2]);   // its device staging slot is free
+        copy_end = start + share * xfer_bytes * ms_per_byte;
+        copy_ends.push_back(copy_end);
         comp_end = std::max(comp_end, copy_end) + t_chunk[c];
         comp_ends.push_back(comp_end);
         back_end = std::max(back_end, comp_end) + share * double(out_bytes) * ms_per_byte;
       }
-      const double t_seq = double(in_bytes + out_bytes) * ms_per_byte + t_full;
+      const double t_seq = host_ms + (xfer_bytes + double(out_bytes)) * ms_per_byte + t_full;
       if (debug_level() >= 1)
-        std::fprintf(stderr, "[shorokoo_b200] pipeline model: %.3f ms pipelined vs %.3f ms in one piece (device %d)\n",
-                     back_end, t_seq, P->device);
+        std::fprintf(stderr, "[shorokoo_b200] pipeline model: %.3f ms pipelined vs %.3f ms in one piece (device %d%s)\n",
+                     back_end, t_seq, P->device, pageable ? ", pageable inputs" : "");
       if (back_end >= 0.97 * t_seq) {
         P->rows.clear();
         P->plans.clear();
@@ -762,17 +813,17 @@ std::shared_ptr<Session::Pipeline> Session::build_pipeline(PlanSet& ps, size_t s
 // The pipelines run when they cut a shard into chunks, or when an input sits in pageable memory
 // (staged through page-locked memory either way).
 bool Session::use_pipelines(const PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs) const {
-  if (ps.pipes.empty()) return false;
-  for (const auto& p : ps.pipes)
+  const int mode = staging_mode(inputs);
+  if (ps.pipes[mode].empty()) return false;
+  if (mode == 1) return true;   // pageable inputs: always staged
+  for (const auto& p : ps.pipes[mode])
     if (p->rows.size() > 1) return true;
-  for (const auto& v : inputs)
-    if (numel(v->shape) > kPlanTimeInputMaxElems && !v->pinned && !v->dev) return true;
   return false;
 }
 
-void Session::run_pipelined(PlanSet& ps, size_t si, const std::vector<std::shared_ptr<HostValue>>& inputs,
+void Session::run_pipelined(PlanSet& ps, int mode, size_t si, const std::vector<std::shared_ptr<HostValue>>& inputs,
                             const std::vector<std::shared_ptr<HostValue>>& outs) {
-  Pipeline& P = *ps.pipes[si];
+  Pipeline& P = *ps.pipes[mode][si];
   const Shard& sh = ps.shards[si];
   ck(cudaSetDevice(P.device), "cudaSetDevice");
   cudaStream_t cs = streams_[size_t(sh.device)];
@@ -982,16 +1033,18 @@ std::vector<std::shared_ptr<HostValue>> Session::run(const std::vector<std::shar
     }
   }
   if (pipes) {
-    if (ps->pipes.size() == 1) {
-      run_pipelined(*ps, 0, inputs, outs);
+    const int mode = staging_mode(inputs);
+    const auto& pl = ps->pipes[mode];
+    if (pl.size() == 1) {
+      run_pipelined(*ps, mode, 0, inputs, outs);
     } else {   // one host thread per device
-      std::vector<std::string> errs(ps->pipes.size());
-      std::vector<int32_t> codes(ps->pipes.size(), 0);
+      std::vector<std::string> errs(pl.size());
+      std::vector<int32_t> codes(pl.size(), 0);
       std::vector<std::thread> th;
-      for (size_t si = 0; si < ps->pipes.size(); ++si)
+      for (size_t si = 0; si < pl.size(); ++si)
         th.emplace_back([&, si] {
           try {
-            run_pipelined(*ps, si, inputs, outs);
+            run_pipelined(*ps, mode, si, inputs, outs);
           } catch (const Error& e) {
             errs[si] = e.what();
             codes[si] = e.code;
@@ -1103,7 +1156,7 @@ std::pair<int64_t, int64_t> Session::transfer_bytes(const std::vector<std::share
   for (const auto& sh : ps->shards)
     for (const auto& b : sh.plan->inputs()) {
       const HostValue& v = *inputs[size_t(b.index)];
-      const bool narrow = !ps->pipes.empty() && !v.pinned && !v.dev && b.bf16_ok && v.elem_type == DT_FLOAT;
+      const bool narrow = !ps->pipes[1].empty() && !v.pinned && !v.dev && b.bf16_ok && v.elem_type == DT_FLOAT;
       h2d += int64_t(narrow ? b.bytes / 2 : b.bytes);
     }
   for (size_t j = 0; j < ps->out_shapes.size(); ++j)

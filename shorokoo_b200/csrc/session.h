@@ -117,8 +117,10 @@ class Session {
     bool sharded = false;
     int64_t batch = -1;        // common leading dimension of the device inputs (-1 none, -2 mixed)
     bool separable = false;    // the graph treats batch rows independently
-    bool pipe_checked = false;
-    std::vector<std::shared_ptr<Pipeline>> pipes;   // one per shard, or none
+    bool pipe_checked[2] = {false, false};
+    // one per shard, or none: [0] for inputs in page-locked (or device) memory, [1] for inputs in
+    // pageable memory, whose host staging is a pipeline stage of its own
+    std::vector<std::shared_ptr<Pipeline>> pipes[2];
   };
 
   OnnxModel model_;
@@ -134,11 +136,13 @@ class Session {
   std::shared_ptr<PlanSet> get_plans(const std::vector<std::shared_ptr<HostValue>>& inputs);
   void maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs);
   std::shared_ptr<Pipeline> build_pipeline(PlanSet& ps, size_t si, const std::vector<std::shared_ptr<HostValue>>& inputs,
-                                           bool may_cut, unsigned host_threads);
+                                           bool may_cut, unsigned host_threads, bool pageable);
+  // 1 when an input the plan copies lies in pageable host memory, else 0
+  static int staging_mode(const std::vector<std::shared_ptr<HostValue>>& inputs);
   bool use_pipelines(const PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs) const;
   void run_shards(PlanSet& ps, const std::vector<std::shared_ptr<HostValue>>& inputs,
                   const std::vector<std::shared_ptr<HostValue>>& outs);
-  void run_pipelined(PlanSet& ps, size_t si, const std::vector<std::shared_ptr<HostValue>>& inputs,
+  void run_pipelined(PlanSet& ps, int mode, size_t si, const std::vector<std::shared_ptr<HostValue>>& inputs,
                      const std::vector<std::shared_ptr<HostValue>>& outs);
   std::vector<InputSpec> specs_for(const std::vector<std::shared_ptr<HostValue>>& inputs, int64_t batch_begin,
                                    int64_t batch_count, bool shard) const;
