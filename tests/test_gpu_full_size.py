@@ -1,6 +1,6 @@
 """GPU parity of the five benchmark configurations at their stated sizes, through the plugin
 interface (Run with host buffers, so the micro-batch pipeline and its chunk plans run exactly as a
-caller gets them), against the fp32 oracle at the north-star gate (normwise max|gpu - ref| /
+caller gets them), against the fp32 oracle at the bf16 accuracy gate (normwise max|gpu - ref| /
 max|ref| per output, bf16 1e-2):
 
 * StackedLinear n=1024 depth 8, batch 4096, seed 42      every row checked

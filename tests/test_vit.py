@@ -109,12 +109,13 @@ def test_layer_norm_and_gelu_kernels():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("prec,tol", [("bf16", BF16_TOL), ("tf32", 2e-3)])
-def test_vit_tiny_two_blocks(prec, tol):
+@pytest.mark.parametrize("variant,layers,prec,tol", [("tiny", 2, "bf16", BF16_TOL), ("tiny", 2, "tf32", 2e-3),
+                                                     ("small", 1, "bf16", BF16_TOL)])
+def test_vit_blocks(variant, layers, prec, tol):
     from shorokoo_b200 import B200InferenceSessionFactory
-    case = graphs.vit("tiny", layers=2, affine_scale=0.1)
+    case = graphs.vit(variant, layers=layers, affine_scale=0.1)
     got = run_backend(case, factory=B200InferenceSessionFactory(num_devices=1, precision=prec))[0]
-    assert_close(got, run_oracle(case)[0], tol=tol, what=f"ViT-Ti 2 blocks ({prec})")
+    assert_close(got, run_oracle(case)[0], tol=tol, what=f"ViT-{variant} {layers} blocks ({prec})")
 
 
 @pytest.mark.gpu
