@@ -386,6 +386,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -444,6 +445,11 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  if (BRES && warp == 0 && lane == 0) {   // the whole weight matrix, once (a single N tile)
+    mbar_expect_tx(bfull, uint32_t(KT) * B_BYTES);
+    for (int kt = 0; kt < KT; ++kt) tma_load_2d(sB + kt * B_BYTES, &tmB, kt * BKE, 0, bfull);
+  }
+  pdl_wait();   // the previous kernel's outputs (and the buffers this one overwrites) are settled
 
   const int tiles_m = (a.M + BM - 1) / BM;
   const int tiles_n = (a.Cout + BN - 1) / BN;
@@ -460,10 +466,6 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
       int owner = 0;   // producer of the current k-tile (k-tiles are dealt round-robin)
       const int hw_out = a.Ho * a.Wo;
       const int cblocks = a.Cp / BKE;   // 128-byte channel blocks per filter tap (MODE 3)
-      if (BRES && pid == 0) {   // the whole weight matrix, once (a single N tile)
-        mbar_expect_tx(bfull, uint32_t(KT) * B_BYTES);
-        for (int kt = 0; kt < KT; ++kt) tma_load_2d(sB + kt * B_BYTES, &tmB, kt * BKE, 0, bfull);
-      }
       int it = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
         const int tmn = t / KS, kt0 = (t - tmn * KS) * KTS;
@@ -913,6 +915,7 @@ __global__ void __launch_bounds__(512, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(pool_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -940,15 +943,16 @@ __global__ void __launch_bounds__(512, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  if (warp == 0 && lane == 0) {   // the weights, once
+    mbar_expect_tx(bfull, uint32_t(kStemKT) * kStemBBytes);
+    for (int kt = 0; kt < kStemKT; ++kt) tma_load_2d(sB + kt * kStemBBytes, &tmB, kt * BK, 0, bfull);
+  }
+  pdl_wait();
 
   if (warp == 0 || (warp >= 10 && warp <= 12)) {
     // ---- TMA producers: k-tiles dealt round-robin over NP threads ----
     const int pid = warp == 0 ? 0 : warp - 9;
     if (lane == 0 && pid < NP) {
-      if (pid == 0) {
-        mbar_expect_tx(bfull, uint32_t(kStemKT) * kStemBBytes);
-        for (int kt = 0; kt < kStemKT; ++kt) tma_load_2d(sB + kt * kStemBBytes, &tmB, kt * BK, 0, bfull);
-      }
       int stage = 0, owner = 0;
       uint32_t phase = 0;
       stem_rows(a, blockIdx.x, gridDim.x, [&](int n, int r, bool) {
@@ -1140,6 +1144,7 @@ __global__ void __launch_bounds__(512, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bfull + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -1166,14 +1171,17 @@ __global__ void __launch_bounds__(512, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  if (warp == 0 && lane == 0) {   // the weights, once
+    mbar_expect_tx(bfull, uint32_t(kHaloTaps) * kHaloBBytes);
+    for (int t = 0; t < kHaloTaps; ++t) tma_load_2d(sB + t * kHaloBBytes, &tmB, t * BK, 0, bfull);
+  }
+  pdl_wait();
 
   const int tpi = (a.H + R - 1) / R;   // tiles per image
   const int total = a.N * tpi;
 
   if (warp == 0) {
-    if (lane == 0) {   // ---- producer: the weights once, then one halo box per tile ----
-      mbar_expect_tx(bfull, uint32_t(kHaloTaps) * kHaloBBytes);
-      for (int t = 0; t < kHaloTaps; ++t) tma_load_2d(sB + t * kHaloBBytes, &tmB, t * BK, 0, bfull);
+    if (lane == 0) {   // ---- producer: one halo box per tile (the weights came before the wait) ----
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -1354,10 +1362,27 @@ cudaError_t ensure_attr() {
   return e;
 }
 
+// Launch with programmatic stream serialisation (the kernel may start before its predecessor in the
+// stream has finished; it waits for it after its prologue).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), int grid, int threads, int smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(unsigned(threads));
+  cfg.dynamicSmemBytes = size_t(smem);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 template <int BN, int MODE, int PREC>
 cudaError_t launch_t(const ConvGemmPlan& p, cudaStream_t s) {
-  conv_gemm_kernel<BN, MODE, PREC><<<p.grid, kThreads<MODE, PREC>, p.smem, s>>>(p.tmA, p.tmB, p.tmOut, p.tmRes, p.args);
-  return cudaGetLastError();
+  return launch_pdl(conv_gemm_kernel<BN, MODE, PREC>, p.grid, kThreads<MODE, PREC>, p.smem, s, p.tmA, p.tmB, p.tmOut,
+                    p.tmRes, p.args);
 }
 
 // TF32 / TF32x3 operands use the row-matrix, 16-byte gather and 128-byte im2col modes only.
@@ -1779,8 +1804,7 @@ void conv3x3_prepare(Conv3x3Plan& p, const void* w, int num_sms) {
 }
 
 cudaError_t conv3x3_launch(const Conv3x3Plan& p, cudaStream_t s) {
-  conv3x3_halo_kernel<<<p.grid, 512, p.smem, s>>>(p.tmA, p.tmB, p.tmOut, p.args);
-  return cudaGetLastError();
+  return launch_pdl(conv3x3_halo_kernel, p.grid, 512, p.smem, s, p.tmA, p.tmB, p.tmOut, p.args);
 }
 
 bool stem_pool_supported(int Cout, int Ho, int Wo, int KH, int KW) {
@@ -1832,8 +1856,7 @@ void stem_pool_prepare(StemPoolPlan& p, const void* w, int num_sms) {
 }
 
 cudaError_t stem_pool_launch(const StemPoolPlan& p, cudaStream_t s) {
-  stem_pool_kernel<<<p.grid, 512, p.smem, s>>>(p.tmA, p.tmB, p.args);
-  return cudaGetLastError();
+  return launch_pdl(stem_pool_kernel, p.grid, 512, p.smem, s, p.tmA, p.tmB, p.args);
 }
 
 cudaError_t conv_gemm_launch(const ConvGemmPlan& p, cudaStream_t s) {

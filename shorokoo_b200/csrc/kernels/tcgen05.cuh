@@ -214,6 +214,15 @@ __host__ __device__ constexpr uint32_t idesc_mma(int M, int N, bool tf32) {
          (uint32_t(M >> 4) << 24);
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialisation may start
+// while the kernel before it in the stream is still running. Each persistent tcgen05 kernel lets its
+// successor launch from its first instruction (the successor's CTAs then take each SM as soon as
+// this kernel's CTA there exits) and waits for its predecessor's completion (and memory) after its
+// own prologue (barriers, TMEM, tensor-map prefetch, resident weights) and before its first access
+// to an activation buffer.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 }  // namespace
 }  // namespace k
 }  // namespace sb
