@@ -51,6 +51,23 @@ def test_two_device_shards_match_one_device(case_fn):
         assert_close(b, r, what="two-device shards vs oracle")
 
 
+def test_all_visible_devices_shard_and_match_one_device():
+    """Every visible GPU (up to 8): ResNet-18 batch 13 (ragged shards) and the MLP, against one
+    device and the oracle."""
+    n = min(_gpus(), 8)
+    if n < 3:
+        pytest.skip("needs three or more GPUs")
+    for case in (graphs.resnet(depth=18, batch=13, hw=(64, 64), seed=6),
+                 graphs.mlp(batch=1001, widths=(256, 512, 128), seed=4, bias_scale=0.5)):
+        one = run_backend(case, num_devices=1)
+        many = run_backend(case, num_devices=n)
+        ref = run_oracle(case)
+        for a, b, r in zip(one, many, ref):
+            assert a.shape == b.shape == r.shape
+            assert_close(b, a, what=f"{n}-device shards vs one device")
+            assert_close(b, r, what=f"{n}-device shards vs oracle")
+
+
 def _run(case, num_devices, wrap):
     from shorokoo_b200 import B200InferenceSessionFactory
     f = B200InferenceSessionFactory(num_devices=num_devices)
