@@ -196,6 +196,9 @@ def main():
     if args.devices > 1 and world > 1:
         ap.error("--devices N runs one process over N GPUs; do not combine it with torchrun ranks")
 
+    if world > 1 and "SHOROKOO_B200_HOST_THREADS" not in os.environ:
+        # one process per GPU shares the host: each stages its shard with its share of the cores
+        os.environ["SHOROKOO_B200_HOST_THREADS"] = str(max(2, len(os.sched_getaffinity(0)) // world))
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(local)

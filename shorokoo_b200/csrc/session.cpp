@@ -579,6 +579,20 @@ Session::Pipeline::~Pipeline() {
   if (d2h) cudaStreamDestroy(d2h);
 }
 
+// Host threads for the staging copies of one session: SHOROKOO_B200_HOST_THREADS, else 16 (the
+// narrowing of a large batch saturates the host's memory bandwidth at about 16). Processes that share
+// the host (one per GPU) divide them.
+static unsigned host_staging_threads() {
+  static const unsigned n = [] {
+    if (const char* e = std::getenv("SHOROKOO_B200_HOST_THREADS")) {
+      const int v = std::atoi(e);
+      if (v >= 1 && v <= 256) return unsigned(v);
+    }
+    return 16u;
+  }();
+  return n;
+}
+
 int Session::staging_mode(const std::vector<std::shared_ptr<HostValue>>& inputs) {
   for (const auto& v : inputs)
     if (numel(v->shape) > kPlanTimeInputMaxElems && !v->pinned && !v->dev) return 1;
@@ -627,7 +641,7 @@ void Session::maybe_build_pipeline(PlanSet& ps, const std::vector<std::shared_pt
   // Every shard builds its pipeline on its own device (in parallel, like the shards' plans); the
   // host staging copies of concurrent shards share the host's threads.
   const size_t n = ps.shards.size();
-  const unsigned threads = std::max(2u, 16u / unsigned(n));
+  const unsigned threads = std::max(2u, host_staging_threads() / unsigned(n));
   std::vector<std::shared_ptr<Pipeline>> pipes(n);
   if (n == 1) {
     pipes[0] = build_pipeline(ps, 0, inputs, may_cut, threads, mode == 1);
