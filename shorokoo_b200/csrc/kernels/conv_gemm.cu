@@ -844,25 +844,32 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
 
 // ---- stem convolution + 3x3/2 max pool ----------------------------------------------------------
 // The ResNet stem (7x7/2 conv over 3 channels, run as a 4x4 stride-1 conv over the 2x2
-// space-to-depth image of 16-channel pixels) with bias, ReLU and the following MaxPool 3x3 / stride
-// 2 / pad 1 in one kernel. A tile is one conv output row (Wo <= 128 pixels; the tile's remaining
-// rows see zero fill and are dropped). CTA b walks a contiguous range of pool rows: for each it
-// computes conv rows 2po and 2po + 1 (and, at the start of its range, the halo row 2po - 1), keeps
-// the last three conv rows in a shared-memory ring and, after each odd row, the epilogue warps write
-// one pool row. The conv output (1.6 MB per 224x224 image) never reaches global memory.
-// A operand: k-tile kt is filter column b = kt; one 4D tiled TMA load of 4 image rows x 128 pixels x
-// 16 channels lands as the four 4 KB K=16 sub-tiles of filter rows a = 0..3 (4 loads per tile, where
-// 16 im2col loads of one tap each are needed otherwise). B: the 64 x 256 weights, resident.
-// Warps: 0 and 10-12 TMA producers, 1 and 13-15 MMA issuers (split-K partials in TMEM, as in
-// conv_gemm_kernel), 2-9 epilogue. Every wait is bounded; the epilogue warps synchronise through
-// two mbarriers (ring row written / pool row done), never through an unbounded named barrier.
-constexpr int kStemKT = 4;                      // k-tiles: filter columns
-constexpr uint32_t kStemAStage = 4 * BM * 32;   // 16 KB: four 4 KB sub-tiles
-constexpr uint32_t kStemBBytes = 64 * 128;      // one 64 x 64 bf16 weight k-tile
-constexpr uint32_t kStemRingRow = 128 * 128;    // 128 pixels x 64 bf16 channels
-// TMEM accumulators: the MMA issuer may run this many conv rows ahead of the epilogue, whose pool
-// rows come in bursts (every second conv row also computes a 3x3 max over three ring rows)
-constexpr int kStemAcc = 4;
+// space-to-depth image of 16-channel pixels) with bias, activation and the following MaxPool 3x3 /
+// stride 2 / pad 1 in one kernel. A tile is one conv output row (Wo <= 128 pixels; the tile's
+// remaining rows are junk, computed and dropped). CTA b walks a contiguous range of pool rows: for
+// each it computes conv rows 2po and 2po + 1 (and, at the start of its range, the halo row 2po - 1).
+// The conv output (1.6 MB per 224x224 image) never reaches global memory.
+// A operand: a ring of space-to-depth input rows, one 2D-like TMA box of 131 pixels x 16 channels
+// (32-byte rows, 32-byte swizzle) per row. Conv row r reads input rows r - ph + a (filter row a);
+// consecutive conv rows share three of their four input rows, so a row costs one 4 KB load. Filter
+// tap (a, b) is the 128-row window of input row a starting b pixels in: the descriptor start moves
+// by b x 32 bytes and the swizzle, a function of the address bits, follows it. B: the 64 x 256
+// weights, resident. K order (filter column b, filter row a, channel).
+// Max pool in registers: epilogue warp (q, h) holds pixels 32q .. 32q + 31 (its TMEM lanes) and
+// channels 32h .. 32h + 31. Per pixel it keeps the bf16 values of the last odd conv row (V) and the
+// max over the pool row's first two conv rows (M); after the odd row it has the vertical max F, takes
+// the horizontal max over pixels 2pw - 1 .. 2pw + 1 with lane shuffles (the pixel left of lane 0
+// comes from warp (q - 1, h) through shared memory) and stores pool column 16q + lane / 2 from the
+// even lanes. Bias and activation are applied and rounded to bf16 before any max, as the separate
+// conv and pool kernels would (rounding is monotonic, so the order of max and rounding is immaterial).
+// Warps: 0 TMA producer, 1 and 13-15 MMA issuers (issuer i takes filter columns b = i mod P into its
+// own TMEM partial), 2-9 epilogue. Every wait is bounded.
+constexpr int kStemKT = 4;                      // filter columns (weight k-tiles)
+constexpr uint32_t kStemBBytes = 64 * 128;      // one 64 x 64 bf16 weight k-tile (4 filter rows x 16 channels)
+constexpr int kStemRowPx = BM + 3;              // input pixels per ring row: 128 + the three extra filter columns
+constexpr uint32_t kStemRowBytes = uint32_t(kStemRowPx) * 32u;
+constexpr uint32_t kStemSlot = 5 * 1024;        // ring slot stride (1 KB aligned)
+constexpr int kStemRing = 16;                   // input rows in flight
 
 // The conv rows CTA `cta` computes, in order: calls f(n, r, pool) for each, where pool says that the
 // row completes pool row r / 2 (r odd, and not the halo row of the range's first pool row).
@@ -889,47 +896,47 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* tm, in
       : "memory");
 }
 
-// Swizzled 16-byte chunk j (8 channels) of pixel px in a ring row (128-byte pixel rows).
-__device__ __forceinline__ uint32_t ring_off(int px, int j) { return uint32_t(px * 128 + ((j ^ (px & 7)) << 4)); }
+__device__ __forceinline__ uint32_t bf16x2_max(uint32_t x, uint32_t y) {
+  __nv_bfloat162 r = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&x), *reinterpret_cast<const __nv_bfloat162*>(&y));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
 
 __global__ void __launch_bounds__(512, 1)
     stem_pool_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const StemPoolArgs a) {
   constexpr uint32_t idesc = idesc_mma(BM, 64, false);
-  const int STAGES = a.stages;
-  const int NP = a.producers;
-  const int PE = a.mma_lanes;
-  const uint32_t TMEM_COLS = uint32_t(kStemAcc * PE * 64);
+  const int PE = a.mma_lanes;         // 1, 2 or 4
+  const int NACC = 8 / PE;            // accumulators (conv rows) in TMEM
+  constexpr uint32_t TMEM_COLS = 512;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = sA + STAGES * kStemAStage;
+  uint8_t* sB = smem;
   uint8_t* ring = sB + kStemKT * kStemBBytes;
-  float* sBias = reinterpret_cast<float*>(ring + 3 * kStemRingRow);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sBias + 64);
-  uint64_t* empty = full + kMaxStages;
-  uint64_t* accf = empty + kMaxStages;
-  uint64_t* acce = accf + kStemAcc;
-  uint64_t* bfull = acce + kStemAcc;
-  uint64_t* ring_full = bfull + 1;   // the 8 epilogue warps wrote a pool row's conv rows into the ring
-  uint64_t* pool_done = ring_full + 1;   // the 8 epilogue warps finished computing that pool row
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(pool_done + 1);
+  float* sBias = reinterpret_cast<float*>(ring + kStemRing * kStemSlot);
+  uint4* xch = reinterpret_cast<uint4*>(sBias + 64);   // [pool-row parity][quarter][half][4 x 16 B]
+  uint64_t* full = reinterpret_cast<uint64_t*>(xch + 2 * 4 * 2 * 4);
+  uint64_t* empty = full + kStemRing;
+  uint64_t* accf = empty + kStemRing;
+  uint64_t* acce = accf + 8;
+  uint64_t* bfull = acce + 8;
+  uint64_t* xbar = bfull + 1;   // [2]: the 8 epilogue warps published a pool row's boundary pixels
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xbar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < kStemRing; ++s) {
       mbar_init(&full[s], 1u);
-      mbar_init(&empty[s], 1u);
+      mbar_init(&empty[s], uint32_t(PE));
     }
-    for (int i = 0; i < kStemAcc; ++i) {
+    for (int i = 0; i < NACC; ++i) {
       mbar_init(&accf[i], uint32_t(PE));
       mbar_init(&acce[i], 8u);
     }
     mbar_init(bfull, 1u);
-    mbar_init(ring_full, 8u);
-    mbar_init(pool_done, 8u);
+    mbar_init(&xbar[0], 8u);
+    mbar_init(&xbar[1], 8u);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -950,141 +957,136 @@ __global__ void __launch_bounds__(512, 1)
   }
   pdl_wait();
 
-  if (warp == 0 || (warp >= 10 && warp <= 12)) {
-    // ---- TMA producers: k-tiles dealt round-robin over NP threads ----
-    const int pid = warp == 0 ? 0 : warp - 9;
-    if (lane == 0 && pid < NP) {
-      int stage = 0, owner = 0;
-      uint32_t phase = 0;
+  if (warp == 0) {
+    // ---- TMA producer: load s (in conv-row order, one per row, four at an image or range start)
+    // goes to ring slot s mod kStemRing once every issuer has released the load before it there ----
+    if (lane == 0) {
+      int s = 0, pn = -1, pr = -8;
       stem_rows(a, blockIdx.x, gridDim.x, [&](int n, int r, bool) {
-        for (int kt = 0; kt < kStemKT; ++kt) {
-          const bool mine = owner == pid;
-          if (++owner == NP) owner = 0;
-          if (mine) {
-            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) return false;
-            mbar_expect_tx(&full[stage], kStemAStage);
-            // filter column kt, filter rows 0..3: image rows r - ph .. r - ph + 3, pixels kt - pw ..
-            tma_load_4d(sA + stage * kStemAStage, &tmA, 0, kt - a.pw, r - a.ph, n, &full[stage]);
-          }
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+        const bool cont = n == pn && r == pr + 1;
+        for (int j = cont ? 3 : 0; j < 4; ++j, ++s) {
+          const int slot = s % kStemRing;
+          if (!mbar_wait(&empty[slot], (uint32_t(s / kStemRing) & 1u) ^ 1u, abort_flag, a.err, 1u)) return false;
+          mbar_expect_tx(&full[slot], kStemRowBytes);
+          tma_load_4d(ring + slot * kStemSlot, &tmA, 0, -a.pw, r - a.ph + j, n, &full[slot]);
         }
+        pn = n;
+        pr = r;
         return true;
       });
     }
   } else if (warp == 1 || warp >= 13) {
-    // ---- MMA issuers: issuer mid takes the k-tiles g = mid (mod PE) into its own partial ----
+    // ---- MMA issuers: issuer mid takes filter columns b = mid (mod PE) into its own partial ----
     const int mid = warp == 1 ? 0 : warp - 12;
     if (lane == 0 && mid < PE) {
-      int it = 0, g0 = 0, g = mid, stage = mid;
-      uint32_t phase = 0;
+      int it = 0, s_next = 0, base = 0, pn = -1, pr = -8;
       if (mbar_wait(bfull, 0u, abort_flag, a.err, 128u)) {
-        stem_rows(a, blockIdx.x, gridDim.x, [&](int, int, bool) {
-          const int acc = it % kStemAcc;
-          const uint32_t aph = uint32_t(it / kStemAcc) & 1u;
-          if (!mbar_wait(&acce[acc], aph ^ 1u, abort_flag, a.err, 2u)) return false;
+        stem_rows(a, blockIdx.x, gridDim.x, [&](int n, int r, bool) {
+          const bool cont = n == pn && r == pr + 1;
+          pn = n;
+          pr = r;
+          // this row's input rows are loads base .. base + 3; the previous row's loads before base
+          // are released (the commit fires once the MMAs that read them are done)
+          const int nb = cont ? s_next - 3 : s_next;
+          for (int s = base; s < nb; ++s) umma_commit(&empty[s % kStemRing]);
+          base = nb;
+          for (int s = s_next; s < nb + 4; ++s)   // the loads this row adds
+            if (!mbar_wait(&full[s % kStemRing], uint32_t(s / kStemRing) & 1u, abort_flag, a.err, 4u)) return false;
+          s_next = nb + 4;
+          const int acc = it % NACC;
+          if (!mbar_wait(&acce[acc], (uint32_t(it / NACC) & 1u) ^ 1u, abort_flag, a.err, 2u)) return false;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + uint32_t((acc * PE + mid) * 64);
-          for (bool first = true; g < g0 + kStemKT; first = false) {
-            const int kt = g - g0;
-            if (!mbar_wait(&full[stage], phase, abort_flag, a.err, 4u)) return false;
-            tc_fence_after();
-            const uint64_t bd = sw128_desc(smem_u32(sB + kt * kStemBBytes));
+          for (int b = mid; b < kStemKT; b += PE) {
+            const uint64_t bd = sw128_desc(smem_u32(sB + b * kStemBBytes));
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_bf16(d_tmem, sw32_desc(smem_u32(sA + stage * kStemAStage + kk * (BM * 32))), bd + uint64_t(kk * 2),
-                        idesc, (!first || kk != 0) ? 1u : 0u);
-            umma_commit(&empty[stage]);
-            g += PE;
-            stage += PE;
-            if (stage >= STAGES) {
-              stage -= STAGES;
-              phase ^= 1u;
+            for (int fa = 0; fa < 4; ++fa) {
+              const uint8_t* row = ring + ((base + fa) % kStemRing) * kStemSlot + b * 32;
+              umma_bf16(d_tmem, sw32_desc(smem_u32(row)), bd + uint64_t(fa * 2), idesc, (b != mid || fa != 0) ? 1u : 0u);
             }
           }
           umma_commit(&accf[acc]);
           ++it;
-          g0 += kStemKT;
           return true;
         });
       }
     }
-  } else {
-    // ---- epilogue warps 2-9: warp w holds pixels 32 (w & 3) .. + 31 and channels 32 hsel .. + 31 ----
-    const int q = warp & 3, hsel = (warp - 2) >> 2;
-    const int ew = warp - 2;   // 0..7
+  } else if (warp >= 2 && warp <= 9) {
+    // ---- epilogue warps 2-9: warp w holds pixels 32 (w & 3) .. + 31 and channels 32 h .. + 31 ----
+    const int q = warp & 3, h = (warp - 2) >> 2;
     const int Hp = a.Ho / 2, Wp = a.Wo / 2;
-    const int px = q * 32 + lane;
+    const float* bs = sBias + h * 32;
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
-    int it = 0;
-    int pc = 0;   // pool rows this CTA has completed
+    uint32_t V[16], M[16];   // bf16 pairs: last odd conv row; max of the pool row's first two rows
+#pragma unroll
+    for (int j = 0; j < 16; ++j) V[j] = M[j] = 0u;
+    int it = 0, pc = 0;
     stem_rows(a, blockIdx.x, gridDim.x, [&](int n, int r, bool pool) {
-      const int acc = it % kStemAcc;
-      const uint32_t aph = uint32_t(it / kStemAcc) & 1u;
-      if (!mbar_wait(&accf[acc], aph, abort_flag, a.err, 8u)) return false;
+      const int acc = it % NACC;
+      if (!mbar_wait(&accf[acc], uint32_t(it / NACC) & 1u, abort_flag, a.err, 8u)) return false;
       tc_fence_after();
       float v[32];
-      tmem_ld_sum(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * PE * 64 + hsel * 32), PE, 64, v);
+      tmem_ld_sum(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * PE * 64 + h * 32), PE, 64, v);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce[acc]);
-      // Ring slot r % 3 held row r - 3, last read by the previous pool row: an even row waits until
-      // every warp has finished that pool row (the odd row after it then reuses a slot that the same
-      // pool row was the last to read; the range's halo row follows no pool row).
-      if (!(r & 1) && pc > 0 && !mbar_wait(pool_done, uint32_t(pc - 1) & 1u, abort_flag, a.err, 16u)) return false;
-      if (px < a.Wo) {
-        uint8_t* row = ring + (r % 3) * kStemRingRow;
+      ++it;
+      uint32_t c[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float x = v[2 * j] + bs[2 * j], y = v[2 * j + 1] + bs[2 * j + 1];
+        c[j] = a.act == 1 ? pack_bf16x2_relu(x, y) : pack_bf16x2(x, y);
+      }
+      if (!(r & 1)) {   // conv row 2po: with the row above (none at po = 0: pool padding)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) M[j] = r > 0 ? bf16x2_max(V[j], c[j]) : c[j];
+        return true;
+      }
+      if (!pool) {   // the range's halo row 2po - 1
+#pragma unroll
+        for (int j = 0; j < 16; ++j) V[j] = c[j];
+        return true;
+      }
+      // conv row 2po + 1 completes pool row po
+      const int po = r >> 1;
+      uint32_t F[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        F[j] = bf16x2_max(M[j], c[j]);
+        V[j] = c[j];
+      }
+      uint4* xs = xch + (pc & 1) * 32;   // this pool row's slots: [quarter][half][4]
+      if (lane == 31) {
+        if (q < 3)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) xs[(q * 2 + h) * 4 + j] = make_uint4(F[4 * j], F[4 * j + 1], F[4 * j + 2], F[4 * j + 3]);
+        mbar_arrive(&xbar[pc & 1]);
+      }
+      if (!mbar_wait(&xbar[pc & 1], uint32_t(pc >> 1) & 1u, abort_flag, a.err, 16u)) return false;
+      uint32_t L[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const uint32_t lf = __shfl_up_sync(0xffffffffu, F[j], 1);
+        const uint32_t rt = __shfl_down_sync(0xffffffffu, F[j], 1);
+        L[j] = bf16x2_max(F[j], rt);
+        if (lane > 0) L[j] = bf16x2_max(L[j], lf);
+      }
+      if (lane == 0 && q > 0) {   // pixel 32q - 1, from warp (q - 1, h)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          float t[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) t[e] = v[8 * j + e] + sBias[hsel * 32 + 8 * j + e];
-          uint4 qv;
-          if (a.act == 1) {
-            qv.x = pack_bf16x2_relu(t[0], t[1]);
-            qv.y = pack_bf16x2_relu(t[2], t[3]);
-            qv.z = pack_bf16x2_relu(t[4], t[5]);
-            qv.w = pack_bf16x2_relu(t[6], t[7]);
-          } else {
-            qv.x = pack_bf16x2(t[0], t[1]);
-            qv.y = pack_bf16x2(t[2], t[3]);
-            qv.z = pack_bf16x2(t[4], t[5]);
-            qv.w = pack_bf16x2(t[6], t[7]);
-          }
-          *reinterpret_cast<uint4*>(row + ring_off(px, hsel * 4 + j)) = qv;
+          const uint4 u = xs[((q - 1) * 2 + h) * 4 + j];
+          L[4 * j] = bf16x2_max(L[4 * j], u.x);
+          L[4 * j + 1] = bf16x2_max(L[4 * j + 1], u.y);
+          L[4 * j + 2] = bf16x2_max(L[4 * j + 2], u.z);
+          L[4 * j + 3] = bf16x2_max(L[4 * j + 3], u.w);
         }
       }
-      ++it;
-      if (!pool) return true;
-      // all warps have written the pool row's conv rows r - 2 .. r
-      __syncwarp();
-      if (lane == 0) mbar_arrive(ring_full);
-      if (!mbar_wait(ring_full, uint32_t(pc) & 1u, abort_flag, a.err, 32u)) return false;
-      {   // pool row po = r / 2 from conv rows r - 2 (padding when po = 0), r - 1, r
-        const int po = r >> 1;
-        const uint8_t* rows[3] = {po > 0 ? ring + ((r + 1) % 3) * kStemRingRow : nullptr,
-                                  ring + ((r + 2) % 3) * kStemRingRow, ring + (r % 3) * kStemRingRow};
-        __nv_bfloat16* orow = out + (int64_t(n) * Hp + po) * int64_t(Wp) * 64;
-        for (int i = ew * 32 + lane; i < Wp * 8; i += 256) {
-          const int qo = i >> 3, j = i & 7;
-          uint4 m = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);   // bf16 -inf
+      const int pw = q * 16 + (lane >> 1);
+      if (!(lane & 1) && pw < Wp) {
+        uint4* dst = reinterpret_cast<uint4*>(out + ((int64_t(n) * Hp + po) * Wp + pw) * 64 + h * 32);
 #pragma unroll
-          for (int dr = 0; dr < 3; ++dr) {
-            if (!rows[dr]) continue;
-#pragma unroll
-            for (int dc = -1; dc <= 1; ++dc) {
-              const int c = 2 * qo + dc;
-              if (c < 0 || c >= a.Wo) continue;
-              m = bf16x8_max(m, *reinterpret_cast<const uint4*>(rows[dr] + ring_off(c, j)));
-            }
-          }
-          *reinterpret_cast<uint4*>(orow + qo * 64 + j * 8) = m;
-        }
+        for (int j = 0; j < 4; ++j) dst[j] = make_uint4(L[4 * j], L[4 * j + 1], L[4 * j + 2], L[4 * j + 3]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(pool_done);
       ++pc;
       return true;
     });
@@ -1827,11 +1829,11 @@ void stem_pool_prepare(StemPoolPlan& p, const void* w, int num_sms) {
   std::memset(&p.tmB, 0, sizeof(p.tmB));
   auto fn = get_encode_fn();
   if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled entry point missing");
-  // the space-to-depth image as a 4D tensor (channel, x, y, image); one box = 4 rows x 128 pixels
-  // x 16 channels, 32-byte rows swizzled as the K=16 MMA sub-tiles expect
+  // the space-to-depth image as a 4D tensor (channel, x, y, image); one box = one input row of
+  // 131 pixels x 16 channels, 32-byte rows swizzled as the K=16 MMA sub-tiles expect
   cuuint64_t dims[4] = {16, cuuint64_t(a.Ws), cuuint64_t(a.Hs), cuuint64_t(a.N)};
   cuuint64_t strides[3] = {32, cuuint64_t(a.Ws) * 32, cuuint64_t(a.Hs) * a.Ws * 32};
-  cuuint32_t box[4] = {16, BM, 4, 1};
+  cuuint32_t box[4] = {16, uint32_t(kStemRowPx), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(&p.tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(a.x), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1839,19 +1841,12 @@ void stem_pool_prepare(StemPoolPlan& p, const void* w, int num_sms) {
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed for the stem input");
   if (!encode_2d(&p.tmB, w, uint64_t(kStemKT) * BK, 64, uint64_t(kStemKT) * BK * 2, BK, 64))
     throw std::runtime_error("cuTensorMapEncodeTiled failed for the stem weights");
-  // two MMA issuers (one: 621 us at ResNet-50 bs512, two: 494, four: 494-499); the producer count
-  // (one to four) made no difference
-  a.mma_lanes = 2;
-  a.producers = 2;
-  const int fixed = int(kStemKT * kStemBBytes + 3 * kStemRingRow) + 256 + 1024 + 512;
-  int stages = std::min(kMaxStages, (kSmemLimit - fixed) / int(kStemAStage));
-  {
-    const int l = std::max(a.mma_lanes, a.producers);   // (both powers of two up to 4)
-    stages -= stages % l;
-  }
-  if (stages < 2) throw std::runtime_error("stem_pool: shared-memory plan leaves fewer than 2 stages");
-  a.stages = stages;
-  p.smem = stages * int(kStemAStage) + fixed;
+  // four MMA issuers, one filter column each (two accumulators in TMEM); one TMA producer (a
+  // 4 KB input row per conv row)
+  a.mma_lanes = 4;
+  a.producers = 1;
+  a.stages = kStemRing;
+  p.smem = int(kStemKT * kStemBBytes + kStemRing * kStemSlot) + 256 + 1024 + 512 + 1024;
   const int64_t pool_rows = int64_t(a.N) * (a.Ho / 2);
   p.grid = int(std::min<int64_t>(num_sms, pool_rows));
   static std::atomic<uint64_t> done_mask{0};

@@ -130,7 +130,7 @@ struct StemPoolArgs {
   int stages, producers, mma_lanes;
 };
 struct StemPoolPlan {
-  CUtensorMap tmA;   // 4D tiled map of x: box 16 channels x 128 pixels x 4 rows
+  CUtensorMap tmA;   // 4D tiled map of x: box 16 channels x 131 pixels x 1 row
   CUtensorMap tmB;   // weights, 64 x 64 boxes (one k-tile)
   int grid, smem;
   StemPoolArgs args;
