@@ -862,14 +862,15 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
 // comes from warp (q - 1, h) through shared memory) and stores pool column 16q + lane / 2 from the
 // even lanes. Bias and activation are applied and rounded to bf16 before any max, as the separate
 // conv and pool kernels would (rounding is monotonic, so the order of max and rounding is immaterial).
-// Warps: 0 TMA producer, 1 and 13-15 MMA issuers (issuer i takes filter columns b = i mod P into its
-// own TMEM partial), 2-9 epilogue. Every wait is bounded.
+// Warps: 0 TMA producer, 1 and 13-15 MMA issuers (issuer i takes conv rows i mod P, all 16 taps of
+// each, into one of eight TMEM accumulators), 2-9 epilogue. Every wait is bounded.
 constexpr int kStemKT = 4;                      // filter columns (weight k-tiles)
 constexpr uint32_t kStemBBytes = 64 * 128;      // one 64 x 64 bf16 weight k-tile (4 filter rows x 16 channels)
 constexpr int kStemRowPx = BM + 3;              // input pixels per ring row: 128 + the three extra filter columns
 constexpr uint32_t kStemRowBytes = uint32_t(kStemRowPx) * 32u;
 constexpr uint32_t kStemSlot = 5 * 1024;        // ring slot stride (1 KB aligned)
 constexpr int kStemRing = 16;                   // input rows in flight
+constexpr int kStemAcc = 8;                     // TMEM accumulators (conv rows) of 64 columns
 
 // The conv rows CTA `cta` computes, in order: calls f(n, r, pool) for each, where pool says that the
 // row completes pool row r / 2 (r odd, and not the halo row of the range's first pool row).
@@ -905,9 +906,8 @@ __global__ void __launch_bounds__(512, 1)
     stem_pool_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const StemPoolArgs a) {
   constexpr uint32_t idesc = idesc_mma(BM, 64, false);
-  const int PE = a.mma_lanes;         // 1, 2 or 4
-  const int NACC = 8 / PE;            // accumulators (conv rows) in TMEM
-  constexpr uint32_t TMEM_COLS = 512;
+  const int PE = a.mma_lanes;         // MMA issuers (1 to 4)
+  constexpr uint32_t TMEM_COLS = 512; // kStemAcc accumulators of 64 columns
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sB = smem;
@@ -917,8 +917,8 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(xch + 2 * 4 * 2 * 4);
   uint64_t* empty = full + kStemRing;
   uint64_t* accf = empty + kStemRing;
-  uint64_t* acce = accf + 8;
-  uint64_t* bfull = acce + 8;
+  uint64_t* acce = accf + kStemAcc;
+  uint64_t* bfull = acce + kStemAcc;
   uint64_t* xbar = bfull + 1;   // [2]: the 8 epilogue warps published a pool row's boundary pixels
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xbar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
@@ -930,8 +930,8 @@ __global__ void __launch_bounds__(512, 1)
       mbar_init(&full[s], 1u);
       mbar_init(&empty[s], uint32_t(PE));
     }
-    for (int i = 0; i < NACC; ++i) {
-      mbar_init(&accf[i], uint32_t(PE));
+    for (int i = 0; i < kStemAcc; ++i) {
+      mbar_init(&accf[i], 1u);
       mbar_init(&acce[i], 8u);
     }
     mbar_init(bfull, 1u);
@@ -976,37 +976,39 @@ __global__ void __launch_bounds__(512, 1)
       });
     }
   } else if (warp == 1 || warp >= 13) {
-    // ---- MMA issuers: issuer mid takes filter columns b = mid (mod PE) into its own partial ----
+    // ---- MMA issuers: issuer mid takes the conv rows i = mid (mod PE), all 16 taps of each, into
+    // accumulator i mod 8. Loads are released per issuer: at the start of each of its rows an issuer
+    // commits the release of every load below that row's first (its earlier rows were its last
+    // reads of them; the commit fires once those MMAs are done), so each load gets PE releases ----
     const int mid = warp == 1 ? 0 : warp - 12;
     if (lane == 0 && mid < PE) {
-      int it = 0, s_next = 0, base = 0, pn = -1, pr = -8;
+      int row = 0, s_next = 0, rel = 0, pn = -1, pr = -8;
       if (mbar_wait(bfull, 0u, abort_flag, a.err, 128u)) {
         stem_rows(a, blockIdx.x, gridDim.x, [&](int n, int r, bool) {
           const bool cont = n == pn && r == pr + 1;
           pn = n;
           pr = r;
-          // this row's input rows are loads base .. base + 3; the previous row's loads before base
-          // are released (the commit fires once the MMAs that read them are done)
-          const int nb = cont ? s_next - 3 : s_next;
-          for (int s = base; s < nb; ++s) umma_commit(&empty[s % kStemRing]);
-          base = nb;
-          for (int s = s_next; s < nb + 4; ++s)   // the loads this row adds
+          const int base = cont ? s_next - 3 : s_next;   // this row's input rows: loads base .. base + 3
+          s_next = base + 4;
+          const int it = row++;
+          if (it % PE != mid) return true;
+          for (; rel < base; ++rel) umma_commit(&empty[rel % kStemRing]);
+          for (int s = base; s < base + 4; ++s)
             if (!mbar_wait(&full[s % kStemRing], uint32_t(s / kStemRing) & 1u, abort_flag, a.err, 4u)) return false;
-          s_next = nb + 4;
-          const int acc = it % NACC;
-          if (!mbar_wait(&acce[acc], (uint32_t(it / NACC) & 1u) ^ 1u, abort_flag, a.err, 2u)) return false;
+          const int acc = it % kStemAcc;
+          if (!mbar_wait(&acce[acc], (uint32_t(it / kStemAcc) & 1u) ^ 1u, abort_flag, a.err, 2u)) return false;
           tc_fence_after();
-          const uint32_t d_tmem = tmem_base + uint32_t((acc * PE + mid) * 64);
-          for (int b = mid; b < kStemKT; b += PE) {
+          const uint32_t d_tmem = tmem_base + uint32_t(acc * 64);
+#pragma unroll
+          for (int b = 0; b < kStemKT; ++b) {
             const uint64_t bd = sw128_desc(smem_u32(sB + b * kStemBBytes));
 #pragma unroll
             for (int fa = 0; fa < 4; ++fa) {
-              const uint8_t* row = ring + ((base + fa) % kStemRing) * kStemSlot + b * 32;
-              umma_bf16(d_tmem, sw32_desc(smem_u32(row)), bd + uint64_t(fa * 2), idesc, (b != mid || fa != 0) ? 1u : 0u);
+              const uint8_t* rowp = ring + ((base + fa) % kStemRing) * kStemSlot + b * 32;
+              umma_bf16(d_tmem, sw32_desc(smem_u32(rowp)), bd + uint64_t(fa * 2), idesc, (b | fa) != 0 ? 1u : 0u);
             }
           }
           umma_commit(&accf[acc]);
-          ++it;
           return true;
         });
       }
@@ -1022,20 +1024,24 @@ __global__ void __launch_bounds__(512, 1)
     for (int j = 0; j < 16; ++j) V[j] = M[j] = 0u;
     int it = 0, pc = 0;
     stem_rows(a, blockIdx.x, gridDim.x, [&](int n, int r, bool pool) {
-      const int acc = it % NACC;
-      if (!mbar_wait(&accf[acc], uint32_t(it / NACC) & 1u, abort_flag, a.err, 8u)) return false;
+      const int acc = it % kStemAcc;
+      if (!mbar_wait(&accf[acc], uint32_t(it / kStemAcc) & 1u, abort_flag, a.err, 8u)) return false;
       tc_fence_after();
-      float v[32];
-      tmem_ld_sum(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * PE * 64 + h * 32), PE, 64, v);
+      uint32_t u[32];
+      tmem_ld32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * 64 + h * 32), u);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce[acc]);
       ++it;
       uint32_t c[16];
+      const float4* b4 = reinterpret_cast<const float4*>(bs);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float x = v[2 * j] + bs[2 * j], y = v[2 * j + 1] + bs[2 * j + 1];
-        c[j] = a.act == 1 ? pack_bf16x2_relu(x, y) : pack_bf16x2(x, y);
+      for (int j = 0; j < 8; ++j) {
+        const float4 bb = b4[j];
+        const float2 x = __fadd2_rn(make_float2(__uint_as_float(u[4 * j]), __uint_as_float(u[4 * j + 1])), make_float2(bb.x, bb.y));
+        const float2 y = __fadd2_rn(make_float2(__uint_as_float(u[4 * j + 2]), __uint_as_float(u[4 * j + 3])), make_float2(bb.z, bb.w));
+        c[2 * j] = a.act == 1 ? pack_bf16x2_relu(x.x, x.y) : pack_bf16x2(x.x, x.y);
+        c[2 * j + 1] = a.act == 1 ? pack_bf16x2_relu(y.x, y.y) : pack_bf16x2(y.x, y.y);
       }
       if (!(r & 1)) {   // conv row 2po: with the row above (none at po = 0: pool padding)
 #pragma unroll
@@ -1841,8 +1847,9 @@ void stem_pool_prepare(StemPoolPlan& p, const void* w, int num_sms) {
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed for the stem input");
   if (!encode_2d(&p.tmB, w, uint64_t(kStemKT) * BK, 64, uint64_t(kStemKT) * BK * 2, BK, 64))
     throw std::runtime_error("cuTensorMapEncodeTiled failed for the stem weights");
-  // four MMA issuers, one filter column each (two accumulators in TMEM); one TMA producer (a
-  // 4 KB input row per conv row)
+  // four MMA issuers taking every fourth conv row (ResNet-50 bs512: 457 us with two, 320 with four;
+  // an issuer waits on its row's loads and accumulator between rows); one TMA producer (a 4 KB input
+  // row per conv row)
   a.mma_lanes = 4;
   a.producers = 1;
   a.stages = kStemRing;
