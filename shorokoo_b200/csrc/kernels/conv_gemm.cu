@@ -314,7 +314,10 @@ __device__ __forceinline__ void epilogue_slab(const ConvGemmArgs& a, const CUten
 // Warps: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-9 epilogue (two per TMEM lane quarter,
 // splitting the column slabs), then either 10-13 im2col gather (MODE 1/2) or 10-12 more TMA
 // producers and 13-15 more MMA issuers. One thread keeps only one TMA load per few hundred cycles
-// and one tcgen05.mma per ~164 cycles in flight, whatever the tile shape, so the k-tiles are
+// in flight, and an issuer that waits on a stage barrier per k-tile averages about one tcgen05.mma
+// per 160 cycles (back to back, without waits, one thread issues one per ~59 cycles; the tensor core
+// retires an M=128 MMA every 48 / 64 / 128 cycles at N = 64 / 128 / 256, N=64 held above its 32 by
+// the 6 KB of operands it reads from shared memory at 128 B per cycle), so the k-tiles are
 // dealt round-robin to Q producer threads and P MMA-issuing threads (each in its own warp). The stage count is a
 // multiple of both, so each stage's full and empty barriers have exactly one producer and one
 // consumer, each moving through the stage's phases in order: no waiter can face a barrier two
@@ -588,9 +591,9 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
   split_done:;
   } else if (warp == 1 || (A_TMA && warp >= 13)) {
     // Issuer `mid` (lane 0 of warp 1, 13, 14 or 15) issues the MMAs of the k-tiles with sequence
-    // number g = mid (mod PE) into its own partial accumulator: one thread sustains only about one
-    // tcgen05.mma per ~164 cycles whatever the shape, so N=64/128 tiles need several issuing
-    // threads to keep the tensor pipe busy. Each issuer commits its own k-tiles' stages and
+    // number g = mid (mod PE) into its own partial accumulator: with its per-k-tile barrier waits one
+    // thread averages about one tcgen05.mma per 160 cycles, so N=64/128 tiles (48 / 64 cycles of
+    // tensor work each) need several issuing threads. Each issuer commits its own k-tiles' stages and
     // arrives once per tile on the accumulator-full barrier.
     const int mid = warp == 1 ? 0 : warp - 12;
     if (lane == 0 && mid < PE) {
@@ -1592,7 +1595,8 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   int bn = a.Cout <= 64 ? 64 : (a.Cout <= 128 || res_ring || a.x3 ? 128 : 256);
   {
     // The widest tile among those with the fewest waves of persistent CTAs: one tcgen05.mma costs
-    // the issuing thread about the same whatever its N, so a narrower tile only pays when it cuts
+    // the issuing thread about the same whatever its N (and reads more operand bytes per MAC at a
+    // narrower N), so a narrower tile only pays when it cuts
     // the number of waves (measured on ResNet-50 bs64: 1.41 -> 1.39 ms against halving N until
     // every SM has a tile).
     // Among equal wave counts the tile that fills the most SMs wins (ties: the widest): a small batch
