@@ -730,7 +730,10 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
                                   : sb0;
             const int wm = inplace ? 0 : OB;
             const float* bsl = wbias + ((s2 - hsel) >> 1) * SC;
-            if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, srow0, n0, sb, rslab, bsl, wm, PE, BN);
+            if (a.out_bf16 && a.epi_half) {   // two 32-column halves through the warp's 2 KB slab
+              for (int hh = 0; hh < 2 && n0 + hh * 32 < a.Cout; ++hh)
+                epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, srow0, n0, sb, rslab, bsl + hh * 32, wm, PE, BN, hh);
+            } else if (a.out_bf16) epilogue_slab<true>(a, &tmOut, tbase, s2 * SC, srow0, n0, sb, rslab, bsl, wm, PE, BN);
             else epilogue_slab<false>(a, &tmOut, tbase, s2 * SC, srow0, n0, sb, rslab, bsl, wm, PE, BN);
           }
         } else {
@@ -1675,8 +1678,11 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   // bf16 output of 64-column tiles is one 128-byte slab per 32 rows, which would leave one of each
   // TMEM quarter's two epilogue warps idle: it is split into two 32-column halves, one per warp,
   // each stored from its own 64-byte slab through a 32x32 box (not for in-place output, whose slab
-  // is the residual ring's 128-byte layout). The halved slabs also leave room for more stages.
-  auto half_for = [&](int ob) { return a.epi == 2 && a.out_bf16 && bn == 64 && ob != 0; };
+  // is the residual ring's 128-byte layout). The halved slabs also leave room for more stages, so
+  // wider bf16 tiles take them too when that buys a stage (each warp then stores its 64-column
+  // slabs as two 32-column halves through the one 2 KB slab).
+  bool wide_half = false;
+  auto half_for = [&](int ob) { return a.epi == 2 && a.out_bf16 && ob != 0 && (bn == 64 || wide_half); };
   auto fixed_for = [&](int ob) {
     return int(8 * ob * (half_for(ob) ? kOutSlab / 2 : kOutSlab) + kBiasStage) + 1024 + 512 + (bres ? int(w_bytes) : 0) + (a.res_mma ? int(kIdBytes) : 0) +
            (a.bias_mma ? int(kOnesBytes) + bias_rows * 32 : 0);
@@ -1690,31 +1696,50 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   int ob = ring && KT >= 8 ? 0 : 1;
   int rs = ring_for(ob);
   if (rs == 0 && ob == 0) ob = 1;   // writing in place needs a residual ring
-  const int smax = stages_for(ob, rs);
   // Producers and stages. With one MMA issuer the stages are consumed in order, and at least as
   // many stages as producers keeps every barrier wait within one phase. With several issuers the
   // stage count must be a multiple of both counts (one producer and one consumer per stage).
   // Prefer three or four producers (TMA issue rate), then the deepest ring.
   auto lcm = [](int x, int y) { int g = x, h = y; while (h) { int r = g % h; g = h; h = r; } return x / g * y; };
-  int np = 1, stages = (smax / pl) * pl;
-  if (!gather && pl == 1) {
-    np = std::min(3, smax);
-    stages = smax;
-  } else if (!gather) {
-    int best_np = 0, best_s = 0;
-    for (int q : {3, 4, 2, 1}) {
-      const int l = lcm(q, pl);
-      const int s_q = (smax / l) * l;
-      if (s_q < std::max(2, l)) continue;
-      if (best_np == 0 || (std::min(q, 3) > std::min(best_np, 3)) ||
-          (std::min(q, 3) == std::min(best_np, 3) && s_q > best_s)) {
-        best_np = q;
-        best_s = s_q;
+  auto split_stages = [&](int smax, int& np, int& stages) {
+    np = 1;
+    stages = (smax / pl) * pl;
+    if (!gather && pl == 1) {
+      np = std::min(3, smax);
+      stages = smax;
+    } else if (!gather) {
+      int best_np = 0, best_s = 0;
+      for (int q : {3, 4, 2, 1}) {
+        const int l = lcm(q, pl);
+        const int s_q = (smax / l) * l;
+        if (s_q < std::max(2, l)) continue;
+        if (best_np == 0 || (std::min(q, 3) > std::min(best_np, 3)) ||
+            (std::min(q, 3) == std::min(best_np, 3) && s_q > best_s)) {
+          best_np = q;
+          best_s = s_q;
+        }
       }
+      if (best_np == 0) throw std::runtime_error("conv_gemm: no producer/stage split fits shared memory");
+      np = best_np;
+      stages = best_s;
     }
-    if (best_np == 0) throw std::runtime_error("conv_gemm: no producer/stage split fits shared memory");
-    np = best_np;
-    stages = best_s;
+  };
+  int np = 1, stages = 0;
+  split_stages(stages_for(ob, rs), np, stages);
+  // Half slabs for wider bf16 tiles when the pipeline is shallow and they buy a stage. Measured on
+  // ResNet-50 bs512 (A/B on one box): 3 -> 4 stages (the 256-column layer-3/4 convs) -7 to -10%, the
+  // layer-2 3x3 convs (4 stages of 4 producers -> 6 of 3) -12%; where five or more stages fit already
+  // the extra stage gains nothing and the four half stores per tile cost up to 25%.
+  if (bn > 64 && a.epi == 2 && a.out_bf16 && ob != 0 && stages < 5) {
+    wide_half = true;
+    int np2 = 0, st2 = 0;
+    if (ring_for(ob) == rs) split_stages(stages_for(ob, rs), np2, st2);
+    if (st2 > stages) {
+      np = np2;
+      stages = st2;
+    } else {
+      wide_half = false;
+    }
   }
   a.producers = np;
   if (stages < 2) throw std::runtime_error("conv_gemm: shared-memory plan leaves fewer than 2 stages");
@@ -1873,6 +1898,21 @@ void stem_pool_prepare(StemPoolPlan& p, const void* w, int num_sms) {
 
 cudaError_t stem_pool_launch(const StemPoolPlan& p, cudaStream_t s) {
   return launch_pdl(stem_pool_kernel, p.grid, 512, p.smem, s, p.tmA, p.tmB, p.args);
+}
+
+std::string conv_gemm_describe(const ConvGemmPlan& p) {
+  static const char* kModes[] = {"tma", "gather", "gather8", "im2col", "im2col16"};
+  const ConvGemmArgs& a = p.args;
+  const char* res = !a.res ? "none" : a.res_mma ? "mma" : a.res_slots ? "ring" : "direct";
+  char buf[320];
+  std::snprintf(buf, sizeof(buf),
+                "M=%d N=%d K=%d mode=%s%s bn=%d grid=%d stages=%d producers=%d issuers=%d residual=%s%s "
+                "out_slabs=%d%s weights=%s bias=%s split=%d smem=%d",
+                a.M, a.Cout, a.Kpad, kModes[p.mode], a.x3 ? " tf32x3" : (a.tf32 ? " tf32" : ""), p.bn, p.grid, a.stages,
+                a.producers, a.mma_lanes, res, a.res_slots ? (a.res_slots == 2 ? " x2" : " x1") : "", a.out_bufs,
+                a.epi_half ? " (half slabs)" : "", a.b_resident ? "resident" : "streamed", a.bias_mma ? "mma" : "epilogue",
+                a.ksplit > 1 ? a.ksplit : 1, p.smem);
+  return buf;
 }
 
 cudaError_t conv_gemm_launch(const ConvGemmPlan& p, cudaStream_t s) {

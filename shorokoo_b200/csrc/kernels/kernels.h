@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <string>
 
 namespace sb {
 namespace k {
@@ -111,6 +112,8 @@ struct ConvGemmPlan {
 // driver entry point for tensor-map encoding is unavailable.
 void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const void* w, int num_sms);
 cudaError_t conv_gemm_launch(const ConvGemmPlan& p, cudaStream_t s);
+// One line with the launch shape and pipeline choices of a prepared plan (debug output).
+std::string conv_gemm_describe(const ConvGemmPlan& p);
 
 // ---- stem convolution with its 3x3/2 max pool fused into the epilogue (conv_gemm.cu) ----------
 // y = maxpool3x3/2,pad1( act( conv(x) + bias ) ) for the ResNet stem run as a 4x4 stride-1 conv over

@@ -826,6 +826,7 @@ void Plan::plan_conv(const Op& op) {
       a.round_tf32 = 0;
     }
     k::conv_gemm_prepare(*p, ptr(x), Cp, ptr(wt), sms);
+    if (debug_level() >= 2) std::fprintf(stderr, "[shorokoo_b200] conv_gemm %s\n", k::conv_gemm_describe(*p).c_str());
     return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::conv_gemm_launch(*p, s); });
   });
   if (ksplit > 1) add_split_reduce(ws, ksplit, Mp, Mrows, Cout, bt, r, ldr, op.act, y, round_out);
@@ -949,6 +950,7 @@ void Plan::plan_gemm(const Op& op) {
       a.round_tf32 = 0;
     }
     k::conv_gemm_prepare(*p, ptr(x), lda, ptr(wt), sms);
+    if (debug_level() >= 2) std::fprintf(stderr, "[shorokoo_b200] conv_gemm %s\n", k::conv_gemm_describe(*p).c_str());
     return std::function<cudaError_t(cudaStream_t)>([p](cudaStream_t s) { return k::conv_gemm_launch(*p, s); });
   });
   if (ksplit > 1) add_split_reduce(ws, ksplit, Mp, M, Nn, bt, r, Nn, op.act, y, round_out);
