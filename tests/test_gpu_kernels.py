@@ -282,6 +282,9 @@ def _conv(B, x, cin, cout, k, relu=False, res=None):
 # channel counts (48: the second half is partly outside; 24: the second half is empty). The middle
 # conv's bf16 residual is added by the tensor core as one extra k-tile per 64 channels (96: the
 # second residual k-tile is partly outside the tensor; 200: four of them, the last partly outside).
+# At 96 and 200 channels the convs take 128- and 256-column tiles with too few pipeline stages, so
+# their bf16 output also goes out in 32-column halves (200: the last 64-column slab's second half is
+# empty, its first half partly outside).
 @pytest.mark.parametrize("cmid", [64, 48, 24, 96, 200])
 def test_conv_chain_64_column_tiles(cmid):
     from shorokoo_b200.emit import onnx_writer as W
