@@ -282,15 +282,16 @@ def _conv(B, x, cin, cout, k, relu=False, res=None):
 # channel counts (48: the second half is partly outside; 24: the second half is empty). The middle
 # conv's bf16 residual is added by the tensor core as one extra k-tile per 64 channels (96: the
 # second residual k-tile is partly outside the tensor; 200: four of them, the last partly outside).
-# At 96 and 200 channels the convs take 128- and 256-column tiles with too few pipeline stages, so
-# their bf16 output also goes out in 32-column halves (200: the last 64-column slab's second half is
-# empty, its first half partly outside).
-@pytest.mark.parametrize("cmid", [64, 48, 24, 96, 200])
-def test_conv_chain_64_column_tiles(cmid):
+# The 8-image 64x64 case takes 256-column tiles with too few pipeline stages for full output slabs,
+# so its bf16 output also goes out in 32-column halves (the last 64-column slab's first half partly
+# outside the 200 channels, its second half empty).
+@pytest.mark.parametrize("cmid,n,h,w", [(64, 2, 48, 40), (48, 2, 48, 40), (24, 2, 48, 40), (96, 2, 48, 40),
+                                        (200, 2, 48, 40), (200, 8, 64, 64)])
+def test_conv_chain_64_column_tiles(cmid, n, h, w):
     from shorokoo_b200.emit import onnx_writer as W
     from shorokoo_b200.emit.graphs import Builder, ModelCase
     rng = np.random.Generator(np.random.PCG64(23))
-    n, c, h, w = 2, 32, 48, 40
+    c = 32
     x = rng.standard_normal((n, c, h, w), dtype=np.float32)
     B = Builder(24)
     xi = B.graph_input(W.FLOAT, 4, x.shape)

@@ -5,7 +5,8 @@ accumulation (the arithmetic of the bf16 tensor-core path), independent of the l
 session path. Every call reuses the same fixed scratch array, so the calls run back to back: a
 large layer, then a ragged one (K and N not multiples of 8 or 4, no bias, so the row-store epilogue
 and the zero padding of the reduction are exercised) whose scratch still holds the first call's
-operands, then the large layer again.
+operands, then the large layer again. It is also checked against the library's session entry point
+(a one-layer MLP model run through a session) on two calls in a row.
 
 This file is collected last on purpose, so a run that stops at the first failure has already run
 every other test."""
@@ -68,6 +69,21 @@ def test_noalloc_linear_matches_bf16_gemm_on_consecutive_calls():
         assert_close(got, ref, tol=BF16_TOL, what=f"noalloc linear {m}x{k}->{n} bias={bias} relu={relu}")
         # fp32 accumulation of exact bf16 products: far tighter than the bf16 gate
         assert np.abs(got - ref).max() <= 1e-4 * max(1.0, float(np.abs(ref).max())), f"{m}x{k}->{n}"
+
+
+@pytest.mark.parametrize("m,k,n", [(300, 200, 100), (513, 1024, 1000)])
+def test_noalloc_linear_matches_the_session_entry_point(m, k, n):
+    """The same layer through a session (sb_session_run over a one-layer MLP model whose weights are
+    known) and through sb_linear_noalloc, twice in a row, within the bf16 gate of the other GPU tests."""
+    from helpers import run_backend
+    from shorokoo_b200.emit import graphs
+    case = graphs.mlp(batch=m, widths=(k, n), seed=11, bias_scale=0.5)
+    x = case.inputs[0][1]
+    w, b = case.params["layers.0.weight"], case.params["layers.0.bias"]
+    ref = run_backend(case)[0]
+    for _ in range(2):
+        got = _noalloc(x, w, b, False)
+        assert_close(got, ref, tol=BF16_TOL, what=f"noalloc vs session linear {m}x{k}->{n}")
 
 
 def test_noalloc_linear_rejects_sizes_beyond_scratch():
