@@ -848,6 +848,248 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
   }
 }
 
+// ---- CTA-pair implicit GEMM (tcgen05.mma.cta_group::2) ----------------------------------------------
+// Two CTAs of a cluster compute one 256 x 256 output tile. Each loads its own 128 rows of A and its
+// own 128 rows (output channels) of B into the same shared-memory offsets; the even CTA's issuer runs
+// M=256, N=256 MMAs that read both CTAs' operands, and each CTA's TMEM holds the accumulator of its
+// own 128 rows x all 256 columns. Per SM this halves the B traffic (TMA writes into shared memory, the
+// MMAs' operand reads, L2 reads) of a 128 x 256 tile on one SM; each stage is 32 KB instead of 48.
+// Barriers sit at the same offsets in both CTAs: full[s] is used in the even CTA (its producer
+// expects both CTAs' bytes, the odd CTA's loads complete on it); empty[s] and accf[acc] in both (the
+// issuer commits to each CTA's copy separately); acce[acc] in the even CTA (both CTAs' 8 epilogue
+// warps arrive, the odd CTA's remotely). Every mbarrier wait is bounded; both CTAs always reach the
+// final cluster barrier, before which neither leaves (the issuer reads the odd CTA's shared memory).
+// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer (even CTA), 2-9 epilogue.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory location in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void remote_arrive(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// the tcgen05 operations of a CTA pair: all of the kernel's use cta_group::2
+__device__ __forceinline__ void tmem_alloc2(uint32_t* holder, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void umma2_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrives on the mbarrier at this shared::cluster address once the issuer's MMAs so far are done
+__device__ __forceinline__ void umma2_commit(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+// TMA loads into this CTA's shared memory whose completion counts on the even CTA's barrier
+__device__ __forceinline__ void tma2_load_2d(void* dst, const CUtensorMap* tm, int c0, int c1, uint32_t leader_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(tm), "r"(c0), "r"(c1), "r"(leader_bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma2_load_im2col(void* dst, const CUtensorMap* tm, int c, int w, int h, int n, uint16_t ow,
+                                                 uint16_t oh, uint32_t leader_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.im2col.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(smem_u32(dst)),
+      "l"(tm), "r"(c), "r"(w), "r"(h), "r"(n), "r"(leader_bar), "h"(ow), "h"(oh)
+      : "memory");
+}
+
+constexpr uint32_t kPairB = 128 * 128;              // this CTA's 128 weight rows x one 128-byte k-tile
+constexpr uint32_t kPairStage = BM * 128 + kPairB;  // 32 KB
+
+template <int MODE>
+__global__ void __launch_bounds__(512, 1)
+    conv_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmOut, const ConvGemmArgs a) {
+  constexpr int BN = 256;
+  constexpr uint32_t A_BYTES = BM * 128;
+  const int STAGES = a.stages;
+  const int OB = a.out_bufs;
+  const uint32_t SLAB = a.epi_half ? kOutSlab / 2 : kOutSlab;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* sOut = sB + STAGES * kPairB;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + 8 * OB * SLAB);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* accf = empty + kMaxStages;
+  uint64_t* acce = accf + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acce + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  pdl_launch_dependents();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1u);
+      mbar_init(&empty[s], 1u);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf[i], 1u);
+      mbar_init(&acce[i], 16u);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmOut) : "memory");
+  }
+  if (warp == 1) tmem_alloc2(tmem_holder, 2 * BN);
+  tc_fence_before();
+  cluster_sync();   // both CTAs' barriers initialised and TMEM allocated before any cross-CTA traffic
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  pdl_wait();
+
+  const int KT = a.Kpad / BK;
+  const int tiles_m = (a.M + 2 * BM - 1) / (2 * BM);
+  const int tiles_n = (a.Cout + BN - 1) / BN;
+  const int total = tiles_m * tiles_n;
+  const int pair = int(blockIdx.x >> 1), npairs = int(gridDim.x >> 1);
+
+  if (warp == 0) {
+    if (lane == 0) {   // ---- TMA producer (both CTAs) ----
+      const int hw_out = a.Ho * a.Wo;
+      const int cblocks = a.Cp / BK;
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = pair; t < total; t += npairs) {
+        const int mt = t / tiles_n, nt = t - (t / tiles_n) * tiles_n;
+        const int m0 = mt * 2 * BM + int(rank) * BM;
+        int img = 0, cw = 0, ch = 0;
+        if (MODE == 3) {
+          img = m0 / hw_out;
+          const int rem = m0 - img * hw_out;
+          const int ho = rem / a.Wo;
+          ch = ho * a.sh - a.ph;
+          cw = (rem - ho * a.Wo) * a.sw - a.pw;
+        }
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) goto producer_done;
+          const uint32_t fb = peer_addr(&full[stage], 0);
+          if (leader) mbar_expect_tx(&full[stage], 2 * kPairStage);
+          if (MODE == 0) {
+            tma2_load_2d(sA + stage * A_BYTES, &tmA, kt * BK, m0, fb);
+          } else {
+            const int tap = kt / cblocks, cb = kt - tap * cblocks;
+            const int kh = tap / a.KW, kw = tap - (tap / a.KW) * a.KW;
+            tma2_load_im2col(sA + stage * A_BYTES, &tmA, cb * BK, cw, ch, img, uint16_t(kw * a.dw), uint16_t(kh * a.dh),
+                             fb);
+          }
+          tma2_load_2d(sB + stage * kPairB, &tmB, kt * BK, nt * BN + int(rank) * 128, fb);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {   // ---- MMA issuer (even CTA) ----
+      constexpr uint32_t idesc = idesc_mma(2 * BM, BN, false);
+      int stage = 0, it = 0;
+      uint32_t phase = 0;
+      for (int t = pair; t < total; t += npairs, ++it) {
+        const int acc = it & 1;
+        if (!mbar_wait(&acce[acc], (uint32_t(it >> 1) & 1u) ^ 1u, abort_flag, a.err, 2u)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        bool ok = true;
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, a.err, 4u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(smem_u32(sA + stage * A_BYTES));
+          const uint64_t bd = sw128_desc(smem_u32(sB + stage * kPairB));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma2_bf16(d_tmem, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), idesc, (kt | kk) != 0 ? 1u : 0u);
+          umma2_commit(smem_u32(&empty[stage]));
+          umma2_commit(peer_addr(&empty[stage], 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma2_commit(smem_u32(&accf[acc]));
+        umma2_commit(peer_addr(&accf[acc], 1));
+      }
+    }
+  } else if (warp < 10) {
+    // ---- epilogue (both CTAs): this CTA's 128 rows of the tile, all 256 columns ----
+    const int q = warp & 3;
+    const int hsel = (warp - 2) >> 2;
+    uint8_t* sb0 = sOut + (warp - 2) * OB * SLAB;
+    const uint32_t acce0 = peer_addr(&acce[0], 0), acce1 = peer_addr(&acce[1], 0);
+    int it = 0;
+    for (int t = pair; t < total; t += npairs, ++it) {
+      const int mt = t / tiles_n, nt = t - (t / tiles_n) * tiles_n;
+      const int acc = it & 1;
+      if (!mbar_wait(&accf[acc], uint32_t(it >> 1) & 1u, abort_flag, a.err, 8u)) break;
+      tc_fence_after();
+      const int row0 = mt * 2 * BM + int(rank) * BM + q * 32;
+      const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
+      if (row0 < a.M) {   // warp-uniform
+        for (int s2 = hsel; s2 < BN / 64; s2 += 2) {
+          const int n0 = nt * BN + s2 * 64;
+          if (n0 >= a.Cout) break;
+          if (a.epi_half) {
+            for (int hh = 0; hh < 2 && n0 + hh * 32 < a.Cout; ++hh)
+              epilogue_slab<true>(a, &tmOut, tbase, s2 * 64, row0, n0, sb0, nullptr, a.bias + n0 + hh * 32, OB, 1, BN, hh);
+          } else {
+            epilogue_slab<true>(a, &tmOut, tbase, s2 * 64, row0, n0, sb0, nullptr, a.bias + n0, OB, 1, BN);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(&acce[acc]);
+        else remote_arrive(acc ? acce1 : acce0);
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();   // neither CTA leaves while the other may still touch its shared memory or barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc2(tmem_base, 2 * BN);
+  }
+}
+
 // ---- stem convolution + 3x3/2 max pool ----------------------------------------------------------
 // The ResNet stem (7x7/2 conv over 3 channels, run as a 4x4 stride-1 conv over the 2x2
 // space-to-depth image of 16-channel pixels) with bias, activation and the following MaxPool 3x3 /
@@ -1435,6 +1677,55 @@ cudaError_t launch_f32(const ConvGemmPlan& p, cudaStream_t s) {
   }
 }
 
+// CTA pairs: clusters of two, with programmatic stream serialisation like the others.
+template <int MODE>
+cudaLaunchConfig_t pair_config(int grid, int smem, cudaStream_t s, cudaLaunchAttribute (&attr)[2]) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(512u);
+  cfg.dynamicSmemBytes = size_t(smem);
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cfg;
+}
+
+template <int MODE>
+cudaError_t launch_pair(const ConvGemmPlan& p, cudaStream_t s) {
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = pair_config<MODE>(p.grid, p.smem, s, attr);
+  return cudaLaunchKernelEx(&cfg, conv_pair_kernel<MODE>, p.tmA, p.tmB, p.tmOut, p.args);
+}
+
+// Sets the shared-memory limit of the pair kernel (once per device) and returns how many CTA pairs
+// fit on the device at once (0 if the query fails).
+template <int MODE>
+int pair_setup(int smem, int num_sms) {
+  static std::atomic<uint64_t> done_mask{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = uint64_t(1) << (dev & 63);
+  if (!(done_mask.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(conv_pair_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    done_mask.fetch_or(bit);
+  }
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = pair_config<MODE>(2 * (num_sms / 2), smem, nullptr, attr);
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, conv_pair_kernel<MODE>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return clusters;
+}
+
 template <int BN>
 cudaError_t launch_mode(const ConvGemmPlan& p, cudaStream_t s) {
   if (p.args.tf32) return p.args.x3 ? launch_f32<BN, 2>(p, s) : launch_f32<BN, 1>(p, s);
@@ -1794,6 +2085,27 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   cudaError_t e = bn == 64 ? ensure_attr_mode<64>(mode, prec)
                            : (bn == 128 ? ensure_attr_mode<128>(mode, prec) : ensure_attr_mode<256>(mode, prec));
   if (e != cudaSuccess) throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  // CTA pairs for the 256-column bf16 tiles that stream their weights (no residual, no second
+  // operand, no split): each SM loads and reads half of every weight k-tile.
+  p.pair = 0;
+  const int64_t pair_tiles = int64_t((a.M + 2 * BM - 1) / (2 * BM)) * ((a.Cout + 255) / 256);
+  if (bn == 256 && !a.tf32 && (p.mode == kARows || p.mode == kAIm2col64) && !a.res && !a.a2 && KSP == 1 &&
+      a.epi == 2 && a.out_bf16 && a.group_rows == 0 && !a.bias_mma && !bres && num_sms >= 2) {
+    const int fixed_pair = int(8 * (a.epi_half ? kOutSlab / 2 : kOutSlab)) + 1024 + 512;
+    const int st = std::min(kMaxStages, (kSmemLimit - fixed_pair) / int(kPairStage));
+    const int smem_pair = st * int(kPairStage) + fixed_pair;
+    const int clusters = st >= 2 ? (p.mode == kARows ? pair_setup<0>(smem_pair, num_sms) : pair_setup<3>(smem_pair, num_sms)) : 0;
+    if (clusters >= 1 && encode_2d(&p.tmB, w, uint64_t(a.Kpad), uint64_t(a.Cout), uint64_t(a.Kpad) * 2, uint32_t(bke),
+                                   128, false)) {
+      p.pair = 1;
+      a.stages = st;
+      a.producers = 1;
+      a.mma_lanes = 1;
+      a.out_bufs = 1;
+      p.smem = smem_pair;
+      p.grid = int(2 * std::min<int64_t>(std::min(clusters, num_sms / 2), pair_tiles));
+    }
+  }
 }
 
 int conv3x3_tile_width(int H, int W) {
@@ -1906,9 +2218,10 @@ std::string conv_gemm_describe(const ConvGemmPlan& p) {
   const char* res = !a.res ? "none" : a.res_mma ? "mma" : a.res_slots ? "ring" : "direct";
   char buf[320];
   std::snprintf(buf, sizeof(buf),
-                "M=%d N=%d K=%d mode=%s%s bn=%d grid=%d stages=%d producers=%d issuers=%d residual=%s%s "
+                "M=%d N=%d K=%d mode=%s%s bn=%d%s grid=%d stages=%d producers=%d issuers=%d residual=%s%s "
                 "out_slabs=%d%s weights=%s bias=%s split=%d smem=%d",
-                a.M, a.Cout, a.Kpad, kModes[p.mode], a.x3 ? " tf32x3" : (a.tf32 ? " tf32" : ""), p.bn, p.grid, a.stages,
+                a.M, a.Cout, a.Kpad, kModes[p.mode], a.x3 ? " tf32x3" : (a.tf32 ? " tf32" : ""), p.bn,
+                p.pair ? " (CTA pairs)" : "", p.grid, a.stages,
                 a.producers, a.mma_lanes, res, a.res_slots ? (a.res_slots == 2 ? " x2" : " x1") : "", a.out_bufs,
                 a.epi_half ? " (half slabs)" : "", a.b_resident ? "resident" : "streamed", a.bias_mma ? "mma" : "epilogue",
                 a.ksplit > 1 ? a.ksplit : 1, p.smem);
@@ -1916,6 +2229,7 @@ std::string conv_gemm_describe(const ConvGemmPlan& p) {
 }
 
 cudaError_t conv_gemm_launch(const ConvGemmPlan& p, cudaStream_t s) {
+  if (p.pair) return p.mode == kARows ? launch_pair<0>(p, s) : launch_pair<3>(p, s);
   switch (p.bn) {
     case 64: return launch_mode<64>(p, s);
     case 128: return launch_mode<128>(p, s);

@@ -101,6 +101,7 @@ struct ConvGemmPlan {
   CUtensorMap tmOut;   // valid when args.epi == 2
   CUtensorMap tmRes;   // valid when args.res_slots > 0
   int bn;            // 64, 128 or 256
+  int pair;          // 1: CTA pairs (clusters of two) compute 256 x 256 tiles with cta_group::2 MMAs
   int mode;          // ConvAMode
   int grid;
   int smem;

@@ -308,6 +308,30 @@ def test_conv_chain_64_column_tiles(cmid, n, h, w):
     assert_close(got, ref, what=f"conv chain through {cmid} channels")
 
 
+# 256-column bf16 tiles that stream their weights run on CTA pairs (clusters of two, cta_group::2
+# MMAs of 256 x 256): a 3x3 conv through TMA im2col to 320 channels (the second column tile holds 64
+# of them) and a 1x1 conv through row-matrix TMA, both feeding another conv.
+def test_cta_pair_convs():
+    from shorokoo_b200.emit import onnx_writer as W
+    from shorokoo_b200.emit.graphs import Builder, ModelCase
+    rng = np.random.Generator(np.random.PCG64(31))
+    n, c, h, w = 8, 64, 64, 64
+    x = rng.standard_normal((n, c, h, w), dtype=np.float32)
+    B = Builder(32)
+    xi = B.graph_input(W.FLOAT, 4, x.shape)
+    y1 = _conv(B, xi, c, 320, 3, relu=True)
+    y2 = _conv(B, y1, 320, 256, 1, relu=True)
+    y3 = _conv(B, y2, 256, 16, 3)
+    for t, ch in ((y1, 320), (y2, 256), (y3, 16)):
+        B.shape[t] = (n, ch, h, w)
+    B.outputs.append(W.ValueInfo(y3))
+    case = ModelCase("pair_chain", B.model("pair_chain"), [(xi, x)], [y3], 0)
+    got = run_backend(case)[0]
+    ref = run_oracle(case)[0]
+    assert got.shape == (n, 16, h, w)
+    assert_close(got, ref, what="conv chain on CTA pairs")
+
+
 def _conv_s(B, x, cin, cout, k, stride=1, relu=False, res=None):
     from shorokoo_b200.emit.graphs import kaiming_normal
     w = B.init(kaiming_normal(B.rng, (cout, cin, k, k)), "w")
