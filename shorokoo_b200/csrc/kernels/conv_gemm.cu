@@ -859,6 +859,9 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
 // issuer commits to each CTA's copy separately); acce[acc] in the even CTA (both CTAs' 8 epilogue
 // warps arrive, the odd CTA's remotely). Every mbarrier wait is bounded; both CTAs always reach the
 // final cluster barrier, before which neither leaves (the issuer reads the odd CTA's shared memory).
+// A bf16 residual is added by the tensor core as in the one-SM kernel: after the weight k-tiles come
+// four k-tiles of residual rows (64 channels each) against a 64 x 64 identity, whose rows 32r .. 32r + 31
+// CTA r holds (the B operand of an N=64 pair MMA is split between the two CTAs like any other).
 // Warps: 0 TMA producer, 1 TMEM owner + MMA issuer (even CTA), 2-9 epilogue.
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -922,7 +925,8 @@ constexpr uint32_t kPairStage = BM * 128 + kPairB;  // 32 KB
 template <int MODE>
 __global__ void __launch_bounds__(512, 1)
     conv_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmOut, const ConvGemmArgs a) {
+                     const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
+                     const ConvGemmArgs a) {
   constexpr int BN = 256;
   constexpr uint32_t A_BYTES = BM * 128;
   const int STAGES = a.stages;
@@ -933,7 +937,9 @@ __global__ void __launch_bounds__(512, 1)
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_BYTES;
   uint8_t* sOut = sB + STAGES * kPairB;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + 8 * OB * SLAB);
+  const bool RESM = a.res_mma != 0;
+  uint8_t* sId = sOut + 8 * OB * SLAB;   // RESM: this CTA's 32 rows of the identity (1 KB aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sId + (RESM ? kIdBytes / 2 : 0u));
   uint64_t* empty = full + kMaxStages;
   uint64_t* accf = empty + kMaxStages;
   uint64_t* acce = accf + 2;
@@ -960,6 +966,18 @@ __global__ void __launch_bounds__(512, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmOut) : "memory");
+    if (RESM) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmRes) : "memory");
+  }
+  if (RESM) {   // local row i is identity row n = 32 rank + i: 1.0 at k = n; chunk c of row i holds
+                // logical chunk (c % 8) ^ (i % 8)
+    for (int c = threadIdx.x; c < int(kIdBytes / 32); c += blockDim.x) {
+      const int i = c >> 3, n = int(rank) * 32 + i, lc = (c & 7) ^ (i & 7);
+      const int word = (n >> 3) == lc ? (n & 7) >> 1 : -1;   // the 32-bit word holding element n
+      const uint32_t one = (n & 1) ? 0x3F800000u : 0x00003F80u;
+      reinterpret_cast<uint4*>(sId)[c] =
+          make_uint4(word == 0 ? one : 0u, word == 1 ? one : 0u, word == 2 ? one : 0u, word == 3 ? one : 0u);
+    }
+    fence_async_smem();   // generic writes -> the MMA's async-proxy reads
   }
   if (warp == 1) tmem_alloc2(tmem_holder, 2 * BN);
   tc_fence_before();
@@ -969,6 +987,7 @@ __global__ void __launch_bounds__(512, 1)
   pdl_wait();
 
   const int KT = a.Kpad / BK;
+  const int KTE = KT + (RESM ? BN / 64 : 0);   // k-tiles per tile: weights, then residual
   const int tiles_m = (a.M + 2 * BM - 1) / (2 * BM);
   const int tiles_n = (a.Cout + BN - 1) / BN;
   const int total = tiles_m * tiles_n;
@@ -991,9 +1010,18 @@ __global__ void __launch_bounds__(512, 1)
           ch = ho * a.sh - a.ph;
           cw = (rem - ho * a.Wo) * a.sw - a.pw;
         }
-        for (int kt = 0; kt < KT; ++kt) {
+        for (int kt = 0; kt < KTE; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) goto producer_done;
           const uint32_t fb = peer_addr(&full[stage], 0);
+          if (kt >= KT) {   // residual k-tile: this CTA's 128 rows x 64 residual channels, no weights
+            if (leader) mbar_expect_tx(&full[stage], 2 * A_BYTES);
+            tma2_load_2d(sA + stage * A_BYTES, &tmRes, nt * BN + (kt - KT) * 64, m0, fb);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
           if (leader) mbar_expect_tx(&full[stage], 2 * kPairStage);
           if (MODE == 0) {
             tma2_load_2d(sA + stage * A_BYTES, &tmA, kt * BK, m0, fb);
@@ -1015,6 +1043,8 @@ __global__ void __launch_bounds__(512, 1)
   } else if (warp == 1) {
     if (lane == 0 && leader) {   // ---- MMA issuer (even CTA) ----
       constexpr uint32_t idesc = idesc_mma(2 * BM, BN, false);
+      constexpr uint32_t idesc64 = idesc_mma(2 * BM, 64, false);   // residual k-tiles: 64 columns each
+      const uint64_t idd = sw128_desc(smem_u32(sId));
       int stage = 0, it = 0;
       uint32_t phase = 0;
       for (int t = pair; t < total; t += npairs, ++it) {
@@ -1023,7 +1053,7 @@ __global__ void __launch_bounds__(512, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
         bool ok = true;
-        for (int kt = 0; kt < KT; ++kt) {
+        for (int kt = 0; kt < KTE; ++kt) {
           if (!mbar_wait(&full[stage], phase, abort_flag, a.err, 4u)) {
             ok = false;
             break;
@@ -1031,9 +1061,15 @@ __global__ void __launch_bounds__(512, 1)
           tc_fence_after();
           const uint64_t ad = sw128_desc(smem_u32(sA + stage * A_BYTES));
           const uint64_t bd = sw128_desc(smem_u32(sB + stage * kPairB));
+          if (kt >= KT) {   // D[:, 64j .. 64j + 64) += R_j * I
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma2_bf16(d_tmem, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), idesc, (kt | kk) != 0 ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk)
+              umma2_bf16(d_tmem + uint32_t((kt - KT) * 64), ad + uint64_t(kk * 2), idd + uint64_t(kk * 2), idesc64, 1u);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma2_bf16(d_tmem, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), idesc, (kt | kk) != 0 ? 1u : 0u);
+          }
           umma2_commit(smem_u32(&empty[stage]));
           umma2_commit(peer_addr(&empty[stage], 1));
           if (++stage == STAGES) {
@@ -1700,7 +1736,7 @@ template <int MODE>
 cudaError_t launch_pair(const ConvGemmPlan& p, cudaStream_t s) {
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = pair_config<MODE>(p.grid, p.smem, s, attr);
-  return cudaLaunchKernelEx(&cfg, conv_pair_kernel<MODE>, p.tmA, p.tmB, p.tmOut, p.args);
+  return cudaLaunchKernelEx(&cfg, conv_pair_kernel<MODE>, p.tmA, p.tmB, p.tmOut, p.tmRes, p.args);
 }
 
 // Sets the shared-memory limit of the pair kernel (once per device) and returns how many CTA pairs
@@ -2085,13 +2121,13 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
   cudaError_t e = bn == 64 ? ensure_attr_mode<64>(mode, prec)
                            : (bn == 128 ? ensure_attr_mode<128>(mode, prec) : ensure_attr_mode<256>(mode, prec));
   if (e != cudaSuccess) throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-  // CTA pairs for the 256-column bf16 tiles that stream their weights (no residual, no second
-  // operand, no split): each SM loads and reads half of every weight k-tile.
+  // CTA pairs for the 256-column bf16 tiles that stream their weights (no residual or one the tensor
+  // core adds, no second operand, no split): each SM loads and reads half of every weight k-tile.
   p.pair = 0;
   const int64_t pair_tiles = int64_t((a.M + 2 * BM - 1) / (2 * BM)) * ((a.Cout + 255) / 256);
-  if (bn == 256 && !a.tf32 && (p.mode == kARows || p.mode == kAIm2col64) && !a.res && !a.a2 && KSP == 1 &&
-      a.epi == 2 && a.out_bf16 && a.group_rows == 0 && !a.bias_mma && !bres && num_sms >= 2) {
-    const int fixed_pair = int(8 * (a.epi_half ? kOutSlab / 2 : kOutSlab)) + 1024 + 512;
+  if (bn == 256 && !a.tf32 && (p.mode == kARows || p.mode == kAIm2col64) && (!a.res || a.res_mma) && !a.a2 &&
+      KSP == 1 && a.epi == 2 && a.out_bf16 && a.group_rows == 0 && !a.bias_mma && !bres && num_sms >= 2) {
+    const int fixed_pair = int(8 * (a.epi_half ? kOutSlab / 2 : kOutSlab)) + (a.res_mma ? int(kIdBytes / 2) : 0) + 1024 + 512;
     const int st = std::min(kMaxStages, (kSmemLimit - fixed_pair) / int(kPairStage));
     const int smem_pair = st * int(kPairStage) + fixed_pair;
     const int clusters = st >= 2 ? (p.mode == kARows ? pair_setup<0>(smem_pair, num_sms) : pair_setup<3>(smem_pair, num_sms)) : 0;
