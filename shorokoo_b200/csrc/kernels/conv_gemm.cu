@@ -859,6 +859,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
 // issuer commits to each CTA's copy separately); acce[acc] in the even CTA (both CTAs' 8 epilogue
 // warps arrive, the odd CTA's remotely). Every mbarrier wait is bounded; both CTAs always reach the
 // final cluster barrier, before which neither leaves (the issuer reads the odd CTA's shared memory).
+// A merged projection shortcut's second A operand comes through tmRes as in the one-SM kernel.
 // A bf16 residual is added by the tensor core as in the one-SM kernel: after the weight k-tiles come
 // four k-tiles of residual rows (64 channels each) against a 64 x 64 identity, whose rows 32r .. 32r + 31
 // CTA r holds (the B operand of an N=64 pair MMA is split between the two CTAs like any other).
@@ -966,7 +967,7 @@ __global__ void __launch_bounds__(512, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmOut) : "memory");
-    if (RESM) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmRes) : "memory");
+    if (RESM || a.a2) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmRes) : "memory");
   }
   if (RESM) {   // local row i is identity row n = 32 rank + i: 1.0 at k = n; chunk c of row i holds
                 // logical chunk (c % 8) ^ (i % 8)
@@ -1023,8 +1024,16 @@ __global__ void __launch_bounds__(512, 1)
             continue;
           }
           if (leader) mbar_expect_tx(&full[stage], 2 * kPairStage);
-          if (MODE == 0) {
-            tma2_load_2d(sA + stage * A_BYTES, &tmA, kt * BK, m0, fb);
+          if (MODE == 0) {   // (k-tiles from a2_kt on come from the second operand, through tmRes)
+            if (a.a2 && kt >= a.a2_kt && a.a2_s > 0) {   // strided image: im2col of a 1x1 conv at stride s
+              const int im = m0 / hw_out, rem = m0 - (m0 / hw_out) * hw_out;
+              const int ho = rem / a.Wo, wo = rem - (rem / a.Wo) * a.Wo;
+              tma2_load_im2col(sA + stage * A_BYTES, &tmRes, (kt - a.a2_kt) * BK, wo * a.a2_s, ho * a.a2_s, im, 0, 0, fb);
+            } else if (a.a2 && kt >= a.a2_kt) {
+              tma2_load_2d(sA + stage * A_BYTES, &tmRes, (kt - a.a2_kt) * BK, m0, fb);
+            } else {
+              tma2_load_2d(sA + stage * A_BYTES, &tmA, kt * BK, m0, fb);
+            }
           } else {
             const int tap = kt / cblocks, cb = kt - tap * cblocks;
             const int kh = tap / a.KW, kw = tap - (tap / a.KW) * a.KW;
@@ -2122,10 +2131,11 @@ void conv_gemm_prepare(ConvGemmPlan& p, const void* a_rows, int64_t lda, const v
                            : (bn == 128 ? ensure_attr_mode<128>(mode, prec) : ensure_attr_mode<256>(mode, prec));
   if (e != cudaSuccess) throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   // CTA pairs for the 256-column bf16 tiles that stream their weights (no residual or one the tensor
-  // core adds, no second operand, no split): each SM loads and reads half of every weight k-tile.
+  // core adds, a merged projection shortcut's second operand or none, no split): each SM loads and
+  // reads half of every weight k-tile.
   p.pair = 0;
   const int64_t pair_tiles = int64_t((a.M + 2 * BM - 1) / (2 * BM)) * ((a.Cout + 255) / 256);
-  if (bn == 256 && !a.tf32 && (p.mode == kARows || p.mode == kAIm2col64) && (!a.res || a.res_mma) && !a.a2 &&
+  if (bn == 256 && !a.tf32 && (p.mode == kARows || p.mode == kAIm2col64) && (!a.res || a.res_mma) &&
       KSP == 1 && a.epi == 2 && a.out_bf16 && a.group_rows == 0 && !a.bias_mma && !bres && num_sms >= 2) {
     const int fixed_pair = int(8 * (a.epi_half ? kOutSlab / 2 : kOutSlab)) + (a.res_mma ? int(kIdBytes / 2) : 0) + 1024 + 512;
     const int st = std::min(kMaxStages, (kSmemLimit - fixed_pair) / int(kPairStage));

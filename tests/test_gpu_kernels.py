@@ -348,22 +348,26 @@ def _conv_s(B, x, cin, cout, k, stride=1, relu=False, res=None):
 # A bottleneck whose 1x1 projection shortcut (stride 1, or stride 2 over an odd-sized map) is merged
 # into the last 1x1 conv: one GEMM over both operands' channels, the shortcut's input read through
 # a second tensor map (row matrix, or im2col at the shortcut's stride).
-@pytest.mark.parametrize("stride,h,w,cout", [(1, 12, 10, 256), (2, 15, 13, 256), (2, 16, 16, 192)])
-def test_merged_projection_shortcut(stride, h, w, cout):
+# The 8-image cases with 256 middle channels (K = 256 + 128 streamed weights, 32768 output pixels)
+# run the merged conv on CTA pairs.
+@pytest.mark.parametrize("stride,h,w,cout,n,mid", [(1, 12, 10, 256, 2, 64), (2, 15, 13, 256, 2, 64),
+                                                   (2, 16, 16, 192, 2, 64), (1, 64, 64, 256, 8, 256),
+                                                   (2, 128, 128, 256, 8, 256)])
+def test_merged_projection_shortcut(stride, h, w, cout, n, mid):
     from shorokoo_b200.emit import onnx_writer as W
     from shorokoo_b200.emit.graphs import Builder, ModelCase
     rng = np.random.Generator(np.random.PCG64(31))
-    n, c = 2, 128
+    c = 128
     x = rng.standard_normal((n, c, h, w), dtype=np.float32)
     B = Builder(32)
     xi = B.graph_input(W.FLOAT, 4, x.shape)
     ho, wo = (h - 1) // stride + 1, (w - 1) // stride + 1
-    a = _conv_s(B, xi, c, 64, 1, relu=True)
-    bb = _conv_s(B, a, 64, 64, 3, stride=stride, relu=True)
+    a = _conv_s(B, xi, c, mid, 1, relu=True)
+    bb = _conv_s(B, a, mid, mid, 3, stride=stride, relu=True)
     sc = _conv_s(B, xi, c, cout, 1, stride=stride)
-    y = _conv_s(B, bb, 64, cout, 1, relu=True, res=sc)
+    y = _conv_s(B, bb, mid, cout, 1, relu=True, res=sc)
     z = _conv_s(B, y, cout, 16, 1)   # y feeds a conv, so the merged conv writes bf16
-    for t, ch, hh, ww in ((a, 64, h, w), (bb, 64, ho, wo), (sc, cout, ho, wo), (y, cout, ho, wo), (z, 16, ho, wo)):
+    for t, ch, hh, ww in ((a, mid, h, w), (bb, mid, ho, wo), (sc, cout, ho, wo), (y, cout, ho, wo), (z, 16, ho, wo)):
         B.shape[t] = (n, ch, hh, ww)
     B.outputs.append(W.ValueInfo(z))
     case = ModelCase("merged_shortcut", B.model("merged_shortcut"), [(xi, x)], [z], 0)
