@@ -311,7 +311,9 @@ def test_conv_chain_64_column_tiles(cmid, n, h, w):
 # 256-column bf16 tiles that stream their weights run on CTA pairs (clusters of two, cta_group::2
 # MMAs of 256 x 256): a 3x3 conv through TMA im2col to 320 channels (the second column tile holds 64
 # of them), a 1x1 conv through row-matrix TMA, and a 1x1 conv whose residual the pair's tensor core
-# adds (each CTA holding half of the identity operand), each feeding another conv.
+# adds (each CTA holding half of the identity operand), each feeding another conv; then 3x3 convs to
+# 128 channels (one-SM 128-column tiles: pairs of 256 x 128 measured slower, their single MMA issuer
+# the limit), the second with a residual.
 def test_cta_pair_convs():
     from shorokoo_b200.emit import onnx_writer as W
     from shorokoo_b200.emit.graphs import Builder, ModelCase
@@ -323,11 +325,13 @@ def test_cta_pair_convs():
     y1 = _conv(B, xi, c, 320, 3, relu=True)
     y2 = _conv(B, y1, 320, 256, 1, relu=True)
     y3 = _conv(B, y2, 256, 256, 1, relu=True, res=y2)
-    y4 = _conv(B, y3, 256, 16, 3)
-    for t, ch in ((y1, 320), (y2, 256), (y3, 256), (y4, 16)):
+    y4 = _conv(B, y3, 256, 128, 3, relu=True)
+    y5 = _conv(B, y4, 128, 128, 3, relu=True, res=y4)
+    y6 = _conv(B, y5, 128, 16, 3)
+    for t, ch in ((y1, 320), (y2, 256), (y3, 256), (y4, 128), (y5, 128), (y6, 16)):
         B.shape[t] = (n, ch, h, w)
-    B.outputs.append(W.ValueInfo(y4))
-    case = ModelCase("pair_chain", B.model("pair_chain"), [(xi, x)], [y4], 0)
+    B.outputs.append(W.ValueInfo(y6))
+    case = ModelCase("pair_chain", B.model("pair_chain"), [(xi, x)], [y6], 0)
     got = run_backend(case)[0]
     ref = run_oracle(case)[0]
     assert got.shape == (n, 16, h, w)
