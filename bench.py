@@ -330,7 +330,8 @@ def main():
                          "traffic_note": "DRAM bytes read + written per step by these launches, one ncu capture of "
                                          "this workload (profiles/resnet50_bs512_dram_launch_list.md); algorithmic "
                                          "minimum ~23.2e9" if traffic else None,
-                         "kernel": f"conv_gemm_kernel (tcgen05 implicit GEMM), {tc_launches} launches/step, "
+                         "kernel": f"tcgen05 implicit GEMM (conv_gemm_kernel, conv_pair_kernel on CTA pairs, stem and halo "
+                                   f"kernels), {tc_launches} launches/step, "
                                    f"{tc_ms:.3f} of {all_ms:.3f} ms per step timed per launch with CUDA events",
                          "peak_kind": peak_note},
             "clocks": clocks,
