@@ -863,7 +863,7 @@ __global__ void __launch_bounds__(kThreads<MODE, PREC>, 1)
 // A bf16 residual is added by the tensor core as in the one-SM kernel: after the weight k-tiles come
 // four k-tiles of residual rows (64 channels each) against a 64 x 64 identity, whose rows 32r .. 32r + 31
 // CTA r holds (the B operand of an N=64 pair MMA is split between the two CTAs like any other).
-// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer (even CTA), 2-9 epilogue.
+// Warps: 0 and 10 TMA producers (A and B), 1 TMEM owner + MMA issuer (even CTA), 2-9 epilogue.
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -994,8 +994,11 @@ __global__ void __launch_bounds__(512, 1)
   const int total = tiles_m * tiles_n;
   const int pair = int(blockIdx.x >> 1), npairs = int(gridDim.x >> 1);
 
-  if (warp == 0) {
-    if (lane == 0) {   // ---- TMA producer (both CTAs) ----
+  if (warp == 0 || warp == 10) {
+    // ---- TMA producers (both CTAs): warp 0 loads A (and the residual or second operand) and, in
+    // the even CTA, expects the stage's bytes; warp 10 loads this CTA's half of the weights ----
+    const bool bprod = warp == 10;
+    if (lane == 0) {
       const int hw_out = a.Ho * a.Wo;
       const int cblocks = a.Cp / BK;
       int stage = 0;
@@ -1014,6 +1017,14 @@ __global__ void __launch_bounds__(512, 1)
         for (int kt = 0; kt < KTE; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.err, 1u)) goto producer_done;
           const uint32_t fb = peer_addr(&full[stage], 0);
+          if (bprod) {
+            if (kt < KT) tma2_load_2d(sB + stage * kPairB, &tmB, kt * BK, nt * BN + int(rank) * 128, fb);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
           if (kt >= KT) {   // residual k-tile: this CTA's 128 rows x 64 residual channels, no weights
             if (leader) mbar_expect_tx(&full[stage], 2 * A_BYTES);
             tma2_load_2d(sA + stage * A_BYTES, &tmRes, nt * BN + (kt - KT) * 64, m0, fb);
@@ -1040,7 +1051,6 @@ __global__ void __launch_bounds__(512, 1)
             tma2_load_im2col(sA + stage * A_BYTES, &tmA, cb * BK, cw, ch, img, uint16_t(kw * a.dw), uint16_t(kh * a.dh),
                              fb);
           }
-          tma2_load_2d(sB + stage * kPairB, &tmB, kt * BK, nt * BN + int(rank) * 128, fb);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
